@@ -1,0 +1,397 @@
+// Memory-bound kernels: sanitize, RMSNorm fwd/bwd, depthwise causal conv1d
+// (+bias, +SiLU, +clamp) fwd/bwd, gradient accumulation and embedding gather/scatter.
+//
+// Weight gradients (RMSNorm scale, conv taps/bias, embedding rows) are added
+// straight into the caller's fp32 accumulator (the flat gradient store), so no
+// per-micro-step weight-gradient tensor is materialised.
+//
+// Plain CUDA (no framework headers): the launchers below take raw pointers and
+// a stream; `bindings.cpp` adapts them to torch tensors.
+#include "common.cuh"
+#include "launchers.h"
+#include <algorithm>
+
+using namespace ahb;
+using bf16 = __nv_bfloat16;
+// ----------------------------------------------------------------- sanitize
+template <typename T>
+__global__ void sanitize_kernel(T* __restrict__ out, const T* __restrict__ in, int64_t n, float c) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = from_f<T>(sanitize(to_f(in[i]), c));
+}
+
+
+// ----------------------------------------------------------------- RMSNorm
+// A group of G warps handles one row; each thread holds VPL values (D <= 32*G*VPL).
+// Blocks are 256 threads = 8/G rows.
+template <int G>
+AHB_DEVICE float group_sum(float v, float* sh) {
+  v = warp_sum(v);
+  if constexpr (G == 1) return v;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncwarp();
+  if (lane == 0) sh[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int g0 = (w / G) * G;
+#pragma unroll
+  for (int i = 0; i < G; ++i) t += sh[g0 + i];
+  __syncthreads();
+  return t;
+}
+
+template <typename T, int VPL, int G>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ scale,
+    T* __restrict__ y, float* __restrict__ rstd_out, int64_t M, int D, float eps) {
+  __shared__ float sh[8];
+  const int gl = threadIdx.x % (32 * G);
+  const int64_t row = blockIdx.x * (int64_t)(8 / G) + threadIdx.x / (32 * G);
+  const bool live = row < M;
+  const T* xr = x + (live ? row : 0) * D;
+  float v[VPL];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int c = i * 32 * G + gl;
+    v[i] = (live && c < D) ? to_f(xr[c]) : 0.f;
+    ss += v[i] * v[i];
+  }
+  ss = group_sum<G>(ss, sh);
+  if (!live) return;
+  float r = rsqrtf(ss / D + eps);
+  if (gl == 0) rstd_out[row] = r;
+  T* yr = y + row * D;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    int c = i * 32 * G + gl;
+    if (c < D) yr[c] = from_f<T>(v[i] * r * scale[c]);
+  }
+}
+
+template <typename T, int VPL, int G>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+    const float* __restrict__ scale, const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dscale,
+    int64_t M, int D) {
+  __shared__ float sh[8];
+  const int gl = threadIdx.x % (32 * G);
+  const int rpb = 8 / G;
+  float acc[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  const int64_t nrow_iters = (M + (int64_t)gridDim.x * rpb - 1) / ((int64_t)gridDim.x * rpb);
+  for (int64_t it = 0; it < nrow_iters; ++it) {
+    const int64_t row = (it * gridDim.x + blockIdx.x) * rpb + threadIdx.x / (32 * G);
+    const bool live = row < M;
+    const T* xr = x + (live ? row : 0) * D;
+    const T* dyr = dy + (live ? row : 0) * D;
+    float r = live ? rstd[row] : 0.f;
+    float xh[VPL], g[VPL];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = i * 32 * G + gl;
+      bool ok = live && c < D;
+      xh[i] = ok ? to_f(xr[c]) * r : 0.f;
+      float d = ok ? to_f(dyr[c]) : 0.f;
+      acc[i] += d * xh[i];
+      g[i] = ok ? d * scale[c] : 0.f;
+      dot += g[i] * xh[i];
+    }
+    dot = group_sum<G>(dot, sh) / D;
+    if (live) {
+      T* dxr = dx + row * D;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        int c = i * 32 * G + gl;
+        if (c < D) dxr[c] = from_f<T>(r * (g[i] - xh[i] * dot));
+      }
+    }
+  }
+  if (dscale) {
+    // every group of the block holds partials for the same columns: add them all
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      int c = i * 32 * G + gl;
+      if (c < D) atomicAdd(dscale + c, acc[i]);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- causal conv1d
+// x: (B, L, C) with row stride `xs` (elements); w: (C, W) fp32 or bf16; b: (C,) fp32.
+// y[b,t,c] = act(sum_k w[c,k] * x[b, t-(W-1)+k, c] + bias[c]), then clamp(+-clip) if clip>0.
+// Each thread: 8 consecutive channels x TT consecutive timesteps.
+constexpr int CONV_TT = 16;
+
+template <typename T, typename WT, int W>
+__global__ void conv1d_fwd_kernel(const T* __restrict__ x, int64_t xs, const WT* __restrict__ w,
+                                  const float* __restrict__ bias, T* __restrict__ y, int B, int L, int C,
+                                  bool silu, float clip) {
+  const int cg = C / 8;
+  int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int nt = (L + CONV_TT - 1) / CONV_TT;
+  if (idx >= (int64_t)B * nt * cg) return;
+  const int c0 = (int)(idx % cg) * 8;
+  const int tb = (int)((idx / cg) % nt) * CONV_TT;
+  const int b = (int)(idx / ((int64_t)cg * nt));
+  float wk[8][W], bs[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int k = 0; k < W; ++k) wk[j][k] = to_f(w[(c0 + j) * W + k]);
+    bs[j] = bias ? bias[c0 + j] : 0.f;
+  }
+  float hist[W][8];
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+    int t = tb - (W - 1) + k;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[k][j] = t >= 0 ? to_f(x[((int64_t)b * L + t) * xs + c0 + j]) : 0.f;
+  }
+  for (int tt = 0; tt < CONV_TT; ++tt) {
+    int t = tb + tt;
+    if (t >= L) break;
+    const T* xr = x + ((int64_t)b * L + t) * xs + c0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[W - 1][j] = to_f(xr[j]);
+    T* yr = y + ((int64_t)b * L + t) * C + c0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = bs[j];
+#pragma unroll
+      for (int k = 0; k < W; ++k) a += wk[j][k] * hist[k][j];
+      if (silu) a = siluf_(a);
+      if (clip > 0.f) a = fminf(fmaxf(a, -clip), clip);
+      yr[j] = from_f<T>(a);
+    }
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[k][j] = hist[k + 1][j];
+  }
+}
+
+// Backward.  dpre[t] = dy[t] * act'(pre[t]) (masked by the clamp);
+// dx[s] = sum_k w[k] dpre[s + W-1-k]; dw[k] += sum_t dpre[t] x[t-(W-1)+k]; db += sum_t dpre[t].
+template <typename T, typename WT, int W>
+__global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT* __restrict__ w,
+                                  const float* __restrict__ bias, const T* __restrict__ dy, T* __restrict__ dx,
+                                  int64_t dxs, float* __restrict__ dw, float* __restrict__ db, int B, int L, int C,
+                                  bool silu, float clip) {
+  const int cg = C / 8;
+  int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int nt = (L + CONV_TT - 1) / CONV_TT;
+  if (idx >= (int64_t)B * nt * cg) return;
+  const int c0 = (int)(idx % cg) * 8;
+  const int tb = (int)((idx / cg) % nt) * CONV_TT;
+  const int b = (int)(idx / ((int64_t)cg * nt));
+  float wk[8][W], bs[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int k = 0; k < W; ++k) wk[j][k] = to_f(w[(c0 + j) * W + k]);
+    bs[j] = bias ? bias[c0 + j] : 0.f;
+  }
+  // x window covering [tb-(W-1), tb+TT+W-2]; dpre for t in [tb, tb+TT+W-2]
+  constexpr int NX = CONV_TT + 2 * (W - 1);
+  float dwl[8][W], dbl[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { dbl[j] = 0.f;
+#pragma unroll
+    for (int k = 0; k < W; ++k) dwl[j][k] = 0.f; }
+  // dpre ring: we compute dpre for t in [tb, tb+TT+W-2] (needed by dx of s in [tb, tb+TT-1])
+  float dp[CONV_TT + W - 1][8];
+#pragma unroll
+  for (int i = 0; i < CONV_TT + W - 1; ++i) {
+    int t = tb + i;
+    if (t >= L) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dp[i][j] = 0.f;
+      continue;
+    }
+    float xv[W][8];
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      int tx = t - (W - 1) + k;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[k][j] = tx >= 0 ? to_f(x[((int64_t)b * L + tx) * xs + c0 + j]) : 0.f;
+    }
+    const T* dyr = dy + ((int64_t)b * L + t) * C + c0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = bs[j];
+#pragma unroll
+      for (int k = 0; k < W; ++k) a += wk[j][k] * xv[k][j];
+      float g = to_f(dyr[j]);
+      float post = a;
+      if (silu) {
+        float s = sigmoidf_(a);
+        post = a * s;
+        g *= s * (1.f + a * (1.f - s));
+      }
+      if (clip > 0.f && fabsf(post) > clip) g = 0.f;
+      dp[i][j] = g;
+      if (i < CONV_TT) {  // weight/bias grads counted once per t (owned t range)
+        dbl[j] += g;
+#pragma unroll
+        for (int k = 0; k < W; ++k) dwl[j][k] += g * xv[k][j];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < CONV_TT; ++i) {
+    int s = tb + i;
+    if (s >= L) break;
+    T* dxr = dx + ((int64_t)b * L + s) * dxs + c0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = 0.f;
+#pragma unroll
+      for (int k = 0; k < W; ++k) a += wk[j][k] * dp[i + (W - 1) - k][j];
+      dxr[j] = from_f<T>(a);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (db) atomicAdd(db + c0 + j, dbl[j]);
+#pragma unroll
+    for (int k = 0; k < W; ++k) atomicAdd(dw + (c0 + j) * W + k, dwl[j][k]);
+  }
+  (void)NX;
+}
+
+
+
+// x: (B, L, C) possibly a column slice (stride(1) = xs >= C, stride(2) = 1).
+
+// Returns dx (B,L,C) contiguous; dw_acc (C,W) fp32 and db_acc (C,) fp32 are ADDED to.
+
+// ----------------------------------------------------------------- grad accumulate / embedding
+template <typename T>
+__global__ void accum_kernel(float* __restrict__ acc, const T* __restrict__ g, int64_t n, float scale) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    acc[i] += scale * to_f(g[i]);
+}
+
+
+// out[t, :] = emb[ids[t], :] (bf16 or fp32 table -> out dtype)
+template <typename TI, typename TO>
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const TI* __restrict__ emb, TO* __restrict__ out,
+                                 int64_t T, int D, int64_t V) {
+  int64_t t = blockIdx.x;
+  int64_t id = ids[t];
+  id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+  for (int c = threadIdx.x; c < D; c += blockDim.x) out[t * D + c] = from_f<TO>(to_f(emb[id * D + c]));
+}
+
+
+template <typename T>
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ dout, float* __restrict__ acc,
+                                 int64_t T_, int D, int64_t V) {
+  int64_t t = blockIdx.x;
+  int64_t id = ids[t];
+  if (id < 0 || id >= V) return;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(acc + id * D + c, to_f(dout[t * D + c]));
+}
+
+
+
+// ===================================================================== launchers
+static int sm_count() {
+  static int n = 0;
+  if (!n) { int d; cudaGetDevice(&d); cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d); }
+  return n;
+}
+static int ew_blocks(int64_t n, int threads) {
+  return (int)std::min<int64_t>((n + threads - 1) / threads, (int64_t)sm_count() * 16);
+}
+
+void ahb_sanitize(void* out, const void* in, int64_t n, int dtype, float clip, cudaStream_t st) {
+  if (n == 0) return;
+  if (dtype == AHB_BF16) sanitize_kernel<bf16><<<ew_blocks(n, 256), 256, 0, st>>>((bf16*)out, (const bf16*)in, n, clip);
+  else sanitize_kernel<float><<<ew_blocks(n, 256), 256, 0, st>>>((float*)out, (const float*)in, n, clip);
+}
+
+#define RMS_DISPATCH(KER, ...)                                                     \
+  if (D <= 256) KER(T, 8, 1, __VA_ARGS__);                                         \
+  else if (D <= 512) KER(T, 16, 1, __VA_ARGS__);                                   \
+  else if (D <= 1024) KER(T, 32, 1, __VA_ARGS__);                                  \
+  else if (D <= 2048) KER(T, 32, 2, __VA_ARGS__);                                  \
+  else if (D <= 4096) KER(T, 32, 4, __VA_ARGS__);                                  \
+  else KER(T, 32, 8, __VA_ARGS__);
+
+#define RMS_F(T, V, G, _) rmsnorm_fwd_kernel<T, V, G><<<(unsigned)((M + 8 / G - 1) / (8 / G)), 256, 0, st>>>( \
+    (const T*)x, s, (T*)y, r, M, D, eps)
+template <typename T>
+static void rms_fwd_t(const void* x, const float* s, void* y, float* r, int64_t M, int D, float eps, cudaStream_t st) {
+  RMS_DISPATCH(RMS_F, 0)
+}
+#undef RMS_F
+void ahb_rmsnorm_fwd(const void* x, const float* scale, void* y, float* rstd, int64_t M, int D, int dtype, float eps,
+                     cudaStream_t st) {
+  if (M == 0) return;
+  if (D > 8192) return;
+  if (dtype == AHB_BF16) rms_fwd_t<bf16>(x, scale, y, rstd, M, D, eps, st);
+  else rms_fwd_t<float>(x, scale, y, rstd, M, D, eps, st);
+}
+
+#define RMS_B(T, V, G, _) rmsnorm_bwd_kernel<T, V, G><<<(unsigned)std::min<int64_t>((M + 8 / G - 1) / (8 / G), \
+    (int64_t)sm_count() * 8), 256, 0, st>>>((const T*)dy, (const T*)x, s, r, (T*)dx, ds, M, D)
+template <typename T>
+static void rms_bwd_t(const void* dy, const void* x, const float* s, const float* r, void* dx, float* ds, int64_t M,
+                      int D, cudaStream_t st) {
+  RMS_DISPATCH(RMS_B, 0)
+}
+#undef RMS_B
+void ahb_rmsnorm_bwd(const void* dy, const void* x, const float* scale, const float* rstd, void* dx, float* dscale_acc,
+                     int64_t M, int D, int dtype, cudaStream_t st) {
+  if (M == 0) return;
+  if (dtype == AHB_BF16) rms_bwd_t<bf16>(dy, x, scale, rstd, dx, dscale_acc, M, D, st);
+  else rms_bwd_t<float>(dy, x, scale, rstd, dx, dscale_acc, M, D, st);
+}
+
+void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,
+                    int C, int dtype, int silu, float clip, cudaStream_t st) {
+  int64_t n = (int64_t)B * ((L + CONV_TT - 1) / CONV_TT) * (C / 8);
+  if (n == 0) return;
+  unsigned blocks = (unsigned)((n + 127) / 128);
+#define CF(T, WT) conv1d_fwd_kernel<T, WT, 4><<<blocks, 128, 0, st>>>((const T*)x, xs, (const WT*)w, bias, (T*)y, B, L, C, silu != 0, clip)
+  if (dtype == AHB_BF16) { if (wdtype == AHB_BF16) CF(bf16, bf16); else CF(bf16, float); }
+  else { if (wdtype == AHB_BF16) CF(float, bf16); else CF(float, float); }
+#undef CF
+}
+
+void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, const void* dy, void* dx,
+                    float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
+                    cudaStream_t st) {
+  int64_t n = (int64_t)B * ((L + CONV_TT - 1) / CONV_TT) * (C / 8);
+  if (n == 0) return;
+  unsigned blocks = (unsigned)((n + 127) / 128);
+#define CB(T, WT) conv1d_bwd_kernel<T, WT, 4><<<blocks, 128, 0, st>>>((const T*)x, xs, (const WT*)w, bias, (const T*)dy, \
+      (T*)dx, (int64_t)C, dw_acc, db_acc, B, L, C, silu != 0, clip)
+  if (dtype == AHB_BF16) { if (wdtype == AHB_BF16) CB(bf16, bf16); else CB(bf16, float); }
+  else { if (wdtype == AHB_BF16) CB(float, bf16); else CB(float, float); }
+#undef CB
+}
+
+void ahb_accumulate(float* acc, const void* g, int64_t n, int dtype, float scale, cudaStream_t st) {
+  if (n == 0) return;
+  if (dtype == AHB_BF16) accum_kernel<bf16><<<ew_blocks(n, 256), 256, 0, st>>>(acc, (const bf16*)g, n, scale);
+  else accum_kernel<float><<<ew_blocks(n, 256), 256, 0, st>>>(acc, (const float*)g, n, scale);
+}
+
+void ahb_embedding_fwd(const int64_t* ids, const void* emb, int edtype, void* out, int odtype, int64_t T, int D,
+                       int64_t V, cudaStream_t st) {
+  if (T == 0) return;
+#define EF(TI, TO) embed_fwd_kernel<TI, TO><<<(unsigned)T, 256, 0, st>>>(ids, (const TI*)emb, (TO*)out, T, D, V)
+  bool ib = edtype == AHB_BF16, ob = odtype == AHB_BF16;
+  if (ib && ob) EF(bf16, bf16); else if (ib) EF(bf16, float); else if (ob) EF(float, bf16); else EF(float, float);
+#undef EF
+}
+
+void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* acc, int64_t T, int D, int64_t V,
+                       cudaStream_t st) {
+  if (T == 0) return;
+  if (dtype == AHB_BF16) embed_bwd_kernel<bf16><<<(unsigned)T, 256, 0, st>>>(ids, (const bf16*)dout, acc, T, D, V);
+  else embed_bwd_kernel<float><<<(unsigned)T, 256, 0, st>>>(ids, (const float*)dout, acc, T, D, V);
+}

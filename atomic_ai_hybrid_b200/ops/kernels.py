@@ -1,0 +1,237 @@
+"""Autograd wrappers around the sm_100a kernels of ``_ahb_cuda``.
+
+Weight gradients are accumulated directly into the fp32 gradient store when a
+parameter carries ``_ahb_grad_acc`` (set by ``FlatParamStore``): the kernel adds
+into the accumulator and autograd sees no gradient for that weight, so no bf16
+weight-gradient tensor is materialised per micro-step.  Without an accumulator
+(plain module use) the wrapper returns an ordinary gradient.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as R
+from ._ext import ext
+
+
+def _acc_for(p: Optional[torch.Tensor]):
+    """(accumulator, owned_here) for a parameter: the store's fp32 view if any,
+    else a fresh zero fp32 buffer whose content becomes the returned gradient."""
+    if p is None:
+        return None, False
+    acc = getattr(p, "_ahb_grad_acc", None)
+    if acc is not None:
+        return acc, True
+    return torch.zeros(p.shape, dtype=torch.float32, device=p.device), False
+
+
+def _ret_grad(p, acc, direct):
+    if p is None or not p.requires_grad or direct:
+        return None
+    return acc.to(p.dtype)
+
+
+# ----------------------------------------------------------------- sanitize
+def sanitize(g: torch.Tensor, clip: float) -> torch.Tensor:
+    if g.dtype not in (torch.bfloat16, torch.float32):
+        return R.sanitize(g, clip)
+    return ext().sanitize(g, clip)
+
+
+class _SanitizeFwd(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, clip):
+        y = ext().sanitize(x, clip)
+        ctx.save_for_backward(x)
+        ctx.clip = clip
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        # d clip: pass where |x| < clip (NaN/inf inputs get no gradient)
+        mask = x.abs() < ctx.clip
+        return g * mask, None
+
+
+def sanitize_fwd(x: torch.Tensor, clip: float) -> torch.Tensor:
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        return R.sanitize(x, clip)
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _SanitizeFwd.apply(x, clip)
+    return ext().sanitize(x, clip)
+
+
+# ----------------------------------------------------------------- RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, scale, eps):
+        shp = x.shape
+        y, rstd = ext().rmsnorm_fwd(x.reshape(-1, shp[-1]), scale, eps)
+        ctx.save_for_backward(x, scale, rstd)
+        return y.view(shp)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, scale, rstd = ctx.saved_tensors
+        acc, direct = _acc_for(scale) if ctx.needs_input_grad[1] else (None, False)
+        d = x.shape[-1]
+        dx = ext().rmsnorm_bwd(dy.reshape(-1, d), x.reshape(-1, d), scale, rstd, acc)
+        return dx.view(x.shape), _ret_grad(scale, acc, direct), None
+
+
+def rmsnorm(x, scale, eps):
+    return _RMSNorm.apply(x, scale, eps)
+
+
+# ----------------------------------------------------------------- conv1d
+class _Conv1d(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, silu, clip):
+        y = ext().conv1d_fwd(x, w, b, silu, clip)
+        ctx.save_for_backward(x, w, b)
+        ctx.silu, ctx.clip = silu, clip
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, b = ctx.saved_tensors
+        wacc, wdir = _acc_for(w)
+        bacc, bdir = _acc_for(b) if b is not None else (None, False)
+        dx = ext().conv1d_bwd(x, w, b, dy.to(x.dtype), ctx.silu, ctx.clip, wacc, bacc)
+        return dx, _ret_grad(w, wacc, wdir), _ret_grad(b, bacc, bdir), None, None
+
+
+def conv1d(x, w, b, silu=True, clip=None):
+    if x.stride(-1) != 1 or x.stride(0) != x.shape[1] * x.stride(1):
+        x = x.contiguous()
+    return _Conv1d.apply(x, w, b, silu, 0.0 if clip is None else float(clip))
+
+
+# ----------------------------------------------------------------- embedding
+class _Embed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table, dtype):
+        out = ext().embedding_fwd(ids.reshape(-1), table, dtype)
+        ctx.save_for_backward(ids)
+        ctx.table = table
+        return out.view(*ids.shape, table.shape[1])
+
+    @staticmethod
+    def backward(ctx, dout):
+        (ids,) = ctx.saved_tensors
+        table = ctx.table
+        acc, direct = _acc_for(table)
+        ext().embedding_bwd_(ids.reshape(-1), dout.reshape(-1, table.shape[1]), acc)
+        return None, _ret_grad(table, acc, direct), None
+
+
+def embedding(ids, table, dtype):
+    return _Embed.apply(ids, table, dtype)
+
+
+# ----------------------------------------------------------------- not yet native
+def gdn2(q, k, v, w, b, g, scale, chunk):
+    o, _ = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
+    return o
+
+
+def ssd(dt, A, Bm, Cm, x, chunk):
+    y, _ = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
+    return y
+
+
+def attention(q, k, v, sm_scale):
+    return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=sm_scale)
+
+
+def grouped_ffn(x_sorted, group_sizes, w1, w2, w3, act):
+    dt = x_sorted.dtype
+    return R.grouped_ffn(x_sorted, group_sizes.tolist(), w1.to(dt), w2.to(dt),
+                         None if w3 is None else w3.to(dt), act)
+
+
+def cross_entropy(h, labels, weight, label_smoothing):
+    import torch.utils.checkpoint as ckpt
+    wd = weight.to(h.dtype)
+
+    def piece(hc, lc):
+        return R.label_smoothed_ce((hc @ wd.t()).float(), lc, label_smoothing)
+
+    tot = h.new_zeros((), dtype=torch.float32)
+    cnt = h.new_zeros((), dtype=torch.float32)
+    for s in range(0, h.shape[0], 4096):
+        a, c = ckpt.checkpoint(piece, h[s:s + 4096], labels[s:s + 4096], use_reentrant=False)
+        tot, cnt = tot + a, cnt + c
+    return tot, cnt
+
+
+def gdn2_layer(mod, x):
+    return _gdn2_layer_composed(mod, x)
+
+
+def _gdn2_layer_composed(mod, x):
+    Bsz, L, d = x.shape
+    H, D = mod.n_heads, mod.d_head
+    q = conv1d(mod.q_proj(x), mod.q_conv_w, mod.q_conv_b, True)
+    k = conv1d(mod.k_proj(x), mod.k_conv_w, mod.k_conv_b, True)
+    v = conv1d(mod.v_proj(x), mod.v_conv_w, mod.v_conv_b, True, 50.0)
+    q = R.safe_l2norm(q.view(Bsz, L, H, D), 1e-12)
+    k = R.safe_l2norm(k.view(Bsz, L, H, D), 1e-12)
+    from .. import ops
+    q = ops.grad_sanitize(q)
+    k = ops.grad_sanitize(k)
+    v = v.view(Bsz, L, H, D)
+    bg = torch.sigmoid(mod.erase_gate(x)).view(Bsz, L, H, D)
+    wg = torch.sigmoid(mod.write_gate(x)).view(Bsz, L, H, D)
+    f = mod.decay_proj(x).view(Bsz, L, H, D).float()
+    g = -torch.exp(mod.decay_a.float().clamp(-20.0, 20.0))[None, None, :, None] * F.softplus(f)
+    g = torch.nan_to_num(g, nan=0.0, posinf=0.0, neginf=-20.0).clamp(-1e3, 1e3)
+    og = mod.out_gate(x).clamp(-1e2, 1e2)
+    o = gdn2(q, k, v, wg, bg, g, 1.0, mod.cfg.gdn_chunk).reshape(Bsz, L, d)
+    o = rmsnorm(o, mod.out_norm.scale, 1e-6)
+    return mod.out_proj(o * F.silu(og))
+
+
+def mamba2_layer(mod, x):
+    Bsz, L, d = x.shape
+    di, Hs = mod.cfg.d_inner, mod.cfg.n_heads_ssm
+    P = di // Hs
+    xz = mod.in_proj(x)
+    x_bc, res = xz[..., :di], xz[..., di:]
+    x_conv = conv1d(x_bc, mod.conv_w, mod.conv_b, True)
+    A = -torch.exp(mod.A_log.float().clamp(-20.0, 20.0))
+    Bm = mod.B_proj(x_bc)
+    Cm = mod.C_proj(x_bc)
+    dt = F.softplus(mod.dt_proj(x_bc)).clamp(1e-2, 1.0)
+    y = ssd(dt.view(Bsz, L, Hs, P), A, Bm.clamp(-1e3, 1e3), Cm.clamp(-1e3, 1e3), x_conv.view(Bsz, L, Hs, P),
+            mod.cfg.ssd_chunk)
+    y = rmsnorm(y.reshape(Bsz, L, di).to(x_bc.dtype), mod.ssm_out_norm.scale, 1e-6)
+    out = (y * F.silu(res)).clamp(-3e2, 3e2)
+    return mod.out_proj(out)
+
+
+def moe_routed(flat, top_idx, gate, w1, w2, w3, E, act):
+    T, d = flat.shape
+    eidx = top_idx.t().reshape(-1)
+    perm = torch.argsort(eidx, stable=True)
+    sizes = torch.bincount(eidx, minlength=E)
+    rows = perm % T
+    xs = flat[rows]
+    y = grouped_ffn(xs, sizes, w1, w2, w3, act)
+    y = R.sanitize(y.float(), 1e3)
+    wgt = gate.t().reshape(-1)[perm]
+    out = torch.zeros(T, d, device=flat.device, dtype=torch.float32)
+    out.index_add_(0, rows, y * wgt[:, None])
+    return out
+
+
+def newton_schulz3(g):
+    return R.newton_schulz3(g)
+
+
+_ = math

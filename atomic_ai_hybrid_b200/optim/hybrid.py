@@ -86,6 +86,8 @@ class HybridOptimizer:
         use_k = ops.use_cuda(gbuf)
         if use_k:
             from ..ops import kernels as K
+            use_k = hasattr(K, "optim_apply")
+        if use_k:
             K.optim_prepare(self, inv, red)
         else:
             for s in self.owned:

@@ -121,6 +121,7 @@ class FlatParamStore:
         if not p.requires_grad:
             return
         g = self.grad_view(s)
+        p._ahb_grad_acc = g
         if s.fp32:
             p.grad = g
         else:

@@ -1,0 +1,28 @@
+"""Counts launches of this package's CUDA kernels (the ``gpu_launches`` figure of
+``bench.py``).  Every call into the extension is counted with the number of
+kernels that binding launches (1 unless listed in ``MULTI``)."""
+from __future__ import annotations
+
+
+class LaunchCounter:
+    MULTI = {}
+
+    def __init__(self):
+        self.count = 0
+        self.on = False
+
+    def reset(self):
+        self.count = 0
+
+    def enable(self):
+        self.on = True
+
+    def disable(self):
+        self.on = False
+
+    def add(self, name: str):
+        if self.on:
+            self.count += self.MULTI.get(name, 1)
+
+
+launch_counter = LaunchCounter()

@@ -1,0 +1,243 @@
+"""Training-throughput benchmark (train tokens/sec, whole job, max over ranks).
+
+Contract: ``python bench.py --gpus N --steps K --warmup W`` (torchrun for N>1)
+runs the flagship training step -- the hybrid GDN-2/Mamba2 MoE LM of the
+benchmark's config 3 (d_model 2048, 24 layers alternating GDN 16x128 and Mamba2
+32x64 with d_state 128, 32 routed SwiGLU experts top-4 of hidden 1024 plus one
+shared expert, vocab 50304, seq 4096), bf16 compute, fp32 master weights,
+AdamW -- on synthetic tokens with random-init weights, and rank 0 prints one
+JSON line.  Scaling is weak: every GPU processes ``--seqs-per-gpu`` sequences per
+optimizer step (32 by default, i.e. global batch 256 at 8 GPUs).
+
+``--impl cuda`` (default) runs the sm_100a kernels; ``--impl eager`` runs the
+unfused PyTorch + cuBLAS + NCCL baseline of the identical model; ``--impl
+reference`` would run the reference project itself, which cannot be installed
+on this image (its JAX/Flax/Optax/Orbax stack is absent and it has no build
+metadata), so that arm prints its ``unavailable`` line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "eager", "reference"])
+    ap.add_argument("--model", default="hybrid_1b")
+    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--seqs-per-gpu", type=int, default=32)
+    ap.add_argument("--micro-batch", type=int, default=4)
+    ap.add_argument("--layers", type=int, default=None, help="override num_layers (debug only; invalid for the bench)")
+    ap.add_argument("--optimizer", default="adamw", choices=["adamw", "hybrid"])
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples SM clocks / throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/ahb_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args, rank):
+    why = ("reference project (JAX/Flax/Optax/Orbax + Pallas-TPU kernels) is not installable offline: "
+           "/root/reference has no setup.py/pyproject.toml and jax is not in the image")
+    try:
+        sys.path.insert(0, os.path.join(HERE, "baseline", "_ref"))
+        import jax  # noqa: F401
+        import train_setup  # noqa: F401
+    except Exception:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from atomic_ai_hybrid_b200 import get_preset, ops
+    from atomic_ai_hybrid_b200.models import HybridMoEModel, count_params
+    from atomic_ai_hybrid_b200.training.trainer import Trainer
+    from atomic_ai_hybrid_b200.utils.counters import launch_counter
+
+    ops.set_impl("cuda" if args.impl == "cuda" else "eager")
+    over = {}
+    if args.layers:
+        over["num_layers"] = args.layers
+    cfg = get_preset(args.model, **over)
+    torch.manual_seed(1234)
+    with torch.device(dev):
+        model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16)
+    # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if p.ndim >= 2 and "conv_w" not in n:
+                p.normal_(0.0, 0.02)
+    model = model.to(dev)
+    nparams = count_params(model)
+    trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev)
+    trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
+
+    S, mb = args.seq_len, args.micro_batch
+    n_micro = max(1, args.seqs_per_gpu // mb)
+    seqs = n_micro * mb
+    gen = torch.Generator().manual_seed(17 + rank)
+    host_ids = torch.randint(0, cfg.vocab_size, (n_micro, mb, S + 1), generator=gen, dtype=torch.int32).pin_memory()
+    dev_ids = host_ids.to(dev)
+
+    def batches_dev():
+        return [{"input_ids": dev_ids[i, :, :-1].long(), "labels": dev_ids[i, :, 1:].long()} for i in range(n_micro)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for _ in range(args.warmup):
+        trainer.train_step(batches_dev())
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    launch_counter.reset()
+    launch_counter.enable()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        out = trainer.train_step(batches_dev())
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = launch_counter.count
+    launch_counter.disable()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tokens_step = seqs * S * world
+    value = tokens_step / (ms / 1e3)
+
+    e2e = None
+    if not args.no_e2e:
+        # end to end through the public API: per step, H2D of the step's tokens from pinned
+        # memory and D2H of the loss.
+        h2d = 0
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        e0.record()
+        for _ in range(args.steps):
+            ids = host_ids.to(dev, non_blocking=True)
+            h2d += host_ids.numel() * host_ids.element_size()
+            bs = [{"input_ids": ids[i, :, :-1].long(), "labels": ids[i, :, 1:].long()} for i in range(n_micro)]
+            out = trainer.train_step(bs)
+            _ = out["loss"].item()
+        e1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - w0) / args.steps * 1e3
+        t = torch.tensor([wall], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        wall = float(t.item())
+        e2e = {"value": tokens_step / (wall / 1e3), "unit": "tokens/s", "ms_per_step": wall,
+               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": 4,
+               "loss": float(out["loss"].item())}
+
+    if rank == 0:
+        line = {
+            "metric": "train tokens/sec (box, max over ranks)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic tokens, random-init weights",
+            "impl": args.impl,
+            "config": {"model": args.model, "global_batch": seqs * world, "seq_len": S,
+                       "micro_batch": mb, "grad_accum": n_micro, "parallelism": f"dp{world}" if world > 1 else "dp1",
+                       "sharding": "param/optimizer owner-sharded, bf16 weights resident",
+                       "optimizer": args.optimizer, "params_total": nparams["total"],
+                       "num_layers": cfg.num_layers,
+                       "l2": "inputs larger than L2 (11+ GB of weights streamed per micro-step)"},
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
