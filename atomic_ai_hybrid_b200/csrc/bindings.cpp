@@ -128,6 +128,141 @@ void embedding_bwd_(torch::Tensor ids, torch::Tensor dout, torch::Tensor acc) {
                     (int)acc.size(1), acc.size(0), cur_stream());
 }
 
+
+// ------------------------------------------------------------ GDN-2
+void check_gdn(const torch::Tensor& t, at::ScalarType dt, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == dt && t.dim() == 4, "gdn2: ", n,
+              " must be a contiguous (B,L,H,128) CUDA tensor of type ", dt);
+}
+
+struct GdnShapes { int B, L, H, NC; };
+
+GdnShapes gdn_shapes(const torch::Tensor& q) {
+  int B = (int)q.size(0), L = (int)q.size(1), H = (int)q.size(2), D = (int)q.size(3);
+  TORCH_CHECK(ahb_gdn_supported(D) == 64, "gdn2: head dim must be 128");
+  TORCH_CHECK(L % 64 == 0, "gdn2: sequence length must be a multiple of 64");
+  return {B, L, H, L / 64};
+}
+
+std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                   torch::Tensor bg, torch::Tensor wg, double scale, bool want_state) {
+  for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
+  check_gdn(g, at::kFloat, "g");
+  auto s = gdn_shapes(q);
+  auto bf = q.options();
+  auto f32 = q.options().dtype(at::kFloat);
+  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
+  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
+  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
+  auto st = cur_stream();
+  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
+                    (float)scale, s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(),
+                    aqk.data_ptr<float>(), gcl.data_ptr<float>(), nullptr, st);
+  auto o = torch::empty_like(q);
+  torch::Tensor hf;
+  if (want_state) hf = torch::empty({s.B, s.H, 128, 128}, f32);
+  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(),
+                    want_state ? hf.data_ptr<float>() : nullptr, nullptr, nullptr, st);
+  if (want_state) return {o, hf};
+  return {o};
+}
+
+std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                   torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale) {
+  auto s = gdn_shapes(q);
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  auto bf = q.options();
+  auto f32 = q.options().dtype(at::kFloat);
+  auto st = cur_stream();
+  const float sc = (float)scale;
+  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
+  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
+  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  auto A = torch::empty_like(aqk);
+  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
+  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), sc,
+                    s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), A.data_ptr<float>(), st);
+  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
+  auto vn = torch::empty_like(wt);
+  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, nullptr, nullptr, hs.data_ptr(), vn.data_ptr(),
+                    st);
+  auto dhs = torch::empty_like(hs);
+  auto dvn = torch::empty_like(wt);
+  ahb_gdn_inter_bwd(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(), gcl.data_ptr<float>(),
+                    doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr, st);
+  u = torch::Tensor(); qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor();
+  auto dq_p = torch::empty({s.B, s.H, s.NC, 64, 128}, f32);
+  auto dk_p = torch::empty_like(dq_p), dgc_p = torch::empty_like(dq_p), dwt = torch::empty_like(dq_p);
+  auto dgcl = torch::empty_like(gcl);
+  auto daqk = torch::empty_like(aqk);
+  ahb_gdn_bwd_states(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), doc.data_ptr(), hs.data_ptr(), dhs.data_ptr(),
+                     vn.data_ptr(), dvn.data_ptr(), sc, s.B, s.L, s.H, dq_p.data_ptr<float>(),
+                     dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(), dwt.data_ptr<float>(), dgcl.data_ptr<float>(),
+                     daqk.data_ptr<float>(), st);
+  hs = torch::Tensor(); dhs = torch::Tensor(); vn = torch::Tensor();
+  auto dv = torch::empty_like(q), dw = torch::empty_like(q);
+  auto dbk_wy = torch::empty_like(dq_p), dgc_wy = torch::empty_like(dq_p);
+  auto dakk = torch::empty_like(aqk);
+  ahb_gdn_bwd_wy(k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), A.data_ptr<float>(),
+                 dvn.data_ptr(), dwt.data_ptr<float>(), s.B, s.L, s.H, dv.data_ptr(), dw.data_ptr(),
+                 dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dakk.data_ptr<float>(), st);
+  auto dq = torch::empty_like(q), dk = torch::empty_like(q), db = torch::empty_like(q);
+  auto dg = torch::empty_like(g);
+  ahb_gdn_bwd_intra(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), daqk.data_ptr<float>(),
+                    dakk.data_ptr<float>(), dq_p.data_ptr<float>(), dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(),
+                    dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dgcl.data_ptr<float>(), sc, s.B, s.L, s.H,
+                    dq.data_ptr(), dk.data_ptr(), db.data_ptr(), dg.data_ptr<float>(), st);
+  return {dq, dk, dv, dg, db, dw};
+}
+
+// ------------------------------------------------------------ Mamba2 SSD
+void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Tensor& A, const torch::Tensor& Bm,
+               const torch::Tensor& Cm) {
+  for (auto* t : {&x, &dt, &Bm, &Cm})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                "ssd: x, dt, B, C must be contiguous bf16 CUDA tensors");
+  TORCH_CHECK(x.dim() == 4 && dt.sizes() == x.sizes(), "ssd: x, dt must be (B,L,H,64)");
+  TORCH_CHECK(ahb_ssd_supported((int)x.size(3), (int)Bm.size(2)) == 64, "ssd: head dim 64 and d_state 128 only");
+  TORCH_CHECK(x.size(1) % 64 == 0, "ssd: L must be a multiple of 64");
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kFloat && A.numel() == x.size(2), "ssd: A must be fp32 (H,)");
+  TORCH_CHECK(Bm.dim() == 3 && Bm.sizes() == Cm.sizes() && Bm.size(0) == x.size(0) && Bm.size(1) == x.size(1),
+              "ssd: B, C must be (B,L,128)");
+}
+
+torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm, torch::Tensor Cm) {
+  check_ssd(x, dt, A, Bm, Cm);
+  int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
+  auto f32 = x.options().dtype(at::kFloat);
+  auto sbuf = torch::empty({B, H, NC, 64, 128}, f32);
+  auto cuml = torch::empty({B, H, NC, 64}, f32);
+  auto y = torch::empty_like(x);
+  ahb_ssd_fwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
+              sbuf.data_ptr<float>(), cuml.data_ptr<float>(), nullptr, nullptr, y.data_ptr(), cur_stream());
+  return y;
+}
+
+std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
+                                   torch::Tensor Cm, torch::Tensor dy) {
+  check_ssd(x, dt, A, Bm, Cm);
+  int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
+  auto dyc = dy.to(at::kBFloat16).contiguous();
+  auto f32 = x.options().dtype(at::kFloat);
+  auto sbuf = torch::empty({B, H, NC, 64, 128}, f32);
+  auto gbuf = torch::empty_like(sbuf);
+  auto cuml = torch::empty({B, H, NC, 64}, f32);
+  auto dx = torch::empty_like(x), ddt = torch::empty_like(x);
+  auto dB = torch::empty(Bm.sizes(), f32), dC = torch::empty(Cm.sizes(), f32);
+  auto dA = torch::zeros({H}, f32);
+  ahb_ssd_bwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B, L,
+              H, sbuf.data_ptr<float>(), cuml.data_ptr<float>(), gbuf.data_ptr<float>(), dx.data_ptr(),
+              ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), cur_stream());
+  return {dx, ddt, dA, dB, dC};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -140,4 +275,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("accumulate_", &accumulate_);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd_", &embedding_bwd_);
+  m.def("gdn_fwd", &gdn_fwd);
+  m.def("gdn_bwd", &gdn_bwd);
+  m.def("ssd_fwd", &ssd_fwd);
+  m.def("ssd_bwd", &ssd_bwd);
 }

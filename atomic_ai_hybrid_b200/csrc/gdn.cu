@@ -1,0 +1,898 @@
+// GDN-2 chunked gated delta rule with per-channel gates (head dim 128, chunk 64).
+//
+// Recurrence per token (reference `atomic_ops/gdn2_wy_reference.py:33-56`):
+//   h <- diag(e^g) h ; v' = w*v - (b*k)^T h ; h += k v'^T ; o = h^T (q*scale)
+// Chunked WY form (reference kernels A/B/C/D, `atomic_ops/kernel_{a,b,c,d}_*.py`):
+//   gc = cumsum_t g                       (per channel, within the chunk)
+//   Aqk[i,j] = scale sum_d q_id k_jd e^{gc_id-gc_jd}   (i >= j)
+//   Akk[i,j] =       sum_d (bk)_id k_jd e^{gc_id-gc_jd} (i > j)
+//   A = (I + Akk)^-1 ; w~ = A (bk e^gc) ; u = A (w v)
+//   v_new = u - w~ h ; o = scale (q e^gc) h + Aqk v_new
+//   h' = diag(e^{gc_last}) h + (k e^{gc_last-gc})^T v_new
+//
+// Design for sm_100a: one CTA per (chunk, head, batch) computes everything that
+// is chunk-local (parallel over all chunks); a second kernel runs the
+// sequential state recurrence with one CTA per (value block of 32, head,
+// batch), the state slice living in registers.  Pairwise decays use a
+// reference row r between j and i (r = first row of i's 16-row block), so both
+// factors e^{gc_i-gc_r} and e^{gc_r-gc_j} are <= 1 and the products run on the
+// tensor cores without overflow; the four 16x16 diagonal blocks are summed
+// exactly per channel (with the reference's -20 floor on the exponent).
+// The inverse (I+Akk)^-1 is blocked: 16x16 diagonal inverses by substitution,
+// then the off-diagonal blocks by distance.
+//
+// Backward (reference B1..B6, `atomic_ops/kernel_bwd_b*.py`, `kernel_trainable_B6.py`):
+//   gdn_intra_fwd (recompute, also stores A) -> gdn_inter_fwd (stores h, v_new)
+//   -> gdn_inter_bwd (reverse recurrence: dh per chunk, dv_new)
+//   -> gdn_bwd_states (products with h/dh: qg/kg chains, dw~, dAqk)
+//   -> gdn_bwd_wy (through A: dw, dv, d(bk), dAkk)
+//   -> gdn_bwd_intra (through Aqk/Akk + assembly + reverse cumsum for dg).
+#include "common.cuh"
+#include "mma.cuh"
+#include "launchers.h"
+
+using namespace ahb;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int C = 64;       // chunk length
+constexpr int D = 128;      // head dim (dk = dv)
+constexpr int LDB = D + 8;  // bf16 row stride of C x D tiles
+constexpr int LDF = D + 4;  // fp32 row stride of C x D tiles
+constexpr int LDC = C + 4;  // fp32 row stride of C x C tiles
+constexpr int BV = 32;      // value-block width of the recurrence kernels
+constexpr int LDV = BV + 8;
+
+AHB_DEVICE float bf(bf16 x) { return __bfloat162float(x); }
+AHB_DEVICE float guard(float x) {  // nan_to_num(nan=0, +-inf -> +-1e4)
+  if (x != x) return 0.f;
+  return fminf(fmaxf(x, -1e4f), 1e4f);
+}
+
+// row index helpers
+struct Idx {
+  int64_t L, H, NC;
+  AHB_DEVICE int64_t seq(int b, int64_t t, int h) const { return ((b * L + t) * H + h) * D; }  // (B,L,H,D)
+  AHB_DEVICE int64_t chunk(int b, int h, int n) const { return ((int64_t)b * H + h) * NC + n; }
+};
+
+// Load a C x D bf16 tile of a (B,L,H,D) tensor into smem (row stride LDB).
+AHB_DEVICE void load_seq_tile(bf16* dst, const bf16* src, const Idx& ix, int b, int n, int h, int nthreads) {
+  for (int i = threadIdx.x; i < C * (D / 8); i += nthreads) {
+    int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
+    *reinterpret_cast<uint4*>(dst + r * LDB + c8) =
+        *reinterpret_cast<const uint4*>(src + ix.seq(b, (int64_t)n * C + r, h) + c8);
+  }
+}
+// Load g (fp32, (B,L,H,D)) chunk and write its inclusive cumsum over rows into gc (stride LDF).
+AHB_DEVICE void load_gc(float* gc, const float* g, const Idx& ix, int b, int n, int h, int nthreads) {
+  for (int i = threadIdx.x; i < C * (D / 4); i += nthreads) {
+    int r = i / (D / 4), c4 = (i % (D / 4)) * 4;
+    *reinterpret_cast<float4*>(gc + r * LDF + c4) =
+        *reinterpret_cast<const float4*>(g + ix.seq(b, (int64_t)n * C + r, h) + c4);
+  }
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) {
+      s += gc[r * LDF + threadIdx.x];
+      gc[r * LDF + threadIdx.x] = s;
+    }
+  }
+  __syncthreads();
+}
+// contiguous C x D tile (chunk-major tensors) -> smem
+AHB_DEVICE void load_chunk_tile(bf16* dst, const bf16* src, int nthreads) {
+  for (int i = threadIdx.x; i < C * (D / 8); i += nthreads) {
+    int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
+    *reinterpret_cast<uint4*>(dst + r * LDB + c8) = *reinterpret_cast<const uint4*>(src + r * D + c8);
+  }
+}
+AHB_DEVICE void load_chunk_tile_f32(float* dst, int ld, const float* src, int rows, int cols, int nthreads) {
+  for (int i = threadIdx.x; i < rows * (cols / 4); i += nthreads) {
+    int r = i / (cols / 4), c4 = (i % (cols / 4)) * 4;
+    *reinterpret_cast<float4*>(dst + r * ld + c4) = *reinterpret_cast<const float4*>(src + r * cols + c4);
+  }
+}
+
+// Store an accumulator tile (NT n-tiles) as bf16 pairs: dst[row*ld + col]
+template <int NT, class F>
+AHB_DEVICE void store_pairs(float (*acc)[4], int m0, int n0, F&& put) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int c = n0 + 8 * j + 2 * t;
+    put(m0 + g, c, acc[j][0], acc[j][1]);
+    put(m0 + g + 8, c, acc[j][2], acc[j][3]);
+  }
+}
+
+AHB_DEVICE void st_bf16x2(bf16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack2(a, b); }
+
+// 16x16 block pair enumeration below the diagonal: p -> (I, J), J < I
+AHB_DEVICE void pair_ij(int p, int& I, int& J) {
+  I = p < 1 ? 1 : (p < 3 ? 2 : 3);
+  J = p - I * (I - 1) / 2;
+}
+// triangular pair index -> (i, j), i >= j, within 16
+AHB_DEVICE void tri_ij(int p, int& i, int& j) {
+  i = (int)((sqrtf(8.f * p + 1.f) - 1.f) * 0.5f);
+  while ((i + 1) * (i + 2) / 2 <= p) ++i;
+  while (i * (i + 1) / 2 > p) --i;
+  j = p - i * (i + 1) / 2;
+}
+
+// ============================================================ intra forward
+// smem: q,k,bk,wv,bke bf16 [C][LDB]; gc f32 [C][LDF]; aqk, akk, a f32 [C][LDC]; t 768 f32
+constexpr size_t SMEM_INTRA = 5 * C * LDB * 2 + C * LDF * 4 + 3 * C * LDC * 4 + 768 * 4;
+
+__global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+    const float* __restrict__ g, const bf16* __restrict__ bg, const bf16* __restrict__ wg, float scale, int L,
+    int H, bf16* __restrict__ wt_o, bf16* __restrict__ u_o, bf16* __restrict__ qg_o, bf16* __restrict__ kg_o,
+    float* __restrict__ aqk_o, float* __restrict__ gcl_o, float* __restrict__ a_o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* q_s = reinterpret_cast<bf16*>(smem);
+  bf16* k_s = q_s + C * LDB;
+  bf16* bk_s = k_s + C * LDB;
+  bf16* wv_s = bk_s + C * LDB;
+  bf16* bke_s = wv_s + C * LDB;
+  float* gc_s = reinterpret_cast<float*>(bke_s + C * LDB);
+  float* aqk_s = gc_s + C * LDF;
+  float* akk_s = aqk_s + C * LDC;
+  float* a_s = akk_s + C * LDC;
+  float* t_s = a_s + C * LDC;
+
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // 1. loads (q, k raw; bk = b*k, wv = w*v)
+  for (int i = tid; i < C * (D / 8); i += 256) {
+    int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
+    int64_t gi = ix.seq(b, (int64_t)n * C + r, h) + c8;
+    uint4 qv = *reinterpret_cast<const uint4*>(q + gi);
+    uint4 kv = *reinterpret_cast<const uint4*>(k + gi);
+    uint4 vv = *reinterpret_cast<const uint4*>(v + gi);
+    uint4 bv = *reinterpret_cast<const uint4*>(bg + gi);
+    uint4 wv = *reinterpret_cast<const uint4*>(wg + gi);
+    *reinterpret_cast<uint4*>(q_s + r * LDB + c8) = qv;
+    *reinterpret_cast<uint4*>(k_s + r * LDB + c8) = kv;
+    const bf16* kp = reinterpret_cast<const bf16*>(&kv);
+    const bf16* vp = reinterpret_cast<const bf16*>(&vv);
+    const bf16* bp = reinterpret_cast<const bf16*>(&bv);
+    const bf16* wp = reinterpret_cast<const bf16*>(&wv);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      st_bf16x2(bk_s + r * LDB + c8 + e, bf(bp[e]) * bf(kp[e]), bf(bp[e + 1]) * bf(kp[e + 1]));
+      st_bf16x2(wv_s + r * LDB + c8 + e, bf(wp[e]) * bf(vp[e]), bf(wp[e + 1]) * bf(vp[e + 1]));
+    }
+  }
+  load_gc(gc_s, g, ix, b, n, h, 256);  // includes __syncthreads
+
+  // 2. bke = bk * e^gc
+  for (int i = tid; i < C * D; i += 256) {
+    int r = i / D, d = i % D;
+    bke_s[r * LDB + d] = __float2bfloat16_rn(bf(bk_s[r * LDB + d]) * __expf(gc_s[r * LDF + d]));
+  }
+  // 3a. off-diagonal 16x16 blocks of Aqk / Akk on tensor cores
+  for (int job = warp; job < 12; job += 8) {
+    int I, J;
+    pair_ij(job >> 1, I, J);
+    const bool is_kk = job & 1;
+    const int r0 = 16 * I;
+    const float* gr = gc_s + r0 * LDF;
+    const bf16* xs = is_kk ? bk_s : q_s;
+    auto fa = [&](int rr, int cc) -> uint32_t {
+      const float* gi = gc_s + (r0 + rr) * LDF;
+      return pack2(bf(xs[(r0 + rr) * LDB + cc]) * __expf(gi[cc] - gr[cc]),
+                   bf(xs[(r0 + rr) * LDB + cc + 1]) * __expf(gi[cc + 1] - gr[cc + 1]));
+    };
+    auto fb = [&](int kd, int nj) -> uint32_t {
+      const int j = 16 * J + nj;
+      const float* gj = gc_s + j * LDF;
+      return pack2(bf(k_s[j * LDB + kd]) * __expf(gr[kd] - gj[kd]),
+                   bf(k_s[j * LDB + kd + 1]) * __expf(gr[kd + 1] - gj[kd + 1]));
+    };
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2>(acc, fa, fb, 0, 0, 0, D);
+    float* dst = is_kk ? akk_s : aqk_s;
+    const float sc = is_kk ? 1.f : scale;
+    for_acc<2>(acc, 0, 0, [&](int rr, int cc, float& val) { dst[(r0 + rr) * LDC + 16 * J + cc] = guard(val * sc); });
+  }
+  // 3b. diagonal blocks, exact per-channel sums (-20 floor on the exponent, as the reference)
+  for (int p = warp; p < 4 * 136; p += 8) {
+    int blk = p / 136, i, j;
+    tri_ij(p % 136, i, j);
+    const int ri = 16 * blk + i, rj = 16 * blk + j;
+    float sq = 0.f, sk = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      float e = __expf(fmaxf(gc_s[ri * LDF + d] - gc_s[rj * LDF + d], -20.f));
+      float kj = bf(k_s[rj * LDB + d]) * e;
+      sq += bf(q_s[ri * LDB + d]) * kj;
+      sk += bf(bk_s[ri * LDB + d]) * kj;
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    if (lane == 0) {
+      aqk_s[ri * LDC + rj] = guard(sq * scale);
+      akk_s[ri * LDC + rj] = i > j ? guard(sk) : 0.f;
+    }
+  }
+  // upper parts are zero
+  for (int i = tid; i < C * C; i += 256) {
+    int r = i / C, c = i % C;
+    if (c > r) { aqk_s[r * LDC + c] = 0.f; akk_s[r * LDC + c] = 0.f; }
+    if ((c >> 4) != (r >> 4)) a_s[r * LDC + c] = 0.f;
+  }
+  __syncthreads();
+
+  // 4a. inverses of the 16x16 diagonal blocks of I + Akk
+  if (warp < 4) {
+    const int base = 16 * warp;
+    for (int i = 0; i < 16; ++i) {
+      float x = 0.f;
+      if (lane < 16) {
+        x = lane == i ? 1.f : 0.f;
+        for (int j = lane; j < i; ++j) x -= akk_s[(base + i) * LDC + base + j] * a_s[(base + j) * LDC + base + lane];
+      }
+      __syncwarp();
+      if (lane < 16) a_s[(base + i) * LDC + base + lane] = lane <= i ? x : 0.f;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // 4b. off-diagonal blocks by distance: X_IJ = -X_II sum_{K=J}^{I-1} S_IK X_KJ
+  for (int dist = 1; dist < 4; ++dist) {
+    const int np = 4 - dist;
+    for (int e = tid; e < np * 256; e += 256) {
+      int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
+      int J = p, I = p + dist;
+      float s = 0.f;
+      for (int K = J; K < I; ++K)
+#pragma unroll 4
+        for (int kk = 0; kk < 16; ++kk)
+          s += akk_s[(16 * I + ii) * LDC + 16 * K + kk] * a_s[(16 * K + kk) * LDC + 16 * J + cc];
+      t_s[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < np * 256; e += 256) {
+      int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
+      int J = p, I = p + dist;
+      float s = 0.f;
+      for (int m = 0; m <= ii; ++m) s += a_s[(16 * I + ii) * LDC + 16 * I + m] * t_s[(p << 8) + (m << 4) + cc];
+      a_s[(16 * I + ii) * LDC + 16 * J + cc] = guard(-s);
+    }
+    __syncthreads();
+  }
+
+  // 5. w~ = A bke, u = A wv  (warp: 16-row tile mt, 64-col half nh)
+  const int64_t cb = ix.chunk(b, h, n);
+  {
+    const int mt = warp & 3, nh = warp >> 2;
+    float accw[8][4], accu[8][4];
+    zero_acc<8>(accw);
+    zero_acc<8>(accu);
+    RowA32 fa{a_s, LDC};
+    KNB16 fbk{bke_s, LDB}, fbv{wv_s, LDB};
+    for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 16) {
+      uint32_t a[4];
+      load_a(a, fa, 16 * mt, k0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t bb[2];
+        load_b(bb, fbk, k0, 64 * nh + 8 * j);
+        mma16816(accw[j], a, bb);
+        load_b(bb, fbv, k0, 64 * nh + 8 * j);
+        mma16816(accu[j], a, bb);
+      }
+    }
+    bf16* wto = wt_o + cb * C * D;
+    bf16* uo = u_o + cb * C * D;
+    store_pairs<8>(accw, 16 * mt, 64 * nh, [&](int r, int c, float x0, float x1) {
+      st_bf16x2(wto + r * D + c, guard(x0), guard(x1));
+    });
+    store_pairs<8>(accu, 16 * mt, 64 * nh, [&](int r, int c, float x0, float x1) {
+      st_bf16x2(uo + r * D + c, guard(x0), guard(x1));
+    });
+  }
+  // 6. qg, kg, gc_last, Aqk (and A) out
+  for (int i = tid; i < C * D / 2; i += 256) {
+    int r = (2 * i) / D, d = (2 * i) % D;
+    float g0 = gc_s[r * LDF + d], g1 = gc_s[r * LDF + d + 1];
+    float l0 = gc_s[(C - 1) * LDF + d], l1 = gc_s[(C - 1) * LDF + d + 1];
+    st_bf16x2(qg_o + cb * C * D + r * D + d, bf(q_s[r * LDB + d]) * __expf(g0), bf(q_s[r * LDB + d + 1]) * __expf(g1));
+    st_bf16x2(kg_o + cb * C * D + r * D + d, bf(k_s[r * LDB + d]) * __expf(l0 - g0),
+              bf(k_s[r * LDB + d + 1]) * __expf(l1 - g1));
+  }
+  if (tid < D) gcl_o[cb * D + tid] = gc_s[(C - 1) * LDF + tid];
+  for (int i = tid; i < C * C; i += 256) {
+    int r = i / C, c = i % C;
+    aqk_o[cb * C * C + i] = aqk_s[r * LDC + c];
+    if (a_o) a_o[cb * C * C + i] = a_s[r * LDC + c];
+  }
+}
+
+// ============================================================ inter forward
+// smem: wt, qg, kg bf16 [C][LDB]; u bf16 [C][LDV]; aqk f32 [C][LDC]; h bf16 [D][LDV]; vn bf16 [C][LDV]; gcl f32 [D]
+constexpr size_t SMEM_INTER_F = 3 * C * LDB * 2 + C * LDV * 2 + C * LDC * 4 + D * LDV * 2 + C * LDV * 2 + D * 4;
+
+__global__ void __launch_bounds__(128) gdn_inter_fwd_kernel(
+    const bf16* __restrict__ wt, const bf16* __restrict__ u, const bf16* __restrict__ qg,
+    const bf16* __restrict__ kg, const float* __restrict__ aqk, const float* __restrict__ gcl, float scale, int L,
+    int H, int NC, const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final,
+    bf16* __restrict__ h_store, bf16* __restrict__ vn_store) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* wt_s = reinterpret_cast<bf16*>(smem);
+  bf16* qg_s = wt_s + C * LDB;
+  bf16* kg_s = qg_s + C * LDB;
+  bf16* u_s = kg_s + C * LDB;
+  float* aqk_s = reinterpret_cast<float*>(u_s + C * LDV);
+  bf16* h_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
+  bf16* vn_s = h_s + D * LDV;
+  float* gcl_s = reinterpret_cast<float*>(vn_s + C * LDV);
+
+  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, w = tid >> 5;
+  // state slice: rows d in [32w, 32w+32) (2 m-tiles), cols [0, 32) of this value block
+  float hr[2][4][4];
+  for (int mi = 0; mi < 2; ++mi)
+    for_acc<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
+      x = h0 ? h0[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
+    });
+  for (int n = 0; n < NC; ++n) {
+    const int64_t cb = ix.chunk(b, h, n);
+    for (int mi = 0; mi < 2; ++mi)
+      store_pairs<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
+        st_bf16x2(h_s + r * LDV + c, x0, x1);
+        if (h_store) st_bf16x2(h_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
+      });
+    load_chunk_tile(wt_s, wt + cb * C * D, 128);
+    load_chunk_tile(qg_s, qg + cb * C * D, 128);
+    load_chunk_tile(kg_s, kg + cb * C * D, 128);
+    for (int i = tid; i < C * (BV / 8); i += 128) {
+      int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
+      *reinterpret_cast<uint4*>(u_s + r * LDV + c8) =
+          *reinterpret_cast<const uint4*>(u + cb * C * D + r * D + vb * BV + c8);
+    }
+    load_chunk_tile_f32(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
+    if (tid < D) gcl_s[tid] = gcl[cb * D + tid];
+    __syncthreads();
+    float accv[4][4], acco[4][4];
+    zero_acc<4>(accv);
+    zero_acc<4>(acco);
+    warp_mma<4>(accv, RowA16{wt_s, LDB}, KNB16{h_s, LDV}, 16 * w, 0, 0, D);
+    if (o) warp_mma<4>(acco, RowA16{qg_s, LDB}, KNB16{h_s, LDV}, 16 * w, 0, 0, D);
+    store_pairs<4>(accv, 16 * w, 0, [&](int r, int c, float x0, float x1) {
+      float v0 = bf(u_s[r * LDV + c]) - x0, v1 = bf(u_s[r * LDV + c + 1]) - x1;
+      st_bf16x2(vn_s + r * LDV + c, v0, v1);
+      if (vn_store) st_bf16x2(vn_store + cb * C * D + r * D + vb * BV + c, v0, v1);
+    });
+    __syncthreads();
+    if (o) {
+      for_acc<4>(acco, 0, 0, [&](int, int, float& x) { x *= scale; });
+      warp_mma<4>(acco, RowA32{aqk_s, LDC}, KNB16{vn_s, LDV}, 16 * w, 0, 0, 16 * (w + 1));
+      store_pairs<4>(acco, 16 * w, 0, [&](int r, int c, float x0, float x1) {
+        st_bf16x2(o + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c, guard(x0), guard(x1));
+      });
+    }
+    for (int mi = 0; mi < 2; ++mi) {
+      const int d0 = 32 * w + 16 * mi;
+      for_acc<4>(hr[mi], d0, 0, [&](int r, int, float& x) { x *= __expf(gcl_s[r]); });
+      warp_mma<4>(hr[mi], ColA16{kg_s, LDB}, KNB16{vn_s, LDV}, d0, 0, 0, C);
+      for_acc<4>(hr[mi], d0, 0, [&](int, int, float& x) { x = sanitize(x, 1e4f); });
+    }
+    __syncthreads();
+  }
+  if (h_final)
+    for (int mi = 0; mi < 2; ++mi)
+      for_acc<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
+        h_final[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] = x;
+      });
+}
+
+// ============================================================ inter backward (reverse recurrence)
+// smem: wt, qg, kg bf16 [C][LDB]; aqk f32 [C][LDC]; do bf16 [C][LDV]; dh bf16 [D][LDV]; dvn bf16 [C][LDV]; gcl f32[D]
+constexpr size_t SMEM_INTER_B = 3 * C * LDB * 2 + C * LDC * 4 + C * LDV * 2 + D * LDV * 2 + C * LDV * 2 + D * 4;
+
+__global__ void __launch_bounds__(128) gdn_inter_bwd_kernel(
+    const bf16* __restrict__ wt, const bf16* __restrict__ qg, const bf16* __restrict__ kg,
+    const float* __restrict__ aqk, const float* __restrict__ gcl, const bf16* __restrict__ dout, float scale, int L,
+    int H, int NC, const float* __restrict__ dh_final, bf16* __restrict__ dh_store, bf16* __restrict__ dvn_store,
+    float* __restrict__ dh0) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* wt_s = reinterpret_cast<bf16*>(smem);
+  bf16* qg_s = wt_s + C * LDB;
+  bf16* kg_s = qg_s + C * LDB;
+  float* aqk_s = reinterpret_cast<float*>(kg_s + C * LDB);
+  bf16* do_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
+  bf16* dh_s = do_s + C * LDV;
+  bf16* dvn_s = dh_s + D * LDV;
+  float* gcl_s = reinterpret_cast<float*>(dvn_s + C * LDV);
+
+  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, w = tid >> 5;
+  float dr[2][4][4];
+  for (int mi = 0; mi < 2; ++mi)
+    for_acc<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
+      x = dh_final ? dh_final[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
+    });
+  for (int n = NC - 1; n >= 0; --n) {
+    const int64_t cb = ix.chunk(b, h, n);
+    for (int mi = 0; mi < 2; ++mi)
+      store_pairs<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
+        st_bf16x2(dh_s + r * LDV + c, x0, x1);
+        st_bf16x2(dh_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
+      });
+    load_chunk_tile(wt_s, wt + cb * C * D, 128);
+    load_chunk_tile(qg_s, qg + cb * C * D, 128);
+    load_chunk_tile(kg_s, kg + cb * C * D, 128);
+    load_chunk_tile_f32(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
+    for (int i = tid; i < C * (BV / 8); i += 128) {
+      int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
+      *reinterpret_cast<uint4*>(do_s + r * LDV + c8) =
+          *reinterpret_cast<const uint4*>(dout + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c8);
+    }
+    if (tid < D) gcl_s[tid] = gcl[cb * D + tid];
+    __syncthreads();
+    // dv_new = Aqk^T do + kg dh
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, ColA32{aqk_s, LDC}, KNB16{do_s, LDV}, 16 * w, 0, 16 * w, C);
+    warp_mma<4>(acc, RowA16{kg_s, LDB}, KNB16{dh_s, LDV}, 16 * w, 0, 0, D);
+    store_pairs<4>(acc, 16 * w, 0, [&](int r, int c, float x0, float x1) {
+      st_bf16x2(dvn_s + r * LDV + c, x0, x1);
+      st_bf16x2(dvn_store + cb * C * D + r * D + vb * BV + c, x0, x1);
+    });
+    __syncthreads();
+    // dh_prev = e^{gcl} dh + scale qg^T do - wt^T dv_new
+    for (int mi = 0; mi < 2; ++mi) {
+      const int d0 = 32 * w + 16 * mi;
+      float t1[4][4], t2[4][4];
+      zero_acc<4>(t1);
+      zero_acc<4>(t2);
+      warp_mma<4>(t1, ColA16{qg_s, LDB}, KNB16{do_s, LDV}, d0, 0, 0, C);
+      warp_mma<4>(t2, ColA16{wt_s, LDB}, KNB16{dvn_s, LDV}, d0, 0, 0, C);
+      const int lane = tid & 31, gq = lane >> 2;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float e0 = __expf(gcl_s[d0 + gq]), e1 = __expf(gcl_s[d0 + gq + 8]);
+        dr[mi][j][0] = dr[mi][j][0] * e0 + scale * t1[j][0] - t2[j][0];
+        dr[mi][j][1] = dr[mi][j][1] * e0 + scale * t1[j][1] - t2[j][1];
+        dr[mi][j][2] = dr[mi][j][2] * e1 + scale * t1[j][2] - t2[j][2];
+        dr[mi][j][3] = dr[mi][j][3] * e1 + scale * t1[j][3] - t2[j][3];
+      }
+    }
+    __syncthreads();
+  }
+  if (dh0)
+    for (int mi = 0; mi < 2; ++mi)
+      for_acc<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
+        dh0[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] = x;
+      });
+}
+
+// ============================================================ backward: products with the states
+// smem: h, dh bf16 [D][LDB]; do, vn, dvn, q, k bf16 [C][LDB]; gc f32 [C][LDF]; red f32 [D]
+constexpr size_t SMEM_BWD_STATES = 2 * D * LDB * 2 + 5 * C * LDB * 2 + C * LDF * 4 + D * 4;
+
+__global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
+    const bf16* __restrict__ dout, const bf16* __restrict__ h_store, const bf16* __restrict__ dh_store,
+    const bf16* __restrict__ vn_store, const bf16* __restrict__ dvn_store, float scale, int L, int H,
+    float* __restrict__ dq_p, float* __restrict__ dk_p, float* __restrict__ dgc_p, float* __restrict__ dwt_o,
+    float* __restrict__ dgcl_o, float* __restrict__ daqk_o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* h_s = reinterpret_cast<bf16*>(smem);
+  bf16* dh_s = h_s + D * LDB;
+  bf16* do_s = dh_s + D * LDB;
+  bf16* vn_s = do_s + C * LDB;
+  bf16* dvn_s = vn_s + C * LDB;
+  bf16* q_s = dvn_s + C * LDB;
+  bf16* k_s = q_s + C * LDB;
+  float* gc_s = reinterpret_cast<float*>(k_s + C * LDB);
+  float* red_s = gc_s + C * LDF;
+
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t cb = ix.chunk(b, h, n);
+  for (int i = tid; i < D * (D / 8); i += 256) {
+    int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
+    *reinterpret_cast<uint4*>(h_s + r * LDB + c8) = *reinterpret_cast<const uint4*>(h_store + cb * D * D + r * D + c8);
+    *reinterpret_cast<uint4*>(dh_s + r * LDB + c8) =
+        *reinterpret_cast<const uint4*>(dh_store + cb * D * D + r * D + c8);
+  }
+  load_seq_tile(do_s, dout, ix, b, n, h, 256);
+  load_seq_tile(q_s, q, ix, b, n, h, 256);
+  load_seq_tile(k_s, k, ix, b, n, h, 256);
+  load_chunk_tile(vn_s, vn_store + cb * C * D, 256);
+  load_chunk_tile(dvn_s, dvn_store + cb * C * D, 256);
+  if (tid < D) red_s[tid] = 0.f;
+  load_gc(gc_s, g, ix, b, n, h, 256);
+
+  const int mt = warp & 3, nh = warp >> 2;
+  const int m0 = 16 * mt, n0 = 64 * nh;
+  float acc[8][4], dg[8][4];
+  zero_acc<8>(dg);
+  // P1 = do h^T  -> dq_p = scale P1 e^gc ; dgc += dq_p q
+  zero_acc<8>(acc);
+  warp_mma<8>(acc, RowA16{do_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
+  {
+    const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+        float x = scale * acc[j][e] * __expf(gc_s[r * LDF + c]);
+        dq_p[cb * C * D + r * D + c] = x;
+        dg[j][e] += x * bf(q_s[r * LDB + c]);
+      }
+  }
+  // P2 = vn dh^T -> dk_p = P2 e^{gcl-gc}; dgc -= P2 kg; dgcl += P2 kg
+  zero_acc<8>(acc);
+  warp_mma<8>(acc, RowA16{vn_s, LDB}, NKB16{dh_s, LDB}, m0, n0, 0, D);
+  {
+    const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+        float ex = __expf(gc_s[(C - 1) * LDF + c] - gc_s[r * LDF + c]);
+        float x = acc[j][e];
+        dk_p[cb * C * D + r * D + c] = x * ex;
+        float t2 = x * ex * bf(k_s[r * LDB + c]);
+        dg[j][e] -= t2;
+        atomicAdd(red_s + c, t2);
+      }
+  }
+  // P3 = dvn h^T -> dwt = -P3
+  zero_acc<8>(acc);
+  warp_mma<8>(acc, RowA16{dvn_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
+  store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+    *reinterpret_cast<float2*>(dwt_o + cb * C * D + r * D + c) = make_float2(-x0, -x1);
+  });
+  store_pairs<8>(dg, m0, n0, [&](int r, int c, float x0, float x1) {
+    *reinterpret_cast<float2*>(dgc_p + cb * C * D + r * D + c) = make_float2(x0, x1);
+  });
+  // dAqk = do vn^T (causal), unscaled
+  {
+    float a4[4][4];
+    zero_acc<4>(a4);
+    warp_mma<4>(a4, RowA16{do_s, LDB}, NKB16{vn_s, LDB}, m0, 32 * nh, 0, D);
+    store_pairs<4>(a4, m0, 32 * nh, [&](int r, int c, float x0, float x1) {
+      *reinterpret_cast<float2*>(daqk_o + cb * C * C + r * C + c) =
+          make_float2(c <= r ? x0 : 0.f, c + 1 <= r ? x1 : 0.f);
+    });
+  }
+  // dgcl += e^{gcl} sum_v dh h
+  {
+    const int d = tid >> 1, half = tid & 1;
+    float s = 0.f;
+    for (int vv = half * 64; vv < half * 64 + 64; ++vv) s += bf(dh_s[d * LDB + vv]) * bf(h_s[d * LDB + vv]);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    __syncthreads();
+    if (half == 0) dgcl_o[cb * D + d] = red_s[d] + __expf(gc_s[(C - 1) * LDF + d]) * s;
+  }
+}
+
+// ============================================================ backward through the WY representation
+// smem: k, b, w, v, du bf16 [C][LDB]; gc, dwt f32 [C][LDF]; a, da, t f32 [C][LDC]
+constexpr size_t SMEM_BWD_WY = 5 * C * LDB * 2 + 2 * C * LDF * 4 + 3 * C * LDC * 4;
+
+__global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
+    const bf16* __restrict__ k, const bf16* __restrict__ v, const float* __restrict__ g,
+    const bf16* __restrict__ bg, const bf16* __restrict__ wg, const float* __restrict__ a_store,
+    const bf16* __restrict__ dvn_store, const float* __restrict__ dwt, int L, int H, bf16* __restrict__ dv_o,
+    bf16* __restrict__ dw_o, float* __restrict__ dbk_o, float* __restrict__ dgc_o, float* __restrict__ dakk_o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* k_s = reinterpret_cast<bf16*>(smem);
+  bf16* b_s = k_s + C * LDB;
+  bf16* w_s = b_s + C * LDB;
+  bf16* v_s = w_s + C * LDB;
+  bf16* du_s = v_s + C * LDB;
+  float* gc_s = reinterpret_cast<float*>(du_s + C * LDB);
+  float* dwt_s = gc_s + C * LDF;
+  float* a_s = dwt_s + C * LDF;
+  float* da_s = a_s + C * LDC;
+  float* t_s = da_s + C * LDC;
+
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t cb = ix.chunk(b, h, n);
+  load_seq_tile(k_s, k, ix, b, n, h, 256);
+  load_seq_tile(b_s, bg, ix, b, n, h, 256);
+  load_seq_tile(w_s, wg, ix, b, n, h, 256);
+  load_seq_tile(v_s, v, ix, b, n, h, 256);
+  load_chunk_tile(du_s, dvn_store + cb * C * D, 256);
+  load_chunk_tile_f32(dwt_s, LDF, dwt + cb * C * D, C, D, 256);
+  load_chunk_tile_f32(a_s, LDC, a_store + cb * C * C, C, C, 256);
+  load_gc(gc_s, g, ix, b, n, h, 256);
+
+  const int mt = warp & 3, nh = warp >> 2;
+  // dA (strictly lower) = du (w v)^T + dwt (bk e^gc)^T
+  {
+    auto fb_wv = [&](int kv, int nj) -> uint32_t {
+      return pack2(bf(w_s[nj * LDB + kv]) * bf(v_s[nj * LDB + kv]),
+                   bf(w_s[nj * LDB + kv + 1]) * bf(v_s[nj * LDB + kv + 1]));
+    };
+    auto fb_bke = [&](int kd, int nj) -> uint32_t {
+      const float* gj = gc_s + nj * LDF;
+      return pack2(bf(b_s[nj * LDB + kd]) * bf(k_s[nj * LDB + kd]) * __expf(gj[kd]),
+                   bf(b_s[nj * LDB + kd + 1]) * bf(k_s[nj * LDB + kd + 1]) * __expf(gj[kd + 1]));
+    };
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, RowA16{du_s, LDB}, fb_wv, 16 * mt, 32 * nh, 0, D);
+    warp_mma<4>(acc, RowA32{dwt_s, LDF}, fb_bke, 16 * mt, 32 * nh, 0, D);
+    for_acc<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float& x) { da_s[r * LDC + c] = c < r ? x : 0.f; });
+  }
+  // d(wv) = A^T du -> dw, dv ; d(bke) = A^T dwt -> dbk_wy, dgc_wy
+  {
+    const int m0 = 16 * mt, n0 = 64 * nh;
+    float acc[8][4];
+    zero_acc<8>(acc);
+    warp_mma<8>(acc, ColA32{a_s, LDC}, KNB16{du_s, LDB}, m0, n0, m0, C);
+    store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+      int64_t gi = ix.seq(b, (int64_t)n * C + r, h) + c;
+      st_bf16x2(dw_o + gi, x0 * bf(v_s[r * LDB + c]), x1 * bf(v_s[r * LDB + c + 1]));
+      st_bf16x2(dv_o + gi, x0 * bf(w_s[r * LDB + c]), x1 * bf(w_s[r * LDB + c + 1]));
+    });
+    zero_acc<8>(acc);
+    warp_mma<8>(acc, ColA32{a_s, LDC}, KNB32{dwt_s, LDF}, m0, n0, m0, C);
+    store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+      float e0 = __expf(gc_s[r * LDF + c]), e1 = __expf(gc_s[r * LDF + c + 1]);
+      float d0 = x0 * e0, d1 = x1 * e1;
+      *reinterpret_cast<float2*>(dbk_o + cb * C * D + r * D + c) = make_float2(d0, d1);
+      float bk0 = bf(b_s[r * LDB + c]) * bf(k_s[r * LDB + c]);
+      float bk1 = bf(b_s[r * LDB + c + 1]) * bf(k_s[r * LDB + c + 1]);
+      *reinterpret_cast<float2*>(dgc_o + cb * C * D + r * D + c) = make_float2(d0 * bk0, d1 * bk1);
+    });
+  }
+  __syncthreads();
+  // T = dA A^T
+  {
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, RowA32{da_s, LDC}, NKB32{a_s, LDC}, 16 * mt, 32 * nh, 0, 16 * (mt + 1));
+    for_acc<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float& x) { t_s[r * LDC + c] = x; });
+  }
+  __syncthreads();
+  // dAkk = -(A^T T), strictly lower
+  {
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, ColA32{a_s, LDC}, KNB32{t_s, LDC}, 16 * mt, 32 * nh, 16 * mt, C);
+    store_pairs<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float x0, float x1) {
+      *reinterpret_cast<float2*>(dakk_o + cb * C * C + r * C + c) =
+          make_float2(c < r ? -x0 : 0.f, c + 1 < r ? -x1 : 0.f);
+    });
+  }
+}
+
+// ============================================================ backward through Aqk / Akk + assembly
+// smem: q, k, b bf16 [C][LDB]; gc, dgc f32 [C][LDF]; daqk, dakk f32 [C][LDC]
+constexpr size_t SMEM_BWD_INTRA = 3 * C * LDB * 2 + 2 * C * LDF * 4 + 2 * C * LDC * 4;
+
+__global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
+    const bf16* __restrict__ bg, const float* __restrict__ daqk, const float* __restrict__ dakk,
+    const float* __restrict__ dq_p, const float* __restrict__ dk_p, const float* __restrict__ dgc_p,
+    const float* __restrict__ dbk_wy, const float* __restrict__ dgc_wy, const float* __restrict__ dgcl,
+    float scale, int L, int H, bf16* __restrict__ dq_o, bf16* __restrict__ dk_o, bf16* __restrict__ db_o,
+    float* __restrict__ dg_o) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* q_s = reinterpret_cast<bf16*>(smem);
+  bf16* k_s = q_s + C * LDB;
+  bf16* b_s = k_s + C * LDB;
+  float* gc_s = reinterpret_cast<float*>(b_s + C * LDB);
+  float* dgc_s = gc_s + C * LDF;
+  float* daqk_s = dgc_s + C * LDF;
+  float* dakk_s = daqk_s + C * LDC;
+
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
+  const Idx ix{L, H, NC};
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t cb = ix.chunk(b, h, n);
+  load_seq_tile(q_s, q, ix, b, n, h, 256);
+  load_seq_tile(k_s, k, ix, b, n, h, 256);
+  load_seq_tile(b_s, bg, ix, b, n, h, 256);
+  load_chunk_tile_f32(daqk_s, LDC, daqk + cb * C * C, C, C, 256);
+  load_chunk_tile_f32(dakk_s, LDC, dakk + cb * C * C, C, C, 256);
+  load_gc(gc_s, g, ix, b, n, h, 256);
+
+  // warp tile: rows of block I = mt (16 rows), 64 columns (channel half nh)
+  const int I = warp & 3, nh = warp >> 2;
+  const int m0 = 16 * I, n0 = 64 * nh;
+  const int r0 = m0;  // reference row of block I
+  float dq[8][4], dbk[8][4], dk[8][4];
+  zero_acc<8>(dq);
+  zero_acc<8>(dbk);
+  zero_acc<8>(dk);
+  // (a) row side, columns j < 16I: dq_I, dbk_I  (B = k_j e^{gc_r - gc_j})
+  if (I > 0) {
+    const float* gr = gc_s + r0 * LDF;
+    auto fb = [&](int kj, int nd) -> uint32_t {
+      return pack2(bf(k_s[kj * LDB + nd]) * __expf(gr[nd] - gc_s[kj * LDF + nd]),
+                   bf(k_s[(kj + 1) * LDB + nd]) * __expf(gr[nd] - gc_s[(kj + 1) * LDF + nd]));
+    };
+    warp_mma<8>(dq, RowA32{daqk_s, LDC}, fb, m0, n0, 0, r0);
+    warp_mma<8>(dbk, RowA32{dakk_s, LDC}, fb, m0, n0, 0, r0);
+    for_acc<8>(dq, m0, n0, [&](int r, int c, float& x) { x *= scale * __expf(gc_s[r * LDF + c] - gr[c]); });
+    for_acc<8>(dbk, m0, n0, [&](int r, int c, float& x) { x *= __expf(gc_s[r * LDF + c] - gr[c]); });
+  }
+  // (b) column side from later blocks I2 > I: dk_j += e^{gc_r2 - gc_j} sum_i dA[i,j] x_i e^{gc_i - gc_r2}
+  for (int I2 = I + 1; I2 < 4; ++I2) {
+    const int r2 = 16 * I2;
+    const float* gr = gc_s + r2 * LDF;
+    auto fa_q = [&](int rj, int ci) -> uint32_t {  // A(j, i) = daqk[r2+i][m0+j]
+      return pack2(daqk_s[(r2 + ci) * LDC + rj], daqk_s[(r2 + ci + 1) * LDC + rj]);
+    };
+    auto fa_k = [&](int rj, int ci) -> uint32_t {
+      return pack2(dakk_s[(r2 + ci) * LDC + rj], dakk_s[(r2 + ci + 1) * LDC + rj]);
+    };
+    auto fb_q = [&](int ki, int nd) -> uint32_t {
+      return pack2(bf(q_s[(r2 + ki) * LDB + nd]) * __expf(gc_s[(r2 + ki) * LDF + nd] - gr[nd]),
+                   bf(q_s[(r2 + ki + 1) * LDB + nd]) * __expf(gc_s[(r2 + ki + 1) * LDF + nd] - gr[nd]));
+    };
+    auto fb_k = [&](int ki, int nd) -> uint32_t {
+      const int i0 = r2 + ki, i1 = i0 + 1;
+      return pack2(bf(b_s[i0 * LDB + nd]) * bf(k_s[i0 * LDB + nd]) * __expf(gc_s[i0 * LDF + nd] - gr[nd]),
+                   bf(b_s[i1 * LDB + nd]) * bf(k_s[i1 * LDB + nd]) * __expf(gc_s[i1 * LDF + nd] - gr[nd]));
+    };
+    float t1[8][4], t2[8][4];
+    zero_acc<8>(t1);
+    zero_acc<8>(t2);
+    // A operand rows are j within block I: pass m0 offset through the loader (rj includes m0)
+    warp_mma<8>(t1, fa_q, fb_q, m0, n0, 0, 16);
+    warp_mma<8>(t2, fa_k, fb_k, m0, n0, 0, 16);
+    const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+        dk[j][e] += (scale * t1[j][e] + t2[j][e]) * __expf(gr[c] - gc_s[r * LDF + c]);
+      }
+  }
+  // (c) diagonal block, exact: element (i, d) of this thread's fragments
+  {
+    const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+        const float gi = gc_s[r * LDF + c];
+        const float qi = bf(q_s[r * LDB + c]);
+        const float bki = bf(b_s[r * LDB + c]) * bf(k_s[r * LDB + c]);
+        const float ki = bf(k_s[r * LDB + c]);
+        float aq = 0.f, ab = 0.f, ak = 0.f;
+        for (int s = m0; s < m0 + 16; ++s) {
+          const float gs = gc_s[s * LDF + c];
+          if (s <= r) {  // row side: pairs (r, s), s <= r
+            const float ex = __expf(fmaxf(gi - gs, -20.f));
+            const float ks = bf(k_s[s * LDB + c]) * ex;
+            aq += daqk_s[r * LDC + s] * ks;
+            if (s < r) ab += dakk_s[r * LDC + s] * ks;
+          }
+          if (s >= r) {  // column side: pairs (s, r), s >= r
+            const float ex = __expf(fmaxf(gs - gi, -20.f));
+            const float qs = bf(q_s[s * LDB + c]);
+            const float bks = bf(b_s[s * LDB + c]) * bf(k_s[s * LDB + c]);
+            ak += (scale * daqk_s[s * LDC + r] * qs + (s > r ? dakk_s[s * LDC + r] * bks : 0.f)) * ex;
+          }
+        }
+        dq[j][e] += scale * aq;
+        dbk[j][e] += ab;
+        dk[j][e] += ak;
+        // assembly
+        const int64_t ci = cb * C * D + (int64_t)r * D + c;
+        const float dbk_t = dbk[j][e] + dbk_wy[ci];
+        const float dq_t = dq[j][e] + dq_p[ci];
+        const float dk_t = dk[j][e] + dk_p[ci] + dbk_t * bf(b_s[r * LDB + c]);
+        const float db_t = dbk_t * ki;
+        float dgc = dgc_p[ci] + dgc_wy[ci] + qi * dq[j][e] + bki * dbk[j][e] - ki * dk[j][e];
+        if (r == C - 1) dgc += dgcl[cb * D + c];
+        dgc_s[r * LDF + c] = dgc;
+        const int64_t gi2 = ix.seq(b, (int64_t)n * C + r, h) + c;
+        dq_o[gi2] = __float2bfloat16_rn(dq_t);
+        dk_o[gi2] = __float2bfloat16_rn(dk_t);
+        db_o[gi2] = __float2bfloat16_rn(db_t);
+      }
+  }
+  __syncthreads();
+  // dg = reverse cumsum over the chunk rows
+  if (tid < D) {
+    float s = 0.f;
+    for (int r = C - 1; r >= 0; --r) {
+      s += dgc_s[r * LDF + tid];
+      dg_o[ix.seq(b, (int64_t)n * C + r, h) + tid] = s;
+    }
+  }
+}
+
+template <class K>
+void set_smem(K kernel, size_t bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+
+// ===================================================================== launchers
+int ahb_gdn_supported(int D_) { return D_ == D ? C : 0; }
+
+void ahb_gdn_intra_fwd(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                       float scale, int B, int L, int H, void* wt, void* u, void* qg, void* kg, float* aqk,
+                       float* gcl, float* a_out, cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_intra_fwd_kernel, SMEM_INTRA); init = true; }
+  dim3 grid(L / C, H, B);
+  gdn_intra_fwd_kernel<<<grid, 256, SMEM_INTRA, st>>>(
+      (const bf16*)q, (const bf16*)k, (const bf16*)v, g, (const bf16*)bg, (const bf16*)wg, scale, L, H, (bf16*)wt,
+      (bf16*)u, (bf16*)qg, (bf16*)kg, aqk, gcl, a_out);
+}
+
+void ahb_gdn_inter_fwd(const void* wt, const void* u, const void* qg, const void* kg, const float* aqk,
+                       const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
+                       void* h_store, void* vn_store, cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_inter_fwd_kernel, SMEM_INTER_F); init = true; }
+  dim3 grid(D / BV, H, B);
+  gdn_inter_fwd_kernel<<<grid, 128, SMEM_INTER_F, st>>>(
+      (const bf16*)wt, (const bf16*)u, (const bf16*)qg, (const bf16*)kg, aqk, gcl, scale, L, H, L / C, h0, (bf16*)o,
+      h_final, (bf16*)h_store, (bf16*)vn_store);
+}
+
+void ahb_gdn_inter_bwd(const void* wt, const void* qg, const void* kg, const float* aqk, const float* gcl,
+                       const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
+                       void* dvn_store, float* dh0, cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_inter_bwd_kernel, SMEM_INTER_B); init = true; }
+  dim3 grid(D / BV, H, B);
+  gdn_inter_bwd_kernel<<<grid, 128, SMEM_INTER_B, st>>>((const bf16*)wt, (const bf16*)qg, (const bf16*)kg, aqk, gcl,
+                                                        (const bf16*)dout, scale, L, H, L / C, dh_final,
+                                                        (bf16*)dh_store, (bf16*)dvn_store, dh0);
+}
+
+void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void* dout, const void* h_store,
+                        const void* dh_store, const void* vn_store, const void* dvn_store, float scale, int B, int L,
+                        int H, float* dq_p, float* dk_p, float* dgc_p, float* dwt, float* dgcl, float* daqk,
+                        cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_bwd_states_kernel, SMEM_BWD_STATES); init = true; }
+  dim3 grid(L / C, H, B);
+  gdn_bwd_states_kernel<<<grid, 256, SMEM_BWD_STATES, st>>>(
+      (const bf16*)q, (const bf16*)k, g, (const bf16*)dout, (const bf16*)h_store, (const bf16*)dh_store,
+      (const bf16*)vn_store, (const bf16*)dvn_store, scale, L, H, dq_p, dk_p, dgc_p, dwt, dgcl, daqk);
+}
+
+void ahb_gdn_bwd_wy(const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                    const float* a_store, const void* dvn_store, const float* dwt, int B, int L, int H, void* dv,
+                    void* dw, float* dbk_wy, float* dgc_wy, float* dakk, cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_bwd_wy_kernel, SMEM_BWD_WY); init = true; }
+  dim3 grid(L / C, H, B);
+  gdn_bwd_wy_kernel<<<grid, 256, SMEM_BWD_WY, st>>>((const bf16*)k, (const bf16*)v, g, (const bf16*)bg,
+                                                    (const bf16*)wg, a_store, (const bf16*)dvn_store, dwt, L, H,
+                                                    (bf16*)dv, (bf16*)dw, dbk_wy, dgc_wy, dakk);
+}
+
+void ahb_gdn_bwd_intra(const void* q, const void* k, const float* g, const void* bg, const float* daqk,
+                       const float* dakk, const float* dq_p, const float* dk_p, const float* dgc_p,
+                       const float* dbk_wy, const float* dgc_wy, const float* dgcl, float scale, int B, int L, int H,
+                       void* dq, void* dk, void* db, float* dg, cudaStream_t st) {
+  static bool init = false;
+  if (!init) { set_smem(gdn_bwd_intra_kernel, SMEM_BWD_INTRA); init = true; }
+  dim3 grid(L / C, H, B);
+  gdn_bwd_intra_kernel<<<grid, 256, SMEM_BWD_INTRA, st>>>(
+      (const bf16*)q, (const bf16*)k, g, (const bf16*)bg, daqk, dakk, dq_p, dk_p, dgc_p, dbk_wy, dgc_wy, dgcl, scale,
+      L, H, (bf16*)dq, (bf16*)dk, (bf16*)db, dg);
+}

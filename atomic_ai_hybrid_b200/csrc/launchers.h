@@ -23,3 +23,34 @@ void ahb_embedding_fwd(const int64_t* ids, const void* emb, int edtype, void* ou
                        int64_t V, cudaStream_t st);
 void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* acc, int64_t T, int D, int64_t V,
                        cudaStream_t st);
+
+// gdn.cu (head dim 128, chunk 64; all sequence tensors (B, L, H, 128), chunk tensors (B, H, L/64, 64, .))
+int ahb_gdn_supported(int D);
+void ahb_gdn_intra_fwd(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                       float scale, int B, int L, int H, void* wt, void* u, void* qg, void* kg, float* aqk,
+                       float* gcl, float* a_out, cudaStream_t st);
+void ahb_gdn_inter_fwd(const void* wt, const void* u, const void* qg, const void* kg, const float* aqk,
+                       const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
+                       void* h_store, void* vn_store, cudaStream_t st);
+void ahb_gdn_inter_bwd(const void* wt, const void* qg, const void* kg, const float* aqk, const float* gcl,
+                       const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
+                       void* dvn_store, float* dh0, cudaStream_t st);
+void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void* dout, const void* h_store,
+                        const void* dh_store, const void* vn_store, const void* dvn_store, float scale, int B, int L,
+                        int H, float* dq_p, float* dk_p, float* dgc_p, float* dwt, float* dgcl, float* daqk,
+                        cudaStream_t st);
+void ahb_gdn_bwd_wy(const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                    const float* a_store, const void* dvn_store, const float* dwt, int B, int L, int H, void* dv,
+                    void* dw, float* dbk_wy, float* dgc_wy, float* dakk, cudaStream_t st);
+void ahb_gdn_bwd_intra(const void* q, const void* k, const float* g, const void* bg, const float* daqk,
+                       const float* dakk, const float* dq_p, const float* dk_p, const float* dgc_p,
+                       const float* dbk_wy, const float* dgc_wy, const float* dgcl, float scale, int B, int L, int H,
+                       void* dq, void* dk, void* db, float* dg, cudaStream_t st);
+
+// ssd.cu (head dim 64, d_state 128, chunk 64; x, dt (B,L,H,64); B, C (B,L,128); A (H,) fp32)
+int ahb_ssd_supported(int P, int N);
+void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
+                 float* state_buf, float* cuml, const float* s0, float* s_final, void* y, cudaStream_t st);
+void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
+                 int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
+                 float* dC, float* dA, cudaStream_t st);

@@ -1,0 +1,519 @@
+// Mamba2 SSD with per-channel dt (headdim 64, d_state 128, chunk 64, B/C shared
+// by all heads), following the reference's chunked form and clip discipline
+// (reference `atomic_ops/mamba2_ssd_reference.py:56-148`):
+//   dA = clip(dt*A_h, +-20) ; c = cumsum_t dA            (per channel p)
+//   CB[i,j] = C_i . B_j ; dBx = dt*x
+//   y_diag[i,p] = sum_{j<=i} e^{max(c_ip-c_jp,-20)} CB[i,j] dBx[j,p]
+//   y_off[i,p]  = e^{max(c_ip,-20)} sum_s C[i,s] S_in[p,s]
+//   S_end[p,s]  = sum_j e^{max(cL_p-c_jp,-20)} dBx[j,p] B[j,s]
+//   S_in(next)  = S_in e^{max(cL_p,-20)} + S_end
+//
+// sm_100a layout: ssd_state_fwd / ssd_out_fwd / ssd_bwd_chunk use one CTA per
+// (chunk, batch) that loops over the heads, so C B^T and the B/C tiles are read
+// once per chunk and the B/C gradients of all heads accumulate in registers
+// (no atomics).  ssd_scan carries the chunk states: each thread owns one (p, s)
+// state element of one head and walks the chunks (forward or reverse).
+// Pairwise decays inside a chunk use the reference-row factorisation of the
+// GDN kernels (both factors <= 1); diagonal 16x16 blocks are exact.
+#include "common.cuh"
+#include "mma.cuh"
+#include "launchers.h"
+
+using namespace ahb;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int C = 64;    // chunk
+constexpr int P = 64;    // head dim
+constexpr int N = 128;   // state dim
+constexpr int LDN = N + 8;   // bf16 stride for C x N / P x N tiles
+constexpr int LDP = P + 8;   // bf16 stride for C x P tiles
+constexpr int LDPF = P + 4;  // fp32 stride for C x P tiles
+constexpr int LDCC = C + 4;  // fp32 stride for C x C tiles
+
+AHB_DEVICE float bf(bf16 x) { return __bfloat162float(x); }
+AHB_DEVICE void st2(bf16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack2(a, b); }
+
+struct SIdx {
+  int64_t L, H, NC;
+  AHB_DEVICE int64_t xp(int b, int64_t t, int h) const { return ((b * L + t) * H + h) * P; }  // (B,L,H,P)
+  AHB_DEVICE int64_t bn(int b, int64_t t) const { return (b * L + t) * N; }                  // (B,L,N)
+  AHB_DEVICE int64_t ch(int b, int h, int n) const { return ((int64_t)b * H + h) * NC + n; }
+};
+
+AHB_DEVICE void load_bn_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, int n) {
+  for (int i = threadIdx.x; i < C * (N / 8); i += 256) {
+    int r = i / (N / 8), c8 = (i % (N / 8)) * 8;
+    *reinterpret_cast<uint4*>(dst + r * LDN + c8) =
+        *reinterpret_cast<const uint4*>(src + ix.bn(b, (int64_t)n * C + r) + c8);
+  }
+}
+AHB_DEVICE void load_xp_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, int n, int h) {
+  for (int i = threadIdx.x; i < C * (P / 8); i += 256) {
+    int r = i / (P / 8), c8 = (i % (P / 8)) * 8;
+    *reinterpret_cast<uint4*>(dst + r * LDP + c8) =
+        *reinterpret_cast<const uint4*>(src + ix.xp(b, (int64_t)n * C + r, h) + c8);
+  }
+}
+// fp32 (P x N) state tile -> bf16 smem [P][LDN]
+AHB_DEVICE void load_state_bf(bf16* dst, const float* src) {
+  for (int i = threadIdx.x; i < P * (N / 4); i += 256) {
+    int r = i / (N / 4), c4 = (i % (N / 4)) * 4;
+    float4 v = *reinterpret_cast<const float4*>(src + r * N + c4);
+    st2(dst + r * LDN + c4, v.x, v.y);
+    st2(dst + r * LDN + c4 + 2, v.z, v.w);
+  }
+}
+// c = cumsum(clip(dt*A, +-20)), clipped to +-1e4 (reference sanitize)
+AHB_DEVICE void cum_decay(float* cum, const bf16* dt_s, float A) {
+  __syncthreads();
+  if (threadIdx.x < P) {
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) {
+      s += fminf(fmaxf(bf(dt_s[r * LDP + threadIdx.x]) * A, -20.f), 20.f);
+      cum[r * LDPF + threadIdx.x] = fminf(fmaxf(s, -1e4f), 1e4f);
+    }
+  }
+  __syncthreads();
+}
+AHB_DEVICE float dbx(const bf16* x_s, const bf16* dt_s, int r, int p) {
+  return bf(x_s[r * LDP + p]) * bf(dt_s[r * LDP + p]);
+}
+
+// y_diag for the warp's tile: rows [16I, 16I+16), cols [n0, n0+32) (NT = 4)
+AHB_DEVICE void ydiag_tile(float (*acc)[4], const float* cb_s, const bf16* x_s, const bf16* dt_s, const float* cum,
+                           int I, int n0) {
+  const int r0 = 16 * I;
+  zero_acc<4>(acc);
+  if (I > 0) {
+    const float* cr = cum + r0 * LDPF;
+    auto fb = [&](int kj, int np) -> uint32_t {
+      return pack2(dbx(x_s, dt_s, kj, np) * __expf(cr[np] - cum[kj * LDPF + np]),
+                   dbx(x_s, dt_s, kj + 1, np) * __expf(cr[np] - cum[(kj + 1) * LDPF + np]));
+    };
+    warp_mma<4>(acc, RowA32{cb_s, LDCC}, fb, r0, n0, 0, r0);
+    for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) { v *= __expf(cum[r * LDPF + c] - cr[c]); });
+  }
+  for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) {
+    float s = 0.f;
+    const float ci = cum[r * LDPF + c];
+    for (int j = r0; j <= r; ++j)
+      s += cb_s[r * LDCC + j] * dbx(x_s, dt_s, j, c) * __expf(fmaxf(ci - cum[j * LDPF + c], -20.f));
+    v += s;
+  });
+}
+
+// y_off tile: e^{max(c,-20)} * (C S^T)
+AHB_DEVICE void yoff_tile(float (*acc)[4], const bf16* c_s, const bf16* sin_s, const float* cum, int I, int n0) {
+  zero_acc<4>(acc);
+  warp_mma<4>(acc, RowA16{c_s, LDN}, NKB16{sin_s, LDN}, 16 * I, n0, 0, N);
+  for_acc<4>(acc, 16 * I, n0, [&](int r, int c, float& v) { v *= __expf(fmaxf(cum[r * LDPF + c], -20.f)); });
+}
+
+// C B^T (C x C), sanitized
+AHB_DEVICE void compute_cb(float* cb_s, const bf16* c_s, const bf16* b_s) {
+  const int warp = threadIdx.x >> 5;
+  float acc[4][4];
+  zero_acc<4>(acc);
+  warp_mma<4>(acc, RowA16{c_s, LDN}, NKB16{b_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, N);
+  for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2),
+             [&](int r, int c, float& v) { cb_s[r * LDCC + c] = sanitize(v, 1e4f); });
+}
+
+// ============================================================ forward: chunk states
+constexpr size_t SMEM_STATE_F = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
+
+__global__ void __launch_bounds__(256) ssd_state_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
+                                                            const float* __restrict__ A, const bf16* __restrict__ Bm,
+                                                            int L, int H, float* __restrict__ send,
+                                                            float* __restrict__ cuml) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* b_s = reinterpret_cast<bf16*>(smem);
+  bf16* x_s = b_s + C * LDN;
+  bf16* dt_s = x_s + C * LDP;
+  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
+  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
+  const SIdx ix{L, H, NC};
+  const int warp = threadIdx.x >> 5;
+  load_bn_tile(b_s, Bm, ix, b, n);
+  for (int h = 0; h < H; ++h) {
+    load_xp_tile(x_s, x, ix, b, n, h);
+    load_xp_tile(dt_s, dt, ix, b, n, h);
+    cum_decay(cum, dt_s, A[h]);
+    const int64_t cb = ix.ch(b, h, n);
+    if (threadIdx.x < P) cuml[cb * P + threadIdx.x] = cum[(C - 1) * LDPF + threadIdx.x];
+    // S_end[p, s] = sum_j (dBx[j,p] e^{cL-c_j}) B[j,s]
+    const float* cl = cum + (C - 1) * LDPF;
+    auto fa = [&](int rp, int kj) -> uint32_t {
+      return pack2(dbx(x_s, dt_s, kj, rp) * __expf(fmaxf(cl[rp] - cum[kj * LDPF + rp], -20.f)),
+                   dbx(x_s, dt_s, kj + 1, rp) * __expf(fmaxf(cl[rp] - cum[(kj + 1) * LDPF + rp], -20.f)));
+    };
+    float acc[8][4];
+    zero_acc<8>(acc);
+    warp_mma<8>(acc, fa, KNB16{b_s, LDN}, 16 * (warp & 3), 64 * (warp >> 2), 0, C);
+    float* out = send + cb * P * N;
+    for_acc<8>(acc, 16 * (warp & 3), 64 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = sanitize(v, 1e4f); });
+    __syncthreads();
+  }
+}
+
+// ============================================================ state scan (forward / reverse)
+// forward: buf holds S_end on entry and S_in on exit; reverse: buf holds G on entry, dS_end on exit.
+__global__ void __launch_bounds__(256) ssd_scan_kernel(float* __restrict__ buf, const float* __restrict__ cuml,
+                                                       int H, int NC, int reverse, const float* __restrict__ s0,
+                                                       float* __restrict__ s_final) {
+  const int e = blockIdx.x * 256 + threadIdx.x;  // element of P x N
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int p = e / N;
+  const int64_t base = ((int64_t)b * H + h) * NC;
+  float S = s0 ? s0[((int64_t)b * H + h) * P * N + e] : 0.f;
+  if (!reverse) {
+    for (int n = 0; n < NC; ++n) {
+      float* q = buf + (base + n) * P * N + e;
+      const float se = *q;
+      *q = S;
+      S = sanitize(S * __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) + se, 1e4f);
+    }
+  } else {
+    for (int n = NC - 1; n >= 0; --n) {
+      float* q = buf + (base + n) * P * N + e;
+      const float gn = *q;
+      *q = S;
+      S = S * __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) + gn;
+    }
+  }
+  if (s_final) s_final[((int64_t)b * H + h) * P * N + e] = S;
+}
+
+// ============================================================ forward: outputs
+constexpr size_t SMEM_OUT_F = 2 * C * LDN * 2 + C * LDCC * 4 + 2 * C * LDP * 2 + C * LDPF * 4 + P * LDN * 2;
+
+__global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
+                                                          const float* __restrict__ A, const bf16* __restrict__ Bm,
+                                                          const bf16* __restrict__ Cm, const float* __restrict__ sin,
+                                                          int L, int H, bf16* __restrict__ y) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* b_s = reinterpret_cast<bf16*>(smem);
+  bf16* c_s = b_s + C * LDN;
+  float* cb_s = reinterpret_cast<float*>(c_s + C * LDN);
+  bf16* x_s = reinterpret_cast<bf16*>(cb_s + C * LDCC);
+  bf16* dt_s = x_s + C * LDP;
+  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
+  bf16* sin_s = reinterpret_cast<bf16*>(cum + C * LDPF);
+  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
+  const SIdx ix{L, H, NC};
+  const int warp = threadIdx.x >> 5;
+  load_bn_tile(b_s, Bm, ix, b, n);
+  load_bn_tile(c_s, Cm, ix, b, n);
+  __syncthreads();
+  compute_cb(cb_s, c_s, b_s);
+  const int I = warp & 3, n0 = 32 * (warp >> 2);
+  for (int h = 0; h < H; ++h) {
+    const int64_t cb = ix.ch(b, h, n);
+    load_xp_tile(x_s, x, ix, b, n, h);
+    load_xp_tile(dt_s, dt, ix, b, n, h);
+    load_state_bf(sin_s, sin + cb * P * N);
+    cum_decay(cum, dt_s, A[h]);
+    float yd[4][4], yo[4][4];
+    ydiag_tile(yd, cb_s, x_s, dt_s, cum, I, n0);
+    yoff_tile(yo, c_s, sin_s, cum, I, n0);
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = n0 + 8 * j + 2 * t;
+      const int r = 16 * I + g;
+      st2(y + ix.xp(b, (int64_t)n * C + r, h) + c, sanitize(sanitize(yd[j][0], 1e4f) + sanitize(yo[j][0], 1e4f), 1e4f),
+          sanitize(sanitize(yd[j][1], 1e4f) + sanitize(yo[j][1], 1e4f), 1e4f));
+      st2(y + ix.xp(b, (int64_t)n * C + r + 8, h) + c,
+          sanitize(sanitize(yd[j][2], 1e4f) + sanitize(yo[j][2], 1e4f), 1e4f),
+          sanitize(sanitize(yd[j][3], 1e4f) + sanitize(yo[j][3], 1e4f), 1e4f));
+    }
+    __syncthreads();
+  }
+}
+
+// ============================================================ backward: G = (dy e^c)^T C  per chunk/head
+constexpr size_t SMEM_G = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
+
+__global__ void __launch_bounds__(256) ssd_dstate_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dt,
+                                                         const float* __restrict__ A, const bf16* __restrict__ Cm,
+                                                         int L, int H, float* __restrict__ gbuf) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* c_s = reinterpret_cast<bf16*>(smem);
+  bf16* dy_s = c_s + C * LDN;
+  bf16* dt_s = dy_s + C * LDP;
+  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
+  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
+  const SIdx ix{L, H, NC};
+  const int warp = threadIdx.x >> 5;
+  load_bn_tile(c_s, Cm, ix, b, n);
+  for (int h = 0; h < H; ++h) {
+    load_xp_tile(dy_s, dy, ix, b, n, h);
+    load_xp_tile(dt_s, dt, ix, b, n, h);
+    cum_decay(cum, dt_s, A[h]);
+    auto fa = [&](int rp, int ki) -> uint32_t {
+      return pack2(bf(dy_s[ki * LDP + rp]) * __expf(fmaxf(cum[ki * LDPF + rp], -20.f)),
+                   bf(dy_s[(ki + 1) * LDP + rp]) * __expf(fmaxf(cum[(ki + 1) * LDPF + rp], -20.f)));
+    };
+    float acc[8][4];
+    zero_acc<8>(acc);
+    warp_mma<8>(acc, fa, KNB16{c_s, LDN}, 16 * (warp & 3), 64 * (warp >> 2), 0, C);
+    float* out = gbuf + ix.ch(b, h, n) * P * N;
+    for_acc<8>(acc, 16 * (warp & 3), 64 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = v; });
+    __syncthreads();
+  }
+}
+
+// ============================================================ backward: per chunk, all heads
+// smem: b, c bf16 [C][LDN]; cb, dcb f32 [C][LDCC]; x, dt, dy bf16 [C][LDP]; cum, dc, ddbx f32 [C][LDPF];
+//       sin, dse bf16 [P][LDN]
+constexpr size_t SMEM_BWD =
+    2 * C * LDN * 2 + 2 * C * LDCC * 4 + 3 * C * LDP * 2 + 3 * C * LDPF * 4 + 2 * P * LDN * 2 + P * 4;
+
+__global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
+    const bf16* __restrict__ x, const bf16* __restrict__ dt, const float* __restrict__ A,
+    const bf16* __restrict__ Bm, const bf16* __restrict__ Cm, const bf16* __restrict__ dy,
+    const float* __restrict__ sin, const float* __restrict__ dse, int L, int H, bf16* __restrict__ dx,
+    bf16* __restrict__ ddt, float* __restrict__ dB, float* __restrict__ dC, float* __restrict__ dA) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  bf16* b_s = reinterpret_cast<bf16*>(smem);
+  bf16* c_s = b_s + C * LDN;
+  float* cb_s = reinterpret_cast<float*>(c_s + C * LDN);
+  float* dcb_s = cb_s + C * LDCC;
+  bf16* x_s = reinterpret_cast<bf16*>(dcb_s + C * LDCC);
+  bf16* dt_s = x_s + C * LDP;
+  bf16* dy_s = dt_s + C * LDP;
+  float* cum = reinterpret_cast<float*>(dy_s + C * LDP);
+  float* dc_s = cum + C * LDPF;
+  float* ddbx_s = dc_s + C * LDPF;
+  bf16* sin_s = reinterpret_cast<bf16*>(ddbx_s + C * LDPF);
+  bf16* dse_s = sin_s + P * LDN;
+  float* dcl_s = reinterpret_cast<float*>(dse_s + P * LDN);
+
+  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
+  const SIdx ix{L, H, NC};
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  load_bn_tile(b_s, Bm, ix, b, n);
+  load_bn_tile(c_s, Cm, ix, b, n);
+  __syncthreads();
+  compute_cb(cb_s, c_s, b_s);
+  // dB / dC accumulators: warp tile rows [16*(warp&3)), cols [64*(warp>>2)), 8 n-tiles
+  const int mt = warp & 3, nh = warp >> 2;
+  float dBa[8][4], dCa[8][4];
+  zero_acc<8>(dBa);
+  zero_acc<8>(dCa);
+  for (int h = 0; h < H; ++h) {
+    const int64_t cbi = ix.ch(b, h, n);
+    const float Ah = A[h];
+    load_xp_tile(x_s, x, ix, b, n, h);
+    load_xp_tile(dt_s, dt, ix, b, n, h);
+    load_xp_tile(dy_s, dy, ix, b, n, h);
+    load_state_bf(sin_s, sin + cbi * P * N);
+    load_state_bf(dse_s, dse + cbi * P * N);
+    if (tid < P) dcl_s[tid] = 0.f;
+    cum_decay(cum, dt_s, Ah);
+    const float* cl = cum + (C - 1) * LDPF;
+    // (1) dCB[i,j] = sum_p dy[i,p] e^{c_i-c_j} dBx[j,p]   (j <= i)
+    {
+      const int I = mt, r0 = 16 * I;
+      float acc[4][4];
+      zero_acc<4>(acc);
+      const int n0 = 32 * nh;  // j columns [n0, n0+32)
+      if (I > 0 && n0 < r0) {
+        const float* cr = cum + r0 * LDPF;
+        auto fa = [&](int ri, int kp) -> uint32_t {
+          return pack2(bf(dy_s[ri * LDP + kp]) * __expf(cum[ri * LDPF + kp] - cr[kp]),
+                       bf(dy_s[ri * LDP + kp + 1]) * __expf(cum[ri * LDPF + kp + 1] - cr[kp + 1]));
+        };
+        auto fb = [&](int kp, int nj) -> uint32_t {
+          return pack2(dbx(x_s, dt_s, nj, kp) * __expf(cr[kp] - cum[nj * LDPF + kp]),
+                       dbx(x_s, dt_s, nj, kp + 1) * __expf(cr[kp + 1] - cum[nj * LDPF + kp + 1]));
+        };
+        warp_mma<4>(acc, fa, fb, r0, n0, 0, P);
+      }
+      for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) {
+        if (c >= r0) {  // diagonal block (exact) or above it (zero)
+          float s = 0.f;
+          if (c <= r)
+            for (int p = 0; p < P; ++p)
+              s += bf(dy_s[r * LDP + p]) * dbx(x_s, dt_s, c, p) *
+                   __expf(fmaxf(cum[r * LDPF + p] - cum[c * LDPF + p], -20.f));
+          v = s;
+        }
+        dcb_s[r * LDCC + c] = v;
+      });
+    }
+    __syncthreads();
+    // (2) dC += dCB B + (dy e^c) S_in^T ;  (3) dB += dCB^T C + (dBx e^{cL-c}) dS_end^T
+    {
+      const int m0 = 16 * mt, n0 = 64 * nh;
+      warp_mma<8>(dCa, RowA32{dcb_s, LDCC}, KNB16{b_s, LDN}, m0, n0, 0, m0 + 16);
+      auto fa_dy = [&](int ri, int kp) -> uint32_t {
+        return pack2(bf(dy_s[ri * LDP + kp]) * __expf(fmaxf(cum[ri * LDPF + kp], -20.f)),
+                     bf(dy_s[ri * LDP + kp + 1]) * __expf(fmaxf(cum[ri * LDPF + kp + 1], -20.f)));
+      };
+      warp_mma<8>(dCa, fa_dy, KNB16{sin_s, LDN}, m0, n0, 0, P);
+      warp_mma<8>(dBa, ColA32{dcb_s, LDCC}, KNB16{c_s, LDN}, m0, n0, m0, C);
+      auto fa_bx = [&](int rj, int kp) -> uint32_t {
+        return pack2(dbx(x_s, dt_s, rj, kp) * __expf(fmaxf(cl[kp] - cum[rj * LDPF + kp], -20.f)),
+                     dbx(x_s, dt_s, rj, kp + 1) * __expf(fmaxf(cl[kp + 1] - cum[rj * LDPF + kp + 1], -20.f)));
+      };
+      warp_mma<8>(dBa, fa_bx, KNB16{dse_s, LDN}, m0, n0, 0, P);
+    }
+    // (4)+(5) per (t,p) tile: y_diag, y_off, ddBx (diag part, state part) -> dc, ddBx
+    {
+      const int I = mt, n0 = 32 * nh, r0 = 16 * I;
+      float yd[4][4], yo[4][4], dd[4][4], ds[4][4];
+      ydiag_tile(yd, cb_s, x_s, dt_s, cum, I, n0);
+      yoff_tile(yo, c_s, sin_s, cum, I, n0);
+      // ddBx_diag[j,p] = sum_{i>=j} CB[i,j] dy[i,p] e^{c_i-c_j}
+      zero_acc<4>(dd);
+      for (int I2 = I + 1; I2 < 4; ++I2) {
+        const int r2 = 16 * I2;
+        const float* cr = cum + r2 * LDPF;
+        auto fa = [&](int rj, int ki) -> uint32_t {
+          return pack2(cb_s[(r2 + ki) * LDCC + rj], cb_s[(r2 + ki + 1) * LDCC + rj]);
+        };
+        auto fb = [&](int ki, int np) -> uint32_t {
+          return pack2(bf(dy_s[(r2 + ki) * LDP + np]) * __expf(cum[(r2 + ki) * LDPF + np] - cr[np]),
+                       bf(dy_s[(r2 + ki + 1) * LDP + np]) * __expf(cum[(r2 + ki + 1) * LDPF + np] - cr[np]));
+        };
+        float tacc[4][4];
+        zero_acc<4>(tacc);
+        warp_mma<4>(tacc, fa, fb, r0, n0, 0, 16);
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int r = r0 + g + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+            dd[j][e] += tacc[j][e] * __expf(cr[c] - cum[r * LDPF + c]);
+          }
+      }
+      for_acc<4>(dd, r0, n0, [&](int r, int c, float& v) {
+        float s = 0.f;
+        const float cj = cum[r * LDPF + c];
+        for (int i = r; i < r0 + 16; ++i)
+          s += cb_s[i * LDCC + r] * bf(dy_s[i * LDP + c]) * __expf(fmaxf(cum[i * LDPF + c] - cj, -20.f));
+        v += s;
+      });
+      // ddBx_state[j,p] = e^{cL-c_j} sum_s B[j,s] dS_end[p,s]
+      zero_acc<4>(ds);
+      warp_mma<4>(ds, RowA16{b_s, LDN}, NKB16{dse_s, LDN}, r0, n0, 0, N);
+      const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = r0 + g + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
+          const float cr = cum[r * LDPF + c];
+          const float dlt = cl[c] - cr;
+          const float eds = __expf(fmaxf(dlt, -20.f));
+          const float dsv = ds[j][e] * eds;
+          const float bxv = dbx(x_s, dt_s, r, c);
+          const float dyv = bf(dy_s[r * LDP + c]);
+          float dcv = dyv * yd[j][e] - bxv * dd[j][e];
+          if (cr > -20.f) dcv += dyv * yo[j][e];
+          if (dlt > -20.f) {
+            dcv -= bxv * dsv;
+            atomicAdd(dcl_s + c, bxv * dsv);
+          }
+          dc_s[r * LDPF + c] = dcv;
+          ddbx_s[r * LDPF + c] = dd[j][e] + dsv;
+        }
+    }
+    __syncthreads();
+    // dcL (last row): sum_j dBx ddBx_state (accumulated above into dcl_s) + state carry
+    {
+      const int p = tid >> 2, q4 = tid & 3;
+      float s_car = 0.f;
+      for (int s2 = q4 * 32; s2 < q4 * 32 + 32; ++s2) s_car += bf(dse_s[p * LDN + s2]) * bf(sin_s[p * LDN + s2]);
+      s_car += __shfl_xor_sync(0xffffffffu, s_car, 1);
+      s_car += __shfl_xor_sync(0xffffffffu, s_car, 2);
+      if (q4 == 0) {
+        float add = dcl_s[p];
+        if (cl[p] > -20.f) add += s_car * __expf(cl[p]);
+        dc_s[(C - 1) * LDPF + p] += add;
+      }
+    }
+    __syncthreads();
+    // reverse cumsum of dc -> d(dA); outputs dx, ddt; dA_h
+    float dAh = 0.f;
+    if (tid < P) {
+      const int p = tid;
+      float s = 0.f;
+      for (int r = C - 1; r >= 0; --r) {
+        s += dc_s[r * LDPF + p];
+        const float dtv = bf(dt_s[r * LDP + p]);
+        const float pre = dtv * Ah;
+        const float g = (pre > -20.f && pre < 20.f) ? s : 0.f;
+        dc_s[r * LDPF + p] = g * Ah;  // contribution to ddt
+        dAh += g * dtv;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < C * P; i += 256) {
+      const int r = i / P, p = i % P;
+      const float dd = ddbx_s[r * LDPF + p];
+      const int64_t gi = ix.xp(b, (int64_t)n * C + r, h) + p;
+      dx[gi] = __float2bfloat16_rn(dd * bf(dt_s[r * LDP + p]));
+      ddt[gi] = __float2bfloat16_rn(dd * bf(x_s[r * LDP + p]) + dc_s[r * LDPF + p]);
+    }
+    dAh = warp_sum(dAh);
+    if (lane == 0 && tid < P) atomicAdd(dA + h, dAh);
+    __syncthreads();
+  }
+  // write dB, dC for this chunk (sum over heads)
+  const int m0 = 16 * mt, n0 = 64 * nh;
+  for_acc<8>(dBa, m0, n0, [&](int r, int c, float& v) { dB[ix.bn(b, (int64_t)n * C + r) + c] = v; });
+  for_acc<8>(dCa, m0, n0, [&](int r, int c, float& v) { dC[ix.bn(b, (int64_t)n * C + r) + c] = v; });
+}
+
+template <class K>
+void set_smem(K kernel, size_t bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+
+int ahb_ssd_supported(int P_, int N_) { return (P_ == P && N_ == N) ? C : 0; }
+
+void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
+                 float* state_buf, float* cuml, const float* s0, float* s_final, void* y, cudaStream_t st) {
+  static bool init = false;
+  if (!init) {
+    set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
+    set_smem(ssd_out_fwd_kernel, SMEM_OUT_F);
+    init = true;
+  }
+  const int NC = L / C;
+  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                              L, H, state_buf, cuml);
+  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, s0, s_final);
+  if (y)
+    ssd_out_fwd_kernel<<<dim3(NC, B), 256, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                            (const bf16*)Cm, state_buf, L, H, (bf16*)y);
+}
+
+void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
+                 int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
+                 float* dC, float* dA, cudaStream_t st) {
+  static bool init = false;
+  if (!init) {
+    set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
+    set_smem(ssd_dstate_kernel, SMEM_G);
+    set_smem(ssd_bwd_chunk_kernel, SMEM_BWD);
+    init = true;
+  }
+  const int NC = L / C;
+  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                              L, H, state_buf, cuml);
+  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
+  ssd_dstate_kernel<<<dim3(NC, B), 256, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
+                                                      g_buf);
+  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(g_buf, cuml, H, NC, 1, nullptr, nullptr);
+  ssd_bwd_chunk_kernel<<<dim3(NC, B), 256, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                          (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
+                                                          (bf16*)dx, (bf16*)ddt, dB, dC, dA);
+}

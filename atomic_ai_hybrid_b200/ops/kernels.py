@@ -135,14 +135,57 @@ def embedding(ids, table, dtype):
 
 
 # ----------------------------------------------------------------- not yet native
+class _GDN2(torch.autograd.Function):
+    """sm_100a chunked GDN-2 (head dim 128, chunk 64): 2 launches forward, 6 backward
+    (the backward recomputes the chunk-local forward quantities, as the reference's
+    B6 backward does)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, scale):
+        bf = torch.bfloat16
+        q, k, v, b, w = (t.to(bf).contiguous() for t in (q, k, v, b, w))
+        g = g.float().contiguous()
+        (o,) = ext().gdn_fwd(q, k, v, g, b, w, scale, False)
+        ctx.save_for_backward(q, k, v, g, b, w)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, g, b, w = ctx.saved_tensors
+        dq, dk, dv, dg, db, dw = ext().gdn_bwd(q, k, v, g, b, w, do.contiguous(), ctx.scale)
+        return dq, dk, dv, dg, db, dw, None
+
+
 def gdn2(q, k, v, w, b, g, scale, chunk):
-    o, _ = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
-    return o
+    """``(B,L,H,128)`` GDN-2 with per-channel gates; ``chunk`` is fixed at 64 in the kernel
+    (results do not depend on the chunk length)."""
+    return _GDN2.apply(q, k, v, g, b, w, float(scale))
+
+
+class _SSD(torch.autograd.Function):
+    """sm_100a Mamba2 SSD (head dim 64, d_state 128, chunk 64): 3 launches forward,
+    5 backward (forward chunk states are recomputed in backward)."""
+
+    @staticmethod
+    def forward(ctx, dt, A, Bm, Cm, x):
+        bf = torch.bfloat16
+        dt, Bm, Cm, x = (t.to(bf).contiguous() for t in (dt, Bm, Cm, x))
+        A = A.float().contiguous()
+        y = ext().ssd_fwd(x, dt, A, Bm, Cm)
+        ctx.save_for_backward(dt, A, Bm, Cm, x)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dt, A, Bm, Cm, x = ctx.saved_tensors
+        dx, ddt, dA, dB, dC = ext().ssd_bwd(x, dt, A, Bm, Cm, dy.contiguous())
+        return ddt, dA, dB.to(Bm.dtype), dC.to(Cm.dtype), dx
 
 
 def ssd(dt, A, Bm, Cm, x, chunk):
-    y, _ = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
-    return y
+    """``dt, x (B,L,H,64)``, ``A (H,)``, ``B, C (B,L,128)``; chunk fixed at 64 in the kernel."""
+    return _SSD.apply(dt, A, Bm, Cm, x)
 
 
 def attention(q, k, v, sm_scale):

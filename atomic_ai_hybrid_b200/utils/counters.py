@@ -5,7 +5,7 @@ from __future__ import annotations
 
 
 class LaunchCounter:
-    MULTI = {}
+    MULTI = {"gdn_fwd": 2, "gdn_bwd": 6, "ssd_fwd": 3, "ssd_bwd": 5}
 
     def __init__(self):
         self.count = 0
