@@ -263,6 +263,161 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
   return {dx, ddt, dA, dB, dC};
 }
 
+// ------------------------------------------------------------ MoE (grouped GEMM on tcgen05)
+int num_sms() {
+  static int n = 0;
+  if (!n) { int d; cudaGetDevice(&d); cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d); }
+  return n;
+}
+
+torch::Tensor& err_word() {
+  static torch::Tensor e;
+  if (!e.defined()) e = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA));
+  return e;
+}
+
+int64_t gemm_error() { return err_word().item<int>(); }
+void gemm_error_reset() { err_word().zero_(); }
+
+void gemm_check(int rc, const char* what) { TORCH_CHECK(rc == 0, "moe_gemm (", what, ") setup failed: code ", rc); }
+
+// Generic access for tests: C = A B^T (A: M x K, B: N x K, bf16, K-major), single group
+torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.is_contiguous() && b.is_contiguous() &&
+              b.scalar_type() == at::kBFloat16, "gemm_dense: bf16 contiguous");
+  int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(M % 128 == 0 && K % 64 == 0 && N % 256 == 0, "gemm_dense: M%128, K%64, N%256");
+  auto off = torch::tensor({0, (int)M}, torch::dtype(torch::kInt32).device(a.device()));
+  auto c = torch::empty({M, N}, a.options());
+  int rc = ahb_moe_gemm(AHB_GEMM_DENSE, a.data_ptr(), nullptr, M, K, b.data_ptr(), nullptr, N, K, 0,
+                        off.data_ptr<int>(), 1, (int)N, 0, (int)K, (int)(K / 64), c.data_ptr(), nullptr, nullptr,
+                        nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream());
+  gemm_check(rc, "dense");
+  return c;
+}
+
+// forward: returns {out, pos, off, row_src, xs, a1, a3, h, ys}
+std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch::Tensor gate, torch::Tensor w1,
+                                   torch::Tensor w2, c10::optional<torch::Tensor> w3,
+                                   c10::optional<torch::Tensor> shared, bool swiglu) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2, "moe: x bf16 (T,d)");
+  for (auto* w : {&w1, &w2})
+    TORCH_CHECK(w->scalar_type() == at::kBFloat16 && w->is_contiguous(), "moe: expert weights must be contiguous bf16");
+  const int T = (int)x.size(0), d = (int)x.size(1), k = (int)top_idx.size(1);
+  const int E = (int)w1.size(0), F = (int)w1.size(2);
+  TORCH_CHECK(d % 256 == 0 && F % 256 == 0, "moe: d_model and d_ff must be multiples of 256");
+  TORCH_CHECK(E <= 47, "moe: at most 47 routed experts per kernel call");
+  auto dev = x.device();
+  auto i32 = torch::dtype(torch::kInt32).device(dev);
+  auto eidx = top_idx.t().contiguous().to(torch::kInt32);
+  auto gatec = gate.to(at::kFloat).contiguous();
+  const int64_t Rcap = ((int64_t)T * k + (int64_t)E * 128 + 127) / 128 * 128;
+  auto counts = torch::empty({E}, i32), off = torch::empty({E + 1}, i32);
+  auto pos = torch::empty({(int64_t)T * k}, i32), row_src = torch::empty({Rcap}, i32);
+  auto st = cur_stream();
+  ahb_moe_route(eidx.data_ptr<int>(), T, k, E, counts.data_ptr<int>(), off.data_ptr<int>(), pos.data_ptr<int>(),
+                row_src.data_ptr<int>(), Rcap, st);
+  auto xs = torch::empty({Rcap, d}, x.options());
+  ahb_moe_gather(x.data_ptr(), row_src.data_ptr<int>(), Rcap, d, xs.data_ptr(), st);
+  auto h = torch::empty({Rcap, F}, x.options());
+  auto a1 = torch::empty_like(h);
+  torch::Tensor a3;
+  int* err = err_word().data_ptr<int>();
+  int rc;
+  if (swiglu) {
+    TORCH_CHECK(w3.has_value(), "moe: swiglu needs w3");
+    a3 = torch::empty_like(h);
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_SWIGLU, xs.data_ptr(), nullptr, Rcap, d, w1.data_ptr(), w3->data_ptr(),
+                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(),
+                      a3.data_ptr(), nullptr, nullptr, 1e3f, err, num_sms(), st);
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_GELU, xs.data_ptr(), nullptr, Rcap, d, w1.data_ptr(), nullptr, (int64_t)E * d, F,
+                      d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(), nullptr, nullptr,
+                      nullptr, 1e3f, err, num_sms(), st);
+  }
+  gemm_check(rc, "fwd up");
+  auto ys = torch::empty({Rcap, d}, x.options());
+  rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, h.data_ptr(), nullptr, Rcap, F, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+                    off.data_ptr<int>(), E, d, 0, F, F / 64, ys.data_ptr(), nullptr, nullptr, nullptr, nullptr, 1e3f,
+                    err, num_sms(), st);
+  gemm_check(rc, "fwd down");
+  auto out = torch::empty_like(x);
+  const void* sh = nullptr;
+  torch::Tensor shc;
+  if (shared.has_value() && shared->defined()) {
+    shc = shared->to(at::kBFloat16).contiguous();
+    sh = shc.data_ptr();
+  }
+  ahb_moe_combine(ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), sh, T, k, d, out.data_ptr(), st);
+  if (!a3.defined()) a3 = torch::empty({0}, x.options());
+  return {out, pos, off, row_src, xs, a1, a3, h, ys};
+}
+
+// backward: weight gradients are ADDED into dw*_acc (fp32, shapes of w*); returns {dx, dgate}
+std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch::Tensor w1, torch::Tensor w2,
+                                   c10::optional<torch::Tensor> w3, torch::Tensor pos, torch::Tensor off,
+                                   torch::Tensor row_src, torch::Tensor xs, torch::Tensor a1, torch::Tensor a3,
+                                   torch::Tensor h, torch::Tensor ys, torch::Tensor dw1_acc, torch::Tensor dw2_acc,
+                                   c10::optional<torch::Tensor> dw3_acc, bool swiglu) {
+  const int T = (int)dout.size(0), d = (int)dout.size(1), k = (int)gate.size(1);
+  const int E = (int)w1.size(0), F = (int)w1.size(2);
+  const int64_t Rcap = xs.size(0);
+  auto st = cur_stream();
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  auto gatec = gate.to(at::kFloat).contiguous();
+  check_acc(dw1_acc, w1.numel(), "dw1_acc");
+  check_acc(dw2_acc, w2.numel(), "dw2_acc");
+  auto dys = torch::empty({Rcap, d}, xs.options());
+  ahb_moe_zero_pad(dys.data_ptr(), row_src.data_ptr<int>(), Rcap, d, st);
+  auto dgate = torch::empty({T, k}, gatec.options());
+  ahb_moe_combine_bwd(doc.data_ptr(), ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), T, k, d,
+                      dys.data_ptr(), dgate.data_ptr<float>(), st);
+  int* err = err_word().data_ptr<int>();
+  auto dA1 = torch::empty({Rcap, F}, xs.options());
+  torch::Tensor dA3;
+  int rc;
+  if (swiglu) {
+    dA3 = torch::empty_like(dA1);
+    rc = ahb_moe_gemm(AHB_GEMM_DH_SWIGLU, dys.data_ptr(), nullptr, Rcap, d, w2.data_ptr(), nullptr, (int64_t)E * F, d,
+                      F, off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), dA3.data_ptr(), nullptr,
+                      a1.data_ptr(), a3.data_ptr(), 0.f, err, num_sms(), st);
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_DH_GELU, dys.data_ptr(), nullptr, Rcap, d, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+                      off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), nullptr, nullptr, a1.data_ptr(),
+                      nullptr, 0.f, err, num_sms(), st);
+  }
+  gemm_check(rc, "dh");
+  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, h.data_ptr(), nullptr, Rcap, F, dys.data_ptr(), nullptr, Rcap, d, 0,
+                    off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
+                    0.f, err, num_sms(), st);
+  gemm_check(rc, "wgrad w2");
+  auto dxs = torch::empty({Rcap, d}, xs.options());
+  if (swiglu) {
+    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), dA3.data_ptr(), Rcap, F, w1.data_ptr(), w3->data_ptr(),
+                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, d, 0, 2 * F, F / 64, dxs.data_ptr(), nullptr,
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "dx");
+    TORCH_CHECK(dw3_acc.has_value(), "moe_bwd: dw3_acc");
+    check_acc(*dw3_acc, w3->numel(), "dw3_acc");
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL, xs.data_ptr(), nullptr, Rcap, d, dA1.data_ptr(), dA3.data_ptr(), Rcap, F, 0,
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), dw3_acc->data_ptr<float>(),
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "wgrad w1/w3");
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), nullptr, Rcap, F, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
+                      off.data_ptr<int>(), E, d, 0, F, F / 64, dxs.data_ptr(), nullptr, nullptr, nullptr, nullptr,
+                      0.f, err, num_sms(), st);
+    gemm_check(rc, "dx");
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD, xs.data_ptr(), nullptr, Rcap, d, dA1.data_ptr(), nullptr, Rcap, F, 0,
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
+                      nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "wgrad w1");
+  }
+  auto dx = torch::empty({T, d}, xs.options());
+  ahb_moe_scatter_add(dxs.data_ptr(), pos.data_ptr<int>(), T, k, d, dx.data_ptr(), st);
+  return {dx, dgate};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -279,4 +434,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_bwd", &gdn_bwd);
   m.def("ssd_fwd", &ssd_fwd);
   m.def("ssd_bwd", &ssd_bwd);
+  m.def("gemm_dense", &gemm_dense);
+  m.def("gemm_error", &gemm_error);
+  m.def("gemm_error_reset", &gemm_error_reset);
+  m.def("moe_fwd", &moe_fwd);
+  m.def("moe_bwd", &moe_bwd);
 }

@@ -54,3 +54,29 @@ void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, 
 void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                  int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
                  float* dC, float* dA, cudaStream_t st);
+
+// moe_gemm.cu: tcgen05 grouped GEMM.  Returns 0 on success, <0 on a setup error.
+#define AHB_GEMM_DENSE 0        // C[M,N] = A[M,K] B[N,K]^T (single group)
+#define AHB_GEMM_FWD_SWIGLU 1   // h = silu(X W1_e) * (X W3_e); saves a1, a3
+#define AHB_GEMM_FWD_GELU 2     // h = gelu(X W1_e); saves a1
+#define AHB_GEMM_FWD_DOWN 3     // Y = H W2_e
+#define AHB_GEMM_DH_SWIGLU 4    // dH = dY W2_e^T -> dA1, dA3
+#define AHB_GEMM_DH_GELU 5      // dH = dY W2_e^T -> dA1
+#define AHB_GEMM_DX 6           // dX = dA1 W1_e^T (+ dA3 W3_e^T)
+#define AHB_GEMM_WGRAD 7        // dW_e += A_e^T B_e   (fp32 accumulate)
+#define AHB_GEMM_WGRAD_DUAL 8   // dW1_e += X_e^T dA1_e, dW3_e += X_e^T dA3_e
+int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
+                 const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
+                 int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
+                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st);
+
+// moe.cu: routing positions, gather / combine (+ backward)
+void ahb_moe_route(const int* eidx, int T, int k, int E, int* counts, int* off, int* pos, int* row_src, int64_t R_cap,
+                   cudaStream_t st);
+void ahb_moe_gather(const void* x, const int* row_src, int64_t R, int d, void* xs, cudaStream_t st);
+void ahb_moe_zero_pad(void* m, const int* row_src, int64_t R, int d, cudaStream_t st);
+void ahb_moe_combine(const void* ys, const int* pos, const float* gate, const void* shared, int T, int k, int d,
+                     void* out, cudaStream_t st);
+void ahb_moe_combine_bwd(const void* dout, const void* ys, const int* pos, const float* gate, int T, int k, int d,
+                         void* dys, float* dgate, cudaStream_t st);
+void ahb_moe_scatter_add(const void* dxs, const int* pos, int T, int k, int d, void* dx, cudaStream_t st);

@@ -1,0 +1,177 @@
+// MoE dispatch / combine kernels (dropless, reference `atomic_ops/moe_gmm.py:515-583`).
+//
+// Assignments are ordered like the reference's replicated token matrix:
+// a = j*T + t for top-k choice j of token t.  Rows of the expert-sorted matrix
+// keep that order inside each expert (a stable sort by expert id), and every
+// expert's segment is padded to a multiple of 128 rows so the grouped GEMM's
+// tiles never straddle two experts; padding rows are zero.
+#include "common.cuh"
+#include "launchers.h"
+
+using namespace ahb;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+// counts[e] = #assignments to expert e  (grid E, block 1024)
+__global__ void __launch_bounds__(1024) moe_count_kernel(const int* __restrict__ eidx, int64_t n, int* __restrict__ counts) {
+  __shared__ float sh[32];
+  const int e = blockIdx.x;
+  float c = 0.f;
+  for (int64_t a = threadIdx.x; a < n; a += blockDim.x) c += (eidx[a] == e) ? 1.f : 0.f;
+  c = block_sum(c, sh);
+  if (threadIdx.x == 0) counts[e] = (int)c;
+}
+
+// offsets (E+1) of the padded segments (single block)
+__global__ void moe_offsets_kernel(const int* __restrict__ counts, int E, int pad, int* __restrict__ off) {
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int e = 0; e < E; ++e) {
+      off[e] = s;
+      s += (counts[e] + pad - 1) / pad * pad;
+    }
+    off[E] = s;
+  }
+}
+
+// pos[a] = off[e] + stable rank of a among assignments to e; row_src[pos] = token (grid E, block 1024)
+__global__ void __launch_bounds__(1024) moe_positions_kernel(const int* __restrict__ eidx, int64_t n, int T,
+                                                             const int* __restrict__ off, int* __restrict__ pos,
+                                                             int* __restrict__ row_src) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int base = off[e];
+  for (int64_t a0 = 0; a0 < n; a0 += blockDim.x) {
+    const int64_t a = a0 + threadIdx.x;
+    const int f = (a < n && eidx[a] == e) ? 1 : 0;
+    const unsigned m = __ballot_sync(0xffffffffu, f);
+    const int wpre = __popc(m & ((1u << lane) - 1));
+    if (lane == 0) warp_tot[wid] = __popc(m);
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < wid; ++w) before += warp_tot[w];
+    if (f) {
+      const int p = base + carry + before + wpre;
+      pos[a] = p;
+      row_src[p] = (int)(a % T);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tot = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += warp_tot[w];
+      carry += tot;
+    }
+    __syncthreads();
+  }
+}
+
+// xs[r] = row_src[r] >= 0 ? x[row_src[r]] : 0   (one warp per row, 16-byte vectors)
+__global__ void moe_gather_kernel(const bf16* __restrict__ x, const int* __restrict__ row_src, int64_t R, int d,
+                                  bf16* __restrict__ xs) {
+  const int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const int lane = threadIdx.x & 31;
+  const int src = row_src[r];
+  uint4* dst = reinterpret_cast<uint4*>(xs + r * d);
+  const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)(src < 0 ? 0 : src) * d);
+  for (int c = lane; c < d / 8; c += 32) dst[c] = src >= 0 ? s[c] : make_uint4(0, 0, 0, 0);
+}
+
+// out[t] = sanitize(shared[t] + sanitize(sum_j gate[t,j] * sanitize(ys[pos[j*T+t]], 1e3)?), 1e3)
+// routed rows are clipped +-1e3 (reference sanitize after the second gmm), the sum is clipped again.
+__global__ void moe_combine_kernel(const bf16* __restrict__ ys, const int* __restrict__ pos, const float* __restrict__ gate,
+                                   const bf16* __restrict__ shared, int T, int k, int d, bf16* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int p = pos[(int64_t)j * T + t];
+      acc += gate[(int64_t)t * k + j] * sanitize(__bfloat162float(ys[(int64_t)p * d + c]), 1e3f);
+    }
+    if (shared) acc += __bfloat162float(shared[(int64_t)t * d + c]);
+    out[(int64_t)t * d + c] = __float2bfloat16_rn(sanitize(acc, 1e3f));
+  }
+}
+
+// dys[pos[a]] = gate[a] * dout[t];  dgate[t,j] = <dout[t], ys[pos[a]]>
+__global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ ys,
+                                       const int* __restrict__ pos, const float* __restrict__ gate, int T, int k,
+                                       int d, bf16* __restrict__ dys, float* __restrict__ dgate) {
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  for (int j = 0; j < k; ++j) {
+    const int p = pos[(int64_t)j * T + t];
+    const float g = gate[(int64_t)t * k + j];
+    float dot = 0.f;
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+      const float dv = __bfloat162float(dout[(int64_t)t * d + c]);
+      dys[(int64_t)p * d + c] = __float2bfloat16_rn(g * dv);
+      dot += dv * sanitize(__bfloat162float(ys[(int64_t)p * d + c]), 1e3f);
+    }
+    dot = block_sum(dot, sh);
+    if (threadIdx.x == 0) dgate[(int64_t)t * k + j] = dot;
+  }
+}
+
+// dx[t] = sum_j dxs[pos[j*T+t]]
+__global__ void moe_scatter_add_kernel(const bf16* __restrict__ dxs, const int* __restrict__ pos, int T, int k, int d,
+                                       bf16* __restrict__ dx) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += __bfloat162float(dxs[(int64_t)pos[(int64_t)j * T + t] * d + c]);
+    dx[(int64_t)t * d + c] = __float2bfloat16_rn(acc);
+  }
+}
+
+// zero the padding rows of a (R, d) bf16 matrix (rows with row_src < 0)
+__global__ void moe_zero_pad_kernel(bf16* __restrict__ m, const int* __restrict__ row_src, int64_t R, int d) {
+  const int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= R || row_src[r] >= 0) return;
+  uint4* dst = reinterpret_cast<uint4*>(m + r * d);
+  for (int c = threadIdx.x & 31; c < d / 8; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
+}
+
+}  // namespace
+
+void ahb_moe_route(const int* eidx, int T, int k, int E, int* counts, int* off, int* pos, int* row_src, int64_t R_cap,
+                   cudaStream_t st) {
+  const int64_t n = (int64_t)T * k;
+  cudaMemsetAsync(row_src, 0xff, R_cap * sizeof(int), st);
+  moe_count_kernel<<<E, 1024, 0, st>>>(eidx, n, counts);
+  moe_offsets_kernel<<<1, 32, 0, st>>>(counts, E, 128, off);
+  moe_positions_kernel<<<E, 1024, 0, st>>>(eidx, n, T, off, pos, row_src);
+}
+
+void ahb_moe_gather(const void* x, const int* row_src, int64_t R, int d, void* xs, cudaStream_t st) {
+  if (!R) return;
+  moe_gather_kernel<<<(unsigned)((R + 7) / 8), 256, 0, st>>>((const bf16*)x, row_src, R, d, (bf16*)xs);
+}
+
+void ahb_moe_zero_pad(void* m, const int* row_src, int64_t R, int d, cudaStream_t st) {
+  if (!R) return;
+  moe_zero_pad_kernel<<<(unsigned)((R + 7) / 8), 256, 0, st>>>((bf16*)m, row_src, R, d);
+}
+
+void ahb_moe_combine(const void* ys, const int* pos, const float* gate, const void* shared, int T, int k, int d,
+                     void* out, cudaStream_t st) {
+  if (!T) return;
+  moe_combine_kernel<<<T, 256, 0, st>>>((const bf16*)ys, pos, gate, (const bf16*)shared, T, k, d, (bf16*)out);
+}
+
+void ahb_moe_combine_bwd(const void* dout, const void* ys, const int* pos, const float* gate, int T, int k, int d,
+                         void* dys, float* dgate, cudaStream_t st) {
+  if (!T) return;
+  moe_combine_bwd_kernel<<<T, 256, 0, st>>>((const bf16*)dout, (const bf16*)ys, pos, gate, T, k, d, (bf16*)dys,
+                                            dgate);
+}
+
+void ahb_moe_scatter_add(const void* dxs, const int* pos, int T, int k, int d, void* dx, cudaStream_t st) {
+  if (!T) return;
+  moe_scatter_add_kernel<<<T, 256, 0, st>>>((const bf16*)dxs, pos, T, k, d, (bf16*)dx);
+}

@@ -1,0 +1,440 @@
+// Grouped GEMM for the MoE experts on the 5th-generation tensor cores (tcgen05).
+//
+// One persistent, warp-specialised kernel covers every expert GEMM of the MoE
+// forward and backward (reference `atomic_ops/moe_gmm.py:251-336`, megablox
+// gmm/tgmm):
+//   * M-grouped  (fwd, dgrad): rows of the expert-sorted token matrix are split in
+//     groups (one per expert, each padded to a multiple of 128 rows, so no tile
+//     straddles two experts); group e multiplies by expert e's weight.
+//   * K-grouped  (wgrad): the contraction runs over group e's token rows and the
+//     product is ADDED into expert e's fp32 gradient (the flat gradient store).
+// Roles per CTA (192 threads): warp 0 issues TMA tile loads (no multicast) into a
+// 4-stage 128B-swizzled ring; one thread of warp 1 issues tcgen05.mma into a
+// double-buffered TMEM accumulator (2 x 256 fp32 columns); warps 2-5 read the
+// accumulator with tcgen05.ld and run the fused epilogue (SwiGLU / GELU forward
+// with saved pre-activations, their backward, bf16 store or fp32 accumulate)
+// while the next tile's MMAs proceed.  Every mbarrier wait is bounded: on a
+// timeout the kernel records an error code, stops all roles and frees its TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstring>
+#include "common.cuh"
+#include "sm100.cuh"
+#include "launchers.h"
+
+using namespace ahb;
+using namespace ahb::sm100;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int BM = 128, BK = 64, STAGES = 4, NTHREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_BYTES = 256 * BK * 2;  // 32 KB (NB * BNacc = 256 columns)
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 512;
+
+enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5 };
+
+struct Params {
+  CUtensorMap ta0, ta1, tb0, tb1;
+  const int* grp_off;  // E+1 offsets (multiples of 128) into A's rows (M-grouped) or token rows (K-grouped)
+  int E, N, Mout, kb_split, kb_total, b_rows;
+  void* out0;
+  void* out1;
+  void* out2;
+  const bf16* aux0;
+  const bf16* aux1;
+  float clip;
+  int* err;
+};
+
+AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
+AHB_DEVICE float gelu_t(float x) {
+  const float k = 0.7978845608028654f;
+  return 0.5f * x * (1.f + tanhf(k * (x + 0.044715f * x * x * x)));
+}
+AHB_DEVICE float gelu_t_grad(float x) {
+  const float k = 0.7978845608028654f;
+  const float t = tanhf(k * (x + 0.044715f * x * x * x));
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k * (1.f + 3.f * 0.044715f * x * x);
+}
+AHB_DEVICE void store_bf16x32(bf16* dst, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+    __nv_bfloat162 p3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+    uint4 w;
+    w.x = *reinterpret_cast<uint32_t*>(&p0);
+    w.y = *reinterpret_cast<uint32_t*>(&p1);
+    w.z = *reinterpret_cast<uint32_t*>(&p2);
+    w.w = *reinterpret_cast<uint32_t*>(&p3);
+    *reinterpret_cast<uint4*>(dst + i) = w;
+  }
+}
+
+struct Tile {
+  int e, m0, n0, k0row, nkb;
+};
+
+template <bool KGROUP>
+AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, Tile& t) {
+  if (!KGROUP) {
+    const int mt = tile / n_tiles, nt = tile % n_tiles;
+    t.m0 = mt * BM;
+    int e = 0;
+    while (e + 1 < p.E && off[e + 1] <= t.m0) ++e;
+    t.e = e;
+    t.n0 = nt;
+    t.k0row = 0;
+    t.nkb = p.kb_total;
+  } else {
+    const int m_tiles = p.Mout / BM;
+    const int per_e = m_tiles * n_tiles;
+    t.e = tile / per_e;
+    const int r = tile % per_e;
+    t.m0 = (r / n_tiles) * BM;
+    t.n0 = r % n_tiles;
+    t.k0row = off[t.e];
+    t.nkb = (off[t.e + 1] - off[t.e]) / BK;
+  }
+  return true;
+}
+
+template <bool KGROUP, bool A_MN, bool B_MN, int NB, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
+  constexpr int BNA = 256 / NB;  // columns per accumulator
+  constexpr uint32_t IDESC = idesc_bf16(BM, BNA, A_MN, B_MN);
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* off = const_cast<int*>(reinterpret_cast<const int*>(tmem_slot + 2));  // E+1 ints (E <= 48)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i <= p.E; i += NTHREADS) off[i] = p.grp_off[i];
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = p.N / BNA;
+  const int total = KGROUP ? p.E * (p.Mout / BM) * n_tiles : (off[p.E] / BM) * n_tiles;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    prefetch_tmap(&p.ta0);
+    prefetch_tmap(&p.tb0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      Tile t;
+      decode<KGROUP>(p, off, tile, n_tiles, t);
+      const int n0 = t.n0 * BNA;
+      for (int kb = 0; kb < t.nkb; ++kb) {
+        if (!mbar_wait(empty + stage, phase ^ 1, abort_flag, p.err, 1)) { ok = false; break; }
+        unsigned char* sa = smem + stage * STAGE_BYTES;
+        unsigned char* sb = sa + A_BYTES;
+        mbar_expect_tx(full + stage, STAGE_BYTES);
+        const int part = (!KGROUP && kb >= p.kb_split) ? 1 : 0;
+        const int kk = (part ? kb - p.kb_split : kb) * BK;
+        const CUtensorMap* ma = part ? &p.ta1 : &p.ta0;
+        if (!KGROUP) {
+          if (A_MN) {
+            tma_load_2d(sa, ma, full + stage, t.m0, kk);
+            tma_load_2d(sa + 8192, ma, full + stage, t.m0 + 64, kk);
+          } else {
+            tma_load_2d(sa, ma, full + stage, kk, t.m0);
+          }
+        } else {
+          const int r = t.k0row + kb * BK;
+          tma_load_2d(sa, ma, full + stage, t.m0, r);
+          tma_load_2d(sa + 8192, ma, full + stage, t.m0 + 64, r);
+        }
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const CUtensorMap* mb = (NB == 2) ? (nb ? &p.tb1 : &p.tb0) : (part ? &p.tb1 : &p.tb0);
+          unsigned char* sbn = sb + nb * BNA * BK * 2;
+          if (!KGROUP) {
+            if (B_MN) {
+#pragma unroll
+              for (int i = 0; i < BNA / 64; ++i) tma_load_2d(sbn + i * 8192, mb, full + stage, n0 + 64 * i, t.e * p.b_rows + kk);
+            } else {
+              tma_load_2d(sbn, mb, full + stage, kk, t.e * p.b_rows + n0);
+            }
+          } else {
+            const int r = t.k0row + kb * BK;
+#pragma unroll
+            for (int i = 0; i < BNA / 64; ++i) tma_load_2d(sbn + i * 8192, mb, full + stage, n0 + 64 * i, r);
+          }
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) {  // let copies already in flight land before the CTA exits
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 2000000ull) {}
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      Tile t;
+      decode<KGROUP>(p, off, tile, n_tiles, t);
+      if (t.nkb == 0) continue;
+      if (!mbar_wait(tempty + acc, acc_phase ^ 1, abort_flag, p.err, 2)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d0 = tmem_base + acc * 256;
+      for (int kb = 0; kb < t.nkb; ++kb) {
+        if (!mbar_wait(full + stage, phase, abort_flag, p.err, 3)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+        const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = A_MN ? smem_desc(sa + k * 2048, 8192, 1024) : smem_desc(sa + k * 32, 16, 1024);
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            const uint32_t sbn = sb + nb * BNA * BK * 2;
+            const uint64_t bd = B_MN ? smem_desc(sbn + k * 2048, 8192, 1024) : smem_desc(sbn + k * 32, 16, 1024);
+            umma_bf16(d0 + nb * BNA, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+        }
+        issued = true;
+        umma_commit(empty + stage);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      umma_commit(tfull + acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (!ok && issued) {  // wait (bounded) for the MMAs already issued before freeing TMEM
+      umma_commit(drain);
+      volatile int dummy = 0;
+      mbar_wait(drain, 0, &dummy, nullptr, 0, 100000000ull);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      Tile t;
+      decode<KGROUP>(p, off, tile, n_tiles, t);
+      if (t.nkb == 0) continue;
+      if (!mbar_wait(tfull + acc, acc_phase, abort_flag, p.err, 4)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
+      const int row = t.m0 + row_in_tile;
+      const int n0 = t.n0 * BNA;
+#pragma unroll 1
+      for (int c = 0; c < BNA / 32; ++c) {
+        float v0[32];
+        tmem_ld32(tb + c * 32, v0);
+        const int col = n0 + c * 32;
+        const int64_t o = static_cast<int64_t>(row) * p.N + col;
+        if constexpr (EPI == EPI_STORE) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i], p.clip);
+          store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
+        } else if constexpr (EPI == EPI_SWIGLU_FWD) {
+          float v1[32], h[32];
+          tmem_ld32(tb + BNA + c * 32, v1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v0[i] = clampf(v0[i], p.clip);
+            v1[i] = clampf(v1[i], p.clip);
+            h[i] = v0[i] * sigmoidf_(v0[i]) * v1[i];
+          }
+          store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
+          store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
+          store_bf16x32(static_cast<bf16*>(p.out2) + o, v1);
+        } else if constexpr (EPI == EPI_GELU_FWD) {
+          float h[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v0[i] = clampf(v0[i], p.clip);
+            h[i] = gelu_t(v0[i]);
+          }
+          store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
+          store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
+        } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+          float d1[32], d3[32];
+          const bf16* a1p = p.aux0 + o;
+          const bf16* a3p = p.aux1 + o;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float a1 = __bfloat162float(a1p[i]), a3 = __bfloat162float(a3p[i]);
+            const float s = sigmoidf_(a1);
+            d1[i] = v0[i] * a3 * s * (1.f + a1 * (1.f - s));
+            d3[i] = v0[i] * a1 * s;
+          }
+          store_bf16x32(static_cast<bf16*>(p.out0) + o, d1);
+          store_bf16x32(static_cast<bf16*>(p.out1) + o, d3);
+        } else if constexpr (EPI == EPI_GELU_BWD) {
+          const bf16* a1p = p.aux0 + o;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1p[i]));
+          store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
+        } else {  // EPI_ACC: out_e[row, col] += acc  (fp32, (E, Mout, N))
+          const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
+          float* d0p = static_cast<float*>(p.out0) + oo;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 x = *reinterpret_cast<float4*>(d0p + i);
+            x.x += v0[i]; x.y += v0[i + 1]; x.z += v0[i + 2]; x.w += v0[i + 3];
+            *reinterpret_cast<float4*>(d0p + i) = x;
+          }
+          if constexpr (NB == 2) {
+            float v1[32];
+            tmem_ld32(tb + BNA + c * 32, v1);
+            float* d1p = static_cast<float*>(p.out1) + oo;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 x = *reinterpret_cast<float4*>(d1p + i);
+              x.x += v1[i]; x.y += v1[i + 1]; x.z += v1[i + 2]; x.w += v1[i + 3];
+              *reinterpret_cast<float4*>(d1p + i) = x;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: `rows` x `cols` row-major with row stride `ld` elements; box = {64, box_rows}.
+int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !ptr) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+template <bool KG, bool AMN, bool BMN, int NB, int EPI>
+int launch(const Params& p, int grid, cudaStream_t st) {
+  auto k = moe_gemm_kernel<KG, AMN, BMN, NB, EPI>;
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess) return -3;
+    init = true;
+  }
+  k<<<grid, NTHREADS, SMEM_BYTES, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace
+
+// kind: see launchers.h (AHB_GEMM_*)
+int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
+                 const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
+                 int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
+                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st) {
+  if (E + 1 > 48 || N % 128 != 0) return -10;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.grp_off = grp_off;
+  p.E = E;
+  p.N = N;
+  p.Mout = Mout;
+  p.kb_split = kb_split;
+  p.kb_total = K / BK;
+  p.b_rows = b_rows_per_group;
+  p.out0 = out0;
+  p.out1 = out1;
+  p.out2 = out2;
+  p.aux0 = static_cast<const bf16*>(aux0);
+  p.aux1 = static_cast<const bf16*>(aux1);
+  p.clip = clip;
+  p.err = err;
+  const bool kg = kind == AHB_GEMM_WGRAD || kind == AHB_GEMM_WGRAD_DUAL;
+  const bool a_mn = kg;
+  const bool b_mn = kg || kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_FWD_GELU || kind == AHB_GEMM_FWD_DOWN;
+  const int nb = (kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_WGRAD_DUAL) ? 2 : 1;
+  const int bna = 256 / nb;
+  if (N % bna != 0) return -11;
+  if (kg && Mout % BM != 0) return -12;
+  int rc = 0;
+  rc |= make_map(&p.ta0, a0, a_rows, a_cols, a_cols, a_mn ? 64 : BM);
+  if (a1) rc |= make_map(&p.ta1, a1, a_rows, a_cols, a_cols, a_mn ? 64 : BM);
+  rc |= make_map(&p.tb0, b0, b_rows_total, b_cols, b_cols, b_mn ? 64 : bna);
+  if (b1) rc |= make_map(&p.tb1, b1, b_rows_total, b_cols, b_cols, b_mn ? 64 : bna);
+  if (!a1) p.ta1 = p.ta0;
+  if (!b1) p.tb1 = p.tb0;
+  if (rc) return -20;
+  const int grid = num_sms;
+  switch (kind) {
+    case AHB_GEMM_DENSE: return launch<false, false, false, 1, EPI_STORE>(p, grid, st);
+    case AHB_GEMM_FWD_SWIGLU: return launch<false, false, true, 2, EPI_SWIGLU_FWD>(p, grid, st);
+    case AHB_GEMM_FWD_GELU: return launch<false, false, true, 1, EPI_GELU_FWD>(p, grid, st);
+    case AHB_GEMM_FWD_DOWN: return launch<false, false, true, 1, EPI_STORE>(p, grid, st);
+    case AHB_GEMM_DH_SWIGLU: return launch<false, false, false, 1, EPI_SWIGLU_BWD>(p, grid, st);
+    case AHB_GEMM_DH_GELU: return launch<false, false, false, 1, EPI_GELU_BWD>(p, grid, st);
+    case AHB_GEMM_DX: return launch<false, false, false, 1, EPI_STORE>(p, grid, st);
+    case AHB_GEMM_WGRAD: return launch<true, true, true, 1, EPI_ACC>(p, grid, st);
+    case AHB_GEMM_WGRAD_DUAL: return launch<true, true, true, 2, EPI_ACC>(p, grid, st);
+    default: return -30;
+  }
+}

@@ -102,27 +102,29 @@ class MoE(nn.Module):
         return top_idx, gate
 
     # ------------------------------------------------------------------ forward
+    def _shared(self, flat: torch.Tensor) -> torch.Tensor:
+        h = self.shared_w1(flat)
+        if self.swiglu:
+            h = F.silu(h) * self.shared_w3(flat)
+        else:
+            h = R.gelu_tanh(h)
+        if self.training and self.cfg.dropout_rate > 0:
+            h = F.dropout(h, self.cfg.dropout_rate)
+        return self.shared_w2(h)
+
     def forward(self, x: torch.Tensor, stats: Dict[str, torch.Tensor]) -> torch.Tensor:
         Bsz, L, d = x.shape
         flat = x.reshape(-1, d)
-        T = flat.shape[0]
         top_idx, gate = self.route(flat, stats)
-        if ops.use_cuda(flat):
+        shared = self._shared(flat) if self.n_shared > 0 else None
+        if ops.use_cuda(flat) and x.dtype == torch.bfloat16:
             from ..ops import kernels as K
-            routed = K.moe_routed(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3,
-                                  self.E, "swiglu" if self.swiglu else "gelu")
-        else:
-            routed = self._routed_eager(flat, top_idx, gate)
-        out = routed
-        if self.n_shared > 0:
-            h = self.shared_w1(flat)
-            if self.swiglu:
-                h = F.silu(h) * self.shared_w3(flat)
-            else:
-                h = R.gelu_tanh(h)
-            if self.training and self.cfg.dropout_rate > 0:
-                h = F.dropout(h, self.cfg.dropout_rate)
-            out = out + self.shared_w2(h).float()
+            out = K.moe_forward(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3, shared,
+                                "swiglu" if self.swiglu else "gelu")
+            return out.view(Bsz, L, d)
+        out = self._routed_eager(flat, top_idx, gate)
+        if shared is not None:
+            out = out + shared.float()
         out = R.sanitize(out.float(), 1e3)
         return out.view(Bsz, L, d).to(x.dtype)
 

@@ -258,19 +258,52 @@ def mamba2_layer(mod, x):
     return mod.out_proj(out)
 
 
-def moe_routed(flat, top_idx, gate, w1, w2, w3, E, act):
-    T, d = flat.shape
-    eidx = top_idx.t().reshape(-1)
-    perm = torch.argsort(eidx, stable=True)
-    sizes = torch.bincount(eidx, minlength=E)
-    rows = perm % T
-    xs = flat[rows]
-    y = grouped_ffn(xs, sizes, w1, w2, w3, act)
-    y = R.sanitize(y.float(), 1e3)
-    wgt = gate.t().reshape(-1)[perm]
-    out = torch.zeros(T, d, device=flat.device, dtype=torch.float32)
-    out.index_add_(0, rows, y * wgt[:, None])
-    return out
+class _MoE(torch.autograd.Function):
+    """Dropless top-k routed experts + combine on the tcgen05 grouped GEMM.
+
+    Forward: route positions -> gather -> fused up-projection (SwiGLU/GELU in the
+    epilogue) -> down-projection -> gated combine with the shared-expert output.
+    Backward: combine backward -> dH with the activation backward in the epilogue ->
+    dX (both up-projections in one K-concatenated GEMM) -> weight gradients added
+    straight into the fp32 gradient store."""
+
+    @staticmethod
+    def forward(ctx, x, top_idx, gate, w1, w2, w3, shared, swiglu):
+        bf = torch.bfloat16
+        xs_ = x.to(bf).contiguous()
+        w1b, w2b = w1.to(bf).contiguous(), w2.to(bf).contiguous()
+        w3b = None if w3 is None else w3.to(bf).contiguous()
+        outs = ext().moe_fwd(xs_, top_idx, gate.float(), w1b, w2b, w3b,
+                             None if shared is None else shared.to(bf), swiglu)
+        out, pos, off, row_src, xs, a1, a3, h, ys = outs
+        ctx.save_for_backward(gate, pos, off, row_src, xs, a1, a3, h, ys)
+        ctx.w = (w1, w2, w3, w1b, w2b, w3b)
+        ctx.swiglu = swiglu
+        ctx.has_shared = shared is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        gate, pos, off, row_src, xs, a1, a3, h, ys = ctx.saved_tensors
+        w1, w2, w3, w1b, w2b, w3b = ctx.w
+        a1c, d1 = _acc_for(w1)
+        a2c, d2 = _acc_for(w2)
+        a3c, d3 = _acc_for(w3) if w3 is not None else (None, False)
+        dx, dgate = ext().moe_bwd(dout.contiguous(), gate.float(), w1b, w2b, w3b, pos, off, row_src, xs, a1, a3, h,
+                                  ys, a1c, a2c, a3c, ctx.swiglu)
+        dshared = dout if ctx.has_shared else None
+        return (dx, None, dgate, _ret_grad(w1, a1c, d1), _ret_grad(w2, a2c, d2),
+                None if w3 is None else _ret_grad(w3, a3c, d3), dshared, None)
+
+
+def moe_forward(flat, top_idx, gate, w1, w2, w3, shared, act):
+    """Combined MoE output ``sanitize(shared + sum_j gate_j * expert_j(x), 1e3)`` in bf16."""
+    return _MoE.apply(flat, top_idx, gate, w1, w2, w3, shared, act == "swiglu")
+
+
+def gemm_error() -> int:
+    """Error word of the tcgen05 kernels (0 = no timed-out wait since the last reset)."""
+    return int(ext().gemm_error())
 
 
 def newton_schulz3(g):

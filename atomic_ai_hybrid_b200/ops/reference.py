@@ -287,12 +287,12 @@ def grouped_ffn(x_sorted: Tensor, group_sizes, w1: Tensor, w2: Tensor, w3: Optio
     sizes = [int(s) for s in group_sizes]
     for e, n in enumerate(sizes):
         xe = x_sorted[start:start + n]
-        h = xe @ w1[e]
+        h = sanitize(xe @ w1[e], 1e3)
         if act == "swiglu":
-            h = F.silu(h) * (xe @ w3[e])
+            h = F.silu(h) * sanitize(xe @ w3[e], 1e3)
         else:
             h = gelu_tanh(h)
-        outs.append(h @ w2[e])
+        outs.append(sanitize(h @ w2[e], 1e3))
         start += n
     return torch.cat(outs, 0) if outs else x_sorted.new_zeros(0, w2.shape[-1])
 
