@@ -2,7 +2,7 @@
 import pytest
 import torch
 
-from atomic_ai_hybrid_b200.ops import kernels as K
+from atomic_ai_hybrid_b200.ops import kernels as KN
 from atomic_ai_hybrid_b200.ops import reference as R
 from atomic_ai_hybrid_b200.ops._ext import ext
 
@@ -22,7 +22,7 @@ def test_gemm_dense(M, K, N):
     b = torch.randn(N, K, device=dev, dtype=torch.bfloat16)
     c = ext().gemm_dense(a, b)
     torch.cuda.synchronize()
-    assert K.gemm_error() == 0
+    assert KN.gemm_error() == 0
     ref = a.float() @ b.float().t()
     assert _rel(c, ref) < 1e-2, _rel(c, ref)
 
@@ -59,7 +59,7 @@ def test_moe_forward_backward(act, T, d, F, E, k):
     shared = (torch.randn(T, d, device=dev) * 0.1).to(torch.bfloat16)
     ins = [x, gate, w1, w2] + ([w3] if w3 is not None else [])
     xa = [t.clone().requires_grad_(True) for t in ins]
-    out = K.moe_forward(xa[0], top_idx, xa[1], xa[2], xa[3], xa[4] if w3 is not None else None, shared, act)
+    out = KN.moe_forward(xa[0], top_idx, xa[1], xa[2], xa[3], xa[4] if w3 is not None else None, shared, act)
     xr = [t.detach().float().clone().requires_grad_(True) for t in ins]
     ref = _moe_ref(xr[0], top_idx, xr[1], xr[2], xr[3], xr[4] if w3 is not None else None, shared, act)
     assert _rel(out, ref) < 2e-2, _rel(out, ref)
@@ -67,7 +67,7 @@ def test_moe_forward_backward(act, T, d, F, E, k):
     (out.float() * dout).sum().backward()
     (ref * dout).sum().backward()
     torch.cuda.synchronize()
-    assert K.gemm_error() == 0
+    assert KN.gemm_error() == 0
     for name, a, r in zip(["x", "gate", "w1", "w2", "w3"], xa, xr):
         assert a.grad is not None, name
         err = _rel(a.grad, r.grad)
