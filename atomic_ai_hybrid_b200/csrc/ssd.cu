@@ -517,3 +517,55 @@ void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, 
                                                           (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
                                                           (bf16*)dx, (bf16*)ddt, dB, dC, dA);
 }
+
+// ============================================================ allocation-free forward
+// See ssd_noalloc.h: scratch for the chunk states lives in this fixed device array.
+#include <cstdio>
+#include <mutex>
+#include "ssd_noalloc.h"
+
+static __device__ __align__(256) unsigned char g_ssd_noalloc_scratch[AHB_SSD_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm,
+                                   int B, int L, int H, void* y, cudaStream_t stream) {
+  if (!x || !dt || !A || !Bm || !Cm || !y || B <= 0 || L <= 0 || H <= 0 || L % C != 0) return AHB_NOALLOC_EINVAL;
+  const int NC = L / C;
+  const unsigned long long chunk_heads = (unsigned long long)B * H * NC;
+  if (chunk_heads > AHB_SSD_NOALLOC_MAX_CHUNK_HEADS) {
+    fprintf(stderr,
+            "ahb_ssd_fwd_noalloc: B*H*(L/64) = %llu exceeds the fixed scratch limit of %u chunk-heads (%u bytes)\n",
+            chunk_heads, (unsigned)AHB_SSD_NOALLOC_MAX_CHUNK_HEADS, (unsigned)AHB_SSD_NOALLOC_SCRATCH_BYTES);
+    return AHB_NOALLOC_ETOOBIG;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AHB_NOALLOC_ESETUP;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch) != cudaSuccess || !p) return AHB_NOALLOC_ESETUP;
+      if (cudaFuncSetAttribute(ssd_state_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)SMEM_STATE_F) != cudaSuccess ||
+          cudaFuncSetAttribute(ssd_out_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_OUT_F) !=
+              cudaSuccess)
+        return AHB_NOALLOC_ESETUP;
+      g_noalloc_ptr[dev] = p;
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  float* state_buf = static_cast<float*>(base);
+  float* cuml = state_buf + chunk_heads * (unsigned long long)(P * N);
+  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                  (const bf16*)Bm, L, H, state_buf, cuml);
+  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, stream>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
+  ssd_out_fwd_kernel<<<dim3(NC, B), 256, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                              (const bf16*)Cm, state_buf, L, H, (bf16*)y);
+  return cudaGetLastError() == cudaSuccess ? AHB_NOALLOC_OK : AHB_NOALLOC_ELAUNCH;
+}
