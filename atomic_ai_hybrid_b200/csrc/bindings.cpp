@@ -418,6 +418,72 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
   return {dx, dgate};
 }
 
+// ------------------------------------------------------------ fused optimizer
+// table: int64 (S, 8) = [off, coff, len, label, group, flags, bias_row, 0]; gscale fp32 (S,)
+// returns {segs (uint8 device), cstart (int32 device, S+1)} and the block count in cstart[S]
+std::vector<torch::Tensor> optim_make_table(torch::Tensor table, torch::Tensor gscale, int64_t device_index) {
+  TORCH_CHECK(table.device().is_cpu() && table.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 8,
+              "optim_make_table: int64 (S,8) CPU table");
+  const int64_t S = table.size(0);
+  auto t = table.contiguous();
+  auto gs = gscale.to(at::kFloat).contiguous();
+  auto host = torch::empty({S * (int64_t)sizeof(AhbSegInfo)}, torch::kUInt8);
+  auto cs = torch::empty({S + 1}, torch::kInt32);
+  AhbSegInfo* info = reinterpret_cast<AhbSegInfo*>(host.data_ptr<uint8_t>());
+  const int64_t* tp = t.data_ptr<int64_t>();
+  int* cp = cs.data_ptr<int>();
+  const int chunk = ahb_optim_chunk();
+  int64_t blocks = 0;
+  for (int64_t i = 0; i < S; ++i) {
+    info[i].off = tp[i * 8 + 0];
+    info[i].coff = tp[i * 8 + 1];
+    info[i].len = tp[i * 8 + 2];
+    info[i].label = (int32_t)tp[i * 8 + 3];
+    info[i].group = (int32_t)tp[i * 8 + 4];
+    info[i].flags = (int32_t)tp[i * 8 + 5];
+    info[i].bias_row = (int32_t)tp[i * 8 + 6];
+    info[i].gscale = gs.data_ptr<float>()[i];
+    info[i].pad = 0;
+    cp[i] = (int)blocks;
+    blocks += (info[i].len + chunk - 1) / chunk;
+  }
+  TORCH_CHECK(blocks < (1ll << 31), "optim table: too many blocks");
+  cp[S] = (int)blocks;
+  auto dev = torch::Device(torch::kCUDA, (int)device_index);
+  return {host.to(dev), cs.to(dev)};
+}
+
+void optim_prepare(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torch::Tensor grad_shard,
+                   torch::Tensor master, double inv, torch::Tensor red, torch::Tensor flags) {
+  TORCH_CHECK(red.scalar_type() == at::kDouble && flags.scalar_type() == at::kInt, "optim_prepare: red f64, flags i32");
+  ahb_optim_prepare(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
+                    (int)(cstart.numel() - 1), (int)nblocks, grad_shard.data_ptr<float>(), master.data_ptr<float>(),
+                    (float)inv, red.data_ptr<double>(), flags.data_ptr<int>(), cur_stream());
+}
+
+void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torch::Tensor master, torch::Tensor m,
+                 torch::Tensor v, torch::Tensor grad_shard, torch::Tensor coef, torch::Tensor compute,
+                 c10::optional<torch::Tensor> frac, std::vector<double> lr, std::vector<double> wd, double bc1,
+                 double bc2) {
+  TORCH_CHECK(lr.size() == 5 && wd.size() == 5, "optim_apply: 5 labels");
+  AhbOptimArgs a;
+  for (int i = 0; i < 5; ++i) { a.lr[i] = (float)lr[i]; a.wd[i] = (float)wd[i]; }
+  a.bc1 = (float)bc1;
+  a.bc2 = (float)bc2;
+  const float* fp = nullptr;
+  int fe = 0;
+  torch::Tensor fc;
+  if (frac.has_value() && frac->defined()) {
+    fc = frac->to(at::kFloat).contiguous();
+    fp = fc.data_ptr<float>();
+    fe = (int)fc.size(-1);
+  }
+  ahb_optim_apply(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
+                  (int)(cstart.numel() - 1), (int)nblocks, master.data_ptr<float>(), m.data_ptr<float>(),
+                  v.data_ptr<float>(), grad_shard.data_ptr<float>(), coef.data_ptr<float>(), compute.data_ptr(), fp, fe,
+                  a, cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -439,4 +505,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error_reset", &gemm_error_reset);
   m.def("moe_fwd", &moe_fwd);
   m.def("moe_bwd", &moe_bwd);
+  m.def("optim_make_table", &optim_make_table);
+  m.def("optim_prepare", &optim_prepare);
+  m.def("optim_apply", &optim_apply);
 }

@@ -80,3 +80,33 @@ void ahb_moe_combine(const void* ys, const int* pos, const float* gate, const vo
 void ahb_moe_combine_bwd(const void* dout, const void* ys, const int* pos, const float* gate, int T, int k, int d,
                          void* dys, float* dgate, cudaStream_t st);
 void ahb_moe_scatter_add(const void* dxs, const int* pos, int T, int k, int d, void* dx, cudaStream_t st);
+
+// optim.cu: fused optimizer over the owned shard
+#define AHB_LABEL_MUON 0
+#define AHB_LABEL_LION 1
+#define AHB_LABEL_ADAMW_DECAY 2
+#define AHB_LABEL_ADAMW_NODECAY 3
+#define AHB_LABEL_FROZEN 4
+#define AHB_SEG_COMPUTE_FP32 1
+#define AHB_SEG_ROUTER_TEMP 2
+#define AHB_SEG_EXPERT_BIAS 4
+#define AHB_SEG_REQUIRES_GRAD 8
+struct AhbSegInfo {
+  int64_t off;    // state-space offset relative to the owned shard
+  int64_t coff;   // compute-space offset (16-bit units)
+  int64_t len;
+  int32_t label, group, flags, bias_row;
+  float gscale;
+  int32_t pad;
+};
+struct AhbOptimArgs {
+  float lr[5];
+  float wd[5];
+  float bc1, bc2;
+};
+int ahb_optim_chunk();
+void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
+                       const float* master, float inv, double* red, int* flags, cudaStream_t st);
+void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
+                     const float* grad, const float* coef, void* compute, const float* frac, int fracE,
+                     AhbOptimArgs args, cudaStream_t st);

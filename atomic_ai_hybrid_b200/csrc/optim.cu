@@ -1,0 +1,144 @@
+// Fused optimizer step over the owned shard of the flat parameter store
+// (reference `train_setup.py:490-550` apply step + `optimizer.py:84-239`).
+//
+// optim_prepare: avg = grad/n_accum; sum(avg^2) (global norm, NaN-propagating);
+//   per diagnostic-group non-finite flags; g = nan_to_num(avg, 0) * grad_scale;
+//   sum(g^2) (the clip_by_global_norm input); was_clipped = any |p| >= 100.
+// optim_apply: per segment label -- muon (direction precomputed), lion,
+//   adamw (decay / no decay), frozen -- then clip +-100 + nan_to_num, the
+//   router_temp decay-to-init and the expert_bias sign update, and writes the
+//   fp32 master plus the compute copy (bf16 or fp32) in the same pass.
+// Blocks cover CHUNK elements of one segment; a block finds its segment by
+// binary search over the per-segment chunk prefix.
+#include "common.cuh"
+#include "launchers.h"
+
+using namespace ahb;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int CHUNK = 4096;
+constexpr int THREADS = 256;
+
+AHB_DEVICE int find_seg(const int* cstart, int S, int b) {
+  int lo = 0, hi = S;  // cstart[lo] <= b < cstart[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cstart[mid] <= b) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo* __restrict__ segs,
+                                                                const int* __restrict__ cstart, int S,
+                                                                float* __restrict__ grad,
+                                                                const float* __restrict__ master, float inv,
+                                                                double* __restrict__ red, int* __restrict__ flags) {
+  __shared__ float sh[THREADS / 32];
+  const int b = blockIdx.x;
+  const int s = find_seg(cstart, S, b);
+  const AhbSegInfo sg = segs[s];
+  const int64_t base = (int64_t)(b - cstart[s]) * CHUNK;
+  const int64_t rem = sg.len - base;
+  const int n = (int)(rem < CHUNK ? rem : CHUNK);
+  float sa = 0.f, sgq = 0.f;
+  int nonfin = 0, clipped = 0;
+  const bool rg = sg.flags & AHB_SEG_REQUIRES_GRAD;
+  for (int i = threadIdx.x; i < n; i += THREADS) {
+    const int64_t idx = sg.off + base + i;
+    if (rg) {
+      const float a = grad[idx] * inv;
+      sa += a * a;
+      const bool fin = isfinite(a);
+      nonfin |= !fin;
+      const float g = (fin ? a : 0.f) * sg.gscale;
+      grad[idx] = g;
+      sgq += g * g;
+    }
+    clipped |= fabsf(master[idx]) >= 100.f;
+  }
+  sa = block_sum(sa, sh);
+  sgq = block_sum(sgq, sh);
+  if (threadIdx.x == 0) {
+    atomicAdd(red, (double)sa);
+    atomicAdd(red + 1, (double)sgq);
+  }
+  if (__syncthreads_or(clipped) && threadIdx.x == 0) atomicOr(flags, 1);
+  if (__syncthreads_or(nonfin) && threadIdx.x == 0) atomicOr(flags + 1 + sg.group, 1);
+}
+
+AHB_DEVICE float signf_(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
+
+__global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* __restrict__ segs,
+                                                              const int* __restrict__ cstart, int S,
+                                                              float* __restrict__ master, float* __restrict__ m,
+                                                              float* __restrict__ v, const float* __restrict__ grad,
+                                                              const float* __restrict__ coef_p,
+                                                              uint16_t* __restrict__ compute,
+                                                              const float* __restrict__ frac, int fracE,
+                                                              AhbOptimArgs a) {
+  const int b = blockIdx.x;
+  const int s = find_seg(cstart, S, b);
+  const AhbSegInfo sg = segs[s];
+  const int64_t base = (int64_t)(b - cstart[s]) * CHUNK;
+  const int64_t rem = sg.len - base;
+  const int n = (int)(rem < CHUNK ? rem : CHUNK);
+  const float coef = *coef_p;
+  const int lab = sg.label;
+  const float lr = a.lr[lab], wd = a.wd[lab];
+  const bool rg = sg.flags & AHB_SEG_REQUIRES_GRAD;
+  for (int i = threadIdx.x; i < n; i += THREADS) {
+    const int64_t j = base + i;
+    const int64_t idx = sg.off + j;
+    float p = master[idx];
+    if (lab == AHB_LABEL_MUON) {
+      if (rg) p += -lr * grad[idx] - lr * wd * p;
+    } else if (lab == AHB_LABEL_LION) {
+      if (rg) {
+        const float g = grad[idx] * coef;
+        const float mm = m[idx];
+        const float u = signf_(0.1f * g + 0.9f * mm) + wd * p;
+        m[idx] = 0.99f * mm + 0.01f * g;
+        p -= lr * u;
+      }
+    } else if (lab == AHB_LABEL_ADAMW_DECAY || lab == AHB_LABEL_ADAMW_NODECAY) {
+      const float g = rg ? grad[idx] * coef : 0.f;
+      const float mm = 0.9f * m[idx] + 0.1f * g;
+      const float vv = 0.999f * v[idx] + 0.001f * g * g;
+      m[idx] = mm;
+      v[idx] = vv;
+      const float u = (mm / a.bc1) / (sqrtf(vv / a.bc2) + 1e-8f) + wd * p;
+      p -= lr * u;
+    }
+    p = sanitize(p, 100.f);
+    if (sg.flags & AHB_SEG_ROUTER_TEMP) p -= 0.02f * (p - 10.f);
+    if ((sg.flags & AHB_SEG_EXPERT_BIAS) && frac) {
+      const float f = frac[(int64_t)sg.bias_row * fracE + j];
+      p += 0.02f * (f > 1.f / (float)sg.len ? -1.f : 1.f);
+    }
+    master[idx] = p;
+    if (sg.flags & AHB_SEG_COMPUTE_FP32)
+      reinterpret_cast<float*>(compute + sg.coff)[j] = p;
+    else
+      reinterpret_cast<bf16*>(compute + sg.coff)[j] = __float2bfloat16_rn(p);
+  }
+}
+
+}  // namespace
+
+void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
+                       const float* master, float inv, double* red, int* flags, cudaStream_t st) {
+  if (nblocks <= 0) return;
+  optim_prepare_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, grad, master, inv, red, flags);
+}
+
+void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
+                     const float* grad, const float* coef, void* compute, const float* frac, int fracE,
+                     AhbOptimArgs args, cudaStream_t st) {
+  if (nblocks <= 0) return;
+  optim_apply_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, master, m, v, grad, coef, (uint16_t*)compute,
+                                                  frac, fracE, args);
+}
+
+int ahb_optim_chunk() { return CHUNK; }

@@ -307,7 +307,57 @@ def gemm_error() -> int:
 
 
 def newton_schulz3(g):
+    """Muon orthogonalisation (three Newton-Schulz steps) with cuBLAS GEMMs."""
     return R.newton_schulz3(g)
+
+
+# ----------------------------------------------------------------- fused optimizer
+_WD = {"muon": 0.01, "lion": 0.1, "adamw_decay": 0.01, "adamw_nodecay": 0.0, "frozen": 0.0}
+_ORDER = ("muon", "lion", "adamw_decay", "adamw_nodecay", "frozen")
+
+
+def _optim_table(opt):
+    if getattr(opt, "_segs", None) is not None:
+        return
+    from ..optim.schedule import LABEL_ID, diag_group_of, path_key
+    st = opt.store
+    rows, gs, nblocks = [], [], 0
+    chunk = 4096
+    for s in opt.owned:
+        key = path_key(s.name)
+        flags = (1 if s.fp32 else 0) | (2 if "router_temp" in key else 0) | (4 if "expert_bias" in key else 0) \
+            | (8 if s.param.requires_grad else 0)
+        brow = opt.bias_index(s) if "expert_bias" in key else 0
+        rows.append([s.offset - st.lo, s.coff, s.numel, LABEL_ID[s.label], opt.group_idx[diag_group_of(s.name)],
+                     flags, brow, 0])
+        gs.append(s.grad_scale)
+        nblocks += (s.numel + chunk - 1) // chunk
+    dev = st.device.index if st.device.index is not None else torch.cuda.current_device()
+    opt._segs, opt._cstart = ext().optim_make_table(torch.tensor(rows, dtype=torch.int64),
+                                                    torch.tensor(gs, dtype=torch.float32), dev)
+    opt._nblocks = nblocks
+
+
+def optim_prepare(opt, inv, red):
+    """One pass over the owned gradients: average, non-finite flags, both norms, was_clipped."""
+    _optim_table(opt)
+    st = opt.store
+    redd = torch.zeros(2, dtype=torch.float64, device=st.device)
+    flags = torch.zeros(8, dtype=torch.int32, device=st.device)
+    ext().optim_prepare(opt._segs, opt._cstart, opt._nblocks, st.grad[st.lo:st.hi], st.master, float(inv), redd, flags)
+    red[0:2] = redd.float()
+    red[2:] = flags.float()
+
+
+def optim_apply(opt, lrs, coef, frac):
+    """Per-label update + clip + hooks + compute-copy write, one kernel."""
+    st = opt.store
+    t = opt.count + 1
+    lr = [float(lrs[k]) for k in _ORDER]
+    wd = [_WD[k] for k in _ORDER]
+    ext().optim_apply(opt._segs, opt._cstart, opt._nblocks, st.master, opt.m, opt.v, st.grad[st.lo:st.hi],
+                      coef.reshape(1).float().contiguous(), st.compute, frac, lr, wd, 1.0 - 0.9 ** t,
+                      1.0 - 0.999 ** t)
 
 
 _ = math

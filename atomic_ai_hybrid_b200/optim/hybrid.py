@@ -120,11 +120,11 @@ class HybridOptimizer:
                 g = (gbuf[sl] * coef).view(s.shape)
                 gbuf[sl] = R.newton_schulz3(g).reshape(-1) if not use_k else K.newton_schulz3(g).reshape(-1)
         if use_k:
-            K.optim_apply(self, lrs, coef, assignment_frac)
+            K.optim_apply(self, lrs, coef, assignment_frac)  # also writes the compute copy
         else:
             self._apply_eager(lrs, coef, gbuf, assignment_frac)
+            st.publish_owned()
         self.count += 1
-        st.publish_owned()
         return self._info(global_norm, is_finite, red, skipped=False)
 
     def _apply_eager(self, lrs, coef, gbuf, assignment_frac):
