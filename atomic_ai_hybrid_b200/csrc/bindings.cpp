@@ -287,7 +287,8 @@ torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b) {
               b.scalar_type() == at::kBFloat16, "gemm_dense: bf16 contiguous");
   int64_t M = a.size(0), K = a.size(1), N = b.size(0);
   TORCH_CHECK(M % 128 == 0 && K % 64 == 0 && N % 256 == 0, "gemm_dense: M%128, K%64, N%256");
-  auto off = torch::tensor({0, (int)M}, torch::dtype(torch::kInt32).device(a.device()));
+  auto off = torch::zeros({2}, torch::dtype(torch::kInt32).device(a.device()));
+  off.narrow(0, 1, 1).fill_((int)M);
   auto c = torch::empty({M, N}, a.options());
   int rc = ahb_moe_gemm(AHB_GEMM_DENSE, a.data_ptr(), nullptr, M, K, b.data_ptr(), nullptr, N, K, 0,
                         off.data_ptr<int>(), 1, (int)N, 0, (int)K, (int)(K / 64), c.data_ptr(), nullptr, nullptr,
@@ -484,6 +485,54 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
                   a, cur_stream());
 }
 
+// ------------------------------------------------------------ fused LM head + cross entropy
+// forward: logits = h W^T (bf16, tcgen05), then loss + dlogits in place.  Returns {sum_loss, count, dlogits, hpad}
+std::vector<torch::Tensor> ce_fused_fwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, double ls) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == at::kBFloat16 && h.dim() == 2, "ce: h bf16 (T,d)");
+  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.is_contiguous() && W.dim() == 2, "ce: W bf16 (V,d)");
+  const int64_t T = h.size(0), d = h.size(1), V = W.size(0);
+  TORCH_CHECK(W.size(1) == d && d % 256 == 0 && V % 64 == 0, "ce: d % 256 == 0 and V % 64 == 0");
+  const int64_t Tp = (T + 127) / 128 * 128;
+  auto hp = h.contiguous();
+  auto lab = labels.to(at::kLong).contiguous();
+  if (Tp != T) {
+    hp = torch::cat({hp, torch::zeros({Tp - T, d}, h.options())}, 0);
+    lab = torch::cat({lab, torch::full({Tp - T}, -100, lab.options())}, 0);
+  }
+  auto logits = torch::empty({Tp, V}, h.options());
+  auto off = torch::tensor({0, (int)Tp}, torch::dtype(torch::kInt32).device(h.device()));
+  int rc = ahb_moe_gemm(AHB_GEMM_DENSE, hp.data_ptr(), nullptr, Tp, d, W.data_ptr(), nullptr, V, d, 0,
+                        off.data_ptr<int>(), 1, (int)V, 0, (int)d, (int)(d / 64), logits.data_ptr(), nullptr, nullptr,
+                        nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream());
+  gemm_check(rc, "ce logits");
+  auto acc = torch::zeros({2}, h.options().dtype(at::kFloat));
+  ahb_ce_rows(logits.data_ptr(), lab.data_ptr<int64_t>(), Tp, (int)V, (float)ls, acc.data_ptr<float>(),
+              acc.data_ptr<float>() + 1, cur_stream());
+  return {acc.narrow(0, 0, 1), acc.narrow(0, 1, 1), logits, hp};
+}
+
+// backward: dh = g * dlogits W ; dW_acc += g * dlogits^T h   (g: device scalar)
+torch::Tensor ce_fused_bwd(torch::Tensor dlogits, torch::Tensor hp, torch::Tensor W, torch::Tensor g,
+                           torch::Tensor dW_acc, int64_t T) {
+  const int64_t Tp = hp.size(0), d = hp.size(1), V = W.size(0);
+  check_acc(dW_acc, V * d, "dW_acc");
+  auto gc = g.to(at::kFloat).reshape({1}).contiguous();
+  auto off = torch::zeros({2}, torch::dtype(torch::kInt32).device(hp.device()));
+  off.narrow(0, 1, 1).fill_((int)Tp);
+  auto dh = torch::empty({Tp, d}, hp.options());
+  int* err = err_word().data_ptr<int>();
+  int rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, dlogits.data_ptr(), nullptr, Tp, V, W.data_ptr(), nullptr, V, d, 0,
+                        off.data_ptr<int>(), 1, (int)d, 0, (int)V, (int)(V / 64), dh.data_ptr(), nullptr, nullptr,
+                        nullptr, nullptr, 0.f, err, num_sms(), cur_stream(), gc.data_ptr<float>());
+  gemm_check(rc, "ce dh");
+  TORCH_CHECK(V % 128 == 0, "ce: V must be a multiple of 128 for the weight gradient");
+  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, dlogits.data_ptr(), nullptr, Tp, V, hp.data_ptr(), nullptr, Tp, d, 0,
+                    off.data_ptr<int>(), 1, (int)d, (int)V, 0, 0, dW_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
+                    nullptr, 0.f, err, num_sms(), cur_stream(), gc.data_ptr<float>());
+  gemm_check(rc, "ce dW");
+  return dh.narrow(0, 0, T);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -506,6 +555,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_fwd", &moe_fwd);
   m.def("moe_bwd", &moe_bwd);
   m.def("optim_make_table", &optim_make_table);
+  m.def("ce_fused_fwd", &ce_fused_fwd);
+  m.def("ce_fused_bwd", &ce_fused_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
 }

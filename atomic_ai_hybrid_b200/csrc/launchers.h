@@ -68,7 +68,8 @@ void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, 
 int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
-                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st);
+                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st,
+                 const float* alpha = nullptr);
 
 // moe.cu: routing positions, gather / combine (+ backward)
 void ahb_moe_route(const int* eidx, int T, int k, int E, int* counts, int* off, int* pos, int* row_src, int64_t R_cap,
@@ -110,3 +111,7 @@ void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nbl
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
                      const float* grad, const float* coef, void* compute, const float* frac, int fracE,
                      AhbOptimArgs args, cudaStream_t st);
+
+// ce.cu: label-smoothed cross entropy over bf16 logits rows, gradient written in place
+void ahb_ce_rows(void* logits, const int64_t* labels, int64_t R, int V, float ls, float* loss_sum, float* count,
+                 cudaStream_t st);

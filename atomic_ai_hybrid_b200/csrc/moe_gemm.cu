@@ -47,6 +47,7 @@ struct Params {
   void* out2;
   const bf16* aux0;
   const bf16* aux1;
+  const float* alpha;  // optional device scalar multiplying the product (STORE / ACC epilogues)
   float clip;
   int* err;
 };
@@ -141,7 +142,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_tiles = p.N / BNA;
+  const int n_tiles = (p.N + BNA - 1) / BNA;
   const int total = KGROUP ? p.E * (p.Mout / BM) * n_tiles : (off[p.E] / BM) * n_tiles;
 
   if (warp == 0 && lane == 0) {
@@ -258,15 +259,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
       const int row = t.m0 + row_in_tile;
       const int n0 = t.n0 * BNA;
+      const float alpha = p.alpha ? *p.alpha : 1.f;
 #pragma unroll 1
       for (int c = 0; c < BNA / 32; ++c) {
+        const int col = n0 + c * 32;
+        if (col >= p.N) break;  // partial last tile (N % 32 == 0)
         float v0[32];
         tmem_ld32(tb + c * 32, v0);
-        const int col = n0 + c * 32;
         const int64_t o = static_cast<int64_t>(row) * p.N + col;
         if constexpr (EPI == EPI_STORE) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i], p.clip);
+          for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i] * alpha, p.clip);
           store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
         } else if constexpr (EPI == EPI_SWIGLU_FWD) {
           float v1[32], h[32];
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             float4 x = *reinterpret_cast<float4*>(d0p + i);
-            x.x += v0[i]; x.y += v0[i + 1]; x.z += v0[i + 2]; x.w += v0[i + 3];
+            x.x += alpha * v0[i]; x.y += alpha * v0[i + 1]; x.z += alpha * v0[i + 2]; x.w += alpha * v0[i + 3];
             *reinterpret_cast<float4*>(d0p + i) = x;
           }
           if constexpr (NB == 2) {
@@ -323,7 +326,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
               float4 x = *reinterpret_cast<float4*>(d1p + i);
-              x.x += v1[i]; x.y += v1[i + 1]; x.z += v1[i + 2]; x.w += v1[i + 3];
+              x.x += alpha * v1[i]; x.y += alpha * v1[i + 1]; x.z += alpha * v1[i + 2]; x.w += alpha * v1[i + 3];
               *reinterpret_cast<float4*>(d1p + i) = x;
             }
           }
@@ -391,8 +394,8 @@ int launch(const Params& p, int grid, cudaStream_t st) {
 int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
-                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st) {
-  if (E + 1 > 48 || N % 128 != 0) return -10;
+                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st, const float* alpha) {
+  if (E + 1 > 48 || N % 32 != 0 || K % 64 != 0) return -10;
   Params p;
   memset(&p, 0, sizeof(p));
   p.grp_off = grp_off;
@@ -408,13 +411,14 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
   p.aux0 = static_cast<const bf16*>(aux0);
   p.aux1 = static_cast<const bf16*>(aux1);
   p.clip = clip;
+  p.alpha = alpha;
   p.err = err;
   const bool kg = kind == AHB_GEMM_WGRAD || kind == AHB_GEMM_WGRAD_DUAL;
   const bool a_mn = kg;
   const bool b_mn = kg || kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_FWD_GELU || kind == AHB_GEMM_FWD_DOWN;
   const int nb = (kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_WGRAD_DUAL) ? 2 : 1;
   const int bna = 256 / nb;
-  if (N % bna != 0) return -11;
+  if (N % bna != 0 && kind != AHB_GEMM_DENSE && kind != AHB_GEMM_FWD_DOWN) return -11;
   if (kg && Mout % BM != 0) return -12;
   int rc = 0;
   rc |= make_map(&p.ta0, a0, a_rows, a_cols, a_cols, a_mn ? 64 : BM);

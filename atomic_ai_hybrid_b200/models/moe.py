@@ -89,7 +89,8 @@ class MoE(nn.Module):
         biased = logits + self.expert_bias.detach().float()[None, :]
         top_idx = torch.topk(biased, k, dim=-1).indices
         gate = torch.softmax(logits.gather(1, top_idx), dim=-1)
-        counts = torch.bincount(top_idx.reshape(-1), minlength=E).float()
+        counts = torch.zeros(E, device=flat_x.device, dtype=torch.float32).scatter_add_(
+            0, top_idx.reshape(-1), torch.ones(top_idx.numel(), device=flat_x.device, dtype=torch.float32))
         stats["assignment_frac"] = (counts / (flat_x.shape[0] * k)).detach()
         probs = torch.nan_to_num(torch.softmax(logits, -1), nan=0.0, posinf=0.0, neginf=0.0)
         mean_probs = probs.mean(0)

@@ -198,19 +198,31 @@ def grouped_ffn(x_sorted, group_sizes, w1, w2, w3, act):
                          None if w3 is None else w3.to(dt), act)
 
 
+class _FusedCE(torch.autograd.Function):
+    """Tied LM head + label-smoothed CE: bf16 logits from the tcgen05 GEMM (as the
+    reference computes them), loss and dlogits in one pass, then dh and the fp32
+    weight gradient from two more GEMMs in backward."""
+
+    @staticmethod
+    def forward(ctx, h, labels, weight, ls):
+        wb = weight if weight.dtype == torch.bfloat16 else weight.to(torch.bfloat16)
+        sum_loss, count, dlogits, hp = ext().ce_fused_fwd(h.to(torch.bfloat16), wb.contiguous(), labels, ls)
+        ctx.save_for_backward(dlogits, hp)
+        ctx.weight, ctx.wb, ctx.T = weight, wb, h.shape[0]
+        ctx.hdtype = h.dtype
+        return sum_loss.reshape(()), count.reshape(())
+
+    @staticmethod
+    def backward(ctx, g_loss, g_count):
+        dlogits, hp = ctx.saved_tensors
+        acc, direct = _acc_for(ctx.weight)
+        dh = ext().ce_fused_bwd(dlogits, hp, ctx.wb.contiguous(), g_loss.reshape(1), acc, ctx.T)
+        return dh.to(ctx.hdtype), None, _ret_grad(ctx.weight, acc, direct), None
+
+
 def cross_entropy(h, labels, weight, label_smoothing):
-    import torch.utils.checkpoint as ckpt
-    wd = weight.to(h.dtype)
-
-    def piece(hc, lc):
-        return R.label_smoothed_ce((hc @ wd.t()).float(), lc, label_smoothing)
-
-    tot = h.new_zeros((), dtype=torch.float32)
-    cnt = h.new_zeros((), dtype=torch.float32)
-    for s in range(0, h.shape[0], 4096):
-        a, c = ckpt.checkpoint(piece, h[s:s + 4096], labels[s:s + 4096], use_reentrant=False)
-        tot, cnt = tot + a, cnt + c
-    return tot, cnt
+    """``(sum_loss, sum_mask)`` of the tied LM head; see ``_FusedCE``."""
+    return _FusedCE.apply(h, labels, weight, float(label_smoothing))
 
 
 def gdn2_layer(mod, x):

@@ -8,6 +8,12 @@ ranks, runs the hybrid optimizer on the owned shard and gathers the updated
 weights back to every rank (reference ``distributed_apply_step``,
 `train_setup.py:490-550`).  The assignment fractions used by the expert-bias
 hook are averaged over the micro-steps of the step and over ranks.
+
+With ``cuda_graph=True`` the whole micro-step (forward, loss, backward and the
+gradient accumulation into the store) is captured once as a CUDA graph and
+replayed for every micro-batch of the same shape: one launch per micro-step
+instead of thousands.  The graph is built at the start of a step (its warm-up
+iterations are discarded by zeroing the gradients before the real micro-steps).
 """
 from __future__ import annotations
 
@@ -25,7 +31,7 @@ class Trainer:
                  compute_dtype: torch.dtype = torch.bfloat16, device=None,
                  group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
                  ce_chunk_size: int = 2048, collinearity_coef: Optional[float] = None,
-                 skip_nonfinite: bool = False):
+                 skip_nonfinite: bool = False, cuda_graph: bool = False):
         self.model = model
         self.cfg = model.cfg
         self.group = group
@@ -43,48 +49,107 @@ class Trainer:
                                    skip_nonfinite=skip_nonfinite)
         self.ce_chunk_size = ce_chunk_size
         self.collinearity_coef = collinearity_coef
-        self._frac: List[torch.Tensor] = []
         self.global_step = 0
+        dev = self.store.device
+        n_moe = sum(1 for n, _ in model.named_parameters() if n.endswith("expert_bias"))
+        self._frac_sum = torch.zeros(max(n_moe, 1), self.cfg.e_routed, device=dev)
+        self._loss_sum = torch.zeros((), device=dev)
+        self._n_micro = 0
+        self.cuda_graph = cuda_graph and dev.type == "cuda"
+        self._graph = None
+        self._graph_key = None
+        self.graph_kernel_launches = 0
 
     def _allreduce_sum(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
         return t
 
-    def micro_step(self, batch: Dict[str, torch.Tensor]):
+    # ------------------------------------------------------------ micro-step
+    def _micro_body(self, batch: Dict[str, torch.Tensor]):
         self.model.train()
         loss, info = compute_loss(self.model, batch, deterministic=False, ce_chunk_size=self.ce_chunk_size,
                                   collinearity_coef=self.collinearity_coef)
         loss.backward()
         if info.get("assignment_frac") is not None:
-            self._frac.append(info["assignment_frac"])
+            self._frac_sum += info["assignment_frac"]
+        self._loss_sum += loss.detach()
         return loss.detach(), info
 
-    def apply(self, n_accum: int) -> Dict[str, torch.Tensor]:
+    def micro_step(self, batch: Dict[str, torch.Tensor]):
+        if self.cuda_graph and self._graph is not None and self._graph_key == self._key(batch):
+            self._s_ids.copy_(batch["input_ids"])
+            self._s_lab.copy_(batch["labels"])
+            self._graph.replay()
+            self._n_micro += 1
+            return self._s_loss, self._s_info
+        out = self._micro_body(batch)
+        self._n_micro += 1
+        return out
+
+    @staticmethod
+    def _key(batch):
+        return tuple(batch["input_ids"].shape), batch["input_ids"].dtype
+
+    def build_graph(self, batch: Dict[str, torch.Tensor], warmup: int = 2) -> None:
+        """Capture one micro-step for this batch shape.  Leaves gradients zeroed."""
+        from ..utils.counters import launch_counter
+        self._s_ids = batch["input_ids"].clone()
+        self._s_lab = batch["labels"].clone()
+        sb = {"input_ids": self._s_ids, "labels": self._s_lab}
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._micro_body(sb)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        before = launch_counter.count
+        was_on = launch_counter.on
+        launch_counter.enable()
+        with torch.cuda.graph(g):
+            self._s_loss, self._s_info = self._micro_body(sb)
+        if not was_on:
+            launch_counter.disable()
+        self.graph_kernel_launches = launch_counter.count - before
+        launch_counter.count = before
+        torch.cuda.synchronize()
+        self._graph = g
+        self._graph_key = self._key(batch)
+        self.reset_accumulators()
+
+    def reset_accumulators(self) -> None:
+        self.store.zero_grad()
+        self._frac_sum.zero_()
+        self._loss_sum.zero_()
+        self._n_micro = 0
+
+    # ------------------------------------------------------------ apply
+    def apply(self, n_accum: Optional[int] = None) -> Dict[str, torch.Tensor]:
+        n = n_accum if n_accum is not None else max(self._n_micro, 1)
         frac = None
-        if self._frac:
-            frac = torch.stack(self._frac).mean(0)
+        if self._n_micro > 0:
+            frac = self._frac_sum / self._n_micro
             if self.world > 1:
                 dist.all_reduce(frac, group=self.group)
                 frac = frac / self.world
-        self._frac = []
         if self.comm is not None:
             self.comm.reduce_scatter_grads()
-        out = self.opt.step(n_accum, frac)
+        out = self.opt.step(n, frac)
         if self.comm is not None:
             self.comm.all_gather_params()
-        self.store.zero_grad()
+        out["loss"] = self._loss_sum / max(self._n_micro, 1)
+        self.reset_accumulators()
         self.global_step += 1
         return out
 
     def train_step(self, micro_batches: List[Dict[str, torch.Tensor]]):
-        losses = []
+        if self.cuda_graph and (self._graph is None or self._graph_key != self._key(micro_batches[0])):
+            self.build_graph(micro_batches[0])
         for b in micro_batches:
-            loss, _ = self.micro_step(b)
-            losses.append(loss)
-        out = self.apply(len(micro_batches))
-        out["loss"] = torch.stack(losses).mean()
-        return out
+            self.micro_step(b)
+        return self.apply(len(micro_batches))
 
     @torch.no_grad()
     def eval_loss(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:

@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override num_layers (debug only; invalid for the bench)")
     ap.add_argument("--optimizer", default="adamw", choices=["adamw", "hybrid"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="disable CUDA-graph capture of the micro-step")
     return ap.parse_args()
 
 
@@ -144,7 +145,9 @@ def main():
                 p.normal_(0.0, 0.02)
     model = model.to(dev)
     nparams = count_params(model)
-    trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev)
+    use_graph = args.impl == "cuda" and not args.no_graph
+    trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev,
+                      cuda_graph=use_graph)
     trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
 
     S, mb = args.seq_len, args.micro_batch
@@ -179,6 +182,8 @@ def main():
     ev1.record()
     torch.cuda.synchronize()
     launches = launch_counter.count
+    if use_graph:  # kernels inside the replayed micro-step graph
+        launches += trainer.graph_kernel_launches * n_micro * args.steps
     launch_counter.disable()
     barrier()
     torch.cuda.synchronize()
