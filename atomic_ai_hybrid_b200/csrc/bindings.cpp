@@ -287,8 +287,7 @@ torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b) {
               b.scalar_type() == at::kBFloat16, "gemm_dense: bf16 contiguous");
   int64_t M = a.size(0), K = a.size(1), N = b.size(0);
   TORCH_CHECK(M % 128 == 0 && K % 64 == 0 && N % 256 == 0, "gemm_dense: M%128, K%64, N%256");
-  auto off = torch::zeros({2}, torch::dtype(torch::kInt32).device(a.device()));
-  off.narrow(0, 1, 1).fill_((int)M);
+  auto off = torch::arange(0, M + 1, M, torch::dtype(torch::kInt32).device(a.device()));
   auto c = torch::empty({M, N}, a.options());
   int rc = ahb_moe_gemm(AHB_GEMM_DENSE, a.data_ptr(), nullptr, M, K, b.data_ptr(), nullptr, N, K, 0,
                         off.data_ptr<int>(), 1, (int)N, 0, (int)K, (int)(K / 64), c.data_ptr(), nullptr, nullptr,
@@ -500,7 +499,7 @@ std::vector<torch::Tensor> ce_fused_fwd(torch::Tensor h, torch::Tensor W, torch:
     lab = torch::cat({lab, torch::full({Tp - T}, -100, lab.options())}, 0);
   }
   auto logits = torch::empty({Tp, V}, h.options());
-  auto off = torch::tensor({0, (int)Tp}, torch::dtype(torch::kInt32).device(h.device()));
+  auto off = torch::arange(0, Tp + 1, Tp, torch::dtype(torch::kInt32).device(h.device()));
   int rc = ahb_moe_gemm(AHB_GEMM_DENSE, hp.data_ptr(), nullptr, Tp, d, W.data_ptr(), nullptr, V, d, 0,
                         off.data_ptr<int>(), 1, (int)V, 0, (int)d, (int)(d / 64), logits.data_ptr(), nullptr, nullptr,
                         nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream());
@@ -517,8 +516,7 @@ torch::Tensor ce_fused_bwd(torch::Tensor dlogits, torch::Tensor hp, torch::Tenso
   const int64_t Tp = hp.size(0), d = hp.size(1), V = W.size(0);
   check_acc(dW_acc, V * d, "dW_acc");
   auto gc = g.to(at::kFloat).reshape({1}).contiguous();
-  auto off = torch::zeros({2}, torch::dtype(torch::kInt32).device(hp.device()));
-  off.narrow(0, 1, 1).fill_((int)Tp);
+  auto off = torch::arange(0, Tp + 1, Tp, torch::dtype(torch::kInt32).device(hp.device()));
   auto dh = torch::empty({Tp, d}, hp.options());
   int* err = err_word().data_ptr<int>();
   int rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, dlogits.data_ptr(), nullptr, Tp, V, W.data_ptr(), nullptr, V, d, 0,
