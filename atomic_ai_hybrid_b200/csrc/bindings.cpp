@@ -62,8 +62,11 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor scale
   auto sc = scale.to(at::kFloat).contiguous();
   if (dscale_acc.has_value()) check_acc(*dscale_acc, D, "dscale_acc");
   auto dx = torch::empty_like(xc);
+  torch::Tensor part;
+  if (dscale_acc.has_value()) part = torch::zeros({(int64_t)ahb_rmsnorm_bwd_blocks(M, D), D}, xc.options().dtype(at::kFloat));
   ahb_rmsnorm_bwd(dyc.data_ptr(), xc.data_ptr(), sc.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
-                  opt_ptr(dscale_acc), M, D, dt_code(xc), cur_stream());
+                  opt_ptr(dscale_acc), part.defined() ? part.data_ptr<float>() : nullptr, M, D, dt_code(xc),
+                  cur_stream());
   return dx;
 }
 

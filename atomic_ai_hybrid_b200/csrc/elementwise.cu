@@ -108,13 +108,22 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const T* __restrict__ 
     }
   }
   if (dscale) {
-    // every group of the block holds partials for the same columns: add them all
+    // partial column sums of this block -> dscale_part[blockIdx.x * D + c] (reduced by colsum_add_kernel)
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       int c = i * 32 * G + gl;
-      if (c < D) atomicAdd(dscale + c, acc[i]);
+      if (c < D) atomicAdd(dscale + (int64_t)blockIdx.x * D + c, acc[i]);
     }
   }
+}
+
+// out[c] += sum_b part[b * D + c]
+__global__ void colsum_add_kernel(const float* __restrict__ part, int nb, int D, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= D) return;
+  float s = 0.f;
+  for (int b = 0; b < nb; ++b) s += part[(int64_t)b * D + c];
+  out[c] += s;
 }
 
 // ----------------------------------------------------------------- causal conv1d
@@ -173,6 +182,8 @@ __global__ void conv1d_fwd_kernel(const T* __restrict__ x, int64_t xs, const WT*
 
 // Backward.  dpre[t] = dy[t] * act'(pre[t]) (masked by the clamp);
 // dx[s] = sum_k w[k] dpre[s + W-1-k]; dw[k] += sum_t dpre[t] x[t-(W-1)+k]; db += sum_t dpre[t].
+constexpr int CONV_SUB = 8;  // 16-step tiles per thread in the backward (fewer weight-grad atomics)
+
 template <typename T, typename WT, int W>
 __global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT* __restrict__ w,
                                   const float* __restrict__ bias, const T* __restrict__ dy, T* __restrict__ dx,
@@ -180,10 +191,11 @@ __global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT*
                                   bool silu, float clip) {
   const int cg = C / 8;
   int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int nt = (L + CONV_TT - 1) / CONV_TT;
+  const int span = CONV_TT * CONV_SUB;
+  const int nt = (L + span - 1) / span;
   if (idx >= (int64_t)B * nt * cg) return;
   const int c0 = (int)(idx % cg) * 8;
-  const int tb = (int)((idx / cg) % nt) * CONV_TT;
+  const int tspan = (int)((idx / cg) % nt) * span;
   const int b = (int)(idx / ((int64_t)cg * nt));
   float wk[8][W], bs[8];
 #pragma unroll
@@ -192,63 +204,67 @@ __global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT*
     for (int k = 0; k < W; ++k) wk[j][k] = to_f(w[(c0 + j) * W + k]);
     bs[j] = bias ? bias[c0 + j] : 0.f;
   }
-  // x window covering [tb-(W-1), tb+TT+W-2]; dpre for t in [tb, tb+TT+W-2]
-  constexpr int NX = CONV_TT + 2 * (W - 1);
   float dwl[8][W], dbl[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) { dbl[j] = 0.f;
+  for (int j = 0; j < 8; ++j) {
+    dbl[j] = 0.f;
 #pragma unroll
-    for (int k = 0; k < W; ++k) dwl[j][k] = 0.f; }
-  // dpre ring: we compute dpre for t in [tb, tb+TT+W-2] (needed by dx of s in [tb, tb+TT-1])
-  float dp[CONV_TT + W - 1][8];
-#pragma unroll
-  for (int i = 0; i < CONV_TT + W - 1; ++i) {
-    int t = tb + i;
-    if (t >= L) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dp[i][j] = 0.f;
-      continue;
-    }
-    float xv[W][8];
-#pragma unroll
-    for (int k = 0; k < W; ++k) {
-      int tx = t - (W - 1) + k;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) xv[k][j] = tx >= 0 ? to_f(x[((int64_t)b * L + tx) * xs + c0 + j]) : 0.f;
-    }
-    const T* dyr = dy + ((int64_t)b * L + t) * C + c0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float a = bs[j];
-#pragma unroll
-      for (int k = 0; k < W; ++k) a += wk[j][k] * xv[k][j];
-      float g = to_f(dyr[j]);
-      float post = a;
-      if (silu) {
-        float s = sigmoidf_(a);
-        post = a * s;
-        g *= s * (1.f + a * (1.f - s));
-      }
-      if (clip > 0.f && fabsf(post) > clip) g = 0.f;
-      dp[i][j] = g;
-      if (i < CONV_TT) {  // weight/bias grads counted once per t (owned t range)
-        dbl[j] += g;
-#pragma unroll
-        for (int k = 0; k < W; ++k) dwl[j][k] += g * xv[k][j];
-      }
-    }
+    for (int k = 0; k < W; ++k) dwl[j][k] = 0.f;
   }
+  for (int sub = 0; sub < CONV_SUB; ++sub) {
+    const int tb = tspan + sub * CONV_TT;
+    if (tb >= L) break;
+    // dpre for t in [tb, tb+TT+W-2] (needed by dx of s in [tb, tb+TT-1])
+    float dp[CONV_TT + W - 1][8];
 #pragma unroll
-  for (int i = 0; i < CONV_TT; ++i) {
-    int s = tb + i;
-    if (s >= L) break;
-    T* dxr = dx + ((int64_t)b * L + s) * dxs + c0;
+    for (int i = 0; i < CONV_TT + W - 1; ++i) {
+      int t = tb + i;
+      if (t >= L) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float a = 0.f;
+        for (int j = 0; j < 8; ++j) dp[i][j] = 0.f;
+        continue;
+      }
+      float xv[W][8];
 #pragma unroll
-      for (int k = 0; k < W; ++k) a += wk[j][k] * dp[i + (W - 1) - k][j];
-      dxr[j] = from_f<T>(a);
+      for (int k = 0; k < W; ++k) {
+        int tx = t - (W - 1) + k;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xv[k][j] = tx >= 0 ? to_f(x[((int64_t)b * L + tx) * xs + c0 + j]) : 0.f;
+      }
+      const T* dyr = dy + ((int64_t)b * L + t) * C + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float a = bs[j];
+#pragma unroll
+        for (int k = 0; k < W; ++k) a += wk[j][k] * xv[k][j];
+        float g = to_f(dyr[j]);
+        float post = a;
+        if (silu) {
+          float sg = sigmoidf_(a);
+          post = a * sg;
+          g *= sg * (1.f + a * (1.f - sg));
+        }
+        if (clip > 0.f && fabsf(post) > clip) g = 0.f;
+        dp[i][j] = g;
+        if (i < CONV_TT) {  // weight/bias grads counted once per t (owned t range)
+          dbl[j] += g;
+#pragma unroll
+          for (int k = 0; k < W; ++k) dwl[j][k] += g * xv[k][j];
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < CONV_TT; ++i) {
+      int sidx = tb + i;
+      if (sidx >= L) break;
+      T* dxr = dx + ((int64_t)b * L + sidx) * dxs + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float a = 0.f;
+#pragma unroll
+        for (int k = 0; k < W; ++k) a += wk[j][k] * dp[i + (W - 1) - k][j];
+        dxr[j] = from_f<T>(a);
+      }
     }
   }
 #pragma unroll
@@ -257,14 +273,7 @@ __global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT*
 #pragma unroll
     for (int k = 0; k < W; ++k) atomicAdd(dw + (c0 + j) * W + k, dwl[j][k]);
   }
-  (void)NX;
 }
-
-
-
-// x: (B, L, C) possibly a column slice (stride(1) = xs >= C, stride(2) = 1).
-
-// Returns dx (B,L,C) contiguous; dw_acc (C,W) fp32 and db_acc (C,) fp32 are ADDED to.
 
 // ----------------------------------------------------------------- grad accumulate / embedding
 template <typename T>
@@ -312,6 +321,11 @@ void ahb_sanitize(void* out, const void* in, int64_t n, int dtype, float clip, c
   else sanitize_kernel<float><<<ew_blocks(n, 256), 256, 0, st>>>((float*)out, (const float*)in, n, clip);
 }
 
+static int rms_bwd_blocks(int64_t M, int D) {
+  const int G = D <= 1024 ? 1 : (D <= 2048 ? 2 : (D <= 4096 ? 4 : 8));
+  return (int)std::min<int64_t>((M + 8 / G - 1) / (8 / G), (int64_t)sm_count() * 2);
+}
+
 #define RMS_DISPATCH(KER, ...)                                                     \
   if (D <= 256) KER(T, 8, 1, __VA_ARGS__);                                         \
   else if (D <= 512) KER(T, 16, 1, __VA_ARGS__);                                   \
@@ -335,19 +349,25 @@ void ahb_rmsnorm_fwd(const void* x, const float* scale, void* y, float* rstd, in
   else rms_fwd_t<float>(x, scale, y, rstd, M, D, eps, st);
 }
 
-#define RMS_B(T, V, G, _) rmsnorm_bwd_kernel<T, V, G><<<(unsigned)std::min<int64_t>((M + 8 / G - 1) / (8 / G), \
-    (int64_t)sm_count() * 8), 256, 0, st>>>((const T*)dy, (const T*)x, s, r, (T*)dx, ds, M, D)
+#define RMS_B(T, V, G, _) rmsnorm_bwd_kernel<T, V, G><<<(unsigned)rms_bwd_blocks(M, D), 256, 0, st>>>( \
+    (const T*)dy, (const T*)x, s, r, (T*)dx, ds, M, D)
 template <typename T>
 static void rms_bwd_t(const void* dy, const void* x, const float* s, const float* r, void* dx, float* ds, int64_t M,
                       int D, cudaStream_t st) {
   RMS_DISPATCH(RMS_B, 0)
 }
 #undef RMS_B
+int ahb_rmsnorm_bwd_blocks(int64_t M, int D) { return rms_bwd_blocks(M, D); }
+
+// dscale_part: zeroed fp32 scratch of ahb_rmsnorm_bwd_blocks(M, D) * D floats (or null);
+// the column sums are added into dscale_acc.
 void ahb_rmsnorm_bwd(const void* dy, const void* x, const float* scale, const float* rstd, void* dx, float* dscale_acc,
-                     int64_t M, int D, int dtype, cudaStream_t st) {
+                     float* dscale_part, int64_t M, int D, int dtype, cudaStream_t st) {
   if (M == 0) return;
-  if (dtype == AHB_BF16) rms_bwd_t<bf16>(dy, x, scale, rstd, dx, dscale_acc, M, D, st);
-  else rms_bwd_t<float>(dy, x, scale, rstd, dx, dscale_acc, M, D, st);
+  float* ds = dscale_acc ? dscale_part : nullptr;
+  if (dtype == AHB_BF16) rms_bwd_t<bf16>(dy, x, scale, rstd, dx, ds, M, D, st);
+  else rms_bwd_t<float>(dy, x, scale, rstd, dx, ds, M, D, st);
+  if (dscale_acc) colsum_add_kernel<<<(D + 255) / 256, 256, 0, st>>>(dscale_part, rms_bwd_blocks(M, D), D, dscale_acc);
 }
 
 void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,
@@ -364,7 +384,7 @@ void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const 
 void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, const void* dy, void* dx,
                     float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
                     cudaStream_t st) {
-  int64_t n = (int64_t)B * ((L + CONV_TT - 1) / CONV_TT) * (C / 8);
+  int64_t n = (int64_t)B * ((L + CONV_TT * CONV_SUB - 1) / (CONV_TT * CONV_SUB)) * (C / 8);
   if (n == 0) return;
   unsigned blocks = (unsigned)((n + 127) / 128);
 #define CB(T, WT) conv1d_bwd_kernel<T, WT, 4><<<blocks, 128, 0, st>>>((const T*)x, xs, (const WT*)w, bias, (const T*)dy, \

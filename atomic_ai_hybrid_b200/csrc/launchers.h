@@ -11,8 +11,9 @@
 void ahb_sanitize(void* out, const void* in, int64_t n, int dtype, float clip, cudaStream_t st);
 void ahb_rmsnorm_fwd(const void* x, const float* scale, void* y, float* rstd, int64_t M, int D, int dtype, float eps,
                      cudaStream_t st);
+int ahb_rmsnorm_bwd_blocks(int64_t M, int D);
 void ahb_rmsnorm_bwd(const void* dy, const void* x, const float* scale, const float* rstd, void* dx, float* dscale_acc,
-                     int64_t M, int D, int dtype, cudaStream_t st);
+                     float* dscale_part, int64_t M, int D, int dtype, cudaStream_t st);
 void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,
                     int C, int dtype, int silu, float clip, cudaStream_t st);
 void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, const void* dy, void* dx,

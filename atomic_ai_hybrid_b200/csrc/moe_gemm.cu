@@ -294,11 +294,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
           store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
         } else if constexpr (EPI == EPI_SWIGLU_BWD) {
           float d1[32], d3[32];
-          const bf16* a1p = p.aux0 + o;
-          const bf16* a3p = p.aux1 + o;
+          bf16 a1v[32], a3v[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
+            *reinterpret_cast<uint4*>(a3v + i) = *reinterpret_cast<const uint4*>(p.aux1 + o + i);
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float a1 = __bfloat162float(a1p[i]), a3 = __bfloat162float(a3p[i]);
+            const float a1 = __bfloat162float(a1v[i]), a3 = __bfloat162float(a3v[i]);
             const float s = sigmoidf_(a1);
             d1[i] = v0[i] * a3 * s * (1.f + a1 * (1.f - s));
             d3[i] = v0[i] * a1 * s;
@@ -306,9 +310,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
           store_bf16x32(static_cast<bf16*>(p.out0) + o, d1);
           store_bf16x32(static_cast<bf16*>(p.out1) + o, d3);
         } else if constexpr (EPI == EPI_GELU_BWD) {
-          const bf16* a1p = p.aux0 + o;
+          bf16 a1v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1p[i]));
+          for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1v[i]));
           store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
         } else {  // EPI_ACC: out_e[row, col] += acc  (fp32, (E, Mout, N))
           const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;

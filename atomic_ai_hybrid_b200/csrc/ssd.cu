@@ -168,19 +168,42 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(float* __restrict__ buf, 
   const int p = e / N;
   const int64_t base = ((int64_t)b * H + h) * NC;
   float S = s0 ? s0[((int64_t)b * H + h) * P * N + e] : 0.f;
+  constexpr int U = 8;  // loads for U chunks are issued before the dependent updates
   if (!reverse) {
-    for (int n = 0; n < NC; ++n) {
-      float* q = buf + (base + n) * P * N + e;
-      const float se = *q;
-      *q = S;
-      S = sanitize(S * __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) + se, 1e4f);
+    for (int n0 = 0; n0 < NC; n0 += U) {
+      float se[U], dc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int n = n0 + u;
+        se[u] = n < NC ? buf[(base + n) * P * N + e] : 0.f;
+        dc[u] = n < NC ? __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) : 1.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int n = n0 + u;
+        if (n < NC) {
+          buf[(base + n) * P * N + e] = S;
+          S = sanitize(S * dc[u] + se[u], 1e4f);
+        }
+      }
     }
   } else {
-    for (int n = NC - 1; n >= 0; --n) {
-      float* q = buf + (base + n) * P * N + e;
-      const float gn = *q;
-      *q = S;
-      S = S * __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) + gn;
+    for (int n0 = NC - 1; n0 >= 0; n0 -= U) {
+      float gn[U], dc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int n = n0 - u;
+        gn[u] = n >= 0 ? buf[(base + n) * P * N + e] : 0.f;
+        dc[u] = n >= 0 ? __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) : 1.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int n = n0 - u;
+        if (n >= 0) {
+          buf[(base + n) * P * N + e] = S;
+          S = S * dc[u] + gn[u];
+        }
+      }
     }
   }
   if (s_final) s_final[((int64_t)b * H + h) * P * N + e] = S;

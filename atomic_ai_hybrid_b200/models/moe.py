@@ -27,6 +27,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
+from ..parallel.context import dp_mean
 from .layers import Dense, lecun_normal_
 
 ROUTER_LOGIT_CLIP = 8.0
@@ -93,7 +94,7 @@ class MoE(nn.Module):
             0, top_idx.reshape(-1), torch.ones(top_idx.numel(), device=flat_x.device, dtype=torch.float32))
         stats["assignment_frac"] = (counts / (flat_x.shape[0] * k)).detach()
         probs = torch.nan_to_num(torch.softmax(logits, -1), nan=0.0, posinf=0.0, neginf=0.0)
-        mean_probs = probs.mean(0)
+        mean_probs = dp_mean(probs.mean(0))  # batch-global, as the reference's GSPMD mean
         stats["aux_loss"] = E * (mean_probs * mean_probs).sum()
         stats["z_loss"] = torch.logsumexp(logits, -1).square().mean()
         stats["expert_utilization"] = mean_probs.detach()

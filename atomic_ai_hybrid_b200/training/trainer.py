@@ -43,6 +43,9 @@ class Trainer:
                                     compute_dtype=compute_dtype, device=device)
         self.comm = None
         if self.world > 1:
+            from ..parallel.context import ParallelContext, get_parallel_context, set_parallel_context
+            if get_parallel_context().dp_world != self.world:
+                set_parallel_context(ParallelContext(dp_group=group, dp_world=self.world))
             from ..parallel.fsdp import make_shard_comm
             self.comm = make_shard_comm(self.store, group, comm)
         self.opt = HybridOptimizer(self.store, total_steps, reduce_fn=self._allreduce_sum,
@@ -136,7 +139,9 @@ class Trainer:
                 frac = frac / self.world
         if self.comm is not None:
             self.comm.reduce_scatter_grads()
-        out = self.opt.step(n, frac)
+        # every rank's loss is the mean over its own tokens, and the reduction sums the
+        # ranks: dividing by n_accum * world gives the gradient of the global-batch mean
+        out = self.opt.step(n * self.world, frac)
         if self.comm is not None:
             self.comm.all_gather_params()
         out["loss"] = self._loss_sum / max(self._n_micro, 1)
