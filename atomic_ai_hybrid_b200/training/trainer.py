@@ -156,6 +156,18 @@ class Trainer:
             self.micro_step(b)
         return self.apply(len(micro_batches))
 
+    def close(self) -> None:
+        """Release the captured CUDA graph.  A graph that contains NCCL collectives
+        (the data-parallel MoE statistics) must be released before the process
+        group is destroyed, or the teardown waits on it forever."""
+        if self._graph is not None:
+            torch.cuda.synchronize()
+            self._graph.reset()
+            self._graph = None
+            self._graph_key = None
+            self._s_loss = self._s_info = None
+            torch.cuda.synchronize()
+
     @torch.no_grad()
     def eval_loss(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:
         self.model.eval()

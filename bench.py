@@ -123,7 +123,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     from atomic_ai_hybrid_b200 import get_preset, ops
     from atomic_ai_hybrid_b200.models import HybridMoEModel, count_params
@@ -239,9 +239,30 @@ def main():
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
+    shutdown(trainer, world)
+
+
+def shutdown(trainer, world: int, deadline_s: float = 120.0) -> None:
+    """Release the CUDA graph (it may hold NCCL collectives) and tear the process
+    group down; if teardown stalls past the deadline, exit the process directly."""
+    import gc
+    import threading
+
+    def force_exit():
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
+
+    timer = threading.Timer(deadline_s, force_exit)
+    timer.daemon = True
+    timer.start()
+    trainer.close()
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    timer.cancel()
 
 
 if __name__ == "__main__":
