@@ -1,0 +1,241 @@
+"""Checkpoints keyed by the reference's parameter-tree paths
+(reference `checkpointing.py:78-203`, restore `train.py:217-341`).
+
+Layout: ``{root}/{slot}/{step}/`` holds, per rank, ``params-rank{r}.safetensors``
+and ``opt-rank{r}.safetensors`` with the tensors that rank owns, ``metadata.json``
+(global_step, epoch, best_val_loss, best_train_loss, timestamp, train_loss, the
+optimizer step count and the world size) and a ``COMMIT`` marker written last.
+A step directory without ``COMMIT`` (for instance a save interrupted by a crash)
+is ignored by ``steps()``/``restore``.
+
+* Parameter names are the flax paths (``block_0/layer_1/sublayer/gdn2/q_proj/kernel``)
+  with the flax ``(in, out)`` kernel layout, stored in the reference's dtypes
+  (fp32, except the routed expert weights which are bf16), so trees round-trip.
+* Optimizer moments are stored as ``mu/<path>`` / ``nu/<path>`` (fp32) plus the
+  step count; a checkpoint written with any world size restores on any other
+  (every tensor is stored whole by its owner).
+* Saves are asynchronous: owned tensors are copied into pinned host buffers on a
+  side stream, and a writer thread waits for that copy and writes the files
+  (the reference snapshots to host first for the same reasons).
+* ``restore`` is a graft-merge: tensors whose name and shape match are loaded,
+  anything new or reshaped keeps its fresh initialisation and is reported.
+"""
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import threading
+import time
+from typing import Dict, List, Optional
+
+import torch
+
+from ..models.hybrid import flax_path
+from .safetensors_io import load_file, save_file
+
+SLOTS = ("latest", "best_train", "best_val")
+
+
+def reference_dtype(name: str) -> torch.dtype:
+    """Dtype of a tensor in the reference's tree: routed experts are bf16."""
+    return torch.bfloat16 if name.split(".")[-1] in ("routed_w1", "routed_w2", "routed_w3") else torch.float32
+
+
+class CheckpointManager:
+    def __init__(self, root: str, slot: str = "latest", max_to_keep: int = 1, rank: int = 0, world: int = 1):
+        self.dir = os.path.join(root, slot)
+        self.max_to_keep = max_to_keep
+        self.rank, self.world = rank, world
+        self._thread: Optional[threading.Thread] = None
+        self._error: Optional[BaseException] = None
+        os.makedirs(self.dir, exist_ok=True)
+
+    # ------------------------------------------------------------ listing
+    def steps(self) -> List[int]:
+        out = []
+        if not os.path.isdir(self.dir):
+            return out
+        for d in os.listdir(self.dir):
+            if d.isdigit() and os.path.exists(os.path.join(self.dir, d, "COMMIT")):
+                out.append(int(d))
+        return sorted(out)
+
+    def latest_step(self) -> Optional[int]:
+        s = self.steps()
+        return s[-1] if s else None
+
+    def step_dir(self, step: int) -> str:
+        return os.path.join(self.dir, str(step))
+
+    # ------------------------------------------------------------ save
+    def save(self, step: int, trainer, metadata: Optional[Dict] = None, asynchronous: bool = True) -> None:
+        self.finalize()
+        st, opt = trainer.store, trainer.opt
+        dev = st.device
+        stream = torch.cuda.Stream() if dev.type == "cuda" else None
+        params: Dict[str, torch.Tensor] = {}
+        moments: Dict[str, torch.Tensor] = {}
+        if stream is not None:
+            stream.wait_stream(torch.cuda.current_stream())
+        ctx = torch.cuda.stream(stream) if stream is not None else _null()
+        with ctx:
+            for s in st.owned():
+                name = flax_path(s.name)
+                master = st.master_view(s)
+                params[name] = _to_host(master.to(reference_dtype(s.name)), dev)
+                o = s.offset - st.lo
+                moments[f"mu/{name}"] = _to_host(opt.m[o:o + s.numel].view(s.shape), dev)
+                moments[f"nu/{name}"] = _to_host(opt.v[o:o + s.numel].view(s.shape), dev)
+        ev = None
+        if stream is not None:
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        meta = dict(metadata or {})
+        meta.update({"global_step": int(meta.get("global_step", step)), "opt_count": int(opt.count),
+                     "world": self.world, "timestamp": time.time()})
+        labels = {flax_path(s.name): s.label for s in st.owned()}
+
+        def write():
+            try:
+                if ev is not None:
+                    ev.synchronize()
+                d = self.step_dir(step)
+                os.makedirs(d, exist_ok=True)
+                save_file(params, os.path.join(d, f"params-rank{self.rank}.safetensors"),
+                          {"format": "atomic_ai_hybrid_b200/params"})
+                save_file(moments, os.path.join(d, f"opt-rank{self.rank}.safetensors"),
+                          {"format": "atomic_ai_hybrid_b200/opt", "labels": json.dumps(labels)})
+                with open(os.path.join(d, f"rank{self.rank}.done"), "w") as f:
+                    f.write("ok")
+                if self.rank == 0:
+                    with open(os.path.join(d, "metadata.json"), "w") as f:
+                        json.dump(meta, f, indent=1)
+                    deadline = time.time() + 600
+                    while time.time() < deadline:
+                        if all(os.path.exists(os.path.join(d, f"rank{r}.done")) for r in range(self.world)):
+                            break
+                        time.sleep(0.05)
+                    else:
+                        raise TimeoutError(f"checkpoint {d}: not all ranks finished writing")
+                    with open(os.path.join(d, "COMMIT"), "w") as f:
+                        f.write(str(step))
+                    self._prune()
+            except BaseException as e:  # surfaced by finalize()
+                self._error = e
+
+        if asynchronous:
+            self._thread = threading.Thread(target=write, daemon=True)
+            self._thread.start()
+        else:
+            write()
+            self._raise()
+
+    def finalize(self, timeout: Optional[float] = None) -> None:
+        """Wait for a pending asynchronous save (reference ``_finalize_pending_save``)."""
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+        self._raise()
+
+    def _raise(self):
+        if self._error is not None:
+            e, self._error = self._error, None
+            raise e
+
+    def _prune(self):
+        steps = self.steps()
+        for s in steps[:-self.max_to_keep] if self.max_to_keep > 0 else []:
+            shutil.rmtree(self.step_dir(s), ignore_errors=True)
+
+    # ------------------------------------------------------------ restore
+    def load_tensors(self, step: int):
+        d = self.step_dir(step)
+        if not os.path.exists(os.path.join(d, "COMMIT")):
+            raise FileNotFoundError(f"{d} is not a committed checkpoint")
+        params, moments = {}, {}
+        for fn in sorted(os.listdir(d)):
+            if fn.startswith("params-rank") and fn.endswith(".safetensors"):
+                params.update(load_file(os.path.join(d, fn)))
+            elif fn.startswith("opt-rank") and fn.endswith(".safetensors"):
+                moments.update(load_file(os.path.join(d, fn)))
+        with open(os.path.join(d, "metadata.json")) as f:
+            meta = json.load(f)
+        return params, moments, meta
+
+    def restore(self, step: int, trainer, load_optimizer: bool = True) -> Dict:
+        """Graft-merge restore into ``trainer``; returns the metadata plus
+        ``restored``/``fresh`` name lists."""
+        params, moments, meta = self.load_tensors(step)
+        st, opt = trainer.store, trainer.opt
+        restored, fresh = [], []
+        with torch.no_grad():
+            for s in st.segs:
+                name = flax_path(s.name)
+                t = params.get(name)
+                if t is None or tuple(t.shape) != tuple(s.shape):
+                    fresh.append(name)
+                    continue
+                t32 = t.to(device=st.device, dtype=torch.float32)
+                st.compute_view(s).copy_(t32)
+                if s.owner == st.rank:
+                    st.master_view(s).copy_(t32)
+                    o = s.offset - st.lo
+                    mu, nu = moments.get(f"mu/{name}"), moments.get(f"nu/{name}")
+                    if load_optimizer and mu is not None and tuple(mu.shape) == tuple(s.shape):
+                        opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(st.device))
+                        opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(st.device))
+                restored.append(name)
+        if load_optimizer:
+            opt.count = int(meta.get("opt_count", 0))
+        meta = dict(meta)
+        meta["restored"], meta["fresh"] = restored, fresh
+        return meta
+
+
+def _to_host(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    if dev.type != "cuda":
+        return t.detach().clone()
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t, non_blocking=True)
+    return h
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def make_manager(root: str, slot: str, max_to_keep: int = 1, rank: int = 0, world: int = 1) -> CheckpointManager:
+    """Reference ``make_manager``: one manager per slot (latest / best_train / best_val)."""
+    return CheckpointManager(root, slot, max_to_keep, rank, world)
+
+
+def upload_slot(local_dir: str, repo_subdir: str, step: int, repo_id: Optional[str] = None, keep_last_n: int = 1):
+    """Mirror a committed step to the Hugging Face Hub (reference ``upload_slot``).
+    Needs ``huggingface_hub`` and network access; raises a clear error otherwise."""
+    try:
+        from huggingface_hub import HfApi  # type: ignore
+    except ImportError as e:
+        raise RuntimeError("upload_slot needs the huggingface_hub package, which is not installed") from e
+    repo_id = repo_id or os.environ.get("HF_REPO_ID")
+    if not repo_id:
+        raise RuntimeError("upload_slot: set HF_REPO_ID or pass repo_id")
+    api = HfApi()
+    api.upload_folder(folder_path=os.path.join(local_dir, str(step)), repo_id=repo_id,
+                      path_in_repo=f"{repo_subdir}/{step}")
+
+
+def download_slot(local_dir: str, repo_subdir: str, repo_id: Optional[str] = None) -> Optional[int]:
+    """Fetch the newest step of a slot from the Hub (reference ``download_slot``)."""
+    try:
+        from huggingface_hub import snapshot_download  # type: ignore
+    except ImportError as e:
+        raise RuntimeError("download_slot needs the huggingface_hub package, which is not installed") from e
+    repo_id = repo_id or os.environ.get("HF_REPO_ID")
+    path = snapshot_download(repo_id=repo_id, allow_patterns=[f"{repo_subdir}/*"], local_dir=local_dir)
+    steps = [int(d) for d in os.listdir(os.path.join(path, repo_subdir)) if d.isdigit()]
+    return max(steps) if steps else None

@@ -260,9 +260,12 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
   auto dx = torch::empty_like(x), ddt = torch::empty_like(x);
   auto dB = torch::empty(Bm.sizes(), f32), dC = torch::empty(Cm.sizes(), f32);
   auto dA = torch::zeros({H}, f32);
+  const int G = ahb_ssd_head_groups(H);
+  auto dBp = torch::empty({G, B, L, 128}, f32), dCp = torch::empty({G, B, L, 128}, f32);
   ahb_ssd_bwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B, L,
               H, sbuf.data_ptr<float>(), cuml.data_ptr<float>(), gbuf.data_ptr<float>(), dx.data_ptr(),
-              ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), cur_stream());
+              ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(),
+              dCp.data_ptr<float>(), cur_stream());
   return {dx, ddt, dA, dB, dC};
 }
 

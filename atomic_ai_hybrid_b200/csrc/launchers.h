@@ -52,9 +52,10 @@ void ahb_gdn_bwd_intra(const void* q, const void* k, const float* g, const void*
 int ahb_ssd_supported(int P, int N);
 void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
                  float* state_buf, float* cuml, const float* s0, float* s_final, void* y, cudaStream_t st);
+int ahb_ssd_head_groups(int H);
 void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                  int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
-                 float* dC, float* dA, cudaStream_t st);
+                 float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st);
 
 // moe_gemm.cu: tcgen05 grouped GEMM.  Returns 0 on success, <0 on a setup error.
 #define AHB_GEMM_DENSE 0        // C[M,N] = A[M,K] B[N,K]^T (single group)

@@ -136,8 +136,9 @@ __global__ void __launch_bounds__(256) ssd_state_fwd_kernel(const bf16* __restri
   const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
   const SIdx ix{L, H, NC};
   const int warp = threadIdx.x >> 5;
+  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
   load_bn_tile(b_s, Bm, ix, b, n);
-  for (int h = 0; h < H; ++h) {
+  for (int h = h0; h < h0 + hpg; ++h) {
     load_xp_tile(x_s, x, ix, b, n, h);
     load_xp_tile(dt_s, dt, ix, b, n, h);
     cum_decay(cum, dt_s, A[h]);
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict
   __syncthreads();
   compute_cb(cb_s, c_s, b_s);
   const int I = warp & 3, n0 = 32 * (warp >> 2);
-  for (int h = 0; h < H; ++h) {
+  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
+  for (int h = h0; h < h0 + hpg; ++h) {
     const int64_t cb = ix.ch(b, h, n);
     load_xp_tile(x_s, x, ix, b, n, h);
     load_xp_tile(dt_s, dt, ix, b, n, h);
@@ -271,7 +273,8 @@ __global__ void __launch_bounds__(256) ssd_dstate_kernel(const bf16* __restrict_
   const SIdx ix{L, H, NC};
   const int warp = threadIdx.x >> 5;
   load_bn_tile(c_s, Cm, ix, b, n);
-  for (int h = 0; h < H; ++h) {
+  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
+  for (int h = h0; h < h0 + hpg; ++h) {
     load_xp_tile(dy_s, dy, ix, b, n, h);
     load_xp_tile(dt_s, dt, ix, b, n, h);
     cum_decay(cum, dt_s, A[h]);
@@ -326,7 +329,8 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
   float dBa[8][4], dCa[8][4];
   zero_acc<8>(dBa);
   zero_acc<8>(dCa);
-  for (int h = 0; h < H; ++h) {
+  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
+  for (int h = h0; h < h0 + hpg; ++h) {
     const int64_t cbi = ix.ch(b, h, n);
     const float Ah = A[h];
     load_xp_tile(x_s, x, ix, b, n, h);
@@ -487,10 +491,25 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
     if (lane == 0 && tid < P) atomicAdd(dA + h, dAh);
     __syncthreads();
   }
-  // write dB, dC for this chunk (sum over heads)
+  // partial dB, dC of this head group: (G, B, L, N)
   const int m0 = 16 * mt, n0 = 64 * nh;
-  for_acc<8>(dBa, m0, n0, [&](int r, int c, float& v) { dB[ix.bn(b, (int64_t)n * C + r) + c] = v; });
-  for_acc<8>(dCa, m0, n0, [&](int r, int c, float& v) { dC[ix.bn(b, (int64_t)n * C + r) + c] = v; });
+  const int64_t goff = (int64_t)blockIdx.z * ix.L * N * gridDim.y;
+  for_acc<8>(dBa, m0, n0, [&](int r, int c, float& v) { dB[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
+  for_acc<8>(dCa, m0, n0, [&](int r, int c, float& v) { dC[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
+}
+
+// out[i] = sum_g part[g * n + i]
+__global__ void sum_groups_kernel(const float* __restrict__ part, int G, int64_t n, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int g = 0; g < G; ++g) s += part[g * n + i];
+    out[i] = s;
+  }
+}
+
+int head_groups(int H) {
+  for (int g : {8, 4, 2}) if (H % g == 0) return g;
+  return 1;
 }
 
 template <class K>
@@ -511,17 +530,23 @@ void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, 
     init = true;
   }
   const int NC = L / C;
-  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                              L, H, state_buf, cuml);
+  const int G = head_groups(H);
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                 (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, s0, s_final);
   if (y)
-    ssd_out_fwd_kernel<<<dim3(NC, B), 256, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                            (const bf16*)Cm, state_buf, L, H, (bf16*)y);
+    ssd_out_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+                                                               (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
+                                                               (bf16*)y);
 }
 
+int ahb_ssd_head_groups(int H) { return head_groups(H); }
+
+// dB_part / dC_part: (G, B, L, N) fp32 scratch with G = ahb_ssd_head_groups(H); the sums over
+// head groups are written to dB / dC.
 void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                  int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
-                 float* dC, float* dA, cudaStream_t st) {
+                 float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st) {
   static bool init = false;
   if (!init) {
     set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
@@ -530,15 +555,20 @@ void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, 
     init = true;
   }
   const int NC = L / C;
-  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                              L, H, state_buf, cuml);
+  const int G = head_groups(H);
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                 (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  ssd_dstate_kernel<<<dim3(NC, B), 256, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
-                                                      g_buf);
+  ssd_dstate_kernel<<<dim3(NC, B, G), 256, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
+                                                         g_buf);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(g_buf, cuml, H, NC, 1, nullptr, nullptr);
-  ssd_bwd_chunk_kernel<<<dim3(NC, B), 256, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                          (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
-                                                          (bf16*)dx, (bf16*)ddt, dB, dC, dA);
+  ssd_bwd_chunk_kernel<<<dim3(NC, B, G), 256, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+                                                             (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
+                                                             (bf16*)dx, (bf16*)ddt, dB_part, dC_part, dA);
+  const int64_t n = (int64_t)B * L * N;
+  const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  sum_groups_kernel<<<blocks, 256, 0, st>>>(dB_part, G, n, dB);
+  sum_groups_kernel<<<blocks, 256, 0, st>>>(dC_part, G, n, dC);
 }
 
 // ============================================================ allocation-free forward
@@ -585,10 +615,12 @@ extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A
   }
   float* state_buf = static_cast<float*>(base);
   float* cuml = state_buf + chunk_heads * (unsigned long long)(P * N);
-  ssd_state_fwd_kernel<<<dim3(NC, B), 256, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                  (const bf16*)Bm, L, H, state_buf, cuml);
+  const int G = head_groups(H);
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                     (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, stream>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  ssd_out_fwd_kernel<<<dim3(NC, B), 256, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                              (const bf16*)Cm, state_buf, L, H, (bf16*)y);
+  ssd_out_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                 (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
+                                                                 (bf16*)y);
   return cudaGetLastError() == cudaSuccess ? AHB_NOALLOC_OK : AHB_NOALLOC_ELAUNCH;
 }

@@ -1,0 +1,332 @@
+"""The training entry loop (reference ``main_execution``, `train.py:344-1302`).
+
+Behaviour kept from the reference:
+
+* three checkpoint slots -- ``latest`` (time-based, every ``checkpoint_every_s``),
+  ``best_train`` (when the training loss improves at a save) and ``best_val``
+  (when the evaluation loss improves); resume from the newest committed step of
+  ``resume_slot`` with graft-merge, then a NaN check of the restored weights;
+* data resume by skipping the consumed micro-steps without reading them;
+* a first-batch sanity check (token ids inside the vocabulary, labels equal to
+  the inputs shifted by one);
+* per-step diagnostics: global gradient norm, clip factor, per-group non-finite
+  flags, parameter-clip flag; a burst guard (norm > 20 three steps running);
+* non-finite steps: a snapshot (weights, optimizer state, the step's
+  micro-batches and ``SNAPSHOT_META.json``) and an auto-stop after 4 in a row or
+  25% of the last 15, saving ``latest`` first;
+* SIGTERM / SIGINT: emergency save at the next step boundary, then exit;
+* a session time budget, periodic evaluation with early stopping.
+
+Differences by design: statistics stay on the device and are read once per
+optimizer step (a few scalars), and the non-finite snapshot holds the weights
+after the step (the reference copies every weight to the host before every
+apply to have the pre-apply values; with ``skip_nonfinite=True`` the update is
+skipped and the snapshot equals the pre-apply state).
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import time
+from dataclasses import asdict, dataclass, field
+from datetime import timedelta
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..ckpt import CheckpointManager
+from ..config import get_preset, load_yaml_config
+from ..data import Prefetcher, dataloader_multi_source, resolve_source_files, synthetic_batches
+from ..models import HybridMoEModel
+from ..optim.schedule import DIAG_GROUPS
+from ..utils import wandb_logging
+from ..utils.monitor import (SESSION_TIME_BUDGET_SECONDS, BurstGuard, FaultInjector, NonFiniteMonitor,
+                             StopSignals)
+from .trainer import Trainer
+
+CHECKPOINT_EVERY_SECONDS = 95 * 60
+
+
+@dataclass
+class TrainArgs:
+    preset: str = "tiny"
+    config_yaml: Optional[str] = None
+    overrides: Dict = field(default_factory=dict)
+    ckpt_root: str = "checkpoints"
+    data_dir: Optional[str] = None
+    data_prefixes: List[str] = field(default_factory=list)
+    source_fractions: List[float] = field(default_factory=list)
+    data_mode: str = "mixed"
+    val_split: float = 0.05
+    seq_len: int = 512
+    global_batch: int = 8          # sequences per micro-step over all data-parallel ranks
+    accum_steps: int = 1
+    epochs: int = 1
+    max_steps: Optional[int] = None
+    total_steps: Optional[int] = None
+    optimizer: str = "hybrid"
+    eval_every: int = 1000
+    eval_batches: int = 20
+    log_every: int = 10
+    checkpoint_every_s: float = CHECKPOINT_EVERY_SECONDS
+    session_budget_s: float = SESSION_TIME_BUDGET_SECONDS
+    early_stop_patience: int = 5
+    resume: bool = True
+    resume_slot: str = "latest"
+    wandb_project: Optional[str] = None
+    impl: str = "cuda"
+    cuda_graph: bool = True
+    skip_nonfinite: bool = False
+    seed: int = 0
+    compute_dtype: str = "bf16"
+
+
+def _dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    use_cuda = torch.cuda.is_available()
+    dev = torch.device("cuda", local) if use_cuda else torch.device("cpu")
+    if use_cuda:
+        torch.cuda.set_device(dev)
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if use_cuda else "gloo"
+        kw = {"device_id": dev} if use_cuda else {}
+        timeout = timedelta(seconds=float(os.environ.get("AHB_PG_TIMEOUT_S", "300")))
+        dist.init_process_group(backend, timeout=timeout, **kw)
+    return rank, world, dev
+
+
+def _to_device(b: Dict[str, torch.Tensor], dev) -> Dict[str, torch.Tensor]:
+    return {k: (v.to(dev, non_blocking=True) if isinstance(v, torch.Tensor) else v) for k, v in b.items()}
+
+
+def sanity_check_batch(batch: Dict[str, torch.Tensor], vocab: int) -> List[str]:
+    """Reference first-batch checks (`train.py:590-618`): ids in range, label shift."""
+    issues = []
+    ids, lab = batch["input_ids"], batch["labels"]
+    if int(ids.min()) < 0 or int(ids.max()) >= vocab:
+        issues.append(f"token ids outside [0, {vocab})")
+    valid = lab[:, :-1] != -100
+    if valid.any() and not bool((lab[:, :-1] == ids[:, 1:])[valid].float().mean() > 0.99):
+        issues.append("labels are not the inputs shifted by one")
+    return issues
+
+
+def main_execution(args: TrainArgs) -> Dict:
+    rank, world, dev = _dist_setup()
+    ops.set_impl(args.impl if dev.type == "cuda" else "eager")
+    cfg = load_yaml_config(args.config_yaml) if args.config_yaml else get_preset(args.preset, **args.overrides)
+    torch.manual_seed(args.seed)
+    cdt = torch.bfloat16 if (args.compute_dtype == "bf16" and dev.type == "cuda") else torch.float32
+    with torch.device(dev):
+        model = HybridMoEModel(cfg, compute_dtype=cdt)
+
+    # ---------------------------------------------------------------- data
+    per_rank = args.global_batch // world
+    if args.data_dir and args.data_prefixes:
+        pairs = []
+        for i, pfx in enumerate(args.data_prefixes):
+            for p in resolve_source_files(args.data_dir, pfx):
+                frac = args.source_fractions[i] if i < len(args.source_fractions) else 1.0
+                pairs.append((p[0], p[1], frac))
+    else:
+        pairs = None
+
+    mgrs = {s: CheckpointManager(args.ckpt_root, s, max_to_keep=1, rank=rank, world=world)
+            for s in ("latest", "best_train", "best_val")}
+    steps_per_epoch = None
+    if pairs is not None:
+        _, _, micro_per_epoch, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
+                                                           mode=args.data_mode, rank=rank, world=world, pin=False)
+        steps_per_epoch = max(1, micro_per_epoch // args.accum_steps)
+    total_steps = args.total_steps or (steps_per_epoch * args.epochs if steps_per_epoch else (args.max_steps or 1000))
+    trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
+                      cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite)
+
+    # ---------------------------------------------------------------- resume
+    global_step, start_epoch = 0, 0
+    best_val, best_train = math.inf, math.inf
+    if args.resume:
+        slot = args.resume_slot if mgrs[args.resume_slot].latest_step() is not None else None
+        if slot is None:
+            for s in ("latest", "best_train", "best_val"):
+                if mgrs[s].latest_step() is not None:
+                    slot = s
+                    break
+        if slot is not None:
+            step = mgrs[slot].latest_step()
+            meta = mgrs[slot].restore(step, trainer)
+            global_step = int(meta.get("global_step", step))
+            start_epoch = int(meta.get("epoch", 0))
+            best_val = float(meta.get("best_val_loss", math.inf))
+            best_train = float(meta.get("best_train_loss", math.inf))
+            if not bool(torch.isfinite(trainer.store.master).all()):
+                raise RuntimeError(f"restored weights from {slot}/{step} contain non-finite values")
+            if rank == 0:
+                print(f"[RESUME] {slot}/{step}: step={global_step} restored={len(meta['restored'])} "
+                      f"fresh={len(meta['fresh'])}", flush=True)
+
+    def make_stream(skip):
+        if pairs is None:
+            it = synthetic_batches(cfg.vocab_size, args.global_batch, args.seq_len, args.seed + skip, rank, world)
+            return it, None
+        it, val_f, _, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
+                                                  skip_batches=skip, mode=args.data_mode, rank=rank, world=world)
+        return Prefetcher(it), val_f
+
+    train_stream, val_factory = make_stream(global_step * args.accum_steps)
+    if rank == 0 and args.wandb_project:
+        wandb_logging.init_wandb(args.wandb_project, config=asdict(args))
+
+    # ---------------------------------------------------------------- loop
+    signals = StopSignals().install()
+    injector = FaultInjector(rank)
+    nonfin, burst = NonFiniteMonitor(), BurstGuard()
+    t_start = time.time()
+    last_ckpt = time.time()
+    eval_no_improve = 0
+    stop_reason = None
+    tokens_per_step = args.global_batch * args.seq_len * args.accum_steps
+    t_log, steps_since_log = time.time(), 0
+    loss_hist: List[float] = []
+
+    def save_latest(step, loss_val, asynchronous=True, tag=""):
+        nonlocal best_train
+        meta = {"global_step": step, "epoch": epoch, "best_val_loss": best_val, "best_train_loss": best_train,
+                "train_loss": loss_val, "tag": tag}
+        mgrs["latest"].save(step, trainer, meta, asynchronous=asynchronous)
+        if loss_val is not None and loss_val < best_train:
+            best_train = loss_val
+            mgrs["latest"].finalize()
+            meta["best_train_loss"] = best_train
+            mgrs["best_train"].save(step, trainer, meta, asynchronous=asynchronous)
+
+    def evaluate():
+        if val_factory is None:
+            return None
+        tot, n = 0.0, 0
+        for i, b in enumerate(val_factory()):
+            if i >= args.eval_batches:
+                break
+            tot += float(trainer.eval_loss(_to_device(b, dev)))
+            n += 1
+        return tot / max(n, 1)
+
+    epoch = start_epoch
+    done = False
+    first = True
+    for epoch in range(start_epoch, args.epochs):
+        for _ in range(steps_per_epoch or 10 ** 12):
+            if args.max_steps is not None and global_step >= args.max_steps:
+                done = True
+                break
+            micro = []
+            for _m in range(args.accum_steps):
+                b = next(train_stream)
+                src = b.pop("_source_idx", None)
+                if first:
+                    issues = sanity_check_batch(b, cfg.vocab_size)
+                    if issues and rank == 0:
+                        print(f"[SANITY] first batch: {'; '.join(issues)}", flush=True)
+                    first = False
+                micro.append((_to_device(b, dev), src, b))
+            if trainer.cuda_graph and (trainer._graph is None or trainer._graph_key != trainer._key(micro[0][0])):
+                trainer.build_graph(micro[0][0])
+            for db, _, _ in micro:
+                trainer.micro_step(db)
+            injector.before_apply(global_step + 1, trainer)
+            info = trainer.apply(args.accum_steps)
+            global_step += 1
+            finite = bool(info["is_finite"])
+            gnorm = float(info["global_norm"])
+            loss_val = float(info["loss"])
+            loss_hist.append(loss_val)
+            flags = info["group_nonfinite_flags"].tolist()
+            bad_groups = [g for g, f in zip(DIAG_GROUPS, flags) if f]
+            if rank == 0:
+                m = {"train/loss": loss_val, "train/global_grad_norm": gnorm,
+                     "train/clip_factor": float(info["clip_factor"]),
+                     "train/param_clip_triggered": int(bool(info["was_clipped"])),
+                     "train/step_skipped_nonfinite": int(not finite)}
+                m.update({f"nonfinite/group_{g}": int(g in bad_groups) for g in DIAG_GROUPS})
+                wandb_logging.log_metrics(global_step, m)
+            if burst.update(gnorm) and rank == 0:
+                wandb_logging.log_alert("Burst guard triggered",
+                                        f"global_grad_norm > 20 three steps running at step={global_step}")
+            if not finite:
+                snap = os.path.join(args.ckpt_root, "nonfinite_snapshots", str(global_step))
+                smgr = CheckpointManager(snap, "state", max_to_keep=1, rank=rank, world=world)
+                smgr.save(global_step, trainer, {"epoch": epoch, "tag": "NONFINITE"}, asynchronous=False)
+                for i, (_, src, hb) in enumerate(micro):
+                    np.save(os.path.join(snap, f"micro_{i}_rank{rank}_input_ids.npy"), hb["input_ids"].numpy())
+                    np.save(os.path.join(snap, f"micro_{i}_rank{rank}_labels.npy"), hb["labels"].numpy())
+                if rank == 0:
+                    with open(os.path.join(snap, "SNAPSHOT_META.json"), "w") as f:
+                        json.dump({"n_micro": len(micro), "global_step": global_step,
+                                   "source_idx_per_micro": [s for _, s, _ in micro],
+                                   "nonfinite_groups": bad_groups}, f)
+            reason = nonfin.update(finite)
+            if reason is not None:
+                if rank == 0:
+                    wandb_logging.log_alert("AUTO-STOP: frequent non-finite gradients",
+                                            f"stopped at step {global_step}: {reason}", level="ERROR")
+                save_latest(global_step, None, asynchronous=False, tag="AUTO_STOP_NONFINITE")
+                stop_reason = "nonfinite"
+                done = True
+                break
+            steps_since_log += 1
+            if rank == 0 and global_step % args.log_every == 0:
+                dt = time.time() - t_log
+                print(f"[step {global_step}] loss={loss_val:.4f} gnorm={gnorm:.3f} "
+                      f"tok/s={tokens_per_step * steps_since_log / max(dt, 1e-9):.0f}", flush=True)
+                t_log, steps_since_log = time.time(), 0
+            if time.time() - last_ckpt >= args.checkpoint_every_s:
+                save_latest(global_step, loss_val)
+                last_ckpt = time.time()
+            if args.eval_every and global_step % args.eval_every == 0:
+                vl = evaluate()
+                if vl is not None:
+                    if rank == 0:
+                        wandb_logging.log_metrics(global_step, {"eval/loss": vl})
+                    if vl < best_val:
+                        best_val, eval_no_improve = vl, 0
+                        mgrs["best_val"].save(global_step, trainer, {"global_step": global_step, "epoch": epoch,
+                                                                   "best_val_loss": best_val,
+                                                                   "best_train_loss": best_train})
+                    else:
+                        eval_no_improve += 1
+                        if eval_no_improve >= args.early_stop_patience:
+                            stop_reason, done = "early_stop", True
+            injector.after_step(global_step)
+            if signals.requested is not None:
+                save_latest(global_step, loss_val, asynchronous=False, tag="EMERGENCY_SIGNAL")
+                stop_reason, done = "signal", True
+            if time.time() - t_start >= args.session_budget_s:
+                save_latest(global_step, loss_val, asynchronous=False, tag="SESSION_BUDGET")
+                stop_reason, done = "time_budget", True
+            if done:
+                break
+        if done:
+            break
+        if val_factory is not None:
+            vl = evaluate()
+            if vl is not None and vl < best_val:
+                best_val = vl
+    for mg in mgrs.values():
+        mg.finalize()
+    if stop_reason is None and global_step > 0:
+        save_latest(global_step, loss_hist[-1] if loss_hist else None, asynchronous=False, tag="FINAL")
+    signals.uninstall()
+    trainer.close()
+    wandb_logging.finish()
+    summary = {"global_step": global_step, "stop_reason": stop_reason, "losses": loss_hist,
+               "best_val": best_val, "best_train": best_train}
+    if world > 1 and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return summary

@@ -1,0 +1,75 @@
+"""End-to-end training loop on CPU: checkpoint/resume, fault injection on the host
+(NaN gradients -> snapshot + auto-stop, SIGTERM -> emergency save), and a
+failing rank among gloo ranks ending the others with an error instead of a hang."""
+import json
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from atomic_ai_hybrid_b200.training.loop import TrainArgs, main_execution
+
+PRESET_OVER = dict(num_layers=2, layer_types=("mamba2", "gdn2"), vocab_size=512, d_model=128, n_heads=2,
+                   n_heads_ssm=2, d_ff=128, n_routed_experts=4, d_state=32)
+
+
+def _args(tmp, **kw):
+    a = TrainArgs(preset="tiny", overrides=dict(PRESET_OVER), ckpt_root=str(tmp), seq_len=64, global_batch=2,
+                  accum_steps=2, max_steps=3, eval_every=0, log_every=1, impl="eager", cuda_graph=False)
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def _write_data(d):
+    rng = np.random.RandomState(0)
+    ids = rng.randint(0, 512, size=(64, 65)).astype(np.int32)
+    np.save(os.path.join(d, "src_input_ids.npy"), ids[:, :-1])
+    np.save(os.path.join(d, "src_labels.npy"), ids[:, 1:])
+
+
+def test_checkpoint_and_resume_on_files(tmp_path):
+    _write_data(str(tmp_path))
+    kw = dict(data_dir=str(tmp_path), data_prefixes=["src"], eval_every=2, eval_batches=2)
+    s1 = main_execution(_args(tmp_path / "ck", **kw))
+    assert s1["global_step"] == 3 and s1["stop_reason"] is None
+    s2 = main_execution(_args(tmp_path / "ck", max_steps=5, **kw))
+    assert s2["global_step"] == 5 and len(s2["losses"]) == 2
+    assert os.path.exists(tmp_path / "ck" / "latest" / "5" / "COMMIT")
+    assert os.path.exists(tmp_path / "ck" / "best_val")
+
+
+def test_nonfinite_injection_snapshots_and_autostops(tmp_path, monkeypatch):
+    monkeypatch.setenv("AHB_INJECT_NAN_STEP", "2-9")
+    s = main_execution(_args(tmp_path, max_steps=20))
+    assert s["stop_reason"] == "nonfinite" and s["global_step"] == 5
+    snap = tmp_path / "nonfinite_snapshots" / "2"
+    meta = json.loads((snap / "SNAPSHOT_META.json").read_text())
+    assert meta["n_micro"] == 2 and meta["global_step"] == 2
+    assert os.path.exists(tmp_path / "latest" / "5" / "COMMIT")
+
+
+def test_sigterm_triggers_emergency_save(tmp_path, monkeypatch):
+    monkeypatch.setenv("AHB_INJECT_SIGNAL_STEP", "2")
+    s = main_execution(_args(tmp_path, max_steps=10))
+    assert s["stop_reason"] == "signal" and s["global_step"] == 2
+    meta = json.loads((tmp_path / "latest" / "2" / "metadata.json").read_text())
+    assert meta["tag"] == "EMERGENCY_SIGNAL"
+
+
+def _rank_main(rank, world, port, tmp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="10", AHB_INJECT_RAISE_STEP="2",
+                      AHB_INJECT_RAISE_RANK="1")
+    main_execution(_args(tmp, max_steps=5, global_batch=2, accum_steps=1))
+
+
+def test_failing_rank_ends_peers_with_error(tmp_path):
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    with pytest.raises(Exception):
+        mp.spawn(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)

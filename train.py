@@ -1,0 +1,71 @@
+"""Training entry point (the reference's ``train.py``).
+
+Example (one GPU):   python train.py --preset hybrid_1b --seq-len 4096 --global-batch 32 --accum-steps 8
+Example (8 GPUs):    torchrun --standalone --nproc-per-node 8 train.py --preset hybrid_1b ...
+Data: ``--data-dir DIR --data-prefix NAME[:FRACTION] ...`` reads the reference's
+``.npy`` token files; without data arguments the run uses synthetic tokens.
+"""
+import argparse
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from atomic_ai_hybrid_b200.training.loop import TrainArgs, main_execution  # noqa: E402
+
+
+def parse(argv=None) -> TrainArgs:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--preset", default="tiny")
+    ap.add_argument("--config", dest="config_yaml", default=None, help="YAML {preset:, overrides:}")
+    ap.add_argument("--set", action="append", default=[], help="config override key=value (repeatable)")
+    ap.add_argument("--ckpt-root", default="checkpoints")
+    ap.add_argument("--data-dir", default=None)
+    ap.add_argument("--data-prefix", action="append", default=[], help="NAME or NAME:FRACTION")
+    ap.add_argument("--data-mode", default="mixed", choices=["mixed", "sequential", "round_robin"])
+    ap.add_argument("--seq-len", type=int, default=512)
+    ap.add_argument("--global-batch", type=int, default=8)
+    ap.add_argument("--accum-steps", type=int, default=1)
+    ap.add_argument("--epochs", type=int, default=1)
+    ap.add_argument("--max-steps", type=int, default=None)
+    ap.add_argument("--total-steps", type=int, default=None)
+    ap.add_argument("--optimizer", default="hybrid", choices=["hybrid", "adamw"])
+    ap.add_argument("--eval-every", type=int, default=1000)
+    ap.add_argument("--log-every", type=int, default=10)
+    ap.add_argument("--checkpoint-every-s", type=float, default=95 * 60)
+    ap.add_argument("--session-budget-s", type=float, default=9 * 3600 - 300)
+    ap.add_argument("--no-resume", action="store_true")
+    ap.add_argument("--resume-slot", default="latest")
+    ap.add_argument("--wandb-project", default=None)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "eager"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--skip-nonfinite", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+    over = {}
+    for kv in a.set:
+        k, v = kv.split("=", 1)
+        try:
+            over[k] = json.loads(v)
+        except json.JSONDecodeError:
+            over[k] = v
+    prefixes, fracs = [], []
+    for p in a.data_prefix:
+        name, _, fr = p.partition(":")
+        prefixes.append(name)
+        fracs.append(float(fr) if fr else 1.0)
+    return TrainArgs(preset=a.preset, config_yaml=a.config_yaml, overrides=over, ckpt_root=a.ckpt_root,
+                     data_dir=a.data_dir, data_prefixes=prefixes, source_fractions=fracs, data_mode=a.data_mode,
+                     seq_len=a.seq_len, global_batch=a.global_batch, accum_steps=a.accum_steps, epochs=a.epochs,
+                     max_steps=a.max_steps, total_steps=a.total_steps, optimizer=a.optimizer,
+                     eval_every=a.eval_every, log_every=a.log_every, checkpoint_every_s=a.checkpoint_every_s,
+                     session_budget_s=a.session_budget_s, resume=not a.no_resume, resume_slot=a.resume_slot,
+                     wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
+                     skip_nonfinite=a.skip_nonfinite, seed=a.seed)
+
+
+if __name__ == "__main__":
+    out = main_execution(parse())
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({k: v for k, v in out.items() if k != "losses"}))
