@@ -28,15 +28,14 @@ template <int G>
 AHB_DEVICE float group_sum(float v, float* sh) {
   v = warp_sum(v);
   if constexpr (G == 1) return v;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncwarp();
+  // only the G warps of this row's group synchronise (named barrier 1 + group)
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = w / G;
   if (lane == 0) sh[w] = v;
-  __syncthreads();
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * G) : "memory");
   float t = 0.f;
-  const int g0 = (w / G) * G;
 #pragma unroll
-  for (int i = 0; i < G; ++i) t += sh[g0 + i];
-  __syncthreads();
+  for (int i = 0; i < G; ++i) t += sh[grp * G + i];
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * G) : "memory");
   return t;
 }
 

@@ -1,0 +1,141 @@
+"""Single-GPU operator benchmark (the benchmark spec's config 2): GDN-2 chunked
+delta rule and Mamba2 SSD, forward + backward, bf16, timed with CUDA events.
+
+``python -m atomic_ai_hybrid_b200.utils.opbench --op gdn --B 8 --T 4096 --H 16``
+``python -m atomic_ai_hybrid_b200.utils.opbench --op ssd --B 8 --T 4096 --H 32``
+
+Inputs follow the spec: GDN q, k ~ N(0,1) then L2-normalised per head, v ~ N(0,1),
+beta = sigmoid(N(0,1)), g = -softplus(N(0,1)) (per head, broadcast over the
+channels of the per-channel kernels; erase gate = beta, write gate = 1).  SSD x, B,
+C ~ N(0,1), dt = softplus(N(0,1) - 4) per head (broadcast over channels),
+A = -exp(U[0, log 16]).  Reported TFLOP/s count the chunked algorithm's matmul
+FLOPs (``ops.reference.flops_*``; backward counted as 2x forward).  Between timed
+iterations a 256 MiB buffer is rewritten to flush L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def _timeit(fn, warmup: int, iters: int, flush: torch.Tensor) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd"):
+    from ..ops import kernels as K
+    from ..ops.reference import flops_gdn_chunked
+    D = 128
+    dev = "cuda"
+    q = F.normalize(torch.randn(B, T, H, D, device=dev), dim=-1).to(torch.bfloat16).requires_grad_(True)
+    k = F.normalize(torch.randn(B, T, H, D, device=dev), dim=-1).to(torch.bfloat16).requires_grad_(True)
+    v = torch.randn(B, T, H, D, device=dev).to(torch.bfloat16).requires_grad_(True)
+    beta = torch.sigmoid(torch.randn(B, T, H, 1, device=dev)).expand(B, T, H, D).contiguous()
+    b = beta.to(torch.bfloat16).requires_grad_(True)
+    w = torch.ones(B, T, H, D, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    g = (-F.softplus(torch.randn(B, T, H, 1, device=dev))).expand(B, T, H, D).contiguous().requires_grad_(True)
+    do = torch.randn(B, T, H, D, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        o = K.gdn2(q, k, v, w, b, g, 1.0, 64)
+        if mode == "fwdbwd":
+            torch.autograd.backward(o, do)
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = flops_gdn_chunked(B, T, H, D, 64) * (3 if mode == "fwdbwd" else 1)
+    io_bytes = B * T * H * D * (2 * 5 + 4) * (3 if mode == "fwdbwd" else 1)
+    return {"op": "gdn2", "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9,
+            "min_io_gb_s": io_bytes / ms / 1e6}
+
+
+def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd"):
+    from ..ops import kernels as K
+    from ..ops.reference import flops_ssd_chunked
+    P, N = 64, 128
+    dev = "cuda"
+    x = torch.randn(B, T, H, P, device=dev).to(torch.bfloat16).requires_grad_(True)
+    dt = F.softplus(torch.randn(B, T, H, 1, device=dev) - 4).clamp(1e-2, 1.0).expand(B, T, H, P).contiguous()
+    dt = dt.to(torch.bfloat16).requires_grad_(True)
+    A = (-torch.exp(torch.rand(H, device=dev) * math.log(16.0))).requires_grad_(True)
+    Bm = torch.randn(B, T, N, device=dev).to(torch.bfloat16).requires_grad_(True)
+    Cm = torch.randn(B, T, N, device=dev).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(B, T, H, P, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        y = K.ssd(dt, A, Bm, Cm, x, 64)
+        if mode == "fwdbwd":
+            torch.autograd.backward(y, dy)
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = flops_ssd_chunked(B, T, H, P, N, 64) * (3 if mode == "fwdbwd" else 1)
+    io_bytes = (B * T * H * P * 2 * 3 + B * T * N * 2 * 2) * (3 if mode == "fwdbwd" else 1)
+    return {"op": "ssd", "mode": mode, "B": B, "T": T, "H": H, "P": P, "N": N, "ms": ms, "tflops": fl / ms / 1e9,
+            "min_io_gb_s": io_bytes / ms / 1e6}
+
+
+def bench_moe(T, d, F_, E, k, warmup, iters, flush, mode="fwdbwd"):
+    from ..ops import kernels as K
+    dev = "cuda"
+    x = (torch.randn(T, d, device=dev) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    logits = torch.randn(T, E, device=dev)
+    top_idx = torch.topk(logits, k, -1).indices
+    gate = torch.softmax(logits.gather(1, top_idx), -1).requires_grad_(True)
+    w1 = (torch.randn(E, d, F_, device=dev) * d ** -0.5).to(torch.bfloat16).requires_grad_(True)
+    w2 = (torch.randn(E, F_, d, device=dev) * F_ ** -0.5).to(torch.bfloat16).requires_grad_(True)
+    w3 = (torch.randn(E, d, F_, device=dev) * d ** -0.5).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(T, d, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        y = K.moe_forward(x, top_idx, gate, w1, w2, w3, None, "swiglu")
+        if mode == "fwdbwd":
+            torch.autograd.backward(y, dy)
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = 2 * T * k * d * F_ * 3 * (3 if mode == "fwdbwd" else 1)
+    return {"op": "moe_swiglu", "mode": mode, "T": T, "d": d, "F": F_, "E": E, "k": k, "ms": ms,
+            "tflops": fl / ms / 1e9}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe"])
+    ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--T", type=int, default=4096)
+    ap.add_argument("--H", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args(argv)
+    from .. import ops
+    ops.set_impl("cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
+    torch.manual_seed(0)
+    if a.op == "gdn":
+        r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "ssd":
+        r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode)
+    else:
+        r = bench_moe(a.B * a.T, 2048, 1024, 32, 4, a.warmup, a.iters, flush, a.mode)
+    print(json.dumps(r), flush=True)
+    return r
+
+
+if __name__ == "__main__":
+    main()
