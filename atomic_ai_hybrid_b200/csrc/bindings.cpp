@@ -26,6 +26,13 @@ void check_acc(const torch::Tensor& t, int64_t n, const char* name) {
               " must be a contiguous fp32 CUDA tensor with ", n, " elements");
 }
 
+// Fail loudly if a launch of this binding was rejected (bad configuration,
+// missing shared-memory opt-in, no kernel image for the device ...).
+void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, "atomic_ai_hybrid_b200: launch of ", what, " failed: ", cudaGetErrorString(e));
+}
+
 float* opt_ptr(const c10::optional<torch::Tensor>& t) {
   return t.has_value() && t->defined() ? t->data_ptr<float>() : nullptr;
 }
@@ -36,6 +43,7 @@ torch::Tensor sanitize(torch::Tensor x, double clip) {
   auto xc = x.contiguous();
   auto out = torch::empty_like(xc);
   ahb_sanitize(out.data_ptr(), xc.data_ptr(), xc.numel(), dt_code(xc), (float)clip, cur_stream());
+  check_launch("ahb_sanitize");
   return out;
 }
 
@@ -50,6 +58,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor scale, dou
   auto r = torch::empty({M}, xc.options().dtype(at::kFloat));
   ahb_rmsnorm_fwd(xc.data_ptr(), sc.data_ptr<float>(), y.data_ptr(), r.data_ptr<float>(), M, D, dt_code(xc),
                   (float)eps, cur_stream());
+  check_launch("ahb_rmsnorm_fwd");
   return {y, r};
 }
 
@@ -67,6 +76,7 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor scale
   ahb_rmsnorm_bwd(dyc.data_ptr(), xc.data_ptr(), sc.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
                   opt_ptr(dscale_acc), part.defined() ? part.data_ptr<float>() : nullptr, M, D, dt_code(xc),
                   cur_stream());
+  check_launch("ahb_rmsnorm_bwd");
   return dx;
 }
 
@@ -86,6 +96,7 @@ torch::Tensor conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::
   if (bias.has_value()) bf = bias->to(at::kFloat).contiguous();
   ahb_conv1d_fwd(x.data_ptr(), x.stride(1), w.data_ptr(), dt_code(w), opt_ptr(bf), y.data_ptr(), B, L, C, dt_code(x),
                  silu ? 1 : 0, (float)clip, cur_stream());
+  check_launch("ahb_conv1d_fwd");
   return y;
 }
 
@@ -103,6 +114,7 @@ torch::Tensor conv1d_bwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::
   ahb_conv1d_bwd(x.data_ptr(), x.stride(1), w.data_ptr(), dt_code(w), opt_ptr(bf), dyc.data_ptr(), dx.data_ptr(),
                  dw_acc.data_ptr<float>(), opt_ptr(db_acc), B, L, C, dt_code(x), silu ? 1 : 0, (float)clip,
                  cur_stream());
+  check_launch("ahb_conv1d_bwd");
   return dx;
 }
 
@@ -110,6 +122,7 @@ void accumulate_(torch::Tensor acc, torch::Tensor g, double scale) {
   auto gc = g.contiguous();
   check_acc(acc, gc.numel(), "acc");
   ahb_accumulate(acc.data_ptr<float>(), gc.data_ptr(), gc.numel(), dt_code(gc), (float)scale, cur_stream());
+  check_launch("ahb_accumulate");
 }
 
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor emb, at::ScalarType out_dtype) {
@@ -120,6 +133,7 @@ torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor emb, at::ScalarType
   auto out = torch::empty({T, D}, emb.options().dtype(out_dtype));
   ahb_embedding_fwd(idc.data_ptr<int64_t>(), emb.data_ptr(), dt_code(emb), out.data_ptr(),
                     out_dtype == at::kBFloat16 ? AHB_BF16 : AHB_F32, T, D, emb.size(0), cur_stream());
+  check_launch("ahb_embedding_fwd");
   return out;
 }
 
@@ -129,6 +143,7 @@ void embedding_bwd_(torch::Tensor ids, torch::Tensor dout, torch::Tensor acc) {
   check_acc(acc, acc.numel(), "acc");
   ahb_embedding_bwd(idc.data_ptr<int64_t>(), dc.data_ptr(), dt_code(dc), acc.data_ptr<float>(), idc.numel(),
                     (int)acc.size(1), acc.size(0), cur_stream());
+  check_launch("ahb_embedding_bwd");
 }
 
 
@@ -162,12 +177,14 @@ std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tens
   ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
                     (float)scale, s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(),
                     aqk.data_ptr<float>(), gcl.data_ptr<float>(), nullptr, st);
+  check_launch("ahb_gdn_intra_fwd");
   auto o = torch::empty_like(q);
   torch::Tensor hf;
   if (want_state) hf = torch::empty({s.B, s.H, 128, 128}, f32);
   ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
                     gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(),
                     want_state ? hf.data_ptr<float>() : nullptr, nullptr, nullptr, st);
+  check_launch("ahb_gdn_inter_fwd");
   if (want_state) return {o, hf};
   return {o};
 }
@@ -188,6 +205,7 @@ std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tens
   ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), sc,
                     s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
                     gcl.data_ptr<float>(), A.data_ptr<float>(), st);
+  check_launch("ahb_gdn_intra_fwd");
   auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
   auto vn = torch::empty_like(wt);
   ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
@@ -197,6 +215,7 @@ std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tens
   auto dvn = torch::empty_like(wt);
   ahb_gdn_inter_bwd(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(), gcl.data_ptr<float>(),
                     doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr, st);
+  check_launch("ahb_gdn_inter_bwd");
   u = torch::Tensor(); qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor();
   auto dq_p = torch::empty({s.B, s.H, s.NC, 64, 128}, f32);
   auto dk_p = torch::empty_like(dq_p), dgc_p = torch::empty_like(dq_p), dwt = torch::empty_like(dq_p);
@@ -206,6 +225,7 @@ std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tens
                      vn.data_ptr(), dvn.data_ptr(), sc, s.B, s.L, s.H, dq_p.data_ptr<float>(),
                      dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(), dwt.data_ptr<float>(), dgcl.data_ptr<float>(),
                      daqk.data_ptr<float>(), st);
+  check_launch("ahb_gdn_bwd_states");
   hs = torch::Tensor(); dhs = torch::Tensor(); vn = torch::Tensor();
   auto dv = torch::empty_like(q), dw = torch::empty_like(q);
   auto dbk_wy = torch::empty_like(dq_p), dgc_wy = torch::empty_like(dq_p);
@@ -213,12 +233,14 @@ std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tens
   ahb_gdn_bwd_wy(k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), A.data_ptr<float>(),
                  dvn.data_ptr(), dwt.data_ptr<float>(), s.B, s.L, s.H, dv.data_ptr(), dw.data_ptr(),
                  dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dakk.data_ptr<float>(), st);
+  check_launch("ahb_gdn_bwd_wy");
   auto dq = torch::empty_like(q), dk = torch::empty_like(q), db = torch::empty_like(q);
   auto dg = torch::empty_like(g);
   ahb_gdn_bwd_intra(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), daqk.data_ptr<float>(),
                     dakk.data_ptr<float>(), dq_p.data_ptr<float>(), dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(),
                     dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dgcl.data_ptr<float>(), sc, s.B, s.L, s.H,
                     dq.data_ptr(), dk.data_ptr(), db.data_ptr(), dg.data_ptr<float>(), st);
+  check_launch("ahb_gdn_bwd_intra");
   return {dq, dk, dv, dg, db, dw};
 }
 
@@ -245,6 +267,7 @@ torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch:
   auto y = torch::empty_like(x);
   ahb_ssd_fwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
               sbuf.data_ptr<float>(), cuml.data_ptr<float>(), nullptr, nullptr, y.data_ptr(), cur_stream());
+  check_launch("ahb_ssd_fwd");
   return y;
 }
 
@@ -266,6 +289,7 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
               H, sbuf.data_ptr<float>(), cuml.data_ptr<float>(), gbuf.data_ptr<float>(), dx.data_ptr(),
               ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(),
               dCp.data_ptr<float>(), cur_stream());
+  check_launch("ahb_ssd_bwd");
   return {dx, ddt, dA, dB, dC};
 }
 
@@ -323,8 +347,10 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
   auto st = cur_stream();
   ahb_moe_route(eidx.data_ptr<int>(), T, k, E, counts.data_ptr<int>(), off.data_ptr<int>(), pos.data_ptr<int>(),
                 row_src.data_ptr<int>(), Rcap, st);
+  check_launch("ahb_moe_route");
   auto xs = torch::empty({Rcap, d}, x.options());
   ahb_moe_gather(x.data_ptr(), row_src.data_ptr<int>(), Rcap, d, xs.data_ptr(), st);
+  check_launch("ahb_moe_gather");
   auto h = torch::empty({Rcap, F}, x.options());
   auto a1 = torch::empty_like(h);
   torch::Tensor a3;
@@ -355,6 +381,7 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
     sh = shc.data_ptr();
   }
   ahb_moe_combine(ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), sh, T, k, d, out.data_ptr(), st);
+  check_launch("ahb_moe_combine");
   if (!a3.defined()) a3 = torch::empty({0}, x.options());
   return {out, pos, off, row_src, xs, a1, a3, h, ys};
 }
@@ -375,9 +402,11 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
   check_acc(dw2_acc, w2.numel(), "dw2_acc");
   auto dys = torch::empty({Rcap, d}, xs.options());
   ahb_moe_zero_pad(dys.data_ptr(), row_src.data_ptr<int>(), Rcap, d, st);
+  check_launch("ahb_moe_zero_pad");
   auto dgate = torch::empty({T, k}, gatec.options());
   ahb_moe_combine_bwd(doc.data_ptr(), ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), T, k, d,
                       dys.data_ptr(), dgate.data_ptr<float>(), st);
+  check_launch("ahb_moe_combine_bwd");
   int* err = err_word().data_ptr<int>();
   auto dA1 = torch::empty({Rcap, F}, xs.options());
   torch::Tensor dA3;
@@ -421,6 +450,7 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
   }
   auto dx = torch::empty({T, d}, xs.options());
   ahb_moe_scatter_add(dxs.data_ptr(), pos.data_ptr<int>(), T, k, d, dx.data_ptr(), st);
+  check_launch("ahb_moe_scatter_add");
   return {dx, dgate};
 }
 
@@ -465,6 +495,7 @@ void optim_prepare(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, to
   ahb_optim_prepare(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
                     (int)(cstart.numel() - 1), (int)nblocks, grad_shard.data_ptr<float>(), master.data_ptr<float>(),
                     (float)inv, red.data_ptr<double>(), flags.data_ptr<int>(), cur_stream());
+  check_launch("ahb_optim_prepare");
 }
 
 void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torch::Tensor master, torch::Tensor m,
@@ -488,6 +519,7 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
                   (int)(cstart.numel() - 1), (int)nblocks, master.data_ptr<float>(), m.data_ptr<float>(),
                   v.data_ptr<float>(), grad_shard.data_ptr<float>(), coef.data_ptr<float>(), compute.data_ptr(), fp, fe,
                   a, cur_stream());
+  check_launch("ahb_optim_apply");
 }
 
 // ------------------------------------------------------------ fused LM head + cross entropy
@@ -513,6 +545,7 @@ std::vector<torch::Tensor> ce_fused_fwd(torch::Tensor h, torch::Tensor W, torch:
   auto acc = torch::zeros({2}, h.options().dtype(at::kFloat));
   ahb_ce_rows(logits.data_ptr(), lab.data_ptr<int64_t>(), Tp, (int)V, (float)ls, acc.data_ptr<float>(),
               acc.data_ptr<float>() + 1, cur_stream());
+  check_launch("ahb_ce_rows");
   return {acc.narrow(0, 0, 1), acc.narrow(0, 1, 1), logits, hp};
 }
 

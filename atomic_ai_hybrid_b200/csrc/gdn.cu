@@ -42,6 +42,7 @@ constexpr int LDB = D + 8;  // bf16 row stride of C x D tiles
 constexpr int LDF = D + 4;  // fp32 row stride of C x D tiles
 constexpr int LDC = C + 4;  // fp32 row stride of C x C tiles
 constexpr int BV = 32;      // value-block width of the recurrence kernels
+constexpr int NTH = 512;    // threads of the chunk-parallel kernels (16 warps: 4 row tiles x 4 column quarters)
 constexpr int LDV = BV + 8;
 
 AHB_DEVICE float bf(bf16 x) { return __bfloat162float(x); }
@@ -127,7 +128,7 @@ AHB_DEVICE void tri_ij(int p, int& i, int& j) {
 // smem: q,k,bk,wv,bke bf16 [C][LDB]; gc f32 [C][LDF]; aqk, akk, a f32 [C][LDC]; t 768 f32
 constexpr size_t SMEM_INTRA = 5 * C * LDB * 2 + C * LDF * 4 + 3 * C * LDC * 4 + 768 * 4;
 
-__global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
+__global__ void __launch_bounds__(NTH, 1) gdn_intra_fwd_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
     const float* __restrict__ g, const bf16* __restrict__ bg, const bf16* __restrict__ wg, float scale, int L,
     int H, bf16* __restrict__ wt_o, bf16* __restrict__ u_o, bf16* __restrict__ qg_o, bf16* __restrict__ kg_o,
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // 1. loads (q, k raw; bk = b*k, wv = w*v)
-  for (int i = tid; i < C * (D / 8); i += 256) {
+  for (int i = tid; i < C * (D / 8); i += NTH) {
     int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
     int64_t gi = ix.seq(b, (int64_t)n * C + r, h) + c8;
     uint4 qv = *reinterpret_cast<const uint4*>(q + gi);
@@ -169,15 +170,15 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
       st_bf16x2(wv_s + r * LDB + c8 + e, bf(wp[e]) * bf(vp[e]), bf(wp[e + 1]) * bf(vp[e + 1]));
     }
   }
-  load_gc(gc_s, g, ix, b, n, h, 256);  // includes __syncthreads
+  load_gc(gc_s, g, ix, b, n, h, NTH);  // includes __syncthreads
 
   // 2. bke = bk * e^gc
-  for (int i = tid; i < C * D; i += 256) {
+  for (int i = tid; i < C * D; i += NTH) {
     int r = i / D, d = i % D;
     bke_s[r * LDB + d] = __float2bfloat16_rn(bf(bk_s[r * LDB + d]) * __expf(gc_s[r * LDF + d]));
   }
   // 3a. off-diagonal 16x16 blocks of Aqk / Akk on tensor cores
-  for (int job = warp; job < 12; job += 8) {
+  for (int job = warp; job < 12; job += NTH / 32) {
     int I, J;
     pair_ij(job >> 1, I, J);
     const bool is_kk = job & 1;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
     for_acc<2>(acc, 0, 0, [&](int rr, int cc, float& val) { dst[(r0 + rr) * LDC + 16 * J + cc] = guard(val * sc); });
   }
   // 3b. diagonal blocks, exact per-channel sums (-20 floor on the exponent, as the reference)
-  for (int p = warp; p < 4 * 136; p += 8) {
+  for (int p = warp; p < 4 * 136; p += NTH / 32) {
     int blk = p / 136, i, j;
     tri_ij(p % 136, i, j);
     const int ri = 16 * blk + i, rj = 16 * blk + j;
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
     }
   }
   // upper parts are zero
-  for (int i = tid; i < C * C; i += 256) {
+  for (int i = tid; i < C * C; i += NTH) {
     int r = i / C, c = i % C;
     if (c > r) { aqk_s[r * LDC + c] = 0.f; akk_s[r * LDC + c] = 0.f; }
     if ((c >> 4) != (r >> 4)) a_s[r * LDC + c] = 0.f;
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
   // 4b. off-diagonal blocks by distance: X_IJ = -X_II sum_{K=J}^{I-1} S_IK X_KJ
   for (int dist = 1; dist < 4; ++dist) {
     const int np = 4 - dist;
-    for (int e = tid; e < np * 256; e += 256) {
+    for (int e = tid; e < np * 256; e += NTH) {
       int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
       int J = p, I = p + dist;
       float s = 0.f;
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
       t_s[e] = s;
     }
     __syncthreads();
-    for (int e = tid; e < np * 256; e += 256) {
+    for (int e = tid; e < np * 256; e += NTH) {
       int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
       int J = p, I = p + dist;
       float s = 0.f;
@@ -271,35 +272,35 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
   // 5. w~ = A bke, u = A wv  (warp: 16-row tile mt, 64-col half nh)
   const int64_t cb = ix.chunk(b, h, n);
   {
-    const int mt = warp & 3, nh = warp >> 2;
-    float accw[8][4], accu[8][4];
-    zero_acc<8>(accw);
-    zero_acc<8>(accu);
+    const int mt = warp & 3, nq = warp >> 2;
+    float accw[4][4], accu[4][4];
+    zero_acc<4>(accw);
+    zero_acc<4>(accu);
     RowA32 fa{a_s, LDC};
     KNB16 fbk{bke_s, LDB}, fbv{wv_s, LDB};
     for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 16) {
       uint32_t a[4];
       load_a(a, fa, 16 * mt, k0);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         uint32_t bb[2];
-        load_b(bb, fbk, k0, 64 * nh + 8 * j);
+        load_b(bb, fbk, k0, 32 * nq + 8 * j);
         mma16816(accw[j], a, bb);
-        load_b(bb, fbv, k0, 64 * nh + 8 * j);
+        load_b(bb, fbv, k0, 32 * nq + 8 * j);
         mma16816(accu[j], a, bb);
       }
     }
     bf16* wto = wt_o + cb * C * D;
     bf16* uo = u_o + cb * C * D;
-    store_pairs<8>(accw, 16 * mt, 64 * nh, [&](int r, int c, float x0, float x1) {
+    store_pairs<4>(accw, 16 * mt, 32 * nq, [&](int r, int c, float x0, float x1) {
       st_bf16x2(wto + r * D + c, guard(x0), guard(x1));
     });
-    store_pairs<8>(accu, 16 * mt, 64 * nh, [&](int r, int c, float x0, float x1) {
+    store_pairs<4>(accu, 16 * mt, 32 * nq, [&](int r, int c, float x0, float x1) {
       st_bf16x2(uo + r * D + c, guard(x0), guard(x1));
     });
   }
   // 6. qg, kg, gc_last, Aqk (and A) out
-  for (int i = tid; i < C * D / 2; i += 256) {
+  for (int i = tid; i < C * D / 2; i += NTH) {
     int r = (2 * i) / D, d = (2 * i) % D;
     float g0 = gc_s[r * LDF + d], g1 = gc_s[r * LDF + d + 1];
     float l0 = gc_s[(C - 1) * LDF + d], l1 = gc_s[(C - 1) * LDF + d + 1];
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(256) gdn_intra_fwd_kernel(
               bf(k_s[r * LDB + d + 1]) * __expf(l1 - g1));
   }
   if (tid < D) gcl_o[cb * D + tid] = gc_s[(C - 1) * LDF + tid];
-  for (int i = tid; i < C * C; i += 256) {
+  for (int i = tid; i < C * C; i += NTH) {
     int r = i / C, c = i % C;
     aqk_o[cb * C * C + i] = aqk_s[r * LDC + c];
     if (a_o) a_o[cb * C * C + i] = a_s[r * LDC + c];
@@ -480,7 +481,7 @@ __global__ void __launch_bounds__(128) gdn_inter_bwd_kernel(
 // smem: h, dh bf16 [D][LDB]; do, vn, dvn, q, k bf16 [C][LDB]; gc f32 [C][LDF]; red f32 [D]
 constexpr size_t SMEM_BWD_STATES = 2 * D * LDB * 2 + 5 * C * LDB * 2 + C * LDF * 4 + D * 4;
 
-__global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
+__global__ void __launch_bounds__(NTH, 1) gdn_bwd_states_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
     const bf16* __restrict__ dout, const bf16* __restrict__ h_store, const bf16* __restrict__ dh_store,
     const bf16* __restrict__ vn_store, const bf16* __restrict__ dvn_store, float scale, int L, int H,
@@ -501,31 +502,31 @@ __global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
   const Idx ix{L, H, NC};
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t cb = ix.chunk(b, h, n);
-  for (int i = tid; i < D * (D / 8); i += 256) {
+  for (int i = tid; i < D * (D / 8); i += NTH) {
     int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
     *reinterpret_cast<uint4*>(h_s + r * LDB + c8) = *reinterpret_cast<const uint4*>(h_store + cb * D * D + r * D + c8);
     *reinterpret_cast<uint4*>(dh_s + r * LDB + c8) =
         *reinterpret_cast<const uint4*>(dh_store + cb * D * D + r * D + c8);
   }
-  load_seq_tile(do_s, dout, ix, b, n, h, 256);
-  load_seq_tile(q_s, q, ix, b, n, h, 256);
-  load_seq_tile(k_s, k, ix, b, n, h, 256);
-  load_chunk_tile(vn_s, vn_store + cb * C * D, 256);
-  load_chunk_tile(dvn_s, dvn_store + cb * C * D, 256);
+  load_seq_tile(do_s, dout, ix, b, n, h, NTH);
+  load_seq_tile(q_s, q, ix, b, n, h, NTH);
+  load_seq_tile(k_s, k, ix, b, n, h, NTH);
+  load_chunk_tile(vn_s, vn_store + cb * C * D, NTH);
+  load_chunk_tile(dvn_s, dvn_store + cb * C * D, NTH);
   if (tid < D) red_s[tid] = 0.f;
-  load_gc(gc_s, g, ix, b, n, h, 256);
+  load_gc(gc_s, g, ix, b, n, h, NTH);
 
-  const int mt = warp & 3, nh = warp >> 2;
-  const int m0 = 16 * mt, n0 = 64 * nh;
-  float acc[8][4], dg[8][4];
-  zero_acc<8>(dg);
+  const int mt = warp & 3, nq = warp >> 2;
+  const int m0 = 16 * mt, n0 = 32 * nq;
+  float acc[4][4], dg[4][4];
+  zero_acc<4>(dg);
   // P1 = do h^T  -> dq_p = scale P1 e^gc ; dgc += dq_p q
-  zero_acc<8>(acc);
-  warp_mma<8>(acc, RowA16{do_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
+  zero_acc<4>(acc);
+  warp_mma<4>(acc, RowA16{do_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
   {
     const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
@@ -535,12 +536,12 @@ __global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
       }
   }
   // P2 = vn dh^T -> dk_p = P2 e^{gcl-gc}; dgc -= P2 kg; dgcl += P2 kg
-  zero_acc<8>(acc);
-  warp_mma<8>(acc, RowA16{vn_s, LDB}, NKB16{dh_s, LDB}, m0, n0, 0, D);
+  zero_acc<4>(acc);
+  warp_mma<4>(acc, RowA16{vn_s, LDB}, NKB16{dh_s, LDB}, m0, n0, 0, D);
   {
     const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
@@ -553,32 +554,33 @@ __global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
       }
   }
   // P3 = dvn h^T -> dwt = -P3
-  zero_acc<8>(acc);
-  warp_mma<8>(acc, RowA16{dvn_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
-  store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+  zero_acc<4>(acc);
+  warp_mma<4>(acc, RowA16{dvn_s, LDB}, NKB16{h_s, LDB}, m0, n0, 0, D);
+  store_pairs<4>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
     *reinterpret_cast<float2*>(dwt_o + cb * C * D + r * D + c) = make_float2(-x0, -x1);
   });
-  store_pairs<8>(dg, m0, n0, [&](int r, int c, float x0, float x1) {
+  store_pairs<4>(dg, m0, n0, [&](int r, int c, float x0, float x1) {
     *reinterpret_cast<float2*>(dgc_p + cb * C * D + r * D + c) = make_float2(x0, x1);
   });
   // dAqk = do vn^T (causal), unscaled
   {
-    float a4[4][4];
-    zero_acc<4>(a4);
-    warp_mma<4>(a4, RowA16{do_s, LDB}, NKB16{vn_s, LDB}, m0, 32 * nh, 0, D);
-    store_pairs<4>(a4, m0, 32 * nh, [&](int r, int c, float x0, float x1) {
+    float a4[2][4];
+    zero_acc<2>(a4);
+    warp_mma<2>(a4, RowA16{do_s, LDB}, NKB16{vn_s, LDB}, m0, 16 * nq, 0, D);
+    store_pairs<2>(a4, m0, 16 * nq, [&](int r, int c, float x0, float x1) {
       *reinterpret_cast<float2*>(daqk_o + cb * C * C + r * C + c) =
           make_float2(c <= r ? x0 : 0.f, c + 1 <= r ? x1 : 0.f);
     });
   }
   // dgcl += e^{gcl} sum_v dh h
   {
-    const int d = tid >> 1, half = tid & 1;
+    const int d = tid >> 2, quarter = tid & 3;
     float s = 0.f;
-    for (int vv = half * 64; vv < half * 64 + 64; ++vv) s += bf(dh_s[d * LDB + vv]) * bf(h_s[d * LDB + vv]);
+    for (int vv = quarter * 32; vv < quarter * 32 + 32; ++vv) s += bf(dh_s[d * LDB + vv]) * bf(h_s[d * LDB + vv]);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
     __syncthreads();
-    if (half == 0) dgcl_o[cb * D + d] = red_s[d] + __expf(gc_s[(C - 1) * LDF + d]) * s;
+    if (quarter == 0) dgcl_o[cb * D + d] = red_s[d] + __expf(gc_s[(C - 1) * LDF + d]) * s;
   }
 }
 
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_states_kernel(
 // smem: k, b, w, v, du bf16 [C][LDB]; gc, dwt f32 [C][LDF]; a, da, t f32 [C][LDC]
 constexpr size_t SMEM_BWD_WY = 5 * C * LDB * 2 + 2 * C * LDF * 4 + 3 * C * LDC * 4;
 
-__global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
+__global__ void __launch_bounds__(NTH, 1) gdn_bwd_wy_kernel(
     const bf16* __restrict__ k, const bf16* __restrict__ v, const float* __restrict__ g,
     const bf16* __restrict__ bg, const bf16* __restrict__ wg, const float* __restrict__ a_store,
     const bf16* __restrict__ dvn_store, const float* __restrict__ dwt, int L, int H, bf16* __restrict__ dv_o,
@@ -607,16 +609,16 @@ __global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
   const Idx ix{L, H, NC};
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t cb = ix.chunk(b, h, n);
-  load_seq_tile(k_s, k, ix, b, n, h, 256);
-  load_seq_tile(b_s, bg, ix, b, n, h, 256);
-  load_seq_tile(w_s, wg, ix, b, n, h, 256);
-  load_seq_tile(v_s, v, ix, b, n, h, 256);
-  load_chunk_tile(du_s, dvn_store + cb * C * D, 256);
-  load_chunk_tile_f32(dwt_s, LDF, dwt + cb * C * D, C, D, 256);
-  load_chunk_tile_f32(a_s, LDC, a_store + cb * C * C, C, C, 256);
-  load_gc(gc_s, g, ix, b, n, h, 256);
+  load_seq_tile(k_s, k, ix, b, n, h, NTH);
+  load_seq_tile(b_s, bg, ix, b, n, h, NTH);
+  load_seq_tile(w_s, wg, ix, b, n, h, NTH);
+  load_seq_tile(v_s, v, ix, b, n, h, NTH);
+  load_chunk_tile(du_s, dvn_store + cb * C * D, NTH);
+  load_chunk_tile_f32(dwt_s, LDF, dwt + cb * C * D, C, D, NTH);
+  load_chunk_tile_f32(a_s, LDC, a_store + cb * C * C, C, C, NTH);
+  load_gc(gc_s, g, ix, b, n, h, NTH);
 
-  const int mt = warp & 3, nh = warp >> 2;
+  const int mt = warp & 3, nq = warp >> 2;
   // dA (strictly lower) = du (w v)^T + dwt (bk e^gc)^T
   {
     auto fb_wv = [&](int kv, int nj) -> uint32_t {
@@ -628,26 +630,26 @@ __global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
       return pack2(bf(b_s[nj * LDB + kd]) * bf(k_s[nj * LDB + kd]) * __expf(gj[kd]),
                    bf(b_s[nj * LDB + kd + 1]) * bf(k_s[nj * LDB + kd + 1]) * __expf(gj[kd + 1]));
     };
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, RowA16{du_s, LDB}, fb_wv, 16 * mt, 32 * nh, 0, D);
-    warp_mma<4>(acc, RowA32{dwt_s, LDF}, fb_bke, 16 * mt, 32 * nh, 0, D);
-    for_acc<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float& x) { da_s[r * LDC + c] = c < r ? x : 0.f; });
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2>(acc, RowA16{du_s, LDB}, fb_wv, 16 * mt, 16 * nq, 0, D);
+    warp_mma<2>(acc, RowA32{dwt_s, LDF}, fb_bke, 16 * mt, 16 * nq, 0, D);
+    for_acc<2>(acc, 16 * mt, 16 * nq, [&](int r, int c, float& x) { da_s[r * LDC + c] = c < r ? x : 0.f; });
   }
   // d(wv) = A^T du -> dw, dv ; d(bke) = A^T dwt -> dbk_wy, dgc_wy
   {
-    const int m0 = 16 * mt, n0 = 64 * nh;
-    float acc[8][4];
-    zero_acc<8>(acc);
-    warp_mma<8>(acc, ColA32{a_s, LDC}, KNB16{du_s, LDB}, m0, n0, m0, C);
-    store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+    const int m0 = 16 * mt, n0 = 32 * nq;
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, ColA32{a_s, LDC}, KNB16{du_s, LDB}, m0, n0, m0, C);
+    store_pairs<4>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
       int64_t gi = ix.seq(b, (int64_t)n * C + r, h) + c;
       st_bf16x2(dw_o + gi, x0 * bf(v_s[r * LDB + c]), x1 * bf(v_s[r * LDB + c + 1]));
       st_bf16x2(dv_o + gi, x0 * bf(w_s[r * LDB + c]), x1 * bf(w_s[r * LDB + c + 1]));
     });
-    zero_acc<8>(acc);
-    warp_mma<8>(acc, ColA32{a_s, LDC}, KNB32{dwt_s, LDF}, m0, n0, m0, C);
-    store_pairs<8>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, ColA32{a_s, LDC}, KNB32{dwt_s, LDF}, m0, n0, m0, C);
+    store_pairs<4>(acc, m0, n0, [&](int r, int c, float x0, float x1) {
       float e0 = __expf(gc_s[r * LDF + c]), e1 = __expf(gc_s[r * LDF + c + 1]);
       float d0 = x0 * e0, d1 = x1 * e1;
       *reinterpret_cast<float2*>(dbk_o + cb * C * D + r * D + c) = make_float2(d0, d1);
@@ -659,18 +661,18 @@ __global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
   __syncthreads();
   // T = dA A^T
   {
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, RowA32{da_s, LDC}, NKB32{a_s, LDC}, 16 * mt, 32 * nh, 0, 16 * (mt + 1));
-    for_acc<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float& x) { t_s[r * LDC + c] = x; });
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2>(acc, RowA32{da_s, LDC}, NKB32{a_s, LDC}, 16 * mt, 16 * nq, 0, 16 * (mt + 1));
+    for_acc<2>(acc, 16 * mt, 16 * nq, [&](int r, int c, float& x) { t_s[r * LDC + c] = x; });
   }
   __syncthreads();
   // dAkk = -(A^T T), strictly lower
   {
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, ColA32{a_s, LDC}, KNB32{t_s, LDC}, 16 * mt, 32 * nh, 16 * mt, C);
-    store_pairs<4>(acc, 16 * mt, 32 * nh, [&](int r, int c, float x0, float x1) {
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2>(acc, ColA32{a_s, LDC}, KNB32{t_s, LDC}, 16 * mt, 16 * nq, 16 * mt, C);
+    store_pairs<2>(acc, 16 * mt, 16 * nq, [&](int r, int c, float x0, float x1) {
       *reinterpret_cast<float2*>(dakk_o + cb * C * C + r * C + c) =
           make_float2(c < r ? -x0 : 0.f, c + 1 < r ? -x1 : 0.f);
     });
@@ -681,7 +683,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_wy_kernel(
 // smem: q, k, b bf16 [C][LDB]; gc, dgc f32 [C][LDF]; daqk, dakk f32 [C][LDC]
 constexpr size_t SMEM_BWD_INTRA = 3 * C * LDB * 2 + 2 * C * LDF * 4 + 2 * C * LDC * 4;
 
-__global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
+__global__ void __launch_bounds__(NTH, 1) gdn_bwd_intra_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
     const bf16* __restrict__ bg, const float* __restrict__ daqk, const float* __restrict__ dakk,
     const float* __restrict__ dq_p, const float* __restrict__ dk_p, const float* __restrict__ dgc_p,
@@ -701,21 +703,21 @@ __global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
   const Idx ix{L, H, NC};
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t cb = ix.chunk(b, h, n);
-  load_seq_tile(q_s, q, ix, b, n, h, 256);
-  load_seq_tile(k_s, k, ix, b, n, h, 256);
-  load_seq_tile(b_s, bg, ix, b, n, h, 256);
-  load_chunk_tile_f32(daqk_s, LDC, daqk + cb * C * C, C, C, 256);
-  load_chunk_tile_f32(dakk_s, LDC, dakk + cb * C * C, C, C, 256);
-  load_gc(gc_s, g, ix, b, n, h, 256);
+  load_seq_tile(q_s, q, ix, b, n, h, NTH);
+  load_seq_tile(k_s, k, ix, b, n, h, NTH);
+  load_seq_tile(b_s, bg, ix, b, n, h, NTH);
+  load_chunk_tile_f32(daqk_s, LDC, daqk + cb * C * C, C, C, NTH);
+  load_chunk_tile_f32(dakk_s, LDC, dakk + cb * C * C, C, C, NTH);
+  load_gc(gc_s, g, ix, b, n, h, NTH);
 
-  // warp tile: rows of block I = mt (16 rows), 64 columns (channel half nh)
-  const int I = warp & 3, nh = warp >> 2;
-  const int m0 = 16 * I, n0 = 64 * nh;
+  // warp tile: rows of block I (16 rows), 32 channel columns (quarter nq)
+  const int I = warp & 3, nq = warp >> 2;
+  const int m0 = 16 * I, n0 = 32 * nq;
   const int r0 = m0;  // reference row of block I
-  float dq[8][4], dbk[8][4], dk[8][4];
-  zero_acc<8>(dq);
-  zero_acc<8>(dbk);
-  zero_acc<8>(dk);
+  float dq[4][4], dbk[4][4], dk[4][4];
+  zero_acc<4>(dq);
+  zero_acc<4>(dbk);
+  zero_acc<4>(dk);
   // (a) row side, columns j < 16I: dq_I, dbk_I  (B = k_j e^{gc_r - gc_j})
   if (I > 0) {
     const float* gr = gc_s + r0 * LDF;
@@ -723,10 +725,10 @@ __global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
       return pack2(bf(k_s[kj * LDB + nd]) * __expf(gr[nd] - gc_s[kj * LDF + nd]),
                    bf(k_s[(kj + 1) * LDB + nd]) * __expf(gr[nd] - gc_s[(kj + 1) * LDF + nd]));
     };
-    warp_mma<8>(dq, RowA32{daqk_s, LDC}, fb, m0, n0, 0, r0);
-    warp_mma<8>(dbk, RowA32{dakk_s, LDC}, fb, m0, n0, 0, r0);
-    for_acc<8>(dq, m0, n0, [&](int r, int c, float& x) { x *= scale * __expf(gc_s[r * LDF + c] - gr[c]); });
-    for_acc<8>(dbk, m0, n0, [&](int r, int c, float& x) { x *= __expf(gc_s[r * LDF + c] - gr[c]); });
+    warp_mma<4>(dq, RowA32{daqk_s, LDC}, fb, m0, n0, 0, r0);
+    warp_mma<4>(dbk, RowA32{dakk_s, LDC}, fb, m0, n0, 0, r0);
+    for_acc<4>(dq, m0, n0, [&](int r, int c, float& x) { x *= scale * __expf(gc_s[r * LDF + c] - gr[c]); });
+    for_acc<4>(dbk, m0, n0, [&](int r, int c, float& x) { x *= __expf(gc_s[r * LDF + c] - gr[c]); });
   }
   // (b) column side from later blocks I2 > I: dk_j += e^{gc_r2 - gc_j} sum_i dA[i,j] x_i e^{gc_i - gc_r2}
   for (int I2 = I + 1; I2 < 4; ++I2) {
@@ -747,15 +749,15 @@ __global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
       return pack2(bf(b_s[i0 * LDB + nd]) * bf(k_s[i0 * LDB + nd]) * __expf(gc_s[i0 * LDF + nd] - gr[nd]),
                    bf(b_s[i1 * LDB + nd]) * bf(k_s[i1 * LDB + nd]) * __expf(gc_s[i1 * LDF + nd] - gr[nd]));
     };
-    float t1[8][4], t2[8][4];
-    zero_acc<8>(t1);
-    zero_acc<8>(t2);
+    float t1[4][4], t2[4][4];
+    zero_acc<4>(t1);
+    zero_acc<4>(t2);
     // A operand rows are j within block I: pass m0 offset through the loader (rj includes m0)
-    warp_mma<8>(t1, fa_q, fb_q, m0, n0, 0, 16);
-    warp_mma<8>(t2, fa_k, fb_k, m0, n0, 0, 16);
+    warp_mma<4>(t1, fa_q, fb_q, m0, n0, 0, 16);
+    warp_mma<4>(t2, fa_k, fb_k, m0, n0, 0, 16);
     const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
@@ -766,7 +768,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_intra_kernel(
   {
     const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = m0 + gq + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
@@ -835,7 +837,7 @@ void ahb_gdn_intra_fwd(const void* q, const void* k, const void* v, const float*
   static bool init = false;
   if (!init) { set_smem(gdn_intra_fwd_kernel, SMEM_INTRA); init = true; }
   dim3 grid(L / C, H, B);
-  gdn_intra_fwd_kernel<<<grid, 256, SMEM_INTRA, st>>>(
+  gdn_intra_fwd_kernel<<<grid, NTH, SMEM_INTRA, st>>>(
       (const bf16*)q, (const bf16*)k, (const bf16*)v, g, (const bf16*)bg, (const bf16*)wg, scale, L, H, (bf16*)wt,
       (bf16*)u, (bf16*)qg, (bf16*)kg, aqk, gcl, a_out);
 }
@@ -869,7 +871,7 @@ void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void
   static bool init = false;
   if (!init) { set_smem(gdn_bwd_states_kernel, SMEM_BWD_STATES); init = true; }
   dim3 grid(L / C, H, B);
-  gdn_bwd_states_kernel<<<grid, 256, SMEM_BWD_STATES, st>>>(
+  gdn_bwd_states_kernel<<<grid, NTH, SMEM_BWD_STATES, st>>>(
       (const bf16*)q, (const bf16*)k, g, (const bf16*)dout, (const bf16*)h_store, (const bf16*)dh_store,
       (const bf16*)vn_store, (const bf16*)dvn_store, scale, L, H, dq_p, dk_p, dgc_p, dwt, dgcl, daqk);
 }
@@ -880,7 +882,7 @@ void ahb_gdn_bwd_wy(const void* k, const void* v, const float* g, const void* bg
   static bool init = false;
   if (!init) { set_smem(gdn_bwd_wy_kernel, SMEM_BWD_WY); init = true; }
   dim3 grid(L / C, H, B);
-  gdn_bwd_wy_kernel<<<grid, 256, SMEM_BWD_WY, st>>>((const bf16*)k, (const bf16*)v, g, (const bf16*)bg,
+  gdn_bwd_wy_kernel<<<grid, NTH, SMEM_BWD_WY, st>>>((const bf16*)k, (const bf16*)v, g, (const bf16*)bg,
                                                     (const bf16*)wg, a_store, (const bf16*)dvn_store, dwt, L, H,
                                                     (bf16*)dv, (bf16*)dw, dbk_wy, dgc_wy, dakk);
 }
@@ -892,7 +894,7 @@ void ahb_gdn_bwd_intra(const void* q, const void* k, const float* g, const void*
   static bool init = false;
   if (!init) { set_smem(gdn_bwd_intra_kernel, SMEM_BWD_INTRA); init = true; }
   dim3 grid(L / C, H, B);
-  gdn_bwd_intra_kernel<<<grid, 256, SMEM_BWD_INTRA, st>>>(
+  gdn_bwd_intra_kernel<<<grid, NTH, SMEM_BWD_INTRA, st>>>(
       (const bf16*)q, (const bf16*)k, g, (const bf16*)bg, daqk, dakk, dq_p, dk_p, dgc_p, dbk_wy, dgc_wy, dgcl, scale,
       L, H, (bf16*)dq, (bf16*)dk, (bf16*)db, dg);
 }

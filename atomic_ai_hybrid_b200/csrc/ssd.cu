@@ -43,14 +43,14 @@ struct SIdx {
 };
 
 AHB_DEVICE void load_bn_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, int n) {
-  for (int i = threadIdx.x; i < C * (N / 8); i += 256) {
+  for (int i = threadIdx.x; i < C * (N / 8); i += blockDim.x) {
     int r = i / (N / 8), c8 = (i % (N / 8)) * 8;
     *reinterpret_cast<uint4*>(dst + r * LDN + c8) =
         *reinterpret_cast<const uint4*>(src + ix.bn(b, (int64_t)n * C + r) + c8);
   }
 }
 AHB_DEVICE void load_xp_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, int n, int h) {
-  for (int i = threadIdx.x; i < C * (P / 8); i += 256) {
+  for (int i = threadIdx.x; i < C * (P / 8); i += blockDim.x) {
     int r = i / (P / 8), c8 = (i % (P / 8)) * 8;
     *reinterpret_cast<uint4*>(dst + r * LDP + c8) =
         *reinterpret_cast<const uint4*>(src + ix.xp(b, (int64_t)n * C + r, h) + c8);
@@ -58,7 +58,7 @@ AHB_DEVICE void load_xp_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, 
 }
 // fp32 (P x N) state tile -> bf16 smem [P][LDN]
 AHB_DEVICE void load_state_bf(bf16* dst, const float* src) {
-  for (int i = threadIdx.x; i < P * (N / 4); i += 256) {
+  for (int i = threadIdx.x; i < P * (N / 4); i += blockDim.x) {
     int r = i / (N / 4), c4 = (i % (N / 4)) * 4;
     float4 v = *reinterpret_cast<const float4*>(src + r * N + c4);
     st2(dst + r * LDN + c4, v.x, v.y);
@@ -77,25 +77,34 @@ AHB_DEVICE void cum_decay(float* cum, const bf16* dt_s, float A) {
   }
   __syncthreads();
 }
+// triangular pair index -> (i, j), i >= j, within 16
+AHB_DEVICE void tri_ij(int p, int& i, int& j) {
+  i = (int)((sqrtf(8.f * p + 1.f) - 1.f) * 0.5f);
+  while ((i + 1) * (i + 2) / 2 <= p) ++i;
+  while (i * (i + 1) / 2 > p) --i;
+  j = p - i * (i + 1) / 2;
+}
+
 AHB_DEVICE float dbx(const bf16* x_s, const bf16* dt_s, int r, int p) {
   return bf(x_s[r * LDP + p]) * bf(dt_s[r * LDP + p]);
 }
 
-// y_diag for the warp's tile: rows [16I, 16I+16), cols [n0, n0+32) (NT = 4)
+// y_diag for the warp's tile: rows [16I, 16I+16), cols [n0, n0+8*NT)
+template <int NT>
 AHB_DEVICE void ydiag_tile(float (*acc)[4], const float* cb_s, const bf16* x_s, const bf16* dt_s, const float* cum,
                            int I, int n0) {
   const int r0 = 16 * I;
-  zero_acc<4>(acc);
+  zero_acc<NT>(acc);
   if (I > 0) {
     const float* cr = cum + r0 * LDPF;
     auto fb = [&](int kj, int np) -> uint32_t {
       return pack2(dbx(x_s, dt_s, kj, np) * __expf(cr[np] - cum[kj * LDPF + np]),
                    dbx(x_s, dt_s, kj + 1, np) * __expf(cr[np] - cum[(kj + 1) * LDPF + np]));
     };
-    warp_mma<4>(acc, RowA32{cb_s, LDCC}, fb, r0, n0, 0, r0);
-    for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) { v *= __expf(cum[r * LDPF + c] - cr[c]); });
+    warp_mma<NT>(acc, RowA32{cb_s, LDCC}, fb, r0, n0, 0, r0);
+    for_acc<NT>(acc, r0, n0, [&](int r, int c, float& v) { v *= __expf(cum[r * LDPF + c] - cr[c]); });
   }
-  for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) {
+  for_acc<NT>(acc, r0, n0, [&](int r, int c, float& v) {
     float s = 0.f;
     const float ci = cum[r * LDPF + c];
     for (int j = r0; j <= r; ++j)
@@ -105,26 +114,27 @@ AHB_DEVICE void ydiag_tile(float (*acc)[4], const float* cb_s, const bf16* x_s, 
 }
 
 // y_off tile: e^{max(c,-20)} * (C S^T)
+template <int NT>
 AHB_DEVICE void yoff_tile(float (*acc)[4], const bf16* c_s, const bf16* sin_s, const float* cum, int I, int n0) {
-  zero_acc<4>(acc);
-  warp_mma<4>(acc, RowA16{c_s, LDN}, NKB16{sin_s, LDN}, 16 * I, n0, 0, N);
-  for_acc<4>(acc, 16 * I, n0, [&](int r, int c, float& v) { v *= __expf(fmaxf(cum[r * LDPF + c], -20.f)); });
+  zero_acc<NT>(acc);
+  warp_mma<NT>(acc, RowA16{c_s, LDN}, NKB16{sin_s, LDN}, 16 * I, n0, 0, N);
+  for_acc<NT>(acc, 16 * I, n0, [&](int r, int c, float& v) { v *= __expf(fmaxf(cum[r * LDPF + c], -20.f)); });
 }
 
 // C B^T (C x C), sanitized
 AHB_DEVICE void compute_cb(float* cb_s, const bf16* c_s, const bf16* b_s) {
   const int warp = threadIdx.x >> 5;
-  float acc[4][4];
-  zero_acc<4>(acc);
-  warp_mma<4>(acc, RowA16{c_s, LDN}, NKB16{b_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, N);
-  for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2),
+  float acc[2][4];
+  zero_acc<2>(acc);
+  warp_mma<2>(acc, RowA16{c_s, LDN}, NKB16{b_s, LDN}, 16 * (warp & 3), 16 * (warp >> 2), 0, N);
+  for_acc<2>(acc, 16 * (warp & 3), 16 * (warp >> 2),
              [&](int r, int c, float& v) { cb_s[r * LDCC + c] = sanitize(v, 1e4f); });
 }
 
 // ============================================================ forward: chunk states
 constexpr size_t SMEM_STATE_F = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
 
-__global__ void __launch_bounds__(256) ssd_state_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
+__global__ void __launch_bounds__(512, 1) ssd_state_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
                                                             const float* __restrict__ A, const bf16* __restrict__ Bm,
                                                             int L, int H, float* __restrict__ send,
                                                             float* __restrict__ cuml) {
@@ -150,11 +160,11 @@ __global__ void __launch_bounds__(256) ssd_state_fwd_kernel(const bf16* __restri
       return pack2(dbx(x_s, dt_s, kj, rp) * __expf(fmaxf(cl[rp] - cum[kj * LDPF + rp], -20.f)),
                    dbx(x_s, dt_s, kj + 1, rp) * __expf(fmaxf(cl[rp] - cum[(kj + 1) * LDPF + rp], -20.f)));
     };
-    float acc[8][4];
-    zero_acc<8>(acc);
-    warp_mma<8>(acc, fa, KNB16{b_s, LDN}, 16 * (warp & 3), 64 * (warp >> 2), 0, C);
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, fa, KNB16{b_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, C);
     float* out = send + cb * P * N;
-    for_acc<8>(acc, 16 * (warp & 3), 64 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = sanitize(v, 1e4f); });
+    for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = sanitize(v, 1e4f); });
     __syncthreads();
   }
 }
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(256) ssd_scan_kernel(float* __restrict__ buf, 
 // ============================================================ forward: outputs
 constexpr size_t SMEM_OUT_F = 2 * C * LDN * 2 + C * LDCC * 4 + 2 * C * LDP * 2 + C * LDPF * 4 + P * LDN * 2;
 
-__global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
+__global__ void __launch_bounds__(512, 1) ssd_out_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
                                                           const float* __restrict__ A, const bf16* __restrict__ Bm,
                                                           const bf16* __restrict__ Cm, const float* __restrict__ sin,
                                                           int L, int H, bf16* __restrict__ y) {
@@ -232,7 +242,7 @@ __global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict
   load_bn_tile(c_s, Cm, ix, b, n);
   __syncthreads();
   compute_cb(cb_s, c_s, b_s);
-  const int I = warp & 3, n0 = 32 * (warp >> 2);
+  const int I = warp & 3, n0 = 16 * (warp >> 2);
   const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
   for (int h = h0; h < h0 + hpg; ++h) {
     const int64_t cb = ix.ch(b, h, n);
@@ -240,12 +250,12 @@ __global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict
     load_xp_tile(dt_s, dt, ix, b, n, h);
     load_state_bf(sin_s, sin + cb * P * N);
     cum_decay(cum, dt_s, A[h]);
-    float yd[4][4], yo[4][4];
-    ydiag_tile(yd, cb_s, x_s, dt_s, cum, I, n0);
-    yoff_tile(yo, c_s, sin_s, cum, I, n0);
+    float yd[2][4], yo[2][4];
+    ydiag_tile<2>(yd, cb_s, x_s, dt_s, cum, I, n0);
+    yoff_tile<2>(yo, c_s, sin_s, cum, I, n0);
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2; ++j) {
       const int c = n0 + 8 * j + 2 * t;
       const int r = 16 * I + g;
       st2(y + ix.xp(b, (int64_t)n * C + r, h) + c, sanitize(sanitize(yd[j][0], 1e4f) + sanitize(yo[j][0], 1e4f), 1e4f),
@@ -261,7 +271,7 @@ __global__ void __launch_bounds__(256) ssd_out_fwd_kernel(const bf16* __restrict
 // ============================================================ backward: G = (dy e^c)^T C  per chunk/head
 constexpr size_t SMEM_G = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
 
-__global__ void __launch_bounds__(256) ssd_dstate_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dt,
+__global__ void __launch_bounds__(512, 1) ssd_dstate_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dt,
                                                          const float* __restrict__ A, const bf16* __restrict__ Cm,
                                                          int L, int H, float* __restrict__ gbuf) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -282,11 +292,11 @@ __global__ void __launch_bounds__(256) ssd_dstate_kernel(const bf16* __restrict_
       return pack2(bf(dy_s[ki * LDP + rp]) * __expf(fmaxf(cum[ki * LDPF + rp], -20.f)),
                    bf(dy_s[(ki + 1) * LDP + rp]) * __expf(fmaxf(cum[(ki + 1) * LDPF + rp], -20.f)));
     };
-    float acc[8][4];
-    zero_acc<8>(acc);
-    warp_mma<8>(acc, fa, KNB16{c_s, LDN}, 16 * (warp & 3), 64 * (warp >> 2), 0, C);
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4>(acc, fa, KNB16{c_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, C);
     float* out = gbuf + ix.ch(b, h, n) * P * N;
-    for_acc<8>(acc, 16 * (warp & 3), 64 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = v; });
+    for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = v; });
     __syncthreads();
   }
 }
@@ -297,7 +307,7 @@ __global__ void __launch_bounds__(256) ssd_dstate_kernel(const bf16* __restrict_
 constexpr size_t SMEM_BWD =
     2 * C * LDN * 2 + 2 * C * LDCC * 4 + 3 * C * LDP * 2 + 3 * C * LDPF * 4 + 2 * P * LDN * 2 + P * 4;
 
-__global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
+__global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ dt, const float* __restrict__ A,
     const bf16* __restrict__ Bm, const bf16* __restrict__ Cm, const bf16* __restrict__ dy,
     const float* __restrict__ sin, const float* __restrict__ dse, int L, int H, bf16* __restrict__ dx,
@@ -325,10 +335,10 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
   __syncthreads();
   compute_cb(cb_s, c_s, b_s);
   // dB / dC accumulators: warp tile rows [16*(warp&3)), cols [64*(warp>>2)), 8 n-tiles
-  const int mt = warp & 3, nh = warp >> 2;
-  float dBa[8][4], dCa[8][4];
-  zero_acc<8>(dBa);
-  zero_acc<8>(dCa);
+  const int mt = warp & 3, nq = warp >> 2;
+  float dBa[4][4], dCa[4][4];
+  zero_acc<4>(dBa);
+  zero_acc<4>(dCa);
   const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
   for (int h = h0; h < h0 + hpg; ++h) {
     const int64_t cbi = ix.ch(b, h, n);
@@ -344,9 +354,9 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
     // (1) dCB[i,j] = sum_p dy[i,p] e^{c_i-c_j} dBx[j,p]   (j <= i)
     {
       const int I = mt, r0 = 16 * I;
-      float acc[4][4];
-      zero_acc<4>(acc);
-      const int n0 = 32 * nh;  // j columns [n0, n0+32)
+      float acc[2][4];
+      zero_acc<2>(acc);
+      const int n0 = 16 * nq;  // j columns [n0, n0+16)
       if (I > 0 && n0 < r0) {
         const float* cr = cum + r0 * LDPF;
         auto fa = [&](int ri, int kp) -> uint32_t {
@@ -357,45 +367,50 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
           return pack2(dbx(x_s, dt_s, nj, kp) * __expf(cr[kp] - cum[nj * LDPF + kp]),
                        dbx(x_s, dt_s, nj, kp + 1) * __expf(cr[kp + 1] - cum[nj * LDPF + kp + 1]));
         };
-        warp_mma<4>(acc, fa, fb, r0, n0, 0, P);
+        warp_mma<2>(acc, fa, fb, r0, n0, 0, P);
       }
-      for_acc<4>(acc, r0, n0, [&](int r, int c, float& v) {
-        if (c >= r0) {  // diagonal block (exact) or above it (zero)
-          float s = 0.f;
-          if (c <= r)
-            for (int p = 0; p < P; ++p)
-              s += bf(dy_s[r * LDP + p]) * dbx(x_s, dt_s, c, p) *
-                   __expf(fmaxf(cum[r * LDPF + p] - cum[c * LDPF + p], -20.f));
-          v = s;
-        }
-        dcb_s[r * LDCC + c] = v;
+      for_acc<2>(acc, r0, n0, [&](int r, int c, float& v) {
+        const bool diag = c >= r0 && c < r0 + 16 && c <= r;  // written by the exact pass below
+        if (!diag) dcb_s[r * LDCC + c] = c >= r0 ? 0.f : v;
       });
+    }
+    // exact per-channel sums of the diagonal 16x16 blocks: one (i, j) pair per thread
+    for (int q = tid; q < 4 * 136; q += blockDim.x) {
+      int i, j;
+      tri_ij(q % 136, i, j);
+      const int r = 16 * (q / 136) + i, c = 16 * (q / 136) + j;
+      float sacc = 0.f;
+#pragma unroll 8
+      for (int p = 0; p < P; ++p)
+        sacc += bf(dy_s[r * LDP + p]) * dbx(x_s, dt_s, c, p) *
+                __expf(fmaxf(cum[r * LDPF + p] - cum[c * LDPF + p], -20.f));
+      dcb_s[r * LDCC + c] = sacc;
     }
     __syncthreads();
     // (2) dC += dCB B + (dy e^c) S_in^T ;  (3) dB += dCB^T C + (dBx e^{cL-c}) dS_end^T
     {
-      const int m0 = 16 * mt, n0 = 64 * nh;
-      warp_mma<8>(dCa, RowA32{dcb_s, LDCC}, KNB16{b_s, LDN}, m0, n0, 0, m0 + 16);
+      const int m0 = 16 * mt, n0 = 32 * nq;
+      warp_mma<4>(dCa, RowA32{dcb_s, LDCC}, KNB16{b_s, LDN}, m0, n0, 0, m0 + 16);
       auto fa_dy = [&](int ri, int kp) -> uint32_t {
         return pack2(bf(dy_s[ri * LDP + kp]) * __expf(fmaxf(cum[ri * LDPF + kp], -20.f)),
                      bf(dy_s[ri * LDP + kp + 1]) * __expf(fmaxf(cum[ri * LDPF + kp + 1], -20.f)));
       };
-      warp_mma<8>(dCa, fa_dy, KNB16{sin_s, LDN}, m0, n0, 0, P);
-      warp_mma<8>(dBa, ColA32{dcb_s, LDCC}, KNB16{c_s, LDN}, m0, n0, m0, C);
+      warp_mma<4>(dCa, fa_dy, KNB16{sin_s, LDN}, m0, n0, 0, P);
+      warp_mma<4>(dBa, ColA32{dcb_s, LDCC}, KNB16{c_s, LDN}, m0, n0, m0, C);
       auto fa_bx = [&](int rj, int kp) -> uint32_t {
         return pack2(dbx(x_s, dt_s, rj, kp) * __expf(fmaxf(cl[kp] - cum[rj * LDPF + kp], -20.f)),
                      dbx(x_s, dt_s, rj, kp + 1) * __expf(fmaxf(cl[kp + 1] - cum[rj * LDPF + kp + 1], -20.f)));
       };
-      warp_mma<8>(dBa, fa_bx, KNB16{dse_s, LDN}, m0, n0, 0, P);
+      warp_mma<4>(dBa, fa_bx, KNB16{dse_s, LDN}, m0, n0, 0, P);
     }
     // (4)+(5) per (t,p) tile: y_diag, y_off, ddBx (diag part, state part) -> dc, ddBx
     {
-      const int I = mt, n0 = 32 * nh, r0 = 16 * I;
-      float yd[4][4], yo[4][4], dd[4][4], ds[4][4];
-      ydiag_tile(yd, cb_s, x_s, dt_s, cum, I, n0);
-      yoff_tile(yo, c_s, sin_s, cum, I, n0);
+      const int I = mt, n0 = 16 * nq, r0 = 16 * I;
+      float yd[2][4], yo[2][4], dd[2][4], ds[2][4];
+      ydiag_tile<2>(yd, cb_s, x_s, dt_s, cum, I, n0);
+      yoff_tile<2>(yo, c_s, sin_s, cum, I, n0);
       // ddBx_diag[j,p] = sum_{i>=j} CB[i,j] dy[i,p] e^{c_i-c_j}
-      zero_acc<4>(dd);
+      zero_acc<2>(dd);
       for (int I2 = I + 1; I2 < 4; ++I2) {
         const int r2 = 16 * I2;
         const float* cr = cum + r2 * LDPF;
@@ -406,19 +421,19 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
           return pack2(bf(dy_s[(r2 + ki) * LDP + np]) * __expf(cum[(r2 + ki) * LDPF + np] - cr[np]),
                        bf(dy_s[(r2 + ki + 1) * LDP + np]) * __expf(cum[(r2 + ki + 1) * LDPF + np] - cr[np]));
         };
-        float tacc[4][4];
-        zero_acc<4>(tacc);
-        warp_mma<4>(tacc, fa, fb, r0, n0, 0, 16);
+        float tacc[2][4];
+        zero_acc<2>(tacc);
+        warp_mma<2>(tacc, fa, fb, r0, n0, 0, 16);
         const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 2; ++j)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             int r = r0 + g + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
             dd[j][e] += tacc[j][e] * __expf(cr[c] - cum[r * LDPF + c]);
           }
       }
-      for_acc<4>(dd, r0, n0, [&](int r, int c, float& v) {
+      for_acc<2>(dd, r0, n0, [&](int r, int c, float& v) {
         float s = 0.f;
         const float cj = cum[r * LDPF + c];
         for (int i = r; i < r0 + 16; ++i)
@@ -426,11 +441,11 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
         v += s;
       });
       // ddBx_state[j,p] = e^{cL-c_j} sum_s B[j,s] dS_end[p,s]
-      zero_acc<4>(ds);
-      warp_mma<4>(ds, RowA16{b_s, LDN}, NKB16{dse_s, LDN}, r0, n0, 0, N);
+      zero_acc<2>(ds);
+      warp_mma<2>(ds, RowA16{b_s, LDN}, NKB16{dse_s, LDN}, r0, n0, 0, N);
       const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = r0 + g + (e >> 1) * 8, c = n0 + 8 * j + 2 * t + (e & 1);
@@ -453,12 +468,13 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
     __syncthreads();
     // dcL (last row): sum_j dBx ddBx_state (accumulated above into dcl_s) + state carry
     {
-      const int p = tid >> 2, q4 = tid & 3;
+      const int p = tid >> 3, q8 = tid & 7;
       float s_car = 0.f;
-      for (int s2 = q4 * 32; s2 < q4 * 32 + 32; ++s2) s_car += bf(dse_s[p * LDN + s2]) * bf(sin_s[p * LDN + s2]);
+      for (int s2 = q8 * 16; s2 < q8 * 16 + 16; ++s2) s_car += bf(dse_s[p * LDN + s2]) * bf(sin_s[p * LDN + s2]);
       s_car += __shfl_xor_sync(0xffffffffu, s_car, 1);
       s_car += __shfl_xor_sync(0xffffffffu, s_car, 2);
-      if (q4 == 0) {
+      s_car += __shfl_xor_sync(0xffffffffu, s_car, 4);
+      if (q8 == 0) {
         float add = dcl_s[p];
         if (cl[p] > -20.f) add += s_car * __expf(cl[p]);
         dc_s[(C - 1) * LDPF + p] += add;
@@ -480,7 +496,7 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
       }
     }
     __syncthreads();
-    for (int i = tid; i < C * P; i += 256) {
+    for (int i = tid; i < C * P; i += blockDim.x) {
       const int r = i / P, p = i % P;
       const float dd = ddbx_s[r * LDPF + p];
       const int64_t gi = ix.xp(b, (int64_t)n * C + r, h) + p;
@@ -492,10 +508,10 @@ __global__ void __launch_bounds__(256) ssd_bwd_chunk_kernel(
     __syncthreads();
   }
   // partial dB, dC of this head group: (G, B, L, N)
-  const int m0 = 16 * mt, n0 = 64 * nh;
+  const int m0 = 16 * mt, n0 = 32 * nq;
   const int64_t goff = (int64_t)blockIdx.z * ix.L * N * gridDim.y;
-  for_acc<8>(dBa, m0, n0, [&](int r, int c, float& v) { dB[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
-  for_acc<8>(dCa, m0, n0, [&](int r, int c, float& v) { dC[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
+  for_acc<4>(dBa, m0, n0, [&](int r, int c, float& v) { dB[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
+  for_acc<4>(dCa, m0, n0, [&](int r, int c, float& v) { dC[goff + ix.bn(b, (int64_t)n * C + r) + c] = v; });
 }
 
 // out[i] = sum_g part[g * n + i]
@@ -531,11 +547,11 @@ void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, 
   }
   const int NC = L / C;
   const int G = head_groups(H);
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
                                                                  (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, s0, s_final);
   if (y)
-    ssd_out_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+    ssd_out_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A,
                                                                (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
                                                                (bf16*)y);
 }
@@ -556,13 +572,13 @@ void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, 
   }
   const int NC = L / C;
   const int G = head_groups(H);
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
                                                                  (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  ssd_dstate_kernel<<<dim3(NC, B, G), 256, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
+  ssd_dstate_kernel<<<dim3(NC, B, G), 512, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
                                                          g_buf);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(g_buf, cuml, H, NC, 1, nullptr, nullptr);
-  ssd_bwd_chunk_kernel<<<dim3(NC, B, G), 256, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
+  ssd_bwd_chunk_kernel<<<dim3(NC, B, G), 512, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
                                                              (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
                                                              (bf16*)dx, (bf16*)ddt, dB_part, dC_part, dA);
   const int64_t n = (int64_t)B * L * N;
@@ -616,10 +632,10 @@ extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A
   float* state_buf = static_cast<float*>(base);
   float* cuml = state_buf + chunk_heads * (unsigned long long)(P * N);
   const int G = head_groups(H);
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
+  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
                                                                      (const bf16*)Bm, L, H, state_buf, cuml);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, stream>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  ssd_out_fwd_kernel<<<dim3(NC, B, G), 256, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
+  ssd_out_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
                                                                  (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
                                                                  (bf16*)y);
   return cudaGetLastError() == cudaSuccess ? AHB_NOALLOC_OK : AHB_NOALLOC_ELAUNCH;
