@@ -489,19 +489,29 @@ std::vector<torch::Tensor> optim_make_table(torch::Tensor table, torch::Tensor g
   return {host.to(dev), cs.to(dev)};
 }
 
+// peer tables: int64 CUDA tensors of device pointers, one per rank (own rank included)
+static std::pair<void* const*, int> peer_table(const c10::optional<torch::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return {nullptr, 0};
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kLong && t->is_contiguous(), "peer table: int64 CUDA tensor");
+  return {reinterpret_cast<void* const*>(t->data_ptr<int64_t>()), (int)t->numel()};
+}
+
 void optim_prepare(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torch::Tensor grad_shard,
-                   torch::Tensor master, double inv, torch::Tensor red, torch::Tensor flags) {
+                   torch::Tensor master, double inv, torch::Tensor red, torch::Tensor flags,
+                   c10::optional<torch::Tensor> grad_peers, int64_t lo) {
   TORCH_CHECK(red.scalar_type() == at::kDouble && flags.scalar_type() == at::kInt, "optim_prepare: red f64, flags i32");
+  auto pt = peer_table(grad_peers);
   ahb_optim_prepare(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
                     (int)(cstart.numel() - 1), (int)nblocks, grad_shard.data_ptr<float>(), master.data_ptr<float>(),
-                    (float)inv, red.data_ptr<double>(), flags.data_ptr<int>(), cur_stream());
+                    (float)inv, red.data_ptr<double>(), flags.data_ptr<int>(),
+                    reinterpret_cast<const float* const*>(pt.first), pt.second, lo, cur_stream());
   check_launch("ahb_optim_prepare");
 }
 
 void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torch::Tensor master, torch::Tensor m,
                  torch::Tensor v, torch::Tensor grad_shard, torch::Tensor coef, torch::Tensor compute,
                  c10::optional<torch::Tensor> frac, std::vector<double> lr, std::vector<double> wd, double bc1,
-                 double bc2) {
+                 double bc2, c10::optional<torch::Tensor> compute_peers) {
   TORCH_CHECK(lr.size() == 5 && wd.size() == 5, "optim_apply: 5 labels");
   AhbOptimArgs a;
   for (int i = 0; i < 5; ++i) { a.lr[i] = (float)lr[i]; a.wd[i] = (float)wd[i]; }
@@ -518,8 +528,55 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
   ahb_optim_apply(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
                   (int)(cstart.numel() - 1), (int)nblocks, master.data_ptr<float>(), m.data_ptr<float>(),
                   v.data_ptr<float>(), grad_shard.data_ptr<float>(), coef.data_ptr<float>(), compute.data_ptr(), fp, fe,
-                  a, cur_stream());
+                  a, peer_table(compute_peers).first, peer_table(compute_peers).second, cur_stream());
   check_launch("ahb_optim_apply");
+}
+
+// ------------------------------------------------------------ NVLink peer memory (CUDA IPC)
+int64_t ipc_alloc(int64_t nbytes) {
+  void* p = nullptr;
+  TORCH_CHECK(ahb_ipc_alloc(nbytes, &p) == 0, "ipc_alloc failed (", nbytes, " bytes)");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_free(int64_t ptr) { TORCH_CHECK(ahb_ipc_free(reinterpret_cast<void*>(ptr)) == 0, "ipc_free failed"); }
+torch::Tensor ipc_handle(int64_t ptr) {
+  auto h = torch::empty({64}, torch::kUInt8);
+  TORCH_CHECK(ahb_ipc_handle(reinterpret_cast<void*>(ptr), h.data_ptr<uint8_t>()) == 0, "cudaIpcGetMemHandle failed");
+  return h;
+}
+int64_t ipc_open(torch::Tensor handle) {
+  TORCH_CHECK(handle.device().is_cpu() && handle.numel() == 64 && handle.scalar_type() == at::kByte, "ipc_open: 64 bytes");
+  void* p = nullptr;
+  TORCH_CHECK(ahb_ipc_open(handle.contiguous().data_ptr<uint8_t>(), &p) == 0, "cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_close(int64_t ptr) { TORCH_CHECK(ahb_ipc_close(reinterpret_cast<void*>(ptr)) == 0, "ipc_close failed"); }
+// a tensor view of raw device memory; the caller keeps the allocation alive
+torch::Tensor ipc_tensor(int64_t ptr, int64_t numel, torch::Tensor like) {
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, like.options());
+}
+void symm_barrier(torch::Tensor pads, int64_t rank, int64_t epoch, torch::Tensor err, double timeout_s) {
+  TORCH_CHECK(pads.is_cuda() && pads.scalar_type() == at::kLong && pads.numel() <= 32, "symm_barrier: <= 32 ranks");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "symm_barrier: err int32");
+  ahb_symm_barrier(reinterpret_cast<uint32_t* const*>(pads.data_ptr<int64_t>()), (int)rank, (int)pads.numel(),
+                   (uint32_t)epoch, err.data_ptr<int>(), timeout_s, cur_stream());
+  check_launch("ahb_symm_barrier");
+}
+void reduce_scatter_f32(torch::Tensor peers, int64_t lo, torch::Tensor out) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() % 4 == 0 &&
+                  lo % 4 == 0, "reduce_scatter_f32: fp32 out, 16-byte aligned slice");
+  auto pt = peer_table(peers);
+  ahb_reduce_scatter_f32(reinterpret_cast<const float* const*>(pt.first), pt.second, lo, out.numel(),
+                         out.data_ptr<float>(), cur_stream());
+  check_launch("ahb_reduce_scatter_f32");
+}
+void copy_out(torch::Tensor src, torch::Tensor peers, int64_t off_bytes) {
+  const int64_t nb = src.numel() * src.element_size();
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous() && nb % 16 == 0 && off_bytes % 16 == 0,
+              "copy_out: 16-byte aligned slice");
+  auto pt = peer_table(peers);
+  ahb_copy_out(src.data_ptr(), pt.first, pt.second, off_bytes, nb, cur_stream());
+  check_launch("ahb_copy_out");
 }
 
 // ------------------------------------------------------------ fused LM head + cross entropy
@@ -596,4 +653,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fused_bwd", &ce_fused_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_free", &ipc_free);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_tensor", &ipc_tensor);
+  m.def("symm_barrier", &symm_barrier);
+  m.def("reduce_scatter_f32", &reduce_scatter_f32);
+  m.def("copy_out", &copy_out);
 }

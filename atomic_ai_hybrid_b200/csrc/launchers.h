@@ -109,10 +109,24 @@ struct AhbOptimArgs {
 };
 int ahb_optim_chunk();
 void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
-                       const float* master, float inv, double* red, int* flags, cudaStream_t st);
+                       const float* master, float inv, double* red, int* flags, const float* const* gpeers,
+                       int npeers, int64_t lo, cudaStream_t st);
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
                      const float* grad, const float* coef, void* compute, const float* frac, int fracE,
-                     AhbOptimArgs args, cudaStream_t st);
+                     AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st);
+
+// comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
+int ahb_ipc_alloc(int64_t nbytes, void** ptr);
+int ahb_ipc_free(void* ptr);
+int ahb_ipc_handle(void* ptr, void* handle64);
+int ahb_ipc_open(const void* handle64, void** ptr);
+int ahb_ipc_close(void* ptr);
+void ahb_symm_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t epoch, int* err, double timeout_s,
+                      cudaStream_t st);
+void ahb_reduce_scatter_f32(const float* const* peers_dev, int world, int64_t lo, int64_t n, float* out,
+                            cudaStream_t st);
+void ahb_copy_out(const void* src, void* const* peers_dev, int world, int64_t off_bytes, int64_t nbytes,
+                  cudaStream_t st);
 
 // ce.cu: label-smoothed cross entropy over bf16 logits rows, gradient written in place
 void ahb_ce_rows(void* logits, const int64_t* labels, int64_t R, int V, float ls, float* loss_sum, float* count,

@@ -10,6 +10,14 @@
 //   fp32 master plus the compute copy (bf16 or fp32) in the same pass.
 // Blocks cover CHUNK elements of one segment; a block finds its segment by
 // binary search over the per-segment chunk prefix.
+//
+// Data parallelism over NVLink peer memory: given the table of every rank's
+// full-size gradient buffer, prepare sums the owned slice over the ranks while
+// it reads it (the reduce-scatter fused into the first pass; the sum is written
+// to the local slice for apply), and given the table of every rank's compute
+// buffer, apply stores each updated weight into all of them (the all-gather
+// fused into the update).  Plain loads/stores only; the caller orders the
+// phases with peer barriers.
 #include "common.cuh"
 #include "launchers.h"
 
@@ -34,7 +42,9 @@ __global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo
                                                                 const int* __restrict__ cstart, int S,
                                                                 float* __restrict__ grad,
                                                                 const float* __restrict__ master, float inv,
-                                                                double* __restrict__ red, int* __restrict__ flags) {
+                                                                double* __restrict__ red, int* __restrict__ flags,
+                                                                const float* const* __restrict__ gpeers, int npeers,
+                                                                int64_t lo) {
   __shared__ float sh[THREADS / 32];
   const int b = blockIdx.x;
   const int s = find_seg(cstart, S, b);
@@ -48,7 +58,14 @@ __global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo
   for (int i = threadIdx.x; i < n; i += THREADS) {
     const int64_t idx = sg.off + base + i;
     if (rg) {
-      const float a = grad[idx] * inv;
+      float a;
+      if (npeers > 0) {
+        a = 0.f;
+        for (int r = 0; r < npeers; ++r) a += gpeers[r][lo + idx];
+        a *= inv;
+      } else {
+        a = grad[idx] * inv;
+      }
       sa += a * a;
       const bool fin = isfinite(a);
       nonfin |= !fin;
@@ -77,7 +94,8 @@ __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* 
                                                               const float* __restrict__ coef_p,
                                                               uint16_t* __restrict__ compute,
                                                               const float* __restrict__ frac, int fracE,
-                                                              AhbOptimArgs a) {
+                                                              AhbOptimArgs a, uint16_t* const* __restrict__ cpeers,
+                                                              int npeers) {
   const int b = blockIdx.x;
   const int s = find_seg(cstart, S, b);
   const AhbSegInfo sg = segs[s];
@@ -118,27 +136,37 @@ __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* 
       p += 0.02f * (f > 1.f / (float)sg.len ? -1.f : 1.f);
     }
     master[idx] = p;
-    if (sg.flags & AHB_SEG_COMPUTE_FP32)
+    if (npeers > 0) {
+      if (sg.flags & AHB_SEG_COMPUTE_FP32)
+        for (int r = 0; r < npeers; ++r) reinterpret_cast<float*>(cpeers[r] + sg.coff)[j] = p;
+      else {
+        const bf16 pb = __float2bfloat16_rn(p);
+        for (int r = 0; r < npeers; ++r) reinterpret_cast<bf16*>(cpeers[r] + sg.coff)[j] = pb;
+      }
+    } else if (sg.flags & AHB_SEG_COMPUTE_FP32) {
       reinterpret_cast<float*>(compute + sg.coff)[j] = p;
-    else
+    } else {
       reinterpret_cast<bf16*>(compute + sg.coff)[j] = __float2bfloat16_rn(p);
+    }
   }
 }
 
 }  // namespace
 
 void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
-                       const float* master, float inv, double* red, int* flags, cudaStream_t st) {
+                       const float* master, float inv, double* red, int* flags, const float* const* gpeers,
+                       int npeers, int64_t lo, cudaStream_t st) {
   if (nblocks <= 0) return;
-  optim_prepare_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, grad, master, inv, red, flags);
+  optim_prepare_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, grad, master, inv, red, flags, gpeers, npeers,
+                                                    lo);
 }
 
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
                      const float* grad, const float* coef, void* compute, const float* frac, int fracE,
-                     AhbOptimArgs args, cudaStream_t st) {
+                     AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st) {
   if (nblocks <= 0) return;
   optim_apply_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, master, m, v, grad, coef, (uint16_t*)compute,
-                                                  frac, fracE, args);
+                                                  frac, fracE, args, (uint16_t* const*)cpeers, npeers);
 }
 
 int ahb_optim_chunk() { return CHUNK; }

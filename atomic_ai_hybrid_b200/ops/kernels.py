@@ -356,20 +356,25 @@ def optim_prepare(opt, inv, red):
     st = opt.store
     redd = torch.zeros(2, dtype=torch.float64, device=st.device)
     flags = torch.zeros(8, dtype=torch.int32, device=st.device)
-    ext().optim_prepare(opt._segs, opt._cstart, opt._nblocks, st.grad[st.lo:st.hi], st.master, float(inv), redd, flags)
+    peers = getattr(opt, "peers", None)
+    ext().optim_prepare(opt._segs, opt._cstart, opt._nblocks, st.grad[st.lo:st.hi], st.master, float(inv), redd, flags,
+                        peers[0] if peers else None, st.lo)
     red[0:2] = redd.float()
     red[2:] = flags.float()
 
 
 def optim_apply(opt, lrs, coef, frac):
-    """Per-label update + clip + hooks + compute-copy write, one kernel."""
+    """Per-label update + clip + hooks + compute-copy write, one kernel.  With
+    ``opt.peers`` set, prepare sums the owned gradient slice over the peers'
+    buffers and apply writes the compute copies of every peer."""
     st = opt.store
+    peers = getattr(opt, "peers", None)
     t = opt.count + 1
     lr = [float(lrs[k]) for k in _ORDER]
     wd = [_WD[k] for k in _ORDER]
     ext().optim_apply(opt._segs, opt._cstart, opt._nblocks, st.master, opt.m, opt.v, st.grad[st.lo:st.hi],
                       coef.reshape(1).float().contiguous(), st.compute, frac, lr, wd, 1.0 - 0.9 ** t,
-                      1.0 - 0.999 ** t)
+                      1.0 - 0.999 ** t, peers[1] if peers else None)
 
 
 _ = math

@@ -60,6 +60,15 @@ class HybridOptimizer:
         self.v = torch.zeros(store.shard, dtype=torch.float32, device=dev)
         self.owned = store.owned()
         self.group_idx = {g: i for i, g in enumerate(DIAG_GROUPS)}
+        # (gradient peer table, compute peer table): set by a peer-memory shard comm
+        self.peers = None
+
+    def uses_kernels(self) -> bool:
+        gbuf = self.store.grad
+        if not ops.use_cuda(gbuf):
+            return False
+        from ..ops import kernels as K
+        return hasattr(K, "optim_apply")
 
     # -------------------------------------------------------------- lr values
     def lrs(self, step: int) -> Dict[str, float]:
@@ -83,11 +92,9 @@ class HybridOptimizer:
         red = torch.zeros(3 + ng, dtype=torch.float32, device=dev)
         gbuf = st.grad[st.lo:st.hi]
         inv = 1.0 / float(n_accum)
-        use_k = ops.use_cuda(gbuf)
+        use_k = self.uses_kernels()
         if use_k:
             from ..ops import kernels as K
-            use_k = hasattr(K, "optim_apply")
-        if use_k:
             K.optim_prepare(self, inv, red)
         else:
             for s in self.owned:

@@ -108,6 +108,19 @@ class FlatParamStore:
             self.compute_view(s).copy_(src.view(s.shape))
             self._rebind(s)
 
+    def adopt_buffers(self, grad: torch.Tensor, compute: torch.Tensor) -> None:
+        """Move the gradient and compute buffers into caller-provided memory (e.g.
+        peer-mapped allocations) and rebind every parameter to it."""
+        assert grad.shape == self.grad.shape and compute.shape == self.compute.shape
+        grad.copy_(self.grad)
+        compute.copy_(self.compute)
+        self.grad, self.compute = grad, compute
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+        for s in self.segs:
+            self._rebind(s)
+
     # ------------------------------------------------------------------ views
     def compute_view(self, s: Seg) -> torch.Tensor:
         raw = self.compute[s.coff:s.coff + s.cunits]

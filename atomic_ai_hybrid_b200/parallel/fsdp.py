@@ -13,12 +13,15 @@ Two implementations:
 
 * ``NcclShardComm`` -- ``reduce_scatter_tensor`` / ``all_gather_into_tensor``
   (NCCL on GPUs; emulated with ``all_reduce``/``all_gather`` on gloo for CPU tests).
-* ``SymmShardComm`` (``parallel.symm``) -- one sm_100a kernel pulls the peers'
-  gradient slices over NVLink and sums them (P2P loads), and a second pushes the
-  updated shard into every peer's compute buffer (P2P stores).
+* ``SymmShardComm`` (``parallel.symm``) -- gradient and compute buffers in
+  CUDA-IPC peer memory; the optimizer's prepare kernel sums the owned gradient
+  slice straight from the peers' buffers over NVLink and its apply kernel stores
+  the updated weights into every peer's compute buffer.  Chosen by default on a
+  single node with NCCL; ``AHB_SHARD_COMM=nccl`` forces the NCCL path.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -54,13 +57,14 @@ class NcclShardComm:
 
 
 def make_shard_comm(store, group=None, kind: str = "auto"):
+    kind = os.environ.get("AHB_SHARD_COMM", kind)
     backend = dist.get_backend(group)
     if kind in ("auto", "symm") and backend == "nccl" and store.device.type == "cuda":
         try:
             from .symm import SymmShardComm
             return SymmShardComm(store, group)
-        except Exception as e:  # symmetric memory unavailable: say so, use NCCL
+        except Exception as e:  # peer memory unavailable: say so, use NCCL
             if kind == "symm":
                 raise
-            print(f"[fsdp] symmetric-memory path unavailable ({e!r}); using NCCL collectives")
+            print(f"[fsdp] peer-memory path unavailable ({e!r}); using NCCL collectives")
     return NcclShardComm(store, group)

@@ -50,6 +50,12 @@ class Trainer:
             self.comm = make_shard_comm(self.store, group, comm)
         self.opt = HybridOptimizer(self.store, total_steps, reduce_fn=self._allreduce_sum,
                                    skip_nonfinite=skip_nonfinite)
+        # peer-memory comm + fused optimizer kernels: reduce-scatter and all-gather
+        # happen inside the optimizer's prepare / apply kernels
+        self.fused_comm = bool(self.comm is not None and getattr(self.comm, "fused", False)
+                               and self.opt.uses_kernels())
+        if self.fused_comm:
+            self.opt.peers = (self.comm.grad_peers, self.comm.compute_peers)
         self.ce_chunk_size = ce_chunk_size
         self.collinearity_coef = collinearity_coef
         self.global_step = 0
@@ -137,12 +143,16 @@ class Trainer:
             if self.world > 1:
                 dist.all_reduce(frac, group=self.group)
                 frac = frac / self.world
-        if self.comm is not None:
+        if self.fused_comm:
+            self.comm.begin_step()
+        elif self.comm is not None:
             self.comm.reduce_scatter_grads()
         # every rank's loss is the mean over its own tokens, and the reduction sums the
         # ranks: dividing by n_accum * world gives the gradient of the global-batch mean
         out = self.opt.step(n * self.world, frac)
-        if self.comm is not None:
+        if self.fused_comm:
+            self.comm.end_step()
+        elif self.comm is not None:
             self.comm.all_gather_params()
         out["loss"] = self._loss_sum / max(self._n_micro, 1)
         self.reset_accumulators()
@@ -167,6 +177,8 @@ class Trainer:
             self._graph_key = None
             self._s_loss = self._s_info = None
             torch.cuda.synchronize()
+        if self.comm is not None and hasattr(self.comm, "close"):
+            self.comm.close()
 
     @torch.no_grad()
     def eval_loss(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:

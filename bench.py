@@ -99,7 +99,7 @@ class ClockSampler:
 
 def reference_arm(args, rank):
     why = ("reference project (JAX/Flax/Optax/Orbax + Pallas-TPU kernels) is not installable offline: "
-           "/root/reference has no setup.py/pyproject.toml and jax is not in the image")
+           "the reference source tree has no setup.py/pyproject.toml and jax is not in the image")
     try:
         sys.path.insert(0, os.path.join(HERE, "baseline", "_ref"))
         import jax  # noqa: F401
@@ -146,8 +146,9 @@ def main():
     model = model.to(dev)
     nparams = count_params(model)
     use_graph = args.impl == "cuda" and not args.no_graph
+    # the eager baseline keeps NCCL collectives; the CUDA path uses the peer-memory fused step
     trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev,
-                      cuda_graph=use_graph)
+                      cuda_graph=use_graph, comm="nccl" if args.impl == "eager" else "auto")
     trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
 
     S, mb = args.seq_len, args.micro_batch
@@ -233,6 +234,10 @@ def main():
             "config": {"model": args.model, "global_batch": seqs * world, "seq_len": S,
                        "micro_batch": mb, "grad_accum": n_micro, "parallelism": f"dp{world}" if world > 1 else "dp1",
                        "sharding": "param/optimizer owner-sharded, bf16 weights resident",
+                       "collectives": ("none" if world == 1 else
+                                       "NVLink peer memory: reduce-scatter fused into the optimizer's first pass, "
+                                       "all-gather fused into its update" if trainer.fused_comm else
+                                       type(trainer.comm).__name__),
                        "optimizer": args.optimizer, "params_total": nparams["total"],
                        "num_layers": cfg.num_layers,
                        "l2": "inputs larger than L2 (11+ GB of weights streamed per micro-step)"},
