@@ -189,34 +189,23 @@ std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tens
   return {o};
 }
 
-std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                   torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale) {
+// Backward from the chunk intermediates of the forward (wt, qg, kg, aqk, gcl, A and the
+// per-chunk states hs / vn): inter-chunk reverse scan, then the chunk-local backward.
+static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                                               const torch::Tensor& g, const torch::Tensor& bg,
+                                               const torch::Tensor& wg, const torch::Tensor& doc, float sc,
+                                               torch::Tensor wt, torch::Tensor qg, torch::Tensor kg,
+                                               const torch::Tensor& aqk, const torch::Tensor& gcl,
+                                               const torch::Tensor& A, torch::Tensor hs, torch::Tensor vn) {
   auto s = gdn_shapes(q);
-  auto doc = dout.to(at::kBFloat16).contiguous();
-  auto bf = q.options();
   auto f32 = q.options().dtype(at::kFloat);
   auto st = cur_stream();
-  const float sc = (float)scale;
-  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
-  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
-  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
-  auto A = torch::empty_like(aqk);
-  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
-  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), sc,
-                    s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), A.data_ptr<float>(), st);
-  check_launch("ahb_gdn_intra_fwd");
-  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
-  auto vn = torch::empty_like(wt);
-  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, nullptr, nullptr, hs.data_ptr(), vn.data_ptr(),
-                    st);
   auto dhs = torch::empty_like(hs);
   auto dvn = torch::empty_like(wt);
   ahb_gdn_inter_bwd(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(), gcl.data_ptr<float>(),
                     doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr, st);
   check_launch("ahb_gdn_inter_bwd");
-  u = torch::Tensor(); qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor();
+  qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor();
   auto dq_p = torch::empty({s.B, s.H, s.NC, 64, 128}, f32);
   auto dk_p = torch::empty_like(dq_p), dgc_p = torch::empty_like(dq_p), dwt = torch::empty_like(dq_p);
   auto dgcl = torch::empty_like(gcl);
@@ -244,6 +233,72 @@ std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tens
   return {dq, dk, dv, dg, db, dw};
 }
 
+// Forward for training: also returns the chunk intermediates the backward needs
+// {o, wt, qg, kg, aqk, gcl, A, hs, vn}, so nothing is recomputed there.
+std::vector<torch::Tensor> gdn_fwd_train(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                         torch::Tensor bg, torch::Tensor wg, double scale) {
+  for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
+  check_gdn(g, at::kFloat, "g");
+  auto s = gdn_shapes(q);
+  auto bf = q.options();
+  auto f32 = q.options().dtype(at::kFloat);
+  auto st = cur_stream();
+  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
+  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
+  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  auto A = torch::empty_like(aqk);
+  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
+  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
+                    (float)scale, s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(),
+                    aqk.data_ptr<float>(), gcl.data_ptr<float>(), A.data_ptr<float>(), st);
+  check_launch("ahb_gdn_intra_fwd");
+  auto o = torch::empty_like(q);
+  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
+  auto vn = torch::empty_like(wt);
+  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(), nullptr,
+                    hs.data_ptr(), vn.data_ptr(), st);
+  check_launch("ahb_gdn_inter_fwd");
+  return {o, wt, qg, kg, aqk, gcl, A, hs, vn};
+}
+
+std::vector<torch::Tensor> gdn_bwd_saved(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                         torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale,
+                                         std::vector<torch::Tensor> saved) {
+  TORCH_CHECK(saved.size() == 8, "gdn_bwd_saved: expects {wt, qg, kg, aqk, gcl, A, hs, vn}");
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  return gdn_bwd_core(q, k, v, g, bg, wg, doc, (float)scale, saved[0], saved[1], saved[2], saved[3], saved[4],
+                      saved[5], saved[6], saved[7]);
+}
+
+// Backward that recomputes the forward's chunk intermediates (memory-lean path).
+std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+                                   torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale) {
+  auto s = gdn_shapes(q);
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  auto bf = q.options();
+  auto f32 = q.options().dtype(at::kFloat);
+  auto st = cur_stream();
+  const float sc = (float)scale;
+  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
+  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
+  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  auto A = torch::empty_like(aqk);
+  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
+  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), sc,
+                    s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), A.data_ptr<float>(), st);
+  check_launch("ahb_gdn_intra_fwd");
+  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
+  auto vn = torch::empty_like(wt);
+  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
+                    gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, nullptr, nullptr, hs.data_ptr(), vn.data_ptr(),
+                    st);
+  check_launch("ahb_gdn_inter_fwd");
+  u = torch::Tensor();
+  return gdn_bwd_core(q, k, v, g, bg, wg, doc, sc, wt, qg, kg, aqk, gcl, A, hs, vn);
+}
+
 // ------------------------------------------------------------ Mamba2 SSD
 void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Tensor& A, const torch::Tensor& Bm,
                const torch::Tensor& Cm) {
@@ -258,7 +313,8 @@ void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Ten
               "ssd: B, C must be (B,L,128)");
 }
 
-torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm, torch::Tensor Cm) {
+static std::vector<torch::Tensor> ssd_fwd_impl(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
+                                               torch::Tensor Cm) {
   check_ssd(x, dt, A, Bm, Cm);
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
   auto f32 = x.options().dtype(at::kFloat);
@@ -268,18 +324,33 @@ torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch:
   ahb_ssd_fwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
               sbuf.data_ptr<float>(), cuml.data_ptr<float>(), nullptr, nullptr, y.data_ptr(), cur_stream());
   check_launch("ahb_ssd_fwd");
-  return y;
+  return {y, sbuf, cuml};
+}
+
+torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm, torch::Tensor Cm) {
+  return ssd_fwd_impl(x, dt, A, Bm, Cm)[0];
+}
+
+// Forward for training: {y, chunk states (scanned), chunk decay cumsums}; ssd_bwd takes them back.
+std::vector<torch::Tensor> ssd_fwd_train(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
+                                         torch::Tensor Cm) {
+  return ssd_fwd_impl(x, dt, A, Bm, Cm);
 }
 
 std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
-                                   torch::Tensor Cm, torch::Tensor dy) {
+                                   torch::Tensor Cm, torch::Tensor dy, c10::optional<torch::Tensor> states,
+                                   c10::optional<torch::Tensor> cumsums) {
   check_ssd(x, dt, A, Bm, Cm);
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
   auto dyc = dy.to(at::kBFloat16).contiguous();
   auto f32 = x.options().dtype(at::kFloat);
-  auto sbuf = torch::empty({B, H, NC, 64, 128}, f32);
-  auto gbuf = torch::empty_like(sbuf);
-  auto cuml = torch::empty({B, H, NC, 64}, f32);
+  const bool ready = states.has_value() && states->defined() && cumsums.has_value() && cumsums->defined();
+  auto sbuf = ready ? *states : torch::empty({B, H, NC, 64, 128}, f32);
+  auto gbuf = torch::empty({B, H, NC, 64, 128}, f32);
+  auto cuml = ready ? *cumsums : torch::empty({B, H, NC, 64}, f32);
+  if (ready)
+    TORCH_CHECK(sbuf.is_contiguous() && sbuf.numel() == (int64_t)B * H * NC * 64 * 128 && cuml.numel() ==
+                    (int64_t)B * H * NC * 64, "ssd_bwd: saved states do not match");
   auto dx = torch::empty_like(x), ddt = torch::empty_like(x);
   auto dB = torch::empty(Bm.sizes(), f32), dC = torch::empty(Cm.sizes(), f32);
   auto dA = torch::zeros({H}, f32);
@@ -288,7 +359,7 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
   ahb_ssd_bwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B, L,
               H, sbuf.data_ptr<float>(), cuml.data_ptr<float>(), gbuf.data_ptr<float>(), dx.data_ptr(),
               ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(),
-              dCp.data_ptr<float>(), cur_stream());
+              dCp.data_ptr<float>(), ready ? 1 : 0, cur_stream());
   check_launch("ahb_ssd_bwd");
   return {dx, ddt, dA, dB, dC};
 }
@@ -532,6 +603,186 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
   check_launch("ahb_optim_apply");
 }
 
+// ------------------------------------------------------------ fused layer glue (fused_norm.cu)
+static void check_rows(const torch::Tensor& t, int64_t D, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.size(-1) == D, n,
+              ": contiguous bf16 CUDA tensor with last dim ", D);
+}
+
+static void add_scale_grad(const torch::Tensor& part, const c10::optional<torch::Tensor>& acc, int64_t D) {
+  if (!acc.has_value() || !acc->defined()) return;
+  check_acc(*acc, D, "dscale_acc");
+  ahb_colsum_add(part.data_ptr<float>(), (int)part.size(0), (int)D, acc->data_ptr<float>(), cur_stream());
+  check_launch("ahb_colsum_add");
+}
+
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor delta, torch::Tensor scale, double clip,
+                                           double eps) {
+  const int64_t D = x.size(-1);
+  TORCH_CHECK(ahb_row_supported((int)D), "add_rmsnorm: D % 256 != 0");
+  check_rows(x, D, "x");
+  check_rows(delta, D, "delta");
+  TORCH_CHECK(delta.numel() == x.numel(), "add_rmsnorm: shape mismatch");
+  const int64_t M = x.numel() / D;
+  auto sc = scale.to(at::kFloat).contiguous();
+  auto xo = torch::empty_like(x), y = torch::empty_like(x);
+  auto r = torch::empty({M}, x.options().dtype(at::kFloat));
+  ahb_add_rmsnorm_fwd(x.data_ptr(), delta.data_ptr(), sc.data_ptr<float>(), xo.data_ptr(), y.data_ptr(),
+                      r.data_ptr<float>(), M, (int)D, (float)clip, (float)eps, cur_stream());
+  check_launch("ahb_add_rmsnorm_fwd");
+  return {xo, y, r};
+}
+
+std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, c10::optional<torch::Tensor> gres, torch::Tensor xo,
+                                           torch::Tensor scale, torch::Tensor rstd, double clip, bool want_ddelta,
+                                           c10::optional<torch::Tensor> dscale_acc) {
+  const int64_t D = xo.size(-1);
+  check_rows(xo, D, "xo");
+  auto dyc = dy.contiguous();
+  check_rows(dyc, D, "dy");
+  torch::Tensor gr;
+  if (gres.has_value() && gres->defined()) {
+    gr = gres->contiguous();
+    check_rows(gr, D, "gres");
+  }
+  const int64_t M = xo.numel() / D;
+  auto sc = scale.to(at::kFloat).contiguous();
+  auto dx = torch::empty_like(xo);
+  torch::Tensor dd = want_ddelta ? torch::empty_like(xo) : torch::Tensor();
+  const bool wacc = dscale_acc.has_value() && dscale_acc->defined();
+  torch::Tensor part;
+  if (wacc) part = torch::empty({(int64_t)ahb_row_bwd_blocks(M), D}, xo.options().dtype(at::kFloat));
+  ahb_add_rmsnorm_bwd(dyc.data_ptr(), gr.defined() ? gr.data_ptr() : nullptr, xo.data_ptr(), sc.data_ptr<float>(),
+                      rstd.data_ptr<float>(), dx.data_ptr(), dd.defined() ? dd.data_ptr() : nullptr,
+                      wacc ? part.data_ptr<float>() : nullptr, M, (int)D, (float)clip, cur_stream());
+  check_launch("ahb_add_rmsnorm_bwd");
+  if (wacc) add_scale_grad(part, dscale_acc, D);
+  return {dx, dd.defined() ? dd : dx};
+}
+
+std::vector<torch::Tensor> norm_gate_fwd(torch::Tensor x, torch::Tensor z, torch::Tensor scale, double eps,
+                                         double zclip, double oclip) {
+  const int64_t D = x.size(-1);
+  TORCH_CHECK(ahb_row_supported((int)D), "norm_gate: D % 256 != 0");
+  check_rows(x, D, "x");
+  TORCH_CHECK(z.is_cuda() && z.scalar_type() == at::kBFloat16 && z.stride(-1) == 1 && z.size(-1) == D &&
+                  z.numel() == x.numel() && z.dim() >= 2, "norm_gate: z bf16 with unit channel stride");
+  const int64_t zs = z.stride(-2);
+  for (int i = 0; i < z.dim() - 2; ++i)
+    TORCH_CHECK(z.stride(i) == z.size(i + 1) * z.stride(i + 1), "norm_gate: z rows must be evenly strided");
+  TORCH_CHECK(zs % 8 == 0, "norm_gate: z row stride must be a multiple of 8");
+  const int64_t M = x.numel() / D;
+  auto sc = scale.to(at::kFloat).contiguous();
+  auto y = torch::empty_like(x);
+  auto r = torch::empty({M}, x.options().dtype(at::kFloat));
+  ahb_norm_gate_fwd(x.data_ptr(), z.data_ptr(), zs, sc.data_ptr<float>(), y.data_ptr(), r.data_ptr<float>(), M,
+                    (int)D, (float)eps, (float)zclip, (float)oclip, cur_stream());
+  check_launch("ahb_norm_gate_fwd");
+  return {y, r};
+}
+
+std::vector<torch::Tensor> norm_gate_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor z, torch::Tensor scale,
+                                         torch::Tensor rstd, double zclip, double oclip,
+                                         c10::optional<torch::Tensor> dscale_acc) {
+  const int64_t D = x.size(-1);
+  check_rows(x, D, "x");
+  auto dyc = dy.contiguous();
+  check_rows(dyc, D, "dy");
+  const int64_t zs = z.stride(-2);
+  const int64_t M = x.numel() / D;
+  auto sc = scale.to(at::kFloat).contiguous();
+  auto dx = torch::empty_like(x);
+  auto dz = torch::empty_like(x);
+  const bool wacc = dscale_acc.has_value() && dscale_acc->defined();
+  torch::Tensor part;
+  if (wacc) part = torch::empty({(int64_t)ahb_row_bwd_blocks(M), D}, x.options().dtype(at::kFloat));
+  ahb_norm_gate_bwd(dyc.data_ptr(), x.data_ptr(), z.data_ptr(), zs, sc.data_ptr<float>(), rstd.data_ptr<float>(),
+                    dx.data_ptr(), dz.data_ptr(), wacc ? part.data_ptr<float>() : nullptr, M, (int)D, (float)zclip,
+                    (float)oclip, cur_stream());
+  check_launch("ahb_norm_gate_bwd");
+  if (wacc) add_scale_grad(part, dscale_acc, D);
+  return {dx, dz};
+}
+
+std::vector<torch::Tensor> gdn_gates_fwd(torch::Tensor bp, torch::Tensor wp, torch::Tensor fp, torch::Tensor decay_a,
+                                         int64_t Dh) {
+  const int64_t d = bp.size(-1);
+  for (auto* t : {&bp, &wp, &fp}) check_rows(*t, d, "gate input");
+  TORCH_CHECK(wp.numel() == bp.numel() && fp.numel() == bp.numel() && d % Dh == 0 && Dh % 8 == 0,
+              "gdn_gates: shapes");
+  auto a = decay_a.to(at::kFloat).contiguous();
+  TORCH_CHECK(a.numel() == d / Dh, "gdn_gates: decay_a must have d/Dh entries");
+  auto bg = torch::empty_like(bp), wg = torch::empty_like(bp);
+  auto g = torch::empty(bp.sizes(), bp.options().dtype(at::kFloat));
+  ahb_gdn_gates_fwd(bp.data_ptr(), wp.data_ptr(), fp.data_ptr(), a.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
+                    g.data_ptr<float>(), bp.numel(), (int)d, (int)Dh, cur_stream());
+  check_launch("ahb_gdn_gates_fwd");
+  return {bg, wg, g};
+}
+
+std::vector<torch::Tensor> gdn_gates_bwd(torch::Tensor dbg, torch::Tensor dwg, torch::Tensor dg, torch::Tensor bg,
+                                         torch::Tensor wg, torch::Tensor fp, torch::Tensor decay_a, int64_t Dh,
+                                         c10::optional<torch::Tensor> da_acc) {
+  const int64_t d = bg.size(-1);
+  auto dbc = dbg.to(at::kBFloat16).contiguous(), dwc = dwg.to(at::kBFloat16).contiguous();
+  auto dgc = dg.to(at::kFloat).contiguous();
+  for (auto* t : {&dbc, &dwc, &bg, &wg, &fp}) check_rows(*t, d, "gate tensor");
+  auto a = decay_a.to(at::kFloat).contiguous();
+  torch::Tensor acc;
+  if (da_acc.has_value() && da_acc->defined()) {
+    check_acc(*da_acc, d / Dh, "da_acc");
+    acc = *da_acc;
+  } else {
+    acc = torch::zeros({d / Dh}, bg.options().dtype(at::kFloat));
+  }
+  auto dbp = torch::empty_like(bg), dwp = torch::empty_like(bg), dfp = torch::empty_like(bg);
+  ahb_gdn_gates_bwd(dbc.data_ptr(), dwc.data_ptr(), dgc.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
+                    fp.data_ptr(), a.data_ptr<float>(), dbp.data_ptr(), dwp.data_ptr(), dfp.data_ptr(),
+                    acc.data_ptr<float>(), bg.numel(), (int)d, (int)Dh, cur_stream());
+  check_launch("ahb_gdn_gates_bwd");
+  return {dbp, dwp, dfp, acc};
+}
+
+std::vector<torch::Tensor> l2norm_heads_fwd(torch::Tensor x) {
+  TORCH_CHECK(x.size(-1) == 128, "l2norm_heads: head dim 128");
+  check_rows(x, 128, "x");
+  const int64_t nh = x.numel() / 128;
+  auto y = torch::empty_like(x);
+  auto rn = torch::empty({nh}, x.options().dtype(at::kFloat));
+  ahb_l2norm_heads_fwd(x.data_ptr(), y.data_ptr(), rn.data_ptr<float>(), nh, cur_stream());
+  check_launch("ahb_l2norm_heads_fwd");
+  return {y, rn};
+}
+
+torch::Tensor l2norm_heads_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor rn) {
+  auto dyc = dy.to(at::kBFloat16).contiguous();
+  check_rows(dyc, 128, "dy");
+  check_rows(x, 128, "x");
+  auto dx = torch::empty_like(x);
+  ahb_l2norm_heads_bwd(dyc.data_ptr(), x.data_ptr(), rn.data_ptr<float>(), dx.data_ptr(), x.numel() / 128,
+                       cur_stream());
+  check_launch("ahb_l2norm_heads_bwd");
+  return dx;
+}
+
+torch::Tensor dt_act_fwd(torch::Tensor u) {
+  TORCH_CHECK(u.is_cuda() && u.scalar_type() == at::kBFloat16 && u.is_contiguous() && u.numel() % 8 == 0,
+              "dt_act: contiguous bf16, numel % 8 == 0");
+  auto dt = torch::empty_like(u);
+  ahb_dt_act_fwd(u.data_ptr(), dt.data_ptr(), u.numel(), cur_stream());
+  check_launch("ahb_dt_act_fwd");
+  return dt;
+}
+
+torch::Tensor dt_act_bwd(torch::Tensor ddt, torch::Tensor u) {
+  auto dc = ddt.to(at::kBFloat16).contiguous();
+  TORCH_CHECK(dc.numel() == u.numel() && u.is_contiguous(), "dt_act_bwd: shapes");
+  auto du = torch::empty_like(u);
+  ahb_dt_act_bwd(dc.data_ptr(), u.data_ptr(), du.data_ptr(), u.numel(), cur_stream());
+  check_launch("ahb_dt_act_bwd");
+  return du;
+}
+
 // ------------------------------------------------------------ NVLink peer memory (CUDA IPC)
 int64_t ipc_alloc(int64_t nbytes) {
   void* p = nullptr;
@@ -641,8 +892,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd_", &embedding_bwd_);
   m.def("gdn_fwd", &gdn_fwd);
   m.def("gdn_bwd", &gdn_bwd);
+  m.def("gdn_fwd_train", &gdn_fwd_train);
+  m.def("gdn_bwd_saved", &gdn_bwd_saved);
+  m.def("ssd_fwd_train", &ssd_fwd_train);
   m.def("ssd_fwd", &ssd_fwd);
-  m.def("ssd_bwd", &ssd_bwd);
+  m.def("ssd_bwd", &ssd_bwd, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"), py::arg("dy"),
+        py::arg("states") = py::none(), py::arg("cumsums") = py::none());
   m.def("gemm_dense", &gemm_dense);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_error_reset", &gemm_error_reset);
@@ -653,6 +908,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fused_bwd", &ce_fused_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);
+  m.def("norm_gate_fwd", &norm_gate_fwd);
+  m.def("norm_gate_bwd", &norm_gate_bwd);
+  m.def("gdn_gates_fwd", &gdn_gates_fwd);
+  m.def("gdn_gates_bwd", &gdn_gates_bwd);
+  m.def("l2norm_heads_fwd", &l2norm_heads_fwd);
+  m.def("l2norm_heads_bwd", &l2norm_heads_bwd);
+  m.def("dt_act_fwd", &dt_act_fwd);
+  m.def("dt_act_bwd", &dt_act_bwd);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

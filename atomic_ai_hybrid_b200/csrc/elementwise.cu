@@ -369,6 +369,11 @@ void ahb_rmsnorm_bwd(const void* dy, const void* x, const float* scale, const fl
   if (dscale_acc) colsum_add_kernel<<<(D + 255) / 256, 256, 0, st>>>(dscale_part, rms_bwd_blocks(M, D), D, dscale_acc);
 }
 
+void ahb_colsum_add(const float* part, int nb, int D, float* out, cudaStream_t st) {
+  if (D <= 0 || nb <= 0) return;
+  colsum_add_kernel<<<(D + 255) / 256, 256, 0, st>>>(part, nb, D, out);
+}
+
 void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,
                     int C, int dtype, int silu, float clip, cudaStream_t st) {
   int64_t n = (int64_t)B * ((L + CONV_TT - 1) / CONV_TT) * (C / 8);

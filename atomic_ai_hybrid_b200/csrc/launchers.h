@@ -20,6 +20,8 @@ void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const 
                     float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
                     cudaStream_t st);
 void ahb_accumulate(float* acc, const void* g, int64_t n, int dtype, float scale, cudaStream_t st);
+// out[c] += sum_b part[b * D + c]
+void ahb_colsum_add(const float* part, int nb, int D, float* out, cudaStream_t st);
 void ahb_embedding_fwd(const int64_t* ids, const void* emb, int edtype, void* out, int odtype, int64_t T, int D,
                        int64_t V, cudaStream_t st);
 void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* acc, int64_t T, int D, int64_t V,
@@ -55,7 +57,7 @@ void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, 
 int ahb_ssd_head_groups(int H);
 void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                  int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
-                 float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st);
+                 float* dC, float* dA, float* dB_part, float* dC_part, int states_ready, cudaStream_t st);
 
 // moe_gemm.cu: tcgen05 grouped GEMM.  Returns 0 on success, <0 on a setup error.
 #define AHB_GEMM_DENSE 0        // C[M,N] = A[M,K] B[N,K]^T (single group)
@@ -114,6 +116,29 @@ void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nbl
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
                      const float* grad, const float* coef, void* compute, const float* frac, int fracE,
                      AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st);
+
+// fused_norm.cu: residual add + clip + RMSNorm, RMSNorm x SiLU gate, GDN gates, per-head L2 norm, Mamba2 dt
+// (bf16 activations, fp32 scales / statistics; rows of D channels need D % 256 == 0)
+int ahb_row_supported(int D);
+int ahb_row_bwd_blocks(int64_t M);
+void ahb_add_rmsnorm_fwd(const void* x, const void* delta, const float* scale, void* xo, void* y, float* rstd,
+                         int64_t M, int D, float clip, float eps, cudaStream_t st);
+void ahb_add_rmsnorm_bwd(const void* dy, const void* gres, const void* xo, const float* scale, const float* rstd,
+                         void* dx, void* ddelta, float* dscale_part, int64_t M, int D, float clip, cudaStream_t st);
+void ahb_norm_gate_fwd(const void* x, const void* z, int64_t zs, const float* scale, void* y, float* rstd, int64_t M,
+                       int D, float eps, float zclip, float oclip, cudaStream_t st);
+void ahb_norm_gate_bwd(const void* dy, const void* x, const void* z, int64_t zs, const float* scale, const float* rstd,
+                       void* dx, void* dz, float* dscale_part, int64_t M, int D, float zclip, float oclip,
+                       cudaStream_t st);
+void ahb_gdn_gates_fwd(const void* bp, const void* wp, const void* fp, const float* decay_a, void* bg, void* wg,
+                       float* g, int64_t n, int d, int Dh, cudaStream_t st);
+void ahb_gdn_gates_bwd(const void* dbg, const void* dwg, const float* dg, const void* bg, const void* wg,
+                       const void* fp, const float* decay_a, void* dbp, void* dwp, void* dfp, float* da_acc,
+                       int64_t n, int d, int Dh, cudaStream_t st);
+void ahb_l2norm_heads_fwd(const void* x, void* y, float* rn, int64_t nheads, cudaStream_t st);
+void ahb_l2norm_heads_bwd(const void* dy, const void* x, const float* rn, void* dx, int64_t nheads, cudaStream_t st);
+void ahb_dt_act_fwd(const void* u, void* dt, int64_t n, cudaStream_t st);
+void ahb_dt_act_bwd(const void* ddt, const void* u, void* du, int64_t n, cudaStream_t st);
 
 // comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
 int ahb_ipc_alloc(int64_t nbytes, void** ptr);

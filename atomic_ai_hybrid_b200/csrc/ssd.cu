@@ -562,7 +562,7 @@ int ahb_ssd_head_groups(int H) { return head_groups(H); }
 // head groups are written to dB / dC.
 void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                  int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
-                 float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st) {
+                 float* dC, float* dA, float* dB_part, float* dC_part, int states_ready, cudaStream_t st) {
   static bool init = false;
   if (!init) {
     set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
@@ -572,9 +572,11 @@ void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, 
   }
   const int NC = L / C;
   const int G = head_groups(H);
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                 (const bf16*)Bm, L, H, state_buf, cuml);
-  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
+  if (!states_ready) {  // otherwise state_buf / cuml hold the forward's scanned chunk states
+    ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
+                                                                   (const bf16*)Bm, L, H, state_buf, cuml);
+    ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
+  }
   ssd_dstate_kernel<<<dim3(NC, B, G), 512, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
                                                          g_buf);
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(g_buf, cuml, H, NC, 1, nullptr, nullptr);

@@ -163,6 +163,20 @@ class InterleavedLayer(nn.Module):
         stats.append(st)
         return x
 
+    def forward_fused(self, x, h, next_scale, cos, sin, stats: List[Dict]):
+        """Same computation with each residual update fused into the following
+        RMSNorm: takes ``h = pre_norm(x)``, returns the new residual and its
+        normalisation by ``next_scale`` (the next layer's ``pre_norm`` or the
+        final norm)."""
+        from ..ops import kernels as K
+        delta = self.sublayer(h, cos, sin)
+        clip = 5e2 if self.layer_type == "mamba2" else 1e3
+        x, h2 = K.add_rmsnorm(x, delta, self.norm_2.scale, clip, 1e-6, sanitize_delta_grad=True)
+        st: Dict[str, torch.Tensor] = {}
+        m = self.moe(h2, st)
+        stats.append(st)
+        return K.add_rmsnorm(x, m, next_scale, 1e3, 1e-6)
+
 
 class Embed(nn.Module):
     def __init__(self, vocab: int, d: int):
@@ -222,6 +236,8 @@ class HybridMoEModel(nn.Module):
             history: List[torch.Tensor] = []
             for blk in self.blocks():
                 x = blk(x, history, cos, sin, stats)
+        elif self._fused_residuals(x):
+            return self._forward_fused(x, cos, sin, stats, return_hidden)
         else:
             for layer in self.blocks():
                 if self.remat and torch.is_grad_enabled():
@@ -236,6 +252,30 @@ class HybridMoEModel(nn.Module):
             return h, stats
         w = self.lm_weight()
         return h @ w.to(h.dtype).t(), stats
+
+    def _fused_residuals(self, x: torch.Tensor) -> bool:
+        if not ops.use_cuda(x) or x.dtype != torch.bfloat16:
+            return False
+        from ..ops import kernels as K
+        return K.row_fusable(self.cfg.d_model)
+
+    def _forward_fused(self, x, cos, sin, stats: List[Dict], return_hidden: bool):
+        """Interleaved stack with the residual updates fused into the RMSNorms
+        that follow them (``InterleavedLayer.forward_fused``)."""
+        layers = self.blocks()
+        h = ops.rmsnorm(x, layers[0].pre_norm.scale, 1e-6)
+        for i, layer in enumerate(layers):
+            nxt = layers[i + 1].pre_norm.scale if i + 1 < len(layers) else self.final_norm.scale
+            if self.remat and torch.is_grad_enabled():
+                import torch.utils.checkpoint as ckpt
+                st: List[Dict] = []
+                x, h = ckpt.checkpoint(layer.forward_fused, x, h, nxt, cos, sin, st, use_reentrant=False)
+                stats.extend(st)
+            else:
+                x, h = layer.forward_fused(x, h, nxt, cos, sin, stats)
+        if return_hidden:
+            return h, stats
+        return h @ self.lm_weight().to(h.dtype).t(), stats
 
     def lm_weight(self) -> torch.Tensor:
         """``(V, d)`` weight of the tied (or separate) LM head."""

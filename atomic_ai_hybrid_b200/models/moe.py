@@ -119,7 +119,8 @@ class MoE(nn.Module):
         flat = x.reshape(-1, d)
         top_idx, gate = self.route(flat, stats)
         shared = self._shared(flat) if self.n_shared > 0 else None
-        if ops.use_cuda(flat) and x.dtype == torch.bfloat16:
+        # the grouped GEMM tiles need d_model and d_ff in multiples of 256
+        if ops.use_cuda(flat) and x.dtype == torch.bfloat16 and d % 256 == 0 and self.cfg.d_ff % 256 == 0:
             from ..ops import kernels as K
             out = K.moe_forward(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3, shared,
                                 "swiglu" if self.swiglu else "gelu")

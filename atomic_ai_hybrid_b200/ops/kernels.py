@@ -9,6 +9,7 @@ weight-gradient tensor is materialised per micro-step.  Without an accumulator
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -135,56 +136,96 @@ def embedding(ids, table, dtype):
 
 
 # ----------------------------------------------------------------- not yet native
+# Keep the chunk intermediates of the scans for the backward (default) instead of
+# recomputing them there, as the reference's B6 backward does (`atomic_ops/
+# kernel_trainable_B6.py:104-109`); AHB_SCAN_RECOMPUTE=1 trades the memory back.
+SCAN_RECOMPUTE = os.environ.get("AHB_SCAN_RECOMPUTE", "0") == "1"
+
+
 class _GDN2(torch.autograd.Function):
-    """sm_100a chunked GDN-2 (head dim 128, chunk 64): 2 launches forward, 6 backward
-    (the backward recomputes the chunk-local forward quantities, as the reference's
-    B6 backward does)."""
+    """sm_100a chunked GDN-2 (head dim 128, chunk 64): 2 launches forward; the
+    backward runs 4 launches on the saved chunk intermediates (WY factors, scores,
+    per-chunk states), or 6 when it recomputes them."""
 
     @staticmethod
     def forward(ctx, q, k, v, g, b, w, scale):
         bf = torch.bfloat16
         q, k, v, b, w = (t.to(bf).contiguous() for t in (q, k, v, b, w))
         g = g.float().contiguous()
-        (o,) = ext().gdn_fwd(q, k, v, g, b, w, scale, False)
-        ctx.save_for_backward(q, k, v, g, b, w)
+        keep = any(ctx.needs_input_grad) and not SCAN_RECOMPUTE
+        if keep:
+            o, *inter = ext().gdn_fwd_train(q, k, v, g, b, w, scale)
+        else:
+            (o,) = ext().gdn_fwd(q, k, v, g, b, w, scale, False)
+            inter = []
+        ctx.n_inter = len(inter)
+        ctx.save_for_backward(q, k, v, g, b, w, *inter)
         ctx.scale = scale
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, g, b, w = ctx.saved_tensors
-        dq, dk, dv, dg, db, dw = ext().gdn_bwd(q, k, v, g, b, w, do.contiguous(), ctx.scale)
+        q, k, v, g, b, w, *inter = ctx.saved_tensors
+        if inter:
+            dq, dk, dv, dg, db, dw = ext().gdn_bwd_saved(q, k, v, g, b, w, do.contiguous(), ctx.scale, inter)
+        else:
+            dq, dk, dv, dg, db, dw = ext().gdn_bwd(q, k, v, g, b, w, do.contiguous(), ctx.scale)
         return dq, dk, dv, dg, db, dw, None
+
+
+_WARNED = set()
+
+
+def _unsupported(what: str) -> None:
+    if what not in _WARNED:
+        _WARNED.add(what)
+        print(f"[atomic_ai_hybrid_b200] {what}: shape not covered by the sm_100a kernel; "
+              f"using the PyTorch chunked path", flush=True)
 
 
 def gdn2(q, k, v, w, b, g, scale, chunk):
     """``(B,L,H,128)`` GDN-2 with per-channel gates; ``chunk`` is fixed at 64 in the kernel
-    (results do not depend on the chunk length)."""
+    (results do not depend on the chunk length).  Other head dims or lengths that are
+    not a multiple of 64 run the PyTorch chunked path."""
+    if q.shape[-1] != 128 or q.shape[1] % 64:
+        _unsupported(f"gdn2 D={q.shape[-1]} L={q.shape[1]}")
+        o, _ = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
+        return o
     return _GDN2.apply(q, k, v, g, b, w, float(scale))
 
 
 class _SSD(torch.autograd.Function):
-    """sm_100a Mamba2 SSD (head dim 64, d_state 128, chunk 64): 3 launches forward,
-    5 backward (forward chunk states are recomputed in backward)."""
+    """sm_100a Mamba2 SSD (head dim 64, d_state 128, chunk 64): 3 launches forward;
+    the backward reuses the forward's scanned chunk states (5 launches) or
+    recomputes them (7)."""
 
     @staticmethod
     def forward(ctx, dt, A, Bm, Cm, x):
         bf = torch.bfloat16
         dt, Bm, Cm, x = (t.to(bf).contiguous() for t in (dt, Bm, Cm, x))
         A = A.float().contiguous()
-        y = ext().ssd_fwd(x, dt, A, Bm, Cm)
-        ctx.save_for_backward(dt, A, Bm, Cm, x)
+        if any(ctx.needs_input_grad) and not SCAN_RECOMPUTE:
+            y, states, cums = ext().ssd_fwd_train(x, dt, A, Bm, Cm)
+            ctx.save_for_backward(dt, A, Bm, Cm, x, states, cums)
+        else:
+            y = ext().ssd_fwd(x, dt, A, Bm, Cm)
+            ctx.save_for_backward(dt, A, Bm, Cm, x)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        dt, A, Bm, Cm, x = ctx.saved_tensors
-        dx, ddt, dA, dB, dC = ext().ssd_bwd(x, dt, A, Bm, Cm, dy.contiguous())
+        dt, A, Bm, Cm, x, *st = ctx.saved_tensors
+        dx, ddt, dA, dB, dC = ext().ssd_bwd(x, dt, A, Bm, Cm, dy.contiguous(), *st)
         return ddt, dA, dB.to(Bm.dtype), dC.to(Cm.dtype), dx
 
 
 def ssd(dt, A, Bm, Cm, x, chunk):
-    """``dt, x (B,L,H,64)``, ``A (H,)``, ``B, C (B,L,128)``; chunk fixed at 64 in the kernel."""
+    """``dt, x (B,L,H,64)``, ``A (H,)``, ``B, C (B,L,128)``; chunk fixed at 64 in the kernel.
+    Other head dims / state sizes run the PyTorch chunked path."""
+    if x.shape[-1] != 64 or Bm.shape[-1] != 128 or x.shape[1] % 64:
+        _unsupported(f"ssd P={x.shape[-1]} N={Bm.shape[-1]} L={x.shape[1]}")
+        y, _ = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
+        return y
     return _SSD.apply(dt, A, Bm, Cm, x)
 
 
@@ -225,8 +266,141 @@ def cross_entropy(h, labels, weight, label_smoothing):
     return _FusedCE.apply(h, labels, weight, float(label_smoothing))
 
 
+# ----------------------------------------------------------------- fused layer glue
+def row_fusable(d: int) -> bool:
+    """Rows handled by the fused row kernels: D/8 threads with 16-byte accesses."""
+    return d % 256 == 0 and d <= 8192
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    """``xo = sanitize(x + delta, clip)``, ``y = rmsnorm(xo) * scale``; the
+    backward optionally sanitizes the delta gradient (grad sanitizer on a sublayer
+    output)."""
+
+    @staticmethod
+    def forward(ctx, x, delta, scale, clip, eps, sanitize_delta_grad):
+        xo, y, rstd = ext().add_rmsnorm_fwd(x, delta.contiguous(), scale, clip, eps)
+        ctx.save_for_backward(xo, scale, rstd)
+        ctx.clip, ctx.sdg = clip, sanitize_delta_grad
+        return xo, y
+
+    @staticmethod
+    def backward(ctx, gxo, gy):
+        xo, scale, rstd = ctx.saved_tensors
+        acc, direct = _acc_for(scale) if ctx.needs_input_grad[2] else (None, False)
+        if gy is None:
+            gy = torch.zeros_like(xo)
+        dx, dd = ext().add_rmsnorm_bwd(gy, gxo, xo, scale, rstd, ctx.clip, ctx.sdg, acc)
+        return dx, dd, _ret_grad(scale, acc, direct), None, None, None
+
+
+def add_rmsnorm(x, delta, scale, clip: float, eps: float = 1e-6, sanitize_delta_grad: bool = False):
+    return _AddRMSNorm.apply(x, delta, scale, clip, eps, sanitize_delta_grad)
+
+
+class _NormGate(torch.autograd.Function):
+    """``clamp(rmsnorm(x) * scale * silu(clamp(z, +-zclip)), +-oclip)``."""
+
+    @staticmethod
+    def forward(ctx, x, z, scale, eps, zclip, oclip):
+        y, rstd = ext().norm_gate_fwd(x, z, scale, eps, zclip, oclip)
+        ctx.save_for_backward(x, z, scale, rstd)
+        ctx.zclip, ctx.oclip = zclip, oclip
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, z, scale, rstd = ctx.saved_tensors
+        acc, direct = _acc_for(scale) if ctx.needs_input_grad[2] else (None, False)
+        dx, dz = ext().norm_gate_bwd(dy, x, z, scale, rstd, ctx.zclip, ctx.oclip, acc)
+        return dx, dz.view(z.shape), _ret_grad(scale, acc, direct), None, None, None
+
+
+def norm_gate(x, z, scale, eps: float = 1e-6, zclip: float = math.inf, oclip: float = math.inf):
+    return _NormGate.apply(x.contiguous(), z, scale, eps, zclip, oclip)
+
+
+class _GDNGates(torch.autograd.Function):
+    """Per-channel GDN-2 gates: ``sigmoid`` erase / write gates and the decay
+    ``g = clamp(nan_to_num(-exp(clamp(a)) * softplus(f)), +-1e3)`` (fp32)."""
+
+    @staticmethod
+    def forward(ctx, bp, wp, fp, decay_a, Dh):
+        bg, wg, g = ext().gdn_gates_fwd(bp, wp, fp, decay_a, Dh)
+        ctx.save_for_backward(bg, wg, fp, decay_a)
+        ctx.Dh = Dh
+        return bg, wg, g
+
+    @staticmethod
+    def backward(ctx, dbg, dwg, dg):
+        bg, wg, fp, decay_a = ctx.saved_tensors
+        dbg = torch.zeros_like(bg) if dbg is None else dbg
+        dwg = torch.zeros_like(wg) if dwg is None else dwg
+        dg = torch.zeros(bg.shape, dtype=torch.float32, device=bg.device) if dg is None else dg
+        acc, direct = _acc_for(decay_a) if ctx.needs_input_grad[3] else (None, False)
+        dbp, dwp, dfp, acc_out = ext().gdn_gates_bwd(dbg, dwg, dg, bg, wg, fp, decay_a, ctx.Dh, acc)
+        return dbp, dwp, dfp, _ret_grad(decay_a, acc_out, direct), None
+
+
+def gdn_gates(bp, wp, fp, decay_a, Dh: int):
+    return _GDNGates.apply(bp.contiguous(), wp.contiguous(), fp.contiguous(), decay_a, Dh)
+
+
+class _L2NormHeads(torch.autograd.Function):
+    """Per-head L2 normalisation (head dim 128) followed by the gradient sanitizer."""
+
+    @staticmethod
+    def forward(ctx, x):
+        y, rn = ext().l2norm_heads_fwd(x)
+        ctx.save_for_backward(x, rn)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rn = ctx.saved_tensors
+        return ext().l2norm_heads_bwd(dy, x, rn)
+
+
+def l2norm_heads(x):
+    return _L2NormHeads.apply(x.contiguous())
+
+
+class _DtAct(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, u):
+        ctx.save_for_backward(u)
+        return ext().dt_act_fwd(u)
+
+    @staticmethod
+    def backward(ctx, ddt):
+        (u,) = ctx.saved_tensors
+        return ext().dt_act_bwd(ddt, u)
+
+
+def dt_act(u):
+    """Mamba2 ``clamp(softplus(u), 0.01, 1)``."""
+    return _DtAct.apply(u.contiguous())
+
+
 def gdn2_layer(mod, x):
+    if x.dtype == torch.bfloat16 and mod.d_head == 128 and row_fusable(x.shape[-1]):
+        return _gdn2_layer_fused(mod, x)
     return _gdn2_layer_composed(mod, x)
+
+
+def _gdn2_layer_fused(mod, x):
+    Bsz, L, d = x.shape
+    H, D = mod.n_heads, mod.d_head
+    q = conv1d(mod.q_proj(x), mod.q_conv_w, mod.q_conv_b, True)
+    k = conv1d(mod.k_proj(x), mod.k_conv_w, mod.k_conv_b, True)
+    v = conv1d(mod.v_proj(x), mod.v_conv_w, mod.v_conv_b, True, 50.0)
+    q = l2norm_heads(q.view(Bsz, L, H, D))
+    k = l2norm_heads(k.view(Bsz, L, H, D))
+    bg, wg, g = gdn_gates(mod.erase_gate(x), mod.write_gate(x), mod.decay_proj(x), mod.decay_a, D)
+    shp = (Bsz, L, H, D)
+    o = gdn2(q, k, v.view(shp), wg.view(shp), bg.view(shp), g.view(shp), 1.0, mod.cfg.gdn_chunk)
+    o = norm_gate(o.reshape(Bsz, L, d).to(x.dtype), mod.out_gate(x), mod.out_norm.scale, 1e-6, zclip=1e2)
+    return mod.out_proj(o)
 
 
 def _gdn2_layer_composed(mod, x):
@@ -256,16 +430,21 @@ def mamba2_layer(mod, x):
     Bsz, L, d = x.shape
     di, Hs = mod.cfg.d_inner, mod.cfg.n_heads_ssm
     P = di // Hs
+    fused = x.dtype == torch.bfloat16 and row_fusable(di)
     xz = mod.in_proj(x)
     x_bc, res = xz[..., :di], xz[..., di:]
     x_conv = conv1d(x_bc, mod.conv_w, mod.conv_b, True)
     A = -torch.exp(mod.A_log.float().clamp(-20.0, 20.0))
     Bm = mod.B_proj(x_bc)
     Cm = mod.C_proj(x_bc)
-    dt = F.softplus(mod.dt_proj(x_bc)).clamp(1e-2, 1.0)
+    dtp = mod.dt_proj(x_bc)
+    dt = dt_act(dtp) if fused else F.softplus(dtp).clamp(1e-2, 1.0)
     y = ssd(dt.view(Bsz, L, Hs, P), A, Bm.clamp(-1e3, 1e3), Cm.clamp(-1e3, 1e3), x_conv.view(Bsz, L, Hs, P),
             mod.cfg.ssd_chunk)
-    y = rmsnorm(y.reshape(Bsz, L, di).to(x_bc.dtype), mod.ssm_out_norm.scale, 1e-6)
+    y = y.reshape(Bsz, L, di).to(x_bc.dtype)
+    if fused:
+        return mod.out_proj(norm_gate(y, res, mod.ssm_out_norm.scale, 1e-6, oclip=3e2))
+    y = rmsnorm(y, mod.ssm_out_norm.scale, 1e-6)
     out = (y * F.silu(res)).clamp(-3e2, 3e2)
     return mod.out_proj(out)
 

@@ -240,6 +240,7 @@ def main():
                                        type(trainer.comm).__name__),
                        "optimizer": args.optimizer, "params_total": nparams["total"],
                        "num_layers": cfg.num_layers,
+                       "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1) if dev.type == "cuda" else None,
                        "l2": "inputs larger than L2 (11+ GB of weights streamed per micro-step)"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }
