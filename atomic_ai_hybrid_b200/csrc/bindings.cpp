@@ -783,6 +783,83 @@ torch::Tensor dt_act_bwd(torch::Tensor ddt, torch::Tensor u) {
   return du;
 }
 
+// ------------------------------------------------------------ fused MoE router (router.cu)
+bool router_supported(int64_t d, int64_t E, int64_t k) { return ahb_router_supported((int)d, (int)E, (int)k) != 0; }
+
+// kn (d, E) fp32 -> zero-padded bf16 terms hi (+ mid (+ lo)) whose sum is kn;
+// transposed: (terms, EP, d), else (terms, d, EP)
+static torch::Tensor router_split(const torch::Tensor& kn, int terms, bool transposed) {
+  const int64_t d = kn.size(0), E = kn.size(1), EP = ahb_router_padded_experts((int)E);
+  auto knp = torch::zeros({d, EP}, kn.options());
+  knp.narrow(1, 0, E).copy_(kn);
+  std::vector<torch::Tensor> parts;
+  auto rem = knp;
+  for (int i = 0; i < terms; ++i) {
+    auto h = rem.to(at::kBFloat16);
+    parts.push_back(transposed ? h.t() : h);
+    rem = rem - h.to(at::kFloat);
+  }
+  return torch::stack(parts).contiguous();
+}
+
+std::vector<torch::Tensor> router_fwd(torch::Tensor x, torch::Tensor kn, torch::Tensor temp, torch::Tensor bias,
+                                      c10::optional<torch::Tensor> noise, int64_t k) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 2,
+              "router: x (T, d) contiguous bf16");
+  const int64_t T = x.size(0), d = x.size(1);
+  auto knc = kn.to(at::kFloat).contiguous();
+  TORCH_CHECK(knc.dim() == 2 && knc.size(0) == d, "router: kn (d, E)");
+  const int64_t E = knc.size(1);
+  TORCH_CHECK(ahb_router_supported((int)d, (int)E, (int)k), "router: unsupported d / E / k");
+  auto knT3 = router_split(knc, 3, true);
+  auto tc = temp.to(at::kFloat).contiguous();
+  auto bc = bias.to(at::kFloat).contiguous();
+  torch::Tensor nz;
+  if (noise.has_value() && noise->defined()) {
+    nz = noise->to(at::kFloat).contiguous();
+    TORCH_CHECK(nz.numel() == T * E, "router: noise (T, E)");
+  }
+  auto f32 = x.options().dtype(at::kFloat);
+  auto logits = torch::empty({T, E}, f32), cosv = torch::empty({T, E}, f32);
+  auto rn = torch::empty({T}, f32);
+  auto top = torch::empty({T, k}, x.options().dtype(at::kLong));
+  auto gate = torch::empty({T, k}, f32);
+  auto psum = torch::zeros({E}, f32), counts = torch::zeros({E}, f32);
+  // [sum lse^2, max |pre|, sum |x|, max |x|, min |x| (starts at the largest finite float)]
+  auto scal = torch::arange(0, 5, f32).mul_(0).add_(torch::arange(0, 5, f32).eq(4).to(at::kFloat).mul_(3.0e38));
+  ahb_router_fwd(x.data_ptr(), knT3.data_ptr(), tc.data_ptr<float>(), bc.data_ptr<float>(),
+                 nz.defined() ? nz.data_ptr<float>() : nullptr, T, (int)d, (int)E, (int)k, logits.data_ptr<float>(),
+                 cosv.data_ptr<float>(), rn.data_ptr<float>(), top.data_ptr<int64_t>(), gate.data_ptr<float>(),
+                 psum.data_ptr<float>(), scal.data_ptr<float>(), counts.data_ptr<float>(), cur_stream());
+  check_launch("ahb_router_fwd");
+  return {logits, cosv, rn, top, gate, psum, scal, counts};
+}
+
+std::vector<torch::Tensor> router_bwd(torch::Tensor x, torch::Tensor kn, torch::Tensor temp, torch::Tensor logits,
+                                      torch::Tensor cosv, torch::Tensor rn, torch::Tensor top, torch::Tensor gate,
+                                      torch::Tensor dgate, torch::Tensor dps, c10::optional<torch::Tensor> dlse_sq) {
+  const int64_t T = x.size(0), d = x.size(1), E = logits.size(1), k = top.size(1);
+  auto knc = kn.to(at::kFloat).contiguous();
+  auto tc = temp.to(at::kFloat).contiguous();
+  auto dg = dgate.to(at::kFloat).contiguous();
+  auto dp = dps.to(at::kFloat).contiguous();
+  torch::Tensor dl;
+  if (dlse_sq.has_value() && dlse_sq->defined()) dl = dlse_sq->to(at::kFloat).contiguous();
+  auto f32 = x.options().dtype(at::kFloat);
+  auto kn2 = router_split(knc, 2, false);
+  auto dcos = torch::empty({T, (int64_t)ahb_router_padded_experts((int)E)}, f32);
+  auto dtemp = torch::zeros({1}, f32);
+  auto dkn = torch::zeros({d, E}, f32);
+  auto dx = torch::empty_like(x);
+  ahb_router_bwd(x.data_ptr(), kn2.data_ptr(), tc.data_ptr<float>(), logits.data_ptr<float>(),
+                 cosv.data_ptr<float>(), rn.data_ptr<float>(), top.data_ptr<int64_t>(), gate.data_ptr<float>(),
+                 dg.data_ptr<float>(), dp.data_ptr<float>(), dl.defined() ? dl.data_ptr<float>() : nullptr, T, (int)d,
+                 (int)E, (int)k, dcos.data_ptr<float>(), dtemp.data_ptr<float>(), dx.data_ptr(),
+                 dkn.data_ptr<float>(), cur_stream());
+  check_launch("ahb_router_bwd");
+  return {dx, dkn, dtemp};
+}
+
 // ------------------------------------------------------------ NVLink peer memory (CUDA IPC)
 int64_t ipc_alloc(int64_t nbytes) {
   void* p = nullptr;
@@ -918,6 +995,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("l2norm_heads_bwd", &l2norm_heads_bwd);
   m.def("dt_act_fwd", &dt_act_fwd);
   m.def("dt_act_bwd", &dt_act_bwd);
+  m.def("router_supported", &router_supported);
+  m.def("router_fwd", &router_fwd);
+  m.def("router_bwd", &router_bwd);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

@@ -274,6 +274,179 @@ __global__ void conv1d_bwd_kernel(const T* __restrict__ x, int64_t xs, const WT*
   }
 }
 
+// Streaming variants for bf16 activations (C % 128 == 0): a warp owns 128 channels
+// (4 per lane, 8-byte accesses) over a span of CSPAN steps and slides a 4-tap window
+// along time, so every x / dy element is read once and dx is written once.  The 8
+// warps of a CTA take consecutive spans of the same channels and pre-reduce the
+// weight gradients in shared memory before one atomic per (channel, tap).
+constexpr int CSPAN = 64;
+
+AHB_DEVICE void ld4(const bf16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+AHB_DEVICE void st4(bf16* p, const float (&v)[4]) {
+  uint2 u;
+  *reinterpret_cast<__nv_bfloat162*>(&u.x) = __floats2bfloat162_rn(v[0], v[1]);
+  *reinterpret_cast<__nv_bfloat162*>(&u.y) = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(256) conv1d_fwd_stream_kernel(const bf16* __restrict__ x, int64_t xs,
+                                                                const WT* __restrict__ w,
+                                                                const float* __restrict__ bias, bf16* __restrict__ y,
+                                                                int B, int L, int C, bool silu, float clip) {
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 128 + lane * 4;
+  const int nspan = (L + CSPAN - 1) / CSPAN;
+  const int64_t gs = (int64_t)blockIdx.y * 8 + wp;
+  if (gs >= (int64_t)B * nspan) return;
+  const int b = (int)(gs / nspan), t0 = (int)(gs % nspan) * CSPAN;
+  float wk[4][4], bs[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) wk[j][k] = to_f(w[(c0 + j) * 4 + k]);
+    bs[j] = bias ? bias[c0 + j] : 0.f;
+  }
+  const bf16* xb = x + (int64_t)b * L * xs + c0;
+  bf16* yb = y + (int64_t)b * L * C + c0;
+  float xw[3][4];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int t = t0 - 3 + k;
+    if (t >= 0) ld4(xb + (int64_t)t * xs, xw[k]);
+    else { xw[k][0] = xw[k][1] = xw[k][2] = xw[k][3] = 0.f; }
+  }
+  const int tend = t0 + CSPAN < L ? t0 + CSPAN : L;
+#pragma unroll 4
+  for (int t = t0; t < tend; ++t) {
+    float xc[4], o[4];
+    ld4(xb + (int64_t)t * xs, xc);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a = bs[j] + wk[j][0] * xw[0][j] + wk[j][1] * xw[1][j] + wk[j][2] * xw[2][j] + wk[j][3] * xc[j];
+      if (silu) a = siluf_(a);
+      if (clip > 0.f) a = fminf(fmaxf(a, -clip), clip);
+      o[j] = a;
+      xw[0][j] = xw[1][j];
+      xw[1][j] = xw[2][j];
+      xw[2][j] = xc[j];
+    }
+    st4(yb + (int64_t)t * C, o);
+  }
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(256) conv1d_bwd_stream_kernel(const bf16* __restrict__ x, int64_t xs,
+                                                                const WT* __restrict__ w,
+                                                                const float* __restrict__ bias,
+                                                                const bf16* __restrict__ dy, bf16* __restrict__ dx,
+                                                                int64_t dxs, float* __restrict__ dw,
+                                                                float* __restrict__ db, int B, int L, int C,
+                                                                bool silu, float clip) {
+  __shared__ float red[128][5];  // per channel: 4 taps + bias
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 128 * 5; i += blockDim.x) (&red[0][0])[i] = 0.f;
+  __syncthreads();
+  const int c0 = blockIdx.x * 128 + lane * 4;
+  const int nspan = (L + CSPAN - 1) / CSPAN;
+  const int64_t gs = (int64_t)blockIdx.y * 8 + wp;
+  if (gs < (int64_t)B * nspan) {
+    const int b = (int)(gs / nspan), t0 = (int)(gs % nspan) * CSPAN;
+    float wk[4][4], bs[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) wk[j][k] = to_f(w[(c0 + j) * 4 + k]);
+      bs[j] = bias ? bias[c0 + j] : 0.f;
+    }
+    const bf16* xb = x + (int64_t)b * L * xs + c0;
+    const bf16* dyb = dy + (int64_t)b * L * C + c0;
+    bf16* dxb = dx + (int64_t)b * L * dxs + c0;
+    float xw[3][4], dpw[3][4], dwl[4][4], dbl[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      dbl[j] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) dwl[j][k] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dpw[k][j] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int t = t0 - 3 + k;
+      if (t >= 0) ld4(xb + (int64_t)t * xs, xw[k]);
+      else { xw[k][0] = xw[k][1] = xw[k][2] = xw[k][3] = 0.f; }
+    }
+    const int own_end = t0 + CSPAN < L ? t0 + CSPAN : L;
+    // dp(t) for t in [t0, own_end + 3): the last three steps only feed dx of the span's tail
+#pragma unroll 2
+    for (int t = t0; t < own_end + 3; ++t) {
+      float xc[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (t < L) {
+        float dv[4];
+        ld4(xb + (int64_t)t * xs, xc);
+        ld4(dyb + (int64_t)t * C, dv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = bs[j] + wk[j][0] * xw[0][j] + wk[j][1] * xw[1][j] + wk[j][2] * xw[2][j] + wk[j][3] * xc[j];
+          float gj = dv[j], post = a;
+          if (silu) {
+            const float sg = sigmoidf_(a);
+            post = a * sg;
+            gj *= sg * (1.f + a * (1.f - sg));
+          }
+          if (clip > 0.f && fabsf(post) > clip) gj = 0.f;
+          g[j] = gj;
+        }
+        if (t < own_end) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dbl[j] += g[j];
+            dwl[j][0] += g[j] * xw[0][j];
+            dwl[j][1] += g[j] * xw[1][j];
+            dwl[j][2] += g[j] * xw[2][j];
+            dwl[j][3] += g[j] * xc[j];
+          }
+        }
+      }
+      const int sx = t - 3;  // dx[s] = sum_k w_k dp[s + 3 - k]
+      if (sx >= t0) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = wk[j][0] * g[j] + wk[j][1] * dpw[2][j] + wk[j][2] * dpw[1][j] + wk[j][3] * dpw[0][j];
+        st4(dxb + (int64_t)sx * dxs, o);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xw[0][j] = xw[1][j];
+        xw[1][j] = xw[2][j];
+        xw[2][j] = xc[j];
+        dpw[0][j] = dpw[1][j];
+        dpw[1][j] = dpw[2][j];
+        dpw[2][j] = g[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) atomicAdd(&red[lane * 4 + j][k], dwl[j][k]);
+      atomicAdd(&red[lane * 4 + j][4], dbl[j]);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128 * 5; i += blockDim.x) {
+    const int ch = blockIdx.x * 128 + i / 5, k = i % 5;
+    const float v = (&red[0][0])[i];
+    if (k < 4) atomicAdd(dw + ch * 4 + k, v);
+    else if (db) atomicAdd(db + ch, v);
+  }
+}
+
 // ----------------------------------------------------------------- grad accumulate / embedding
 template <typename T>
 __global__ void accum_kernel(float* __restrict__ acc, const T* __restrict__ g, int64_t n, float scale) {
@@ -376,6 +549,17 @@ void ahb_colsum_add(const float* part, int nb, int D, float* out, cudaStream_t s
 
 void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,
                     int C, int dtype, int silu, float clip, cudaStream_t st) {
+  if (dtype == AHB_BF16 && C % 128 == 0 && xs % 4 == 0 && B > 0 && L > 0) {
+    const int64_t spans = (int64_t)B * ((L + CSPAN - 1) / CSPAN);
+    const dim3 grid(C / 128, (unsigned)((spans + 7) / 8));
+    if (wdtype == AHB_BF16)
+      conv1d_fwd_stream_kernel<bf16><<<grid, 256, 0, st>>>((const bf16*)x, xs, (const bf16*)w, bias, (bf16*)y, B, L,
+                                                           C, silu != 0, clip);
+    else
+      conv1d_fwd_stream_kernel<float><<<grid, 256, 0, st>>>((const bf16*)x, xs, (const float*)w, bias, (bf16*)y, B,
+                                                            L, C, silu != 0, clip);
+    return;
+  }
   int64_t n = (int64_t)B * ((L + CONV_TT - 1) / CONV_TT) * (C / 8);
   if (n == 0) return;
   unsigned blocks = (unsigned)((n + 127) / 128);
@@ -388,6 +572,19 @@ void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const 
 void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, const void* dy, void* dx,
                     float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
                     cudaStream_t st) {
+  if (dtype == AHB_BF16 && C % 128 == 0 && xs % 4 == 0 && B > 0 && L > 0) {
+    const int64_t spans = (int64_t)B * ((L + CSPAN - 1) / CSPAN);
+    const dim3 grid(C / 128, (unsigned)((spans + 7) / 8));
+    if (wdtype == AHB_BF16)
+      conv1d_bwd_stream_kernel<bf16><<<grid, 256, 0, st>>>((const bf16*)x, xs, (const bf16*)w, bias, (const bf16*)dy,
+                                                           (bf16*)dx, (int64_t)C, dw_acc, db_acc, B, L, C, silu != 0,
+                                                           clip);
+    else
+      conv1d_bwd_stream_kernel<float><<<grid, 256, 0, st>>>((const bf16*)x, xs, (const float*)w, bias,
+                                                            (const bf16*)dy, (bf16*)dx, (int64_t)C, dw_acc, db_acc, B,
+                                                            L, C, silu != 0, clip);
+    return;
+  }
   int64_t n = (int64_t)B * ((L + CONV_TT * CONV_SUB - 1) / (CONV_TT * CONV_SUB)) * (C / 8);
   if (n == 0) return;
   unsigned blocks = (unsigned)((n + 127) / 128);

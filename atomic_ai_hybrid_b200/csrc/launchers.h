@@ -140,6 +140,21 @@ void ahb_l2norm_heads_bwd(const void* dy, const void* x, const float* rn, void* 
 void ahb_dt_act_fwd(const void* u, void* dt, int64_t n, cudaStream_t st);
 void ahb_dt_act_bwd(const void* ddt, const void* u, void* du, int64_t n, cudaStream_t st);
 
+// router.cu: fused cosine router (fp32-exact logits on tensor cores, clip, noise, biased top-k, gate
+// softmax, aux/z statistics).  EP = ahb_router_padded_experts(E).
+int ahb_router_supported(int d, int E, int k);
+int ahb_router_padded_experts(int E);
+// knT3: (3, EP, d) bf16 = hi/mid/lo terms of kn^T (zero padded);
+// scal (5 floats, zero except scal[4] = +large): sum lse^2, max |pre-clip logit|, sum |x|, max |x|, min |x|
+void ahb_router_fwd(const void* x, const void* knT3, const float* temp, const float* bias, const float* noise,
+                    int64_t T, int d, int E, int k, float* logits, float* cosv, float* rn, int64_t* top_idx,
+                    float* gate, float* probs_sum, float* scal, float* counts, cudaStream_t st);
+// kn2: (2, d, EP) bf16 = hi/mid terms of kn; dcos: (T, EP) fp32 scratch; dtemp and dkn (d, E) accumulate
+void ahb_router_bwd(const void* x, const void* kn2, const float* temp, const float* logits, const float* cosv,
+                    const float* rn, const int64_t* top_idx, const float* gate, const float* dgate, const float* dps,
+                    const float* dlse_sq, int64_t T, int d, int E, int k, float* dcos, float* dtemp, void* dx,
+                    float* dkn, cudaStream_t st);
+
 // comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
 int ahb_ipc_alloc(int64_t nbytes, void** ptr);
 int ahb_ipc_free(void* ptr);

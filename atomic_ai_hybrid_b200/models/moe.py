@@ -68,6 +68,10 @@ class MoE(nn.Module):
     # ------------------------------------------------------------------ router
     def route(self, flat_x: torch.Tensor, stats: Dict[str, torch.Tensor]):
         E, k = self.E, self.k
+        if ops.use_cuda(flat_x) and flat_x.dtype == torch.bfloat16:
+            from ..ops import kernels as K
+            if K.router_supported(flat_x.shape[1], E, k):
+                return self._route_fused(flat_x, stats)
         xr = ops.grad_sanitize(flat_x).float()
         nrm = xr.norm(dim=1)
         stats["norm_x_mean"] = nrm.mean().detach()
@@ -97,6 +101,39 @@ class MoE(nn.Module):
         mean_probs = dp_mean(probs.mean(0))  # batch-global, as the reference's GSPMD mean
         stats["aux_loss"] = E * (mean_probs * mean_probs).sum()
         stats["z_loss"] = torch.logsumexp(logits, -1).square().mean()
+        stats["expert_utilization"] = mean_probs.detach()
+        stats["router_temp"] = self.router_temp.detach().float()
+        stats["expert_bias"] = self.expert_bias.detach().float()
+        stats["moe_dropped_ratio"] = torch.zeros((), device=flat_x.device)
+        return top_idx, gate
+
+    def _route_fused(self, flat_x: torch.Tensor, stats: Dict[str, torch.Tensor]):
+        """Same router with the (T, d) work in one sm_100a kernel (``ops.kernels.router``):
+        the (d, E) column normalisation, Gram statistics and loss reductions stay here."""
+        from ..ops import kernels as K
+        E, k = self.E, self.k
+        T = flat_x.shape[0]
+        kern = self.router.float()
+        kn = kern * torch.rsqrt((kern * kern).sum(0, keepdim=True) + 1e-6)
+        gram = kn.t() @ kn
+        eye = torch.eye(E, device=gram.device, dtype=gram.dtype)
+        stats["router_collinearity"] = ((gram - eye).square() * (1 - eye)).sum() / (E * (E - 1))
+        stats["router_max_cos"] = (gram - eye).abs().max().detach()
+        temp = self.router_temp.float().clamp(1.0, 15.0).reshape(1)
+        noise = None
+        if self.training and self.cfg.router_noise_std > 0:
+            noise = self.cfg.router_noise_std * torch.randn(T, E, device=flat_x.device)
+        gate, psum, lse_sq, top_idx, counts, scal = K.router(flat_x, kn, temp, self.expert_bias.detach().float(),
+                                                             noise, k)
+        stats["norm_x_mean"] = (scal[2] / T).detach()
+        stats["norm_x_max"] = scal[3].detach()
+        stats["norm_x_min"] = scal[4].detach()
+        stats["max_abs_logit_preclip"] = scal[1].detach()
+        stats["min_col_norm"] = kern.square().sum(0).sqrt().min().detach()
+        stats["assignment_frac"] = (counts / (T * k)).detach()
+        mean_probs = dp_mean(psum / T)  # batch-global, as the reference's GSPMD mean
+        stats["aux_loss"] = E * (mean_probs * mean_probs).sum()
+        stats["z_loss"] = lse_sq.reshape(()) / T
         stats["expert_utilization"] = mean_probs.detach()
         stats["router_temp"] = self.router_temp.detach().float()
         stats["expert_bias"] = self.expert_bias.detach().float()

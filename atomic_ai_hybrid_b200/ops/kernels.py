@@ -382,6 +382,35 @@ def dt_act(u):
     return _DtAct.apply(u.contiguous())
 
 
+class _Router(torch.autograd.Function):
+    """Fused cosine router: returns the differentiable (gate, sum_t softmax(l),
+    sum_t lse^2) and the non-differentiable (top_idx, expert counts, statistics)."""
+
+    @staticmethod
+    def forward(ctx, x, kn, temp, bias, noise, k):
+        logits, cosv, rn, top, gate, psum, scal, counts = ext().router_fwd(x, kn, temp, bias, noise, k)
+        ctx.save_for_backward(x, kn, temp, logits, cosv, rn, top, gate)
+        ctx.mark_non_differentiable(top, counts, scal)
+        return gate, psum, scal[0:1].clone(), top, counts, scal
+
+    @staticmethod
+    def backward(ctx, dgate, dpsum, dlse, _dtop, _dcounts, _dscal):
+        x, kn, temp, logits, cosv, rn, top, gate = ctx.saved_tensors
+        dgate = torch.zeros_like(gate) if dgate is None else dgate
+        dpsum = torch.zeros(logits.shape[1], device=x.device) if dpsum is None else dpsum
+        dx, dkn, dtemp = ext().router_bwd(x, kn, temp, logits, cosv, rn, top, gate, dgate, dpsum, dlse)
+        return dx, dkn, dtemp.view(temp.shape), None, None, None
+
+
+def router_supported(d: int, E: int, k: int) -> bool:
+    return bool(ext().router_supported(d, E, k))
+
+
+def router(x, kn, temp, bias, noise, k: int):
+    """``x (T, d)`` bf16, ``kn (d, E)`` unit-column router kernel, ``temp (1,)``."""
+    return _Router.apply(x.contiguous(), kn, temp, bias, noise, k)
+
+
 def gdn2_layer(mod, x):
     if x.dtype == torch.bfloat16 and mod.d_head == 128 and row_fusable(x.shape[-1]):
         return _gdn2_layer_fused(mod, x)

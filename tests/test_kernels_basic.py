@@ -74,3 +74,31 @@ def test_sanitize_and_embedding():
     ref = torch.zeros_like(emb)
     ref.index_add_(0, ids.reshape(-1), torch.ones(21, 64, device=dev))
     torch.testing.assert_close(emb.grad, ref)
+
+
+@pytest.mark.parametrize("silu,clip,wdt", [(True, 0.0, torch.bfloat16), (True, 50.0, torch.float32),
+                                           (False, 0.0, torch.bfloat16)])
+def test_conv1d_streaming_bf16_fwd_bwd(silu, clip, wdt):
+    """bf16 activations with C % 128 == 0 take the streaming kernels (spans of 64 steps)."""
+    torch.manual_seed(3)
+    B, L, C = 2, 203, 256
+    xz = (torch.randn(B, L, 2 * C, device=dev) * 3).to(torch.bfloat16)
+    x = xz[..., C:]  # strided rows
+    w = (0.5 * torch.randn(C, 4, device=dev)).to(wdt).requires_grad_(True)
+    b = (0.1 * torch.randn(C, device=dev)).requires_grad_(True)
+    xk = xz.clone().requires_grad_(True)
+    y = K.conv1d(xk[..., C:], w, b, silu, clip if clip else None)
+    xr = x.float().clone().requires_grad_(True)
+    w2 = w.detach().float().clone().requires_grad_(True)
+    b2 = b.detach().clone().requires_grad_(True)
+    y2 = R.causal_conv1d(xr, w2, b2, silu)
+    if clip:
+        y2 = y2.clamp(-clip, clip)
+    torch.testing.assert_close(y.float(), y2, atol=3e-2, rtol=2e-2)
+    dy = torch.randn(B, L, C, device=dev).to(torch.bfloat16)
+    y.backward(dy)
+    y2.backward(dy.float())
+    torch.testing.assert_close(xk.grad[..., C:].float(), xr.grad, atol=3e-2, rtol=2e-2)
+    assert not xk.grad[..., :C].any()
+    torch.testing.assert_close(w.grad.float(), w2.grad, atol=0.5, rtol=2e-2)
+    torch.testing.assert_close(b.grad, b2.grad, atol=0.5, rtol=2e-2)

@@ -196,3 +196,37 @@ def test_saved_scan_intermediates_match_recompute(op, monkeypatch):
         grads[recompute] = [t.grad.float() for t in ts]
     for a, r in zip(grads[False], grads[True]):  # equal up to atomics' summation order
         torch.testing.assert_close(a, r, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("E,k,d", [(32, 4, 2048), (8, 2, 256), (64, 6, 512)])
+def test_fused_router_matches_torch(E, k, d, monkeypatch):
+    """Fused router kernel vs the PyTorch router: selection, gates, statistics, gradients."""
+    from atomic_ai_hybrid_b200 import get_preset, ops
+    from atomic_ai_hybrid_b200.models.moe import MoE
+    ops.set_impl("cuda")
+    cfg = get_preset("hybrid_1b", d_model=d, n_routed_experts=E, top_k=k, router_noise_std=0.0)
+    torch.manual_seed(6)
+    moe = MoE(cfg).to(DEV)
+    moe.expert_bias.data = torch.randn(E, device=DEV) * 0.05
+    x = (torch.randn(700, d, device=DEV) * 2).to(torch.bfloat16)
+    res = {}
+    for fused in (True, False):
+        monkeypatch.setattr(K, "router_supported", lambda *a, f=fused: f)
+        moe.zero_grad(set_to_none=True)
+        xx = x.clone().requires_grad_(True)
+        st = {}
+        top, gate = moe.route(xx, st)
+        wg = torch.linspace(0.5, 1.5, gate.numel(), device=DEV).view_as(gate)
+        loss = (gate * wg).sum() + 3.0 * st["aux_loss"] + 0.5 * st["z_loss"] + st["router_collinearity"]
+        loss.backward()
+        res[fused] = (top, gate.detach(), {kk: v.detach().float() for kk, v in st.items()}, xx.grad.float(),
+                      moe.router.grad.clone(), moe.router_temp.grad.clone())
+    (t1, g1, s1, dx1, dr1, dt1), (t0, g0, s0, dx0, dr0, dt0) = res[True], res[False]
+    assert torch.equal(t1, t0)
+    _close(g1, g0, 1e-4, 1e-5, "gate")
+    for kk in ("aux_loss", "z_loss", "norm_x_mean", "norm_x_max", "norm_x_min", "max_abs_logit_preclip",
+               "assignment_frac", "expert_utilization"):
+        _close(s1[kk], s0[kk], 1e-4, 1e-4, kk)
+    _close(dx1, dx0, 2e-2, 1e-4, "dx")
+    _close(dr1, dr0, 1e-3, 1e-5, "drouter")
+    _close(dt1, dt0, 1e-3, 1e-6, "dtemp")
