@@ -407,7 +407,7 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
   const int T = (int)x.size(0), d = (int)x.size(1), k = (int)top_idx.size(1);
   const int E = (int)w1.size(0), F = (int)w1.size(2);
   TORCH_CHECK(d % 256 == 0 && F % 256 == 0, "moe: d_model and d_ff must be multiples of 256");
-  TORCH_CHECK(E <= 47, "moe: at most 47 routed experts per kernel call");
+  TORCH_CHECK(E <= 192 && k <= 8, "moe: at most 192 routed experts and top-8 per kernel call");
   auto dev = x.device();
   auto i32 = torch::dtype(torch::kInt32).device(dev);
   auto eidx = top_idx.t().contiguous().to(torch::kInt32);

@@ -82,39 +82,83 @@ __global__ void moe_gather_kernel(const bf16* __restrict__ x, const int* __restr
   for (int c = lane; c < d / 8; c += 32) dst[c] = src >= 0 ? s[c] : make_uint4(0, 0, 0, 0);
 }
 
-// out[t] = sanitize(shared[t] + sanitize(sum_j gate[t,j] * sanitize(ys[pos[j*T+t]], 1e3)?), 1e3)
-// routed rows are clipped +-1e3 (reference sanitize after the second gmm), the sum is clipped again.
+// One token per CTA, d/8 threads, 16-byte vectors (8 bf16 channels per thread).
+AHB_DEVICE void ld8f(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+AHB_DEVICE void st8f(bf16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// out[t] = sanitize(shared[t] + sum_j gate[t,j] * sanitize(ys[pos[j*T+t]], 1e3), 1e3):
+// routed rows are clipped +-1e3 (reference sanitize after the second gmm), the sum again.
 __global__ void moe_combine_kernel(const bf16* __restrict__ ys, const int* __restrict__ pos, const float* __restrict__ gate,
                                    const bf16* __restrict__ shared, int T, int k, int d, bf16* __restrict__ out) {
   const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int p = pos[(int64_t)j * T + t];
-      acc += gate[(int64_t)t * k + j] * sanitize(__bfloat162float(ys[(int64_t)p * d + c]), 1e3f);
-    }
-    if (shared) acc += __bfloat162float(shared[(int64_t)t * d + c]);
-    out[(int64_t)t * d + c] = __float2bfloat16_rn(sanitize(acc, 1e3f));
-  }
-}
-
-// dys[pos[a]] = gate[a] * dout[t];  dgate[t,j] = <dout[t], ys[pos[a]]>
-__global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ ys,
-                                       const int* __restrict__ pos, const float* __restrict__ gate, int T, int k,
-                                       int d, bf16* __restrict__ dys, float* __restrict__ dgate) {
-  __shared__ float sh[32];
-  const int t = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int j = 0; j < k; ++j) {
     const int p = pos[(int64_t)j * T + t];
     const float g = gate[(int64_t)t * k + j];
+    float v[8];
+    ld8f(ys + (int64_t)p * d + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += g * sanitize(v[i], 1e3f);
+  }
+  if (shared) {
+    float v[8];
+    ld8f(shared + (int64_t)t * d + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += v[i];
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = sanitize(acc[i], 1e3f);
+  st8f(out + (int64_t)t * d + c, acc);
+}
+
+// dys[pos[a]] = gate[a] * dout[t];  dgate[t,j] = <dout[t], sanitize(ys[pos[a]])>
+__global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ ys,
+                                       const int* __restrict__ pos, const float* __restrict__ gate, int T, int k,
+                                       int d, bf16* __restrict__ dys, float* __restrict__ dgate) {
+  __shared__ float sh[32][8];
+  const int t = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float dv[8];
+  ld8f(dout + (int64_t)t * d + c, dv);
+  float dots[8];
+  for (int j = 0; j < k; ++j) {
+    const int p = pos[(int64_t)j * T + t];
+    const float g = gate[(int64_t)t * k + j];
+    float yv[8], o[8];
+    ld8f(ys + (int64_t)p * d + c, yv);
     float dot = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-      const float dv = __bfloat162float(dout[(int64_t)t * d + c]);
-      dys[(int64_t)p * d + c] = __float2bfloat16_rn(g * dv);
-      dot += dv * sanitize(__bfloat162float(ys[(int64_t)p * d + c]), 1e3f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i] = g * dv[i];
+      dot += dv[i] * sanitize(yv[i], 1e3f);
     }
-    dot = block_sum(dot, sh);
-    if (threadIdx.x == 0) dgate[(int64_t)t * k + j] = dot;
+    st8f(dys + (int64_t)p * d + c, o);
+    dots[j] = warp_sum(dot);
+  }
+  if (lane == 0)
+    for (int j = 0; j < k; ++j) sh[w][j] = dots[j];
+  __syncthreads();
+  if (threadIdx.x < k) {
+    float s = 0.f;
+    for (int i = 0; i < nw; ++i) s += sh[i][threadIdx.x];
+    dgate[(int64_t)t * k + threadIdx.x] = s;
   }
 }
 
@@ -122,11 +166,15 @@ __global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dout, const bf16
 __global__ void moe_scatter_add_kernel(const bf16* __restrict__ dxs, const int* __restrict__ pos, int T, int k, int d,
                                        bf16* __restrict__ dx) {
   const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) acc += __bfloat162float(dxs[(int64_t)pos[(int64_t)j * T + t] * d + c]);
-    dx[(int64_t)t * d + c] = __float2bfloat16_rn(acc);
+  const int c = threadIdx.x * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < k; ++j) {
+    float v[8];
+    ld8f(dxs + (int64_t)pos[(int64_t)j * T + t] * d + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += v[i];
   }
+  st8f(dx + (int64_t)t * d + c, acc);
 }
 
 // zero the padding rows of a (R, d) bf16 matrix (rows with row_src < 0)
@@ -161,17 +209,17 @@ void ahb_moe_zero_pad(void* m, const int* row_src, int64_t R, int d, cudaStream_
 void ahb_moe_combine(const void* ys, const int* pos, const float* gate, const void* shared, int T, int k, int d,
                      void* out, cudaStream_t st) {
   if (!T) return;
-  moe_combine_kernel<<<T, 256, 0, st>>>((const bf16*)ys, pos, gate, (const bf16*)shared, T, k, d, (bf16*)out);
+  moe_combine_kernel<<<T, d / 8, 0, st>>>((const bf16*)ys, pos, gate, (const bf16*)shared, T, k, d, (bf16*)out);
 }
 
 void ahb_moe_combine_bwd(const void* dout, const void* ys, const int* pos, const float* gate, int T, int k, int d,
                          void* dys, float* dgate, cudaStream_t st) {
   if (!T) return;
-  moe_combine_bwd_kernel<<<T, 256, 0, st>>>((const bf16*)dout, (const bf16*)ys, pos, gate, T, k, d, (bf16*)dys,
+  moe_combine_bwd_kernel<<<T, d / 8, 0, st>>>((const bf16*)dout, (const bf16*)ys, pos, gate, T, k, d, (bf16*)dys,
                                             dgate);
 }
 
 void ahb_moe_scatter_add(const void* dxs, const int* pos, int T, int k, int d, void* dx, cudaStream_t st) {
   if (!T) return;
-  moe_scatter_add_kernel<<<T, 256, 0, st>>>((const bf16*)dxs, pos, T, k, d, (bf16*)dx);
+  moe_scatter_add_kernel<<<T, d / 8, 0, st>>>((const bf16*)dxs, pos, T, k, d, (bf16*)dx);
 }

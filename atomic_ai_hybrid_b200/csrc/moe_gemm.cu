@@ -34,7 +34,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB
 constexpr int B_BYTES = 256 * BK * 2;  // 32 KB (NB * BNacc = 256 columns)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 512;
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 1024;  // tile ring, alignment, barriers + offsets
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5 };
 
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* off = const_cast<int*>(reinterpret_cast<const int*>(tmem_slot + 2));  // E+1 ints (E <= 48)
+  int* off = const_cast<int*>(reinterpret_cast<const int*>(tmem_slot + 2));  // E+1 ints (E <= 192)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -401,7 +401,7 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
                  const void* aux1, float clip, int* err, int num_sms, cudaStream_t st, const float* alpha) {
-  if (E + 1 > 48 || N % 32 != 0 || K % 64 != 0) return -10;
+  if (E < 1 || E > 192 || N % 32 != 0 || K % 64 != 0) return -10;  // offsets live in the kernel's smem tail
   Params p;
   memset(&p, 0, sizeof(p));
   p.grp_off = grp_off;

@@ -45,7 +45,8 @@ def _moe_ref(x, top_idx, gate, w1, w2, w3, shared, act):
 
 
 @pytest.mark.parametrize("act", ["swiglu", "gelu"])
-@pytest.mark.parametrize("T,d,F,E,k", [(256, 256, 256, 4, 2), (1000, 512, 256, 8, 2), (512, 256, 512, 5, 3)])
+@pytest.mark.parametrize("T,d,F,E,k", [(256, 256, 256, 4, 2), (1000, 512, 256, 8, 2), (512, 256, 512, 5, 3),
+                                         (700, 256, 256, 64, 6)])
 def test_moe_forward_backward(act, T, d, F, E, k):
     ext().gemm_error_reset()
     torch.manual_seed(1)
