@@ -80,13 +80,14 @@ class CheckpointManager:
             stream.wait_stream(torch.cuda.current_stream())
         ctx = torch.cuda.stream(stream) if stream is not None else _null()
         with ctx:
-            for s in st.owned():
-                name = flax_path(s.name)
-                master = st.master_view(s)
-                params[name] = _to_host(master.to(reference_dtype(s.name)), dev)
-                o = s.offset - st.lo
-                moments[f"mu/{name}"] = _to_host(opt.m[o:o + s.numel].view(s.shape), dev)
-                moments[f"nu/{name}"] = _to_host(opt.v[o:o + s.numel].view(s.shape), dev)
+            for store, sopt, ep in _stores(trainer):
+                for s in store.owned():
+                    name = _key(s, ep)
+                    master = store.master_view(s)
+                    params[name] = _to_host(master.to(reference_dtype(s.name)), dev)
+                    o = s.offset - store.lo
+                    moments[f"mu/{name}"] = _to_host(sopt.m[o:o + s.numel].view(s.shape), dev)
+                    moments[f"nu/{name}"] = _to_host(sopt.v[o:o + s.numel].view(s.shape), dev)
         ev = None
         if stream is not None:
             ev = torch.cuda.Event()
@@ -94,7 +95,7 @@ class CheckpointManager:
         meta = dict(metadata or {})
         meta.update({"global_step": int(meta.get("global_step", step)), "opt_count": int(opt.count),
                      "world": self.world, "timestamp": time.time()})
-        labels = {flax_path(s.name): s.label for s in st.owned()}
+        labels = {_key(s, ep): s.label for store, _, ep in _stores(trainer) for s in store.owned()}
 
         def write():
             try:
@@ -167,30 +168,88 @@ class CheckpointManager:
         """Graft-merge restore into ``trainer``; returns the metadata plus
         ``restored``/``fresh`` name lists."""
         params, moments, meta = self.load_tensors(step)
-        st, opt = trainer.store, trainer.opt
         restored, fresh = [], []
         with torch.no_grad():
-            for s in st.segs:
-                name = flax_path(s.name)
-                t = params.get(name)
-                if t is None or tuple(t.shape) != tuple(s.shape):
-                    fresh.append(name)
-                    continue
-                t32 = t.to(device=st.device, dtype=torch.float32)
-                st.compute_view(s).copy_(t32)
-                if s.owner == st.rank:
-                    st.master_view(s).copy_(t32)
-                    o = s.offset - st.lo
-                    mu, nu = moments.get(f"mu/{name}"), moments.get(f"nu/{name}")
-                    if load_optimizer and mu is not None and tuple(mu.shape) == tuple(s.shape):
-                        opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(st.device))
-                        opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(st.device))
-                restored.append(name)
-        if load_optimizer:
-            opt.count = int(meta.get("opt_count", 0))
+            for st, opt, ep in _stores(trainer):
+                for s in st.segs:
+                    name = flax_path(s.name)
+                    rng = _expert_range(s, ep)
+                    t = _lookup(params, name, rng)
+                    if t is None or tuple(t.shape) != tuple(s.shape):
+                        fresh.append(name)
+                        continue
+                    t32 = t.to(device=st.device, dtype=torch.float32)
+                    st.compute_view(s).copy_(t32)
+                    if s.owner == st.rank:
+                        st.master_view(s).copy_(t32)
+                        o = s.offset - st.lo
+                        mu, nu = _lookup(moments, f"mu/{name}", rng), _lookup(moments, f"nu/{name}", rng)
+                        if load_optimizer and mu is not None and tuple(mu.shape) == tuple(s.shape):
+                            opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(st.device))
+                            opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(st.device))
+                    restored.append(name)
+                if load_optimizer:
+                    opt.count = int(meta.get("opt_count", 0))
         meta = dict(meta)
         meta["restored"], meta["fresh"] = restored, fresh
         return meta
+
+
+def _stores(trainer):
+    """(store, optimizer, expert_parallel) for the data-parallel store and, with
+    expert parallelism, the store of this rank's experts."""
+    yield trainer.store, trainer.opt, False
+    if getattr(trainer, "ep_store", None) is not None:
+        yield trainer.ep_store, trainer.ep_opt, True
+
+
+def _expert_range(s, ep: bool):
+    """Global expert rows [lo, hi) held by a segment of the expert-parallel store."""
+    if not ep:
+        return None
+    from ..parallel.context import get_parallel_context
+    El = s.shape[0]
+    lo = get_parallel_context().ep_rank * El
+    return lo, lo + El
+
+
+def _key(s, ep: bool) -> str:
+    """Tensor name in the files: the flax path, plus ``#experts[lo:hi]`` for a block of
+    routed experts held by one expert-parallel rank."""
+    name = flax_path(s.name)
+    rng = _expert_range(s, ep)
+    return name if rng is None else f"{name}#experts[{rng[0]}:{rng[1]}]"
+
+
+def _lookup(tensors: Dict[str, torch.Tensor], name: str, rng):
+    """The tensor ``name`` (rows ``rng`` of it when given), assembled from expert
+    blocks when the checkpoint was written with expert parallelism."""
+    t = tensors.get(name if rng is None else f"{name}#experts[{rng[0]}:{rng[1]}]")
+    if t is not None:
+        return t
+    full = tensors.get(name)
+    if full is not None:
+        return full if rng is None else full[rng[0]:rng[1]]
+    blocks = []
+    prefix = name + "#experts["
+    for key, v in tensors.items():
+        if key.startswith(prefix):
+            lo, hi = (int(x) for x in key[len(prefix):-1].split(":"))
+            blocks.append((lo, hi, v))
+    if not blocks:
+        return None
+    blocks.sort(key=lambda b: b[0])
+    n = max(b[1] for b in blocks)
+    lo, hi = rng if rng is not None else (0, n)
+    parts, cur = [], lo
+    for b_lo, b_hi, v in blocks:
+        if b_hi <= cur or b_lo >= hi:
+            continue
+        if b_lo > cur:
+            return None  # a gap: the checkpoint does not cover these experts
+        parts.append(v[cur - b_lo:min(hi, b_hi) - b_lo])
+        cur = min(hi, b_hi)
+    return torch.cat(parts, 0) if cur == hi else None
 
 
 def _to_host(t: torch.Tensor, dev: torch.device) -> torch.Tensor:

@@ -364,6 +364,8 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
   return {dx, ddt, dA, dB, dC};
 }
 
+static std::pair<void* const*, int> peer_table(const c10::optional<torch::Tensor>& t);
+
 // ------------------------------------------------------------ MoE (grouped GEMM on tcgen05)
 int num_sms() {
   static int n = 0;
@@ -397,6 +399,98 @@ torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b) {
   return c;
 }
 
+// Expert FFN on expert-grouped rows (segments of `off`, padded to 128 rows):
+// returns {a1, a3 (empty for GELU), h, ys}.
+static std::vector<torch::Tensor> moe_expert_fwd_impl(const torch::Tensor& xs, const torch::Tensor& off, int64_t R,
+                                                      const torch::Tensor& w1, const torch::Tensor& w2,
+                                                      const c10::optional<torch::Tensor>& w3, bool swiglu) {
+  const int d = (int)xs.size(1), E = (int)w1.size(0), F = (int)w1.size(2);
+  TORCH_CHECK(d % 256 == 0 && F % 256 == 0, "moe: d_model and d_ff must be multiples of 256");
+  TORCH_CHECK(E <= 192, "moe: at most 192 experts per call");
+  auto st = cur_stream();
+  auto h = torch::empty({R, F}, xs.options());
+  auto a1 = torch::empty_like(h);
+  torch::Tensor a3;
+  int* err = err_word().data_ptr<int>();
+  int rc;
+  if (swiglu) {
+    TORCH_CHECK(w3.has_value(), "moe: swiglu needs w3");
+    a3 = torch::empty_like(h);
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_SWIGLU, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), w3->data_ptr(),
+                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(),
+                      a3.data_ptr(), nullptr, nullptr, 1e3f, err, num_sms(), st);
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_GELU, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
+                      off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(), nullptr, nullptr, nullptr,
+                      1e3f, err, num_sms(), st);
+    a3 = torch::empty({0}, xs.options());
+  }
+  gemm_check(rc, "fwd up");
+  auto ys = torch::empty({R, d}, xs.options());
+  rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, h.data_ptr(), nullptr, R, F, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+                    off.data_ptr<int>(), E, d, 0, F, F / 64, ys.data_ptr(), nullptr, nullptr, nullptr, nullptr, 1e3f,
+                    err, num_sms(), st);
+  gemm_check(rc, "fwd down");
+  return {a1, a3, h, ys};
+}
+
+// Backward of the expert FFN from the row gradients dys (padding rows zero): weight
+// gradients are ADDED into dw*_acc; returns the row gradients dxs.
+static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::Tensor& off, const torch::Tensor& xs,
+                                         const torch::Tensor& a1, const torch::Tensor& a3, const torch::Tensor& h,
+                                         const torch::Tensor& w1, const torch::Tensor& w2,
+                                         const c10::optional<torch::Tensor>& w3, const torch::Tensor& dw1_acc,
+                                         const torch::Tensor& dw2_acc, const c10::optional<torch::Tensor>& dw3_acc,
+                                         bool swiglu) {
+  const int64_t R = xs.size(0);
+  const int d = (int)xs.size(1), E = (int)w1.size(0), F = (int)w1.size(2);
+  auto st = cur_stream();
+  check_acc(dw1_acc, w1.numel(), "dw1_acc");
+  check_acc(dw2_acc, w2.numel(), "dw2_acc");
+  int* err = err_word().data_ptr<int>();
+  auto dA1 = torch::empty({R, F}, xs.options());
+  torch::Tensor dA3;
+  int rc;
+  if (swiglu) {
+    dA3 = torch::empty_like(dA1);
+    rc = ahb_moe_gemm(AHB_GEMM_DH_SWIGLU, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d,
+                      F, off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), dA3.data_ptr(), nullptr,
+                      a1.data_ptr(), a3.data_ptr(), 0.f, err, num_sms(), st);
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_DH_GELU, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+                      off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), nullptr, nullptr, a1.data_ptr(),
+                      nullptr, 0.f, err, num_sms(), st);
+  }
+  gemm_check(rc, "dh");
+  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, h.data_ptr(), nullptr, R, F, dys.data_ptr(), nullptr, R, d, 0,
+                    off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
+                    0.f, err, num_sms(), st);
+  gemm_check(rc, "wgrad w2");
+  auto dxs = torch::empty({R, d}, xs.options());
+  if (swiglu) {
+    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), dA3.data_ptr(), R, F, w1.data_ptr(), w3->data_ptr(),
+                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, d, 0, 2 * F, F / 64, dxs.data_ptr(), nullptr,
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "dx");
+    TORCH_CHECK(dw3_acc.has_value(), "moe_bwd: dw3_acc");
+    check_acc(*dw3_acc, w3->numel(), "dw3_acc");
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), dA3.data_ptr(), R, F, 0,
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), dw3_acc->data_ptr<float>(),
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "wgrad w1/w3");
+  } else {
+    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), nullptr, R, F, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
+                      off.data_ptr<int>(), E, d, 0, F, F / 64, dxs.data_ptr(), nullptr, nullptr, nullptr, nullptr,
+                      0.f, err, num_sms(), st);
+    gemm_check(rc, "dx");
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), nullptr, R, F, 0,
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
+                      nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "wgrad w1");
+  }
+  return dxs;
+}
+
 // forward: returns {out, pos, off, row_src, xs, a1, a3, h, ys}
 std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch::Tensor gate, torch::Tensor w1,
                                    torch::Tensor w2, c10::optional<torch::Tensor> w3,
@@ -422,28 +516,8 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
   auto xs = torch::empty({Rcap, d}, x.options());
   ahb_moe_gather(x.data_ptr(), row_src.data_ptr<int>(), Rcap, d, xs.data_ptr(), st);
   check_launch("ahb_moe_gather");
-  auto h = torch::empty({Rcap, F}, x.options());
-  auto a1 = torch::empty_like(h);
-  torch::Tensor a3;
-  int* err = err_word().data_ptr<int>();
-  int rc;
-  if (swiglu) {
-    TORCH_CHECK(w3.has_value(), "moe: swiglu needs w3");
-    a3 = torch::empty_like(h);
-    rc = ahb_moe_gemm(AHB_GEMM_FWD_SWIGLU, xs.data_ptr(), nullptr, Rcap, d, w1.data_ptr(), w3->data_ptr(),
-                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(),
-                      a3.data_ptr(), nullptr, nullptr, 1e3f, err, num_sms(), st);
-  } else {
-    rc = ahb_moe_gemm(AHB_GEMM_FWD_GELU, xs.data_ptr(), nullptr, Rcap, d, w1.data_ptr(), nullptr, (int64_t)E * d, F,
-                      d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(), nullptr, nullptr,
-                      nullptr, 1e3f, err, num_sms(), st);
-  }
-  gemm_check(rc, "fwd up");
-  auto ys = torch::empty({Rcap, d}, x.options());
-  rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, h.data_ptr(), nullptr, Rcap, F, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
-                    off.data_ptr<int>(), E, d, 0, F, F / 64, ys.data_ptr(), nullptr, nullptr, nullptr, nullptr, 1e3f,
-                    err, num_sms(), st);
-  gemm_check(rc, "fwd down");
+  auto g = moe_expert_fwd_impl(xs, off, Rcap, w1, w2, w3, swiglu);
+  auto a1 = g[0], a3 = g[1], h = g[2], ys = g[3];
   auto out = torch::empty_like(x);
   const void* sh = nullptr;
   torch::Tensor shc;
@@ -453,7 +527,6 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
   }
   ahb_moe_combine(ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), sh, T, k, d, out.data_ptr(), st);
   check_launch("ahb_moe_combine");
-  if (!a3.defined()) a3 = torch::empty({0}, x.options());
   return {out, pos, off, row_src, xs, a1, a3, h, ys};
 }
 
@@ -464,13 +537,10 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
                                    torch::Tensor h, torch::Tensor ys, torch::Tensor dw1_acc, torch::Tensor dw2_acc,
                                    c10::optional<torch::Tensor> dw3_acc, bool swiglu) {
   const int T = (int)dout.size(0), d = (int)dout.size(1), k = (int)gate.size(1);
-  const int E = (int)w1.size(0), F = (int)w1.size(2);
   const int64_t Rcap = xs.size(0);
   auto st = cur_stream();
   auto doc = dout.to(at::kBFloat16).contiguous();
   auto gatec = gate.to(at::kFloat).contiguous();
-  check_acc(dw1_acc, w1.numel(), "dw1_acc");
-  check_acc(dw2_acc, w2.numel(), "dw2_acc");
   auto dys = torch::empty({Rcap, d}, xs.options());
   ahb_moe_zero_pad(dys.data_ptr(), row_src.data_ptr<int>(), Rcap, d, st);
   check_launch("ahb_moe_zero_pad");
@@ -478,51 +548,111 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
   ahb_moe_combine_bwd(doc.data_ptr(), ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), T, k, d,
                       dys.data_ptr(), dgate.data_ptr<float>(), st);
   check_launch("ahb_moe_combine_bwd");
-  int* err = err_word().data_ptr<int>();
-  auto dA1 = torch::empty({Rcap, F}, xs.options());
-  torch::Tensor dA3;
-  int rc;
-  if (swiglu) {
-    dA3 = torch::empty_like(dA1);
-    rc = ahb_moe_gemm(AHB_GEMM_DH_SWIGLU, dys.data_ptr(), nullptr, Rcap, d, w2.data_ptr(), nullptr, (int64_t)E * F, d,
-                      F, off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), dA3.data_ptr(), nullptr,
-                      a1.data_ptr(), a3.data_ptr(), 0.f, err, num_sms(), st);
-  } else {
-    rc = ahb_moe_gemm(AHB_GEMM_DH_GELU, dys.data_ptr(), nullptr, Rcap, d, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
-                      off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), nullptr, nullptr, a1.data_ptr(),
-                      nullptr, 0.f, err, num_sms(), st);
-  }
-  gemm_check(rc, "dh");
-  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, h.data_ptr(), nullptr, Rcap, F, dys.data_ptr(), nullptr, Rcap, d, 0,
-                    off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
-                    0.f, err, num_sms(), st);
-  gemm_check(rc, "wgrad w2");
-  auto dxs = torch::empty({Rcap, d}, xs.options());
-  if (swiglu) {
-    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), dA3.data_ptr(), Rcap, F, w1.data_ptr(), w3->data_ptr(),
-                      (int64_t)E * d, F, d, off.data_ptr<int>(), E, d, 0, 2 * F, F / 64, dxs.data_ptr(), nullptr,
-                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
-    gemm_check(rc, "dx");
-    TORCH_CHECK(dw3_acc.has_value(), "moe_bwd: dw3_acc");
-    check_acc(*dw3_acc, w3->numel(), "dw3_acc");
-    rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL, xs.data_ptr(), nullptr, Rcap, d, dA1.data_ptr(), dA3.data_ptr(), Rcap, F, 0,
-                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), dw3_acc->data_ptr<float>(),
-                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
-    gemm_check(rc, "wgrad w1/w3");
-  } else {
-    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), nullptr, Rcap, F, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
-                      off.data_ptr<int>(), E, d, 0, F, F / 64, dxs.data_ptr(), nullptr, nullptr, nullptr, nullptr,
-                      0.f, err, num_sms(), st);
-    gemm_check(rc, "dx");
-    rc = ahb_moe_gemm(AHB_GEMM_WGRAD, xs.data_ptr(), nullptr, Rcap, d, dA1.data_ptr(), nullptr, Rcap, F, 0,
-                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
-                      nullptr, 0.f, err, num_sms(), st);
-    gemm_check(rc, "wgrad w1");
-  }
+  auto dxs = moe_expert_bwd_impl(dys, off, xs, a1, a3, h, w1, w2, w3, dw1_acc, dw2_acc, dw3_acc, swiglu);
   auto dx = torch::empty({T, d}, xs.options());
   ahb_moe_scatter_add(dxs.data_ptr(), pos.data_ptr<int>(), T, k, d, dx.data_ptr(), st);
   check_launch("ahb_moe_scatter_add");
   return {dx, dgate};
+}
+
+// ------------------------------------------------------------ expert parallelism (ep.cu + the expert FFN)
+// Local routing of this rank's assignments: {eidx (k*T, order a = j*T + t), counts (E), off (E+1, segments
+// padded to 128), pos (k*T: off[e] + stable rank of a among the assignments to e)}
+std::vector<torch::Tensor> moe_route_local(torch::Tensor top_idx, int64_t E) {
+  const int T = (int)top_idx.size(0), k = (int)top_idx.size(1);
+  auto i32 = torch::dtype(torch::kInt32).device(top_idx.device());
+  auto eidx = top_idx.t().contiguous().to(torch::kInt32);
+  const int64_t Rcap = ((int64_t)T * k + E * 128 + 127) / 128 * 128;
+  auto counts = torch::empty({E}, i32), off = torch::empty({E + 1}, i32);
+  auto pos = torch::empty({(int64_t)T * k}, i32), row_src = torch::empty({Rcap}, i32);
+  ahb_moe_route(eidx.data_ptr<int>(), T, k, (int)E, counts.data_ptr<int>(), off.data_ptr<int>(), pos.data_ptr<int>(),
+                row_src.data_ptr<int>(), Rcap, cur_stream());
+  check_launch("ahb_moe_route");
+  return {eidx, counts, off, pos};
+}
+
+void ep_publish(torch::Tensor counts, torch::Tensor peers, int64_t rank) {
+  auto pt = peer_table(peers);
+  ahb_ep_publish(counts.data_ptr<int>(), (int)counts.numel(), reinterpret_cast<int* const*>(pt.first), pt.second,
+                 (int)rank, cur_stream());
+  check_launch("ahb_ep_publish");
+}
+
+// src: x (T, d) when src_by_token, else rows (k*T, d) in assignment order
+void ep_dispatch(torch::Tensor src, bool src_by_token, int64_t T, int64_t k, torch::Tensor eidx, torch::Tensor pos,
+                 torch::Tensor off, torch::Tensor dst_base, int64_t El, torch::Tensor recv_peers,
+                 c10::optional<torch::Tensor> meta_peers, int64_t rank, c10::optional<torch::Tensor> dst_pos) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.is_contiguous() && src.size(1) % 8 == 0,
+              "ep_dispatch: bf16 rows");
+  auto rp = peer_table(recv_peers);
+  auto mp = peer_table(meta_peers);
+  ahb_ep_dispatch(src.data_ptr(), src_by_token ? 1 : 0, (int)T, (int)k, (int)src.size(1), eidx.data_ptr<int>(),
+                  pos.data_ptr<int>(), off.data_ptr<int>(), dst_base.data_ptr<int>(), (int)El, rp.first, mp.first,
+                  (int)rank, dst_pos.has_value() && dst_pos->defined() ? dst_pos->data_ptr<int>() : nullptr,
+                  cur_stream());
+  check_launch("ahb_ep_dispatch");
+}
+
+void ep_return(torch::Tensor rows, torch::Tensor meta, int64_t R, torch::Tensor ret_peers) {
+  auto pt = peer_table(ret_peers);
+  ahb_ep_return(rows.data_ptr(), meta.data_ptr(), R, (int)rows.size(1), pt.first, cur_stream());
+  check_launch("ahb_ep_return");
+}
+
+void ep_zero_pad(torch::Tensor rows, c10::optional<torch::Tensor> meta, torch::Tensor off, torch::Tensor seg) {
+  ahb_ep_zero_pad(rows.data_ptr(), meta.has_value() && meta->defined() ? meta->data_ptr() : nullptr,
+                  off.data_ptr<int>(), seg.data_ptr<int>(), (int)seg.numel(), (int)rows.size(1), cur_stream());
+  check_launch("ahb_ep_zero_pad");
+}
+
+std::vector<torch::Tensor> moe_expert_fwd(torch::Tensor xs, torch::Tensor off, torch::Tensor w1, torch::Tensor w2,
+                                          c10::optional<torch::Tensor> w3, bool swiglu) {
+  return moe_expert_fwd_impl(xs, off, xs.size(0), w1, w2, w3, swiglu);
+}
+
+torch::Tensor moe_expert_bwd(torch::Tensor dys, torch::Tensor off, torch::Tensor xs, torch::Tensor a1,
+                             torch::Tensor a3, torch::Tensor h, torch::Tensor w1, torch::Tensor w2,
+                             c10::optional<torch::Tensor> w3, torch::Tensor dw1_acc, torch::Tensor dw2_acc,
+                             c10::optional<torch::Tensor> dw3_acc, bool swiglu) {
+  return moe_expert_bwd_impl(dys, off, xs, a1, a3, h, w1, w2, w3, dw1_acc, dw2_acc, dw3_acc, swiglu);
+}
+
+// rows (k*T, d) in assignment order: out[t] = sanitize(shared[t] + sum_j gate[t,j] sanitize(rows[j*T+t]))
+torch::Tensor moe_combine_rows(torch::Tensor rows, torch::Tensor gate, c10::optional<torch::Tensor> shared) {
+  const int T = (int)gate.size(0), k = (int)gate.size(1), d = (int)rows.size(1);
+  auto ident = torch::arange(0, (int64_t)T * k, rows.options().dtype(at::kInt));
+  auto gatec = gate.to(at::kFloat).contiguous();
+  auto out = torch::empty({T, d}, rows.options());
+  torch::Tensor shc;
+  if (shared.has_value() && shared->defined()) shc = shared->to(at::kBFloat16).contiguous();
+  ahb_moe_combine(rows.data_ptr(), ident.data_ptr<int>(), gatec.data_ptr<float>(),
+                  shc.defined() ? shc.data_ptr() : nullptr, T, k, d, out.data_ptr(), cur_stream());
+  check_launch("ahb_moe_combine");
+  return out;
+}
+
+// {drows (k*T, d), dgate (T, k)}
+std::vector<torch::Tensor> moe_combine_rows_bwd(torch::Tensor dout, torch::Tensor rows, torch::Tensor gate) {
+  const int T = (int)gate.size(0), k = (int)gate.size(1), d = (int)rows.size(1);
+  auto ident = torch::arange(0, (int64_t)T * k, rows.options().dtype(at::kInt));
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  auto gatec = gate.to(at::kFloat).contiguous();
+  auto drows = torch::empty_like(rows);
+  auto dgate = torch::empty({T, k}, gatec.options());
+  ahb_moe_combine_bwd(doc.data_ptr(), rows.data_ptr(), ident.data_ptr<int>(), gatec.data_ptr<float>(), T, k, d,
+                      drows.data_ptr(), dgate.data_ptr<float>(), cur_stream());
+  check_launch("ahb_moe_combine_bwd");
+  return {drows, dgate};
+}
+
+// dx[t] = sum_j rows[j*T+t]
+torch::Tensor moe_sum_rows(torch::Tensor rows, int64_t T, int64_t k) {
+  const int d = (int)rows.size(1);
+  auto ident = torch::arange(0, T * k, rows.options().dtype(at::kInt));
+  auto dx = torch::empty({T, d}, rows.options());
+  ahb_moe_scatter_add(rows.data_ptr(), ident.data_ptr<int>(), (int)T, (int)k, d, dx.data_ptr(), cur_stream());
+  check_launch("ahb_moe_scatter_add");
+  return dx;
 }
 
 // ------------------------------------------------------------ fused optimizer
@@ -998,6 +1128,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_supported", &router_supported);
   m.def("router_fwd", &router_fwd);
   m.def("router_bwd", &router_bwd);
+  m.def("moe_route_local", &moe_route_local);
+  m.def("ep_publish", &ep_publish);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_return", &ep_return);
+  m.def("ep_zero_pad", &ep_zero_pad);
+  m.def("moe_expert_fwd", &moe_expert_fwd);
+  m.def("moe_expert_bwd", &moe_expert_bwd);
+  m.def("moe_combine_rows", &moe_combine_rows);
+  m.def("moe_combine_rows_bwd", &moe_combine_rows_bwd);
+  m.def("moe_sum_rows", &moe_sum_rows);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

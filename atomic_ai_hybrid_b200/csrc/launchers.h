@@ -155,6 +155,14 @@ void ahb_router_bwd(const void* x, const void* kn2, const float* temp, const flo
                     const float* dlse_sq, int64_t T, int d, int E, int k, float* dcos, float* dtemp, void* dx,
                     float* dkn, cudaStream_t st);
 
+// ep.cu: expert-parallel token exchange over peer memory
+void ahb_ep_publish(const int* counts, int E, int* const* peers_dev, int W, int rank, cudaStream_t st);
+void ahb_ep_dispatch(const void* src, int src_by_token, int T, int k, int d, const int* eidx, const int* pos_local,
+                     const int* off_local, const int* dst_base, int El, void* const* recv_peers,
+                     void* const* meta_peers, int rank, int* dst_pos, cudaStream_t st);
+void ahb_ep_return(const void* rows, const void* meta, int64_t R, int d, void* const* ret_peers, cudaStream_t st);
+void ahb_ep_zero_pad(void* rows, void* meta, const int* off, const int* seg, int El, int d, cudaStream_t st);
+
 // comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
 int ahb_ipc_alloc(int64_t nbytes, void** ptr);
 int ahb_ipc_free(void* ptr);

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
-from ..parallel.context import dp_mean
+from ..parallel.context import dp_mean, get_parallel_context
 from .layers import Dense, lecun_normal_
 
 ROUTER_LOGIT_CLIP = 8.0
@@ -54,16 +54,26 @@ class MoE(nn.Module):
         lecun_normal_(self.router.data, d)
         self.router_temp = nn.Parameter(torch.tensor(ROUTER_TEMP_INIT))
         self.expert_bias = nn.Parameter(torch.zeros(E), requires_grad=False)
-        # Routed expert weights are bf16 in the reference's parameter tree.
-        self.routed_w1 = nn.Parameter(torch.empty(E, d, F_))
-        self.routed_w2 = nn.Parameter(torch.empty(E, F_, d))
+        # Routed expert weights are bf16 in the reference's parameter tree.  With expert
+        # parallelism this rank holds experts [ep_rank * El, (ep_rank + 1) * El) only.
+        pc = get_parallel_context()
+        self.ep_world, self.ep_rank = pc.ep_world, pc.ep_rank
+        if E % self.ep_world:
+            raise ValueError(f"{E} routed experts do not split over {self.ep_world} expert-parallel ranks")
+        El = E // self.ep_world
+        self.routed_w1 = nn.Parameter(torch.empty(El, d, F_))
+        self.routed_w2 = nn.Parameter(torch.empty(El, F_, d))
         lecun_normal_(self.routed_w1.data, d)
         lecun_normal_(self.routed_w2.data, F_)
         if self.swiglu:
-            self.routed_w3 = nn.Parameter(torch.empty(E, d, F_))
+            self.routed_w3 = nn.Parameter(torch.empty(El, d, F_))
             lecun_normal_(self.routed_w3.data, d)
         else:
             self.routed_w3 = None
+        if self.ep_world > 1:
+            for w in (self.routed_w1, self.routed_w2, self.routed_w3):
+                if w is not None:
+                    w._ahb_ep_local = True
 
     # ------------------------------------------------------------------ router
     def route(self, flat_x: torch.Tensor, stats: Dict[str, torch.Tensor]):
@@ -156,6 +166,14 @@ class MoE(nn.Module):
         flat = x.reshape(-1, d)
         top_idx, gate = self.route(flat, stats)
         shared = self._shared(flat) if self.n_shared > 0 else None
+        if self.ep_world > 1:
+            ep = get_parallel_context().ep
+            if ep is None:
+                raise RuntimeError("expert-parallel MoE needs the EPGroup (parallel.ep) in the parallel context")
+            from ..parallel.ep import moe_forward_ep
+            out = moe_forward_ep(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3, shared,
+                                 "swiglu" if self.swiglu else "gelu", ep)
+            return out.view(Bsz, L, d)
         # the grouped GEMM tiles need d_model and d_ff in multiples of 256
         if ops.use_cuda(flat) and x.dtype == torch.bfloat16 and d % 256 == 0 and self.cfg.d_ff % 256 == 0:
             from ..ops import kernels as K

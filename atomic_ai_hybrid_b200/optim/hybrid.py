@@ -62,6 +62,8 @@ class HybridOptimizer:
         self.group_idx = {g: i for i, g in enumerate(DIAG_GROUPS)}
         # (gradient peer table, compute peer table): set by a peer-memory shard comm
         self.peers = None
+        # optimizers of further stores stepped together with this one (shared norm / clip)
+        self.partners: list = []
 
     def uses_kernels(self) -> bool:
         gbuf = self.store.grad
@@ -85,42 +87,63 @@ class HybridOptimizer:
     # -------------------------------------------------------------- the step
     @torch.no_grad()
     def step(self, n_accum: int, assignment_frac: Optional[torch.Tensor] = None) -> Dict[str, torch.Tensor]:
-        st = self.store
-        dev = st.device
+        """One optimizer step.  ``partners`` (optimizers of other parameter stores,
+        e.g. the expert-parallel experts) share the global norm, the clip coefficient
+        and the non-finite flags with this one: their statistics are added to this
+        optimizer's before the single cross-rank reduction."""
         ng = len(DIAG_GROUPS)
         # one small vector reduced across ranks: [sumsq(avg), sumsq(g), was_clipped, flags...]
-        red = torch.zeros(3 + ng, dtype=torch.float32, device=dev)
-        gbuf = st.grad[st.lo:st.hi]
-        inv = 1.0 / float(n_accum)
-        use_k = self.uses_kernels()
-        if use_k:
-            from ..ops import kernels as K
-            K.optim_prepare(self, inv, red)
-        else:
-            for s in self.owned:
-                if not s.param.requires_grad:
-                    continue
-                sl = self._sl(s)
-                avg = gbuf[sl] * inv
-                red[0] += avg.double().square().sum().float()
-                if not torch.isfinite(avg).all():
-                    red[3 + self.group_idx[diag_group_of(s.name)]] = 1.0
-                g = torch.nan_to_num(avg, nan=0.0, posinf=0.0, neginf=0.0) * s.grad_scale
-                gbuf[sl] = g
-                red[1] += g.double().square().sum().float()
-            for s in self.owned:
-                if (st.master_view(s).abs() >= PARAM_CLIP).any():
-                    red[2] = 1.0
+        red = torch.zeros(3 + ng, dtype=torch.float32, device=self.store.device)
+        self._prepare(n_accum, red)
+        for p in self.partners:
+            p._prepare(n_accum, red)
         red = self.reduce_fn(red)
         global_norm = red[0].sqrt()
         is_finite = torch.isfinite(global_norm)
         clip_norm = red[1].sqrt()
         coef = torch.where(clip_norm < GLOBAL_CLIP, torch.ones_like(clip_norm), GLOBAL_CLIP / clip_norm)
         if self.skip_nonfinite and not bool(is_finite):
-            self.count += 0
             return self._info(global_norm, is_finite, red, skipped=True)
+        for opt in [self] + list(self.partners):
+            opt._finish(coef, assignment_frac)
+        return self._info(global_norm, is_finite, red, skipped=False)
+
+    def _prepare(self, n_accum: int, red: torch.Tensor) -> None:
+        """Average, non-finite flags, nan_to_num, per-tensor gradient scales and both
+        squared norms of the owned gradients, added into ``red``."""
+        st = self.store
+        gbuf = st.grad[st.lo:st.hi]
+        inv = 1.0 / float(n_accum)
+        if self.uses_kernels():
+            from ..ops import kernels as K
+            part = torch.zeros_like(red)
+            K.optim_prepare(self, inv, part)
+            red[0:2] += part[0:2]
+            red[2:] = torch.maximum(red[2:], part[2:])
+            return
+        for s in self.owned:
+            if not s.param.requires_grad:
+                continue
+            sl = self._sl(s)
+            avg = gbuf[sl] * inv
+            red[0] += avg.double().square().sum().float()
+            if not torch.isfinite(avg).all():
+                red[3 + self.group_idx[diag_group_of(s.name)]] = 1.0
+            g = torch.nan_to_num(avg, nan=0.0, posinf=0.0, neginf=0.0) * s.grad_scale
+            gbuf[sl] = g
+            red[1] += g.double().square().sum().float()
+        for s in self.owned:
+            if (st.master_view(s).abs() >= PARAM_CLIP).any():
+                red[2] = 1.0
+
+    def _finish(self, coef: torch.Tensor, assignment_frac: Optional[torch.Tensor]) -> None:
+        st = self.store
+        gbuf = st.grad[st.lo:st.hi]
+        use_k = self.uses_kernels()
         lrs = self.lrs(self.count)
         # Muon directions first (matrix-wise), written over the gradient buffer
+        if use_k:
+            from ..ops import kernels as K
         for s in self.owned:
             if s.label == "muon" and s.param.requires_grad:
                 sl = self._sl(s)
@@ -132,7 +155,6 @@ class HybridOptimizer:
             self._apply_eager(lrs, coef, gbuf, assignment_frac)
             st.publish_owned()
         self.count += 1
-        return self._info(global_norm, is_finite, red, skipped=False)
 
     def _apply_eager(self, lrs, coef, gbuf, assignment_frac):
         st = self.store

@@ -23,7 +23,7 @@ master and moments hold only the owned shard.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Callable, Dict, List
+from typing import Callable, Dict, List, Optional
 
 import torch
 import torch.nn as nn
@@ -57,14 +57,21 @@ def default_keep_fp32(name: str, p: torch.Tensor) -> bool:
     return p.ndim < 2 or name.endswith("router")
 
 
+def is_ep_local(name: str, p: torch.Tensor) -> bool:
+    """Expert-parallel parameters (this rank's block of routed experts): neither
+    reduced nor gathered across ranks."""
+    return bool(getattr(p, "_ahb_ep_local", False))
+
+
 class FlatParamStore:
     def __init__(self, model: nn.Module, label_fn: Callable[[str, int], str],
                  grad_scale_fn: Callable[[str], float], world: int = 1, rank: int = 0,
                  compute_dtype: torch.dtype = torch.bfloat16, device=None,
-                 keep_fp32: Callable[[str, torch.Tensor], bool] = default_keep_fp32):
+                 keep_fp32: Callable[[str, torch.Tensor], bool] = default_keep_fp32,
+                 param_filter: Optional[Callable[[str, torch.Tensor], bool]] = None):
         self.world, self.rank = world, rank
         self.compute_dtype = compute_dtype
-        named = list(model.named_parameters())
+        named = [(n, p) for n, p in model.named_parameters() if param_filter is None or param_filter(n, p)]
         self.device = device = device or named[0][1].device
         all32 = compute_dtype == torch.float32
         fp32 = [all32 or keep_fp32(n, p) for n, p in named]

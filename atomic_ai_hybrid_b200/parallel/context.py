@@ -30,6 +30,8 @@ class ParallelContext:
     ep_world: int = 1
     tp_group: Optional[dist.ProcessGroup] = None
     tp_world: int = 1
+    ep_rank: int = 0
+    ep: Optional[object] = None  # the EPGroup (peer buffers) once built
 
 
 _CTX = ParallelContext()

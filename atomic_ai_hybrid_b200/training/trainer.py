@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 
 from ..optim import FlatParamStore, HybridOptimizer, grad_scale_of, label_adamw_only, label_of
+from ..optim.store import is_ep_local
 from .loss import compute_loss
 
 
@@ -31,7 +32,7 @@ class Trainer:
                  compute_dtype: torch.dtype = torch.bfloat16, device=None,
                  group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
                  ce_chunk_size: int = 2048, collinearity_coef: Optional[float] = None,
-                 skip_nonfinite: bool = False, cuda_graph: bool = False):
+                 skip_nonfinite: bool = False, cuda_graph: bool = False, ep_max_tokens: int = 0):
         self.model = model
         self.cfg = model.cfg
         self.group = group
@@ -39,8 +40,15 @@ class Trainer:
         self.world = dist.get_world_size(group) if dist_on else 1
         self.rank = dist.get_rank(group) if dist_on else 0
         label_fn = label_of if optimizer == "hybrid" else label_adamw_only
+        ep_params = any(is_ep_local(n, p) for n, p in model.named_parameters())
         self.store = FlatParamStore(model, label_fn, grad_scale_of, self.world, self.rank,
-                                    compute_dtype=compute_dtype, device=device)
+                                    compute_dtype=compute_dtype, device=device,
+                                    param_filter=(lambda n, p: not is_ep_local(n, p)) if ep_params else None)
+        # expert-parallel experts: a local store (no reduction / gathering) stepped with the main one
+        self.ep_store = None
+        if ep_params:
+            self.ep_store = FlatParamStore(model, label_fn, grad_scale_of, 1, 0, compute_dtype=compute_dtype,
+                                           device=device, param_filter=is_ep_local)
         self.comm = None
         if self.world > 1:
             from ..parallel.context import ParallelContext, get_parallel_context, set_parallel_context
@@ -50,6 +58,20 @@ class Trainer:
             self.comm = make_shard_comm(self.store, group, comm)
         self.opt = HybridOptimizer(self.store, total_steps, reduce_fn=self._allreduce_sum,
                                    skip_nonfinite=skip_nonfinite)
+        self.ep_opt = None
+        if self.ep_store is not None:
+            self.ep_opt = HybridOptimizer(self.ep_store, total_steps)
+            self.opt.partners.append(self.ep_opt)
+            from ..parallel.context import get_parallel_context
+            pc = get_parallel_context()
+            if pc.ep is None:
+                if ep_max_tokens <= 0:
+                    raise ValueError("expert parallelism needs ep_max_tokens (tokens per micro-batch)")
+                from ..parallel.ep import EPGroup
+                pc.ep = EPGroup(pc.ep_world, pc.ep_rank, self.cfg.e_routed, self.cfg.top_k, self.cfg.d_model,
+                                ep_max_tokens, self.store.device, group=pc.ep_group)
+            # the per-layer host read of the routing counts cannot be captured
+            cuda_graph = False
         # peer-memory comm + fused optimizer kernels: reduce-scatter and all-gather
         # happen inside the optimizer's prepare / apply kernels
         self.fused_comm = bool(self.comm is not None and getattr(self.comm, "fused", False)
@@ -130,6 +152,8 @@ class Trainer:
 
     def reset_accumulators(self) -> None:
         self.store.zero_grad()
+        if self.ep_store is not None:
+            self.ep_store.zero_grad()
         self._frac_sum.zero_()
         self._loss_sum.zero_()
         self._n_micro = 0
@@ -179,6 +203,11 @@ class Trainer:
             torch.cuda.synchronize()
         if self.comm is not None and hasattr(self.comm, "close"):
             self.comm.close()
+        if self.ep_store is not None:
+            from ..parallel.context import get_parallel_context
+            ep = get_parallel_context().ep
+            if ep is not None:
+                ep.close()
 
     @torch.no_grad()
     def eval_loss(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:

@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--optimizer", default="adamw", choices=["adamw", "hybrid"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA-graph capture of the micro-step")
+    ap.add_argument("--ep", type=int, default=1,
+                    help="expert-parallel ranks (1 or the number of GPUs): routed experts split over the GPUs")
     return ap.parse_args()
 
 
@@ -135,7 +137,12 @@ def main():
     if args.layers:
         over["num_layers"] = args.layers
     cfg = get_preset(args.model, **over)
-    torch.manual_seed(1234)
+    if args.ep > 1:
+        if args.ep != world:
+            raise SystemExit("--ep must equal the number of GPUs")
+        from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
+        set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
+    torch.manual_seed(1234 + (rank if args.ep > 1 else 0))  # distinct experts per expert-parallel rank
     with torch.device(dev):
         model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16)
     # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0
@@ -148,7 +155,8 @@ def main():
     use_graph = args.impl == "cuda" and not args.no_graph
     # the eager baseline keeps NCCL collectives; the CUDA path uses the peer-memory fused step
     trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev,
-                      cuda_graph=use_graph, comm="nccl" if args.impl == "eager" else "auto")
+                      cuda_graph=use_graph, comm="nccl" if args.impl == "eager" else "auto",
+                      ep_max_tokens=args.micro_batch * args.seq_len if args.ep > 1 else 0)
     trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
 
     S, mb = args.seq_len, args.micro_batch
@@ -183,7 +191,7 @@ def main():
     ev1.record()
     torch.cuda.synchronize()
     launches = launch_counter.count
-    if use_graph:  # kernels inside the replayed micro-step graph
+    if trainer.cuda_graph:  # kernels inside the replayed micro-step graph
         launches += trainer.graph_kernel_launches * n_micro * args.steps
     launch_counter.disable()
     barrier()
@@ -232,7 +240,8 @@ def main():
             "dtype": "bf16", "data": "synthetic tokens, random-init weights",
             "impl": args.impl,
             "config": {"model": args.model, "global_batch": seqs * world, "seq_len": S,
-                       "micro_batch": mb, "grad_accum": n_micro, "parallelism": f"dp{world}" if world > 1 else "dp1",
+                       "micro_batch": mb, "grad_accum": n_micro,
+                       "parallelism": (f"dp{world}" if world > 1 else "dp1") + (f"+ep{args.ep}" if args.ep > 1 else ""),
                        "sharding": "param/optimizer owner-sharded, bf16 weights resident",
                        "collectives": ("none" if world == 1 else
                                        "NVLink peer memory: reduce-scatter fused into the optimizer's first pass, "
