@@ -1,5 +1,6 @@
 """Single-GPU operator benchmark (the benchmark spec's config 2): GDN-2 chunked
-delta rule and Mamba2 SSD, forward + backward, bf16, timed with CUDA events.
+delta rule and Mamba2 SSD, forward + backward, bf16, timed with CUDA events; also
+the MoE grouped FFN, the fused router, the fused residual/norm glue and conv1d.
 
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op gdn --B 8 --T 4096 --H 16``
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op ssd --B 8 --T 4096 --H 32``
@@ -113,9 +114,70 @@ def bench_moe(T, d, F_, E, k, warmup, iters, flush, mode="fwdbwd"):
             "tflops": fl / ms / 1e9}
 
 
+def bench_router(T, d, E, k, warmup, iters, flush, mode="fwdbwd"):
+    """Fused MoE router (fp32-exact logits on tensor cores) forward (+ backward)."""
+    from ..ops import kernels as K
+    dev = "cuda"
+    x = (torch.randn(T, d, device=dev) * 2).to(torch.bfloat16).requires_grad_(True)
+    kern = torch.randn(d, E, device=dev)
+    kn = (kern / kern.norm(dim=0, keepdim=True)).requires_grad_(True)
+    temp = torch.full((1,), 10.0, device=dev, requires_grad=True)
+    bias = torch.zeros(E, device=dev)
+
+    def run():
+        gate, psum, lse_sq, _, _, _ = K.router(x, kn, temp, bias, None, k)
+        if mode == "fwdbwd":
+            (gate.sum() + psum.square().sum() + lse_sq.sum()).backward()
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = 2 * T * d * E * 3 * (3 if mode == "fwdbwd" else 1)
+    return {"op": "router", "mode": mode, "T": T, "d": d, "E": E, "k": k, "ms": ms,
+            "min_io_gb_s": T * d * 2 * (3 if mode == "fwdbwd" else 1) / ms / 1e6, "tflops": fl / ms / 1e9}
+
+
+def bench_glue(T, d, warmup, iters, flush, mode="fwdbwd"):
+    """Residual add + clip + RMSNorm and RMSNorm x SiLU gate (fused row kernels)."""
+    from ..ops import kernels as K
+    dev = "cuda"
+    x = torch.randn(T, d, device=dev).to(torch.bfloat16).requires_grad_(True)
+    delta = torch.randn(T, d, device=dev).to(torch.bfloat16).requires_grad_(True)
+    z = torch.randn(T, d, device=dev).to(torch.bfloat16).requires_grad_(True)
+    scale = torch.ones(d, device=dev, requires_grad=True)
+
+    def run():
+        xo, y = K.add_rmsnorm(x, delta, scale, 1e3, 1e-6, sanitize_delta_grad=True)
+        o = K.norm_gate(y, z, scale, 1e-6, 1e2)
+        if mode == "fwdbwd":
+            torch.autograd.backward([o, xo], [torch.ones_like(o), torch.ones_like(xo)])
+
+    ms = _timeit(run, warmup, iters, flush)
+    # forward 6 row passes (x, delta, xo, y | y, z, o), backward 11
+    io = T * d * 2 * (6 + (11 if mode == "fwdbwd" else 0))
+    return {"op": "glue", "mode": mode, "T": T, "d": d, "ms": ms, "min_io_gb_s": io / ms / 1e6}
+
+
+def bench_conv(B, T, C, warmup, iters, flush, mode="fwdbwd"):
+    """Depthwise causal conv1d (width 4) + SiLU, streaming bf16 kernels."""
+    from ..ops import kernels as K
+    dev = "cuda"
+    x = torch.randn(B, T, C, device=dev).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(C, 4, device=dev) * 0.3).requires_grad_(True)
+    b = torch.zeros(C, device=dev, requires_grad=True)
+    dy = torch.randn(B, T, C, device=dev).to(torch.bfloat16)
+
+    def run():
+        y = K.conv1d(x, w, b, True, None)
+        if mode == "fwdbwd":
+            y.backward(dy)
+
+    ms = _timeit(run, warmup, iters, flush)
+    io = B * T * C * 2 * (2 + (3 if mode == "fwdbwd" else 0))
+    return {"op": "conv1d", "mode": mode, "B": B, "T": T, "C": C, "ms": ms, "min_io_gb_s": io / ms / 1e6}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe"])
+    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv"])
     ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--T", type=int, default=4096)
@@ -131,8 +193,14 @@ def main(argv=None):
         r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode)
     elif a.op == "ssd":
         r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode)
-    else:
+    elif a.op == "moe":
         r = bench_moe(a.B * a.T, 2048, 1024, 32, 4, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "router":
+        r = bench_router(a.B * a.T, 2048, 32, 4, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "glue":
+        r = bench_glue(a.B * a.T, 2048, a.warmup, a.iters, flush, a.mode)
+    else:
+        r = bench_conv(a.B, a.T, 2048, a.warmup, a.iters, flush, a.mode)
     print(json.dumps(r), flush=True)
     return r
 
