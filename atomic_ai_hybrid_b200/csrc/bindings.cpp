@@ -990,6 +990,39 @@ std::vector<torch::Tensor> router_bwd(torch::Tensor x, torch::Tensor kn, torch::
   return {dx, dkn, dtemp};
 }
 
+// ------------------------------------------------------------ causal flash attention (attention.cu)
+static void check_attn(const torch::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.dim() == 4, n,
+              ": contiguous bf16 (B, H, L, D)");
+}
+
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale) {
+  for (auto* t : {&q, &k, &v}) check_attn(*t, "attention");
+  const int64_t B = q.size(0), H = q.size(1), L = q.size(2), D = q.size(3);
+  TORCH_CHECK(k.sizes() == q.sizes() && v.sizes() == q.sizes() && ahb_attn_supported((int)D), "attention: shapes / D");
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({B, H, L}, q.options().dtype(at::kFloat));
+  TORCH_CHECK(ahb_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), (int)(B * H), (int)L, (int)D, (float)scale,
+                           o.data_ptr(), lse.data_ptr<float>(), cur_stream()) == 0, "attention: setup failed");
+  check_launch("ahb_attn_fwd");
+  return {o, lse};
+}
+
+std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                                    torch::Tensor dout, torch::Tensor lse, double scale) {
+  auto doc = dout.to(at::kBFloat16).contiguous();
+  for (auto* t : {&q, &k, &v, &o, &doc}) check_attn(*t, "attention bwd");
+  const int64_t B = q.size(0), H = q.size(1), L = q.size(2), D = q.size(3);
+  auto delta = (doc.to(at::kFloat) * o.to(at::kFloat)).sum(-1).contiguous();
+  auto dq = torch::zeros(q.sizes(), q.options().dtype(at::kFloat));
+  auto dk = torch::empty_like(k), dv = torch::empty_like(v);
+  TORCH_CHECK(ahb_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), doc.data_ptr(), lse.data_ptr<float>(),
+                           delta.data_ptr<float>(), (int)(B * H), (int)L, (int)D, (float)scale, dq.data_ptr<float>(),
+                           dk.data_ptr(), dv.data_ptr(), cur_stream()) == 0, "attention bwd: setup failed");
+  check_launch("ahb_attn_bwd");
+  return {dq.to(at::kBFloat16), dk, dv};
+}
+
 // ------------------------------------------------------------ NVLink peer memory (CUDA IPC)
 int64_t ipc_alloc(int64_t nbytes) {
   void* p = nullptr;
@@ -1138,6 +1171,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_rows", &moe_combine_rows);
   m.def("moe_combine_rows_bwd", &moe_combine_rows_bwd);
   m.def("moe_sum_rows", &moe_sum_rows);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

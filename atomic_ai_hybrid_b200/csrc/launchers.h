@@ -163,6 +163,14 @@ void ahb_ep_dispatch(const void* src, int src_by_token, int T, int k, int d, con
 void ahb_ep_return(const void* rows, const void* meta, int64_t R, int d, void* const* ret_peers, cudaStream_t st);
 void ahb_ep_zero_pad(void* rows, void* meta, const int* off, const int* seg, int El, int d, cudaStream_t st);
 
+// attention.cu: causal flash attention (q, k, v, o (BH, L, D) bf16, D in {64, 96, 128}); lse (BH, L) fp32.
+// Backward: delta = rowsum(dO o O) (BH, L) fp32; dq (BH, L, D) fp32 accumulated (zero it first).
+int ahb_attn_supported(int D);
+int ahb_attn_fwd(const void* q, const void* k, const void* v, int BH, int L, int D, float scale, void* o, float* lse,
+                 cudaStream_t st);
+int ahb_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+                 int BH, int L, int D, float scale, float* dq, void* dk, void* dv, cudaStream_t st);
+
 // comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
 int ahb_ipc_alloc(int64_t nbytes, void** ptr);
 int ahb_ipc_free(void* ptr);

@@ -229,7 +229,31 @@ def ssd(dt, A, Bm, Cm, x, chunk):
     return _SSD.apply(dt, A, Bm, Cm, x)
 
 
+class _Attention(torch.autograd.Function):
+    """Causal flash attention (``attention.cu``): forward keeps O and the row
+    log-sum-exp; backward recomputes P per key tile."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, scale):
+        o, lse = ext().attn_fwd(q, k, v, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = ext().attn_bwd(q, k, v, o, do, lse, ctx.scale)
+        return dq, dk, dv, None
+
+
 def attention(q, k, v, sm_scale):
+    """Causal attention on ``(B, H, L, D)`` bf16 with D in {64, 96, 128}; other
+    head dims or dtypes use PyTorch's scaled_dot_product_attention."""
+    if q.dtype == torch.bfloat16 and q.shape[-1] in (64, 96, 128):
+        bf = torch.bfloat16
+        return _Attention.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(), float(sm_scale))
+    _unsupported(f"attention D={q.shape[-1]} dtype={q.dtype}")
     return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=sm_scale)
 
 
