@@ -1023,6 +1023,60 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   return {dq.to(at::kBFloat16), dk, dv};
 }
 
+// ------------------------------------------------------------ BlockDAR source softmax (source_mix.cu)
+static torch::Tensor ptr_table(const std::vector<torch::Tensor>& ts, int64_t numel, const torch::Device& dev,
+                               const char* what) {
+  std::vector<int64_t> p;
+  for (const auto& t : ts) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.numel() == numel, what,
+                ": contiguous bf16 tensors of equal size");
+    p.push_back(reinterpret_cast<int64_t>(t.data_ptr()));
+  }
+  return torch::tensor(p, torch::kInt64).to(dev);
+}
+
+std::vector<torch::Tensor> source_mix_fwd(torch::Tensor q, std::vector<torch::Tensor> ks, std::vector<torch::Tensor> ss,
+                                          double scale) {
+  const int n = (int)ks.size();
+  TORCH_CHECK(n >= 1 && n <= ahb_source_mix_max() && (int)ss.size() == n, "source_mix: 1..32 sources");
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.is_contiguous(), "source_mix: q bf16");
+  const int64_t dl = q.size(-1), T = q.numel() / dl, d = ss[0].size(-1);
+  auto kt = ptr_table(ks, T * dl, q.device(), "keys");
+  auto st_ = ptr_table(ss, T * d, q.device(), "sources");
+  auto out = torch::empty_like(ss[0]);
+  auto wts = torch::empty({n, T}, q.options().dtype(at::kFloat));
+  ahb_source_mix_fwd(q.data_ptr(), reinterpret_cast<const void* const*>(kt.data_ptr<int64_t>()),
+                     reinterpret_cast<const void* const*>(st_.data_ptr<int64_t>()), n, T, (int)dl, (int)d,
+                     (float)scale, out.data_ptr(), wts.data_ptr<float>(), cur_stream());
+  check_launch("ahb_source_mix_fwd");
+  return {out, wts};
+}
+
+// returns [dq, dk_0..dk_{n-1}, ds_0..ds_{n-1}]
+std::vector<torch::Tensor> source_mix_bwd(torch::Tensor g, torch::Tensor q, std::vector<torch::Tensor> ks,
+                                          std::vector<torch::Tensor> ss, torch::Tensor wts, double scale) {
+  const int n = (int)ks.size();
+  const int64_t dl = q.size(-1), T = q.numel() / dl, d = ss[0].size(-1);
+  auto gc = g.to(at::kBFloat16).contiguous();
+  auto kt = ptr_table(ks, T * dl, q.device(), "keys");
+  auto st_ = ptr_table(ss, T * d, q.device(), "sources");
+  std::vector<torch::Tensor> out{torch::empty_like(q)};
+  std::vector<torch::Tensor> dks, dss;
+  for (int i = 0; i < n; ++i) dks.push_back(torch::empty_like(ks[i]));
+  for (int i = 0; i < n; ++i) dss.push_back(torch::empty_like(ss[i]));
+  auto dkt = ptr_table(dks, T * dl, q.device(), "dk");
+  auto dst = ptr_table(dss, T * d, q.device(), "ds");
+  ahb_source_mix_bwd(gc.data_ptr(), q.data_ptr(), reinterpret_cast<const void* const*>(kt.data_ptr<int64_t>()),
+                     reinterpret_cast<const void* const*>(st_.data_ptr<int64_t>()), wts.data_ptr<float>(), n, T,
+                     (int)dl, (int)d, (float)scale, out[0].data_ptr(),
+                     reinterpret_cast<void* const*>(dkt.data_ptr<int64_t>()),
+                     reinterpret_cast<void* const*>(dst.data_ptr<int64_t>()), cur_stream());
+  check_launch("ahb_source_mix_bwd");
+  out.insert(out.end(), dks.begin(), dks.end());
+  out.insert(out.end(), dss.begin(), dss.end());
+  return out;
+}
+
 // ------------------------------------------------------------ NVLink peer memory (CUDA IPC)
 int64_t ipc_alloc(int64_t nbytes) {
   void* p = nullptr;
@@ -1173,6 +1227,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_sum_rows", &moe_sum_rows);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  m.def("source_mix_fwd", &source_mix_fwd);
+  m.def("source_mix_bwd", &source_mix_bwd);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

@@ -171,6 +171,14 @@ int ahb_attn_fwd(const void* q, const void* k, const void* v, int BH, int L, int
 int ahb_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
                  int BH, int L, int D, float scale, float* dq, void* dk, void* dv, cudaStream_t st);
 
+// source_mix.cu: BlockDAR source softmax (out = sum_i softmax_i(scale <q, k_i>) s_i), pointer tables of n <= 32
+int ahb_source_mix_max();
+void ahb_source_mix_fwd(const void* q, const void* const* ks, const void* const* ss, int n, int64_t T, int dl, int d,
+                        float scale, void* out, float* wts, cudaStream_t st);
+void ahb_source_mix_bwd(const void* g, const void* q, const void* const* ks, const void* const* ss, const float* wts,
+                        int n, int64_t T, int dl, int d, float scale, void* dq, void* const* dks, void* const* dss,
+                        cudaStream_t st);
+
 // comm.cu: NVLink peer-memory collectives (CUDA IPC buffers, bounded barriers)
 int ahb_ipc_alloc(int64_t nbytes, void** ptr);
 int ahb_ipc_free(void* ptr);

@@ -48,6 +48,12 @@ class IntraBlockAttention(nn.Module):
             return sources[0]
         q = self.q_proj(block_input)
         scale = 1.0 / math.sqrt(self.d_latent)
+        if ops.use_cuda(q):
+            from ..ops import kernels as K
+            ks = [getattr(self, f"k_proj_{i}")(s) for i, s in enumerate(sources)]
+            out = K.source_mix(q, ks, sources, scale)
+            if out is not None:
+                return out
         scores = torch.stack([(q * getattr(self, f"k_proj_{i}")(s)).sum(-1) for i, s in enumerate(sources)], 0)
         wts = torch.softmax(scores.float() * scale, 0).to(block_input.dtype)
         mixed = sum(wts[i][..., None] * s for i, s in enumerate(sources))
@@ -67,6 +73,11 @@ class HybridDARAttention(nn.Module):
         if len(sources) == 0:
             return torch.zeros_like(current_x)
         q = self.q_proj(current_x)
+        if ops.use_cuda(q):
+            from ..ops import kernels as K
+            out = K.source_mix(q, [self.k_proj(s) for s in sources], sources, 1.0 / math.sqrt(self.d_latent))
+            if out is not None:
+                return out
         scores = torch.stack([(q * self.k_proj(s)).sum(-1) for s in sources], 0) / math.sqrt(self.d_latent)
         wts = torch.softmax(scores.float(), 0).to(current_x.dtype)
         return sum(wts[i][..., None] * s for i, s in enumerate(sources)).to(current_x.dtype)

@@ -435,6 +435,38 @@ def router(x, kn, temp, bias, noise, k: int):
     return _Router.apply(x.contiguous(), kn, temp, bias, noise, k)
 
 
+class _SourceMix(torch.autograd.Function):
+    """``sum_i softmax_i(scale <q, k_i>) s_i`` per token (BlockDAR source softmax)."""
+
+    @staticmethod
+    def forward(ctx, scale, n, q, *ks_ss):
+        ks, ss = list(ks_ss[:n]), list(ks_ss[n:])
+        out, wts = ext().source_mix_fwd(q, ks, ss, scale)
+        ctx.save_for_backward(q, wts, *ks, *ss)
+        ctx.scale, ctx.n = scale, n
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        q, wts, *rest = ctx.saved_tensors
+        n = ctx.n
+        res = ext().source_mix_bwd(g, q, rest[:n], rest[n:], wts, ctx.scale)
+        return (None, None, res[0], *res[1:])
+
+
+def source_mix(q, ks, ss, scale: float):
+    """``q (..., dl)``, ``ks`` n tensors like ``q``, ``ss`` n tensors ``(..., d)``; bf16.
+    Returns ``None`` where the kernel does not apply (the caller uses PyTorch ops)."""
+    n = len(ss)
+    if (n == 0 or n > 32 or q.dtype != torch.bfloat16 or any(t.dtype != torch.bfloat16 for t in ss)
+            or torch.cuda.is_current_stream_capturing()):
+        return None
+    bf = torch.bfloat16
+    ks = [k.to(bf).contiguous() for k in ks]
+    ss = [s.contiguous() for s in ss]
+    return _SourceMix.apply(float(scale), n, q.to(bf).contiguous(), *ks, *ss)
+
+
 def gdn2_layer(mod, x):
     if x.dtype == torch.bfloat16 and mod.d_head == 128 and row_fusable(x.shape[-1]):
         return _gdn2_layer_fused(mod, x)

@@ -24,3 +24,30 @@ def test_attention_fwd_bwd(B, H, L, D):
     for a, b, n in ((qk.grad, qr.grad, "dq"), (kk.grad, kr.grad, "dk"), (vk.grad, vr.grad, "dv")):
         err = (a.float() - b).abs().max() / (b.abs().max() + 1e-6)
         assert err < 3e-2, (n, float(err))
+
+
+@pytest.mark.parametrize("n", [2, 3, 7])
+def test_source_mix(n):
+    """BlockDAR source softmax kernel vs the PyTorch expression."""
+    torch.manual_seed(n)
+    T, dl, d = 300, 384, 768
+    q = torch.randn(T, dl, device="cuda")
+    ks = [torch.randn(T, dl, device="cuda") for _ in range(n)]
+    ss = [torch.randn(T, d, device="cuda") for _ in range(n)]
+    scale = dl ** -0.5
+    qr, ksr, ssr = q.clone().requires_grad_(True), [k.clone().requires_grad_(True) for k in ks], \
+        [s.clone().requires_grad_(True) for s in ss]
+    w = torch.softmax(torch.stack([(qr * k).sum(-1) for k in ksr], 0) * scale, 0)
+    ref = sum(w[i][:, None] * s for i, s in enumerate(ssr))
+    g = torch.randn(T, d, device="cuda")
+    ref.backward(g)
+    qb = q.to(torch.bfloat16).requires_grad_(True)
+    kb = [k.to(torch.bfloat16).requires_grad_(True) for k in ks]
+    sb = [s.to(torch.bfloat16).requires_grad_(True) for s in ss]
+    out = K.source_mix(qb, kb, sb, scale)
+    out.backward(g.to(torch.bfloat16))
+    torch.testing.assert_close(out.float(), ref.detach(), atol=3e-2, rtol=2e-2)
+    for a, b in [(qb.grad, qr.grad)] + list(zip([k.grad for k in kb], [k.grad for k in ksr])) + \
+            list(zip([s.grad for s in sb], [s.grad for s in ssr])):
+        err = (a.float() - b).abs().max() / (b.abs().max() + 1e-6)
+        assert err < 3e-2, float(err)
