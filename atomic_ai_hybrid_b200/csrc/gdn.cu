@@ -172,15 +172,31 @@ __global__ void __launch_bounds__(NTH, 1) gdn_intra_fwd_kernel(
   }
   load_gc(gc_s, g, ix, b, n, h, NTH);  // includes __syncthreads
 
-  // 2. bke = bk * e^gc
+  // 2. bke = bk * e^gc; per diagonal block, the largest decay across its 16 rows
+  __shared__ int exact_blk[4];
   for (int i = tid; i < C * D; i += NTH) {
     int r = i / D, d = i % D;
     bke_s[r * LDB + d] = __float2bfloat16_rn(bf(bk_s[r * LDB + d]) * __expf(gc_s[r * LDF + d]));
   }
-  // 3a. off-diagonal 16x16 blocks of Aqk / Akk on tensor cores
-  for (int job = warp; job < 12; job += NTH / 32) {
+  if (warp < 4) {
+    float span = 0.f;
+    for (int d = lane; d < D; d += 32) span = fmaxf(span, gc_s[16 * warp * LDF + d] - gc_s[(16 * warp + 15) * LDF + d]);
+    span = warp_max(span);
+    // the factorised operands of a diagonal block carry e^{span}; beyond e^60 use exact sums
+    if (lane == 0) exact_blk[warp] = !(span <= 60.f);
+  }
+  __syncthreads();
+  // 3a. 16x16 blocks of Aqk / Akk on tensor cores: 6 off-diagonal and 4 diagonal block pairs,
+  // operands factorised at the block-row's first row r0 (every exponent <= 0 off the diagonal;
+  // on the diagonal B carries e^{gc_r0 - gc_j} <= e^{span})
+  for (int job = warp; job < 20; job += NTH / 32) {
     int I, J;
-    pair_ij(job >> 1, I, J);
+    if (job < 12) {
+      pair_ij(job >> 1, I, J);
+    } else {
+      I = J = (job - 12) >> 1;
+      if (exact_blk[I]) continue;
+    }
     const bool is_kk = job & 1;
     const int r0 = 16 * I;
     const float* gr = gc_s + r0 * LDF;
@@ -201,11 +217,18 @@ __global__ void __launch_bounds__(NTH, 1) gdn_intra_fwd_kernel(
     warp_mma<2>(acc, fa, fb, 0, 0, 0, D);
     float* dst = is_kk ? akk_s : aqk_s;
     const float sc = is_kk ? 1.f : scale;
-    for_acc<2>(acc, 0, 0, [&](int rr, int cc, float& val) { dst[(r0 + rr) * LDC + 16 * J + cc] = guard(val * sc); });
+    const bool diag = I == J;
+    for_acc<2>(acc, 0, 0, [&](int rr, int cc, float& val) {
+      // diagonal blocks: Aqk keeps j <= i, Akk keeps j < i (the rest is zeroed below)
+      if (!diag || cc < rr || (cc == rr && !is_kk)) dst[(r0 + rr) * LDC + 16 * J + cc] = guard(val * sc);
+      else if (cc == rr) dst[(r0 + rr) * LDC + 16 * J + cc] = 0.f;
+    });
   }
-  // 3b. diagonal blocks, exact per-channel sums (-20 floor on the exponent, as the reference)
+  // 3b. diagonal blocks whose decay span is too wide to factorise: exact per-channel sums
+  // (-20 floor on the exponent, as the reference)
   for (int p = warp; p < 4 * 136; p += NTH / 32) {
     int blk = p / 136, i, j;
+    if (!exact_blk[blk]) continue;
     tri_ij(p % 136, i, j);
     const int ri = 16 * blk + i, rj = 16 * blk + j;
     float sq = 0.f, sk = 0.f;
@@ -714,31 +737,53 @@ __global__ void __launch_bounds__(NTH, 1) gdn_bwd_intra_kernel(
   const int I = warp & 3, nq = warp >> 2;
   const int m0 = 16 * I, n0 = 32 * nq;
   const int r0 = m0;  // reference row of block I
+  // diagonal blocks are factorised like the others unless their decay span could overflow
+  __shared__ int exact_blk[4];
+  if (warp < 4) {
+    const int lane = tid & 31;
+    float span = 0.f;
+    for (int d = lane; d < D; d += 32) span = fmaxf(span, gc_s[16 * warp * LDF + d] - gc_s[(16 * warp + 15) * LDF + d]);
+    span = warp_max(span);
+    if (lane == 0) exact_blk[warp] = !(span <= 60.f);
+  }
+  __syncthreads();
+  const bool exact = exact_blk[I];
   float dq[4][4], dbk[4][4], dk[4][4];
   zero_acc<4>(dq);
   zero_acc<4>(dbk);
   zero_acc<4>(dk);
-  // (a) row side, columns j < 16I: dq_I, dbk_I  (B = k_j e^{gc_r - gc_j})
-  if (I > 0) {
+  // (a) row side, columns j < 16I (and j <= i inside block I unless it is exact): dq_I, dbk_I
+  //     (B = k_j e^{gc_r - gc_j}, A masked to the causal pairs)
+  const int a_hi = exact ? r0 : r0 + 16;
+  if (a_hi > 0) {
     const float* gr = gc_s + r0 * LDF;
     auto fb = [&](int kj, int nd) -> uint32_t {
       return pack2(bf(k_s[kj * LDB + nd]) * __expf(gr[nd] - gc_s[kj * LDF + nd]),
                    bf(k_s[(kj + 1) * LDB + nd]) * __expf(gr[nd] - gc_s[(kj + 1) * LDF + nd]));
     };
-    warp_mma<4>(dq, RowA32{daqk_s, LDC}, fb, m0, n0, 0, r0);
-    warp_mma<4>(dbk, RowA32{dakk_s, LDC}, fb, m0, n0, 0, r0);
+    auto fa_q = [&](int r, int kk) -> uint32_t {
+      return pack2(kk <= r ? daqk_s[r * LDC + kk] : 0.f, kk + 1 <= r ? daqk_s[r * LDC + kk + 1] : 0.f);
+    };
+    auto fa_k = [&](int r, int kk) -> uint32_t {
+      return pack2(kk < r ? dakk_s[r * LDC + kk] : 0.f, kk + 1 < r ? dakk_s[r * LDC + kk + 1] : 0.f);
+    };
+    warp_mma<4>(dq, fa_q, fb, m0, n0, 0, a_hi);
+    warp_mma<4>(dbk, fa_k, fb, m0, n0, 0, a_hi);
     for_acc<4>(dq, m0, n0, [&](int r, int c, float& x) { x *= scale * __expf(gc_s[r * LDF + c] - gr[c]); });
     for_acc<4>(dbk, m0, n0, [&](int r, int c, float& x) { x *= __expf(gc_s[r * LDF + c] - gr[c]); });
   }
-  // (b) column side from later blocks I2 > I: dk_j += e^{gc_r2 - gc_j} sum_i dA[i,j] x_i e^{gc_i - gc_r2}
-  for (int I2 = I + 1; I2 < 4; ++I2) {
+  // (b) column side from blocks I2 >= I (I2 = I only when factorised):
+  //     dk_j += e^{gc_r2 - gc_j} sum_i dA[i,j] x_i e^{gc_i - gc_r2}, pairs with i >= j (i > j for Akk)
+  for (int I2 = exact ? I + 1 : I; I2 < 4; ++I2) {
     const int r2 = 16 * I2;
     const float* gr = gc_s + r2 * LDF;
     auto fa_q = [&](int rj, int ci) -> uint32_t {  // A(j, i) = daqk[r2+i][m0+j]
-      return pack2(daqk_s[(r2 + ci) * LDC + rj], daqk_s[(r2 + ci + 1) * LDC + rj]);
+      const int i0 = r2 + ci;
+      return pack2(i0 >= rj ? daqk_s[i0 * LDC + rj] : 0.f, i0 + 1 >= rj ? daqk_s[(i0 + 1) * LDC + rj] : 0.f);
     };
     auto fa_k = [&](int rj, int ci) -> uint32_t {
-      return pack2(dakk_s[(r2 + ci) * LDC + rj], dakk_s[(r2 + ci + 1) * LDC + rj]);
+      const int i0 = r2 + ci;
+      return pack2(i0 > rj ? dakk_s[i0 * LDC + rj] : 0.f, i0 + 1 > rj ? dakk_s[(i0 + 1) * LDC + rj] : 0.f);
     };
     auto fb_q = [&](int ki, int nd) -> uint32_t {
       return pack2(bf(q_s[(r2 + ki) * LDB + nd]) * __expf(gc_s[(r2 + ki) * LDF + nd] - gr[nd]),
@@ -764,7 +809,7 @@ __global__ void __launch_bounds__(NTH, 1) gdn_bwd_intra_kernel(
         dk[j][e] += (scale * t1[j][e] + t2[j][e]) * __expf(gr[c] - gc_s[r * LDF + c]);
       }
   }
-  // (c) diagonal block, exact: element (i, d) of this thread's fragments
+  // (c) exact diagonal sums (blocks with a wide decay span only) and assembly, per fragment element
   {
     const int lane = tid & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -777,7 +822,7 @@ __global__ void __launch_bounds__(NTH, 1) gdn_bwd_intra_kernel(
         const float bki = bf(b_s[r * LDB + c]) * bf(k_s[r * LDB + c]);
         const float ki = bf(k_s[r * LDB + c]);
         float aq = 0.f, ab = 0.f, ak = 0.f;
-        for (int s = m0; s < m0 + 16; ++s) {
+        for (int s = m0; exact && s < m0 + 16; ++s) {
           const float gs = gc_s[s * LDF + c];
           if (s <= r) {  // row side: pairs (r, s), s <= r
             const float ex = __expf(fmaxf(gi - gs, -20.f));

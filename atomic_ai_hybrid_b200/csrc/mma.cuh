@@ -65,6 +65,37 @@ AHB_DEVICE void warp_mma(float (*acc)[4], const FA& fa, const FB& fb, int m0, in
   }
 }
 
+// fp32 pair -> bf16 hi pair + bf16 lo pair (hi + lo = v to ~2^-16 relative)
+AHB_DEVICE void split2(float2 v, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  const float2 hf = __bfloat1622float2(h);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack2(v.x - hf.x, v.y - hf.y);
+}
+
+// warp_mma with fp32 operands split into two bf16 terms: A B ~ Ah Bh + Ah Bl + Al Bh.
+// Loaders return float2: fa(r, c) = (A[r][c], A[r][c+1]), fb(k, n) = (B[k][n], B[k+1][n]).
+template <int NT, class FA, class FB>
+AHB_DEVICE void warp_mma_split(float (*acc)[4], const FA& fa, const FB& fb, int m0, int n0, int k_lo, int k_hi) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  for (int k0 = k_lo; k0 < k_hi; k0 += 16) {
+    uint32_t ah[4], al[4];
+    split2(fa(m0 + g, k0 + 2 * t), ah[0], al[0]);
+    split2(fa(m0 + g + 8, k0 + 2 * t), ah[1], al[1]);
+    split2(fa(m0 + g, k0 + 2 * t + 8), ah[2], al[2]);
+    split2(fa(m0 + g + 8, k0 + 2 * t + 8), ah[3], al[3]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      uint32_t bh[2], bl[2];
+      split2(fb(k0 + 2 * t, n0 + 8 * j + g), bh[0], bl[0]);
+      split2(fb(k0 + 2 * t + 8, n0 + 8 * j + g), bh[1], bl[1]);
+      mma16816(acc[j], ah, bh);
+      mma16816(acc[j], ah, bl);
+      mma16816(acc[j], al, bh);
+    }
+  }
+}
+
 template <int NT>
 AHB_DEVICE void zero_acc(float (*acc)[4]) {
 #pragma unroll

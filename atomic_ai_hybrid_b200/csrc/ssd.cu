@@ -90,20 +90,47 @@ AHB_DEVICE float dbx(const bf16* x_s, const bf16* dt_s, int r, int p) {
 }
 
 // y_diag for the warp's tile: rows [16I, 16I+16), cols [n0, n0+8*NT)
+// Whether a 16-row diagonal block may be factorised at its first row: the largest
+// per-channel decay across its rows (c_r0 - c_r0+15) must keep e^{span} far from overflow.
+// Every lane of the calling warp gets the answer.
+AHB_DEVICE bool block_span_ok(const float* cum, int I) {
+  const int lane = threadIdx.x & 31;
+  const float* a = cum + 16 * I * LDPF;
+  const float* z = cum + (16 * I + 15) * LDPF;
+  float span = fmaxf(a[lane] - z[lane], a[lane + 32] - z[lane + 32]);
+  span = warp_max(span);
+  return span <= 60.f;
+}
+
 template <int NT>
 AHB_DEVICE void ydiag_tile(float (*acc)[4], const float* cb_s, const bf16* x_s, const bf16* dt_s, const float* cum,
                            int I, int n0) {
   const int r0 = 16 * I;
   zero_acc<NT>(acc);
+  // the diagonal block is factorised at row r0 too (B carries e^{c_r0 - c_j} <= e^{span}) unless
+  // its decay span is too wide; then it is summed exactly below
+  const bool fact = block_span_ok(cum, I);
+  const float* cr = cum + r0 * LDPF;
+  auto fbf = [&](int kj, int np) -> float2 {
+    return make_float2(dbx(x_s, dt_s, kj, np) * __expf(cr[np] - cum[kj * LDPF + np]),
+                       dbx(x_s, dt_s, kj + 1, np) * __expf(cr[np] - cum[(kj + 1) * LDPF + np]));
+  };
   if (I > 0) {
-    const float* cr = cum + r0 * LDPF;
     auto fb = [&](int kj, int np) -> uint32_t {
-      return pack2(dbx(x_s, dt_s, kj, np) * __expf(cr[np] - cum[kj * LDPF + np]),
-                   dbx(x_s, dt_s, kj + 1, np) * __expf(cr[np] - cum[(kj + 1) * LDPF + np]));
+      const float2 v = fbf(kj, np);
+      return pack2(v.x, v.y);
     };
     warp_mma<NT>(acc, RowA32{cb_s, LDCC}, fb, r0, n0, 0, r0);
-    for_acc<NT>(acc, r0, n0, [&](int r, int c, float& v) { v *= __expf(cum[r * LDPF + c] - cr[c]); });
   }
+  if (fact) {  // the diagonal block: two-term bf16 operands keep it close to fp32
+    auto fa = [&](int r, int kj) -> float2 {
+      return make_float2(kj <= r ? cb_s[r * LDCC + kj] : 0.f, kj + 1 <= r ? cb_s[r * LDCC + kj + 1] : 0.f);
+    };
+    warp_mma_split<NT>(acc, fa, fbf, r0, n0, r0, r0 + 16);
+  }
+  if (I > 0 || fact)
+    for_acc<NT>(acc, r0, n0, [&](int r, int c, float& v) { v *= __expf(cum[r * LDPF + c] - cr[c]); });
+  if (fact) return;
   for_acc<NT>(acc, r0, n0, [&](int r, int c, float& v) {
     float s = 0.f;
     const float ci = cum[r * LDPF + c];
@@ -327,6 +354,7 @@ __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
   bf16* dse_s = sin_s + P * LDN;
   float* dcl_s = reinterpret_cast<float*>(dse_s + P * LDN);
 
+  __shared__ int exact_s[4];
   const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
   const SIdx ix{L, H, NC};
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -351,31 +379,49 @@ __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
     if (tid < P) dcl_s[tid] = 0.f;
     cum_decay(cum, dt_s, Ah);
     const float* cl = cum + (C - 1) * LDPF;
-    // (1) dCB[i,j] = sum_p dy[i,p] e^{c_i-c_j} dBx[j,p]   (j <= i)
+    if (warp < 4) {
+      const bool ok = block_span_ok(cum, warp);
+      if (lane == 0) exact_s[warp] = !ok;
+    }
+    __syncthreads();
+    // (1) dCB[i,j] = sum_p dy[i,p] e^{c_i-c_j} dBx[j,p]   (j <= i); diagonal blocks factorised
+    //     at row r0 like the others unless their decay span is too wide (exact pass below)
     {
       const int I = mt, r0 = 16 * I;
       float acc[2][4];
       zero_acc<2>(acc);
       const int n0 = 16 * nq;  // j columns [n0, n0+16)
-      if (I > 0 && n0 < r0) {
+      if (n0 < r0 || (n0 == r0 && !exact_s[I])) {
         const float* cr = cum + r0 * LDPF;
-        auto fa = [&](int ri, int kp) -> uint32_t {
-          return pack2(bf(dy_s[ri * LDP + kp]) * __expf(cum[ri * LDPF + kp] - cr[kp]),
-                       bf(dy_s[ri * LDP + kp + 1]) * __expf(cum[ri * LDPF + kp + 1] - cr[kp + 1]));
+        auto faf = [&](int ri, int kp) -> float2 {
+          return make_float2(bf(dy_s[ri * LDP + kp]) * __expf(cum[ri * LDPF + kp] - cr[kp]),
+                             bf(dy_s[ri * LDP + kp + 1]) * __expf(cum[ri * LDPF + kp + 1] - cr[kp + 1]));
         };
-        auto fb = [&](int kp, int nj) -> uint32_t {
-          return pack2(dbx(x_s, dt_s, nj, kp) * __expf(cr[kp] - cum[nj * LDPF + kp]),
-                       dbx(x_s, dt_s, nj, kp + 1) * __expf(cr[kp + 1] - cum[nj * LDPF + kp + 1]));
+        auto fbf = [&](int kp, int nj) -> float2 {
+          return make_float2(dbx(x_s, dt_s, nj, kp) * __expf(cr[kp] - cum[nj * LDPF + kp]),
+                             dbx(x_s, dt_s, nj, kp + 1) * __expf(cr[kp + 1] - cum[nj * LDPF + kp + 1]));
         };
-        warp_mma<2>(acc, fa, fb, r0, n0, 0, P);
+        if (n0 == r0) {  // diagonal block: two-term operands (its sums feed the cancelling dA)
+          warp_mma_split<2>(acc, faf, fbf, r0, n0, 0, P);
+        } else {
+          auto fa = [&](int ri, int kp) -> uint32_t { const float2 v = faf(ri, kp); return pack2(v.x, v.y); };
+          auto fb = [&](int kp, int nj) -> uint32_t { const float2 v = fbf(kp, nj); return pack2(v.x, v.y); };
+          warp_mma<2>(acc, fa, fb, r0, n0, 0, P);
+        }
       }
+      const bool fact_diag = n0 == r0 && !exact_s[I];
       for_acc<2>(acc, r0, n0, [&](int r, int c, float& v) {
-        const bool diag = c >= r0 && c < r0 + 16 && c <= r;  // written by the exact pass below
-        if (!diag) dcb_s[r * LDCC + c] = c >= r0 ? 0.f : v;
+        if (fact_diag) {
+          dcb_s[r * LDCC + c] = c <= r ? v : 0.f;
+        } else {
+          const bool diag = c >= r0 && c < r0 + 16 && c <= r;  // written by the exact pass below
+          if (!diag) dcb_s[r * LDCC + c] = c >= r0 ? 0.f : v;
+        }
       });
     }
-    // exact per-channel sums of the diagonal 16x16 blocks: one (i, j) pair per thread
+    // exact per-channel sums of the diagonal 16x16 blocks with a wide decay span: one (i, j) pair per thread
     for (int q = tid; q < 4 * 136; q += blockDim.x) {
+      if (!exact_s[q / 136]) continue;
       int i, j;
       tri_ij(q % 136, i, j);
       const int r = 16 * (q / 136) + i, c = 16 * (q / 136) + j;
@@ -409,21 +455,28 @@ __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
       float yd[2][4], yo[2][4], dd[2][4], ds[2][4];
       ydiag_tile<2>(yd, cb_s, x_s, dt_s, cum, I, n0);
       yoff_tile<2>(yo, c_s, sin_s, cum, I, n0);
-      // ddBx_diag[j,p] = sum_{i>=j} CB[i,j] dy[i,p] e^{c_i-c_j}
+      // ddBx_diag[j,p] = sum_{i>=j} CB[i,j] dy[i,p] e^{c_i-c_j}  (own block factorised unless exact)
       zero_acc<2>(dd);
-      for (int I2 = I + 1; I2 < 4; ++I2) {
+      const bool exact_i = exact_s[I];
+      for (int I2 = exact_i ? I + 1 : I; I2 < 4; ++I2) {
         const int r2 = 16 * I2;
         const float* cr = cum + r2 * LDPF;
-        auto fa = [&](int rj, int ki) -> uint32_t {
-          return pack2(cb_s[(r2 + ki) * LDCC + rj], cb_s[(r2 + ki + 1) * LDCC + rj]);
+        auto faf = [&](int rj, int ki) -> float2 {
+          const int i0 = r2 + ki;
+          return make_float2(i0 >= rj ? cb_s[i0 * LDCC + rj] : 0.f, i0 + 1 >= rj ? cb_s[(i0 + 1) * LDCC + rj] : 0.f);
         };
-        auto fb = [&](int ki, int np) -> uint32_t {
-          return pack2(bf(dy_s[(r2 + ki) * LDP + np]) * __expf(cum[(r2 + ki) * LDPF + np] - cr[np]),
-                       bf(dy_s[(r2 + ki + 1) * LDP + np]) * __expf(cum[(r2 + ki + 1) * LDPF + np] - cr[np]));
+        auto fa = [&](int rj, int ki) -> uint32_t { const float2 v = faf(rj, ki); return pack2(v.x, v.y); };
+        auto fbf = [&](int ki, int np) -> float2 {
+          return make_float2(bf(dy_s[(r2 + ki) * LDP + np]) * __expf(cum[(r2 + ki) * LDPF + np] - cr[np]),
+                             bf(dy_s[(r2 + ki + 1) * LDP + np]) * __expf(cum[(r2 + ki + 1) * LDPF + np] - cr[np]));
         };
+        auto fb = [&](int ki, int np) -> uint32_t { const float2 v = fbf(ki, np); return pack2(v.x, v.y); };
         float tacc[2][4];
         zero_acc<2>(tacc);
-        warp_mma<2>(tacc, fa, fb, r0, n0, 0, 16);
+        if (I2 == I)  // own block: two-term operands
+          warp_mma_split<2>(tacc, faf, fbf, r0, n0, 0, 16);
+        else
+          warp_mma<2>(tacc, fa, fb, r0, n0, 0, 16);
         const int g = lane >> 2, t = lane & 3;
 #pragma unroll
         for (int j = 0; j < 2; ++j)
@@ -436,7 +489,7 @@ __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
       for_acc<2>(dd, r0, n0, [&](int r, int c, float& v) {
         float s = 0.f;
         const float cj = cum[r * LDPF + c];
-        for (int i = r; i < r0 + 16; ++i)
+        for (int i = r; exact_i && i < r0 + 16; ++i)
           s += cb_s[i * LDCC + r] * bf(dy_s[i * LDP + c]) * __expf(fmaxf(cum[i * LDPF + c] - cj, -20.f));
         v += s;
       });
