@@ -32,6 +32,9 @@ class Dense(nn.Module):
         lecun_normal_(self.kernel.data, d_in)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if ops.use_cuda(x) and x.dtype == torch.bfloat16:
+            from ..ops import kernels as K
+            return K.linear_multi(x, [(self.kernel, self.bias)])[0]
         return ops.linear(x, self.kernel, self.bias)
 
 

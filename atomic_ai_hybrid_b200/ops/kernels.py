@@ -406,6 +406,80 @@ def dt_act(u):
     return _DtAct.apply(u.contiguous())
 
 
+# ----------------------------------------------------------------- dense projections
+_ADDMM_F32 = None  # whether cuBLAS accumulates bf16 products straight into fp32 (probed once)
+
+
+def _wgrad_acc(acc, x2, dy2):
+    """``acc (in, out) fp32 += x2^T dy2`` with bf16 inputs, accumulated by the GEMM
+    itself (beta = 1, fp32 output) when the library offers it."""
+    global _ADDMM_F32
+    if _ADDMM_F32 is not False:
+        try:
+            torch.addmm(acc, x2.t(), dy2, out_dtype=torch.float32, out=acc)
+            _ADDMM_F32 = True
+            return
+        except (RuntimeError, TypeError):
+            _ADDMM_F32 = False
+    acc.add_((x2.t() @ dy2).float())
+
+
+class _MultiLinear(torch.autograd.Function):
+    """Several projections of one input, ``y_i = x W_i (+ b_i)`` (cuBLAS).  The
+    backward accumulates ``dx = sum_i dy_i W_i^T`` in one buffer (beta = 1) instead of
+    separate gradients that autograd adds, and adds the weight gradients of
+    store-backed matrices straight into their fp32 accumulators."""
+
+    @staticmethod
+    def forward(ctx, x, n, *wb):
+        ws, bs = wb[:n], wb[n:]
+        x2 = x.reshape(-1, x.shape[-1])
+        outs = []
+        for w, b in zip(ws, bs):
+            wc = w if w.dtype == x.dtype else w.to(x.dtype)
+            y = torch.addmm(b.to(x.dtype), x2, wc) if b is not None else torch.mm(x2, wc)
+            outs.append(y.view(*x.shape[:-1], w.shape[1]))
+        ctx.save_for_backward(x, *ws)
+        ctx.n, ctx.has_b = n, [b is not None for b in bs]
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *dys):
+        x, *ws = ctx.saved_tensors
+        x2 = x.reshape(-1, x.shape[-1])
+        dx = None
+        dws, dbs = [], []
+        for w, dy, hb in zip(ws, dys, ctx.has_b):
+            if dy is None:
+                dws.append(None)
+                dbs.append(None)
+                continue
+            dy2 = dy.reshape(-1, dy.shape[-1]).to(x.dtype)
+            wc = w if w.dtype == x.dtype else w.to(x.dtype)
+            if ctx.needs_input_grad[0]:
+                if dx is None:
+                    dx = torch.mm(dy2, wc.t())
+                else:
+                    torch.addmm(dx, dy2, wc.t(), out=dx)
+            acc = getattr(w, "_ahb_grad_acc", None)
+            if acc is not None and w.dtype != torch.float32:
+                _wgrad_acc(acc.view(w.shape), x2, dy2)
+                dws.append(None)
+            else:
+                dws.append((x2.t() @ dy2).to(w.dtype))
+            dbs.append(dy2.sum(0, dtype=torch.float32) if hb else None)
+        if dx is not None:
+            dx = dx.view(x.shape)
+        return (dx, None, *dws, *dbs)
+
+
+def linear_multi(x, pairs):
+    """``[(kernel (in, out), bias or None), ...]`` -> the projections of ``x``."""
+    ws = [w for w, _ in pairs]
+    bs = [b for _, b in pairs]
+    return _MultiLinear.apply(x, len(pairs), *ws, *bs)
+
+
 class _Router(torch.autograd.Function):
     """Fused cosine router: returns the differentiable (gate, sum_t softmax(l),
     sum_t lse^2) and the non-differentiable (top_idx, expert counts, statistics)."""
@@ -476,15 +550,17 @@ def gdn2_layer(mod, x):
 def _gdn2_layer_fused(mod, x):
     Bsz, L, d = x.shape
     H, D = mod.n_heads, mod.d_head
-    q = conv1d(mod.q_proj(x), mod.q_conv_w, mod.q_conv_b, True)
-    k = conv1d(mod.k_proj(x), mod.k_conv_w, mod.k_conv_b, True)
-    v = conv1d(mod.v_proj(x), mod.v_conv_w, mod.v_conv_b, True, 50.0)
+    projs = [mod.q_proj, mod.k_proj, mod.v_proj, mod.erase_gate, mod.write_gate, mod.decay_proj, mod.out_gate]
+    qp, kp, vp, bp, wp, fp, og = linear_multi(x, [(m.kernel, m.bias) for m in projs])
+    q = conv1d(qp, mod.q_conv_w, mod.q_conv_b, True)
+    k = conv1d(kp, mod.k_conv_w, mod.k_conv_b, True)
+    v = conv1d(vp, mod.v_conv_w, mod.v_conv_b, True, 50.0)
     q = l2norm_heads(q.view(Bsz, L, H, D))
     k = l2norm_heads(k.view(Bsz, L, H, D))
-    bg, wg, g = gdn_gates(mod.erase_gate(x), mod.write_gate(x), mod.decay_proj(x), mod.decay_a, D)
+    bg, wg, g = gdn_gates(bp, wp, fp, mod.decay_a, D)
     shp = (Bsz, L, H, D)
     o = gdn2(q, k, v.view(shp), wg.view(shp), bg.view(shp), g.view(shp), 1.0, mod.cfg.gdn_chunk)
-    o = norm_gate(o.reshape(Bsz, L, d).to(x.dtype), mod.out_gate(x), mod.out_norm.scale, 1e-6, zclip=1e2)
+    o = norm_gate(o.reshape(Bsz, L, d).to(x.dtype), og, mod.out_norm.scale, 1e-6, zclip=1e2)
     return mod.out_proj(o)
 
 
@@ -520,9 +596,7 @@ def mamba2_layer(mod, x):
     x_bc, res = xz[..., :di], xz[..., di:]
     x_conv = conv1d(x_bc, mod.conv_w, mod.conv_b, True)
     A = -torch.exp(mod.A_log.float().clamp(-20.0, 20.0))
-    Bm = mod.B_proj(x_bc)
-    Cm = mod.C_proj(x_bc)
-    dtp = mod.dt_proj(x_bc)
+    Bm, Cm, dtp = linear_multi(x_bc, [(m.kernel, m.bias) for m in (mod.B_proj, mod.C_proj, mod.dt_proj)])
     dt = dt_act(dtp) if fused else F.softplus(dtp).clamp(1e-2, 1.0)
     y = ssd(dt.view(Bsz, L, Hs, P), A, Bm.clamp(-1e3, 1e3), Cm.clamp(-1e3, 1e3), x_conv.view(Bsz, L, Hs, P),
             mod.cfg.ssd_chunk)

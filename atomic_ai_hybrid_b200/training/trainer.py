@@ -87,6 +87,11 @@ class Trainer:
         self._loss_sum = torch.zeros((), device=dev)
         self._n_micro = 0
         self.cuda_graph = cuda_graph and dev.type == "cuda"
+        if dev.type == "cuda":
+            # the model's construction-time parameter tensors were replaced by views of the
+            # flat store: hand their cached blocks back so that libraries allocating outside
+            # PyTorch's cache (cuBLAS handles and workspaces) find memory
+            torch.cuda.empty_cache()
         self._graph = None
         self._graph_key = None
         self.graph_kernel_launches = 0

@@ -230,3 +230,35 @@ def test_fused_router_matches_torch(E, k, d, monkeypatch):
     _close(dx1, dx0, 2e-2, 1e-4, "dx")
     _close(dr1, dr0, 1e-3, 1e-5, "drouter")
     _close(dt1, dt0, 1e-3, 1e-6, "dtemp")
+
+
+def test_linear_multi_grads():
+    """Several projections of one input: outputs, input gradient and weight gradients
+    (added straight into fp32 accumulators) equal the plain PyTorch expressions."""
+    torch.manual_seed(8)
+    x = torch.randn(3, 100, 256, device=DEV).to(torch.bfloat16)
+    ws = [(torch.randn(256, n, device=DEV) * 0.05).to(torch.bfloat16) for n in (256, 128, 512)]
+    bs = [None, torch.randn(128, device=DEV), torch.randn(512, device=DEV)]
+    accs = [torch.zeros(w.shape, device=DEV) for w in ws]
+    wk = [w.clone().requires_grad_(True) for w in ws]
+    for w, a in zip(wk, accs):
+        w._ahb_grad_acc = a
+    bk = [None if b is None else b.clone().requires_grad_(True) for b in bs]
+    xk = x.clone().requires_grad_(True)
+    outs = K.linear_multi(xk, list(zip(wk, bk)))
+    gs = [torch.randn_like(o) for o in outs]
+    torch.autograd.backward(list(outs), gs)
+    xr = x.float().clone().requires_grad_(True)
+    wr = [w.float().clone().requires_grad_(True) for w in ws]
+    br = [None if b is None else b.clone().requires_grad_(True) for b in bs]
+    refs = [xr @ w + (0 if b is None else b) for w, b in zip(wr, br)]
+    torch.autograd.backward(refs, [g.float() for g in gs])
+    for o, r in zip(outs, refs):
+        _close(o, r.detach(), 2e-2, 5e-2, "y")
+    _close(xk.grad, xr.grad, 2e-2, 1e-1, "dx")
+    for a, w, wkk in zip(accs, wr, wk):
+        assert wkk.grad is None  # accumulated into the fp32 buffer instead
+        _close(a, w.grad, 1e-2, 1e-1, "dW")
+    for b, r in zip(bk, br):
+        if b is not None:
+            _close(b.grad, r.grad, 1e-3, 1e-2, "db")
