@@ -97,6 +97,29 @@ AHB_DEVICE void load_chunk_tile_f32(float* dst, int ld, const float* src, int ro
   }
 }
 
+// Asynchronous 16-byte global -> shared copies (the recurrence kernels prefetch the next
+// chunk's tiles while they compute on the current one).
+AHB_DEVICE void cp16(void* dst, const void* src) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(src) : "memory");
+}
+AHB_DEVICE void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+AHB_DEVICE void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+AHB_DEVICE void cp_chunk_tile(bf16* dst, const bf16* src, int nthreads) {  // C x D bf16 -> [C][LDB]
+  for (int i = threadIdx.x; i < C * (D / 8); i += nthreads) {
+    const int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
+    cp16(dst + r * LDB + c8, src + r * D + c8);
+  }
+}
+AHB_DEVICE void cp_f32_tile(float* dst, int ld, const float* src, int rows, int cols, int nthreads) {
+  for (int i = threadIdx.x; i < rows * (cols / 4); i += nthreads) {
+    const int r = i / (cols / 4), c4 = (i % (cols / 4)) * 4;
+    cp16(dst + r * ld + c4, src + r * cols + c4);
+  }
+}
+
 // Store an accumulator tile (NT n-tiles) as bf16 pairs: dst[row*ld + col]
 template <int NT, class F>
 AHB_DEVICE void store_pairs(float (*acc)[4], int m0, int n0, F&& put) {
@@ -341,7 +364,9 @@ __global__ void __launch_bounds__(NTH, 1) gdn_intra_fwd_kernel(
 
 // ============================================================ inter forward
 // smem: wt, qg, kg bf16 [C][LDB]; u bf16 [C][LDV]; aqk f32 [C][LDC]; h bf16 [D][LDV]; vn bf16 [C][LDV]; gcl f32 [D]
-constexpr size_t SMEM_INTER_F = 3 * C * LDB * 2 + C * LDV * 2 + C * LDC * 4 + D * LDV * 2 + C * LDV * 2 + D * 4;
+// per buffer: wt, qg, kg bf16 [C][LDB]; u bf16 [C][LDV]; aqk f32 [C][LDC]; gcl f32 [D]  (two buffers)
+constexpr size_t INTER_F_BUF = 3 * C * LDB * 2 + C * LDV * 2 + C * LDC * 4 + D * 4;
+constexpr size_t SMEM_INTER_F = 2 * INTER_F_BUF + D * LDV * 2 + C * LDV * 2;
 
 __global__ void __launch_bounds__(128) gdn_inter_fwd_kernel(
     const bf16* __restrict__ wt, const bf16* __restrict__ u, const bf16* __restrict__ qg,
@@ -349,41 +374,61 @@ __global__ void __launch_bounds__(128) gdn_inter_fwd_kernel(
     int H, int NC, const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final,
     bf16* __restrict__ h_store, bf16* __restrict__ vn_store) {
   extern __shared__ __align__(16) unsigned char smem[];
-  bf16* wt_s = reinterpret_cast<bf16*>(smem);
-  bf16* qg_s = wt_s + C * LDB;
-  bf16* kg_s = qg_s + C * LDB;
-  bf16* u_s = kg_s + C * LDB;
-  float* aqk_s = reinterpret_cast<float*>(u_s + C * LDV);
-  bf16* h_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
+  bf16* h_s = reinterpret_cast<bf16*>(smem + 2 * INTER_F_BUF);
   bf16* vn_s = h_s + D * LDV;
-  float* gcl_s = reinterpret_cast<float*>(vn_s + C * LDV);
 
   const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const Idx ix{L, H, NC};
   const int tid = threadIdx.x, w = tid >> 5;
+  auto buf = [&](int i, bf16*& wt_s, bf16*& qg_s, bf16*& kg_s, bf16*& u_s, float*& aqk_s, float*& gcl_s) {
+    unsigned char* base = smem + (size_t)i * INTER_F_BUF;
+    wt_s = reinterpret_cast<bf16*>(base);
+    qg_s = wt_s + C * LDB;
+    kg_s = qg_s + C * LDB;
+    u_s = kg_s + C * LDB;
+    aqk_s = reinterpret_cast<float*>(u_s + C * LDV);
+    gcl_s = aqk_s + C * LDC;
+  };
+  // prefetch chunk n's tiles into buffer n & 1 (one commit group)
+  auto issue = [&](int n) {
+    bf16 *wt_s, *qg_s, *kg_s, *u_s;
+    float *aqk_s, *gcl_s;
+    buf(n & 1, wt_s, qg_s, kg_s, u_s, aqk_s, gcl_s);
+    const int64_t cb = ix.chunk(b, h, n);
+    cp_chunk_tile(wt_s, wt + cb * C * D, 128);
+    cp_chunk_tile(qg_s, qg + cb * C * D, 128);
+    cp_chunk_tile(kg_s, kg + cb * C * D, 128);
+    for (int i = tid; i < C * (BV / 8); i += 128) {
+      const int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
+      cp16(u_s + r * LDV + c8, u + cb * C * D + r * D + vb * BV + c8);
+    }
+    cp_f32_tile(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
+    if (tid < D / 4) cp16(gcl_s + 4 * tid, gcl + cb * D + 4 * tid);
+    cp_commit();
+  };
   // state slice: rows d in [32w, 32w+32) (2 m-tiles), cols [0, 32) of this value block
   float hr[2][4][4];
   for (int mi = 0; mi < 2; ++mi)
     for_acc<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
       x = h0 ? h0[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
     });
+  issue(0);
   for (int n = 0; n < NC; ++n) {
     const int64_t cb = ix.chunk(b, h, n);
+    bf16 *wt_s, *qg_s, *kg_s, *u_s;
+    float *aqk_s, *gcl_s;
+    buf(n & 1, wt_s, qg_s, kg_s, u_s, aqk_s, gcl_s);
     for (int mi = 0; mi < 2; ++mi)
       store_pairs<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
         st_bf16x2(h_s + r * LDV + c, x0, x1);
         if (h_store) st_bf16x2(h_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
       });
-    load_chunk_tile(wt_s, wt + cb * C * D, 128);
-    load_chunk_tile(qg_s, qg + cb * C * D, 128);
-    load_chunk_tile(kg_s, kg + cb * C * D, 128);
-    for (int i = tid; i < C * (BV / 8); i += 128) {
-      int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
-      *reinterpret_cast<uint4*>(u_s + r * LDV + c8) =
-          *reinterpret_cast<const uint4*>(u + cb * C * D + r * D + vb * BV + c8);
+    if (n + 1 < NC) {
+      issue(n + 1);  // the other buffer was released by the barrier that ended chunk n-1
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
     }
-    load_chunk_tile_f32(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
-    if (tid < D) gcl_s[tid] = gcl[cb * D + tid];
     __syncthreads();
     float accv[4][4], acco[4][4];
     zero_acc<4>(accv);
@@ -419,8 +464,10 @@ __global__ void __launch_bounds__(128) gdn_inter_fwd_kernel(
 }
 
 // ============================================================ inter backward (reverse recurrence)
-// smem: wt, qg, kg bf16 [C][LDB]; aqk f32 [C][LDC]; do bf16 [C][LDV]; dh bf16 [D][LDV]; dvn bf16 [C][LDV]; gcl f32[D]
-constexpr size_t SMEM_INTER_B = 3 * C * LDB * 2 + C * LDC * 4 + C * LDV * 2 + D * LDV * 2 + C * LDV * 2 + D * 4;
+// per buffer: wt, qg, kg bf16 [C][LDB]; aqk f32 [C][LDC]; do bf16 [C][LDV]; gcl f32 [D] (two buffers);
+// dh bf16 [D][LDV]; dvn bf16 [C][LDV]
+constexpr size_t INTER_B_BUF = 3 * C * LDB * 2 + C * LDC * 4 + C * LDV * 2 + D * 4;
+constexpr size_t SMEM_INTER_B = 2 * INTER_B_BUF + D * LDV * 2 + C * LDV * 2;
 
 __global__ void __launch_bounds__(128) gdn_inter_bwd_kernel(
     const bf16* __restrict__ wt, const bf16* __restrict__ qg, const bf16* __restrict__ kg,
@@ -428,40 +475,59 @@ __global__ void __launch_bounds__(128) gdn_inter_bwd_kernel(
     int H, int NC, const float* __restrict__ dh_final, bf16* __restrict__ dh_store, bf16* __restrict__ dvn_store,
     float* __restrict__ dh0) {
   extern __shared__ __align__(16) unsigned char smem[];
-  bf16* wt_s = reinterpret_cast<bf16*>(smem);
-  bf16* qg_s = wt_s + C * LDB;
-  bf16* kg_s = qg_s + C * LDB;
-  float* aqk_s = reinterpret_cast<float*>(kg_s + C * LDB);
-  bf16* do_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
-  bf16* dh_s = do_s + C * LDV;
+  bf16* dh_s = reinterpret_cast<bf16*>(smem + 2 * INTER_B_BUF);
   bf16* dvn_s = dh_s + D * LDV;
-  float* gcl_s = reinterpret_cast<float*>(dvn_s + C * LDV);
 
   const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const Idx ix{L, H, NC};
   const int tid = threadIdx.x, w = tid >> 5;
+  auto buf = [&](int i, bf16*& wt_s, bf16*& qg_s, bf16*& kg_s, float*& aqk_s, bf16*& do_s, float*& gcl_s) {
+    unsigned char* base = smem + (size_t)i * INTER_B_BUF;
+    wt_s = reinterpret_cast<bf16*>(base);
+    qg_s = wt_s + C * LDB;
+    kg_s = qg_s + C * LDB;
+    aqk_s = reinterpret_cast<float*>(kg_s + C * LDB);
+    do_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
+    gcl_s = reinterpret_cast<float*>(do_s + C * LDV);
+  };
+  auto issue = [&](int n, int slot) {
+    bf16 *wt_s, *qg_s, *kg_s, *do_s;
+    float *aqk_s, *gcl_s;
+    buf(slot, wt_s, qg_s, kg_s, aqk_s, do_s, gcl_s);
+    const int64_t cb = ix.chunk(b, h, n);
+    cp_chunk_tile(wt_s, wt + cb * C * D, 128);
+    cp_chunk_tile(qg_s, qg + cb * C * D, 128);
+    cp_chunk_tile(kg_s, kg + cb * C * D, 128);
+    cp_f32_tile(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
+    for (int i = tid; i < C * (BV / 8); i += 128) {
+      const int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
+      cp16(do_s + r * LDV + c8, dout + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c8);
+    }
+    if (tid < D / 4) cp16(gcl_s + 4 * tid, gcl + cb * D + 4 * tid);
+    cp_commit();
+  };
   float dr[2][4][4];
   for (int mi = 0; mi < 2; ++mi)
     for_acc<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
       x = dh_final ? dh_final[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
     });
-  for (int n = NC - 1; n >= 0; --n) {
+  issue(NC - 1, 0);
+  for (int n = NC - 1, it = 0; n >= 0; --n, ++it) {
     const int64_t cb = ix.chunk(b, h, n);
+    bf16 *wt_s, *qg_s, *kg_s, *do_s;
+    float *aqk_s, *gcl_s;
+    buf(it & 1, wt_s, qg_s, kg_s, aqk_s, do_s, gcl_s);
     for (int mi = 0; mi < 2; ++mi)
       store_pairs<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
         st_bf16x2(dh_s + r * LDV + c, x0, x1);
         st_bf16x2(dh_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
       });
-    load_chunk_tile(wt_s, wt + cb * C * D, 128);
-    load_chunk_tile(qg_s, qg + cb * C * D, 128);
-    load_chunk_tile(kg_s, kg + cb * C * D, 128);
-    load_chunk_tile_f32(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
-    for (int i = tid; i < C * (BV / 8); i += 128) {
-      int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
-      *reinterpret_cast<uint4*>(do_s + r * LDV + c8) =
-          *reinterpret_cast<const uint4*>(dout + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c8);
+    if (n > 0) {
+      issue(n - 1, (it + 1) & 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
     }
-    if (tid < D) gcl_s[tid] = gcl[cb * D + tid];
     __syncthreads();
     // dv_new = Aqk^T do + kg dh
     float acc[4][4];

@@ -41,6 +41,24 @@ AHB_DEVICE void atomic_min_pos(float* a, float v) { atomicMin(reinterpret_cast<i
 
 // ------------------------------------------------------------------ forward
 // knT: 3 x (EP, d) bf16 (hi, mid, lo of kn^T).
+AHB_DEVICE void cp16z(void* dst, const void* src, bool valid) {  // zero-filled when !valid
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(src), "r"(n) : "memory");
+}
+AHB_DEVICE void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+AHB_DEVICE void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int NTE>
+__host__ __device__ constexpr size_t fwd_stage_bytes() { return (size_t)(TOKC + 3 * NTE * 8) * LDX * 2; }
+template <int NTE>
+__host__ __device__ constexpr size_t fwd_smem_bytes() {
+  return 2 * fwd_stage_bytes<NTE>() > (size_t)TOKC * (NTE * 8 + 1) * 4 ? 2 * fwd_stage_bytes<NTE>()
+                                                                       : (size_t)TOKC * (NTE * 8 + 1) * 4;
+}
+
+// The x and kn slices are double-buffered with cp.async: slice s+1 loads while slice s multiplies.
 template <int NTE>
 __global__ void __launch_bounds__(NT) router_fwd_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ knT, const float* __restrict__ temp_p,
@@ -48,46 +66,61 @@ __global__ void __launch_bounds__(NT) router_fwd_kernel(
     float* __restrict__ logits, float* __restrict__ cosv, float* __restrict__ rn_out, int64_t* __restrict__ top_idx,
     float* __restrict__ gate, float* __restrict__ probs_sum, float* __restrict__ scal, float* __restrict__ counts) {
   constexpr int EP = NTE * 8;
-  constexpr int GEMM_BYTES = (TOKC + 3 * EP) * LDX * 2;
-  constexpr int ROW_BYTES = TOKC * (EP + 1) * 4;
-  // the staged GEMM tiles and the logits rows that follow them share the buffer
-  __shared__ __align__(16) unsigned char raw[GEMM_BYTES > ROW_BYTES ? GEMM_BYTES : ROW_BYTES];
-  bf16* xs = reinterpret_cast<bf16*>(raw);
-  bf16* ks0 = xs + TOKC * LDX;
+  constexpr size_t STAGE = fwd_stage_bytes<NTE>();
+  // two staged (x, kn) slices; after the loop the same memory holds the logits rows
+  extern __shared__ __align__(16) unsigned char raw[];
   float(*cs)[EP + 1] = reinterpret_cast<float(*)[EP + 1]>(raw);
   __shared__ float ssh[TOKC];
   __shared__ float psum[EMAX], csum[EMAX];
   const int64_t t0 = (int64_t)blockIdx.x * TOKC;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  float acc[NTE][4];
-  zero_acc<NTE>(acc);
-  float ss[4] = {0.f, 0.f, 0.f, 0.f};  // rows (tid >> 3) + 16 q of every x tile
-  for (int c0 = 0; c0 < d; c0 += DS) {
-    __syncthreads();
+  auto xs_of = [&](int sl) { return reinterpret_cast<bf16*>(raw + sl * STAGE); };
+  auto ks_of = [&](int sl) { return xs_of(sl) + TOKC * LDX; };
+  auto issue = [&](int c0, int sl) {
+    bf16* xs = xs_of(sl);
+    bf16* ks = ks_of(sl);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int idx = tid + NT * q, r = idx >> 3, c8 = (idx & 7) * 8;
       const int64_t t = t0 + r;
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (t < T) u = *reinterpret_cast<const uint4*>(x + t * d + c0 + c8);
-      *reinterpret_cast<uint4*>(xs + r * LDX + c8) = u;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        ss[q] += f.x * f.x + f.y * f.y;
-      }
+      cp16z(xs + r * LDX + c8, x + (t < T ? t : 0) * d + c0 + c8, t < T);
     }
     for (int idx = tid; idx < 3 * EP * 8; idx += NT) {
       const int s = idx / (EP * 8), rem = idx % (EP * 8), e = rem >> 3, c8 = (rem & 7) * 8;
-      *reinterpret_cast<uint4*>(ks0 + (s * EP + e) * LDX + c8) =
-          *reinterpret_cast<const uint4*>(knT + ((int64_t)s * EP + e) * d + c0 + c8);
+      cp16z(ks + (s * EP + e) * LDX + c8, knT + ((int64_t)s * EP + e) * d + c0 + c8, true);
+    }
+    cp_commit();
+  };
+  float acc[NTE][4];
+  zero_acc<NTE>(acc);
+  float ss[4] = {0.f, 0.f, 0.f, 0.f};  // rows (tid >> 3) + 16 q of every x slice
+  const int nsl = d / DS;
+  issue(0, 0);
+  for (int si = 0; si < nsl; ++si) {
+    if (si + 1 < nsl) {
+      issue((si + 1) * DS, (si + 1) & 1);  // the other stage was released by the previous barrier
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
     }
     __syncthreads();
+    const bf16* xs = xs_of(si & 1);
+    const bf16* ks = ks_of(si & 1);
 #pragma unroll
-    for (int s = 0; s < 3; ++s) warp_mma<NTE>(acc, RowA16{xs, LDX}, NKB16{ks0 + s * EP * LDX, LDX}, 16 * w, 0, 0, DS);
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + NT * q, r = idx >> 3, c8 = (idx & 7) * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(xs + r * LDX + c8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        ss[q] += f.x * f.x + f.y * f.y;
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < 3; ++s) warp_mma<NTE>(acc, RowA16{xs, LDX}, NKB16{ks + s * EP * LDX, LDX}, 16 * w, 0, 0, DS);
+    __syncthreads();
   }
-  __syncthreads();  // the row buffer overwrites the staged tiles
   for_acc<NTE>(acc, 16 * w, 0, [&](int r, int c, float& v) { cs[r][c] = v; });
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -401,8 +434,18 @@ void ahb_router_fwd(const void* x, const void* knT3, const float* temp, const fl
   if (T <= 0) return;
   const int grid = (int)((T + TOKC - 1) / TOKC);
   const int EP = ahb_router_padded_experts(E);
-#define RF(N) router_fwd_kernel<N><<<grid, NT, 0, st>>>((const bf16*)x, (const bf16*)knT3, temp, bias, noise, T, d, \
-    E, k, logits, cosv, rn, top_idx, gate, probs_sum, scal, counts)
+#define RF(N)                                                                                                   \
+  do {                                                                                                          \
+    static bool init = false;                                                                                   \
+    if (!init) {                                                                                                \
+      cudaFuncSetAttribute(router_fwd_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                           (int)fwd_smem_bytes<N>());                                                           \
+      init = true;                                                                                              \
+    }                                                                                                           \
+    router_fwd_kernel<N><<<grid, NT, fwd_smem_bytes<N>(), st>>>((const bf16*)x, (const bf16*)knT3, temp, bias,   \
+                                                               noise, T, d, E, k, logits, cosv, rn, top_idx, gate, \
+                                                               probs_sum, scal, counts);                        \
+  } while (0)
   if (EP == 16) RF(2); else if (EP == 32) RF(4); else if (EP == 48) RF(6); else RF(8);
 #undef RF
 }
