@@ -173,8 +173,7 @@ class CheckpointManager:
             for st, opt, ep in _stores(trainer):
                 for s in st.segs:
                     name = flax_path(s.name)
-                    rng = _expert_range(s, ep)
-                    t = _lookup(params, name, rng)
+                    t = _find(params, name, s, ep)
                     if t is None or tuple(t.shape) != tuple(s.shape):
                         fresh.append(name)
                         continue
@@ -183,7 +182,7 @@ class CheckpointManager:
                     if s.owner == st.rank:
                         st.master_view(s).copy_(t32)
                         o = s.offset - st.lo
-                        mu, nu = _lookup(moments, f"mu/{name}", rng), _lookup(moments, f"nu/{name}", rng)
+                        mu, nu = _find(moments, f"mu/{name}", s, ep), _find(moments, f"nu/{name}", s, ep)
                         if load_optimizer and mu is not None and tuple(mu.shape) == tuple(s.shape):
                             opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(st.device))
                             opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(st.device))
@@ -205,7 +204,7 @@ def _stores(trainer):
 
 def _expert_range(s, ep: bool):
     """Global expert rows [lo, hi) held by a segment of the expert-parallel store."""
-    if not ep:
+    if not ep or not getattr(s.param, "_ahb_ep_local", False):
         return None
     from ..parallel.context import get_parallel_context
     El = s.shape[0]
@@ -213,12 +212,64 @@ def _expert_range(s, ep: bool):
     return lo, lo + El
 
 
+def _tp_spec(s):
+    """``(dim, parts, rank, world)`` of a tensor-parallel piece (``parallel.tp``), else None."""
+    from ..parallel.tp import shard_spec
+    spec = shard_spec(s.param)
+    if spec is None:
+        return None
+    from ..parallel.context import get_parallel_context
+    pc = get_parallel_context()
+    if pc.tp_world <= 1:
+        return None
+    return spec[0], spec[1], pc.tp_rank, pc.tp_world
+
+
 def _key(s, ep: bool) -> str:
     """Tensor name in the files: the flax path, plus ``#experts[lo:hi]`` for a block of
-    routed experts held by one expert-parallel rank."""
+    routed experts held by one expert-parallel rank, or ``#tp[r/W]`` for the piece of
+    tensor-parallel rank ``r`` of ``W``."""
     name = flax_path(s.name)
     rng = _expert_range(s, ep)
-    return name if rng is None else f"{name}#experts[{rng[0]}:{rng[1]}]"
+    if rng is not None:
+        return f"{name}#experts[{rng[0]}:{rng[1]}]"
+    spec = _tp_spec(s)
+    if spec is not None:
+        return f"{name}#tp[{spec[2]}/{spec[3]}]"
+    return name
+
+
+def _find(tensors: Dict[str, torch.Tensor], name: str, s, ep: bool):
+    spec = _tp_spec(s)
+    if spec is not None:
+        return _lookup_tp(tensors, name, spec)
+    return _lookup(tensors, name, _expert_range(s, ep))
+
+
+def _lookup_tp(tensors: Dict[str, torch.Tensor], name: str, spec):
+    """This rank's tensor-parallel piece of ``name``: stored directly, cut from the
+    full tensor, or re-cut from the pieces of a run with another tensor-parallel size."""
+    from ..parallel.tp import shard_tensor, unshard_tensors
+    dim, parts, rank, world = spec
+    t = tensors.get(f"{name}#tp[{rank}/{world}]")
+    if t is not None:
+        return t
+    full = tensors.get(name)
+    if full is None:
+        prefix = name + "#tp["
+        pieces = {}
+        for key, v in tensors.items():
+            if key.startswith(prefix):
+                r, w = (int(x) for x in key[len(prefix):-1].split("/"))
+                pieces[(w, r)] = v
+        worlds = sorted({w for w, _ in pieces})
+        for w in worlds:
+            if all((w, r) in pieces for r in range(w)):
+                full = unshard_tensors([pieces[(w, r)] for r in range(w)], dim, parts)
+                break
+    if full is None:
+        return None
+    return shard_tensor(full, dim, parts, world, rank)
 
 
 def _lookup(tensors: Dict[str, torch.Tensor], name: str, rng):

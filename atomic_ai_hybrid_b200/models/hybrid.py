@@ -28,6 +28,7 @@ import torch.nn as nn
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
+from ..parallel.tp import get_tp
 from .layers import Dense, RMSNorm
 from .mixers import MLA, GatedDeltaNet2, Mamba2
 from .moe import MoE
@@ -240,6 +241,11 @@ class HybridMoEModel(nn.Module):
         """Returns ``(hidden_or_logits, stats)`` where ``stats`` is a list with one
         dict of router statistics per MoE."""
         Bsz, L = input_ids.shape
+        tp = get_tp()
+        if tp is not None:
+            # sequence parallel: this rank embeds (and later scores) its block of the tokens
+            tp.set_batch(Bsz, L)
+            input_ids = tp.local_tokens(input_ids)
         x = self.embed(input_ids, self.compute_dtype)
         cos, sin = self.rope(L, x.device) if self.has_mla() else (None, None)
         stats: List[Dict] = []
@@ -287,6 +293,12 @@ class HybridMoEModel(nn.Module):
         if return_hidden:
             return h, stats
         return h @ self.lm_weight().to(h.dtype).t(), stats
+
+    def token_shard(self, t: torch.Tensor) -> torch.Tensor:
+        """The rows of a per-token ``(B, L, ...)`` tensor (labels) that this rank
+        scores: its sequence-parallel block under tensor parallelism, else all."""
+        tp = get_tp()
+        return tp.local_tokens(t) if tp is not None else t
 
     def lm_weight(self) -> torch.Tensor:
         """``(V, d)`` weight of the tied (or separate) LM head."""

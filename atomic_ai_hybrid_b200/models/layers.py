@@ -23,13 +23,37 @@ def lecun_normal_(t: torch.Tensor, fan_in: int) -> torch.Tensor:
         return nn.init.trunc_normal_(t, 0.0, std, -2 * std, 2 * std)
 
 
+def tp_world_rank():
+    """(world, rank) of the tensor-parallel group the model is built for."""
+    from ..parallel.context import get_parallel_context
+    pc = get_parallel_context()
+    return max(pc.tp_world, 1), pc.tp_rank
+
+
 class Dense(nn.Module):
-    def __init__(self, d_in: int, d_out: int, bias: bool = False, dtype=torch.float32):
+    """``tp``: ``""`` replicated; ``"col"`` output features split over the
+    tensor-parallel ranks (``"col2"``: the output is two equal blocks, each split);
+    ``"row"`` input features split.  ``d_in`` / ``d_out`` are the full sizes."""
+
+    def __init__(self, d_in: int, d_out: int, bias: bool = False, dtype=torch.float32, tp: str = ""):
         super().__init__()
         self.d_in, self.d_out = d_in, d_out
-        self.kernel = nn.Parameter(torch.empty(d_in, d_out, dtype=dtype))
-        self.bias = nn.Parameter(torch.zeros(d_out, dtype=torch.float32)) if bias else None
+        W, _ = tp_world_rank()
+        self.tp = tp if W > 1 else ""
+        li = d_in // W if self.tp == "row" else d_in
+        lo = d_out // W if self.tp in ("col", "col2") else d_out
+        if self.tp and (d_in if self.tp == "row" else d_out) % (W * (2 if self.tp == "col2" else 1)):
+            raise ValueError(f"Dense({d_in}, {d_out}) does not split over {W} tensor-parallel ranks")
+        if self.tp == "row" and bias:
+            raise ValueError("a row-parallel Dense has no bias (it would be added once per rank)")
+        self.kernel = nn.Parameter(torch.empty(li, lo, dtype=dtype))
+        self.bias = nn.Parameter(torch.zeros(lo, dtype=torch.float32)) if bias else None
         lecun_normal_(self.kernel.data, d_in)
+        if self.tp:
+            from ..parallel.tp import mark_shard
+            mark_shard(self.kernel, 0 if self.tp == "row" else 1, 2 if self.tp == "col2" else 1)
+            if self.bias is not None:
+                mark_shard(self.bias, 0, 2 if self.tp == "col2" else 1)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if ops.use_cuda(x) and x.dtype == torch.bfloat16:
@@ -39,10 +63,19 @@ class Dense(nn.Module):
 
 
 class RMSNorm(nn.Module):
-    def __init__(self, d: int, eps: float = 1e-6):
+    """``tp=True``: the scale of a head-split activation, split like its channels
+    (the statistics then need ``parallel.tp.tp_rmsnorm``)."""
+
+    def __init__(self, d: int, eps: float = 1e-6, tp: bool = False):
         super().__init__()
         self.eps = eps
-        self.scale = nn.Parameter(torch.ones(d, dtype=torch.float32))
+        self.d = d
+        W, _ = tp_world_rank()
+        self.tp = tp and W > 1
+        self.scale = nn.Parameter(torch.ones(d // W if self.tp else d, dtype=torch.float32))
+        if self.tp:
+            from ..parallel.tp import mark_shard
+            mark_shard(self.scale, 0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.rmsnorm(x, self.scale, self.eps)

@@ -16,60 +16,103 @@ import torch.nn.functional as F
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
-from .layers import Dense, RMSNorm, lecun_normal_
+from ..parallel.tp import get_tp, mark_shard, tp_rmsnorm
+from .layers import Dense, RMSNorm, lecun_normal_, tp_world_rank
 
 
-def _conv_param(d: int, width: int, std: float = 0.02) -> nn.Parameter:
-    return nn.Parameter(torch.randn(d, width) * std)
+def _shard_vec(t: torch.Tensor, tp: bool) -> nn.Parameter:
+    """A per-channel / per-head parameter; ``tp``: this rank's piece of it."""
+    p = nn.Parameter(t)
+    if tp:
+        mark_shard(p, 0)
+    return p
+
+
+def _conv_param(d: int, width: int, std: float = 0.02, tp: bool = False) -> nn.Parameter:
+    return _shard_vec(torch.randn(d, width) * std, tp)
 
 
 class GatedDeltaNet2(nn.Module):
-    """GDN-2 sublayer with per-channel decay ``g``, erase ``b`` and write ``w`` gates."""
+    """GDN-2 sublayer with per-channel decay ``g``, erase ``b`` and write ``w`` gates.
+
+    With tensor parallelism each rank holds ``n_heads / W`` heads: the seven input
+    projections are column-parallel over the gathered token rows, the conv, gates and
+    scan are per channel / head, ``out_norm`` normalises over all heads (all-reduced
+    statistics) and ``out_proj`` is row-parallel."""
 
     def __init__(self, cfg: ModelConfig):
         super().__init__()
         d = cfg.d_model
+        W, _ = tp_world_rank()
+        if cfg.n_heads % W:
+            raise ValueError(f"{cfg.n_heads} GDN heads do not split over {W} tensor-parallel ranks")
         self.cfg = cfg
-        self.n_heads = cfg.n_heads
+        self.tp_world = W
+        self.n_heads = cfg.n_heads // W
         self.d_head = d // cfg.n_heads
-        self.q_proj = Dense(d, d)
-        self.k_proj = Dense(d, d)
-        self.v_proj = Dense(d, d)
+        dl = d // W
+        self.q_proj = Dense(d, d, tp="col")
+        self.k_proj = Dense(d, d, tp="col")
+        self.v_proj = Dense(d, d, tp="col")
         for n in ("q", "k", "v"):
-            setattr(self, f"{n}_conv_w", _conv_param(d, cfg.d_conv))
-            setattr(self, f"{n}_conv_b", nn.Parameter(torch.zeros(d)))
-        self.erase_gate = Dense(d, d, bias=True)
-        self.write_gate = Dense(d, d, bias=True)
-        self.decay_a = nn.Parameter(torch.zeros(cfg.n_heads))
-        self.decay_proj = Dense(d, d, bias=True)
-        self.out_gate = Dense(d, d)
-        self.out_norm = RMSNorm(d)
-        self.out_proj = Dense(d, d)
+            setattr(self, f"{n}_conv_w", _conv_param(dl, cfg.d_conv, tp=W > 1))
+            setattr(self, f"{n}_conv_b", _shard_vec(torch.zeros(dl), W > 1))
+        self.erase_gate = Dense(d, d, bias=True, tp="col")
+        self.write_gate = Dense(d, d, bias=True, tp="col")
+        self.decay_a = _shard_vec(torch.zeros(self.n_heads), W > 1)
+        self.decay_proj = Dense(d, d, bias=True, tp="col")
+        self.out_gate = Dense(d, d, tp="col")
+        self.out_norm = RMSNorm(d, tp=True)
+        self.out_proj = Dense(d, d, tp="row")
+
+    def projections(self, x: torch.Tensor):
+        """``(q, k, v, erase, write, decay, out_gate)`` pre-activations over full
+        sequences ``(B, L, d / W)`` (the token rows gathered under tensor parallelism)."""
+        mods = (self.q_proj, self.k_proj, self.v_proj, self.erase_gate, self.write_gate, self.decay_proj,
+                self.out_gate)
+        tp = get_tp()
+        if tp is not None:
+            return tp.gather_linear(x, [(m.kernel, m.bias) for m in mods])
+        if ops.use_cuda(x) and x.dtype == torch.bfloat16:
+            from ..ops import kernels as K
+            return list(K.linear_multi(x, [(m.kernel, m.bias) for m in mods]))
+        return [m(x) for m in mods]
+
+    def out_projection(self, o: torch.Tensor) -> torch.Tensor:
+        tp = get_tp()
+        if tp is not None:
+            return tp.linear_scatter(o, self.out_proj.kernel)
+        return self.out_proj(o)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        Bsz, L, d = x.shape
-        H, D = self.n_heads, self.d_head
         if ops.use_cuda(x):
             return self._forward_fused(x)
-        q = ops.conv1d(self.q_proj(x), self.q_conv_w, self.q_conv_b, silu=True)
-        k = ops.conv1d(self.k_proj(x), self.k_conv_w, self.k_conv_b, silu=True)
-        v = ops.conv1d(self.v_proj(x), self.v_conv_w, self.v_conv_b, silu=True, clip=50.0)
+        H, D = self.n_heads, self.d_head
+        qp, kp, vp, bp, wp, fp, og = self.projections(x)
+        Bsz, L, dl = qp.shape
+        q = ops.conv1d(qp, self.q_conv_w, self.q_conv_b, silu=True)
+        k = ops.conv1d(kp, self.k_conv_w, self.k_conv_b, silu=True)
+        v = ops.conv1d(vp, self.v_conv_w, self.v_conv_b, silu=True, clip=50.0)
         q = q.view(Bsz, L, H, D)
         k = k.view(Bsz, L, H, D)
         v = v.view(Bsz, L, H, D)
         q = ops.grad_sanitize(R.safe_l2norm(q, 1e-12))
         k = ops.grad_sanitize(R.safe_l2norm(k, 1e-12))
-        b_gate = torch.sigmoid(self.erase_gate(x)).view(Bsz, L, H, D)
-        w_gate = torch.sigmoid(self.write_gate(x)).view(Bsz, L, H, D)
-        f = self.decay_proj(x).view(Bsz, L, H, D).float()
+        b_gate = torch.sigmoid(bp).view(Bsz, L, H, D)
+        w_gate = torch.sigmoid(wp).view(Bsz, L, H, D)
+        f = fp.view(Bsz, L, H, D).float()
         g = -torch.exp(self.decay_a.float().clamp(-20.0, 20.0))[None, None, :, None] * F.softplus(f)
         g = torch.nan_to_num(g, nan=0.0, posinf=0.0, neginf=-20.0)
-        og = self.out_gate(x).clamp(-1e2, 1e2)
+        og = og.clamp(-1e2, 1e2)
         q, k, v, w_gate, b_gate = (R.sanitize(t, 1e3) for t in (q, k, v, w_gate, b_gate))
         g = R.sanitize(g, 1e3)
-        o = ops.gdn2(q, k, v, w_gate, b_gate, g, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, d)
-        o = self.out_norm(o)
-        return self.out_proj(o * F.silu(og))
+        o = ops.gdn2(q, k, v, w_gate, b_gate, g, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, dl)
+        tp = get_tp()
+        if tp is not None:
+            o = tp_rmsnorm(o, self.out_norm.scale, 1e-6, self.cfg.d_model, tp).to(o.dtype)
+        else:
+            o = self.out_norm(o)
+        return self.out_projection(o * F.silu(og))
 
     def _forward_fused(self, x: torch.Tensor) -> torch.Tensor:
         from ..ops import kernels as K
@@ -77,80 +120,133 @@ class GatedDeltaNet2(nn.Module):
 
 
 class Mamba2(nn.Module):
-    """Mamba2 sublayer: per-head ``A``, per-channel ``dt``, B/C shared by all heads."""
+    """Mamba2 sublayer: per-head ``A``, per-channel ``dt``, B/C shared by all heads.
+
+    With tensor parallelism each rank holds ``n_heads_ssm / W`` heads: ``in_proj``
+    is column-parallel (its ``x_bc`` and gate halves split alike), ``B_proj`` /
+    ``C_proj`` (replicated) and ``dt_proj`` (column-parallel) read the full ``x_bc``
+    gathered along features, and ``out_proj`` is row-parallel."""
 
     def __init__(self, cfg: ModelConfig):
         super().__init__()
         d, di, N = cfg.d_model, cfg.d_inner, cfg.d_state
+        W, rank = tp_world_rank()
+        if cfg.n_heads_ssm % W:
+            raise ValueError(f"{cfg.n_heads_ssm} SSM heads do not split over {W} tensor-parallel ranks")
         self.cfg = cfg
-        self.in_proj = Dense(d, 2 * di)
-        self.conv_w = _conv_param(di, cfg.d_conv)
-        self.conv_b = nn.Parameter(torch.zeros(di))
+        self.tp_world = W
+        dil = di // W
+        self.n_heads = cfg.n_heads_ssm // W
+        self.in_proj = Dense(d, 2 * di, tp="col2")
+        self.conv_w = _conv_param(dil, cfg.d_conv, tp=W > 1)
+        self.conv_b = _shard_vec(torch.zeros(dil), W > 1)
         if cfg.ssm_init == "mamba":
-            a_log = torch.empty(cfg.n_heads_ssm).uniform_(0.0, math.log(16.0))
+            a_log = torch.empty(self.n_heads).uniform_(0.0, math.log(16.0))
         else:
-            a_log = torch.rand(cfg.n_heads_ssm)
-        self.A_log = nn.Parameter(a_log)
+            a_log = torch.rand(self.n_heads)
+        self.A_log = _shard_vec(a_log, W > 1)
         self.B_proj = Dense(di, N)
         self.C_proj = Dense(di, N)
-        self.dt_proj = Dense(di, di, bias=True)
+        self.dt_proj = Dense(di, di, bias=True, tp="col")
         if cfg.ssm_init == "mamba":
-            dt0 = torch.empty(di).uniform_(1e-3, 0.1)
+            dt0 = torch.empty(dil).uniform_(1e-3, 0.1)
             with torch.no_grad():
                 self.dt_proj.bias.copy_(dt0 + torch.log(-torch.expm1(-dt0)))
-        self.ssm_out_norm = RMSNorm(di)
-        self.out_proj = Dense(di, d)
+        self.ssm_out_norm = RMSNorm(di, tp=True)
+        self.out_proj = Dense(di, d, tp="row")
+
+    def in_projection(self, x: torch.Tensor) -> torch.Tensor:
+        tp = get_tp()
+        if tp is not None:
+            return tp.gather_linear(x, [(self.in_proj.kernel, None)])[0]
+        return self.in_proj(x)
+
+    def bc_input(self, x_bc: torch.Tensor) -> torch.Tensor:
+        """The full ``x_bc`` (all channels) that B, C and dt are projected from."""
+        tp = get_tp()
+        return tp.gather_features(x_bc) if tp is not None else x_bc
+
+    def out_projection(self, out: torch.Tensor) -> torch.Tensor:
+        tp = get_tp()
+        if tp is not None:
+            return tp.linear_scatter(out, self.out_proj.kernel)
+        return self.out_proj(out)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if ops.use_cuda(x):
             from ..ops import kernels as K
             return K.mamba2_layer(self, x)
-        Bsz, L, d = x.shape
-        di, Hs = self.cfg.d_inner, self.cfg.n_heads_ssm
-        P = di // Hs
-        xz = self.in_proj(x)
-        x_bc, res = xz[..., :di], xz[..., di:]
+        Hs = self.n_heads
+        xz = self.in_projection(x)
+        Bsz, L, two_dil = xz.shape
+        dil = two_dil // 2
+        P = dil // Hs
+        x_bc, res = xz[..., :dil], xz[..., dil:]
         x_conv = ops.conv1d(x_bc, self.conv_w, self.conv_b, silu=True)
         A = -torch.exp(self.A_log.float().clamp(-20.0, 20.0))
-        Bm = self.B_proj(x_bc)
-        Cm = self.C_proj(x_bc)
-        dt = F.softplus(self.dt_proj(x_bc)).clamp(1e-2, 1.0)
+        xin = self.bc_input(x_bc)
+        Bm = self.B_proj(xin)
+        Cm = self.C_proj(xin)
+        dt = F.softplus(self.dt_proj(xin)).clamp(1e-2, 1.0)
         dt, Bm, Cm, x_conv = (R.sanitize(t, 1e3) for t in (dt, Bm, Cm, x_conv))
         y = ops.ssd(dt.view(Bsz, L, Hs, P), A, Bm, Cm, x_conv.view(Bsz, L, Hs, P), self.cfg.ssd_chunk)
-        y = self.ssm_out_norm(y.reshape(Bsz, L, di).to(x_bc.dtype))
+        y = y.reshape(Bsz, L, dil).to(x_bc.dtype)
+        tp = get_tp()
+        if tp is not None:
+            y = tp_rmsnorm(y, self.ssm_out_norm.scale, 1e-6, self.cfg.d_inner, tp).to(y.dtype)
+        else:
+            y = self.ssm_out_norm(y)
         out = (y * F.silu(res)).clamp(-3e2, 3e2)
-        return self.out_proj(out)
+        return self.out_projection(out)
 
 
 class MLA(nn.Module):
-    """Latent-KV causal attention (reference ``MLAJ``), RoPE on Q and K."""
+    """Latent-KV causal attention (reference ``MLAJ``), RoPE on Q and K.
+
+    With tensor parallelism each rank holds ``n_heads / W`` heads (``W_q``,
+    ``W_k_up``, ``W_v_up`` column-parallel, ``W_o`` row-parallel); the latent
+    down-projection is replicated and computed on the gathered rows."""
 
     def __init__(self, cfg: ModelConfig):
         super().__init__()
         d = cfg.d_model
+        W, _ = tp_world_rank()
+        if cfg.n_heads % W:
+            raise ValueError(f"{cfg.n_heads} attention heads do not split over {W} tensor-parallel ranks")
         self.cfg = cfg
-        self.W_q = Dense(d, d)
+        self.tp_world = W
+        self.n_heads = cfg.n_heads // W
+        self.W_q = Dense(d, d, tp="col")
         self.W_kv_down = Dense(d, cfg.d_latent)
-        self.W_k_up = Dense(cfg.d_latent, d)
-        self.W_v_up = Dense(cfg.d_latent, d)
-        self.attn_out_norm = RMSNorm(d)
-        self.W_o = Dense(d, d)
+        self.W_k_up = Dense(cfg.d_latent, d, tp="col")
+        self.W_v_up = Dense(cfg.d_latent, d, tp="col")
+        self.attn_out_norm = RMSNorm(d, tp=True)
+        self.W_o = Dense(d, d, tp="row")
 
     def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-        Bsz, L, d = x.shape
-        H = self.cfg.n_heads
-        dh = d // H
-        Q = self.W_q(x).view(Bsz, L, H, dh).transpose(1, 2)
-        lat = self.W_kv_down(x)
+        H = self.n_heads
+        dh = self.cfg.d_model // self.cfg.n_heads
+        tp = get_tp()
+        if tp is not None:
+            Qp, lat = tp.gather_linear(x, [(self.W_q.kernel, None), (self.W_kv_down.kernel, None)])
+        else:
+            Qp, lat = self.W_q(x), self.W_kv_down(x)
+        Bsz, L, dl = Qp.shape
+        Q = Qp.view(Bsz, L, H, dh).transpose(1, 2)
         K = self.W_k_up(lat).view(Bsz, L, H, dh).transpose(1, 2)
         V = self.W_v_up(lat).view(Bsz, L, H, dh).transpose(1, 2)
         Q = R.apply_rope(Q, cos[:L, :dh], sin[:L, :dh])
         K = R.apply_rope(K, cos[:L, :dh], sin[:L, :dh])
         Q, K, V = (R.sanitize(t, 1e3) for t in (Q, K, V))
         out = ops.attention(Q.contiguous(), K.contiguous(), V.contiguous(), 1.0 / math.sqrt(dh))
-        out = out.transpose(1, 2).reshape(Bsz, L, d)
-        out = self.attn_out_norm(out)
+        out = out.transpose(1, 2).reshape(Bsz, L, dl)
+        if tp is not None:
+            out = tp_rmsnorm(out, self.attn_out_norm.scale, 1e-6, self.cfg.d_model, tp).to(out.dtype)
+        else:
+            out = self.attn_out_norm(out)
         out = ops.grad_sanitize(out)
+        if tp is not None:
+            return tp.linear_scatter(out, self.W_o.kernel)
         return self.W_o(out)
 
 

@@ -542,16 +542,25 @@ def source_mix(q, ks, ss, scale: float):
 
 
 def gdn2_layer(mod, x):
-    if x.dtype == torch.bfloat16 and mod.d_head == 128 and row_fusable(x.shape[-1]):
+    if x.dtype == torch.bfloat16 and mod.d_head == 128 and row_fusable(mod.cfg.d_model):
         return _gdn2_layer_fused(mod, x)
     return _gdn2_layer_composed(mod, x)
 
 
+def _out_norm_gate(mod_cfg_d, o, z, scale, zclip=math.inf, oclip=math.inf):
+    """Gated RMSNorm of a mixer output; over all heads of the tensor-parallel group
+    when the heads are split (all-reduced statistics)."""
+    from ..parallel.tp import get_tp, tp_norm_gate
+    tp = get_tp()
+    if tp is not None:
+        return tp_norm_gate(o, z, scale, 1e-6, mod_cfg_d, tp, zclip=zclip, oclip=oclip)
+    return norm_gate(o, z, scale, 1e-6, zclip=zclip, oclip=oclip)
+
+
 def _gdn2_layer_fused(mod, x):
-    Bsz, L, d = x.shape
     H, D = mod.n_heads, mod.d_head
-    projs = [mod.q_proj, mod.k_proj, mod.v_proj, mod.erase_gate, mod.write_gate, mod.decay_proj, mod.out_gate]
-    qp, kp, vp, bp, wp, fp, og = linear_multi(x, [(m.kernel, m.bias) for m in projs])
+    qp, kp, vp, bp, wp, fp, og = mod.projections(x)
+    Bsz, L, dl = qp.shape
     q = conv1d(qp, mod.q_conv_w, mod.q_conv_b, True)
     k = conv1d(kp, mod.k_conv_w, mod.k_conv_b, True)
     v = conv1d(vp, mod.v_conv_w, mod.v_conv_b, True, 50.0)
@@ -560,52 +569,65 @@ def _gdn2_layer_fused(mod, x):
     bg, wg, g = gdn_gates(bp, wp, fp, mod.decay_a, D)
     shp = (Bsz, L, H, D)
     o = gdn2(q, k, v.view(shp), wg.view(shp), bg.view(shp), g.view(shp), 1.0, mod.cfg.gdn_chunk)
-    o = norm_gate(o.reshape(Bsz, L, d).to(x.dtype), og, mod.out_norm.scale, 1e-6, zclip=1e2)
-    return mod.out_proj(o)
+    o = _out_norm_gate(mod.cfg.d_model, o.reshape(Bsz, L, dl).to(x.dtype), og, mod.out_norm.scale, zclip=1e2)
+    return mod.out_projection(o)
 
 
 def _gdn2_layer_composed(mod, x):
-    Bsz, L, d = x.shape
     H, D = mod.n_heads, mod.d_head
-    q = conv1d(mod.q_proj(x), mod.q_conv_w, mod.q_conv_b, True)
-    k = conv1d(mod.k_proj(x), mod.k_conv_w, mod.k_conv_b, True)
-    v = conv1d(mod.v_proj(x), mod.v_conv_w, mod.v_conv_b, True, 50.0)
+    qp, kp, vp, bp, wp, fp, og = mod.projections(x)
+    Bsz, L, dl = qp.shape
+    q = conv1d(qp, mod.q_conv_w, mod.q_conv_b, True)
+    k = conv1d(kp, mod.k_conv_w, mod.k_conv_b, True)
+    v = conv1d(vp, mod.v_conv_w, mod.v_conv_b, True, 50.0)
     q = R.safe_l2norm(q.view(Bsz, L, H, D), 1e-12)
     k = R.safe_l2norm(k.view(Bsz, L, H, D), 1e-12)
     from .. import ops
     q = ops.grad_sanitize(q)
     k = ops.grad_sanitize(k)
     v = v.view(Bsz, L, H, D)
-    bg = torch.sigmoid(mod.erase_gate(x)).view(Bsz, L, H, D)
-    wg = torch.sigmoid(mod.write_gate(x)).view(Bsz, L, H, D)
-    f = mod.decay_proj(x).view(Bsz, L, H, D).float()
+    bg = torch.sigmoid(bp).view(Bsz, L, H, D)
+    wg = torch.sigmoid(wp).view(Bsz, L, H, D)
+    f = fp.view(Bsz, L, H, D).float()
     g = -torch.exp(mod.decay_a.float().clamp(-20.0, 20.0))[None, None, :, None] * F.softplus(f)
     g = torch.nan_to_num(g, nan=0.0, posinf=0.0, neginf=-20.0).clamp(-1e3, 1e3)
-    og = mod.out_gate(x).clamp(-1e2, 1e2)
-    o = gdn2(q, k, v, wg, bg, g, 1.0, mod.cfg.gdn_chunk).reshape(Bsz, L, d)
-    o = rmsnorm(o, mod.out_norm.scale, 1e-6)
-    return mod.out_proj(o * F.silu(og))
+    og = og.clamp(-1e2, 1e2)
+    o = gdn2(q, k, v, wg, bg, g, 1.0, mod.cfg.gdn_chunk).reshape(Bsz, L, dl)
+    from ..parallel.tp import get_tp, tp_rmsnorm
+    tp = get_tp()
+    if tp is not None:
+        o = tp_rmsnorm(o, mod.out_norm.scale, 1e-6, mod.cfg.d_model, tp).to(o.dtype)
+    else:
+        o = rmsnorm(o, mod.out_norm.scale, 1e-6)
+    return mod.out_projection(o * F.silu(og))
 
 
 def mamba2_layer(mod, x):
-    Bsz, L, d = x.shape
-    di, Hs = mod.cfg.d_inner, mod.cfg.n_heads_ssm
-    P = di // Hs
-    fused = x.dtype == torch.bfloat16 and row_fusable(di)
-    xz = mod.in_proj(x)
-    x_bc, res = xz[..., :di], xz[..., di:]
+    Hs = mod.n_heads
+    xz = mod.in_projection(x)
+    Bsz, L, two_dil = xz.shape
+    dil = two_dil // 2
+    P = dil // Hs
+    fused = x.dtype == torch.bfloat16 and row_fusable(dil)
+    x_bc, res = xz[..., :dil], xz[..., dil:]
     x_conv = conv1d(x_bc, mod.conv_w, mod.conv_b, True)
     A = -torch.exp(mod.A_log.float().clamp(-20.0, 20.0))
-    Bm, Cm, dtp = linear_multi(x_bc, [(m.kernel, m.bias) for m in (mod.B_proj, mod.C_proj, mod.dt_proj)])
+    xin = mod.bc_input(x_bc)
+    Bm, Cm, dtp = linear_multi(xin, [(m.kernel, m.bias) for m in (mod.B_proj, mod.C_proj, mod.dt_proj)])
     dt = dt_act(dtp) if fused else F.softplus(dtp).clamp(1e-2, 1.0)
     y = ssd(dt.view(Bsz, L, Hs, P), A, Bm.clamp(-1e3, 1e3), Cm.clamp(-1e3, 1e3), x_conv.view(Bsz, L, Hs, P),
             mod.cfg.ssd_chunk)
-    y = y.reshape(Bsz, L, di).to(x_bc.dtype)
+    y = y.reshape(Bsz, L, dil).to(x_bc.dtype)
     if fused:
-        return mod.out_proj(norm_gate(y, res, mod.ssm_out_norm.scale, 1e-6, oclip=3e2))
-    y = rmsnorm(y, mod.ssm_out_norm.scale, 1e-6)
+        return mod.out_projection(_out_norm_gate(mod.cfg.d_inner, y, res, mod.ssm_out_norm.scale, oclip=3e2))
+    from ..parallel.tp import get_tp, tp_rmsnorm
+    tp = get_tp()
+    if tp is not None:
+        y = tp_rmsnorm(y, mod.ssm_out_norm.scale, 1e-6, mod.cfg.d_inner, tp).to(y.dtype)
+    else:
+        y = rmsnorm(y, mod.ssm_out_norm.scale, 1e-6)
     out = (y * F.silu(res)).clamp(-3e2, 3e2)
-    return mod.out_proj(out)
+    return mod.out_projection(out)
 
 
 class _MoE(torch.autograd.Function):

@@ -64,6 +64,8 @@ class HybridOptimizer:
         self.peers = None
         # optimizers of further stores stepped together with this one (shared norm / clip)
         self.partners: list = []
+        # share of this store's norm statistics in the cross-rank sum (1 / replicas)
+        self.norm_share = 1.0
 
     def uses_kernels(self) -> bool:
         gbuf = self.store.grad
@@ -118,7 +120,7 @@ class HybridOptimizer:
             from ..ops import kernels as K
             part = torch.zeros_like(red)
             K.optim_prepare(self, inv, part)
-            red[0:2] += part[0:2]
+            red[0:2] += part[0:2] * self.norm_share
             red[2:] = torch.maximum(red[2:], part[2:])
             return
         for s in self.owned:
@@ -126,12 +128,12 @@ class HybridOptimizer:
                 continue
             sl = self._sl(s)
             avg = gbuf[sl] * inv
-            red[0] += avg.double().square().sum().float()
+            red[0] += avg.double().square().sum().float() * self.norm_share
             if not torch.isfinite(avg).all():
                 red[3 + self.group_idx[diag_group_of(s.name)]] = 1.0
             g = torch.nan_to_num(avg, nan=0.0, posinf=0.0, neginf=0.0) * s.grad_scale
             gbuf[sl] = g
-            red[1] += g.double().square().sum().float()
+            red[1] += g.double().square().sum().float() * self.norm_share
         for s in self.owned:
             if (st.master_view(s).abs() >= PARAM_CLIP).any():
                 red[2] = 1.0

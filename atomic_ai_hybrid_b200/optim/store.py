@@ -58,9 +58,10 @@ def default_keep_fp32(name: str, p: torch.Tensor) -> bool:
 
 
 def is_ep_local(name: str, p: torch.Tensor) -> bool:
-    """Expert-parallel parameters (this rank's block of routed experts): neither
-    reduced nor gathered across ranks."""
-    return bool(getattr(p, "_ahb_ep_local", False))
+    """Parameters that differ between ranks: this rank's block of routed experts
+    (expert parallelism) or its piece of a tensor-parallel weight.  They are not
+    reduced or gathered across the data-parallel ranks of the main store."""
+    return bool(getattr(p, "_ahb_ep_local", False) or getattr(p, "_ahb_tp_shard", None) is not None)
 
 
 class FlatParamStore:

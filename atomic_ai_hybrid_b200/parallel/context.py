@@ -4,9 +4,11 @@ The reference runs on a 1-D device mesh (``("tpu_nodes",)``, reference
 `train_setup.py:361-365`, ``set_model_mesh``/``get_model_mesh`` in
 `model.py:81-93`).  Here one process drives one GPU and the groups are explicit:
 
-* ``dp``: data parallel (sharded optimizer / weights gathered per step),
+* ``dp``: the ranks that hold different tokens (data parallel, and with sequence
+  parallelism the tensor-parallel ranks too); batch-global statistics average over it,
 * ``ep``: expert parallel (routed experts split across ranks),
-* ``tp``: tensor parallel (heads split across ranks).
+* ``tp``: tensor parallel (heads split across ranks, token rows split between the
+  mixers; ``parallel.tp``).
 
 Batch-global statistics that the reference computes over the whole sharded
 batch (the MoE load-balancing mean probabilities) are averaged over ``dp`` with a
@@ -32,6 +34,11 @@ class ParallelContext:
     tp_world: int = 1
     ep_rank: int = 0
     ep: Optional[object] = None  # the EPGroup (peer buffers) once built
+    tp_rank: int = 0
+    tp: Optional[object] = None  # the TPGroup (token layout, collectives)
+    # ranks that hold the same rank-local parameters (data-parallel replicas of a
+    # tensor- or expert-parallel group); None when every such piece has one owner
+    local_group: Optional[dist.ProcessGroup] = None
 
 
 _CTX = ParallelContext()

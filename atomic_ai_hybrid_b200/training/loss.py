@@ -26,7 +26,8 @@ def compute_loss(model, batch: Dict[str, torch.Tensor], deterministic: bool = Fa
                  ce_chunk_size: int = 2048, collinearity_coef: Optional[float] = None):
     cfg = model.cfg
     hidden, stats = model(batch["input_ids"], return_hidden=True)
-    sum_loss, sum_mask = ops.cross_entropy(hidden, batch["labels"], model.lm_weight(),
+    labels = model.token_shard(batch["labels"]) if hasattr(model, "token_shard") else batch["labels"]
+    sum_loss, sum_mask = ops.cross_entropy(hidden, labels, model.lm_weight(),
                                            cfg.label_smoothing, ce_chunk_size)
     ce = sum_loss / sum_mask.clamp_min(1.0)
     ce = torch.nan_to_num(ce, nan=0.0, posinf=1e4, neginf=0.0)

@@ -44,15 +44,21 @@ class Trainer:
         self.store = FlatParamStore(model, label_fn, grad_scale_of, self.world, self.rank,
                                     compute_dtype=compute_dtype, device=device,
                                     param_filter=(lambda n, p: not is_ep_local(n, p)) if ep_params else None)
-        # expert-parallel experts: a local store (no reduction / gathering) stepped with the main one
+        # rank-local parameters (expert-parallel experts, tensor-parallel pieces): a local
+        # store (no reduce-scatter / all-gather) stepped with the main one; when the same
+        # piece lives on several ranks (data-parallel replicas of a tensor-parallel
+        # group) its gradients are summed over ``local_group`` before the step
+        from ..parallel.context import get_parallel_context
+        self.local_group = get_parallel_context().local_group
         self.ep_store = None
         if ep_params:
             self.ep_store = FlatParamStore(model, label_fn, grad_scale_of, 1, 0, compute_dtype=compute_dtype,
                                            device=device, param_filter=is_ep_local)
         self.comm = None
         if self.world > 1:
-            from ..parallel.context import ParallelContext, get_parallel_context, set_parallel_context
-            if get_parallel_context().dp_world != self.world:
+            from ..parallel.context import ParallelContext, set_parallel_context
+            pc = get_parallel_context()
+            if pc.dp_world != self.world and pc.tp is None and pc.ep_world <= 1:
                 set_parallel_context(ParallelContext(dp_group=group, dp_world=self.world))
             from ..parallel.fsdp import make_shard_comm
             self.comm = make_shard_comm(self.store, group, comm)
@@ -61,17 +67,24 @@ class Trainer:
         self.ep_opt = None
         if self.ep_store is not None:
             self.ep_opt = HybridOptimizer(self.ep_store, total_steps)
+            self.ep_opt.schedule = self.opt.schedule  # one learning-rate schedule for both stores
+            if self.local_group is not None:
+                # every replica adds the same statistics to the cross-rank sum
+                self.ep_opt.norm_share = 1.0 / dist.get_world_size(self.local_group)
             self.opt.partners.append(self.ep_opt)
-            from ..parallel.context import get_parallel_context
             pc = get_parallel_context()
-            if pc.ep is None:
-                if ep_max_tokens <= 0:
-                    raise ValueError("expert parallelism needs ep_max_tokens (tokens per micro-batch)")
-                from ..parallel.ep import EPGroup
-                pc.ep = EPGroup(pc.ep_world, pc.ep_rank, self.cfg.e_routed, self.cfg.top_k, self.cfg.d_model,
-                                ep_max_tokens, self.store.device, group=pc.ep_group)
-            # the per-layer host read of the routing counts cannot be captured
-            cuda_graph = False
+            if pc.tp is not None and pc.tp.world > 1:
+                # the head-split layers run eager (per-call peer barriers carry host epochs)
+                cuda_graph = False
+            if pc.ep_world > 1:
+                if pc.ep is None:
+                    if ep_max_tokens <= 0:
+                        raise ValueError("expert parallelism needs ep_max_tokens (tokens per micro-batch)")
+                    from ..parallel.ep import EPGroup
+                    pc.ep = EPGroup(pc.ep_world, pc.ep_rank, self.cfg.e_routed, self.cfg.top_k, self.cfg.d_model,
+                                    ep_max_tokens, self.store.device, group=pc.ep_group)
+                # the per-layer host read of the routing counts cannot be captured
+                cuda_graph = False
         # peer-memory comm + fused optimizer kernels: reduce-scatter and all-gather
         # happen inside the optimizer's prepare / apply kernels
         self.fused_comm = bool(self.comm is not None and getattr(self.comm, "fused", False)
@@ -172,6 +185,8 @@ class Trainer:
             if self.world > 1:
                 dist.all_reduce(frac, group=self.group)
                 frac = frac / self.world
+        if self.local_group is not None and self.ep_store is not None:
+            dist.all_reduce(self.ep_store.grad, group=self.local_group)
         if self.fused_comm:
             self.comm.begin_step()
         elif self.comm is not None:
@@ -210,9 +225,11 @@ class Trainer:
             self.comm.close()
         if self.ep_store is not None:
             from ..parallel.context import get_parallel_context
-            ep = get_parallel_context().ep
-            if ep is not None:
-                ep.close()
+            pc = get_parallel_context()
+            if pc.ep is not None:
+                pc.ep.close()
+            if pc.tp is not None:
+                pc.tp.close()
 
     @torch.no_grad()
     def eval_loss(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:
