@@ -747,7 +747,7 @@ static void add_scale_grad(const torch::Tensor& part, const c10::optional<torch:
 }
 
 std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor delta, torch::Tensor scale, double clip,
-                                           double eps) {
+                                           double eps, c10::optional<torch::Tensor> stats) {
   const int64_t D = x.size(-1);
   TORCH_CHECK(ahb_row_supported((int)D), "add_rmsnorm: D % 256 != 0");
   check_rows(x, D, "x");
@@ -757,8 +757,14 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor delta,
   auto sc = scale.to(at::kFloat).contiguous();
   auto xo = torch::empty_like(x), y = torch::empty_like(x);
   auto r = torch::empty({M}, x.options().dtype(at::kFloat));
+  float* sp = nullptr;
+  if (stats.has_value() && stats->defined()) {
+    TORCH_CHECK(stats->is_cuda() && stats->scalar_type() == at::kFloat && stats->is_contiguous() && stats->numel() >= 2,
+                "add_rmsnorm: stats fp32 (2,)");
+    sp = stats->data_ptr<float>();
+  }
   ahb_add_rmsnorm_fwd(x.data_ptr(), delta.data_ptr(), sc.data_ptr<float>(), xo.data_ptr(), y.data_ptr(),
-                      r.data_ptr<float>(), M, (int)D, (float)clip, (float)eps, cur_stream());
+                      r.data_ptr<float>(), M, (int)D, (float)clip, (float)eps, cur_stream(), sp);
   check_launch("ahb_add_rmsnorm_fwd");
   return {xo, y, r};
 }
@@ -1124,6 +1130,36 @@ void copy_out(torch::Tensor src, torch::Tensor peers, int64_t off_bytes) {
   check_launch("ahb_copy_out");
 }
 
+// ------------------------------------------------------------ tensor parallelism over peer memory
+// Row-parallel projection with the reduce-scatter in the epilogue: rows of group g of `a` times `b`
+// are stored at out_ptrs[g] (rank g's receive slot for this rank; raw device pointers, peers' included).
+void tp_gemm_rs(torch::Tensor a, torch::Tensor b, torch::Tensor grp_off, std::vector<int64_t> out_ptrs, int64_t m_rot) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.dim() == 2 && a.is_contiguous(), "tp_gemm_rs: a bf16 (M,K)");
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.is_contiguous() &&
+                  b.size(0) == a.size(1), "tp_gemm_rs: b bf16 (K,N)");
+  TORCH_CHECK(grp_off.is_cuda() && grp_off.scalar_type() == at::kInt && grp_off.numel() == (int64_t)out_ptrs.size() + 1,
+              "tp_gemm_rs: grp_off int32 (W+1)");
+  std::vector<void*> tab(out_ptrs.size());
+  for (size_t i = 0; i < out_ptrs.size(); ++i) tab[i] = reinterpret_cast<void*>(out_ptrs[i]);
+  const int rc = ahb_gemm_rs_peer(a.data_ptr(), a.size(0), a.size(1), b.data_ptr(), b.size(1), grp_off.data_ptr<int>(),
+                                  (int)out_ptrs.size(), tab.data(), (int)m_rot, err_word().data_ptr<int>(), num_sms(),
+                                  cur_stream());
+  TORCH_CHECK(rc == 0, "ahb_gemm_rs_peer failed: ", rc);
+  check_launch("ahb_gemm_rs_peer");
+}
+// out = sum of `nslots` bf16 slots of out.numel() elements, `stride` elements apart, from raw memory
+void sum_slots(int64_t slots, int64_t nslots, int64_t stride, torch::Tensor out) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() % 8 == 0 &&
+                  stride % 8 == 0, "sum_slots: bf16 out, 16-byte multiples");
+  ahb_sum_slots_bf16(reinterpret_cast<const void*>(slots), (int)nslots, stride, out.numel(), out.data_ptr(), cur_stream());
+  check_launch("ahb_sum_slots_bf16");
+}
+// cudaMemcpyAsync between raw device addresses (peer IPC mappings included) on a given stream
+void memcpy_async(int64_t dst, int64_t src, int64_t nbytes, int64_t stream) {
+  TORCH_CHECK(ahb_memcpy_async(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), nbytes,
+                               reinterpret_cast<cudaStream_t>(stream)) == 0, "memcpy_async failed");
+}
+
 // ------------------------------------------------------------ fused LM head + cross entropy
 // forward: logits = h W^T (bf16, tcgen05), then loss + dlogits in place.  Returns {sum_loss, count, dlogits, hpad}
 std::vector<torch::Tensor> ce_fused_fwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, double ls) {
@@ -1202,7 +1238,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fused_bwd", &ce_fused_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
-  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, py::arg("x"), py::arg("delta"), py::arg("scale"), py::arg("clip"),
+        py::arg("eps"), py::arg("stats") = py::none());
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);
   m.def("norm_gate_fwd", &norm_gate_fwd);
   m.def("norm_gate_bwd", &norm_gate_bwd);
@@ -1238,4 +1275,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &symm_barrier);
   m.def("reduce_scatter_f32", &reduce_scatter_f32);
   m.def("copy_out", &copy_out);
+  m.def("tp_gemm_rs", &tp_gemm_rs);
+  m.def("sum_slots", &sum_slots);
+  m.def("memcpy_async", &memcpy_async);
 }

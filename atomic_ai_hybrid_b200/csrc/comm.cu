@@ -78,6 +78,29 @@ __global__ void copy_out_kernel(const uint4* __restrict__ src, uint4* const* __r
   }
 }
 
+// out[i] = sum_s slots[s * stride + i] (bf16 in, fp32 sum in slot order, bf16 out); 8 per thread
+__global__ void sum_slots_kernel(const uint4* __restrict__ slots, int nslots, int64_t stride16, int64_t n16,
+                                 uint4* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nslots; ++s) {
+      const uint4 v = slots[s * stride16 + i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        a[2 * j] += f.x;
+        a[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(a[2 * j], a[2 * j + 1]);
+    out[i] = o;
+  }
+}
+
 int grid_for(int64_t n) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -140,4 +163,14 @@ void ahb_copy_out(const void* src, void* const* peers_dev, int world, int64_t of
   if (n16 == 0) return;
   copy_out_kernel<<<grid_for(n16), 256, 0, st>>>((const uint4*)src, (uint4* const*)peers_dev, world, off_bytes / 16,
                                                  n16);
+}
+
+void ahb_sum_slots_bf16(const void* slots, int nslots, int64_t stride, int64_t n, void* out, cudaStream_t st) {
+  const int64_t n16 = n / 8;
+  if (n16 == 0) return;
+  sum_slots_kernel<<<grid_for(n16), 256, 0, st>>>((const uint4*)slots, nslots, stride / 8, n16, (uint4*)out);
+}
+
+int ahb_memcpy_async(void* dst, const void* src, int64_t nbytes, cudaStream_t st) {
+  return cudaMemcpyAsync(dst, src, (size_t)nbytes, cudaMemcpyDefault, st) == cudaSuccess ? 0 : -1;
 }

@@ -70,14 +70,19 @@ AHB_DEVICE float row_sum(float v, float* sh) {
 AHB_DEVICE float clampf(float x, float c) { return fminf(fmaxf(x, -c), c); }
 
 // ------------------------------------------------------------------ add_rmsnorm
+// stats (optional): stats[0] = max |x + delta| over finite sums (before the clip),
+// stats[1] = 1 when delta holds a NaN / infinity.  Non-negative floats order like their
+// bit patterns, so both are folded in with integer atomicMax.
 __global__ void add_rmsnorm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ delta,
                                        const float* __restrict__ scale, bf16* __restrict__ xo, bf16* __restrict__ y,
-                                       float* __restrict__ rstd, int64_t M, int D, float clip, float eps) {
+                                       float* __restrict__ rstd, int64_t M, int D, float clip, float eps,
+                                       float* __restrict__ stats) {
   __shared__ float sh[32];
   const int c0 = threadIdx.x * 8;
   float sc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) sc[i] = scale[c0 + i];
+  float mx = 0.f, nf = 0.f;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const int64_t o = row * D + c0;
     const F8 a = ld8(x + o), b = ld8(delta + o);
@@ -86,7 +91,10 @@ __global__ void add_rmsnorm_fwd_kernel(const bf16* __restrict__ x, const bf16* _
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       // bf16 residual add, then nan_to_num(clip): the value the unfused path stores
-      s.v[i] = sanitize(rnd(a.v[i] + b.v[i]), clip);
+      const float raw = rnd(a.v[i] + b.v[i]);
+      if (isfinite(raw)) mx = fmaxf(mx, fabsf(raw));
+      if (!isfinite(b.v[i])) nf = 1.f;
+      s.v[i] = sanitize(raw, clip);
       ss += s.v[i] * s.v[i];
     }
     st8(xo + o, s);
@@ -96,6 +104,14 @@ __global__ void add_rmsnorm_fwd_kernel(const bf16* __restrict__ x, const bf16* _
 #pragma unroll
     for (int i = 0; i < 8; ++i) out.v[i] = s.v[i] * r * sc[i];
     st8(y + o, out);
+  }
+  if (stats) {
+    mx = warp_max(mx);
+    nf = warp_max(nf);
+    if ((threadIdx.x & 31) == 0) {
+      atomicMax(reinterpret_cast<int*>(stats), __float_as_int(mx));
+      if (nf > 0.f) atomicMax(reinterpret_cast<int*>(stats + 1), __float_as_int(1.f));
+    }
   }
 }
 
@@ -385,11 +401,11 @@ int ahb_row_bwd_blocks(int64_t M) {
 }
 
 void ahb_add_rmsnorm_fwd(const void* x, const void* delta, const float* scale, void* xo, void* y, float* rstd,
-                         int64_t M, int D, float clip, float eps, cudaStream_t st) {
+                         int64_t M, int D, float clip, float eps, cudaStream_t st, float* stats) {
   if (M <= 0) return;
   const int grid = (int)(M < (int64_t)sms() * 16 ? M : (int64_t)sms() * 16);
   add_rmsnorm_fwd_kernel<<<grid, D / 8, 0, st>>>((const bf16*)x, (const bf16*)delta, scale, (bf16*)xo, (bf16*)y,
-                                                 rstd, M, D, clip, eps);
+                                                 rstd, M, D, clip, eps, stats);
 }
 
 void ahb_add_rmsnorm_bwd(const void* dy, const void* gres, const void* xo, const float* scale, const float* rstd,

@@ -122,7 +122,8 @@ void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nbloc
 int ahb_row_supported(int D);
 int ahb_row_bwd_blocks(int64_t M);
 void ahb_add_rmsnorm_fwd(const void* x, const void* delta, const float* scale, void* xo, void* y, float* rstd,
-                         int64_t M, int D, float clip, float eps, cudaStream_t st);
+                         int64_t M, int D, float clip, float eps, cudaStream_t st,
+                         float* stats = nullptr);
 void ahb_add_rmsnorm_bwd(const void* dy, const void* gres, const void* xo, const float* scale, const float* rstd,
                          void* dx, void* ddelta, float* dscale_part, int64_t M, int D, float clip, cudaStream_t st);
 void ahb_norm_gate_fwd(const void* x, const void* z, int64_t zs, const float* scale, void* y, float* rstd, int64_t M,
@@ -189,6 +190,11 @@ void ahb_symm_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t e
                       cudaStream_t st);
 void ahb_reduce_scatter_f32(const float* const* peers_dev, int world, int64_t lo, int64_t n, float* out,
                             cudaStream_t st);
+// tensor parallelism over peer memory
+int ahb_gemm_rs_peer(const void* a, int64_t a_rows, int64_t K, const void* b, int64_t N, const int* grp_off, int W,
+                     void* const* out_tab, int m_rot, int* err, int num_sms, cudaStream_t st);
+void ahb_sum_slots_bf16(const void* slots, int nslots, int64_t stride, int64_t n, void* out, cudaStream_t st);
+int ahb_memcpy_async(void* dst, const void* src, int64_t nbytes, cudaStream_t st);
 void ahb_copy_out(const void* src, void* const* peers_dev, int world, int64_t off_bytes, int64_t nbytes,
                   cudaStream_t st);
 

@@ -36,7 +36,10 @@ constexpr int B_BYTES = 256 * BK * 2;  // 32 KB (NB * BNacc = 256 columns)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 1024;  // tile ring, alignment, barriers + offsets
 
-enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5 };
+enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5,
+           EPI_STORE_PEER = 6 };
+
+constexpr int MAX_PEERS = 8;
 
 struct Params {
   CUtensorMap ta0, ta1, tb0, tb1;
@@ -50,6 +53,11 @@ struct Params {
   const float* alpha;  // optional device scalar multiplying the product (STORE / ACC epilogues)
   float clip;
   int* err;
+  // EPI_STORE_PEER: group g's rows go to out_tab[g] (row - grp_off[g]) * N + col, which may
+  // be another GPU's memory (plain 16-byte stores over NVLink); M tiles are visited from
+  // tile m_rot on, so that the ranks start on different destinations
+  void* out_tab[MAX_PEERS];
+  int m_rot;
 };
 
 AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
@@ -85,7 +93,8 @@ struct Tile {
 template <bool KGROUP>
 AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, Tile& t) {
   if (!KGROUP) {
-    const int mt = tile / n_tiles, nt = tile % n_tiles;
+    const int m_total = off[p.E] / BM;
+    const int mt = (tile / n_tiles + p.m_rot) % m_total, nt = tile % n_tiles;
     t.m0 = mt * BM;
     int e = 0;
     while (e + 1 < p.E && off[e + 1] <= t.m0) ++e;
@@ -283,6 +292,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
           store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
           store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
           store_bf16x32(static_cast<bf16*>(p.out2) + o, v1);
+        } else if constexpr (EPI == EPI_STORE_PEER) {
+          bf16* dst = static_cast<bf16*>(p.out_tab[t.e]) + static_cast<int64_t>(row - off[t.e]) * p.N + col;
+          store_bf16x32(dst, v0);
         } else if constexpr (EPI == EPI_GELU_FWD) {
           float h[32];
 #pragma unroll
@@ -344,6 +356,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // peer stores must be visible system-wide before the barrier that follows the kernel
+    if constexpr (EPI == EPI_STORE_PEER) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();
@@ -447,4 +461,29 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
     case AHB_GEMM_WGRAD_DUAL: return launch<true, true, true, 2, EPI_ACC>(p, grid, st);
     default: return -30;
   }
+}
+
+// GEMM -> reduce-scatter over peer memory: out rows of group g (rows [grp_off[g], grp_off[g+1]) of A)
+// are the partial sums owed to rank g and are stored at out_tab[g] (its receive slot for this rank).
+int ahb_gemm_rs_peer(const void* a, int64_t a_rows, int64_t K, const void* b, int64_t N, const int* grp_off, int W,
+                     void* const* out_tab, int m_rot, int* err, int num_sms, cudaStream_t st) {
+  if (W < 1 || W > MAX_PEERS || a_rows % BM != 0 || K % BK != 0 || N % 32 != 0) return -10;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.grp_off = grp_off;
+  p.E = W;
+  p.N = (int)N;
+  p.Mout = 0;
+  p.kb_split = (int)(K / BK);
+  p.kb_total = (int)(K / BK);
+  p.b_rows = 0;  // every group multiplies by the same weight
+  p.err = err;
+  for (int g = 0; g < W; ++g) p.out_tab[g] = out_tab[g];
+  p.m_rot = m_rot;
+  int rc = make_map(&p.ta0, a, a_rows, K, K, BM);
+  rc |= make_map(&p.tb0, b, K, N, N, 64);
+  p.ta1 = p.ta0;
+  p.tb1 = p.tb0;
+  if (rc) return -20;
+  return launch<false, false, true, 1, EPI_STORE_PEER>(p, num_sms, st);
 }

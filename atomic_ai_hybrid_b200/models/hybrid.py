@@ -29,6 +29,8 @@ from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
 from ..parallel.tp import get_tp
+from ..utils.diag import DIAG
+from ..utils.nvtx import nvtx_range
 from .layers import Dense, RMSNorm
 from .mixers import MLA, GatedDeltaNet2, Mamba2
 from .moe import MoE
@@ -144,12 +146,18 @@ class BlockDAR(nn.Module):
         for li in self.layer_ids:
             layer = getattr(self, f"layer_{li}")
             delta = layer(current_x, block_input, local, history, cos, sin)
+            tag = f"block={self.block_idx} layer={li} type={layer.layer_type}"
+            DIAG.nonfinite(f"delta: {tag}", delta)
+            DIAG.resid_breakdown(tag, current_x, delta)
             local.append(delta)
             clip = 5e2 if layer.layer_type == "mamba2" else 1e3
-            current_x = ops.sanitize(current_x + delta, clip)
+            summed = current_x + delta
+            DIAG.maxabs(tag, summed)
+            current_x = ops.sanitize(summed, clip)
         history.append(sum(local))
         st: Dict[str, torch.Tensor] = {}
         moe_out = self.moe(self.norm_2(current_x), st)
+        DIAG.nonfinite(f"moe_out: block={self.block_idx}", moe_out)
         stats.append(st)
         return ops.sanitize(current_x + moe_out, 1e3)
 
@@ -166,12 +174,22 @@ class InterleavedLayer(nn.Module):
         self.norm_2 = RMSNorm(cfg.d_model)
         self.moe = MoE(cfg)
 
+    def _tag(self) -> str:
+        return f"layer={getattr(self, 'layer_idx', '?')} type={self.layer_type}"
+
     def forward(self, x, cos, sin, stats: List[Dict]):
-        delta = ops.grad_sanitize(self.sublayer(self.pre_norm(x), cos, sin))
+        tag = self._tag()
+        delta = ops.grad_sanitize(self.sublayer(self.pre_norm(x), cos, sin), tag=f"sublayer {tag}")
+        DIAG.nonfinite(f"delta: {tag}", delta)
+        DIAG.resid_breakdown(tag, x, delta)
         clip = 5e2 if self.layer_type == "mamba2" else 1e3
-        x = ops.sanitize(x + delta, clip)
+        summed = x + delta
+        DIAG.maxabs(tag, summed)
+        x = ops.sanitize(summed, clip)
         st: Dict[str, torch.Tensor] = {}
-        x = ops.sanitize(x + self.moe(self.norm_2(x), st), 1e3)
+        m = self.moe(self.norm_2(x), st)
+        DIAG.nonfinite(f"moe_out: {tag}", m)
+        x = ops.sanitize(x + m, 1e3)
         stats.append(st)
         return x
 
@@ -181,13 +199,17 @@ class InterleavedLayer(nn.Module):
         normalisation by ``next_scale`` (the next layer's ``pre_norm`` or the
         final norm)."""
         from ..ops import kernels as K
+        tag = self._tag()
         delta = self.sublayer(h, cos, sin)
+        DIAG.resid_breakdown(tag, x, delta)
         clip = 5e2 if self.layer_type == "mamba2" else 1e3
-        x, h2 = K.add_rmsnorm(x, delta, self.norm_2.scale, clip, 1e-6, sanitize_delta_grad=True)
+        # the kernel folds max |x + delta| and a non-finite-delta flag into the diagnostics
+        x, h2 = K.add_rmsnorm(x, delta, self.norm_2.scale, clip, 1e-6, sanitize_delta_grad=True,
+                              diag_tag=f"delta: {tag}")
         st: Dict[str, torch.Tensor] = {}
         m = self.moe(h2, st)
         stats.append(st)
-        return K.add_rmsnorm(x, m, next_scale, 1e3, 1e-6)
+        return K.add_rmsnorm(x, m, next_scale, 1e3, 1e-6, diag_tag=f"moe_out: {tag}")
 
 
 class Embed(nn.Module):
@@ -218,6 +240,7 @@ class HybridMoEModel(nn.Module):
         else:
             for i in range(cfg.num_layers):
                 setattr(self, f"layer_{i}", InterleavedLayer(cfg, cfg.layer_types[i]))
+                getattr(self, f"layer_{i}").layer_idx = i
         self.final_norm = RMSNorm(cfg.d_model)
         if not cfg.tie_embeddings:
             self.lm_head = Dense(cfg.d_model, cfg.vocab_size)
@@ -263,7 +286,8 @@ class HybridMoEModel(nn.Module):
                     x = ckpt.checkpoint(layer, x, cos, sin, st, use_reentrant=False)
                     stats.extend(st)
                 else:
-                    x = layer(x, cos, sin, stats)
+                    with nvtx_range(f"layer/{layer.layer_type}"):
+                        x = layer(x, cos, sin, stats)
         h = self.final_norm(x)
         if return_hidden:
             return h, stats
@@ -289,7 +313,8 @@ class HybridMoEModel(nn.Module):
                 x, h = ckpt.checkpoint(layer.forward_fused, x, h, nxt, cos, sin, st, use_reentrant=False)
                 stats.extend(st)
             else:
-                x, h = layer.forward_fused(x, h, nxt, cos, sin, stats)
+                with nvtx_range(f"layer_{i}/{layer.layer_type}"):
+                    x, h = layer.forward_fused(x, h, nxt, cos, sin, stats)
         if return_hidden:
             return h, stats
         return h @ self.lm_weight().to(h.dtype).t(), stats

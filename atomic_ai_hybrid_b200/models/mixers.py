@@ -17,6 +17,7 @@ from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
 from ..parallel.tp import get_tp, mark_shard, tp_rmsnorm
+from ..utils.diag import DIAG
 from .layers import Dense, RMSNorm, lecun_normal_, tp_world_rank
 
 
@@ -106,7 +107,10 @@ class GatedDeltaNet2(nn.Module):
         og = og.clamp(-1e2, 1e2)
         q, k, v, w_gate, b_gate = (R.sanitize(t, 1e3) for t in (q, k, v, w_gate, b_gate))
         g = R.sanitize(g, 1e3)
+        for name, t in (("q", q), ("k", k), ("v", v), ("g", g)):
+            DIAG.stage("GDN2", name, t)
         o = ops.gdn2(q, k, v, w_gate, b_gate, g, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, dl)
+        DIAG.stage("GDN2", "o", o)
         tp = get_tp()
         if tp is not None:
             o = tp_rmsnorm(o, self.out_norm.scale, 1e-6, self.cfg.d_model, tp).to(o.dtype)
@@ -189,7 +193,10 @@ class Mamba2(nn.Module):
         Cm = self.C_proj(xin)
         dt = F.softplus(self.dt_proj(xin)).clamp(1e-2, 1.0)
         dt, Bm, Cm, x_conv = (R.sanitize(t, 1e3) for t in (dt, Bm, Cm, x_conv))
+        for name, t in (("in_proj", xz), ("x_conv", x_conv), ("dt", dt)):
+            DIAG.stage("MAMBA2", name, t)
         y = ops.ssd(dt.view(Bsz, L, Hs, P), A, Bm, Cm, x_conv.view(Bsz, L, Hs, P), self.cfg.ssd_chunk)
+        DIAG.stage("MAMBA2", "ssd_y", y)
         y = y.reshape(Bsz, L, dil).to(x_bc.dtype)
         tp = get_tp()
         if tp is not None:

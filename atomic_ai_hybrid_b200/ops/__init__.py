@@ -64,21 +64,25 @@ class _GradSanitize(torch.autograd.Function):
     non-finite values (reference ``make_grad_sanitizer``, `model.py:192-217`)."""
 
     @staticmethod
-    def forward(ctx, x, clip):
-        ctx.clip = clip
+    def forward(ctx, x, clip, tag):
+        ctx.clip, ctx.tag = clip, tag
         return x.view_as(x)
 
     @staticmethod
     def backward(ctx, g):
+        if ctx.tag is not None:
+            from ..utils.diag import DIAG
+            DIAG.grad_fixed(ctx.tag, g)
         if g.is_cuda and _IMPL == "cuda":
-            return _k().sanitize(g, ctx.clip), None
-        return R.sanitize(g, ctx.clip), None
+            return _k().sanitize(g, ctx.clip), None, None
+        return R.sanitize(g, ctx.clip), None, None
 
 
-def grad_sanitize(x: torch.Tensor, clip: float = 1e3) -> torch.Tensor:
+def grad_sanitize(x: torch.Tensor, clip: float = 1e3, tag: Optional[str] = None) -> torch.Tensor:
+    """``tag``: report a non-finite incoming gradient as ``[BWD-FIX]`` (``utils.diag``)."""
     if not torch.is_grad_enabled() or not x.requires_grad:
         return x
-    return _GradSanitize.apply(x, clip)
+    return _GradSanitize.apply(x, clip, tag)
 
 
 def sanitize(x: torch.Tensor, clip: float) -> torch.Tensor:

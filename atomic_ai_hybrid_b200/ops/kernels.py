@@ -17,6 +17,7 @@ import torch.nn.functional as F
 
 from . import reference as R
 from ._ext import ext
+from ..utils.diag import DIAG
 
 
 def _acc_for(p: Optional[torch.Tensor]):
@@ -302,8 +303,8 @@ class _AddRMSNorm(torch.autograd.Function):
     output)."""
 
     @staticmethod
-    def forward(ctx, x, delta, scale, clip, eps, sanitize_delta_grad):
-        xo, y, rstd = ext().add_rmsnorm_fwd(x, delta.contiguous(), scale, clip, eps)
+    def forward(ctx, x, delta, scale, clip, eps, sanitize_delta_grad, stats):
+        xo, y, rstd = ext().add_rmsnorm_fwd(x, delta.contiguous(), scale, clip, eps, stats)
         ctx.save_for_backward(xo, scale, rstd)
         ctx.clip, ctx.sdg = clip, sanitize_delta_grad
         return xo, y
@@ -315,11 +316,18 @@ class _AddRMSNorm(torch.autograd.Function):
         if gy is None:
             gy = torch.zeros_like(xo)
         dx, dd = ext().add_rmsnorm_bwd(gy, gxo, xo, scale, rstd, ctx.clip, ctx.sdg, acc)
-        return dx, dd, _ret_grad(scale, acc, direct), None, None, None
+        return dx, dd, _ret_grad(scale, acc, direct), None, None, None, None
 
 
-def add_rmsnorm(x, delta, scale, clip: float, eps: float = 1e-6, sanitize_delta_grad: bool = False):
-    return _AddRMSNorm.apply(x, delta, scale, clip, eps, sanitize_delta_grad)
+def add_rmsnorm(x, delta, scale, clip: float, eps: float = 1e-6, sanitize_delta_grad: bool = False,
+                diag_tag: Optional[str] = None):
+    """``diag_tag``: fold ``max |x + delta|`` and a non-finite-delta flag into the step
+    diagnostics (``utils.diag``) from inside the kernel."""
+    stats = None
+    if diag_tag is not None:
+        from ..utils.diag import DIAG
+        stats = DIAG.residual_pair(diag_tag, x.device)
+    return _AddRMSNorm.apply(x, delta, scale, clip, eps, sanitize_delta_grad, stats)
 
 
 class _NormGate(torch.autograd.Function):
@@ -568,7 +576,12 @@ def _gdn2_layer_fused(mod, x):
     k = l2norm_heads(k.view(Bsz, L, H, D))
     bg, wg, g = gdn_gates(bp, wp, fp, mod.decay_a, D)
     shp = (Bsz, L, H, D)
+    DIAG.stage("GDN2", "q", q)
+    DIAG.stage("GDN2", "k", k)
+    DIAG.stage("GDN2", "v", v)
+    DIAG.stage("GDN2", "g", g)
     o = gdn2(q, k, v.view(shp), wg.view(shp), bg.view(shp), g.view(shp), 1.0, mod.cfg.gdn_chunk)
+    DIAG.stage("GDN2", "o", o)
     o = _out_norm_gate(mod.cfg.d_model, o.reshape(Bsz, L, dl).to(x.dtype), og, mod.out_norm.scale, zclip=1e2)
     return mod.out_projection(o)
 
@@ -610,14 +623,18 @@ def mamba2_layer(mod, x):
     P = dil // Hs
     fused = x.dtype == torch.bfloat16 and row_fusable(dil)
     x_bc, res = xz[..., :dil], xz[..., dil:]
+    DIAG.stage("MAMBA2", "in_proj", xz)
     x_conv = conv1d(x_bc, mod.conv_w, mod.conv_b, True)
+    DIAG.stage("MAMBA2", "x_conv", x_conv)
     A = -torch.exp(mod.A_log.float().clamp(-20.0, 20.0))
     xin = mod.bc_input(x_bc)
     Bm, Cm, dtp = linear_multi(xin, [(m.kernel, m.bias) for m in (mod.B_proj, mod.C_proj, mod.dt_proj)])
     dt = dt_act(dtp) if fused else F.softplus(dtp).clamp(1e-2, 1.0)
+    DIAG.stage("MAMBA2", "dt", dt)
     y = ssd(dt.view(Bsz, L, Hs, P), A, Bm.clamp(-1e3, 1e3), Cm.clamp(-1e3, 1e3), x_conv.view(Bsz, L, Hs, P),
             mod.cfg.ssd_chunk)
     y = y.reshape(Bsz, L, dil).to(x_bc.dtype)
+    DIAG.stage("MAMBA2", "ssd_y", y)
     if fused:
         return mod.out_projection(_out_norm_gate(mod.cfg.d_inner, y, res, mod.ssm_out_norm.scale, oclip=3e2))
     from ..parallel.tp import get_tp, tp_rmsnorm

@@ -25,6 +25,8 @@ import torch.distributed as dist
 from ..optim import FlatParamStore, HybridOptimizer, grad_scale_of, label_adamw_only, label_of
 from ..optim.store import is_ep_local
 from .loss import compute_loss
+from ..utils.diag import DIAG
+from ..utils.nvtx import nvtx_range
 
 
 class Trainer:
@@ -117,9 +119,11 @@ class Trainer:
     # ------------------------------------------------------------ micro-step
     def _micro_body(self, batch: Dict[str, torch.Tensor]):
         self.model.train()
-        loss, info = compute_loss(self.model, batch, deterministic=False, ce_chunk_size=self.ce_chunk_size,
-                                  collinearity_coef=self.collinearity_coef)
-        loss.backward()
+        with nvtx_range("forward"):
+            loss, info = compute_loss(self.model, batch, deterministic=False, ce_chunk_size=self.ce_chunk_size,
+                                      collinearity_coef=self.collinearity_coef)
+        with nvtx_range("backward"):
+            loss.backward()
         if info.get("assignment_frac") is not None:
             self._frac_sum += info["assignment_frac"]
         self._loss_sum += loss.detach()
@@ -193,13 +197,16 @@ class Trainer:
             self.comm.reduce_scatter_grads()
         # every rank's loss is the mean over its own tokens, and the reduction sums the
         # ranks: dividing by n_accum * world gives the gradient of the global-batch mean
-        out = self.opt.step(n * self.world, frac)
+        with nvtx_range("optimizer"):
+            out = self.opt.step(n * self.world, frac)
         if self.fused_comm:
             self.comm.end_step()
         elif self.comm is not None:
             self.comm.all_gather_params()
         out["loss"] = self._loss_sum / max(self._n_micro, 1)
         self.reset_accumulators()
+        # step diagnostics: the previous step's events print now ([FWD-DIAG], [RESID-DIAG], ...)
+        DIAG.end_step(self.global_step)
         self.global_step += 1
         return out
 

@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA-graph capture of the micro-step")
     ap.add_argument("--ep", type=int, default=1,
                     help="expert-parallel ranks (1 or the number of GPUs): routed experts split over the GPUs")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel ranks (heads split, tokens split between the mixers); each group of "
+                         "--tp GPUs trains on --seqs-per-gpu x --tp sequences per step")
     return ap.parse_args()
 
 
@@ -137,12 +140,22 @@ def main():
     if args.layers:
         over["num_layers"] = args.layers
     cfg = get_preset(args.model, **over)
-    if args.ep > 1:
+    S, mb = args.seq_len, args.micro_batch
+    tp = max(1, args.tp)
+    if tp > 1:
+        if world % tp:
+            raise SystemExit("--tp must divide the number of GPUs")
+        if args.ep > 1 and args.ep != tp:
+            raise SystemExit("with --tp, --ep must equal --tp (experts split over the tensor-parallel group)")
+        from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel
+        init_tensor_parallel(tp, dev, expert_parallel=args.ep > 1, max_rows=mb * S // tp, max_width=cfg.d_model)
+    elif args.ep > 1:
         if args.ep != world:
             raise SystemExit("--ep must equal the number of GPUs")
         from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
         set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
-    torch.manual_seed(1234 + (rank if args.ep > 1 else 0))  # distinct experts per expert-parallel rank
+    # distinct experts per expert-parallel rank (its index in the expert-parallel group)
+    torch.manual_seed(1234 + (rank % args.ep if args.ep > 1 else 0))
     with torch.device(dev):
         model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16)
     # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0
@@ -156,13 +169,12 @@ def main():
     # the eager baseline keeps NCCL collectives; the CUDA path uses the peer-memory fused step
     trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev,
                       cuda_graph=use_graph, comm="nccl" if args.impl == "eager" else "auto",
-                      ep_max_tokens=args.micro_batch * args.seq_len if args.ep > 1 else 0)
+                      ep_max_tokens=args.micro_batch * args.seq_len // tp if args.ep > 1 else 0)
     trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
 
-    S, mb = args.seq_len, args.micro_batch
-    n_micro = max(1, args.seqs_per_gpu // mb)
-    seqs = n_micro * mb
-    gen = torch.Generator().manual_seed(17 + rank)
+    n_micro = max(1, args.seqs_per_gpu * tp // mb)
+    seqs = n_micro * mb  # per data-parallel replica (one tensor-parallel group)
+    gen = torch.Generator().manual_seed(17 + rank // tp)
     host_ids = torch.randint(0, cfg.vocab_size, (n_micro, mb, S + 1), generator=gen, dtype=torch.int32).pin_memory()
     dev_ids = host_ids.to(dev)
 
@@ -202,7 +214,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    tokens_step = seqs * S * world
+    tokens_step = seqs * S * (world // tp)
     value = tokens_step / (ms / 1e3)
 
     e2e = None
@@ -239,9 +251,10 @@ def main():
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic tokens, random-init weights",
             "impl": args.impl,
-            "config": {"model": args.model, "global_batch": seqs * world, "seq_len": S,
+            "config": {"model": args.model, "global_batch": seqs * (world // tp), "seq_len": S,
                        "micro_batch": mb, "grad_accum": n_micro,
-                       "parallelism": (f"dp{world}" if world > 1 else "dp1") + (f"+ep{args.ep}" if args.ep > 1 else ""),
+                       "parallelism": f"dp{world // tp}" + (f"+tp{tp}" if tp > 1 else "")
+                       + (f"+ep{args.ep}" if args.ep > 1 else ""),
                        "sharding": "param/optimizer owner-sharded, bf16 weights resident",
                        "collectives": ("none" if world == 1 else
                                        "NVLink peer memory: reduce-scatter fused into the optimizer's first pass, "
