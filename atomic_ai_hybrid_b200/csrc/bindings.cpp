@@ -1130,6 +1130,16 @@ void copy_out(torch::Tensor src, torch::Tensor peers, int64_t off_bytes) {
   check_launch("ahb_copy_out");
 }
 
+// acc (N,) fp32 += column sums of dy (M, N) bf16: the bias gradient added into the gradient store
+void bias_grad_acc(torch::Tensor dy, torch::Tensor acc) {
+  TORCH_CHECK(dy.is_cuda() && dy.scalar_type() == at::kBFloat16 && dy.dim() == 2 && dy.is_contiguous() &&
+                  dy.size(1) % 8 == 0, "bias_grad_acc: dy bf16 (M, N), N % 8 == 0");
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() == dy.size(1),
+              "bias_grad_acc: acc fp32 (N,)");
+  ahb_bias_grad_acc(dy.data_ptr(), dy.size(0), (int)dy.size(1), acc.data_ptr<float>(), cur_stream());
+  check_launch("ahb_bias_grad_acc");
+}
+
 // ------------------------------------------------------------ tensor parallelism over peer memory
 // Row-parallel projection with the reduce-scatter in the epilogue: rows of group g of `a` times `b`
 // are stored at out_ptrs[g] (rank g's receive slot for this rank; raw device pointers, peers' included).
@@ -1276,6 +1286,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_scatter_f32", &reduce_scatter_f32);
   m.def("copy_out", &copy_out);
   m.def("tp_gemm_rs", &tp_gemm_rs);
+  m.def("bias_grad_acc", &bias_grad_acc);
   m.def("sum_slots", &sum_slots);
   m.def("memcpy_async", &memcpy_async);
 }

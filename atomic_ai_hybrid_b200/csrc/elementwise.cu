@@ -125,6 +125,54 @@ __global__ void colsum_add_kernel(const float* __restrict__ part, int nb, int D,
   out[c] += s;
 }
 
+// ----------------------------------------------------------------- bias gradient
+// acc[c] += sum_r dy[r, c]  (dy bf16 (M, N) row-major, N % 8 == 0).  A block covers 256 columns
+// (32 threads x 8 columns, 16-byte loads) and a slice of the rows (8 row lanes); the row lanes
+// are reduced in shared memory and each column gets one fp32 atomic per block.
+__global__ void bias_grad_kernel(const __nv_bfloat16* __restrict__ dy, int64_t M, int N, int64_t rows_per,
+                                 float* __restrict__ acc) {
+  __shared__ float red[8][257];
+  const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + cg * 8;
+  const int64_t r_lo = blockIdx.y * rows_per, r_hi = r_lo + rows_per < M ? r_lo + rows_per : M;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < N) {
+    for (int64_t r = r_lo + rl; r < r_hi; r += 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(dy + r * N + c0);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        a[2 * i] += f.x;
+        a[2 * i + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[rl][cg * 8 + i] = a[i];
+  __syncthreads();
+  const int c = threadIdx.x;  // one column of the block per thread
+  if (blockIdx.x * 256 + c < N) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += red[j][c];
+    atomicAdd(acc + blockIdx.x * 256 + c, s);
+  }
+}
+
+void ahb_bias_grad_acc(const void* dy, int64_t M, int N, float* acc, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int gx = (N + 255) / 256;
+  int64_t gy = ((int64_t)sms * 8 + gx - 1) / gx;
+  int64_t rows_per = (M + gy - 1) / gy;
+  rows_per = (rows_per + 7) / 8 * 8;
+  gy = (M + rows_per - 1) / rows_per;
+  bias_grad_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>((const __nv_bfloat16*)dy, M, N, rows_per, acc);
+}
+
 // ----------------------------------------------------------------- causal conv1d
 // x: (B, L, C) with row stride `xs` (elements); w: (C, W) fp32 or bf16; b: (C,) fp32.
 // y[b,t,c] = act(sum_k w[c,k] * x[b, t-(W-1)+k, c] + bias[c]), then clamp(+-clip) if clip>0.

@@ -190,6 +190,7 @@ void ahb_symm_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t e
                       cudaStream_t st);
 void ahb_reduce_scatter_f32(const float* const* peers_dev, int world, int64_t lo, int64_t n, float* out,
                             cudaStream_t st);
+void ahb_bias_grad_acc(const void* dy, int64_t M, int N, float* acc, cudaStream_t st);
 // tensor parallelism over peer memory
 int ahb_gemm_rs_peer(const void* a, int64_t a_rows, int64_t K, const void* b, int64_t N, const int* grp_off, int W,
                      void* const* out_tab, int m_rot, int* err, int num_sms, cudaStream_t st);

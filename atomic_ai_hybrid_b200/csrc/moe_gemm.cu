@@ -34,12 +34,21 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB
 constexpr int B_BYTES = 256 * BK * 2;  // 32 KB (NB * BNacc = 256 columns)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 1024;  // tile ring, alignment, barriers + offsets
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5,
            EPI_STORE_PEER = 6 };
 
 constexpr int MAX_PEERS = 8;
+// EPI_STORE_PEER stages each warp's 32 x 256 output rows in shared memory and writes every row
+// as one 512-byte warp store (coalesced NVLink writes); it runs a 3-stage ring to make room.
+constexpr int STG_LD = 256 + 8;
+constexpr size_t STG_BYTES = 4 * 32 * STG_LD * 2;
+template <int EPI>
+constexpr int n_stages() { return EPI == EPI_STORE_PEER ? 3 : STAGES; }
+template <int EPI>
+constexpr size_t smem_bytes() {
+  return (size_t)n_stages<EPI>() * STAGE_BYTES + 1024 + 1024 + (EPI == EPI_STORE_PEER ? STG_BYTES : 0);
+}
 
 struct Params {
   CUtensorMap ta0, ta1, tb0, tb1;
@@ -118,12 +127,13 @@ AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, T
 template <bool KGROUP, bool A_MN, bool B_MN, int NB, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_constant__ Params p) {
   constexpr int BNA = 256 / NB;  // columns per accumulator
+  constexpr int NST = n_stages<EPI>();
   constexpr uint32_t IDESC = idesc_bf16(BM, BNA, A_MN, B_MN);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * STAGE_BYTES);
+  uint64_t* empty = full + NST;
+  uint64_t* tfull = empty + NST;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -132,7 +142,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
@@ -202,7 +212,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
             for (int i = 0; i < BNA / 64; ++i) tma_load_2d(sbn + i * 8192, mb, full + stage, n0 + 64 * i, r);
           }
         }
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == NST) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok) {  // let copies already in flight land before the CTA exits
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
         }
         issued = true;
         umma_commit(empty + stage);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == NST) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
       umma_commit(tfull + acc);
@@ -269,8 +279,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
       const int row = t.m0 + row_in_tile;
       const int n0 = t.n0 * BNA;
       const float alpha = p.alpha ? *p.alpha : 1.f;
+      if constexpr (EPI == EPI_STORE_PEER) {
+        bf16* stg = reinterpret_cast<bf16*>(smem + NST * STAGE_BYTES + 1024) + q * 32 * STG_LD;
 #pragma unroll 1
-      for (int c = 0; c < BNA / 32; ++c) {
+        for (int c = 0; c < BNA / 32; ++c) {
+          if (n0 + c * 32 >= p.N) break;
+          float v0[32];
+          tmem_ld32(tb + c * 32, v0);
+          store_bf16x32(stg + lane * STG_LD + c * 32, v0);
+        }
+        __syncwarp();
+        // row r of the warp's 32: lanes write its 256 columns as one 512-byte segment
+        bf16* dst = static_cast<bf16*>(p.out_tab[t.e]) + static_cast<int64_t>(t.m0 + q * 32 - off[t.e]) * p.N;
+        const int col = n0 + lane * 8;
+        if (col < p.N) {
+#pragma unroll 4
+          for (int r = 0; r < 32; ++r)
+            *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r) * p.N + col) =
+                *reinterpret_cast<const uint4*>(stg + r * STG_LD + lane * 8);
+        }
+        __syncwarp();
+      }
+#pragma unroll 1
+      for (int c = 0; c < (EPI == EPI_STORE_PEER ? 0 : BNA / 32); ++c) {
         const int col = n0 + c * 32;
         if (col >= p.N) break;  // partial last tile (N % 32 == 0)
         float v0[32];
@@ -292,9 +323,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
           store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
           store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
           store_bf16x32(static_cast<bf16*>(p.out2) + o, v1);
-        } else if constexpr (EPI == EPI_STORE_PEER) {
-          bf16* dst = static_cast<bf16*>(p.out_tab[t.e]) + static_cast<int64_t>(row - off[t.e]) * p.N + col;
-          store_bf16x32(dst, v0);
         } else if constexpr (EPI == EPI_GELU_FWD) {
           float h[32];
 #pragma unroll
@@ -399,12 +427,13 @@ int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_
 template <bool KG, bool AMN, bool BMN, int NB, int EPI>
 int launch(const Params& p, int grid, cudaStream_t st) {
   auto k = moe_gemm_kernel<KG, AMN, BMN, NB, EPI>;
+  constexpr size_t SMEM = smem_bytes<EPI>();
   static bool init = false;
   if (!init) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess) return -3;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM) != cudaSuccess) return -3;
     init = true;
   }
-  k<<<grid, NTHREADS, SMEM_BYTES, st>>>(p);
+  k<<<grid, NTHREADS, SMEM, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

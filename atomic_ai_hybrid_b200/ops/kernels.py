@@ -432,6 +432,18 @@ def _wgrad_acc(acc, x2, dy2):
     acc.add_((x2.t() @ dy2).float())
 
 
+def bias_grad(b, dy2):
+    """Gradient of a bias from ``dy2 (M, N)``: added straight into the fp32 gradient
+    store by a column-sum kernel when the bias has an accumulator (returns None),
+    else returned as an fp32 tensor."""
+    acc = getattr(b, "_ahb_grad_acc", None) if b is not None else None
+    if (acc is not None and dy2.is_cuda and dy2.dtype == torch.bfloat16 and dy2.shape[1] % 8 == 0
+            and acc.dtype == torch.float32 and acc.numel() == dy2.shape[1]):
+        ext().bias_grad_acc(dy2.contiguous(), acc.view(-1))
+        return None
+    return dy2.sum(0, dtype=torch.float32)
+
+
 class _MultiLinear(torch.autograd.Function):
     """Several projections of one input, ``y_i = x W_i (+ b_i)`` (cuBLAS).  The
     backward accumulates ``dx = sum_i dy_i W_i^T`` in one buffer (beta = 1) instead of
@@ -449,11 +461,13 @@ class _MultiLinear(torch.autograd.Function):
             outs.append(y.view(*x.shape[:-1], w.shape[1]))
         ctx.save_for_backward(x, *ws)
         ctx.n, ctx.has_b = n, [b is not None for b in bs]
+        ctx.bs = list(bs)
         return tuple(outs)
 
     @staticmethod
     def backward(ctx, *dys):
         x, *ws = ctx.saved_tensors
+        b_params = ctx.bs
         x2 = x.reshape(-1, x.shape[-1])
         dx = None
         dws, dbs = [], []
@@ -475,7 +489,7 @@ class _MultiLinear(torch.autograd.Function):
                 dws.append(None)
             else:
                 dws.append((x2.t() @ dy2).to(w.dtype))
-            dbs.append(dy2.sum(0, dtype=torch.float32) if hb else None)
+            dbs.append(bias_grad(b_params[len(dbs)], dy2) if hb else None)
         if dx is not None:
             dx = dx.view(x.shape)
         return (dx, None, *dws, *dbs)

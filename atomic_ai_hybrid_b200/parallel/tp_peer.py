@@ -295,11 +295,12 @@ class _PeerGatherLinear(torch.autograd.Function):
         full = peer.all_gather_rows(x.to(torch.bfloat16), consume)
         ctx.save_for_backward(full, *ws)
         ctx.peer, ctx.n, ctx.has_b = peer, n, [b is not None for b in bs]
+        ctx.bs = list(bs)
         return tuple(outs)
 
     @staticmethod
     def backward(ctx, *dys):
-        from ..ops.kernels import _wgrad_acc
+        from ..ops.kernels import _wgrad_acc, bias_grad
         full, *ws = ctx.saved_tensors
         peer = ctx.peer
         wcs = [_bf16(w) for w in ws]
@@ -331,7 +332,7 @@ class _PeerGatherLinear(torch.autograd.Function):
                 dws.append(None)
             else:
                 dws.append((full.t() @ dy).to(w.dtype))
-            dbs.append(dy.sum(0, dtype=torch.float32) if hb else None)
+            dbs.append(bias_grad(ctx.bs[len(dbs)], dy) if hb else None)
         return (dx, None, None, *dws, *dbs)
 
 

@@ -262,3 +262,14 @@ def test_linear_multi_grads():
     for b, r in zip(bk, br):
         if b is not None:
             _close(b.grad, r.grad, 1e-3, 1e-2, "db")
+
+
+@pytest.mark.parametrize("M,N", [(16384, 2048), (1000, 136), (7, 1024)])
+def test_bias_grad_acc_matches_column_sums(M, N):
+    from atomic_ai_hybrid_b200.ops._ext import ext
+    dev = torch.device("cuda", 0)
+    dy = torch.randn(M, N, device=dev).to(torch.bfloat16)
+    acc = torch.randn(N, device=dev)
+    ref = acc + dy.float().sum(0)
+    ext().bias_grad_acc(dy, acc)
+    torch.testing.assert_close(acc, ref, rtol=1e-4, atol=1e-3)
