@@ -14,6 +14,8 @@ Cases:
   tp_gemm_rs      tcgen05 GEMM whose epilogue stores partial tiles into the owners
   dp_reduce_scatter / dp_all_gather  the data-parallel fused-step transfers as
                   stand-alone kernels (fp32 gradient slice pull-sum, bf16 push)
+  ep_dispatch / ep_return  expert-parallel token rows (uniform top-k routing) stored
+                  into the expert owners' receive buffers and the results back
 """
 from __future__ import annotations
 
@@ -61,6 +63,10 @@ def main(argv=None):
     ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--k", type=int, default=512, help="contraction of the row-parallel GEMM (d_in / W)")
     ap.add_argument("--dp-mb", type=int, default=512, help="fp32 gradient MB per rank for the data-parallel cases")
+    ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens per rank for the expert-parallel cases")
+    ap.add_argument("--ep-experts", type=int, default=64)
+    ap.add_argument("--ep-k", type=int, default=4)
+    ap.add_argument("--ep-d", type=int, default=2048)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
@@ -171,6 +177,55 @@ def main(argv=None):
         E.ipc_free(ptr)
         E.ipc_free(cptr)
     peer.close()
+
+    # expert parallelism: dispatch / return of routed rows (uniform routing, k distinct experts)
+    from ..parallel.ep import EPGroup
+    T, k, d, nE = args.ep_tokens, args.ep_k, args.ep_d, args.ep_experts
+    ep = EPGroup(W, rank, nE, k, d, T, dev)
+    scores = torch.rand(T, nE, device=dev, generator=g)
+    top_idx = scores.topk(k, dim=1).indices.to(torch.int32).contiguous()
+    xb = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+    eidx, counts, off_local, pos = E.moe_route_local(top_idx, nE)
+    E.ep_publish(counts, ep.count_peers, ep.rank)
+    ep.barrier()
+    dst_base, off, seg, R = ep.layout()
+    dst_pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+    cnt = counts.cpu().numpy().reshape(-1)
+    El = nE // W
+    remote_rows = int(cnt.sum() - cnt[rank * El:(rank + 1) * El].sum())
+
+    def dispatch():
+        E.ep_dispatch(xb, True, T, k, eidx, pos, off_local, dst_base, ep.El, ep.recv_peers, ep.meta_peers, ep.rank,
+                      dst_pos)
+        ep.barrier()
+
+    ms = _time(dispatch, args.warmup, args.iters)
+    emit("ep_dispatch", ms, remote_rows * (d * 2 + 8), extra={"rows_out": int(cnt.sum()), "remote_rows": remote_rows})
+    meta = ep.meta[:R].clone()
+    ys = torch.randn(R, d, device=dev, generator=g).to(torch.bfloat16)
+    mine = meta[:, 0].cpu()
+    back_remote = int((mine != rank).sum()) if R > 0 else 0
+
+    def ret():
+        if R > 0:
+            E.ep_return(ys, meta, R, ep.ret_peers)
+        ep.barrier()
+
+    ms = _time(ret, args.warmup, args.iters)
+    emit("ep_return", ms, max(back_remote, 1) * d * 2, extra={"rows_in": R, "remote_rows": back_remote})
+    # the same exchange with NCCL: an all-to-all of the rows grouped by destination rank
+    send = torch.randn(T * k, d, device=dev, generator=g).to(torch.bfloat16)
+    per = [int(cnt[r * El:(r + 1) * El].sum()) for r in range(W)]
+    recv_sizes = torch.tensor(per, dtype=torch.int64, device=dev)
+    allsz = [torch.empty_like(recv_sizes) for _ in range(W)]
+    dist.all_gather(allsz, recv_sizes)
+    rin = [int(a[rank]) for a in allsz]
+    rbuf = torch.empty(sum(rin), d, dtype=torch.bfloat16, device=dev)
+    nccl = _time(lambda: dist.all_to_all_single(rbuf, send, rin, per), args.warmup, args.iters)
+    out[-2]["nccl_all_to_all_ms"] = round(nccl, 4)
+    if rank == 0:
+        print(json.dumps({"case": "ep_nccl_all_to_all", "world": W, "ms": round(nccl, 4)}), flush=True)
+    ep.close()
     dist.barrier()
     dist.destroy_process_group()
     return out
