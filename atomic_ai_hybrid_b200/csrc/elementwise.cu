@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(256) conv1d_fwd_stream_kernel(const bf16* __re
 }
 
 template <typename WT>
-__global__ void __launch_bounds__(256, 2) conv1d_bwd_stream_kernel(const bf16* __restrict__ x, int64_t xs,
+__global__ void __launch_bounds__(256) conv1d_bwd_stream_kernel(const bf16* __restrict__ x, int64_t xs,
                                                                 const WT* __restrict__ w,
                                                                 const float* __restrict__ bias,
                                                                 const bf16* __restrict__ dy, bf16* __restrict__ dx,
@@ -431,74 +431,52 @@ __global__ void __launch_bounds__(256, 2) conv1d_bwd_stream_kernel(const bf16* _
       else { xw[k][0] = xw[k][1] = xw[k][2] = xw[k][3] = 0.f; }
     }
     const int own_end = t0 + CSPAN < L ? t0 + CSPAN : L;
-    const int t_last = own_end + 3;
-    // dp(t) for t in [t0, own_end + 3): the last three steps only feed dx of the span's tail.
-    // The x / dy vectors of step t + 1 are loaded (raw bf16) before step t is computed, so each
-    // step's loads overlap the previous step's arithmetic.
-    uint2 nx = make_uint2(0u, 0u), nd = make_uint2(0u, 0u);
-    if (t0 < L) {
-      nx = *reinterpret_cast<const uint2*>(xb + (int64_t)t0 * xs);
-      nd = *reinterpret_cast<const uint2*>(dyb + (int64_t)t0 * C);
-    }
+    // dp(t) for t in [t0, own_end + 3): the last three steps only feed dx of the span's tail
 #pragma unroll 2
-    for (int t = t0; t < t_last; ++t) {
-      {
-        const uint2 cx = nx, cd = nd;
-        const int tn = t + 1;
-        if (tn < L && tn < t_last) {
-          nx = *reinterpret_cast<const uint2*>(xb + (int64_t)tn * xs);
-          nd = *reinterpret_cast<const uint2*>(dyb + (int64_t)tn * C);
-        }
-        float xc[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
-        if (t < L) {
-          float dv[4];
-          {
-            const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&cx);
-            const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&cd);
-            const float2 x01 = __bfloat1622float2(hx[0]), x23 = __bfloat1622float2(hx[1]);
-            const float2 d01 = __bfloat1622float2(hd[0]), d23 = __bfloat1622float2(hd[1]);
-            xc[0] = x01.x; xc[1] = x01.y; xc[2] = x23.x; xc[3] = x23.y;
-            dv[0] = d01.x; dv[1] = d01.y; dv[2] = d23.x; dv[3] = d23.y;
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float a = bs[j] + wk[j][0] * xw[0][j] + wk[j][1] * xw[1][j] + wk[j][2] * xw[2][j] + wk[j][3] * xc[j];
-            float gj = dv[j], post = a;
-            if (silu) {
-              const float sg = sigmoidf_(a);
-              post = a * sg;
-              gj *= sg * (1.f + a * (1.f - sg));
-            }
-            if (clip > 0.f && fabsf(post) > clip) gj = 0.f;
-            g[j] = gj;
-          }
-          if (t < own_end) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              dbl[j] += g[j];
-              dwl[j][0] += g[j] * xw[0][j];
-              dwl[j][1] += g[j] * xw[1][j];
-              dwl[j][2] += g[j] * xw[2][j];
-              dwl[j][3] += g[j] * xc[j];
-            }
-          }
-        }
-        const int sx = t - 3;  // dx[s] = sum_k w_k dp[s + 3 - k]
-        if (sx >= t0) {
-          float o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = wk[j][0] * g[j] + wk[j][1] * dpw[2][j] + wk[j][2] * dpw[1][j] + wk[j][3] * dpw[0][j];
-          st4(dxb + (int64_t)sx * dxs, o);
-        }
+    for (int t = t0; t < own_end + 3; ++t) {
+      float xc[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (t < L) {
+        float dv[4];
+        ld4(xb + (int64_t)t * xs, xc);
+        ld4(dyb + (int64_t)t * C, dv);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          xw[0][j] = xw[1][j];
-          xw[1][j] = xw[2][j];
-          xw[2][j] = xc[j];
-          dpw[0][j] = dpw[1][j];
-          dpw[1][j] = dpw[2][j];
-          dpw[2][j] = g[j];
+          const float a = bs[j] + wk[j][0] * xw[0][j] + wk[j][1] * xw[1][j] + wk[j][2] * xw[2][j] + wk[j][3] * xc[j];
+          float gj = dv[j], post = a;
+          if (silu) {
+            const float sg = sigmoidf_(a);
+            post = a * sg;
+            gj *= sg * (1.f + a * (1.f - sg));
+          }
+          if (clip > 0.f && fabsf(post) > clip) gj = 0.f;
+          g[j] = gj;
         }
+        if (t < own_end) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dbl[j] += g[j];
+            dwl[j][0] += g[j] * xw[0][j];
+            dwl[j][1] += g[j] * xw[1][j];
+            dwl[j][2] += g[j] * xw[2][j];
+            dwl[j][3] += g[j] * xc[j];
+          }
+        }
+      }
+      const int sx = t - 3;  // dx[s] = sum_k w_k dp[s + 3 - k]
+      if (sx >= t0) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = wk[j][0] * g[j] + wk[j][1] * dpw[2][j] + wk[j][2] * dpw[1][j] + wk[j][3] * dpw[0][j];
+        st4(dxb + (int64_t)sx * dxs, o);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xw[0][j] = xw[1][j];
+        xw[1][j] = xw[2][j];
+        xw[2][j] = xc[j];
+        dpw[0][j] = dpw[1][j];
+        dpw[1][j] = dpw[2][j];
+        dpw[2][j] = g[j];
       }
     }
 #pragma unroll
