@@ -24,10 +24,10 @@ def _port():
     return p
 
 
-def _cfg(kind):
+def _cfg(kind, world=2):
     if kind == "interleaved":
         return get_preset("tiny", num_layers=2, layer_types=("mamba2", "gdn2"), vocab_size=512, d_model=128,
-                          n_heads=2, n_heads_ssm=4, d_ff=128, n_routed_experts=4, d_state=32)
+                          n_heads=max(2, world), n_heads_ssm=4, d_ff=128, n_routed_experts=4, d_state=32)
     return get_preset("reference_tiny", dropout_rate=0.0, router_noise_std=0.0)
 
 
@@ -44,7 +44,7 @@ def _parity(rank, world, port, kind, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, shard_tensor
-        cfg = _cfg(kind)
+        cfg = _cfg(kind, world)
         set_parallel_context(ParallelContext())
         torch.manual_seed(0)
         full = HybridMoEModel(cfg, compute_dtype=torch.float32)
@@ -82,12 +82,12 @@ def _parity(rank, world, port, kind, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind", ["interleaved", "blockdar"])
-def test_tp2_forward_backward_matches_single_rank(kind):
+@pytest.mark.parametrize("kind,world", [("interleaved", 2), ("blockdar", 2), ("interleaved", 4)])
+def test_tp_forward_backward_matches_single_rank(kind, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_parity, args=(r, 2, port, kind, q)) for r in range(2)]
+    procs = [ctx.Process(target=_parity, args=(r, world, port, kind, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
