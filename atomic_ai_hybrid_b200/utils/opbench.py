@@ -175,9 +175,26 @@ def bench_conv(B, T, C, warmup, iters, flush, mode="fwdbwd"):
     return {"op": "conv1d", "mode": mode, "B": B, "T": T, "C": C, "ms": ms, "min_io_gb_s": io / ms / 1e6}
 
 
+def bench_gemm_rs(W, n, K, N, warmup, iters, flush):
+    """The tensor-parallel GEMM + reduce-scatter kernel on one GPU: the W destination
+    slots are local buffers (the NVLink stores become local stores), so this measures
+    the GEMM and its staged epilogue; ``utils.commbench`` measures it across GPUs."""
+    from ..ops._ext import ext
+    E = ext()
+    dev = "cuda"
+    a = torch.randn(W * n, K, device=dev).to(torch.bfloat16)
+    w = (torch.randn(K, N, device=dev) / K ** 0.5).to(torch.bfloat16)
+    outs = [torch.empty(n, N, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    off = torch.arange(W + 1, dtype=torch.int32, device=dev) * n
+    ptrs = [o.data_ptr() for o in outs]
+    ms = _timeit(lambda: E.tp_gemm_rs(a, w, off, ptrs, 0), warmup, iters, flush)
+    fl = 2.0 * W * n * K * N
+    return {"op": "gemm_rs_local", "W": W, "rows": W * n, "K": K, "N": N, "ms": ms, "tflops": fl / ms / 1e9}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv"])
+    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs"])
     ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--T", type=int, default=4096)
@@ -199,6 +216,8 @@ def main(argv=None):
         r = bench_router(a.B * a.T, 2048, 32, 4, a.warmup, a.iters, flush, a.mode)
     elif a.op == "glue":
         r = bench_glue(a.B * a.T, 2048, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "gemm_rs":
+        r = bench_gemm_rs(2, a.B * a.T // 2, 512, 4096, a.warmup, a.iters, flush)
     else:
         r = bench_conv(a.B, a.T, 2048, a.warmup, a.iters, flush, a.mode)
     print(json.dumps(r), flush=True)

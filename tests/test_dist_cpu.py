@@ -63,12 +63,13 @@ def _run(rank, world, port, out_path, steps):
         dist.destroy_process_group()
 
 
-def test_two_rank_sharded_training_matches_single_process(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_training_matches_single_process(tmp_path, world):
     steps = 3
     p1 = str(tmp_path / "one.pt")
     _run(0, 1, _port(), p1, steps)
-    p2 = str(tmp_path / "two.pt")
-    mp.spawn(_run, args=(2, _port(), p2, steps), nprocs=2, join=True)
+    p2 = str(tmp_path / f"w{world}.pt")
+    mp.spawn(_run, args=(world, _port(), p2, steps), nprocs=world, join=True)
     a, b = torch.load(p1), torch.load(p2)
     assert a.keys() == b.keys()
     # the MoE router noise is disabled in this config; every update is deterministic
