@@ -1,7 +1,8 @@
 """Loss-curve parity: 200 optimizer steps of a small hybrid model through the
 sm_100a kernels (fused layers, tcgen05 MoE, fused optimizer) and through the eager
 PyTorch implementation (reference scans, SDPA, cuBLAS, PyTorch optimizer ops) from
-the same weights on the same data must give the same loss curve to 1e-2 relative."""
+the same weights on the same data must give the same loss curve to 1e-2 relative
+(10-step windows; single steps within 5e-2)."""
 import pytest
 import torch
 
@@ -9,18 +10,11 @@ pytestmark = pytest.mark.gpu
 
 
 def _data(cfg, steps, B, L, dev):
-    # learnable sequences: t[i+1] = (a t[i] + c) mod V with per-sequence (a, c)
+    # a small fixed corpus (8 sequences) cycled through: the model memorises it, so the
+    # loss falls steadily and the two curves can be compared over a real descent
     g = torch.Generator().manual_seed(0)
-    out = []
-    for _ in range(steps):
-        a = torch.randint(1, 8, (B, 1), generator=g)
-        c = torch.randint(0, cfg.vocab_size, (B, 1), generator=g)
-        t = torch.empty(B, L + 1, dtype=torch.long)
-        t[:, 0] = torch.randint(0, cfg.vocab_size, (B,), generator=g)
-        for i in range(L):
-            t[:, i + 1] = (a[:, 0] * t[:, i] + c[:, 0]) % cfg.vocab_size
-        out.append(t.to(dev))
-    return out
+    corpus = torch.randint(0, cfg.vocab_size, (8, L + 1), generator=g)
+    return [corpus[(torch.arange(B) + B * s) % 8].to(dev) for s in range(steps)]
 
 
 def _curve(impl, cfg, data, dev):
@@ -52,7 +46,7 @@ def test_kernel_and_eager_loss_curves_agree():
     e = _curve("eager", cfg, data, dev)
     rel = (k - e).abs() / e.abs()
     assert torch.isfinite(k).all() and torch.isfinite(e).all()
-    assert k[-20:].mean() < 0.8 * k[:5].mean(), "the model does not learn the synthetic task"
+    assert k[-20:].mean() < 0.8 * k[:5].mean(), ("the model does not learn the corpus", k[:5], k[-20:])
     # windows of 10 steps (the per-step losses of two bf16 paths jitter independently)
     kw, ew = k.view(20, 10).mean(1), e.view(20, 10).mean(1)
     assert ((kw - ew).abs() / ew.abs()).max() < 1e-2, (kw, ew)
