@@ -227,15 +227,16 @@ def _tp_spec(s):
 
 def _key(s, ep: bool) -> str:
     """Tensor name in the files: the flax path, plus ``#experts[lo:hi]`` for a block of
-    routed experts held by one expert-parallel rank, or ``#tp[r/W]`` for the piece of
-    tensor-parallel rank ``r`` of ``W``."""
+    routed experts held by one expert-parallel rank, or ``#tp[r/W,d<dim>p<parts>]`` for
+    the piece of tensor-parallel rank ``r`` of ``W`` (cut along ``dim``, in ``parts``
+    blocks; ``parallel.tp.shard_tensor``)."""
     name = flax_path(s.name)
     rng = _expert_range(s, ep)
     if rng is not None:
         return f"{name}#experts[{rng[0]}:{rng[1]}]"
     spec = _tp_spec(s)
     if spec is not None:
-        return f"{name}#tp[{spec[2]}/{spec[3]}]"
+        return f"{name}#tp[{spec[2]}/{spec[3]},d{spec[0]}p{spec[1]}]"
     return name
 
 
@@ -243,30 +244,52 @@ def _find(tensors: Dict[str, torch.Tensor], name: str, s, ep: bool):
     spec = _tp_spec(s)
     if spec is not None:
         return _lookup_tp(tensors, name, spec)
-    return _lookup(tensors, name, _expert_range(s, ep))
+    t = _lookup(tensors, name, _expert_range(s, ep))
+    if t is None:  # written with tensor parallelism, restored without it
+        t = _assemble_tp(tensors, name)
+    return t
+
+
+def _tp_pieces(tensors: Dict[str, torch.Tensor], name: str):
+    """{world: {rank: (tensor, dim, parts)}} of the tensor-parallel pieces of ``name``."""
+    prefix = name + "#tp["
+    out: Dict[int, Dict[int, tuple]] = {}
+    for key, v in tensors.items():
+        if not key.startswith(prefix):
+            continue
+        body = key[len(prefix):-1]
+        rw, _, dp = body.partition(",")
+        r, w = (int(x) for x in rw.split("/"))
+        dim, parts = (int(x) for x in dp[1:].split("p")) if dp else (None, None)
+        out.setdefault(w, {})[r] = (v, dim, parts)
+    return out
+
+
+def _assemble_tp(tensors: Dict[str, torch.Tensor], name: str, dim=None, parts=None):
+    """The full tensor ``name`` from the pieces of any complete tensor-parallel run."""
+    from ..parallel.tp import unshard_tensors
+    for w, pieces in sorted(_tp_pieces(tensors, name).items()):
+        if len(pieces) != w or not all(r in pieces for r in range(w)):
+            continue
+        d = pieces[0][1] if pieces[0][1] is not None else dim
+        pa = pieces[0][2] if pieces[0][2] is not None else parts
+        if d is None:
+            continue
+        return unshard_tensors([pieces[r][0] for r in range(w)], d, pa)
+    return None
 
 
 def _lookup_tp(tensors: Dict[str, torch.Tensor], name: str, spec):
     """This rank's tensor-parallel piece of ``name``: stored directly, cut from the
     full tensor, or re-cut from the pieces of a run with another tensor-parallel size."""
-    from ..parallel.tp import shard_tensor, unshard_tensors
+    from ..parallel.tp import shard_tensor
     dim, parts, rank, world = spec
-    t = tensors.get(f"{name}#tp[{rank}/{world}]")
-    if t is not None:
-        return t
+    for key in (f"{name}#tp[{rank}/{world},d{dim}p{parts}]", f"{name}#tp[{rank}/{world}]"):
+        if key in tensors:
+            return tensors[key]
     full = tensors.get(name)
     if full is None:
-        prefix = name + "#tp["
-        pieces = {}
-        for key, v in tensors.items():
-            if key.startswith(prefix):
-                r, w = (int(x) for x in key[len(prefix):-1].split("/"))
-                pieces[(w, r)] = v
-        worlds = sorted({w for w, _ in pieces})
-        for w in worlds:
-            if all((w, r) in pieces for r in range(w)):
-                full = unshard_tensors([pieces[(w, r)] for r in range(w)], dim, parts)
-                break
+        full = _assemble_tp(tensors, name, dim, parts)
     if full is None:
         return None
     return shard_tensor(full, dim, parts, world, rank)

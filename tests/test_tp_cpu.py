@@ -189,3 +189,82 @@ def test_tp_checkpoint_pieces_reassemble_for_any_world():
         assert torch.equal(_lookup_tp({"w": full}, "w", (dim, parts, 1, 2)), shard_tensor(full, dim, parts, 2, 1))
     del pieces["w#tp[1/2]"]
     assert _lookup_tp(pieces, "w", (0, 1, 0, 1)) is None
+
+
+def _ckpt(rank, world, port, root, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
+        from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, unshard_tensors
+        from atomic_ai_hybrid_b200.training.trainer import Trainer
+        cfg = _cfg("interleaved")
+        solo = dist.new_group([0])
+        set_parallel_context(ParallelContext())
+        torch.manual_seed(0)
+        full = HybridMoEModel(cfg, compute_dtype=torch.float32)
+        init_tensor_parallel(world, torch.device("cpu"))
+        m = HybridMoEModel(cfg, compute_dtype=torch.float32)
+        load_full_state(m, full.state_dict())
+        tr = Trainer(m, total_steps=10, optimizer="adamw", compute_dtype=torch.float32, device=torch.device("cpu"))
+        tr.opt.schedule.warmup = 1
+        ids = torch.randint(0, cfg.vocab_size, (2, 129), generator=torch.Generator().manual_seed(4))
+        tr.train_step([{"input_ids": ids[:, :-1], "labels": ids[:, 1:]}])
+        ck = CheckpointManager(root, rank=rank, world=world)
+        ck.save(1, tr, asynchronous=False)
+        dist.barrier()
+        # the full (unsplit) weights after the step
+        ref = {}
+        for n, p in m.named_parameters():
+            t = p.detach().clone()
+            spec = shard_spec(p)
+            if spec is not None:
+                parts = [torch.zeros_like(t) for _ in range(world)]
+                dist.all_gather(parts, t)
+                t = unshard_tensors(parts, spec[0], spec[1])
+            ref[n] = t
+        # restore into a fresh tensor-parallel model
+        m2 = HybridMoEModel(cfg, compute_dtype=torch.float32)
+        tr2 = Trainer(m2, total_steps=10, optimizer="adamw", compute_dtype=torch.float32, device=torch.device("cpu"))
+        meta = CheckpointManager(root, rank=rank, world=world).restore(1, tr2)
+        def err(n, a, b):
+            # routed experts are stored in bf16 (the reference's dtype): within bf16 rounding of
+            # the largest element; everything else bit-exact
+            d = float((a.detach() - b.detach()).abs().max())
+            if "routed_w" in n:
+                return 0.0 if d <= float(b.abs().max()) * 2 ** -8 else d
+            return d
+
+        b_of = dict(m.named_parameters())
+        res = {"tp_restore": max(err(n, p, b_of[n]) for n, p in m2.named_parameters()), "fresh": len(meta["fresh"])}
+        dist.barrier()
+        if rank == 0:
+            # and into a single-rank model: every piece reassembled
+            set_parallel_context(ParallelContext())
+            m1 = HybridMoEModel(cfg, compute_dtype=torch.float32)
+            tr1 = Trainer(m1, total_steps=10, optimizer="adamw", compute_dtype=torch.float32,
+                          device=torch.device("cpu"), group=solo)
+            meta1 = CheckpointManager(root, rank=0, world=1).restore(1, tr1)
+            res["single_restore"] = max(err(n, p, ref[n]) for n, p in m1.named_parameters())
+            res["single_fresh"] = len(meta1["fresh"])
+        q.put((rank, res))
+        dist.barrier()
+    finally:
+        set_parallel_context(ParallelContext())
+        dist.destroy_process_group()
+
+
+def test_tp_checkpoint_restores_into_tp_and_single_rank(tmp_path):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ckpt, args=(r, 2, port, str(tmp_path), q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert res[r]["fresh"] == 0 and res[r]["tp_restore"] == 0.0, res
+    assert res[0]["single_fresh"] == 0 and res[0]["single_restore"] == 0.0, res
