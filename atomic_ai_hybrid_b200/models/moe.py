@@ -152,17 +152,16 @@ class MoE(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def _shared(self, flat: torch.Tensor) -> torch.Tensor:
-        if self.swiglu and ops.use_cuda(flat) and flat.dtype == torch.bfloat16:
-            from ..ops import kernels as K
-            h1, h3 = K.linear_multi(flat, [(self.shared_w1.kernel, self.shared_w1.bias),
-                                           (self.shared_w3.kernel, self.shared_w3.bias)])
+        if self.swiglu:
+            if ops.use_cuda(flat) and flat.dtype == torch.bfloat16:
+                from ..ops import kernels as K
+                h1, h3 = K.linear_multi(flat, [(self.shared_w1.kernel, self.shared_w1.bias),
+                                               (self.shared_w3.kernel, self.shared_w3.bias)])
+            else:
+                h1, h3 = self.shared_w1(flat), self.shared_w3(flat)
             h = F.silu(h1) * h3
         else:
-            h = self.shared_w1(flat)
-        if self.swiglu and not (ops.use_cuda(flat) and flat.dtype == torch.bfloat16):
-            h = F.silu(h) * self.shared_w3(flat)
-        else:
-            h = R.gelu_tanh(h)
+            h = R.gelu_tanh(self.shared_w1(flat))
         if self.training and self.cfg.dropout_rate > 0:
             h = F.dropout(h, self.cfg.dropout_rate)
         return self.shared_w2(h)
