@@ -495,6 +495,161 @@ __global__ void __launch_bounds__(256) conv1d_bwd_stream_kernel(const bf16* __re
   }
 }
 
+// Same computation with the x / dy rows staged in shared memory by cp.async, two chunks of
+// CPF steps per warp in flight: a warp's next chunk loads while it computes the current one
+// (the kernel above keeps one load of each per warp in flight and waits on it every step).
+// Needs 16-byte aligned rows (xs % 8 == 0).  Lanes 0-15 copy the x row of a step and lanes
+// 16-31 its dy row, 16 bytes each; lane l computes channels 4l..4l+3 as above.
+constexpr int CPF = 8;
+
+AHB_DEVICE void ew_cp16(void* dst, const void* src) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(src) : "memory");
+}
+AHB_DEVICE void ew_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+AHB_DEVICE void ew_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename WT>
+__global__ void __launch_bounds__(256, 2) conv1d_bwd_pf_kernel(const bf16* __restrict__ x, int64_t xs,
+                                                               const WT* __restrict__ w,
+                                                               const float* __restrict__ bias,
+                                                               const bf16* __restrict__ dy, bf16* __restrict__ dx,
+                                                               int64_t dxs, float* __restrict__ dw,
+                                                               float* __restrict__ db, int B, int L, int C,
+                                                               bool silu, float clip) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // per warp: [2 buffers][CPF steps][x row 128 | dy row 128] bf16
+  bf16* ring = reinterpret_cast<bf16*>(smem_raw) + (threadIdx.x >> 5) * (2 * CPF * 256);
+  __shared__ float red[128][5];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 128 * 5; i += blockDim.x) (&red[0][0])[i] = 0.f;
+  __syncthreads();
+  const int cb = blockIdx.x * 128;
+  const int c0 = cb + lane * 4;
+  const int nspan = (L + CSPAN - 1) / CSPAN;
+  const int64_t gs = (int64_t)blockIdx.y * 8 + wp;
+  if (gs < (int64_t)B * nspan) {
+    const int b = (int)(gs / nspan), t0 = (int)(gs % nspan) * CSPAN;
+    float wk[4][4], bs[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) wk[j][k] = to_f(w[(c0 + j) * 4 + k]);
+      bs[j] = bias ? bias[c0 + j] : 0.f;
+    }
+    const bf16* xblk = x + (int64_t)b * L * xs + cb;
+    const bf16* dyblk = dy + (int64_t)b * L * C + cb;
+    bf16* dxb = dx + (int64_t)b * L * dxs + c0;
+    float xw[3][4], dpw[3][4], dwl[4][4], dbl[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      dbl[j] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) dwl[j][k] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dpw[k][j] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int t = t0 - 3 + k;
+      if (t >= 0) ld4(x + (int64_t)b * L * xs + c0 + (int64_t)t * xs, xw[k]);
+      else { xw[k][0] = xw[k][1] = xw[k][2] = xw[k][3] = 0.f; }
+    }
+    const int own_end = t0 + CSPAN < L ? t0 + CSPAN : L;
+    const int t_last = own_end + 3 < L ? own_end + 3 : L;  // steps with x / dy to read
+    const int t_stop = own_end + 3;                        // steps that produce dx rows
+    const int nch = (t_stop - t0 + CPF - 1) / CPF;
+    auto issue = [&](int ch) {
+      bf16* dst = ring + (ch & 1) * (CPF * 256);
+      const int half = lane >> 4, piece = lane & 15;
+#pragma unroll
+      for (int s = 0; s < CPF; ++s) {
+        const int t = t0 + ch * CPF + s;
+        if (t < t_last) {
+          const bf16* src = half ? dyblk + (int64_t)t * C : xblk + (int64_t)t * xs;
+          ew_cp16(dst + s * 256 + half * 128 + piece * 8, src + piece * 8);
+        }
+      }
+      ew_cp_commit();
+    };
+    issue(0);
+    for (int ch = 0; ch < nch; ++ch) {
+      if (ch + 1 < nch) {
+        issue(ch + 1);
+        ew_cp_wait<1>();
+      } else {
+        ew_cp_wait<0>();
+      }
+      __syncwarp();
+      const bf16* buf = ring + (ch & 1) * (CPF * 256);
+#pragma unroll 2
+      for (int s = 0; s < CPF; ++s) {
+        const int t = t0 + ch * CPF + s;
+        if (t >= t_stop) break;
+        float xc[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < L) {
+          float dv[4];
+          ld4(buf + s * 256 + lane * 4, xc);
+          ld4(buf + s * 256 + 128 + lane * 4, dv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float a = bs[j] + wk[j][0] * xw[0][j] + wk[j][1] * xw[1][j] + wk[j][2] * xw[2][j] + wk[j][3] * xc[j];
+            float gj = dv[j], post = a;
+            if (silu) {
+              const float sg = sigmoidf_(a);
+              post = a * sg;
+              gj *= sg * (1.f + a * (1.f - sg));
+            }
+            if (clip > 0.f && fabsf(post) > clip) gj = 0.f;
+            g[j] = gj;
+          }
+          if (t < own_end) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              dbl[j] += g[j];
+              dwl[j][0] += g[j] * xw[0][j];
+              dwl[j][1] += g[j] * xw[1][j];
+              dwl[j][2] += g[j] * xw[2][j];
+              dwl[j][3] += g[j] * xc[j];
+            }
+          }
+        }
+        const int sx = t - 3;  // dx[s] = sum_k w_k dp[s + 3 - k]
+        if (sx >= t0) {
+          float o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = wk[j][0] * g[j] + wk[j][1] * dpw[2][j] + wk[j][2] * dpw[1][j] + wk[j][3] * dpw[0][j];
+          st4(dxb + (int64_t)sx * dxs, o);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          xw[0][j] = xw[1][j];
+          xw[1][j] = xw[2][j];
+          xw[2][j] = xc[j];
+          dpw[0][j] = dpw[1][j];
+          dpw[1][j] = dpw[2][j];
+          dpw[2][j] = g[j];
+        }
+      }
+      __syncwarp();  // every lane is done with this buffer before the next issue overwrites it
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) atomicAdd(&red[lane * 4 + j][k], dwl[j][k]);
+      atomicAdd(&red[lane * 4 + j][4], dbl[j]);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128 * 5; i += blockDim.x) {
+    const int ch = blockIdx.x * 128 + i / 5, k = i % 5;
+    const float v = (&red[0][0])[i];
+    if (k < 4) atomicAdd(dw + ch * 4 + k, v);
+    else if (db) atomicAdd(db + ch, v);
+  }
+}
+
 // ----------------------------------------------------------------- grad accumulate / embedding
 template <typename T>
 __global__ void accum_kernel(float* __restrict__ acc, const T* __restrict__ g, int64_t n, float scale) {
@@ -620,6 +775,26 @@ void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const 
 void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, const void* dy, void* dx,
                     float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
                     cudaStream_t st) {
+  if (dtype == AHB_BF16 && C % 128 == 0 && xs % 8 == 0 && B > 0 && L > 0) {
+    const int64_t spans = (int64_t)B * ((L + CSPAN - 1) / CSPAN);
+    const dim3 grid(C / 128, (unsigned)((spans + 7) / 8));
+    constexpr int smem = 8 * 2 * CPF * 256 * 2;  // 8 warps x 2 buffers x CPF steps x (x + dy rows)
+    static bool attr = false;
+    if (!attr) {  // above the 48 KB default: opt in once per kernel
+      cudaFuncSetAttribute(conv1d_bwd_pf_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaFuncSetAttribute(conv1d_bwd_pf_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr = true;
+    }
+    if (wdtype == AHB_BF16)
+      conv1d_bwd_pf_kernel<bf16><<<grid, 256, smem, st>>>((const bf16*)x, xs, (const bf16*)w, bias, (const bf16*)dy,
+                                                          (bf16*)dx, (int64_t)C, dw_acc, db_acc, B, L, C, silu != 0,
+                                                          clip);
+    else
+      conv1d_bwd_pf_kernel<float><<<grid, 256, smem, st>>>((const bf16*)x, xs, (const float*)w, bias,
+                                                           (const bf16*)dy, (bf16*)dx, (int64_t)C, dw_acc, db_acc, B,
+                                                           L, C, silu != 0, clip);
+    return;
+  }
   if (dtype == AHB_BF16 && C % 128 == 0 && xs % 4 == 0 && B > 0 && L > 0) {
     const int64_t spans = (int64_t)B * ((L + CSPAN - 1) / CSPAN);
     const dim3 grid(C / 128, (unsigned)((spans + 7) / 8));
