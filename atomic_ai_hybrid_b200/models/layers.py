@@ -46,14 +46,21 @@ class Dense(nn.Module):
             raise ValueError(f"Dense({d_in}, {d_out}) does not split over {W} tensor-parallel ranks")
         if self.tp == "row" and bias:
             raise ValueError("a row-parallel Dense has no bias (it would be added once per rank)")
-        self.kernel = nn.Parameter(torch.empty(li, lo, dtype=dtype))
         self.bias = nn.Parameter(torch.zeros(lo, dtype=torch.float32)) if bias else None
-        lecun_normal_(self.kernel.data, d_in)
         if self.tp:
-            from ..parallel.tp import mark_shard
-            mark_shard(self.kernel, 0 if self.tp == "row" else 1, 2 if self.tp == "col2" else 1)
+            # every rank draws the full matrix (same seed, same order) and keeps its piece, so the
+            # initial model does not depend on the tensor-parallel layout
+            from ..parallel.tp import mark_shard, shard_tensor
+            _, rank = tp_world_rank()
+            dim, parts = (0 if self.tp == "row" else 1), (2 if self.tp == "col2" else 1)
+            full = lecun_normal_(torch.empty(d_in, d_out, dtype=dtype), d_in)
+            self.kernel = nn.Parameter(shard_tensor(full, dim, parts, W, rank).clone())
+            mark_shard(self.kernel, dim, parts)
             if self.bias is not None:
-                mark_shard(self.bias, 0, 2 if self.tp == "col2" else 1)
+                mark_shard(self.bias, 0, parts)
+        else:
+            self.kernel = nn.Parameter(torch.empty(li, lo, dtype=dtype))
+            lecun_normal_(self.kernel.data, d_in)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if ops.use_cuda(x) and x.dtype == torch.bfloat16:

@@ -16,21 +16,24 @@ import torch.nn.functional as F
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
-from ..parallel.tp import get_tp, mark_shard, tp_rmsnorm
+from ..parallel.tp import get_tp, mark_shard, shard_tensor, tp_rmsnorm
 from ..utils.diag import DIAG
 from .layers import Dense, RMSNorm, lecun_normal_, tp_world_rank
 
 
-def _shard_vec(t: torch.Tensor, tp: bool) -> nn.Parameter:
-    """A per-channel / per-head parameter; ``tp``: this rank's piece of it."""
-    p = nn.Parameter(t)
-    if tp:
-        mark_shard(p, 0)
+def _shard_vec(full: torch.Tensor) -> nn.Parameter:
+    """A per-channel / per-head parameter from its full-size initial value: under tensor
+    parallelism this rank's piece of it (every rank draws the full value)."""
+    W, rank = tp_world_rank()
+    if W <= 1:
+        return nn.Parameter(full)
+    p = nn.Parameter(shard_tensor(full, 0, 1, W, rank).clone())
+    mark_shard(p, 0)
     return p
 
 
-def _conv_param(d: int, width: int, std: float = 0.02, tp: bool = False) -> nn.Parameter:
-    return _shard_vec(torch.randn(d, width) * std, tp)
+def _conv_param(d: int, width: int, std: float = 0.02) -> nn.Parameter:
+    return _shard_vec(torch.randn(d, width) * std)
 
 
 class GatedDeltaNet2(nn.Module):
@@ -56,11 +59,11 @@ class GatedDeltaNet2(nn.Module):
         self.k_proj = Dense(d, d, tp="col")
         self.v_proj = Dense(d, d, tp="col")
         for n in ("q", "k", "v"):
-            setattr(self, f"{n}_conv_w", _conv_param(dl, cfg.d_conv, tp=W > 1))
-            setattr(self, f"{n}_conv_b", _shard_vec(torch.zeros(dl), W > 1))
+            setattr(self, f"{n}_conv_w", _conv_param(d, cfg.d_conv))
+            setattr(self, f"{n}_conv_b", _shard_vec(torch.zeros(d)))
         self.erase_gate = Dense(d, d, bias=True, tp="col")
         self.write_gate = Dense(d, d, bias=True, tp="col")
-        self.decay_a = _shard_vec(torch.zeros(self.n_heads), W > 1)
+        self.decay_a = _shard_vec(torch.zeros(cfg.n_heads))
         self.decay_proj = Dense(d, d, bias=True, tp="col")
         self.out_gate = Dense(d, d, tp="col")
         self.out_norm = RMSNorm(d, tp=True)
@@ -142,20 +145,23 @@ class Mamba2(nn.Module):
         dil = di // W
         self.n_heads = cfg.n_heads_ssm // W
         self.in_proj = Dense(d, 2 * di, tp="col2")
-        self.conv_w = _conv_param(dil, cfg.d_conv, tp=W > 1)
-        self.conv_b = _shard_vec(torch.zeros(dil), W > 1)
+        self.conv_w = _conv_param(di, cfg.d_conv)
+        self.conv_b = _shard_vec(torch.zeros(di))
         if cfg.ssm_init == "mamba":
-            a_log = torch.empty(self.n_heads).uniform_(0.0, math.log(16.0))
+            a_log = torch.empty(cfg.n_heads_ssm).uniform_(0.0, math.log(16.0))
         else:
-            a_log = torch.rand(self.n_heads)
-        self.A_log = _shard_vec(a_log, W > 1)
+            a_log = torch.rand(cfg.n_heads_ssm)
+        self.A_log = _shard_vec(a_log)
         self.B_proj = Dense(di, N)
         self.C_proj = Dense(di, N)
         self.dt_proj = Dense(di, di, bias=True, tp="col")
         if cfg.ssm_init == "mamba":
-            dt0 = torch.empty(dil).uniform_(1e-3, 0.1)
+            dt0 = torch.empty(di).uniform_(1e-3, 0.1)
+            dt_bias = dt0 + torch.log(-torch.expm1(-dt0))
+            if W > 1:
+                dt_bias = shard_tensor(dt_bias, 0, 1, W, rank)
             with torch.no_grad():
-                self.dt_proj.bias.copy_(dt0 + torch.log(-torch.expm1(-dt0)))
+                self.dt_proj.bias.copy_(dt_bias)
         self.ssm_out_norm = RMSNorm(di, tp=True)
         self.out_proj = Dense(di, d, tp="row")
 

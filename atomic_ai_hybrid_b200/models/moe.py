@@ -61,15 +61,17 @@ class MoE(nn.Module):
         if E % self.ep_world:
             raise ValueError(f"{E} routed experts do not split over {self.ep_world} expert-parallel ranks")
         El = E // self.ep_world
-        self.routed_w1 = nn.Parameter(torch.empty(El, d, F_))
-        self.routed_w2 = nn.Parameter(torch.empty(El, F_, d))
-        lecun_normal_(self.routed_w1.data, d)
-        lecun_normal_(self.routed_w2.data, F_)
-        if self.swiglu:
-            self.routed_w3 = nn.Parameter(torch.empty(El, d, F_))
-            lecun_normal_(self.routed_w3.data, d)
-        else:
-            self.routed_w3 = None
+        lo = self.ep_rank * El
+
+        def experts(rows: int, cols: int) -> nn.Parameter:
+            # every rank draws all E experts (same seed, same order) and keeps its block, so the
+            # initial model does not depend on the expert-parallel layout
+            full = lecun_normal_(torch.empty(E, rows, cols), rows)
+            return nn.Parameter(full[lo:lo + El].clone() if self.ep_world > 1 else full)
+
+        self.routed_w1 = experts(d, F_)
+        self.routed_w2 = experts(F_, d)
+        self.routed_w3 = experts(d, F_) if self.swiglu else None
         if self.ep_world > 1:
             for w in (self.routed_w1, self.routed_w2, self.routed_w3):
                 if w is not None:

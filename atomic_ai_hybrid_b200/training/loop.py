@@ -83,6 +83,11 @@ class TrainArgs:
     skip_nonfinite: bool = False
     seed: int = 0
     compute_dtype: str = "bf16"
+    # tensor parallelism (heads split over groups of this many ranks; the ranks of a group
+    # see the same batch) and expert parallelism (routed experts split over the same
+    # group, or over all ranks without tensor parallelism)
+    tensor_parallel: int = 1
+    expert_parallel: int = 1
 
 
 def _dist_setup():
@@ -117,17 +122,41 @@ def sanity_check_batch(batch: Dict[str, torch.Tensor], vocab: int) -> List[str]:
     return issues
 
 
+def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
+    """Install the tensor- / expert-parallel groups; returns the data-parallel (rank,
+    world) that the data loader shards over and the expert-parallel token capacity."""
+    tp, ep = max(1, args.tensor_parallel), max(1, args.expert_parallel)
+    if tp > 1:
+        if ep > 1 and ep != tp:
+            raise ValueError("with tensor parallelism, expert parallelism runs over the same group (ep == tp)")
+        from ..parallel.tp import init_tensor_parallel
+        dp_world = world // tp
+        rows = (args.global_batch // max(dp_world, 1)) * args.seq_len // tp
+        init_tensor_parallel(tp, dev, expert_parallel=ep > 1, max_rows=rows, max_width=cfg.d_model)
+        return rank // tp, dp_world, rows if ep > 1 else 0
+    if ep > 1:
+        if ep != world:
+            raise ValueError("without tensor parallelism, expert parallelism spans all ranks (ep == world)")
+        from ..parallel.context import ParallelContext, set_parallel_context
+        set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
+        return rank, world, args.global_batch // world * args.seq_len
+    return rank, world, 0
+
+
 def main_execution(args: TrainArgs) -> Dict:
     rank, world, dev = _dist_setup()
     ops.set_impl(args.impl if dev.type == "cuda" else "eager")
     cfg = load_yaml_config(args.config_yaml) if args.config_yaml else get_preset(args.preset, **args.overrides)
+    data_rank, data_world, ep_tokens = _parallel_setup(args, cfg, rank, world, dev)
+    # one seed on every rank: the model draws each full tensor and keeps this rank's pieces
+    # (tensor- and expert-parallel), so replicated weights start identical everywhere
     torch.manual_seed(args.seed)
     cdt = torch.bfloat16 if (args.compute_dtype == "bf16" and dev.type == "cuda") else torch.float32
     with torch.device(dev):
         model = HybridMoEModel(cfg, compute_dtype=cdt)
 
     # ---------------------------------------------------------------- data
-    per_rank = args.global_batch // world
+    per_rank = args.global_batch // data_world
     if args.data_dir and args.data_prefixes:
         pairs = []
         for i, pfx in enumerate(args.data_prefixes):
@@ -142,11 +171,13 @@ def main_execution(args: TrainArgs) -> Dict:
     steps_per_epoch = None
     if pairs is not None:
         _, _, micro_per_epoch, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
-                                                           mode=args.data_mode, rank=rank, world=world, pin=False)
+                                                           mode=args.data_mode, rank=data_rank, world=data_world,
+                                                           pin=False)
         steps_per_epoch = max(1, micro_per_epoch // args.accum_steps)
     total_steps = args.total_steps or (steps_per_epoch * args.epochs if steps_per_epoch else (args.max_steps or 1000))
     trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
-                      cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite)
+                      cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
+                      ep_max_tokens=ep_tokens)
 
     # ---------------------------------------------------------------- resume
     global_step, start_epoch = 0, 0
@@ -173,10 +204,12 @@ def main_execution(args: TrainArgs) -> Dict:
 
     def make_stream(skip):
         if pairs is None:
-            it = synthetic_batches(cfg.vocab_size, args.global_batch, args.seq_len, args.seed + skip, rank, world)
+            it = synthetic_batches(cfg.vocab_size, args.global_batch, args.seq_len, args.seed + skip, data_rank,
+                                   data_world)
             return it, None
         it, val_f, _, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
-                                                  skip_batches=skip, mode=args.data_mode, rank=rank, world=world)
+                                                  skip_batches=skip, mode=args.data_mode, rank=data_rank,
+                                                  world=data_world)
         return Prefetcher(it), val_f
 
     train_stream, val_factory = make_stream(global_step * args.accum_steps)

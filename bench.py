@@ -154,15 +154,20 @@ def main():
             raise SystemExit("--ep must equal the number of GPUs")
         from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
         set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
-    # distinct experts per expert-parallel rank (its index in the expert-parallel group)
-    torch.manual_seed(1234 + (rank % args.ep if args.ep > 1 else 0))
+    # the model draws every full tensor and keeps this rank's pieces: one seed for all ranks
+    torch.manual_seed(1234)
     with torch.device(dev):
         model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16)
-    # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0
+    # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0; replicated
+    # matrices draw the same values on every rank, tensor- / expert-parallel pieces their own
+    from atomic_ai_hybrid_b200.parallel.tp import shard_spec
+    g_rep = torch.Generator(device=dev).manual_seed(1234)
+    g_loc = torch.Generator(device=dev).manual_seed(1234 + 7919 * (rank + 1))
     with torch.no_grad():
         for n, p in model.named_parameters():
             if p.ndim >= 2 and "conv_w" not in n:
-                p.normal_(0.0, 0.02)
+                local = shard_spec(p) is not None or getattr(p, "_ahb_ep_local", False)
+                p.normal_(0.0, 0.02, generator=g_loc if local else g_rep)
     model = model.to(dev)
     nparams = count_params(model)
     use_graph = args.impl == "cuda" and not args.no_graph

@@ -53,12 +53,20 @@ def _parity(rank, world, port, kind, q):
         loss_f, grads_f = _loss_grads(full, ids)
 
         init_tensor_parallel(world, torch.device("cpu"))
+        torch.manual_seed(0)
         tpm = HybridMoEModel(cfg, compute_dtype=torch.float32)
-        load_full_state(tpm, full.state_dict())
+        # built from the same seed, the split model already holds the pieces of the full one
+        fsd = full.state_dict()
+        init_diff = 0.0
+        for n, p in tpm.named_parameters():
+            spec = shard_spec(p)
+            ref = shard_tensor(fsd[n], spec[0], spec[1], world, rank) if spec is not None else fsd[n]
+            init_diff = max(init_diff, float((p.detach() - ref).abs().max()))
+        load_full_state(tpm, fsd)
         loss_t, grads_t = _loss_grads(tpm, ids)
         lt = loss_t.clone()
         dist.all_reduce(lt)
-        errs = {"loss": float((lt / world - loss_f).abs() / loss_f.abs())}
+        errs = {"loss": float((lt / world - loss_f).abs() / loss_f.abs()), "init": init_diff}
         worst = 0.0
         for n, p in tpm.named_parameters():
             gt = grads_t[n]
@@ -95,6 +103,7 @@ def test_tp_forward_backward_matches_single_rank(kind, world):
         p.join(timeout=60)
         assert p.exitcode == 0
     for rank, errs in res:
+        assert errs["init"] == 0.0, (rank, errs)
         assert errs["loss"] < 1e-5, (rank, errs)
         # per-head decay gradients sum over every token and channel: fp32 reduction order
         assert errs["grad"] < 1e-3, (rank, errs)

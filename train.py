@@ -2,6 +2,8 @@
 
 Example (one GPU):   python train.py --preset hybrid_1b --seq-len 4096 --global-batch 32 --accum-steps 8
 Example (8 GPUs):    torchrun --standalone --nproc-per-node 8 train.py --preset hybrid_1b ...
+Long context:        torchrun --standalone --nproc-per-node 8 train.py --preset hybrid_long --tp 8 --ep 8 \
+                         --seq-len 32768 --global-batch 8 ...
 Data: ``--data-dir DIR --data-prefix NAME[:FRACTION] ...`` reads the reference's
 ``.npy`` token files; without data arguments the run uses synthetic tokens.
 """
@@ -42,6 +44,9 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-nonfinite", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (heads split, tokens split "
+                                                        "between the mixers)")
+    ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
     a = ap.parse_args(argv)
     over = {}
     for kv in a.set:
@@ -62,7 +67,7 @@ def parse(argv=None) -> TrainArgs:
                      eval_every=a.eval_every, log_every=a.log_every, checkpoint_every_s=a.checkpoint_every_s,
                      session_budget_s=a.session_budget_s, resume=not a.no_resume, resume_slot=a.resume_slot,
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
-                     skip_nonfinite=a.skip_nonfinite, seed=a.seed)
+                     skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep)
 
 
 if __name__ == "__main__":
