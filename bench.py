@@ -62,17 +62,43 @@ class ClockSampler:
         self.proc = None
         self.path = f"/tmp/ahb_clocks_{os.getpid()}.csv"
 
+    def _gpu_id(self) -> str:
+        """nvidia-smi's name for this process's GPU (its UUID when torch reports one, so that
+        a CUDA_VISIBLE_DEVICES remapping cannot point the sampler at another GPU)."""
+        try:
+            u = str(torch.cuda.get_device_properties(self.index).uuid)
+            if u:
+                return u if u.startswith("GPU-") else f"GPU-{u}"
+        except Exception:
+            pass
+        return str(self.index)
+
     def start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-        try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        for gid in dict.fromkeys([self._gpu_id(), str(self.index)]):
+            try:
+                self.f = open(self.path, "w")
+                self.proc = subprocess.Popen(["nvidia-smi", f"--id={gid}", f"--query-gpu={q}",
+                                              "--format=csv,noheader,nounits", "-lms", "200"],
+                                             stdout=self.f, stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
+                return
+            # do not start the timed region before the first sample is in (nvidia-smi can take
+            # seconds to come up on a busy host)
+            t0 = time.time()
+            while time.time() - t0 < 15.0 and self.proc.poll() is None:
+                try:
+                    if os.path.getsize(self.path) > 0:
+                        return
+                except OSError:
+                    pass
+                time.sleep(0.05)
+            if self.proc.poll() is None:
+                return  # still running: samples may yet come
+            self.f.close()  # this id was refused: try the next one
 
     def stop(self):
         if self.proc is None:
