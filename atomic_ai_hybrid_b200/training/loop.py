@@ -88,6 +88,7 @@ class TrainArgs:
     # group, or over all ranks without tensor parallelism)
     tensor_parallel: int = 1
     expert_parallel: int = 1
+    remat: bool = False            # recompute every layer in the backward (activation checkpointing)
 
 
 def _dist_setup():
@@ -153,7 +154,7 @@ def main_execution(args: TrainArgs) -> Dict:
     torch.manual_seed(args.seed)
     cdt = torch.bfloat16 if (args.compute_dtype == "bf16" and dev.type == "cuda") else torch.float32
     with torch.device(dev):
-        model = HybridMoEModel(cfg, compute_dtype=cdt)
+        model = HybridMoEModel(cfg, compute_dtype=cdt, remat=args.remat)
 
     # ---------------------------------------------------------------- data
     per_rank = args.global_batch // data_world

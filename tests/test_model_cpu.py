@@ -70,3 +70,26 @@ def test_training_reduces_loss():
     b = _batch(cfg, L=64)
     losses = [tr.train_step([b])["loss"].item() for _ in range(8)]
     assert losses[-1] < losses[0] - 0.5, losses
+
+
+def test_activation_checkpointing_matches():
+    """``remat=True`` recomputes every layer in the backward: same loss and gradients."""
+    from atomic_ai_hybrid_b200.training.loss import compute_loss
+    cfg = get_preset("tiny", num_layers=2, layer_types=("mamba2", "gdn2"), vocab_size=256, d_model=128,
+                     n_heads=2, n_heads_ssm=2, d_ff=128, n_routed_experts=4, d_state=32)
+    ids = torch.randint(0, cfg.vocab_size, (2, 65), generator=torch.Generator().manual_seed(3))
+    batch = {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
+    res = []
+    for remat in (False, True):
+        torch.manual_seed(0)
+        m = HybridMoEModel(cfg, compute_dtype=torch.float32, remat=remat)
+        loss, info = compute_loss(m, batch)
+        loss.backward()
+        res.append((loss.detach(), {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None},
+                    info["aux_loss"]))
+    (l0, g0, a0), (l1, g1, a1) = res
+    torch.testing.assert_close(l1, l0)
+    torch.testing.assert_close(a1, a0)
+    assert g0.keys() == g1.keys()
+    for n in g0:
+        torch.testing.assert_close(g1[n], g0[n], rtol=1e-5, atol=1e-7, msg=n)

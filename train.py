@@ -47,6 +47,7 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (heads split, tokens split "
                                                         "between the mixers)")
     ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
+    ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
     a = ap.parse_args(argv)
     over = {}
     for kv in a.set:
@@ -67,7 +68,8 @@ def parse(argv=None) -> TrainArgs:
                      eval_every=a.eval_every, log_every=a.log_every, checkpoint_every_s=a.checkpoint_every_s,
                      session_budget_s=a.session_budget_s, resume=not a.no_resume, resume_slot=a.resume_slot,
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
-                     skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep)
+                     skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
+                     remat=a.remat)
 
 
 if __name__ == "__main__":
