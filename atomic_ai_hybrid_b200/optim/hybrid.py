@@ -44,6 +44,23 @@ GLOBAL_CLIP = 0.35
 PARAM_CLIP = 1e2
 
 
+def _muon_direction(s, g: torch.Tensor, ns) -> torch.Tensor:
+    """Newton-Schulz orthogonalisation of a Muon matrix's update.  A tensor-parallel piece
+    is orthogonalised as part of its whole matrix: the pieces are all-gathered over the
+    tensor-parallel group, every rank runs the iteration on the full matrix and keeps its
+    piece (the same direction as without tensor parallelism)."""
+    from ..parallel.tp import get_tp, shard_spec, shard_tensor, unshard_tensors
+    spec = shard_spec(s.param)
+    tp = get_tp()
+    if spec is None or tp is None:
+        return ns(g)
+    import torch.distributed as dist
+    parts = [torch.empty_like(g) for _ in range(tp.world)]
+    dist.all_gather(parts, g.contiguous(), group=tp.group)
+    full = ns(unshard_tensors(parts, spec[0], spec[1]))
+    return shard_tensor(full, spec[0], spec[1], tp.world, tp.rank)
+
+
 class HybridOptimizer:
     def __init__(self, store: FlatParamStore, total_steps: int,
                  reduce_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
@@ -146,11 +163,12 @@ class HybridOptimizer:
         # Muon directions first (matrix-wise), written over the gradient buffer
         if use_k:
             from ..ops import kernels as K
+        ns = K.newton_schulz3 if use_k else R.newton_schulz3
         for s in self.owned:
             if s.label == "muon" and s.param.requires_grad:
                 sl = self._sl(s)
                 g = (gbuf[sl] * coef).view(s.shape)
-                gbuf[sl] = R.newton_schulz3(g).reshape(-1) if not use_k else K.newton_schulz3(g).reshape(-1)
+                gbuf[sl] = _muon_direction(s, g, ns).reshape(-1)
         if use_k:
             K.optim_apply(self, lrs, coef, assignment_frac)  # also writes the compute copy
         else:

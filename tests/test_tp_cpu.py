@@ -109,7 +109,7 @@ def test_tp_forward_backward_matches_single_rank(kind, world):
         assert errs["grad"] < 1e-3, (rank, errs)
 
 
-def _train(rank, world, port, steps, q):
+def _train(rank, world, port, steps, q, optimizer="adamw"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -127,7 +127,7 @@ def _train(rank, world, port, steps, q):
             load_full_state(m, full.state_dict())
         else:
             m = full
-        tr = Trainer(m, total_steps=50, optimizer="adamw", compute_dtype=torch.float32, device=torch.device("cpu"))
+        tr = Trainer(m, total_steps=50, optimizer=optimizer, compute_dtype=torch.float32, device=torch.device("cpu"))
         tr.opt.schedule.warmup = 1
         g = torch.Generator().manual_seed(9)
         ids = torch.randint(0, cfg.vocab_size, (2, 129), generator=g)
@@ -156,19 +156,21 @@ def _train(rank, world, port, steps, q):
             dist.destroy_process_group()
 
 
-def test_tp2_training_follows_single_rank():
+@pytest.mark.parametrize("optimizer", ["adamw", "hybrid"])
+def test_tp2_training_follows_single_rank(optimizer):
     """Losses and global gradient norms per step match; every parameter (split
     pieces included) moves, and by the same amount up to Adam's sign sensitivity on
-    near-zero gradients (bounded by the learning rate)."""
+    near-zero gradients (bounded by the learning rate).  With the hybrid optimizer the
+    Muon matrices split over the ranks are orthogonalised whole."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     steps = 3
-    p1 = ctx.Process(target=_train, args=(0, 1, _port(), steps, q))
+    p1 = ctx.Process(target=_train, args=(0, 1, _port(), steps, q, optimizer))
     p1.start()
     ref_hist, ref = q.get(timeout=300)
     p1.join(timeout=60)
     port = _port()
-    procs = [ctx.Process(target=_train, args=(r, 2, port, steps, q)) for r in range(2)]
+    procs = [ctx.Process(target=_train, args=(r, 2, port, steps, q, optimizer)) for r in range(2)]
     for p in procs:
         p.start()
     hist, got = q.get(timeout=300)
