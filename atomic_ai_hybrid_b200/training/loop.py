@@ -89,6 +89,7 @@ class TrainArgs:
     tensor_parallel: int = 1
     expert_parallel: int = 1
     remat: bool = False            # recompute every layer in the backward (activation checkpointing)
+    reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
 
 
 def _dist_setup():
@@ -202,6 +203,9 @@ def main_execution(args: TrainArgs) -> Dict:
             if rank == 0:
                 print(f"[RESUME] {slot}/{step}: step={global_step} restored={len(meta['restored'])} "
                       f"fresh={len(meta['fresh'])}", flush=True)
+            if args.reset_router:
+                from .router_reset import reset_router
+                reset_router(trainer, seed=args.seed + 1234, verbose=rank == 0)
 
     def make_stream(skip):
         if pairs is None:

@@ -101,3 +101,37 @@ def test_training_loop_with_tensor_parallelism(tmp_path):
     assert steps, os.listdir(root)
     keys = load_file(os.path.join(root, max(steps, key=int), "params-rank1.safetensors")).keys()
     assert any("#tp[1/2," in k for k in keys), sorted(keys)[:10]
+
+
+def test_router_reset_touches_only_router_leaves():
+    import torch
+    from atomic_ai_hybrid_b200 import get_preset
+    from atomic_ai_hybrid_b200.models import HybridMoEModel
+    from atomic_ai_hybrid_b200.training.router_reset import reset_router
+    from atomic_ai_hybrid_b200.training.trainer import Trainer
+    cfg = get_preset("tiny", **PRESET_OVER)
+    torch.manual_seed(0)
+    m = HybridMoEModel(cfg, compute_dtype=torch.float32)
+    tr = Trainer(m, total_steps=10, optimizer="adamw", compute_dtype=torch.float32, device=torch.device("cpu"))
+    ids = torch.randint(0, cfg.vocab_size, (2, 65))
+    tr.train_step([{"input_ids": ids[:, :-1], "labels": ids[:, 1:]}])
+    before = {n: p.detach().clone() for n, p in m.named_parameters()}
+    m_before, v_before = tr.opt.m.clone(), tr.opt.v.clone()
+    changed = reset_router(tr, verbose=False)
+    assert sorted(changed) == sorted(n for n in before if n.endswith(".router") or n.endswith("router_temp"))
+    for n, p in m.named_parameters():
+        if n in changed:
+            if n.endswith("router_temp"):
+                assert float(p) == 10.0
+            else:
+                assert not torch.equal(p, before[n]) and abs(float(p.std()) - 0.02) < 0.01
+        else:
+            assert torch.equal(p, before[n]), n
+    st = tr.store
+    for s in st.segs:
+        o = s.offset - st.lo
+        sl = slice(o, o + s.numel)
+        if s.name in changed:
+            assert not tr.opt.m[sl].any() and not tr.opt.v[sl].any()
+        else:
+            assert torch.equal(tr.opt.m[sl], m_before[sl]) and torch.equal(tr.opt.v[sl], v_before[sl])

@@ -48,6 +48,7 @@ def parse(argv=None) -> TrainArgs:
                                                         "between the mixers)")
     ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
+    ap.add_argument("--reset-router", action="store_true", help="re-draw the routers after a restore")
     a = ap.parse_args(argv)
     over = {}
     for kv in a.set:
@@ -69,7 +70,7 @@ def parse(argv=None) -> TrainArgs:
                      session_budget_s=a.session_budget_s, resume=not a.no_resume, resume_slot=a.resume_slot,
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
                      skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
-                     remat=a.remat)
+                     remat=a.remat, reset_router=a.reset_router)
 
 
 if __name__ == "__main__":
