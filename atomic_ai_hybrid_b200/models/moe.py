@@ -174,13 +174,20 @@ class MoE(nn.Module):
         top_idx, gate = self.route(flat, stats)
         shared = self._shared(flat) if self.n_shared > 0 else None
         if self.ep_world > 1:
-            ep = get_parallel_context().ep
-            if ep is None:
-                raise RuntimeError("expert-parallel MoE needs the EPGroup (parallel.ep) in the parallel context")
-            from ..parallel.ep import moe_forward_ep
-            out = moe_forward_ep(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3, shared,
-                                 "swiglu" if self.swiglu else "gelu", ep)
-            return out.view(Bsz, L, d)
+            pc = get_parallel_context()
+            act = "swiglu" if self.swiglu else "gelu"
+            if pc.ep is not None and ops.use_cuda(flat):
+                from ..parallel.ep import moe_forward_ep
+                out = moe_forward_ep(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3, shared,
+                                     act, pc.ep)
+                return out.view(Bsz, L, d)
+            # no peer buffers (CPU, or the NCCL baseline): all-to-all through torch.distributed
+            from ..parallel.ep import moe_forward_ep_collective
+            out = moe_forward_ep_collective(flat, top_idx, gate, self.routed_w1, self.routed_w2, self.routed_w3,
+                                            act, pc.ep_group, self.ep_world, self.ep_rank, self.E)
+            if shared is not None:
+                out = out + shared.float()
+            return R.sanitize(out, 1e3).view(Bsz, L, d).to(x.dtype)
         # the grouped GEMM tiles need d_model and d_ff in multiples of 256
         if ops.use_cuda(flat) and x.dtype == torch.bfloat16 and d % 256 == 0 and self.cfg.d_ff % 256 == 0:
             from ..ops import kernels as K

@@ -208,3 +208,44 @@ class _MoEEP(torch.autograd.Function):
 def moe_forward_ep(x, top_idx, gate, w1, w2, w3, shared, act: str, ep: EPGroup):
     """``x (T, d)``; ``w*`` hold this rank's ``El`` experts."""
     return _MoEEP.apply(x, top_idx, gate, w1, w2, w3, shared, act == "swiglu", ep)
+
+
+# ------------------------------------------------------------ collective (NCCL / gloo) path
+def moe_forward_ep_collective(x, top_idx, gate, w1, w2, w3, act: str, group, world: int, rank: int,
+                              n_experts: int):
+    """Expert parallelism with ``torch.distributed`` all-to-all (NCCL on GPUs, gloo on the
+    CPU): the baseline of the peer-memory path above and the path without peer buffers.
+
+    Every token choice ``(t, j)`` travels to the rank of expert ``top_idx[t, j]`` (rows
+    grouped by destination, then by expert), the experts run there on the rows grouped by
+    expert, and the outputs travel back in the order they came; the combine
+    ``sum_j gate[t, j] * y[t, j]`` happens on the token's rank.  Differentiable (the
+    all-to-all's backward is the reverse all-to-all).  Returns the fp32 routed output
+    ``(T, d)`` before the shared expert and the final sanitize."""
+    import torch.distributed.nn.functional as dfn
+    from .. import ops
+    from ..ops import reference as R
+    T, k = top_idx.shape
+    El = n_experts // world
+    eidx = top_idx.reshape(-1)                                   # assignment a = t * k + j
+    order = torch.argsort(eidx, stable=True)                     # by expert = by destination, then expert
+    counts = torch.bincount(eidx, minlength=n_experts)           # (E,) rows this rank sends per expert
+    allc = [torch.zeros_like(counts) for _ in range(world)]
+    dist.all_gather(allc, counts, group=group)
+    table = torch.stack(allc).cpu()                              # (W, E): rows from source s for expert e
+    send = table[rank].view(world, El).sum(1).tolist()           # rows to each destination rank
+    recv = table[:, rank * El:(rank + 1) * El].sum(1).tolist()   # rows from each source rank
+    rows = x[order // k]
+    got = dfn.all_to_all_single(rows.new_empty((sum(recv), x.shape[1])), rows, recv, send, group=group)
+    # received rows: source-major, expert-major inside a source -> regroup by local expert
+    src_e = torch.cat([torch.arange(El).repeat_interleave(table[s, rank * El:(rank + 1) * El])
+                       for s in range(world)]) if sum(recv) else torch.zeros(0, dtype=torch.long)
+    regroup = torch.argsort(src_e.to(x.device), stable=True)
+    sizes = table[:, rank * El:(rank + 1) * El].sum(0).tolist()
+    ys = ops.grouped_ffn(got[regroup], torch.tensor(sizes), w1, w2, w3, act, group_sizes_cpu=sizes)
+    ys = R.sanitize(ys.float(), 1e3)
+    back = torch.empty_like(ys)
+    back = back.index_copy(0, regroup, ys)                       # undo the regrouping (differentiable)
+    out_rows = dfn.all_to_all_single(back.new_empty((T * k, back.shape[1])), back, send, recv, group=group)
+    y = torch.empty_like(out_rows).index_copy(0, order, out_rows)  # assignment order t * k + j
+    return (y.view(T, k, -1) * gate.float().unsqueeze(-1)).sum(1)

@@ -17,6 +17,7 @@ iterations are discarded by zeroing the gradients before the real micro-steps).
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, List, Optional
 
 import torch
@@ -79,7 +80,10 @@ class Trainer:
                 # the head-split layers run eager (per-call peer barriers carry host epochs)
                 cuda_graph = False
             if pc.ep_world > 1:
-                if pc.ep is None:
+                # peer buffers on CUDA (AHB_EP_COMM=nccl keeps the all-to-all baseline); on the
+                # CPU the MoE uses the torch.distributed all-to-all path
+                peer = self.store.device.type == "cuda" and os.environ.get("AHB_EP_COMM", "peer") != "nccl"
+                if pc.ep is None and peer:
                     if ep_max_tokens <= 0:
                         raise ValueError("expert parallelism needs ep_max_tokens (tokens per micro-batch)")
                     from ..parallel.ep import EPGroup

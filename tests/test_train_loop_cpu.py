@@ -75,24 +75,26 @@ def test_failing_rank_ends_peers_with_error(tmp_path):
         mp.spawn(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
 
 
-def _tp_rank_main(rank, world, port, tmp):
+def _tp_rank_main(rank, world, port, tmp, ep=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
     _write_data(tmp)
-    out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], tensor_parallel=2, max_steps=2,
-                               checkpoint_every_s=0.0))
+    out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], tensor_parallel=2, expert_parallel=ep,
+                               max_steps=2, checkpoint_every_s=0.0))
     with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
         json.dump({k: v for k, v in out.items() if k != "losses"}, f)
 
 
-def test_training_loop_with_tensor_parallelism(tmp_path):
-    """train.py's loop with --tp 2 on two gloo ranks: both ranks train on the same batches
-    (one data-parallel replica) and the checkpoint holds the tensor-parallel pieces."""
+@pytest.mark.parametrize("ep", [1, 2])
+def test_training_loop_with_tensor_parallelism(tmp_path, ep):
+    """train.py's loop with --tp 2 (and --ep 2: experts split over the same ranks) on two
+    gloo ranks: both ranks train on the same batches (one data-parallel replica) and the
+    checkpoint holds the tensor-parallel pieces."""
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    mp.spawn(_tp_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_tp_rank_main, args=(2, port, str(tmp_path), ep), nprocs=2, join=True)
     outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(2)]
     assert outs[0]["global_step"] == 2 and outs[1]["global_step"] == 2, outs
     from atomic_ai_hybrid_b200.ckpt.safetensors_io import load_file
@@ -135,3 +137,30 @@ def test_router_reset_touches_only_router_leaves():
             assert not tr.opt.m[sl].any() and not tr.opt.v[sl].any()
         else:
             assert torch.equal(tr.opt.m[sl], m_before[sl]) and torch.equal(tr.opt.v[sl], v_before[sl])
+
+
+def _ep_rank_main(rank, world, port, tmp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
+    _write_data(tmp)
+    out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], expert_parallel=2, max_steps=2,
+                               checkpoint_every_s=0.0))
+    with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
+        json.dump({k: v for k, v in out.items() if k != "losses"}, f)
+
+
+def test_training_loop_with_expert_parallelism(tmp_path):
+    """train.py's loop with --ep 2 on two gloo ranks (all-to-all path): it trains and the
+    checkpoint holds each rank's block of experts."""
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_ep_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(2)]
+    assert outs[0]["global_step"] == 2 and outs[1]["global_step"] == 2, outs
+    from atomic_ai_hybrid_b200.ckpt.safetensors_io import load_file
+    root = os.path.join(tmp_path, "latest")
+    step = max((d for d in os.listdir(root) if d.isdigit()), key=int)
+    keys = load_file(os.path.join(root, step, "params-rank1.safetensors")).keys()
+    assert any("routed_w1#experts[2:4]" in k for k in keys), sorted(keys)[:10]
