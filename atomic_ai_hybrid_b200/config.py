@@ -125,12 +125,27 @@ def _pattern_3to1(n: int) -> Tuple[str, ...]:
 # Reference defaults, exactly `ModelConfig()` of the reference.
 REFERENCE_DEFAULT = ModelConfig()
 
-# The configuration the reference's train.py trains (reference `train.py:405-436`):
-# d_model 768, 6 heads, 21 layers, vocab 151936 with tied embeddings.
+# The configuration the reference's train.py trains (reference `train.py:405-436`, the same
+# in `traivn.py:303-334`): d_model 768, 6 heads, d_latent 768, 24 layers in blocks of 3 with
+# MLA every third layer of blocks 0, 2, 4, 6, vocab 128256 with tied embeddings, aux 0.03,
+# z 3e-4, no label smoothing, router noise 0.1; fields it does not set keep the ModelConfig
+# defaults (n_heads_ssm 8, dropout 0.1, ...).
+REFERENCE_TRAIN_LAYER_TYPES: Tuple[str, ...] = (
+    "gdn2", "gdn2", "mla",
+    "gdn2", "mamba2", "gdn2",
+    "gdn2", "gdn2", "mla",
+    "gdn2", "mamba2", "gdn2",
+    "gdn2", "gdn2", "mla",
+    "gdn2", "mamba2", "gdn2",
+    "gdn2", "gdn2", "mla",
+    "gdn2", "gdn2", "gdn2",
+)
 REFERENCE_TRAIN = ModelConfig(
-    d_model=768, d_state=128, d_conv=4, expand=2, n_heads=6, n_heads_ssm=8,
-    d_latent=384, d_ff=4096, num_experts=8, top_k=2, num_layers=21,
-    layers_per_block=3, vocab_size=151936, deltanet_chunk_size=256,
+    d_model=768, d_state=128, d_conv=4, expand=2, n_heads=6, d_latent=768, d_ff=4096,
+    num_experts=8, top_k=2, moe_capacity_factor=1.25, router_aux_loss_coef=0.03,
+    router_z_loss_coef=0.0003, num_layers=24, layers_per_block=3, vocab_size=128256,
+    tie_embeddings=True, label_smoothing=0.0, router_noise_std=0.1, use_flash_attention=True,
+    deltanet_chunk_size=256, layer_types=REFERENCE_TRAIN_LAYER_TYPES,
 )
 
 # Config 1 of the benchmark spec: tiny CPU model, fp32 parity.
@@ -207,6 +222,7 @@ def load_yaml_config(path: str) -> ModelConfig:
 
     with open(path) as f:
         data = yaml.safe_load(f) or {}
+    data.pop("train", None)  # the run settings of a configuration file (train.py)
     if "preset" in data:
         over = dict(data.get("overrides") or {})
     else:

@@ -93,3 +93,15 @@ def test_activation_checkpointing_matches():
     assert g0.keys() == g1.keys()
     for n in g0:
         torch.testing.assert_close(g1[n], g0[n], rtol=1e-5, atol=1e-7, msg=n)
+
+
+def test_reference_preset_is_the_reference_training_config():
+    """``reference`` = the ModelConfig the reference's train.py builds (`train.py:405-436`)."""
+    c = get_preset("reference")
+    assert (c.d_model, c.n_heads, c.d_latent, c.d_ff, c.num_experts, c.top_k) == (768, 6, 768, 4096, 8, 2)
+    assert (c.num_layers, c.layers_per_block, c.vocab_size) == (24, 3, 128256)
+    assert (c.router_aux_loss_coef, c.router_z_loss_coef, c.label_smoothing, c.router_noise_std) == \
+        (0.03, 0.0003, 0.0, 0.1)
+    assert c.deltanet_chunk_size == 256 and c.tie_embeddings and c.arch == "blockdar"
+    assert c.layer_types[:6] == ("gdn2", "gdn2", "mla", "gdn2", "mamba2", "gdn2")
+    assert c.layer_types[-3:] == ("gdn2", "gdn2", "gdn2") and c.layer_types.count("mla") == 4

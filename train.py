@@ -20,7 +20,8 @@ from atomic_ai_hybrid_b200.training.loop import TrainArgs, main_execution  # noq
 def parse(argv=None) -> TrainArgs:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--preset", default="tiny")
-    ap.add_argument("--config", dest="config_yaml", default=None, help="YAML {preset:, overrides:}")
+    ap.add_argument("--config", dest="config_yaml", default=None,
+                    help="YAML {preset:, overrides:, train:} (atomic_ai_hybrid_b200/configs/)")
     ap.add_argument("--set", action="append", default=[], help="config override key=value (repeatable)")
     ap.add_argument("--ckpt-root", default="checkpoints")
     ap.add_argument("--data-dir", default=None)
@@ -73,7 +74,27 @@ def parse(argv=None) -> TrainArgs:
                      remat=a.remat, reset_router=a.reset_router)
 
 
+def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
+    """A ``--config`` YAML may carry a ``train:`` section (TrainArgs field names); its values
+    apply where the command line left the default."""
+    if not args.config_yaml:
+        return args
+    import dataclasses
+    import yaml
+    with open(args.config_yaml) as f:
+        data = yaml.safe_load(f) or {}
+    train = data.get("train") or {}
+    defaults = parse([])
+    names = {f.name for f in dataclasses.fields(TrainArgs)}
+    for k, v in train.items():
+        if k not in names:
+            raise ValueError(f"{args.config_yaml}: unknown train field {k!r}")
+        if getattr(args, k) == getattr(defaults, k):
+            setattr(args, k, v)
+    return args
+
+
 if __name__ == "__main__":
-    out = main_execution(parse())
+    out = main_execution(apply_yaml_train_section(parse()))
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps({k: v for k, v in out.items() if k != "losses"}))
