@@ -28,6 +28,7 @@ import torch.nn as nn
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
+from ..parallel.cp import get_cp
 from ..parallel.tp import get_tp
 from ..utils.diag import DIAG
 from ..utils.nvtx import nvtx_range
@@ -269,6 +270,11 @@ class HybridMoEModel(nn.Module):
             # sequence parallel: this rank embeds (and later scores) its block of the tokens
             tp.set_batch(Bsz, L)
             input_ids = tp.local_tokens(input_ids)
+        cp = get_cp()
+        if cp is not None:
+            # context parallel: this rank holds one segment of every sequence
+            cp.set_seq(L)
+            input_ids = cp.local_time(input_ids)
         x = self.embed(input_ids, self.compute_dtype)
         cos, sin = self.rope(L, x.device) if self.has_mla() else (None, None)
         stats: List[Dict] = []
@@ -323,7 +329,10 @@ class HybridMoEModel(nn.Module):
         """The rows of a per-token ``(B, L, ...)`` tensor (labels) that this rank
         scores: its sequence-parallel block under tensor parallelism, else all."""
         tp = get_tp()
-        return tp.local_tokens(t) if tp is not None else t
+        if tp is not None:
+            return tp.local_tokens(t)
+        cp = get_cp()
+        return cp.local_time(t) if cp is not None else t
 
     def lm_weight(self) -> torch.Tensor:
         """``(V, d)`` weight of the tied (or separate) LM head."""

@@ -16,6 +16,7 @@ import torch.nn.functional as F
 from .. import ops
 from ..config import ModelConfig
 from ..ops import reference as R
+from ..parallel.cp import get_cp
 from ..parallel.tp import get_tp, mark_shard, shard_tensor, tp_rmsnorm
 from ..utils.diag import DIAG
 from .layers import Dense, RMSNorm, lecun_normal_, tp_world_rank
@@ -89,14 +90,16 @@ class GatedDeltaNet2(nn.Module):
         return self.out_proj(o)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if ops.use_cuda(x):
+        cp = get_cp()
+        if ops.use_cuda(x) and cp is None:
             return self._forward_fused(x)
         H, D = self.n_heads, self.d_head
         qp, kp, vp, bp, wp, fp, og = self.projections(x)
         Bsz, L, dl = qp.shape
-        q = ops.conv1d(qp, self.q_conv_w, self.q_conv_b, silu=True)
-        k = ops.conv1d(kp, self.k_conv_w, self.k_conv_b, silu=True)
-        v = ops.conv1d(vp, self.v_conv_w, self.v_conv_b, silu=True, clip=50.0)
+        conv = ops.conv1d if cp is None else (lambda t, w_, b_, **kw: cp.causal_conv(ops.conv1d, t, w_, b_, **kw))
+        q = conv(qp, self.q_conv_w, self.q_conv_b, silu=True)
+        k = conv(kp, self.k_conv_w, self.k_conv_b, silu=True)
+        v = conv(vp, self.v_conv_w, self.v_conv_b, silu=True, clip=50.0)
         q = q.view(Bsz, L, H, D)
         k = k.view(Bsz, L, H, D)
         v = v.view(Bsz, L, H, D)
@@ -112,7 +115,10 @@ class GatedDeltaNet2(nn.Module):
         g = R.sanitize(g, 1e3)
         for name, t in (("q", q), ("k", k), ("v", v), ("g", g)):
             DIAG.stage("GDN2", name, t)
-        o = ops.gdn2(q, k, v, w_gate, b_gate, g, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, dl)
+        if cp is not None:
+            o = cp.gdn2_scan(q, k, v, g, b_gate, w_gate, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, dl)
+        else:
+            o = ops.gdn2(q, k, v, w_gate, b_gate, g, 1.0, self.cfg.gdn_chunk).reshape(Bsz, L, dl)
         DIAG.stage("GDN2", "o", o)
         tp = get_tp()
         if tp is not None:
@@ -183,7 +189,8 @@ class Mamba2(nn.Module):
         return self.out_proj(out)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if ops.use_cuda(x):
+        cp = get_cp()
+        if ops.use_cuda(x) and cp is None:
             from ..ops import kernels as K
             return K.mamba2_layer(self, x)
         Hs = self.n_heads
@@ -192,7 +199,10 @@ class Mamba2(nn.Module):
         dil = two_dil // 2
         P = dil // Hs
         x_bc, res = xz[..., :dil], xz[..., dil:]
-        x_conv = ops.conv1d(x_bc, self.conv_w, self.conv_b, silu=True)
+        if cp is not None:
+            x_conv = cp.causal_conv(ops.conv1d, x_bc, self.conv_w, self.conv_b, silu=True)
+        else:
+            x_conv = ops.conv1d(x_bc, self.conv_w, self.conv_b, silu=True)
         A = -torch.exp(self.A_log.float().clamp(-20.0, 20.0))
         xin = self.bc_input(x_bc)
         Bm = self.B_proj(xin)
@@ -201,7 +211,10 @@ class Mamba2(nn.Module):
         dt, Bm, Cm, x_conv = (R.sanitize(t, 1e3) for t in (dt, Bm, Cm, x_conv))
         for name, t in (("in_proj", xz), ("x_conv", x_conv), ("dt", dt)):
             DIAG.stage("MAMBA2", name, t)
-        y = ops.ssd(dt.view(Bsz, L, Hs, P), A, Bm, Cm, x_conv.view(Bsz, L, Hs, P), self.cfg.ssd_chunk)
+        if cp is not None:
+            y = cp.ssd_scan(dt.view(Bsz, L, Hs, P), A, Bm, Cm, x_conv.view(Bsz, L, Hs, P), self.cfg.ssd_chunk)
+        else:
+            y = ops.ssd(dt.view(Bsz, L, Hs, P), A, Bm, Cm, x_conv.view(Bsz, L, Hs, P), self.cfg.ssd_chunk)
         DIAG.stage("MAMBA2", "ssd_y", y)
         y = y.reshape(Bsz, L, dil).to(x_bc.dtype)
         tp = get_tp()
@@ -245,13 +258,22 @@ class MLA(nn.Module):
         else:
             Qp, lat = self.W_q(x), self.W_kv_down(x)
         Bsz, L, dl = Qp.shape
+        cp = get_cp()
+        q0, Lk = 0, L
+        if cp is not None:  # keys / values of the whole sequence from the gathered latent
+            lat = cp.gather_time(lat)
+            q0, Lk = cp.seg[0], lat.shape[1]
         Q = Qp.view(Bsz, L, H, dh).transpose(1, 2)
-        K = self.W_k_up(lat).view(Bsz, L, H, dh).transpose(1, 2)
-        V = self.W_v_up(lat).view(Bsz, L, H, dh).transpose(1, 2)
-        Q = R.apply_rope(Q, cos[:L, :dh], sin[:L, :dh])
-        K = R.apply_rope(K, cos[:L, :dh], sin[:L, :dh])
+        K = self.W_k_up(lat).view(Bsz, Lk, H, dh).transpose(1, 2)
+        V = self.W_v_up(lat).view(Bsz, Lk, H, dh).transpose(1, 2)
+        Q = R.apply_rope(Q, cos[q0:q0 + L, :dh], sin[q0:q0 + L, :dh])
+        K = R.apply_rope(K, cos[:Lk, :dh], sin[:Lk, :dh])
         Q, K, V = (R.sanitize(t, 1e3) for t in (Q, K, V))
-        out = ops.attention(Q.contiguous(), K.contiguous(), V.contiguous(), 1.0 / math.sqrt(dh))
+        if cp is not None:
+            keep = torch.arange(Lk, device=Q.device)[None, :] <= (q0 + torch.arange(L, device=Q.device))[:, None]
+            out = F.scaled_dot_product_attention(Q, K, V, attn_mask=keep, scale=1.0 / math.sqrt(dh))
+        else:
+            out = ops.attention(Q.contiguous(), K.contiguous(), V.contiguous(), 1.0 / math.sqrt(dh))
         out = out.transpose(1, 2).reshape(Bsz, L, dl)
         if tp is not None:
             out = tp_rmsnorm(out, self.attn_out_norm.scale, 1e-6, self.cfg.d_model, tp).to(out.dtype)

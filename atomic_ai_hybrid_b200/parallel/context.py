@@ -36,6 +36,7 @@ class ParallelContext:
     ep: Optional[object] = None  # the EPGroup (peer buffers) once built
     tp_rank: int = 0
     tp: Optional[object] = None  # the TPGroup (token layout, collectives)
+    cp: Optional[object] = None  # the CPGroup (sequence segments; parallel.cp)
     # ranks that hold the same rank-local parameters (data-parallel replicas of a
     # tensor- or expert-parallel group); None when every such piece has one owner
     local_group: Optional[dist.ProcessGroup] = None

@@ -89,6 +89,7 @@ class TrainArgs:
     tensor_parallel: int = 1
     expert_parallel: int = 1
     remat: bool = False            # recompute every layer in the backward (activation checkpointing)
+    context_parallel: int = 1      # sequence segments over all ranks (parallel.cp); every rank reads the same batch
     reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
 
 
@@ -128,6 +129,12 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
     """Install the tensor- / expert-parallel groups; returns the data-parallel (rank,
     world) that the data loader shards over and the expert-parallel token capacity."""
     tp, ep = max(1, args.tensor_parallel), max(1, args.expert_parallel)
+    if args.context_parallel > 1:
+        if args.context_parallel != world or tp > 1 or ep > 1:
+            raise ValueError("context parallelism spans all ranks and does not combine with --tp / --ep")
+        from ..parallel.cp import init_context_parallel
+        init_context_parallel(dev)
+        return 0, 1, 0
     if tp > 1:
         if ep > 1 and ep != tp:
             raise ValueError("with tensor parallelism, expert parallelism runs over the same group (ep == tp)")

@@ -23,9 +23,9 @@ def _args(tmp, **kw):
     return a
 
 
-def _write_data(d):
+def _write_data(d, cols=65):
     rng = np.random.RandomState(0)
-    ids = rng.randint(0, 512, size=(64, 65)).astype(np.int32)
+    ids = rng.randint(0, 512, size=(64, cols)).astype(np.int32)
     np.save(os.path.join(d, "src_input_ids.npy"), ids[:, :-1])
     np.save(os.path.join(d, "src_labels.npy"), ids[:, 1:])
 
@@ -164,3 +164,25 @@ def test_training_loop_with_expert_parallelism(tmp_path):
     step = max((d for d in os.listdir(root) if d.isdigit()), key=int)
     keys = load_file(os.path.join(root, step, "params-rank1.safetensors")).keys()
     assert any("routed_w1#experts[2:4]" in k for k in keys), sorted(keys)[:10]
+
+
+def _cp_rank_main(rank, world, port, tmp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
+    _write_data(tmp, cols=129)  # segments of 64 tokens: one scan chunk per rank
+    out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], context_parallel=2, max_steps=2,
+                               seq_len=128))
+    with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
+        json.dump({k: v for k, v in out.items() if k != "losses"}, f)
+
+
+def test_training_loop_with_context_parallelism(tmp_path):
+    """train.py's loop with --cp 2: both ranks read the same batches and hold one half of
+    every sequence."""
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_cp_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(2)]
+    assert outs[0]["global_step"] == 2 and outs[1]["global_step"] == 2, outs
