@@ -39,7 +39,7 @@ def _worker(rank, world, port, kind, q):
         set_parallel_context(ParallelContext())
         torch.manual_seed(0)
         full = HybridMoEModel(cfg, compute_dtype=torch.float32)
-        ids = torch.randint(0, cfg.vocab_size, (2, 64 * 2 * world + 1), generator=torch.Generator().manual_seed(7))
+        ids = torch.randint(0, cfg.vocab_size, (2, 64 * world + 1), generator=torch.Generator().manual_seed(7))
         batch = {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
         lf, _ = compute_loss(full, batch)
         lf.backward()
