@@ -91,6 +91,7 @@ class TrainArgs:
     remat: bool = False            # recompute every layer in the backward (activation checkpointing)
     context_parallel: int = 1      # sequence segments over all ranks (parallel.cp); every rank reads the same batch
     reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
+    pipeline_parallel: int = 1     # contiguous layer stages over all ranks (parallel.pp); every rank reads the same batch
 
 
 def _dist_setup():
@@ -129,6 +130,12 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
     """Install the tensor- / expert-parallel groups; returns the data-parallel (rank,
     world) that the data loader shards over and the expert-parallel token capacity."""
     tp, ep = max(1, args.tensor_parallel), max(1, args.expert_parallel)
+    if args.pipeline_parallel > 1:
+        if args.pipeline_parallel != world or tp > 1 or ep > 1 or args.context_parallel > 1:
+            raise ValueError("pipeline parallelism spans all ranks and does not combine with --tp / --ep / --cp")
+        from ..parallel.context import ParallelContext, set_parallel_context
+        set_parallel_context(ParallelContext())
+        return 0, 1, 0
     if args.context_parallel > 1:
         if args.context_parallel != world or tp > 1 or ep > 1:
             raise ValueError("context parallelism spans all ranks and does not combine with --tp / --ep")
@@ -184,9 +191,14 @@ def main_execution(args: TrainArgs) -> Dict:
                                                            pin=False)
         steps_per_epoch = max(1, micro_per_epoch // args.accum_steps)
     total_steps = args.total_steps or (steps_per_epoch * args.epochs if steps_per_epoch else (args.max_steps or 1000))
-    trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
-                      cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
-                      ep_max_tokens=ep_tokens)
+    if args.pipeline_parallel > 1:
+        from ..parallel.pp import PipelineTrainer
+        trainer = PipelineTrainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt,
+                                  device=dev, skip_nonfinite=args.skip_nonfinite)
+    else:
+        trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
+                          cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
+                          ep_max_tokens=ep_tokens)
 
     # ---------------------------------------------------------------- resume
     global_step, start_epoch = 0, 0

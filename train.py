@@ -50,6 +50,7 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
     ap.add_argument("--cp", type=int, default=1, help="context parallelism over all ranks (sequence segments)")
+    ap.add_argument("--pp", type=int, default=1, help="pipeline parallelism over all ranks (layer stages)")
     ap.add_argument("--reset-router", action="store_true", help="re-draw the routers after a restore")
     a = ap.parse_args(argv)
     over = {}
@@ -72,7 +73,8 @@ def parse(argv=None) -> TrainArgs:
                      session_budget_s=a.session_budget_s, resume=not a.no_resume, resume_slot=a.resume_slot,
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
                      skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
-                     remat=a.remat, reset_router=a.reset_router, context_parallel=a.cp)
+                     remat=a.remat, reset_router=a.reset_router, context_parallel=a.cp,
+                     pipeline_parallel=a.pp)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
