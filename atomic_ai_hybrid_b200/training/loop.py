@@ -91,7 +91,8 @@ class TrainArgs:
     remat: bool = False            # recompute every layer in the backward (activation checkpointing)
     context_parallel: int = 1      # sequence segments over all ranks (parallel.cp); every rank reads the same batch
     reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
-    pipeline_parallel: int = 1     # contiguous layer stages over all ranks (parallel.pp); every rank reads the same batch
+    pipeline_parallel: int = 1     # contiguous layer stages (parallel.pp); world / stages data-parallel replicas
+    pipeline_schedule: str = "1f1b"  # or "gpipe"
 
 
 def _dist_setup():
@@ -131,11 +132,13 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
     world) that the data loader shards over and the expert-parallel token capacity."""
     tp, ep = max(1, args.tensor_parallel), max(1, args.expert_parallel)
     if args.pipeline_parallel > 1:
-        if args.pipeline_parallel != world or tp > 1 or ep > 1 or args.context_parallel > 1:
-            raise ValueError("pipeline parallelism spans all ranks and does not combine with --tp / --ep / --cp")
+        pp = args.pipeline_parallel
+        if world % pp or tp > 1 or ep > 1 or args.context_parallel > 1:
+            raise ValueError("pipeline parallelism needs world % stages == 0 and does not combine with "
+                             "--tp / --ep / --cp")
         from ..parallel.context import ParallelContext, set_parallel_context
         set_parallel_context(ParallelContext())
-        return 0, 1, 0
+        return rank // pp, world // pp, 0  # replica d = rank // stages reads its share
     if args.context_parallel > 1:
         if args.context_parallel != world or tp > 1 or ep > 1:
             raise ValueError("context parallelism spans all ranks and does not combine with --tp / --ep")
@@ -193,8 +196,10 @@ def main_execution(args: TrainArgs) -> Dict:
     total_steps = args.total_steps or (steps_per_epoch * args.epochs if steps_per_epoch else (args.max_steps or 1000))
     if args.pipeline_parallel > 1:
         from ..parallel.pp import PipelineTrainer
-        trainer = PipelineTrainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt,
-                                  device=dev, skip_nonfinite=args.skip_nonfinite)
+        trainer = PipelineTrainer(model, stages=args.pipeline_parallel, total_steps=total_steps,
+                                  optimizer=args.optimizer, compute_dtype=cdt, device=dev,
+                                  skip_nonfinite=args.skip_nonfinite, schedule=args.pipeline_schedule,
+                                  data_parallel=world // args.pipeline_parallel)
     else:
         trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
                           cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,

@@ -28,7 +28,7 @@ def _cfg(layers):
                       d_state=32)
 
 
-def _run(rank, world, port, steps, layers, q):
+def _run(rank, world, port, steps, layers, q, schedule="1f1b", dp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -40,54 +40,97 @@ def _run(rank, world, port, steps, layers, q):
         torch.manual_seed(0)
         m = HybridMoEModel(cfg, compute_dtype=torch.float32)
         if world > 1:
-            tr = PipelineTrainer(m, total_steps=50, optimizer="adamw", device=torch.device("cpu"))
+            tr = PipelineTrainer(m, total_steps=50, optimizer="adamw", device=torch.device("cpu"),
+                                 schedule=schedule, data_parallel=dp)
         else:
             tr = Trainer(m, total_steps=50, optimizer="adamw", compute_dtype=torch.float32,
                          device=torch.device("cpu"))
         tr.opt.schedule.warmup = 1
         g = torch.Generator().manual_seed(9)
         ids = torch.randint(0, cfg.vocab_size, (4, 129), generator=g)
-        micro = [{"input_ids": ids[i:i + 2, :-1], "labels": ids[i:i + 2, 1:]} for i in (0, 2)]
+        micro = [{"input_ids": ids[i:i + 1, :-1], "labels": ids[i:i + 1, 1:]} for i in range(4)]
+        if world > 1 and dp > 1:  # replica d takes its share of the micro-batches
+            per = len(micro) // dp
+            d = rank // (world // dp)
+            micro = micro[d * per:(d + 1) * per]
         hist = []
         for _ in range(steps):
             out = tr.train_step(micro)
-            hist.append((float(out["loss"]), float(out["global_norm"])))
+            loss = out["loss"].clone()
+            if world > 1 and dp > 1:  # the replicas' mean is the single-rank loss
+                dist.all_reduce(loss)
+                loss /= world
+            hist.append((float(loss), float(out["global_norm"])))
         params = {n: p.detach().clone().numpy() for n, p in m.named_parameters()}
+        peak = 0
         if world > 1:
             held = {n for n, _ in tr.part.named_parameters()}
             params = {n: v for n, v in params.items() if n in held}
-        q.put((rank, hist, params))
+            peak = tr.peak_live
+        q.put((rank, hist, params, peak))
     finally:
         if world > 1:
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("layers", [2, 3])
-def test_pp2_training_follows_single_rank(layers):
+def _reference(steps, layers):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    steps = 3
     p1 = ctx.Process(target=_run, args=(0, 1, _port(), steps, layers, q))
     p1.start()
-    _, ref_hist, ref = q.get(timeout=300)
+    _, ref_hist, ref, _ = q.get(timeout=300)
     p1.join(timeout=60)
+    return ref_hist, ref
+
+
+def _pipeline(world, steps, layers, schedule, dp=1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, steps, layers, q)) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, steps, layers, q, schedule, dp)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for _, hist, params in got:
+    return sorted(got, key=lambda t: t[0])
+
+
+def _check(ref_hist, ref, got, steps):
+    for _, hist, params, _ in got:
         for (l0, n0), (l1, n1) in zip(ref_hist, hist):
             assert abs(l1 - l0) <= 1e-5 * abs(l0), (ref_hist, hist)
             assert abs(n1 - n0) <= 1e-4 * abs(n0), (ref_hist, hist)
         for n, v in params.items():
             r, t = torch.from_numpy(ref[n]), torch.from_numpy(v)
             assert (t - r).abs().max() <= 2 * 6e-4 * steps, n
-    held = set().union(*(set(p) for _, _, p in got))
+    held = set().union(*(set(p) for _, _, p, _ in got))
     assert held == set(ref), set(ref) ^ held
+
+
+@pytest.mark.parametrize("stages,layers,schedule", [(2, 2, "1f1b"), (2, 3, "gpipe"), (3, 3, "1f1b")])
+def test_pipeline_training_follows_single_rank(stages, layers, schedule):
+    """Even and uneven layer splits, both schedules: the loss, the gradient norm and the
+    weights after three steps match one rank running every micro-batch."""
+    steps = 3
+    ref_hist, ref = _reference(steps, layers)
+    got = _pipeline(stages, steps, layers, schedule)
+    _check(ref_hist, ref, got, steps)
+    peaks = [g[3] for g in got]
+    if schedule == "1f1b":  # stage s keeps at most S - s micro-batches' activations
+        assert peaks == [min(stages - s, 4) for s in range(stages)], peaks
+    else:
+        assert peaks == [4] * stages, peaks
+
+
+def test_pipeline_with_data_parallel_replicas():
+    """A 2 x 2 mesh (two replicas of a two-stage pipeline, each stage's store sharded over
+    its two replicas) trains like one rank running both replicas' micro-batches."""
+    steps = 2
+    ref_hist, ref = _reference(steps, 2)
+    got = _pipeline(4, steps, 2, "1f1b", dp=2)
+    _check(ref_hist, ref, got, steps)
 
 
 def _ckpt(rank, world, port, root, q):

@@ -188,26 +188,41 @@ def test_training_loop_with_context_parallelism(tmp_path):
     assert outs[0]["global_step"] == 2 and outs[1]["global_step"] == 2, outs
 
 
-def _pp_rank_main(rank, world, port, tmp):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+def _pp_rank_main(rank, world, ports, tmp, stages):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(ports[0]), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
     _write_data(tmp)
-    kw = dict(data_dir=tmp, data_prefixes=["src"], pipeline_parallel=2, eval_every=2, eval_batches=1)
+    kw = dict(data_dir=tmp, data_prefixes=["src"], pipeline_parallel=stages, eval_every=2, eval_batches=1,
+              global_batch=2 * (world // stages))
     first = main_execution(_args(tmp, max_steps=2, **kw))
+    # the second job gets a rendezvous of its own (the first one's store may still be
+    # closing on rank 0 when the other ranks start the second)
+    os.environ["MASTER_PORT"] = str(ports[1])
     again = main_execution(_args(tmp, max_steps=3, **kw))  # resumes from the stage files
     with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
         json.dump({"first": first["global_step"], "again": again["global_step"],
                    "loss": again["losses"][-1] if again.get("losses") else None}, f)
 
 
-def test_training_loop_with_pipeline_parallelism(tmp_path):
-    """train.py's loop with --pp 2: two layer stages train, evaluate, checkpoint their own
-    parameters and resume from them."""
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    mp.spawn(_pp_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
-    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(2)]
+def _free_ports(n):
+    socks = []
+    for _ in range(n):
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        socks.append(s)
+    ports = [s.getsockname()[1] for s in socks]
+    for s in socks:
+        s.close()
+    return ports
+
+
+@pytest.mark.parametrize("world,stages", [(2, 2), (4, 2)])
+def test_training_loop_with_pipeline_parallelism(tmp_path, world, stages):
+    """train.py's loop with --pp 2 (and, on 4 ranks, two data-parallel replicas of the
+    pipeline): the stages train, evaluate, checkpoint their own parameters and resume."""
+    mp.spawn(_pp_rank_main, args=(world, _free_ports(2), str(tmp_path), stages), nprocs=world, join=True)
+    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(world)]
     assert all(o["first"] == 2 and o["again"] == 3 for o in outs), outs
-    assert outs[0]["loss"] == outs[1]["loss"], outs  # both stages report the whole loss
+    for d in range(world // stages):  # every stage of a replica reports the replica's whole loss
+        rep = outs[d * stages:(d + 1) * stages]
+        assert all(o["loss"] == rep[0]["loss"] for o in rep), outs

@@ -50,7 +50,9 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
     ap.add_argument("--cp", type=int, default=1, help="context parallelism over all ranks (sequence segments)")
-    ap.add_argument("--pp", type=int, default=1, help="pipeline parallelism over all ranks (layer stages)")
+    ap.add_argument("--pp", type=int, default=1,
+                    help="pipeline stages (layer blocks); world / pp data-parallel replicas of the pipeline")
+    ap.add_argument("--pp-schedule", default="1f1b", choices=("1f1b", "gpipe"))
     ap.add_argument("--reset-router", action="store_true", help="re-draw the routers after a restore")
     a = ap.parse_args(argv)
     over = {}
@@ -74,7 +76,7 @@ def parse(argv=None) -> TrainArgs:
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
                      skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
                      remat=a.remat, reset_router=a.reset_router, context_parallel=a.cp,
-                     pipeline_parallel=a.pp)
+                     pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
