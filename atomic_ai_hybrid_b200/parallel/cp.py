@@ -137,13 +137,24 @@ def get_cp() -> Optional[CPGroup]:
     return cp if cp is not None and cp.world > 1 else None
 
 
-def init_context_parallel(device: Optional[torch.device] = None) -> CPGroup:
-    """Every rank of the job in one context-parallel group (sequence segments); install it
-    in the parallel context.  Batch statistics average over all ranks (each holds different
-    tokens)."""
+def init_context_parallel(device: Optional[torch.device] = None, cp_size: Optional[int] = None) -> CPGroup:
+    """Context-parallel groups of ``cp_size`` consecutive ranks (all ranks by default; the
+    ``world / cp_size`` groups are data-parallel replicas that read different batches);
+    install this rank's group in the parallel context.  Every parameter is replicated on
+    every rank, so gradients and batch statistics are summed / averaged over all ranks
+    (each rank holds different tokens: its segment of its replica's sequences)."""
     from .context import ParallelContext, set_parallel_context
     world, rank = dist.get_world_size(), dist.get_rank()
-    cp = CPGroup(world, rank, None)
+    size = cp_size or world
+    if world % size:
+        raise ValueError(f"{world} ranks do not split into context-parallel groups of {size}")
+    group = None
+    if size < world:
+        for start in range(0, world, size):  # every rank creates every group, in order
+            g = dist.new_group(list(range(start, start + size)))
+            if start <= rank < start + size:
+                group = g
+    cp = CPGroup(size, rank % size, group)
     ctx = ParallelContext(dp_group=None, dp_world=world)
     ctx.cp = cp
     set_parallel_context(ctx)

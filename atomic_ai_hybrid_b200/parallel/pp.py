@@ -1,8 +1,8 @@
 """Pipeline parallelism for the interleaved stack (1F1B or GPipe schedule over NCCL / gloo p2p).
 
 The reference has no pipeline parallelism (GSPMD FSDP + DP on a 1-D mesh,
-`train_setup.py:361-365`); the survey of this build lists it as optional, with the rule
-that pipeline sends and receives stay on NCCL point-to-point.  Stage ``s`` of ``S`` runs a
+`train_setup.py:361-365`); here it is an additional layout whose stage-to-stage sends and
+receives run on NCCL (or gloo) point-to-point.  Stage ``s`` of ``S`` runs a
 contiguous block of the layers; the first stage also embeds the tokens and the last one
 applies the final norm and the tied LM head, for which it holds a copy of the embedding
 table whose gradient is summed with the first stage's before every optimizer step (both

@@ -89,7 +89,7 @@ class TrainArgs:
     tensor_parallel: int = 1
     expert_parallel: int = 1
     remat: bool = False            # recompute every layer in the backward (activation checkpointing)
-    context_parallel: int = 1      # sequence segments over all ranks (parallel.cp); every rank reads the same batch
+    context_parallel: int = 1      # sequence segments (parallel.cp); world / cp data-parallel replicas
     reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
     pipeline_parallel: int = 1     # contiguous layer stages (parallel.pp); world / stages data-parallel replicas
     pipeline_schedule: str = "1f1b"  # or "gpipe"
@@ -140,11 +140,12 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
         set_parallel_context(ParallelContext())
         return rank // pp, world // pp, 0  # replica d = rank // stages reads its share
     if args.context_parallel > 1:
-        if args.context_parallel != world or tp > 1 or ep > 1:
-            raise ValueError("context parallelism spans all ranks and does not combine with --tp / --ep")
+        cp = args.context_parallel
+        if world % cp or tp > 1 or ep > 1:
+            raise ValueError("context parallelism needs world % cp == 0 and does not combine with --tp / --ep")
         from ..parallel.cp import init_context_parallel
-        init_context_parallel(dev)
-        return 0, 1, 0
+        init_context_parallel(dev, cp)
+        return rank // cp, world // cp, 0  # replica d = rank // cp reads its share
     if tp > 1:
         if ep > 1 and ep != tp:
             raise ValueError("with tensor parallelism, expert parallelism runs over the same group (ep == tp)")

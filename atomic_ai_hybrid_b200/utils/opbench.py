@@ -1,11 +1,11 @@
-"""Single-GPU operator benchmark (the benchmark spec's config 2): GDN-2 chunked
+"""Single-GPU operator benchmark (the scan-operator configuration): GDN-2 chunked
 delta rule and Mamba2 SSD, forward + backward, bf16, timed with CUDA events; also
 the MoE grouped FFN, the fused router, the fused residual/norm glue and conv1d.
 
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op gdn --B 8 --T 4096 --H 16``
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op ssd --B 8 --T 4096 --H 32``
 
-Inputs follow the spec: GDN q, k ~ N(0,1) then L2-normalised per head, v ~ N(0,1),
+Inputs: GDN q, k ~ N(0,1) then L2-normalised per head, v ~ N(0,1),
 beta = sigmoid(N(0,1)), g = -softplus(N(0,1)) (per head, broadcast over the
 channels of the per-channel kernels; erase gate = beta, write gate = 1).  SSD x, B,
 C ~ N(0,1), dt = softplus(N(0,1) - 4) per head (broadcast over channels),

@@ -30,7 +30,7 @@ def _cfg(kind):
     return get_preset("reference_tiny", dropout_rate=0.0, router_noise_std=0.0)
 
 
-def _worker(rank, world, port, kind, q):
+def _worker(rank, world, port, kind, q, cp=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -39,12 +39,15 @@ def _worker(rank, world, port, kind, q):
         set_parallel_context(ParallelContext())
         torch.manual_seed(0)
         full = HybridMoEModel(cfg, compute_dtype=torch.float32)
-        ids = torch.randint(0, cfg.vocab_size, (2, 64 * world + 1), generator=torch.Generator().manual_seed(7))
-        batch = {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
-        lf, _ = compute_loss(full, batch)
+        cp = cp or world
+        reps = world // cp  # data-parallel replicas of the context-parallel group
+        ids = torch.randint(0, cfg.vocab_size, (2 * reps, 64 * cp + 1), generator=torch.Generator().manual_seed(7))
+        lf, _ = compute_loss(full, {"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+        d = rank // cp
+        batch = {"input_ids": ids[2 * d:2 * d + 2, :-1], "labels": ids[2 * d:2 * d + 2, 1:]}
         lf.backward()
         gf = {n: p.grad.clone() for n, p in full.named_parameters() if p.grad is not None}
-        init_context_parallel()
+        init_context_parallel(cp_size=cp)
         m = HybridMoEModel(cfg, compute_dtype=torch.float32)
         m.load_state_dict(full.state_dict())
         loss, _ = compute_loss(m, batch)
@@ -70,12 +73,15 @@ def _worker(rank, world, port, kind, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind,world", [("interleaved", 2), ("interleaved", 4), ("blockdar", 2)])
-def test_cp_matches_single_rank(kind, world):
+@pytest.mark.parametrize("kind,world,cp", [("interleaved", 2, 2), ("interleaved", 4, 4), ("blockdar", 2, 2),
+                                           ("interleaved", 4, 2)])
+def test_cp_matches_single_rank(kind, world, cp):
+    """``cp < world``: two data-parallel replicas of a 2-rank context-parallel group, each
+    with its own sequences; the reference model sees both replicas' sequences."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, kind, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, kind, q, cp)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)

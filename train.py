@@ -49,7 +49,8 @@ def parse(argv=None) -> TrainArgs:
                                                         "between the mixers)")
     ap.add_argument("--ep", type=int, default=1, help="expert-parallel size (== --tp, or == world without --tp)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
-    ap.add_argument("--cp", type=int, default=1, help="context parallelism over all ranks (sequence segments)")
+    ap.add_argument("--cp", type=int, default=1,
+                    help="context-parallel group size (sequence segments); world / cp data-parallel replicas")
     ap.add_argument("--pp", type=int, default=1,
                     help="pipeline stages (layer blocks); world / pp data-parallel replicas of the pipeline")
     ap.add_argument("--pp-schedule", default="1f1b", choices=("1f1b", "gpipe"))
