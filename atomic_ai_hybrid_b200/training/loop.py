@@ -44,6 +44,7 @@ from ..data import Prefetcher, dataloader_multi_source, resolve_source_files, sy
 from ..models import HybridMoEModel
 from ..optim.schedule import DIAG_GROUPS
 from ..utils import wandb_logging
+from ..utils.health import PeerFailure, PeerHealth
 from ..utils.monitor import (SESSION_TIME_BUDGET_SECONDS, BurstGuard, FaultInjector, NonFiniteMonitor,
                              StopSignals)
 from .trainer import Trainer
@@ -105,6 +106,9 @@ def _dist_setup():
         torch.cuda.set_device(dev)
     if world > 1 and not dist.is_initialized():
         backend = "nccl" if use_cuda else "gloo"
+        # a timed-out NCCL collective tears the communicator down instead of leaving
+        # the process waiting on it
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
         kw = {"device_id": dev} if use_cuda else {}
         timeout = timedelta(seconds=float(os.environ.get("AHB_PG_TIMEOUT_S", "300")))
         dist.init_process_group(backend, timeout=timeout, **kw)
@@ -164,7 +168,25 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
 
 
 def main_execution(args: TrainArgs) -> Dict:
+    """Train per ``args``.  A failure on one rank is posted to the others
+    (``utils.health``): they stop at their next step, or when the collective they wait in
+    times out, with ``PeerFailure`` naming the failed rank."""
     rank, world, dev = _dist_setup()
+    health = PeerHealth.create(rank, world)
+    try:
+        return _train(args, rank, world, dev, health)
+    except PeerFailure:
+        raise
+    except Exception as e:
+        if health is not None:
+            failures = health.failed_peers()
+            if failures:  # this rank's error follows from a peer's failure
+                raise PeerFailure(failures, health.step) from e
+            health.report(e)
+        raise
+
+
+def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHealth]) -> Dict:
     ops.set_impl(args.impl if dev.type == "cuda" else "eager")
     cfg = load_yaml_config(args.config_yaml) if args.config_yaml else get_preset(args.preset, **args.overrides)
     data_rank, data_world, ep_tokens = _parallel_setup(args, cfg, rank, world, dev)
@@ -288,6 +310,8 @@ def main_execution(args: TrainArgs) -> Dict:
             if args.max_steps is not None and global_step >= args.max_steps:
                 done = True
                 break
+            if health is not None:
+                health.check(global_step + 1)
             micro = []
             for _m in range(args.accum_steps):
                 b = next(train_stream)

@@ -63,16 +63,47 @@ def _rank_main(rank, world, port, tmp):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="10", AHB_INJECT_RAISE_STEP="2",
                       AHB_INJECT_RAISE_RANK="1")
-    main_execution(_args(tmp, max_steps=5, global_batch=2, accum_steps=1))
+    try:
+        main_execution(_args(tmp, max_steps=5, global_batch=2, accum_steps=1))
+    except Exception as e:
+        with open(os.path.join(tmp, f"err{rank}.txt"), "w") as f:
+            f.write(f"{type(e).__name__}: {e}")
+        raise
 
 
 def test_failing_rank_ends_peers_with_error(tmp_path):
+    """Rank 1 raises at step 2; rank 0, waiting in that step's collective, ends with an
+    error naming rank 1 and its exception (the notice posted through the store)."""
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    with pytest.raises(Exception):
-        mp.spawn(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode not in (0, None) for p in procs), [p.exitcode for p in procs]
+    err0 = (tmp_path / "err0.txt").read_text()
+    assert err0.startswith("PeerFailure") and "rank 1 at step 2" in err0 and "injected failure" in err0, err0
+    assert "injected failure" in (tmp_path / "err1.txt").read_text()
+
+
+def test_peer_health_notice_board():
+    """The notice board alone: nothing posted -> no failure; a posted failure stops the
+    other ranks at their next step check with the failed rank's details."""
+    import torch.distributed as dist
+    from atomic_ai_hybrid_b200.utils.health import PeerFailure, PeerHealth
+    store = dist.HashStore()
+    h0, h1, h2 = (PeerHealth(store, r, 3) for r in range(3))
+    h0.check(1)
+    h1.step = 4
+    h1.report(RuntimeError("boom"))
+    assert h1.failed_peers() == []  # its own notice is not a peer's
+    with pytest.raises(PeerFailure, match="rank 1 at step 4: RuntimeError"):
+        h2.check(5)
+    assert [f["rank"] for f in h0.failed_peers()] == [1]
 
 
 def _tp_rank_main(rank, world, port, tmp, ep=1):
