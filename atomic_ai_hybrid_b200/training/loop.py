@@ -266,7 +266,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
 
     train_stream, val_factory = make_stream(global_step * args.accum_steps)
     if rank == 0 and args.wandb_project:
-        wandb_logging.init_wandb(args.wandb_project, config=asdict(args))
+        wandb_logging.init_for_checkpoints(args.wandb_project, args.ckpt_root, config=asdict(args),
+                                           resume=args.resume, name=f"hybrid-{time.strftime('%Y%m%d-%H%M%S')}")
 
     # ---------------------------------------------------------------- loop
     signals = StopSignals().install()

@@ -12,15 +12,38 @@ _RUN = None
 
 
 def init_wandb(project: str, config: Optional[Dict] = None, run_id: Optional[str] = None,
-               name: Optional[str] = None) -> bool:
+               name: Optional[str] = None) -> Optional[str]:
+    """Start (or, with ``run_id``, continue) a run; returns its id, None without wandb."""
     global _RUN
     try:
         import wandb  # type: ignore
         _RUN = wandb.init(project=project, config=config, id=run_id, name=name, resume="allow")
-        return True
+        return str(getattr(_RUN, "id", None) or run_id or "") or None
     except Exception:
         _RUN = None
-        return False
+        return None
+
+
+RUN_ID_FILE = "wandb_run_id.txt"
+
+
+def init_for_checkpoints(project: str, ckpt_root: str, config: Optional[Dict] = None, resume: bool = True,
+                         name: Optional[str] = None) -> Optional[str]:
+    """Reference `train.py:563-588`: the run id lives in ``{ckpt_root}/wandb_run_id.txt``,
+    so a restarted job that resumes from those checkpoints continues the same run (its
+    curves stay continuous); a fresh start (``resume=False``) opens a new run."""
+    import os
+    path = os.path.join(ckpt_root, RUN_ID_FILE)
+    prev = None
+    if resume and os.path.exists(path):
+        with open(path) as f:
+            prev = f.read().strip() or None
+    run_id = init_wandb(project, config=config, run_id=prev, name=name)
+    if run_id is not None:
+        os.makedirs(ckpt_root, exist_ok=True)
+        with open(path, "w") as f:
+            f.write(run_id)
+    return run_id
 
 
 def log_metrics(step: int, metrics: Dict) -> None:

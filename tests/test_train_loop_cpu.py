@@ -257,3 +257,38 @@ def test_training_loop_with_pipeline_parallelism(tmp_path, world, stages):
     for d in range(world // stages):  # every stage of a replica reports the replica's whole loss
         rep = outs[d * stages:(d + 1) * stages]
         assert all(o["loss"] == rep[0]["loss"] for o in rep), outs
+
+
+def test_wandb_run_continues_across_restarts(tmp_path, monkeypatch):
+    """With a (fake) wandb installed, the first job writes its run id next to the
+    checkpoints and the resumed job continues that run; a fresh start opens a new one."""
+    import sys
+    import types
+    from atomic_ai_hybrid_b200.utils import wandb_logging
+    calls = []
+
+    class _Run:
+        def __init__(self, id):
+            self.id = id
+            self.summary = {}
+
+        def log(self, metrics, step=None):
+            calls.append(("log", step))
+
+        def finish(self):
+            calls.append(("finish", None))
+
+    def init(project=None, config=None, id=None, name=None, resume=None):
+        run = _Run(id or f"run{len([c for c in calls if c[0] == 'init'])}")
+        calls.append(("init", id))
+        return run
+
+    monkeypatch.setitem(sys.modules, "wandb", types.SimpleNamespace(init=init))
+    main_execution(_args(tmp_path, max_steps=1, wandb_project="p"))
+    assert (tmp_path / "wandb_run_id.txt").read_text() == "run0"
+    main_execution(_args(tmp_path, max_steps=2, wandb_project="p"))
+    assert [c[1] for c in calls if c[0] == "init"] == [None, "run0"]
+    assert any(c == ("log", 2) for c in calls)
+    main_execution(_args(tmp_path, max_steps=1, wandb_project="p", resume=False))
+    assert [c[1] for c in calls if c[0] == "init"][-1] is None
+    assert wandb_logging._RUN is None  # finished
