@@ -104,6 +104,10 @@ def _dist_setup():
     dev = torch.device("cuda", local) if use_cuda else torch.device("cpu")
     if use_cuda:
         torch.cuda.set_device(dev)
+    if world > 1 and not use_cuda and "OMP_NUM_THREADS" not in os.environ:
+        # CPU ranks of one host share its cores: one share each instead of all of them
+        local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // max(local, 1)))
     if world > 1 and not dist.is_initialized():
         backend = "nccl" if use_cuda else "gloo"
         # a timed-out NCCL collective tears the communicator down instead of leaving

@@ -33,6 +33,7 @@ def _cfg(kind):
 def _worker(rank, world, port, kind, q, cp=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.parallel.cp import init_context_parallel
         cfg = _cfg(kind)

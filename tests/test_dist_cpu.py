@@ -37,12 +37,13 @@ def _run(rank, world, port, out_path, steps):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
+        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # no oversubscription of the cores
     cfg = _cfg()
     torch.manual_seed(0)
     m = HybridMoEModel(cfg, compute_dtype=torch.float32)
     tr = Trainer(m, total_steps=50, optimizer="hybrid", compute_dtype=torch.float32, device=torch.device("cpu"))
     tr.opt.schedule.warmup = 1
-    ids = _batches(cfg, 2)
+    ids = _batches(cfg, 4)  # 8 sequences: 1, 2 or 4 per rank at world 8, 4 or 2
     per = ids.shape[0] // world
     mine = ids[rank * per:(rank + 1) * per]
     for _ in range(steps):
@@ -63,7 +64,7 @@ def _run(rank, world, port, out_path, steps):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_sharded_training_matches_single_process(tmp_path, world):
     steps = 3
     p1 = str(tmp_path / "one.pt")

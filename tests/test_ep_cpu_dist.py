@@ -1,9 +1,10 @@
 """Expert parallelism through the torch.distributed all-to-all (gloo ranks on the CPU):
-the model with its routed experts split over 2 ranks gives the single-rank loss and
+the model with its routed experts split over 2, 4 or 8 ranks gives the single-rank loss and
 gradients, and trains like it."""
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -22,21 +23,22 @@ def _port():
     return p
 
 
-def _cfg():
+def _cfg(world=2):
     return get_preset("tiny", num_layers=2, layer_types=("mamba2", "gdn2"), vocab_size=512, d_model=128,
-                      n_heads=2, n_heads_ssm=2, d_ff=128, n_routed_experts=4, top_k=2, d_state=32)
+                      n_heads=2, n_heads_ssm=2, d_ff=128, n_routed_experts=max(4, world), top_k=2, d_state=32)
 
 
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # no oversubscription of the cores
     try:
-        cfg = _cfg()
+        cfg = _cfg(world)
         # every rank: the single-rank model on the whole global batch (2 sequences per rank)
         set_parallel_context(ParallelContext())
         torch.manual_seed(0)
         full = HybridMoEModel(cfg, compute_dtype=torch.float32)
-        ids = torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=torch.Generator().manual_seed(5))
+        ids = torch.randint(0, cfg.vocab_size, (2 * world, 65), generator=torch.Generator().manual_seed(5))
         full.zero_grad()
         lf, _ = compute_loss(full, {"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
         lf.backward()
@@ -74,17 +76,19 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_ep2_collective_matches_single_rank():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_collective_matches_single_rank(world):
+    """2, 4 and 8 ranks (8 routed experts at 8 ranks: one per rank)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for r in range(2):
+    for r in range(world):
         assert res[r]["loss"] < 1e-5, res
         assert res[r]["grad"] < 1e-3, res

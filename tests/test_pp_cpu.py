@@ -32,6 +32,7 @@ def _run(rank, world, port, steps, layers, q, schedule="1f1b", dp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
+        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.training.trainer import Trainer
         from atomic_ai_hybrid_b200.parallel.pp import PipelineTrainer
@@ -136,6 +137,7 @@ def test_pipeline_with_data_parallel_replicas():
 def _ckpt(rank, world, port, root, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
         from atomic_ai_hybrid_b200.parallel.pp import PipelineTrainer

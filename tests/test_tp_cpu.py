@@ -42,6 +42,7 @@ def _loss_grads(model, ids):
 def _parity(rank, world, port, kind, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, shard_tensor
         cfg = _cfg(kind, world)
@@ -113,6 +114,7 @@ def _train(rank, world, port, steps, q, optimizer="adamw"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
+        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, unshard_tensors, shard_spec
         from atomic_ai_hybrid_b200.training.trainer import Trainer
@@ -205,6 +207,7 @@ def test_tp_checkpoint_pieces_reassemble_for_any_world():
 def _ckpt(rank, world, port, root, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
     try:
         from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, unshard_tensors
