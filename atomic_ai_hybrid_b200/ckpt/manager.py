@@ -49,6 +49,9 @@ class CheckpointManager:
         self.rank, self.world = rank, world
         self._thread: Optional[threading.Thread] = None
         self._error: Optional[BaseException] = None
+        # rank 0 calls on_commit(step, metadata) from the writer after a step commits
+        # (the Hub relay's upload); its failures are printed, never raised
+        self.on_commit = None
         os.makedirs(self.dir, exist_ok=True)
 
     # ------------------------------------------------------------ listing
@@ -122,6 +125,11 @@ class CheckpointManager:
                     with open(os.path.join(d, "COMMIT"), "w") as f:
                         f.write(str(step))
                     self._prune()
+                    if self.on_commit is not None:
+                        try:
+                            self.on_commit(step, meta)
+                        except Exception as e:
+                            print(f"[CKPT] after-commit hook failed for step {step}: {e!r}", flush=True)
             except BaseException as e:  # surfaced by finalize()
                 self._error = e
 
@@ -347,28 +355,21 @@ def make_manager(root: str, slot: str, max_to_keep: int = 1, rank: int = 0, worl
     return CheckpointManager(root, slot, max_to_keep, rank, world)
 
 
-def upload_slot(local_dir: str, repo_subdir: str, step: int, repo_id: Optional[str] = None, keep_last_n: int = 1):
-    """Mirror a committed step to the Hugging Face Hub (reference ``upload_slot``).
-    Needs ``huggingface_hub`` and network access; raises a clear error otherwise."""
-    try:
-        from huggingface_hub import HfApi  # type: ignore
-    except ImportError as e:
-        raise RuntimeError("upload_slot needs the huggingface_hub package, which is not installed") from e
-    repo_id = repo_id or os.environ.get("HF_REPO_ID")
-    if not repo_id:
-        raise RuntimeError("upload_slot: set HF_REPO_ID or pass repo_id")
-    api = HfApi()
-    api.upload_folder(folder_path=os.path.join(local_dir, str(step)), repo_id=repo_id,
-                      path_in_repo=f"{repo_subdir}/{step}")
+def upload_slot(local_dir: str, repo_subdir: str, step: int, msg: str = "", keep_last_n: int = 1,
+                repo_id: Optional[str] = None) -> bool:
+    """Reference ``upload_slot``: mirror ``{local_dir}/{step}`` to ``{repo}/{repo_subdir}/{step}``
+    and prune older steps of that slot (``ckpt.hub.HubRelay.upload``); False when no relay."""
+    from .hub import HubRelay
+    relay = HubRelay.create(repo_id, keep_last_n=keep_last_n)
+    return relay.upload(local_dir, repo_subdir, step, msg) if relay is not None else False
 
 
-def download_slot(local_dir: str, repo_subdir: str, repo_id: Optional[str] = None) -> Optional[int]:
-    """Fetch the newest step of a slot from the Hub (reference ``download_slot``)."""
-    try:
-        from huggingface_hub import snapshot_download  # type: ignore
-    except ImportError as e:
-        raise RuntimeError("download_slot needs the huggingface_hub package, which is not installed") from e
-    repo_id = repo_id or os.environ.get("HF_REPO_ID")
-    path = snapshot_download(repo_id=repo_id, allow_patterns=[f"{repo_subdir}/*"], local_dir=local_dir)
-    steps = [int(d) for d in os.listdir(os.path.join(path, repo_subdir)) if d.isdigit()]
-    return max(steps) if steps else None
+def download_slot(local_dir: str, repo_subdir: str, repo_id: Optional[str] = None,
+                  bucket_id: Optional[str] = None) -> Optional[int]:
+    """Reference ``download_slot``: the newest step of a slot from the model repo, or from an
+    HF bucket when ``bucket_id`` is given (``ckpt.hub.HubRelay.download``)."""
+    from .hub import HubRelay
+    relay = HubRelay.create(repo_id, bucket_id=bucket_id)
+    if relay is None:
+        return None
+    return relay.download(local_dir, repo_subdir, "bucket" if bucket_id else "hf_model")

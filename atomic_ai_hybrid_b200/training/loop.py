@@ -78,6 +78,13 @@ class TrainArgs:
     early_stop_patience: int = 5
     resume: bool = True
     resume_slot: str = "latest"
+    # Hugging Face Hub mirror of the slots (reference RESUME_SOURCE / HF_REPO_ID): uploads
+    # after each commit when a repo is named; with no local checkpoint a resume fetches
+    # the slot from the model repo ("hf_model") or a storage bucket ("bucket")
+    hf_repo_id: Optional[str] = None
+    hf_bucket_id: Optional[str] = None
+    resume_source: str = "local_only"
+    hf_keep_last_n: int = 1
     wandb_project: Optional[str] = None
     impl: str = "cuda"
     cuda_graph: bool = True
@@ -214,6 +221,22 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
 
     mgrs = {s: CheckpointManager(args.ckpt_root, s, max_to_keep=1, rank=rank, world=world)
             for s in ("latest", "best_train", "best_val")}
+    relay = None
+    if args.hf_repo_id or args.hf_bucket_id or os.environ.get("HF_REPO_ID"):
+        from ..ckpt.hub import HubRelay
+        relay = HubRelay.create(args.hf_repo_id, args.hf_bucket_id, args.hf_keep_last_n)
+    if relay is not None and rank == 0:
+        for slot_name, mg in mgrs.items():
+            mg.on_commit = (lambda step, meta, s=slot_name: relay.upload(
+                mgrs[s].dir, s, step, str(meta.get("tag") or "")))
+    if (args.resume and relay is not None and args.resume_source != "local_only"
+            and all(mg.latest_step() is None for mg in mgrs.values())):
+        if int(os.environ.get("LOCAL_RANK", "0")) == 0:  # one download per host
+            want = args.resume_slot
+            if relay.download(mgrs[want].dir, want, args.resume_source) is None and want != "latest":
+                relay.download(mgrs["latest"].dir, "latest", args.resume_source)
+        if world > 1:
+            dist.barrier()
     steps_per_epoch = None
     if pairs is not None:
         _, _, micro_per_epoch, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,

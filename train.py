@@ -40,6 +40,10 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--session-budget-s", type=float, default=9 * 3600 - 300)
     ap.add_argument("--no-resume", action="store_true")
     ap.add_argument("--resume-slot", default="latest")
+    ap.add_argument("--hf-repo-id", default=None, help="mirror checkpoints to this Hub model repo ($HF_REPO_ID)")
+    ap.add_argument("--hf-bucket-id", default=None, help="Hub storage bucket to resume from")
+    ap.add_argument("--resume-source", default="local_only", choices=["local_only", "hf_model", "bucket"],
+                    help="where a resume looks when no local checkpoint exists")
     ap.add_argument("--wandb-project", default=None)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "eager"])
     ap.add_argument("--no-graph", action="store_true")
@@ -77,7 +81,8 @@ def parse(argv=None) -> TrainArgs:
                      wandb_project=a.wandb_project, impl=a.impl, cuda_graph=not a.no_graph,
                      skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
                      remat=a.remat, reset_router=a.reset_router, context_parallel=a.cp,
-                     pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule)
+                     pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule, hf_repo_id=a.hf_repo_id,
+                     hf_bucket_id=a.hf_bucket_id, resume_source=a.resume_source)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
