@@ -112,6 +112,7 @@ class PipelineTrainer:
 
     cuda_graph = False  # stage-to-stage transfers run between the layers
     _graph = None
+    last_info = None    # the per-layer statistics stay on their stages
 
     def __init__(self, model: nn.Module, stages: Optional[int] = None, total_steps: int = 1000,
                  optimizer: str = "adamw", compute_dtype: torch.dtype = torch.float32, device=None,

@@ -47,6 +47,7 @@ from ..utils import wandb_logging
 from ..utils.health import PeerFailure, PeerHealth
 from ..utils.monitor import (SESSION_TIME_BUDGET_SECONDS, BurstGuard, FaultInjector, NonFiniteMonitor,
                              StopSignals)
+from .metrics import model_metrics, step_metrics
 from .trainer import Trainer
 
 CHECKPOINT_EVERY_SECONDS = 95 * 60
@@ -295,6 +296,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     if rank == 0 and args.wandb_project:
         wandb_logging.init_for_checkpoints(args.wandb_project, args.ckpt_root, config=asdict(args),
                                            resume=args.resume, name=f"hybrid-{time.strftime('%Y%m%d-%H%M%S')}")
+        for k, v in model_metrics(model).items():
+            wandb_logging.set_summary(k, v)
 
     # ---------------------------------------------------------------- loop
     signals = StopSignals().install()
@@ -318,6 +321,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             mgrs["latest"].finalize()
             meta["best_train_loss"] = best_train
             mgrs["best_train"].save(step, trainer, meta, asynchronous=asynchronous)
+            if rank == 0:
+                wandb_logging.log_metrics(step, {"checkpoint/best_train_loss": best_train})
 
     def evaluate():
         if val_factory is None:
@@ -397,8 +402,15 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             steps_since_log += 1
             if rank == 0 and global_step % args.log_every == 0:
                 dt = time.time() - t_log
-                print(f"[step {global_step}] loss={loss_val:.4f} gnorm={gnorm:.3f} "
-                      f"tok/s={tokens_per_step * steps_since_log / max(dt, 1e-9):.0f}", flush=True)
+                tps = tokens_per_step * steps_since_log / max(dt, 1e-9)
+                print(f"[step {global_step}] loss={loss_val:.4f} gnorm={gnorm:.3f} tok/s={tps:.0f}", flush=True)
+                sm, lines, alerts = step_metrics(global_step, loss_val, trainer.last_info, best_train, tps, epoch,
+                                                 cfg.num_experts)
+                for line in lines:
+                    print("           " + line, flush=True)
+                for title, text in alerts:
+                    wandb_logging.log_alert(title, text)
+                wandb_logging.log_metrics(global_step, sm)
                 t_log, steps_since_log = time.time(), 0
             if time.time() - last_ckpt >= args.checkpoint_every_s:
                 save_latest(global_step, loss_val)
@@ -413,6 +425,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                         mgrs["best_val"].save(global_step, trainer, {"global_step": global_step, "epoch": epoch,
                                                                    "best_val_loss": best_val,
                                                                    "best_train_loss": best_train})
+                        if rank == 0:
+                            wandb_logging.log_metrics(global_step, {"checkpoint/best_val_loss": best_val})
                     else:
                         eval_no_improve += 1
                         if eval_no_improve >= args.early_stop_patience:
@@ -430,6 +444,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             break
         if val_factory is not None:
             vl = evaluate()
+            if vl is not None and rank == 0:
+                wandb_logging.log_metrics(global_step, {"eval/epoch_val_loss": vl, "eval/epoch": epoch})
             if vl is not None and vl < best_val:
                 best_val = vl
     for mg in mgrs.values():
@@ -437,6 +453,12 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     if stop_reason is None and global_step > 0:
         save_latest(global_step, loss_hist[-1] if loss_hist else None, asynchronous=False, tag="FINAL")
     signals.uninstall()
+    if rank == 0:
+        final = {"final/global_step": global_step, "final/best_train_loss": best_train,
+                 "final/best_val_loss": best_val, "final/stopped_by_nonfinite_limit": int(stop_reason == "nonfinite"),
+                 "final/stopped_by_time_budget": int(stop_reason == "time_budget")}
+        for k, v in final.items():
+            wandb_logging.set_summary(k, v)
     trainer.close()
     wandb_logging.finish()
     summary = {"global_step": global_step, "stop_reason": stop_reason, "losses": loss_hist,

@@ -114,6 +114,7 @@ class Trainer:
         self._graph = None
         self._graph_key = None
         self.graph_kernel_launches = 0
+        self.last_info: Optional[Dict] = None
 
     def _allreduce_sum(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
@@ -139,9 +140,11 @@ class Trainer:
             self._s_lab.copy_(batch["labels"])
             self._graph.replay()
             self._n_micro += 1
+            self.last_info = self._s_info
             return self._s_loss, self._s_info
         out = self._micro_body(batch)
         self._n_micro += 1
+        self.last_info = out[1]  # the step's statistics, read by the loop on logging steps
         return out
 
     @staticmethod

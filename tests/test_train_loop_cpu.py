@@ -266,6 +266,7 @@ def test_wandb_run_continues_across_restarts(tmp_path, monkeypatch):
     import types
     from atomic_ai_hybrid_b200.utils import wandb_logging
     calls = []
+    keys = set()
 
     class _Run:
         def __init__(self, id):
@@ -274,6 +275,7 @@ def test_wandb_run_continues_across_restarts(tmp_path, monkeypatch):
 
         def log(self, metrics, step=None):
             calls.append(("log", step))
+            keys.update(metrics)
 
         def finish(self):
             calls.append(("finish", None))
@@ -289,6 +291,30 @@ def test_wandb_run_continues_across_restarts(tmp_path, monkeypatch):
     main_execution(_args(tmp_path, max_steps=2, wandb_project="p"))
     assert [c[1] for c in calls if c[0] == "init"] == [None, "run0"]
     assert any(c == ("log", 2) for c in calls)
+    assert {"train/ce_loss", "train/tokens_per_sec", "moe/router_temp_mean", "moe/expert_util_std_max",
+            "checkpoint/best_train_loss"} <= keys, sorted(keys)
     main_execution(_args(tmp_path, max_steps=1, wandb_project="p", resume=False))
     assert [c[1] for c in calls if c[0] == "init"][-1] is None
     assert wandb_logging._RUN is None  # finished
+
+
+def test_step_metrics_follow_the_reference_keys():
+    """The router health summaries: keys, worst layers and alerts (collapsed router
+    column, collinear routers)."""
+    import torch
+    from atomic_ai_hybrid_b200.training.metrics import step_metrics
+    aux = {"ce_loss": torch.tensor(2.5), "aux_loss": torch.tensor(1.0), "z_loss": torch.tensor(3.0),
+           "expert_utilization": torch.tensor([[0.25, 0.25, 0.25, 0.25], [0.7, 0.1, 0.1, 0.1]]),
+           "router_temp": torch.tensor([9.0, 10.0]), "min_col_norm": torch.tensor([0.5, 1e-4]),
+           "router_max_cos_per_layer": torch.tensor([0.9, 0.1]), "max_abs_logit_preclip": torch.tensor([3.0, 13.0]),
+           "norm_x_mean": torch.tensor([1.0, 3.0]), "norm_x_max": torch.tensor([2.0, 5.0]),
+           "norm_x_min": torch.tensor([0.5, 0.1]), "moe_dropped_ratio": torch.tensor([0.0, 0.0])}
+    m, lines, alerts = step_metrics(7, 2.6, aux, 2.4, 1000.0, 0, 5)
+    assert m["train/ce_loss"] == 2.5 and m["train/tokens_per_sec"] == 1000.0
+    assert m["moe/expert_util_std_worst_layer"] == 1 and m["moe/router_temp_worst_layer"] == 1
+    assert m["moe/router_temp_layer0"] == 9.0 and abs(m["moe/min_col_norm_worst"] - 1e-4) < 1e-9
+    assert m["moe/router_max_cos_worst"] == pytest.approx(0.9) and m["moe/norm_x_max"] == 5.0
+    assert [t for t, _ in alerts] == ["Router column near-collapse", "Router collinearity high"]
+    assert any(line.startswith("[MOE-DIAG] router logits far past clip on layer 1") for line in lines)
+    m0, lines0, _ = step_metrics(1, 1.0, None, 1.0, 1.0, 0, 5)
+    assert set(m0) == {"train/loss", "train/best_train_loss", "train/tokens_per_sec", "train/epoch"} and not lines0
