@@ -305,7 +305,9 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     nonfin, burst = NonFiniteMonitor(), BurstGuard()
     t_start = time.time()
     last_ckpt = time.time()
-    eval_no_improve = 0
+    eval_no_improve, epochs_no_improve = 0, 0
+    best_eval = math.inf  # best partial (in-epoch) validation loss
+    t_epoch, epoch_tokens = time.time(), 0
     stop_reason = None
     tokens_per_step = args.global_batch * args.seq_len * args.accum_steps
     t_log, steps_since_log = time.time(), 0
@@ -323,6 +325,13 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             mgrs["best_train"].save(step, trainer, meta, asynchronous=asynchronous)
             if rank == 0:
                 wandb_logging.log_metrics(step, {"checkpoint/best_train_loss": best_train})
+
+    def save_best_val(step):
+        mgrs["best_val"].save(step, trainer, {"global_step": step, "epoch": epoch, "best_val_loss": best_val,
+                                              "best_train_loss": best_train})
+        if rank == 0:
+            print(f"[BEST_VAL] new best val loss {best_val:.4f} at step {step}", flush=True)
+            wandb_logging.log_metrics(step, {"checkpoint/best_val_loss": best_val})
 
     def evaluate():
         if val_factory is None:
@@ -362,6 +371,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             injector.before_apply(global_step + 1, trainer)
             info = trainer.apply(args.accum_steps)
             global_step += 1
+            epoch_tokens += tokens_per_step
             finite = bool(info["is_finite"])
             gnorm = float(info["global_norm"])
             loss_val = float(info["loss"])
@@ -419,17 +429,21 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 vl = evaluate()
                 if vl is not None:
                     if rank == 0:
-                        wandb_logging.log_metrics(global_step, {"eval/loss": vl})
-                    if vl < best_val:
-                        best_val, eval_no_improve = vl, 0
-                        mgrs["best_val"].save(global_step, trainer, {"global_step": global_step, "epoch": epoch,
-                                                                   "best_val_loss": best_val,
-                                                                   "best_train_loss": best_train})
-                        if rank == 0:
-                            wandb_logging.log_metrics(global_step, {"checkpoint/best_val_loss": best_val})
+                        print(f"[EVAL] step {global_step}: val loss (partial, {args.eval_batches} batches) = "
+                              f"{vl:.4f}", flush=True)
+                        wandb_logging.log_metrics(global_step, {"eval/partial_val_loss": vl})
+                    if vl < best_eval:
+                        best_eval, eval_no_improve = vl, 0
+                        if vl < best_val:
+                            best_val = vl
+                            save_best_val(global_step)
                     else:
                         eval_no_improve += 1
                         if eval_no_improve >= args.early_stop_patience:
+                            if rank == 0:
+                                wandb_logging.log_alert("Early stop", f"val loss did not improve for "
+                                                        f"{args.early_stop_patience} evaluations, step {global_step}")
+                            save_latest(global_step, loss_val, asynchronous=False, tag="EARLY_STOP")
                             stop_reason, done = "early_stop", True
             injector.after_step(global_step)
             if signals.requested is not None:
@@ -442,12 +456,27 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 break
         if done:
             break
-        if val_factory is not None:
-            vl = evaluate()
-            if vl is not None and rank == 0:
-                wandb_logging.log_metrics(global_step, {"eval/epoch_val_loss": vl, "eval/epoch": epoch})
-            if vl is not None and vl < best_val:
-                best_val = vl
+        # epoch end (reference `train.py:1237-1274`): validation, a forced save, best-val and
+        # the epoch-level early stop
+        if rank == 0:
+            el = time.time() - t_epoch
+            print(f"[EPOCH] {epoch} done: {epoch_tokens / max(el, 1e-9) / 1e6:.2f} M tokens/s", flush=True)
+        t_epoch, epoch_tokens = time.time(), 0
+        vl = evaluate() if val_factory is not None else None
+        if rank == 0 and vl is not None:
+            print(f"[EPOCH] {epoch}: mean validation loss {vl:.4f}", flush=True)
+            wandb_logging.log_metrics(global_step, {"eval/epoch_val_loss": vl, "eval/epoch": epoch})
+        if global_step > 0:
+            save_latest(global_step, None, asynchronous=False, tag="EPOCH_END")
+        if vl is not None:
+            if vl < best_val:
+                best_val, epochs_no_improve = vl, 0
+                save_best_val(global_step)
+            else:
+                epochs_no_improve += 1
+                if epochs_no_improve >= args.early_stop_patience:
+                    stop_reason = "early_stop"
+                    break
     for mg in mgrs.values():
         mg.finalize()
     if stop_reason is None and global_step > 0:
