@@ -318,3 +318,15 @@ def test_step_metrics_follow_the_reference_keys():
     assert any(line.startswith("[MOE-DIAG] router logits far past clip on layer 1") for line in lines)
     m0, lines0, _ = step_metrics(1, 1.0, None, 1.0, 1.0, 0, 5)
     assert set(m0) == {"train/loss", "train/best_train_loss", "train/tokens_per_sec", "train/epoch"} and not lines0
+
+
+def test_epoch_end_validation_and_save(tmp_path, capsys):
+    """Two passes over a small file source: each epoch ends with the full validation, a
+    forced EPOCH_END save and the best-val slot."""
+    _write_data(str(tmp_path))
+    s = main_execution(_args(tmp_path / "ck", data_dir=str(tmp_path), data_prefixes=["src"], global_batch=8,
+                             accum_steps=1, epochs=2, max_steps=None, eval_batches=1))
+    out = capsys.readouterr().out
+    assert out.count("[EPOCH]") == 4 and "mean validation loss" in out, out[-2000:]
+    assert s["global_step"] > 0 and s["best_val"] < float("inf")
+    assert os.listdir(tmp_path / "ck" / "best_val")
