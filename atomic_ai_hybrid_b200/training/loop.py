@@ -179,6 +179,21 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
     return rank, world, 0
 
 
+def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> None:
+    """The per-GPU memory plan of this layout (the reference prints XLA's memory analysis
+    of the compiled step, `train.py:765-772`); informative only."""
+    try:
+        from ..utils.memplan import plan
+        p = plan(cfg, world=world, micro_batch=micro_batch, seq_len=args.seq_len, tp=max(1, args.tensor_parallel),
+                 ep=max(1, args.expert_parallel), cp=max(1, args.context_parallel), pp=max(1, args.pipeline_parallel),
+                 accum_steps=args.accum_steps, remat=args.remat, schedule=args.pipeline_schedule)
+        print(f"[MEMORY] plan per GPU: state {p['state_total_gb']} GB + activations ~{p['activations_gb_est']} GB "
+              f"+ reserve {p['reserve_gb']} GB = {p['total_gb']} of {p['hbm_gb']} GB"
+              + ("" if p["fits"] else "  -- DOES NOT FIT: reduce the micro-batch or enable --remat"), flush=True)
+    except Exception as e:  # the plan never stops a run
+        print(f"[MEMORY] plan unavailable: {e!r}", flush=True)
+
+
 def main_execution(args: TrainArgs) -> Dict:
     """Train per ``args``.  A failure on one rank is posted to the others
     (``utils.health``): they stop at their next step, or when the collective they wait in
@@ -255,6 +270,9 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
         trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
                           cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
                           ep_max_tokens=ep_tokens)
+
+    if rank == 0 and dev.type == "cuda":
+        _print_memory_plan(args, cfg, world, per_rank)
 
     # ---------------------------------------------------------------- resume
     global_step, start_epoch = 0, 0
@@ -372,6 +390,9 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             info = trainer.apply(args.accum_steps)
             global_step += 1
             epoch_tokens += tokens_per_step
+            if global_step == 1 and rank == 0 and dev.type == "cuda":
+                print(f"[MEMORY] peak allocated after the first step: "
+                      f"{torch.cuda.max_memory_allocated(dev) / 1e9:.1f} GB", flush=True)
             finite = bool(info["is_finite"])
             gnorm = float(info["global_norm"])
             loss_val = float(info["loss"])
