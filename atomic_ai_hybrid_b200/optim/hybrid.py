@@ -70,6 +70,9 @@ class HybridOptimizer:
         self.schedule = LRSchedule(total_steps)
         self.reduce_fn = reduce_fn or (lambda t: t)
         self.skip_nonfinite = skip_nonfinite
+        # called with the step's global is-finite flag after the statistics are reduced and
+        # before any parameter moves (every rank calls it at the same point)
+        self.before_finish = None
         self.base = {"muon": muon_lr, "lion": lion_lr, "adamw_decay": adamw_lr, "adamw_nodecay": adamw_lr}
         self.count = 0
         dev = store.device
@@ -121,6 +124,8 @@ class HybridOptimizer:
         is_finite = torch.isfinite(global_norm)
         clip_norm = red[1].sqrt()
         coef = torch.where(clip_norm < GLOBAL_CLIP, torch.ones_like(clip_norm), GLOBAL_CLIP / clip_norm)
+        if self.before_finish is not None:
+            self.before_finish(is_finite)  # e.g. the pre-apply snapshot of a non-finite step
         if self.skip_nonfinite and not bool(is_finite):
             return self._info(global_norm, is_finite, red, skipped=True)
         for opt in [self] + list(self.partners):

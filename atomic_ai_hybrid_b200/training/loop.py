@@ -387,7 +387,18 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             for db, _, _ in micro:
                 trainer.micro_step(db)
             injector.before_apply(global_step + 1, trainer)
+
+            def pre_apply_snapshot(is_finite, step=global_step + 1):
+                # reference `train.py:963-993`: the parameters and optimizer state from before
+                # the update of a non-finite step (all ranks reach this point together)
+                if not bool(is_finite):
+                    snap_dir = os.path.join(args.ckpt_root, "nonfinite_snapshots", str(step))
+                    CheckpointManager(snap_dir, "state", max_to_keep=1, rank=rank, world=world).save(
+                        step, trainer, {"epoch": epoch, "tag": "NONFINITE_PRE_APPLY"}, asynchronous=False)
+
+            trainer.opt.before_finish = pre_apply_snapshot
             info = trainer.apply(args.accum_steps)
+            trainer.opt.before_finish = None
             global_step += 1
             epoch_tokens += tokens_per_step
             if global_step == 1 and rank == 0 and dev.type == "cuda":
@@ -411,8 +422,6 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                                         f"global_grad_norm > 20 three steps running at step={global_step}")
             if not finite:
                 snap = os.path.join(args.ckpt_root, "nonfinite_snapshots", str(global_step))
-                smgr = CheckpointManager(snap, "state", max_to_keep=1, rank=rank, world=world)
-                smgr.save(global_step, trainer, {"epoch": epoch, "tag": "NONFINITE"}, asynchronous=False)
                 for i, (_, src, hb) in enumerate(micro):
                     np.save(os.path.join(snap, f"micro_{i}_rank{rank}_input_ids.npy"), hb["input_ids"].numpy())
                     np.save(os.path.join(snap, f"micro_{i}_rank{rank}_labels.npy"), hb["labels"].numpy())

@@ -48,6 +48,9 @@ def test_nonfinite_injection_snapshots_and_autostops(tmp_path, monkeypatch):
     snap = tmp_path / "nonfinite_snapshots" / "2"
     meta = json.loads((snap / "SNAPSHOT_META.json").read_text())
     assert meta["n_micro"] == 2 and meta["global_step"] == 2
+    state = json.loads((snap / "state" / "2" / "metadata.json").read_text())
+    # saved before the update of step 2: the optimizer has taken one step
+    assert state["tag"] == "NONFINITE_PRE_APPLY" and state["opt_count"] == 1, state
     assert os.path.exists(tmp_path / "latest" / "5" / "COMMIT")
 
 
