@@ -372,6 +372,10 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 break
             if health is not None:
                 health.check(global_step + 1)
+            # generator states at the start of the step, kept for a non-finite snapshot
+            rng_state = {"cpu": torch.get_rng_state()}
+            if dev.type == "cuda":
+                rng_state["cuda"] = torch.cuda.get_rng_state(dev)
             micro = []
             for _m in range(args.accum_steps):
                 b = next(train_stream)
@@ -422,6 +426,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                                         f"global_grad_norm > 20 three steps running at step={global_step}")
             if not finite:
                 snap = os.path.join(args.ckpt_root, "nonfinite_snapshots", str(global_step))
+                torch.save(rng_state, os.path.join(snap, f"rng_rank{rank}.pt"))
                 for i, (_, src, hb) in enumerate(micro):
                     np.save(os.path.join(snap, f"micro_{i}_rank{rank}_input_ids.npy"), hb["input_ids"].numpy())
                     np.save(os.path.join(snap, f"micro_{i}_rank{rank}_labels.npy"), hb["labels"].numpy())

@@ -51,6 +51,8 @@ def test_nonfinite_injection_snapshots_and_autostops(tmp_path, monkeypatch):
     state = json.loads((snap / "state" / "2" / "metadata.json").read_text())
     # saved before the update of step 2: the optimizer has taken one step
     assert state["tag"] == "NONFINITE_PRE_APPLY" and state["opt_count"] == 1, state
+    import torch
+    assert torch.load(snap / "rng_rank0.pt")["cpu"].dtype == torch.uint8
     assert os.path.exists(tmp_path / "latest" / "5" / "COMMIT")
 
 
