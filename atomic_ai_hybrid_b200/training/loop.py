@@ -179,6 +179,9 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
     return rank, world, 0
 
 
+TIMING_MICRO_STEPS = 30  # micro-steps timed one by one at the start of a run
+
+
 def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> None:
     """The per-GPU memory plan of this layout (the reference prints XLA's memory analysis
     of the compiled step, `train.py:765-772`); informative only."""
@@ -324,6 +327,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     t_start = time.time()
     last_ckpt = time.time()
     eval_no_improve, epochs_no_improve = 0, 0
+    micro_seen = 0
     best_eval = math.inf  # best partial (in-epoch) validation loss
     t_epoch, epoch_tokens = time.time(), 0
     stop_reason = None
@@ -377,6 +381,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
             if dev.type == "cuda":
                 rng_state["cuda"] = torch.cuda.get_rng_state(dev)
             micro = []
+            t_data = time.perf_counter()
             for _m in range(args.accum_steps):
                 b = next(train_stream)
                 src = b.pop("_source_idx", None)
@@ -388,8 +393,22 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 micro.append((_to_device(b, dev), src, b))
             if trainer.cuda_graph and (trainer._graph is None or trainer._graph_key != trainer._key(micro[0][0])):
                 trainer.build_graph(micro[0][0])
+            t_data = (time.perf_counter() - t_data) / len(micro)
             for db, _, _ in micro:
-                trainer.micro_step(db)
+                if rank == 0 and micro_seen < TIMING_MICRO_STEPS:
+                    # reference `train.py:837-874`: the first micro-steps timed on the host
+                    # around a device synchronisation
+                    if dev.type == "cuda":
+                        torch.cuda.synchronize(dev)
+                    t0 = time.perf_counter()
+                    trainer.micro_step(db)
+                    if dev.type == "cuda":
+                        torch.cuda.synchronize(dev)
+                    print(f"[TIMING] micro step {micro_seen}: data={t_data * 1e3:.0f}ms "
+                          f"device={(time.perf_counter() - t0) * 1e3:.0f}ms (accumulating)", flush=True)
+                else:
+                    trainer.micro_step(db)
+                micro_seen += 1
             injector.before_apply(global_step + 1, trainer)
 
             def pre_apply_snapshot(is_finite, step=global_step + 1):
