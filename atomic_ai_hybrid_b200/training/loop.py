@@ -118,9 +118,6 @@ def _dist_setup():
         torch.set_num_threads(max(1, (os.cpu_count() or 1) // max(local, 1)))
     if world > 1 and not dist.is_initialized():
         backend = "nccl" if use_cuda else "gloo"
-        # a timed-out NCCL collective tears the communicator down instead of leaving
-        # the process waiting on it
-        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
         kw = {"device_id": dev} if use_cuda else {}
         timeout = timedelta(seconds=float(os.environ.get("AHB_PG_TIMEOUT_S", "300")))
         dist.init_process_group(backend, timeout=timeout, **kw)
