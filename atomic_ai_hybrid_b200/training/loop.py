@@ -184,9 +184,11 @@ def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> No
     of the compiled step, `train.py:765-772`); informative only."""
     try:
         from ..utils.memplan import plan
-        p = plan(cfg, world=world, micro_batch=micro_batch, seq_len=args.seq_len, tp=max(1, args.tensor_parallel),
-                 ep=max(1, args.expert_parallel), cp=max(1, args.context_parallel), pp=max(1, args.pipeline_parallel),
-                 accum_steps=args.accum_steps, remat=args.remat, schedule=args.pipeline_schedule)
+        with torch.random.fork_rng(devices=[]):  # the planner's model leaves the generators as they were
+            p = plan(cfg, world=world, micro_batch=micro_batch, seq_len=args.seq_len, tp=max(1, args.tensor_parallel),
+                     ep=max(1, args.expert_parallel), cp=max(1, args.context_parallel),
+                     pp=max(1, args.pipeline_parallel), accum_steps=args.accum_steps, remat=args.remat,
+                     schedule=args.pipeline_schedule)
         print(f"[MEMORY] plan per GPU: state {p['state_total_gb']} GB + activations ~{p['activations_gb_est']} GB "
               f"+ reserve {p['reserve_gb']} GB = {p['total_gb']} of {p['hbm_gb']} GB"
               + ("" if p["fits"] else "  -- DOES NOT FIT: reduce the micro-batch or enable --remat"), flush=True)
