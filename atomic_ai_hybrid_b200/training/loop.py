@@ -64,6 +64,8 @@ class TrainArgs:
     source_fractions: List[float] = field(default_factory=list)
     data_mode: str = "mixed"
     val_split: float = 0.05
+    dataset_fraction: float = 1.0  # reference DATASET_FRACTION (global subsample, seeded)
+    fraction_seed: int = 777
     seq_len: int = 512
     global_batch: int = 8          # sequences per micro-step over all data-parallel ranks
     accum_steps: int = 1
@@ -258,8 +260,9 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     steps_per_epoch = None
     if pairs is not None:
         _, _, micro_per_epoch, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
-                                                           mode=args.data_mode, rank=data_rank, world=data_world,
-                                                           pin=False)
+                                                           mode=args.data_mode, dataset_fraction=args.dataset_fraction,
+                                                           fraction_seed=args.fraction_seed, rank=data_rank,
+                                                           world=data_world, pin=False)
         steps_per_epoch = max(1, micro_per_epoch // args.accum_steps)
     total_steps = args.total_steps or (steps_per_epoch * args.epochs if steps_per_epoch else (args.max_steps or 1000))
     if args.pipeline_parallel > 1:
@@ -308,8 +311,9 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                                    data_world)
             return it, None
         it, val_f, _, _ = dataloader_multi_source(pairs, args.global_batch, args.seq_len, args.val_split,
-                                                  skip_batches=skip, mode=args.data_mode, rank=data_rank,
-                                                  world=data_world)
+                                                  skip_batches=skip, mode=args.data_mode,
+                                                  dataset_fraction=args.dataset_fraction,
+                                                  fraction_seed=args.fraction_seed, rank=data_rank, world=data_world)
         return Prefetcher(it), val_f
 
     train_stream, val_factory = make_stream(global_step * args.accum_steps)

@@ -38,6 +38,10 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--log-every", type=int, default=10)
     ap.add_argument("--checkpoint-every-s", type=float, default=95 * 60)
     ap.add_argument("--session-budget-s", type=float, default=9 * 3600 - 300)
+    ap.add_argument("--eval-batches", type=int, default=20, help="batches per partial validation")
+    ap.add_argument("--early-stop-patience", type=int, default=5)
+    ap.add_argument("--val-split", type=float, default=0.05)
+    ap.add_argument("--dataset-fraction", type=float, default=1.0, help="global subsample of the sources")
     ap.add_argument("--no-resume", action="store_true")
     ap.add_argument("--resume-slot", default="latest")
     ap.add_argument("--hf-repo-id", default=None, help="mirror checkpoints to this Hub model repo ($HF_REPO_ID)")
@@ -82,7 +86,9 @@ def parse(argv=None) -> TrainArgs:
                      skip_nonfinite=a.skip_nonfinite, seed=a.seed, tensor_parallel=a.tp, expert_parallel=a.ep,
                      remat=a.remat, reset_router=a.reset_router, context_parallel=a.cp,
                      pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule, hf_repo_id=a.hf_repo_id,
-                     hf_bucket_id=a.hf_bucket_id, resume_source=a.resume_source)
+                     hf_bucket_id=a.hf_bucket_id, resume_source=a.resume_source, eval_batches=a.eval_batches,
+                     early_stop_patience=a.early_stop_patience, val_split=a.val_split,
+                     dataset_fraction=a.dataset_fraction)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
