@@ -45,6 +45,7 @@ from ..models import HybridMoEModel
 from ..optim.schedule import DIAG_GROUPS
 from ..utils import wandb_logging
 from ..utils.health import PeerFailure, PeerHealth
+from ..utils.phase_timer import PhaseTimer
 from ..utils.monitor import (SESSION_TIME_BUDGET_SECONDS, BurstGuard, FaultInjector, NonFiniteMonitor,
                              StopSignals)
 from .metrics import model_metrics, step_metrics
@@ -331,6 +332,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     last_ckpt = time.time()
     eval_no_improve, epochs_no_improve = 0, 0
     micro_seen = 0
+    timer = PhaseTimer(dev)
     best_eval = math.inf  # best partial (in-epoch) validation loss
     t_epoch, epoch_tokens = time.time(), 0
     stop_reason = None
@@ -385,6 +387,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 rng_state["cuda"] = torch.cuda.get_rng_state(dev)
             micro = []
             t_data = time.perf_counter()
+            data_phase = timer.phase("data", host=True)
+            data_phase.__enter__()
             for _m in range(args.accum_steps):
                 b = next(train_stream)
                 src = b.pop("_source_idx", None)
@@ -396,7 +400,10 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 micro.append((_to_device(b, dev), src, b))
             if trainer.cuda_graph and (trainer._graph is None or trainer._graph_key != trainer._key(micro[0][0])):
                 trainer.build_graph(micro[0][0])
+            data_phase.__exit__(None, None, None)
             t_data = (time.perf_counter() - t_data) / len(micro)
+            compute_phase = timer.phase("compute")
+            compute_phase.__enter__()
             for db, _, _ in micro:
                 if rank == 0 and micro_seen < TIMING_MICRO_STEPS:
                     # reference `train.py:837-874`: the first micro-steps timed on the host
@@ -412,6 +419,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 else:
                     trainer.micro_step(db)
                 micro_seen += 1
+            compute_phase.__exit__(None, None, None)
             injector.before_apply(global_step + 1, trainer)
 
             def pre_apply_snapshot(is_finite, step=global_step + 1):
@@ -423,8 +431,10 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                         step, trainer, {"epoch": epoch, "tag": "NONFINITE_PRE_APPLY"}, asynchronous=False)
 
             trainer.opt.before_finish = pre_apply_snapshot
-            info = trainer.apply(args.accum_steps)
+            with timer.phase("apply"):
+                info = trainer.apply(args.accum_steps)
             trainer.opt.before_finish = None
+            timer.end_step()
             global_step += 1
             epoch_tokens += tokens_per_step
             if global_step == 1 and rank == 0 and dev.type == "cuda":
@@ -467,12 +477,16 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
                 done = True
                 break
             steps_since_log += 1
+            phases = timer.report() if global_step % args.log_every == 0 else None  # every rank: one all-reduce
             if rank == 0 and global_step % args.log_every == 0:
                 dt = time.time() - t_log
                 tps = tokens_per_step * steps_since_log / max(dt, 1e-9)
                 print(f"[step {global_step}] loss={loss_val:.4f} gnorm={gnorm:.3f} tok/s={tps:.0f}", flush=True)
                 sm, lines, alerts = step_metrics(global_step, loss_val, trainer.last_info, best_train, tps, epoch,
                                                  cfg.num_experts)
+                lines.insert(0, "phases (ms per step, max over ranks): "
+                             + " ".join(f"{k}={v:.1f}" for k, v in phases.items()))
+                sm.update({f"timing/{k}_ms": v for k, v in phases.items()})
                 for line in lines:
                     print("           " + line, flush=True)
                 for title, text in alerts:

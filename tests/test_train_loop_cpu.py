@@ -335,3 +335,38 @@ def test_epoch_end_validation_and_save(tmp_path, capsys):
     assert out.count("[EPOCH]") == 4 and "mean validation loss" in out, out[-2000:]
     assert s["global_step"] > 0 and s["best_val"] < float("inf")
     assert os.listdir(tmp_path / "ck" / "best_val")
+
+
+def _timer_rank(rank, world, port, q):
+    import time as _t
+    import torch.distributed as dist
+    from atomic_ai_hybrid_b200.utils.phase_timer import PhaseTimer
+    import torch
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        t = PhaseTimer(torch.device("cpu"))
+        for _ in range(2):
+            with t.phase("compute"):
+                _t.sleep(0.02 * (rank + 1))
+            t.end_step()
+        q.put((rank, t.report()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_phase_timer_reports_max_over_ranks():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_timer_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    # both ranks report the slower rank's per-step time (40 ms)
+    assert got[0] == got[1] and 38.0 < got[0]["compute"] < 80.0, got
