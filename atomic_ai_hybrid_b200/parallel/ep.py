@@ -249,3 +249,28 @@ def moe_forward_ep_collective(x, top_idx, gate, w1, w2, w3, act: str, group, wor
     out_rows = dfn.all_to_all_single(back.new_empty((T * k, back.shape[1])), back, send, recv, group=group)
     y = torch.empty_like(out_rows).index_copy(0, order, out_rows)  # assignment order t * k + j
     return (y.view(T, k, -1) * gate.float().unsqueeze(-1)).sum(1)
+
+
+def init_expert_parallel(ep_size: int):
+    """Expert-parallel groups of ``ep_size`` consecutive ranks; with ``ep_size < world`` the
+    ``world / ep_size`` groups are data-parallel replicas of one another: every rank reads
+    its own tokens, the routed experts are split within a group, and the gradients of a
+    block of experts are summed over the ranks that hold the same block (``local_group``)
+    before the step.  Installs the layout in the parallel context and returns it."""
+    from .context import ParallelContext, set_parallel_context
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if world % ep_size:
+        raise ValueError(f"{world} ranks do not split into expert-parallel groups of {ep_size}")
+    ctx = ParallelContext(dp_world=world, ep_world=ep_size, ep_rank=rank % ep_size)
+    if ep_size < world:
+        reps = world // ep_size
+        for i in range(reps):  # every rank creates every group, in the same order
+            g = dist.new_group(list(range(i * ep_size, (i + 1) * ep_size)))
+            if i == rank // ep_size:
+                ctx.ep_group = g
+        for j in range(ep_size):
+            g = dist.new_group([j + i * ep_size for i in range(reps)])
+            if j == rank % ep_size:
+                ctx.local_group = g
+    set_parallel_context(ctx)
+    return ctx

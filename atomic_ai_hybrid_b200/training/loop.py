@@ -171,10 +171,10 @@ def _parallel_setup(args: TrainArgs, cfg, rank: int, world: int, dev):
         init_tensor_parallel(tp, dev, expert_parallel=ep > 1, max_rows=rows, max_width=cfg.d_model)
         return rank // tp, dp_world, rows if ep > 1 else 0
     if ep > 1:
-        if ep != world:
-            raise ValueError("without tensor parallelism, expert parallelism spans all ranks (ep == world)")
-        from ..parallel.context import ParallelContext, set_parallel_context
-        set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
+        if world % ep:
+            raise ValueError(f"expert parallelism over groups of {ep} does not divide {world} ranks")
+        from ..parallel.ep import init_expert_parallel
+        init_expert_parallel(ep)
         return rank, world, args.global_batch // world * args.seq_len
     return rank, world, 0
 

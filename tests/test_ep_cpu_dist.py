@@ -28,7 +28,7 @@ def _cfg(world=2):
                       n_heads=2, n_heads_ssm=2, d_ff=128, n_routed_experts=max(4, world), top_k=2, d_state=32)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, ep=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # no oversubscription of the cores
@@ -44,7 +44,8 @@ def _worker(rank, world, port, q):
         lf.backward()
         gf = {n: p.grad.clone() for n, p in full.named_parameters() if p.grad is not None}
         # experts split over the ranks, each rank on its own 2 sequences (data parallel)
-        set_parallel_context(ParallelContext(dp_world=world, ep_world=world, ep_rank=rank))
+        from atomic_ai_hybrid_b200.parallel.ep import init_expert_parallel
+        ctx = init_expert_parallel(ep or world)
         torch.manual_seed(0)
         m = HybridMoEModel(cfg, compute_dtype=torch.float32)
         mine = ids[2 * rank:2 * rank + 2]
@@ -55,13 +56,17 @@ def _worker(rank, world, port, q):
         dist.all_reduce(lt)
         res = {"loss": float((lt / world - lf).abs() / lf.abs())}
         worst, which = 0.0, None
-        El = cfg.e_routed // world
+        ep = ep or world
+        El = cfg.e_routed // ep
+        er = rank % ep
         for n, p in m.named_parameters():
             if p.grad is None:
                 continue
             g = p.grad.clone()
             if getattr(p, "_ahb_ep_local", False):
-                ref = gf[n][rank * El:(rank + 1) * El]
+                if ctx.local_group is not None:  # the replicas holding the same experts
+                    dist.all_reduce(g, group=ctx.local_group)
+                ref = gf[n][er * El:(er + 1) * El]
                 got = g / world            # summed over every rank's tokens; the reference is their mean
             else:
                 dist.all_reduce(g)
@@ -76,13 +81,14 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_collective_matches_single_rank(world):
-    """2, 4 and 8 ranks (8 routed experts at 8 ranks: one per rank)."""
+@pytest.mark.parametrize("world,ep", [(2, 2), (4, 4), (8, 8), (4, 2)])
+def test_ep_collective_matches_single_rank(world, ep):
+    """2, 4 and 8 ranks (8 routed experts at 8 ranks: one per rank); and two data-parallel
+    replicas of a 2-rank expert-parallel group."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, ep)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

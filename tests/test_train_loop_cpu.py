@@ -180,21 +180,23 @@ def _ep_rank_main(rank, world, port, tmp):
                       LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
     _write_data(tmp)
     out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], expert_parallel=2, max_steps=2,
-                               checkpoint_every_s=0.0))
+                               checkpoint_every_s=0.0, global_batch=world))
     with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
         json.dump({k: v for k, v in out.items() if k != "losses"}, f)
 
 
-def test_training_loop_with_expert_parallelism(tmp_path):
-    """train.py's loop with --ep 2 on two gloo ranks (all-to-all path): it trains and the
-    checkpoint holds each rank's block of experts."""
+@pytest.mark.parametrize("world", [2, 4])
+def test_training_loop_with_expert_parallelism(tmp_path, world):
+    """train.py's loop with --ep 2 on two gloo ranks (all-to-all path), and on four (two
+    data-parallel replicas of the expert-parallel pair): it trains and the checkpoint holds
+    each rank's block of experts."""
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    mp.spawn(_ep_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True)
-    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(2)]
-    assert outs[0]["global_step"] == 2 and outs[1]["global_step"] == 2, outs
+    mp.spawn(_ep_rank_main, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    outs = [json.load(open(os.path.join(tmp_path, f"out{r}.json"))) for r in range(world)]
+    assert all(o["global_step"] == 2 for o in outs), outs
     from atomic_ai_hybrid_b200.ckpt.safetensors_io import load_file
     root = os.path.join(tmp_path, "latest")
     step = max((d for d in os.listdir(root) if d.isdigit()), key=int)
