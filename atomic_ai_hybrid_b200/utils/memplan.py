@@ -23,8 +23,8 @@ the trainer would build, and adds an activation estimate:
   parallelism divide the tokens a rank holds; a 1F1B stage ``s`` of ``S`` keeps up to
   ``S - s`` micro-batches (GPipe: all of them).
 
-``python -m atomic_ai_hybrid_b200.utils.memplan --config atomic_ai_hybrid_b200/configs/config5_hybrid_long_tp8.yaml --world 8``
-prints the plan as JSON; ``fits`` compares the total with the B200's memory.
+``python -m atomic_ai_hybrid_b200.utils.memplan --config <run file> --world 8`` (run files in
+``atomic_ai_hybrid_b200/configs``) prints the plan as JSON; ``fits`` compares the total with the B200's memory.
 """
 from __future__ import annotations
 

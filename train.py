@@ -55,7 +55,9 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (heads split, tokens split "
                                                         "between the mixers)")
-    ap.add_argument("--ep", type=int, default=1, help="expert-parallel group size (== --tp with --tp; otherwise any size dividing the world, world / ep replicas)")
+    ap.add_argument("--ep", type=int, default=1,
+                    help="expert-parallel group size (== --tp with --tp; otherwise any size dividing the world, "
+                         "world / ep replicas)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
     ap.add_argument("--cp", type=int, default=1,
                     help="context-parallel group size (sequence segments); world / cp data-parallel replicas")
