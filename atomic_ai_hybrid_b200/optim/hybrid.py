@@ -65,7 +65,7 @@ class HybridOptimizer:
     def __init__(self, store: FlatParamStore, total_steps: int,
                  reduce_fn: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
                  skip_nonfinite: bool = False, muon_lr: float = 0.008, lion_lr: float = 2e-4,
-                 adamw_lr: float = 6e-4):
+                 adamw_lr: float = 6e-4, offload_moments: bool = False):
         self.store = store
         self.schedule = LRSchedule(total_steps)
         self.reduce_fn = reduce_fn or (lambda t: t)
@@ -76,8 +76,15 @@ class HybridOptimizer:
         self.base = {"muon": muon_lr, "lion": lion_lr, "adamw_decay": adamw_lr, "adamw_nodecay": adamw_lr}
         self.count = 0
         dev = store.device
-        self.m = torch.zeros(store.shard, dtype=torch.float32, device=dev)
-        self.v = torch.zeros(store.shard, dtype=torch.float32, device=dev)
+        # ``offload_moments``: the two moments live in (pinned) host memory and each
+        # tensor's slice is staged to the device for its update and written back: 8 bytes
+        # per parameter leave the GPU for two PCIe copies per step (the update then runs
+        # as PyTorch ops, not the fused kernel)
+        self.offload = bool(offload_moments)
+        host = self.offload and dev.type == "cuda"
+        mdev = torch.device("cpu") if host else dev
+        self.m = torch.zeros(store.shard, dtype=torch.float32, device=mdev, pin_memory=host)
+        self.v = torch.zeros(store.shard, dtype=torch.float32, device=mdev, pin_memory=host)
         self.owned = store.owned()
         self.group_idx = {g: i for i, g in enumerate(DIAG_GROUPS)}
         # (gradient peer table, compute peer table): set by a peer-memory shard comm
@@ -88,6 +95,8 @@ class HybridOptimizer:
         self.norm_share = 1.0
 
     def uses_kernels(self) -> bool:
+        if self.offload:
+            return False
         gbuf = self.store.grad
         if not ops.use_cuda(gbuf):
             return False
@@ -179,7 +188,20 @@ class HybridOptimizer:
         else:
             self._apply_eager(lrs, coef, gbuf, assignment_frac)
             st.publish_owned()
+            if self.offload and self.m.device != st.device:
+                # the host moments are read by checkpoints on the host: the write-backs land first
+                torch.cuda.current_stream(st.device).synchronize()
         self.count += 1
+
+    def _stage(self, buf: torch.Tensor, sl: slice, dev: torch.device) -> torch.Tensor:
+        """The slice of a moment buffer on ``dev`` (a view when it is there already)."""
+        t = buf[sl]
+        return t if t.device == dev else t.to(dev, non_blocking=True)
+
+    @staticmethod
+    def _unstage(buf: torch.Tensor, sl: slice, t: torch.Tensor) -> None:
+        if buf.device != t.device:  # stream-ordered: the next stage of this slice follows it
+            buf[sl].copy_(t, non_blocking=True)
 
     def _apply_eager(self, lrs, coef, gbuf, assignment_frac):
         st = self.store
@@ -196,19 +218,22 @@ class HybridOptimizer:
                 p.add_(-lr * gbuf[sl] - lr * 0.01 * p)
             elif lab == "lion" and s.param.requires_grad:
                 g = gbuf[sl] * coef
-                m = self.m[sl]
+                m = self._stage(self.m, sl, p.device)
                 upd = torch.sign(0.1 * g + 0.9 * m) + 0.1 * p
                 m.mul_(0.99).add_(0.01 * g)
                 p.add_(-lr * upd)
+                self._unstage(self.m, sl, m)
             elif lab.startswith("adamw"):
                 g = gbuf[sl] * coef if s.param.requires_grad else torch.zeros_like(p)
-                m, v = self.m[sl], self.v[sl]
+                m, v = self._stage(self.m, sl, p.device), self._stage(self.v, sl, p.device)
                 m.mul_(0.9).add_(0.1 * g)
                 v.mul_(0.999).add_(0.001 * g * g)
                 upd = (m / bc1) / ((v / bc2).sqrt() + 1e-8)
                 if lab == "adamw_decay":
                     upd = upd + 0.01 * p
                 p.add_(-lr * upd)
+                self._unstage(self.m, sl, m)
+                self._unstage(self.v, sl, v)
             p.copy_(torch.nan_to_num(p.clamp(-PARAM_CLIP, PARAM_CLIP), nan=0.0, posinf=PARAM_CLIP,
                                      neginf=-PARAM_CLIP))
             key = path_key(s.name)

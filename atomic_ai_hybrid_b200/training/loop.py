@@ -105,6 +105,9 @@ class TrainArgs:
     reset_router: bool = False     # re-draw the routers after a restore (reference RESET_ROUTER_ON_RESUME)
     pipeline_parallel: int = 1     # contiguous layer stages (parallel.pp); world / stages data-parallel replicas
     pipeline_schedule: str = "1f1b"  # or "gpipe"
+    # AdamW moments of the rank-local parameters (expert blocks, tensor-parallel pieces) in
+    # host memory: 8 bytes per such parameter off the GPU (configuration 5 needs it)
+    offload_local_moments: bool = False
 
 
 def _dist_setup():
@@ -191,7 +194,7 @@ def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> No
             p = plan(cfg, world=world, micro_batch=micro_batch, seq_len=args.seq_len, tp=max(1, args.tensor_parallel),
                      ep=max(1, args.expert_parallel), cp=max(1, args.context_parallel),
                      pp=max(1, args.pipeline_parallel), accum_steps=args.accum_steps, remat=args.remat,
-                     schedule=args.pipeline_schedule)
+                     schedule=args.pipeline_schedule, local_moments_on_host=args.offload_local_moments)
         print(f"[MEMORY] plan per GPU: state {p['state_total_gb']} GB + activations ~{p['activations_gb_est']} GB "
               f"+ reserve {p['reserve_gb']} GB = {p['total_gb']} of {p['hbm_gb']} GB"
               + ("" if p["fits"] else "  -- DOES NOT FIT: reduce the micro-batch or enable --remat"), flush=True)
@@ -275,7 +278,7 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     else:
         trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
                           cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
-                          ep_max_tokens=ep_tokens)
+                          ep_max_tokens=ep_tokens, offload_local_moments=args.offload_local_moments)
 
     if rank == 0 and dev.type == "cuda":
         _print_memory_plan(args, cfg, world, per_rank)

@@ -35,7 +35,8 @@ class Trainer:
                  compute_dtype: torch.dtype = torch.bfloat16, device=None,
                  group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
                  ce_chunk_size: int = 2048, collinearity_coef: Optional[float] = None,
-                 skip_nonfinite: bool = False, cuda_graph: bool = False, ep_max_tokens: int = 0):
+                 skip_nonfinite: bool = False, cuda_graph: bool = False, ep_max_tokens: int = 0,
+                 offload_local_moments: bool = False):
         self.model = model
         self.cfg = model.cfg
         self.group = group
@@ -69,7 +70,8 @@ class Trainer:
                                    skip_nonfinite=skip_nonfinite)
         self.ep_opt = None
         if self.ep_store is not None:
-            self.ep_opt = HybridOptimizer(self.ep_store, total_steps)
+            # ``offload_local_moments``: the rank-local parameters' AdamW moments in host memory
+            self.ep_opt = HybridOptimizer(self.ep_store, total_steps, offload_moments=offload_local_moments)
             self.ep_opt.schedule = self.opt.schedule  # one learning-rate schedule for both stores
             if self.local_group is not None:
                 # every replica adds the same statistics to the cross-rank sum

@@ -40,7 +40,7 @@ ACT_BYTES_PER_TOKEN_LAYER_D = 81.0     # calibrated on the 1-GPU benchmark step 
 
 
 def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torch.dtype,
-                  local_grad_bytes: int = 4) -> Dict[str, float]:
+                  local_grad_bytes: int = 4, local_moments_on_host: bool = False) -> Dict[str, float]:
     from ..optim import FlatParamStore, grad_scale_of, label_adamw_only
     from ..optim.store import is_ep_local
     named = list(module.named_parameters())
@@ -64,7 +64,8 @@ def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torc
         out["master"] += 4.0 * st.shard
         out["grad"] += float(local_grad_bytes) * st.numel
         out["compute"] += 2.0 * st.cnumel
-        out["optimizer"] += 8.0 * st.shard
+        if not local_moments_on_host:
+            out["optimizer"] += 8.0 * st.shard
     return out
 
 
@@ -80,7 +81,8 @@ def activation_bytes(cfg, micro_batch: int, seq_len: int, layers: int, tp: int =
 
 def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int = 1, ep: int = 1, cp: int = 1,
          pp: int = 1, accum_steps: int = 1, remat: bool = False, schedule: str = "1f1b",
-         compute_dtype: torch.dtype = torch.bfloat16, local_grad_bytes: int = 4) -> Dict:
+         compute_dtype: torch.dtype = torch.bfloat16, local_grad_bytes: int = 4,
+         local_moments_on_host: bool = False) -> Dict:
     """Memory of the most loaded rank of a layout, in bytes and GB (1e9)."""
     from ..models import HybridMoEModel
     from ..parallel.context import ParallelContext, get_parallel_context, set_parallel_context
@@ -99,14 +101,14 @@ def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int
         best = None
         for s in range(pp):
             part = PipelineStage(model, pp, s)
-            b = _stores_bytes(part, world // pp, compute_dtype, local_grad_bytes)
+            b = _stores_bytes(part, world // pp, compute_dtype, local_grad_bytes, local_moments_on_host)
             tot = b["master"] + b["grad"] + b["compute"] + b["optimizer"]
             if best is None or tot > best[0]:
                 best = (tot, b, s, len(part.layer_ids))
         _, state, stage, layers = best
         in_flight = min(pp - stage, accum_steps) if schedule == "1f1b" else accum_steps
     else:
-        state = _stores_bytes(model, world, compute_dtype, local_grad_bytes)
+        state = _stores_bytes(model, world, compute_dtype, local_grad_bytes, local_moments_on_host)
         layers, in_flight, stage = cfg.num_layers, 1, None
     act = activation_bytes(cfg, micro_batch, seq_len, layers, tp, cp, in_flight, remat)
     state_total = state["master"] + state["grad"] + state["compute"] + state["optimizer"]
@@ -134,6 +136,8 @@ def main(argv: Optional[list] = None) -> Dict:
         ap.add_argument(f"--{k}", type=int, default=None)
     ap.add_argument("--remat", action="store_true", default=None)
     ap.add_argument("--local-grad-bytes", type=int, default=4, help="gradient bytes of rank-local parameters")
+    ap.add_argument("--offload-local-moments", action="store_true", default=None,
+                    help="AdamW moments of rank-local parameters in host memory")
     a = ap.parse_args(argv)
     train: Dict = {}
     if a.config:
@@ -154,7 +158,9 @@ def main(argv: Optional[list] = None) -> Dict:
     out = plan(cfg, world=world, micro_batch=mb, seq_len=a.seq_len or train.get("seq_len", 4096), tp=tp, ep=ep,
                cp=cp, pp=pp, accum_steps=train.get("accum_steps", 1),
                remat=bool(a.remat if a.remat is not None else train.get("remat", False)),
-               local_grad_bytes=a.local_grad_bytes)
+               local_grad_bytes=a.local_grad_bytes,
+               local_moments_on_host=bool(a.offload_local_moments if a.offload_local_moments is not None
+                                          else train.get("offload_local_moments", False)))
     print(json.dumps(out))
     return out
 

@@ -61,12 +61,47 @@ def test_benchmark_config_plans():
 
 
 def test_run_files_for_eight_gpus():
-    """The 8-GPU run files: configurations 3 and 4 fit as written; configuration 5 needs
-    16-bit gradients for its rank-local parameters (see ``test_benchmark_config_plans``)."""
+    """The 8-GPU run files fit as written (configuration 5 with its rank-local AdamW
+    moments in host memory; without that it does not: ``test_benchmark_config_plans``)."""
     import os
     root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "atomic_ai_hybrid_b200",
                         "configs")
     for name, fits in (("config3_hybrid_1b.yaml", True), ("config4_hybrid_7b_ep8.yaml", True),
-                       ("config5_hybrid_long_tp8.yaml", False)):
+                       ("config5_hybrid_long_tp8.yaml", True)):
         out = memplan.main(["--config", os.path.join(root, name), "--world", "8"])
         assert out["fits"] is fits, (name, out)
+
+
+def test_offloaded_moments_train_like_device_moments(tmp_path):
+    """``offload_moments``: the same updates and moments as device-resident ones, no fused
+    kernel, and the moments save to / restore from checkpoints."""
+    from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
+    from atomic_ai_hybrid_b200.optim import FlatParamStore, HybridOptimizer, grad_scale_of, label_adamw_only
+    cfg = _cfg()
+    outs = []
+    for offload in (False, True):
+        torch.manual_seed(0)
+        m = HybridMoEModel(cfg, compute_dtype=torch.float32)
+        st = FlatParamStore(m, label_adamw_only, grad_scale_of, 1, 0, compute_dtype=torch.float32,
+                            device=torch.device("cpu"))
+        opt = HybridOptimizer(st, 10, offload_moments=offload)
+        opt.schedule.warmup = 1
+        g = torch.Generator().manual_seed(3)
+        for _ in range(3):
+            st.grad.copy_(torch.randn(st.grad.shape, generator=g) * 1e-3)
+            opt.step(1)
+        assert opt.uses_kernels() is False
+        outs.append((st.master.clone(), opt.m.clone(), opt.v.clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+    class _T:  # the two attributes a checkpoint reads
+        pass
+    t = _T()
+    t.store, t.opt = st, opt
+    CheckpointManager(str(tmp_path), "latest").save(3, t, asynchronous=False)
+    m2 = opt.m.clone()
+    opt.m.zero_()
+    opt.v.zero_()
+    CheckpointManager(str(tmp_path), "latest").restore(3, t)
+    assert torch.equal(opt.m, m2)

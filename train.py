@@ -59,6 +59,8 @@ def parse(argv=None) -> TrainArgs:
                     help="expert-parallel group size (== --tp with --tp; otherwise any size dividing the world, "
                          "world / ep replicas)")
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
+    ap.add_argument("--offload-local-moments", action="store_true",
+                    help="AdamW moments of expert blocks / tensor-parallel pieces in host memory")
     ap.add_argument("--cp", type=int, default=1,
                     help="context-parallel group size (sequence segments); world / cp data-parallel replicas")
     ap.add_argument("--pp", type=int, default=1,
@@ -90,7 +92,7 @@ def parse(argv=None) -> TrainArgs:
                      pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule, hf_repo_id=a.hf_repo_id,
                      hf_bucket_id=a.hf_bucket_id, resume_source=a.resume_source, eval_batches=a.eval_batches,
                      early_stop_patience=a.early_stop_patience, val_split=a.val_split,
-                     dataset_fraction=a.dataset_fraction)
+                     dataset_fraction=a.dataset_fraction, offload_local_moments=a.offload_local_moments)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
