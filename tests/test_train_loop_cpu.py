@@ -160,7 +160,7 @@ def test_router_reset_touches_only_router_leaves():
     for n, p in m.named_parameters():
         if n in changed:
             if n.endswith("router_temp"):
-                assert float(p) == 10.0
+                assert float(p.detach()) == 10.0
             else:
                 assert not torch.equal(p, before[n]) and abs(float(p.detach().std()) - 0.02) < 0.01
         else:
