@@ -667,6 +667,8 @@ extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A
             chunk_heads, (unsigned)AHB_SSD_NOALLOC_MAX_CHUNK_HEADS, (unsigned)AHB_SSD_NOALLOC_SCRATCH_BYTES);
     return AHB_NOALLOC_ETOOBIG;
   }
+  // an error left pending by earlier work is reported, not cleared: it is not this call's
+  if (cudaPeekAtLastError() != cudaSuccess) return AHB_NOALLOC_EPENDING;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AHB_NOALLOC_ESETUP;
   void* base = nullptr;
@@ -687,11 +689,15 @@ extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A
   float* state_buf = static_cast<float*>(base);
   float* cuml = state_buf + chunk_heads * (unsigned long long)(P * N);
   const int G = head_groups(H);
+  // no error was pending on entry, so a failure seen after a launch is that launch's own
   ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
                                                                      (const bf16*)Bm, L, H, state_buf, cuml);
+  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
   ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, stream>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
   ssd_out_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
                                                                  (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
                                                                  (bf16*)y);
-  return cudaGetLastError() == cudaSuccess ? AHB_NOALLOC_OK : AHB_NOALLOC_ELAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
+  return AHB_NOALLOC_OK;
 }

@@ -28,7 +28,8 @@
 #define AHB_NOALLOC_EINVAL -1   // null pointer or invalid shape
 #define AHB_NOALLOC_ETOOBIG -2  // problem needs more scratch than the fixed array holds
 #define AHB_NOALLOC_ESETUP -3   // device query / symbol lookup failed
-#define AHB_NOALLOC_ELAUNCH -4  // a kernel launch failed
+#define AHB_NOALLOC_ELAUNCH -4  // a kernel launch of this call failed
+#define AHB_NOALLOC_EPENDING -5  // a CUDA error from earlier work was pending on entry (left uncleared)
 #define AHB_SSD_NOALLOC_SCRATCH_BYTES (32u << 20)
 #define AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (AHB_SSD_NOALLOC_SCRATCH_BYTES / ((64u * 128u + 64u) * 4u))
 

@@ -17,8 +17,6 @@ NVCC = [
     "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v" if os.environ.get("AHB_PTXAS_V") else "-DAHB_QUIET",
     "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
-if os.environ.get("AHB_BOUNDS_CHECK"):
-    NVCC.append("-DAHB_BOUNDS_CHECK")
 
 setup(
     name="atomic_ai_hybrid_b200",
