@@ -162,54 +162,78 @@ GdnShapes gdn_shapes(const torch::Tensor& q) {
   return {B, L, H, L / 64};
 }
 
+torch::Tensor& err_word();
+
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, "atomic_ai_hybrid_b200: ", what, " failed with code ", rc);
+  check_launch(what);
+}
+
+// Chunk intermediates of the forward: tile images wt, u, qg, kg (B,H,NC,64,128) and aqk
+// (B,H,NC,64,64) bf16, gcl (B,H,NC,128) fp32, and A (B,H,NC,64,64) fp32 when `want_a`.
+struct GdnChunk { torch::Tensor wt, u, qg, kg, aqk, gcl, A; };
+
+GdnChunk gdn_chunk(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& g,
+                   const torch::Tensor& bg, const torch::Tensor& wg, float scale, bool want_a) {
+  auto s = gdn_shapes(q);
+  auto bf = q.options();
+  auto f32 = q.options().dtype(at::kFloat);
+  GdnChunk c;
+  c.wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
+  c.u = torch::empty_like(c.wt);
+  c.qg = torch::empty_like(c.wt);
+  c.kg = torch::empty_like(c.wt);
+  c.aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, bf);
+  c.gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
+  if (want_a) c.A = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  check_rc(ahb_gdn_chunk_fwd_tc(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(),
+                                wg.data_ptr(), scale, s.B, s.L, s.H, c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(),
+                                c.kg.data_ptr(), c.aqk.data_ptr(), c.gcl.data_ptr<float>(),
+                                want_a ? c.A.data_ptr<float>() : nullptr, err_word().data_ptr<int>(), cur_stream()),
+           "ahb_gdn_chunk_fwd_tc");
+  return c;
+}
+
 std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                    torch::Tensor bg, torch::Tensor wg, double scale, bool want_state) {
   for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
   check_gdn(g, at::kFloat, "g");
   auto s = gdn_shapes(q);
-  auto bf = q.options();
-  auto f32 = q.options().dtype(at::kFloat);
-  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
-  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
-  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
-  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
-  auto st = cur_stream();
-  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
-                    (float)scale, s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(),
-                    aqk.data_ptr<float>(), gcl.data_ptr<float>(), nullptr, st);
-  check_launch("ahb_gdn_intra_fwd");
+  auto c = gdn_chunk(q, k, v, g, bg, wg, (float)scale, false);
   auto o = torch::empty_like(q);
   torch::Tensor hf;
-  if (want_state) hf = torch::empty({s.B, s.H, 128, 128}, f32);
-  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(),
-                    want_state ? hf.data_ptr<float>() : nullptr, nullptr, nullptr, st);
-  check_launch("ahb_gdn_inter_fwd");
+  if (want_state) hf = torch::empty({s.B, s.H, 128, 128}, q.options().dtype(at::kFloat));
+  check_rc(ahb_gdn_state_fwd_tc(c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(), c.kg.data_ptr(), c.aqk.data_ptr(),
+                                c.gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(),
+                                want_state ? hf.data_ptr<float>() : nullptr, nullptr, nullptr,
+                                err_word().data_ptr<int>(), cur_stream()),
+           "ahb_gdn_state_fwd_tc");
   if (want_state) return {o, hf};
   return {o};
 }
 
 // Backward from the chunk intermediates of the forward (wt, qg, kg, aqk, gcl, A and the
-// per-chunk states hs / vn): inter-chunk reverse scan, then the chunk-local backward.
+// per-chunk states hs / vn): reverse state recurrence, then the chunk-local backward.
 static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                                const torch::Tensor& g, const torch::Tensor& bg,
                                                const torch::Tensor& wg, const torch::Tensor& doc, float sc,
                                                torch::Tensor wt, torch::Tensor qg, torch::Tensor kg,
-                                               const torch::Tensor& aqk, const torch::Tensor& gcl,
+                                               torch::Tensor aqk, const torch::Tensor& gcl,
                                                const torch::Tensor& A, torch::Tensor hs, torch::Tensor vn) {
   auto s = gdn_shapes(q);
   auto f32 = q.options().dtype(at::kFloat);
   auto st = cur_stream();
   auto dhs = torch::empty_like(hs);
-  auto dvn = torch::empty_like(wt);
-  ahb_gdn_inter_bwd(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(), gcl.data_ptr<float>(),
-                    doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr, st);
-  check_launch("ahb_gdn_inter_bwd");
-  qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor();
+  auto dvn = torch::empty({s.B, s.H, s.NC, 64, 128}, q.options());
+  check_rc(ahb_gdn_state_bwd_tc(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr(), gcl.data_ptr<float>(),
+                                doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr,
+                                err_word().data_ptr<int>(), st),
+           "ahb_gdn_state_bwd_tc");
+  qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor(); aqk = torch::Tensor();
   auto dq_p = torch::empty({s.B, s.H, s.NC, 64, 128}, f32);
   auto dk_p = torch::empty_like(dq_p), dgc_p = torch::empty_like(dq_p), dwt = torch::empty_like(dq_p);
   auto dgcl = torch::empty_like(gcl);
-  auto daqk = torch::empty_like(aqk);
+  auto daqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
   ahb_gdn_bwd_states(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), doc.data_ptr(), hs.data_ptr(), dhs.data_ptr(),
                      vn.data_ptr(), dvn.data_ptr(), sc, s.B, s.L, s.H, dq_p.data_ptr<float>(),
                      dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(), dwt.data_ptr<float>(), dgcl.data_ptr<float>(),
@@ -218,7 +242,7 @@ static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const tor
   hs = torch::Tensor(); dhs = torch::Tensor(); vn = torch::Tensor();
   auto dv = torch::empty_like(q), dw = torch::empty_like(q);
   auto dbk_wy = torch::empty_like(dq_p), dgc_wy = torch::empty_like(dq_p);
-  auto dakk = torch::empty_like(aqk);
+  auto dakk = torch::empty_like(daqk);
   ahb_gdn_bwd_wy(k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), A.data_ptr<float>(),
                  dvn.data_ptr(), dwt.data_ptr<float>(), s.B, s.L, s.H, dv.data_ptr(), dw.data_ptr(),
                  dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dakk.data_ptr<float>(), st);
@@ -233,33 +257,28 @@ static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const tor
   return {dq, dk, dv, dg, db, dw};
 }
 
+static void gdn_states(const GdnChunk& c, const torch::Tensor& q, float sc, torch::Tensor* o, torch::Tensor& hs,
+                       torch::Tensor& vn) {
+  auto s = gdn_shapes(q);
+  hs = torch::empty({s.B, s.H, s.NC, 128, 128}, q.options());
+  vn = torch::empty({s.B, s.H, s.NC, 64, 128}, q.options());
+  check_rc(ahb_gdn_state_fwd_tc(c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(), c.kg.data_ptr(), c.aqk.data_ptr(),
+                                c.gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, o ? o->data_ptr() : nullptr,
+                                nullptr, hs.data_ptr(), vn.data_ptr(), err_word().data_ptr<int>(), cur_stream()),
+           "ahb_gdn_state_fwd_tc");
+}
+
 // Forward for training: also returns the chunk intermediates the backward needs
 // {o, wt, qg, kg, aqk, gcl, A, hs, vn}, so nothing is recomputed there.
 std::vector<torch::Tensor> gdn_fwd_train(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor bg, torch::Tensor wg, double scale) {
   for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
   check_gdn(g, at::kFloat, "g");
-  auto s = gdn_shapes(q);
-  auto bf = q.options();
-  auto f32 = q.options().dtype(at::kFloat);
-  auto st = cur_stream();
-  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
-  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
-  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
-  auto A = torch::empty_like(aqk);
-  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
-  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(),
-                    (float)scale, s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(),
-                    aqk.data_ptr<float>(), gcl.data_ptr<float>(), A.data_ptr<float>(), st);
-  check_launch("ahb_gdn_intra_fwd");
+  auto c = gdn_chunk(q, k, v, g, bg, wg, (float)scale, true);
   auto o = torch::empty_like(q);
-  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
-  auto vn = torch::empty_like(wt);
-  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(), nullptr,
-                    hs.data_ptr(), vn.data_ptr(), st);
-  check_launch("ahb_gdn_inter_fwd");
-  return {o, wt, qg, kg, aqk, gcl, A, hs, vn};
+  torch::Tensor hs, vn;
+  gdn_states(c, q, (float)scale, &o, hs, vn);
+  return {o, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn};
 }
 
 std::vector<torch::Tensor> gdn_bwd_saved(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
@@ -274,29 +293,13 @@ std::vector<torch::Tensor> gdn_bwd_saved(torch::Tensor q, torch::Tensor k, torch
 // Backward that recomputes the forward's chunk intermediates (memory-lean path).
 std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                    torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale) {
-  auto s = gdn_shapes(q);
   auto doc = dout.to(at::kBFloat16).contiguous();
-  auto bf = q.options();
-  auto f32 = q.options().dtype(at::kFloat);
-  auto st = cur_stream();
   const float sc = (float)scale;
-  auto wt = torch::empty({s.B, s.H, s.NC, 64, 128}, bf);
-  auto u = torch::empty_like(wt), qg = torch::empty_like(wt), kg = torch::empty_like(wt);
-  auto aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
-  auto A = torch::empty_like(aqk);
-  auto gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
-  ahb_gdn_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), sc,
-                    s.B, s.L, s.H, wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), A.data_ptr<float>(), st);
-  check_launch("ahb_gdn_intra_fwd");
-  auto hs = torch::empty({s.B, s.H, s.NC, 128, 128}, bf);
-  auto vn = torch::empty_like(wt);
-  ahb_gdn_inter_fwd(wt.data_ptr(), u.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr<float>(),
-                    gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, nullptr, nullptr, hs.data_ptr(), vn.data_ptr(),
-                    st);
-  check_launch("ahb_gdn_inter_fwd");
-  u = torch::Tensor();
-  return gdn_bwd_core(q, k, v, g, bg, wg, doc, sc, wt, qg, kg, aqk, gcl, A, hs, vn);
+  auto c = gdn_chunk(q, k, v, g, bg, wg, sc, true);
+  torch::Tensor hs, vn;
+  gdn_states(c, q, sc, nullptr, hs, vn);
+  c.u = torch::Tensor();
+  return gdn_bwd_core(q, k, v, g, bg, wg, doc, sc, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn);
 }
 
 // ------------------------------------------------------------ Mamba2 SSD

@@ -1,32 +1,13 @@
-// GDN-2 chunked gated delta rule with per-channel gates (head dim 128, chunk 64).
+// GDN-2 chunk-parallel backward kernels (head dim 128, chunk 64, per-channel gates).
 //
-// Recurrence per token (reference `atomic_ops/gdn2_wy_reference.py:33-56`):
-//   h <- diag(e^g) h ; v' = w*v - (b*k)^T h ; h += k v'^T ; o = h^T (q*scale)
-// Chunked WY form (reference kernels A/B/C/D, `atomic_ops/kernel_{a,b,c,d}_*.py`):
-//   gc = cumsum_t g                       (per channel, within the chunk)
-//   Aqk[i,j] = scale sum_d q_id k_jd e^{gc_id-gc_jd}   (i >= j)
-//   Akk[i,j] =       sum_d (bk)_id k_jd e^{gc_id-gc_jd} (i > j)
-//   A = (I + Akk)^-1 ; w~ = A (bk e^gc) ; u = A (w v)
-//   v_new = u - w~ h ; o = scale (q e^gc) h + Aqk v_new
-//   h' = diag(e^{gc_last}) h + (k e^{gc_last-gc})^T v_new
-//
-// Design for sm_100a: one CTA per (chunk, head, batch) computes everything that
-// is chunk-local (parallel over all chunks); a second kernel runs the
-// sequential state recurrence with one CTA per (value block of 32, head,
-// batch), the state slice living in registers.  Pairwise decays use a
-// reference row r between j and i (r = first row of i's 16-row block), so both
-// factors e^{gc_i-gc_r} and e^{gc_r-gc_j} are <= 1 and the products run on the
-// tensor cores without overflow; the four 16x16 diagonal blocks are summed
-// exactly per channel (with the reference's -20 floor on the exponent).
-// The inverse (I+Akk)^-1 is blocked: 16x16 diagonal inverses by substitution,
-// then the off-diagonal blocks by distance.
-//
-// Backward (reference B1..B6, `atomic_ops/kernel_bwd_b*.py`, `kernel_trainable_B6.py`):
-//   gdn_intra_fwd (recompute, also stores A) -> gdn_inter_fwd (stores h, v_new)
-//   -> gdn_inter_bwd (reverse recurrence: dh per chunk, dv_new)
-//   -> gdn_bwd_states (products with h/dh: qg/kg chains, dw~, dAqk)
+// Chunked WY form and its forward kernels: gdn_tc.cu.  Backward (reference B1..B6,
+// `atomic_ops/kernel_bwd_b*.py`, `kernel_trainable_B6.py`), after the reverse state
+// recurrence (gdn_tc.cu: dh per chunk, dv_new):
+//   gdn_bwd_states (products with h/dh: qg/kg chains, dw~, dAqk)
 //   -> gdn_bwd_wy (through A: dw, dv, d(bk), dAkk)
 //   -> gdn_bwd_intra (through Aqk/Akk + assembly + reverse cumsum for dg).
+// Pairwise decays use a reference row r between j and i (r = first row of i's 16-row block),
+// so both factors e^{gc_i-gc_r} and e^{gc_r-gc_j} stay <= 1 off the diagonal blocks.
 #include "common.cuh"
 #include "mma.cuh"
 #include "launchers.h"
@@ -41,9 +22,7 @@ constexpr int D = 128;      // head dim (dk = dv)
 constexpr int LDB = D + 8;  // bf16 row stride of C x D tiles
 constexpr int LDF = D + 4;  // fp32 row stride of C x D tiles
 constexpr int LDC = C + 4;  // fp32 row stride of C x C tiles
-constexpr int BV = 32;      // value-block width of the recurrence kernels
 constexpr int NTH = 512;    // threads of the chunk-parallel kernels (16 warps: 4 row tiles x 4 column quarters)
-constexpr int LDV = BV + 8;
 
 AHB_DEVICE float bf(bf16 x) { return __bfloat162float(x); }
 AHB_DEVICE float guard(float x) {  // nan_to_num(nan=0, +-inf -> +-1e4)
@@ -97,29 +76,6 @@ AHB_DEVICE void load_chunk_tile_f32(float* dst, int ld, const float* src, int ro
   }
 }
 
-// Asynchronous 16-byte global -> shared copies (the recurrence kernels prefetch the next
-// chunk's tiles while they compute on the current one).
-AHB_DEVICE void cp16(void* dst, const void* src) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(src) : "memory");
-}
-AHB_DEVICE void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-AHB_DEVICE void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-AHB_DEVICE void cp_chunk_tile(bf16* dst, const bf16* src, int nthreads) {  // C x D bf16 -> [C][LDB]
-  for (int i = threadIdx.x; i < C * (D / 8); i += nthreads) {
-    const int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
-    cp16(dst + r * LDB + c8, src + r * D + c8);
-  }
-}
-AHB_DEVICE void cp_f32_tile(float* dst, int ld, const float* src, int rows, int cols, int nthreads) {
-  for (int i = threadIdx.x; i < rows * (cols / 4); i += nthreads) {
-    const int r = i / (cols / 4), c4 = (i % (cols / 4)) * 4;
-    cp16(dst + r * ld + c4, src + r * cols + c4);
-  }
-}
-
 // Store an accumulator tile (NT n-tiles) as bf16 pairs: dst[row*ld + col]
 template <int NT, class F>
 AHB_DEVICE void store_pairs(float (*acc)[4], int m0, int n0, F&& put) {
@@ -133,438 +89,6 @@ AHB_DEVICE void store_pairs(float (*acc)[4], int m0, int n0, F&& put) {
 }
 
 AHB_DEVICE void st_bf16x2(bf16* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack2(a, b); }
-
-// 16x16 block pair enumeration below the diagonal: p -> (I, J), J < I
-AHB_DEVICE void pair_ij(int p, int& I, int& J) {
-  I = p < 1 ? 1 : (p < 3 ? 2 : 3);
-  J = p - I * (I - 1) / 2;
-}
-// triangular pair index -> (i, j), i >= j, within 16
-AHB_DEVICE void tri_ij(int p, int& i, int& j) {
-  i = (int)((sqrtf(8.f * p + 1.f) - 1.f) * 0.5f);
-  while ((i + 1) * (i + 2) / 2 <= p) ++i;
-  while (i * (i + 1) / 2 > p) --i;
-  j = p - i * (i + 1) / 2;
-}
-
-// ============================================================ intra forward
-// smem: q,k,bk,wv,bke bf16 [C][LDB]; gc f32 [C][LDF]; aqk, akk, a f32 [C][LDC]; t 768 f32
-constexpr size_t SMEM_INTRA = 5 * C * LDB * 2 + C * LDF * 4 + 3 * C * LDC * 4 + 768 * 4;
-
-__global__ void __launch_bounds__(NTH, 1) gdn_intra_fwd_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
-    const float* __restrict__ g, const bf16* __restrict__ bg, const bf16* __restrict__ wg, float scale, int L,
-    int H, bf16* __restrict__ wt_o, bf16* __restrict__ u_o, bf16* __restrict__ qg_o, bf16* __restrict__ kg_o,
-    float* __restrict__ aqk_o, float* __restrict__ gcl_o, float* __restrict__ a_o) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* q_s = reinterpret_cast<bf16*>(smem);
-  bf16* k_s = q_s + C * LDB;
-  bf16* bk_s = k_s + C * LDB;
-  bf16* wv_s = bk_s + C * LDB;
-  bf16* bke_s = wv_s + C * LDB;
-  float* gc_s = reinterpret_cast<float*>(bke_s + C * LDB);
-  float* aqk_s = gc_s + C * LDF;
-  float* akk_s = aqk_s + C * LDC;
-  float* a_s = akk_s + C * LDC;
-  float* t_s = a_s + C * LDC;
-
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
-  const Idx ix{L, H, NC};
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  // 1. loads (q, k raw; bk = b*k, wv = w*v)
-  for (int i = tid; i < C * (D / 8); i += NTH) {
-    int r = i / (D / 8), c8 = (i % (D / 8)) * 8;
-    int64_t gi = ix.seq(b, (int64_t)n * C + r, h) + c8;
-    uint4 qv = *reinterpret_cast<const uint4*>(q + gi);
-    uint4 kv = *reinterpret_cast<const uint4*>(k + gi);
-    uint4 vv = *reinterpret_cast<const uint4*>(v + gi);
-    uint4 bv = *reinterpret_cast<const uint4*>(bg + gi);
-    uint4 wv = *reinterpret_cast<const uint4*>(wg + gi);
-    *reinterpret_cast<uint4*>(q_s + r * LDB + c8) = qv;
-    *reinterpret_cast<uint4*>(k_s + r * LDB + c8) = kv;
-    const bf16* kp = reinterpret_cast<const bf16*>(&kv);
-    const bf16* vp = reinterpret_cast<const bf16*>(&vv);
-    const bf16* bp = reinterpret_cast<const bf16*>(&bv);
-    const bf16* wp = reinterpret_cast<const bf16*>(&wv);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      st_bf16x2(bk_s + r * LDB + c8 + e, bf(bp[e]) * bf(kp[e]), bf(bp[e + 1]) * bf(kp[e + 1]));
-      st_bf16x2(wv_s + r * LDB + c8 + e, bf(wp[e]) * bf(vp[e]), bf(wp[e + 1]) * bf(vp[e + 1]));
-    }
-  }
-  load_gc(gc_s, g, ix, b, n, h, NTH);  // includes __syncthreads
-
-  // 2. bke = bk * e^gc; per diagonal block, the largest decay across its 16 rows
-  __shared__ int exact_blk[4];
-  for (int i = tid; i < C * D; i += NTH) {
-    int r = i / D, d = i % D;
-    bke_s[r * LDB + d] = __float2bfloat16_rn(bf(bk_s[r * LDB + d]) * __expf(gc_s[r * LDF + d]));
-  }
-  if (warp < 4) {
-    float span = 0.f;
-    for (int d = lane; d < D; d += 32) span = fmaxf(span, gc_s[16 * warp * LDF + d] - gc_s[(16 * warp + 15) * LDF + d]);
-    span = warp_max(span);
-    // the factorised operands of a diagonal block carry e^{span}; beyond e^60 use exact sums
-    if (lane == 0) exact_blk[warp] = !(span <= 60.f);
-  }
-  __syncthreads();
-  // 3a. 16x16 blocks of Aqk / Akk on tensor cores: 6 off-diagonal and 4 diagonal block pairs,
-  // operands factorised at the block-row's first row r0 (every exponent <= 0 off the diagonal;
-  // on the diagonal B carries e^{gc_r0 - gc_j} <= e^{span})
-  for (int job = warp; job < 20; job += NTH / 32) {
-    int I, J;
-    if (job < 12) {
-      pair_ij(job >> 1, I, J);
-    } else {
-      I = J = (job - 12) >> 1;
-      if (exact_blk[I]) continue;
-    }
-    const bool is_kk = job & 1;
-    const int r0 = 16 * I;
-    const float* gr = gc_s + r0 * LDF;
-    const bf16* xs = is_kk ? bk_s : q_s;
-    auto fa = [&](int rr, int cc) -> uint32_t {
-      const float* gi = gc_s + (r0 + rr) * LDF;
-      return pack2(bf(xs[(r0 + rr) * LDB + cc]) * __expf(gi[cc] - gr[cc]),
-                   bf(xs[(r0 + rr) * LDB + cc + 1]) * __expf(gi[cc + 1] - gr[cc + 1]));
-    };
-    auto fb = [&](int kd, int nj) -> uint32_t {
-      const int j = 16 * J + nj;
-      const float* gj = gc_s + j * LDF;
-      return pack2(bf(k_s[j * LDB + kd]) * __expf(gr[kd] - gj[kd]),
-                   bf(k_s[j * LDB + kd + 1]) * __expf(gr[kd + 1] - gj[kd + 1]));
-    };
-    float acc[2][4];
-    zero_acc<2>(acc);
-    warp_mma<2>(acc, fa, fb, 0, 0, 0, D);
-    float* dst = is_kk ? akk_s : aqk_s;
-    const float sc = is_kk ? 1.f : scale;
-    const bool diag = I == J;
-    for_acc<2>(acc, 0, 0, [&](int rr, int cc, float& val) {
-      // diagonal blocks: Aqk keeps j <= i, Akk keeps j < i (the rest is zeroed below)
-      if (!diag || cc < rr || (cc == rr && !is_kk)) dst[(r0 + rr) * LDC + 16 * J + cc] = guard(val * sc);
-      else if (cc == rr) dst[(r0 + rr) * LDC + 16 * J + cc] = 0.f;
-    });
-  }
-  // 3b. diagonal blocks whose decay span is too wide to factorise: exact per-channel sums
-  // (-20 floor on the exponent, as the reference)
-  for (int p = warp; p < 4 * 136; p += NTH / 32) {
-    int blk = p / 136, i, j;
-    if (!exact_blk[blk]) continue;
-    tri_ij(p % 136, i, j);
-    const int ri = 16 * blk + i, rj = 16 * blk + j;
-    float sq = 0.f, sk = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      float e = __expf(fmaxf(gc_s[ri * LDF + d] - gc_s[rj * LDF + d], -20.f));
-      float kj = bf(k_s[rj * LDB + d]) * e;
-      sq += bf(q_s[ri * LDB + d]) * kj;
-      sk += bf(bk_s[ri * LDB + d]) * kj;
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    if (lane == 0) {
-      aqk_s[ri * LDC + rj] = guard(sq * scale);
-      akk_s[ri * LDC + rj] = i > j ? guard(sk) : 0.f;
-    }
-  }
-  // upper parts are zero
-  for (int i = tid; i < C * C; i += NTH) {
-    int r = i / C, c = i % C;
-    if (c > r) { aqk_s[r * LDC + c] = 0.f; akk_s[r * LDC + c] = 0.f; }
-    if ((c >> 4) != (r >> 4)) a_s[r * LDC + c] = 0.f;
-  }
-  __syncthreads();
-
-  // 4a. inverses of the 16x16 diagonal blocks of I + Akk
-  if (warp < 4) {
-    const int base = 16 * warp;
-    for (int i = 0; i < 16; ++i) {
-      float x = 0.f;
-      if (lane < 16) {
-        x = lane == i ? 1.f : 0.f;
-        for (int j = lane; j < i; ++j) x -= akk_s[(base + i) * LDC + base + j] * a_s[(base + j) * LDC + base + lane];
-      }
-      __syncwarp();
-      if (lane < 16) a_s[(base + i) * LDC + base + lane] = lane <= i ? x : 0.f;
-      __syncwarp();
-    }
-  }
-  __syncthreads();
-  // 4b. off-diagonal blocks by distance: X_IJ = -X_II sum_{K=J}^{I-1} S_IK X_KJ
-  for (int dist = 1; dist < 4; ++dist) {
-    const int np = 4 - dist;
-    for (int e = tid; e < np * 256; e += NTH) {
-      int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
-      int J = p, I = p + dist;
-      float s = 0.f;
-      for (int K = J; K < I; ++K)
-#pragma unroll 4
-        for (int kk = 0; kk < 16; ++kk)
-          s += akk_s[(16 * I + ii) * LDC + 16 * K + kk] * a_s[(16 * K + kk) * LDC + 16 * J + cc];
-      t_s[e] = s;
-    }
-    __syncthreads();
-    for (int e = tid; e < np * 256; e += NTH) {
-      int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
-      int J = p, I = p + dist;
-      float s = 0.f;
-      for (int m = 0; m <= ii; ++m) s += a_s[(16 * I + ii) * LDC + 16 * I + m] * t_s[(p << 8) + (m << 4) + cc];
-      a_s[(16 * I + ii) * LDC + 16 * J + cc] = guard(-s);
-    }
-    __syncthreads();
-  }
-
-  // 5. w~ = A bke, u = A wv  (warp: 16-row tile mt, 64-col half nh)
-  const int64_t cb = ix.chunk(b, h, n);
-  {
-    const int mt = warp & 3, nq = warp >> 2;
-    float accw[4][4], accu[4][4];
-    zero_acc<4>(accw);
-    zero_acc<4>(accu);
-    RowA32 fa{a_s, LDC};
-    KNB16 fbk{bke_s, LDB}, fbv{wv_s, LDB};
-    for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 16) {
-      uint32_t a[4];
-      load_a(a, fa, 16 * mt, k0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t bb[2];
-        load_b(bb, fbk, k0, 32 * nq + 8 * j);
-        mma16816(accw[j], a, bb);
-        load_b(bb, fbv, k0, 32 * nq + 8 * j);
-        mma16816(accu[j], a, bb);
-      }
-    }
-    bf16* wto = wt_o + cb * C * D;
-    bf16* uo = u_o + cb * C * D;
-    store_pairs<4>(accw, 16 * mt, 32 * nq, [&](int r, int c, float x0, float x1) {
-      st_bf16x2(wto + r * D + c, guard(x0), guard(x1));
-    });
-    store_pairs<4>(accu, 16 * mt, 32 * nq, [&](int r, int c, float x0, float x1) {
-      st_bf16x2(uo + r * D + c, guard(x0), guard(x1));
-    });
-  }
-  // 6. qg, kg, gc_last, Aqk (and A) out
-  for (int i = tid; i < C * D / 2; i += NTH) {
-    int r = (2 * i) / D, d = (2 * i) % D;
-    float g0 = gc_s[r * LDF + d], g1 = gc_s[r * LDF + d + 1];
-    float l0 = gc_s[(C - 1) * LDF + d], l1 = gc_s[(C - 1) * LDF + d + 1];
-    st_bf16x2(qg_o + cb * C * D + r * D + d, bf(q_s[r * LDB + d]) * __expf(g0), bf(q_s[r * LDB + d + 1]) * __expf(g1));
-    st_bf16x2(kg_o + cb * C * D + r * D + d, bf(k_s[r * LDB + d]) * __expf(l0 - g0),
-              bf(k_s[r * LDB + d + 1]) * __expf(l1 - g1));
-  }
-  if (tid < D) gcl_o[cb * D + tid] = gc_s[(C - 1) * LDF + tid];
-  for (int i = tid; i < C * C; i += NTH) {
-    int r = i / C, c = i % C;
-    aqk_o[cb * C * C + i] = aqk_s[r * LDC + c];
-    if (a_o) a_o[cb * C * C + i] = a_s[r * LDC + c];
-  }
-}
-
-// ============================================================ inter forward
-// smem: wt, qg, kg bf16 [C][LDB]; u bf16 [C][LDV]; aqk f32 [C][LDC]; h bf16 [D][LDV]; vn bf16 [C][LDV]; gcl f32 [D]
-// per buffer: wt, qg, kg bf16 [C][LDB]; u bf16 [C][LDV]; aqk f32 [C][LDC]; gcl f32 [D]  (two buffers)
-constexpr size_t INTER_F_BUF = 3 * C * LDB * 2 + C * LDV * 2 + C * LDC * 4 + D * 4;
-constexpr size_t SMEM_INTER_F = 2 * INTER_F_BUF + D * LDV * 2 + C * LDV * 2;
-
-__global__ void __launch_bounds__(128) gdn_inter_fwd_kernel(
-    const bf16* __restrict__ wt, const bf16* __restrict__ u, const bf16* __restrict__ qg,
-    const bf16* __restrict__ kg, const float* __restrict__ aqk, const float* __restrict__ gcl, float scale, int L,
-    int H, int NC, const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final,
-    bf16* __restrict__ h_store, bf16* __restrict__ vn_store) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* h_s = reinterpret_cast<bf16*>(smem + 2 * INTER_F_BUF);
-  bf16* vn_s = h_s + D * LDV;
-
-  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const Idx ix{L, H, NC};
-  const int tid = threadIdx.x, w = tid >> 5;
-  auto buf = [&](int i, bf16*& wt_s, bf16*& qg_s, bf16*& kg_s, bf16*& u_s, float*& aqk_s, float*& gcl_s) {
-    unsigned char* base = smem + (size_t)i * INTER_F_BUF;
-    wt_s = reinterpret_cast<bf16*>(base);
-    qg_s = wt_s + C * LDB;
-    kg_s = qg_s + C * LDB;
-    u_s = kg_s + C * LDB;
-    aqk_s = reinterpret_cast<float*>(u_s + C * LDV);
-    gcl_s = aqk_s + C * LDC;
-  };
-  // prefetch chunk n's tiles into buffer n & 1 (one commit group)
-  auto issue = [&](int n) {
-    bf16 *wt_s, *qg_s, *kg_s, *u_s;
-    float *aqk_s, *gcl_s;
-    buf(n & 1, wt_s, qg_s, kg_s, u_s, aqk_s, gcl_s);
-    const int64_t cb = ix.chunk(b, h, n);
-    cp_chunk_tile(wt_s, wt + cb * C * D, 128);
-    cp_chunk_tile(qg_s, qg + cb * C * D, 128);
-    cp_chunk_tile(kg_s, kg + cb * C * D, 128);
-    for (int i = tid; i < C * (BV / 8); i += 128) {
-      const int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
-      cp16(u_s + r * LDV + c8, u + cb * C * D + r * D + vb * BV + c8);
-    }
-    cp_f32_tile(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
-    if (tid < D / 4) cp16(gcl_s + 4 * tid, gcl + cb * D + 4 * tid);
-    cp_commit();
-  };
-  // state slice: rows d in [32w, 32w+32) (2 m-tiles), cols [0, 32) of this value block
-  float hr[2][4][4];
-  for (int mi = 0; mi < 2; ++mi)
-    for_acc<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
-      x = h0 ? h0[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
-    });
-  issue(0);
-  for (int n = 0; n < NC; ++n) {
-    const int64_t cb = ix.chunk(b, h, n);
-    bf16 *wt_s, *qg_s, *kg_s, *u_s;
-    float *aqk_s, *gcl_s;
-    buf(n & 1, wt_s, qg_s, kg_s, u_s, aqk_s, gcl_s);
-    for (int mi = 0; mi < 2; ++mi)
-      store_pairs<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
-        st_bf16x2(h_s + r * LDV + c, x0, x1);
-        if (h_store) st_bf16x2(h_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
-      });
-    if (n + 1 < NC) {
-      issue(n + 1);  // the other buffer was released by the barrier that ended chunk n-1
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    float accv[4][4], acco[4][4];
-    zero_acc<4>(accv);
-    zero_acc<4>(acco);
-    warp_mma<4>(accv, RowA16{wt_s, LDB}, KNB16{h_s, LDV}, 16 * w, 0, 0, D);
-    if (o) warp_mma<4>(acco, RowA16{qg_s, LDB}, KNB16{h_s, LDV}, 16 * w, 0, 0, D);
-    store_pairs<4>(accv, 16 * w, 0, [&](int r, int c, float x0, float x1) {
-      float v0 = bf(u_s[r * LDV + c]) - x0, v1 = bf(u_s[r * LDV + c + 1]) - x1;
-      st_bf16x2(vn_s + r * LDV + c, v0, v1);
-      if (vn_store) st_bf16x2(vn_store + cb * C * D + r * D + vb * BV + c, v0, v1);
-    });
-    __syncthreads();
-    if (o) {
-      for_acc<4>(acco, 0, 0, [&](int, int, float& x) { x *= scale; });
-      warp_mma<4>(acco, RowA32{aqk_s, LDC}, KNB16{vn_s, LDV}, 16 * w, 0, 0, 16 * (w + 1));
-      store_pairs<4>(acco, 16 * w, 0, [&](int r, int c, float x0, float x1) {
-        st_bf16x2(o + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c, guard(x0), guard(x1));
-      });
-    }
-    for (int mi = 0; mi < 2; ++mi) {
-      const int d0 = 32 * w + 16 * mi;
-      for_acc<4>(hr[mi], d0, 0, [&](int r, int, float& x) { x *= __expf(gcl_s[r]); });
-      warp_mma<4>(hr[mi], ColA16{kg_s, LDB}, KNB16{vn_s, LDV}, d0, 0, 0, C);
-      for_acc<4>(hr[mi], d0, 0, [&](int, int, float& x) { x = sanitize(x, 1e4f); });
-    }
-    __syncthreads();
-  }
-  if (h_final)
-    for (int mi = 0; mi < 2; ++mi)
-      for_acc<4>(hr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
-        h_final[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] = x;
-      });
-}
-
-// ============================================================ inter backward (reverse recurrence)
-// per buffer: wt, qg, kg bf16 [C][LDB]; aqk f32 [C][LDC]; do bf16 [C][LDV]; gcl f32 [D] (two buffers);
-// dh bf16 [D][LDV]; dvn bf16 [C][LDV]
-constexpr size_t INTER_B_BUF = 3 * C * LDB * 2 + C * LDC * 4 + C * LDV * 2 + D * 4;
-constexpr size_t SMEM_INTER_B = 2 * INTER_B_BUF + D * LDV * 2 + C * LDV * 2;
-
-__global__ void __launch_bounds__(128) gdn_inter_bwd_kernel(
-    const bf16* __restrict__ wt, const bf16* __restrict__ qg, const bf16* __restrict__ kg,
-    const float* __restrict__ aqk, const float* __restrict__ gcl, const bf16* __restrict__ dout, float scale, int L,
-    int H, int NC, const float* __restrict__ dh_final, bf16* __restrict__ dh_store, bf16* __restrict__ dvn_store,
-    float* __restrict__ dh0) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* dh_s = reinterpret_cast<bf16*>(smem + 2 * INTER_B_BUF);
-  bf16* dvn_s = dh_s + D * LDV;
-
-  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const Idx ix{L, H, NC};
-  const int tid = threadIdx.x, w = tid >> 5;
-  auto buf = [&](int i, bf16*& wt_s, bf16*& qg_s, bf16*& kg_s, float*& aqk_s, bf16*& do_s, float*& gcl_s) {
-    unsigned char* base = smem + (size_t)i * INTER_B_BUF;
-    wt_s = reinterpret_cast<bf16*>(base);
-    qg_s = wt_s + C * LDB;
-    kg_s = qg_s + C * LDB;
-    aqk_s = reinterpret_cast<float*>(kg_s + C * LDB);
-    do_s = reinterpret_cast<bf16*>(aqk_s + C * LDC);
-    gcl_s = reinterpret_cast<float*>(do_s + C * LDV);
-  };
-  auto issue = [&](int n, int slot) {
-    bf16 *wt_s, *qg_s, *kg_s, *do_s;
-    float *aqk_s, *gcl_s;
-    buf(slot, wt_s, qg_s, kg_s, aqk_s, do_s, gcl_s);
-    const int64_t cb = ix.chunk(b, h, n);
-    cp_chunk_tile(wt_s, wt + cb * C * D, 128);
-    cp_chunk_tile(qg_s, qg + cb * C * D, 128);
-    cp_chunk_tile(kg_s, kg + cb * C * D, 128);
-    cp_f32_tile(aqk_s, LDC, aqk + cb * C * C, C, C, 128);
-    for (int i = tid; i < C * (BV / 8); i += 128) {
-      const int r = i / (BV / 8), c8 = (i % (BV / 8)) * 8;
-      cp16(do_s + r * LDV + c8, dout + ix.seq(b, (int64_t)n * C + r, h) + vb * BV + c8);
-    }
-    if (tid < D / 4) cp16(gcl_s + 4 * tid, gcl + cb * D + 4 * tid);
-    cp_commit();
-  };
-  float dr[2][4][4];
-  for (int mi = 0; mi < 2; ++mi)
-    for_acc<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
-      x = dh_final ? dh_final[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] : 0.f;
-    });
-  issue(NC - 1, 0);
-  for (int n = NC - 1, it = 0; n >= 0; --n, ++it) {
-    const int64_t cb = ix.chunk(b, h, n);
-    bf16 *wt_s, *qg_s, *kg_s, *do_s;
-    float *aqk_s, *gcl_s;
-    buf(it & 1, wt_s, qg_s, kg_s, aqk_s, do_s, gcl_s);
-    for (int mi = 0; mi < 2; ++mi)
-      store_pairs<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float x0, float x1) {
-        st_bf16x2(dh_s + r * LDV + c, x0, x1);
-        st_bf16x2(dh_store + cb * D * D + (int64_t)r * D + vb * BV + c, x0, x1);
-      });
-    if (n > 0) {
-      issue(n - 1, (it + 1) & 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    __syncthreads();
-    // dv_new = Aqk^T do + kg dh
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, ColA32{aqk_s, LDC}, KNB16{do_s, LDV}, 16 * w, 0, 16 * w, C);
-    warp_mma<4>(acc, RowA16{kg_s, LDB}, KNB16{dh_s, LDV}, 16 * w, 0, 0, D);
-    store_pairs<4>(acc, 16 * w, 0, [&](int r, int c, float x0, float x1) {
-      st_bf16x2(dvn_s + r * LDV + c, x0, x1);
-      st_bf16x2(dvn_store + cb * C * D + r * D + vb * BV + c, x0, x1);
-    });
-    __syncthreads();
-    // dh_prev = e^{gcl} dh + scale qg^T do - wt^T dv_new
-    for (int mi = 0; mi < 2; ++mi) {
-      const int d0 = 32 * w + 16 * mi;
-      float t1[4][4], t2[4][4];
-      zero_acc<4>(t1);
-      zero_acc<4>(t2);
-      warp_mma<4>(t1, ColA16{qg_s, LDB}, KNB16{do_s, LDV}, d0, 0, 0, C);
-      warp_mma<4>(t2, ColA16{wt_s, LDB}, KNB16{dvn_s, LDV}, d0, 0, 0, C);
-      const int lane = tid & 31, gq = lane >> 2;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float e0 = __expf(gcl_s[d0 + gq]), e1 = __expf(gcl_s[d0 + gq + 8]);
-        dr[mi][j][0] = dr[mi][j][0] * e0 + scale * t1[j][0] - t2[j][0];
-        dr[mi][j][1] = dr[mi][j][1] * e0 + scale * t1[j][1] - t2[j][1];
-        dr[mi][j][2] = dr[mi][j][2] * e1 + scale * t1[j][2] - t2[j][2];
-        dr[mi][j][3] = dr[mi][j][3] * e1 + scale * t1[j][3] - t2[j][3];
-      }
-    }
-    __syncthreads();
-  }
-  if (dh0)
-    for (int mi = 0; mi < 2; ++mi)
-      for_acc<4>(dr[mi], 32 * w + 16 * mi, 0, [&](int r, int c, float& x) {
-        dh0[(((int64_t)b * H + h) * D + r) * D + vb * BV + c] = x;
-      });
-}
 
 // ============================================================ backward: products with the states
 // smem: h, dh bf16 [D][LDB]; do, vn, dvn, q, k bf16 [C][LDB]; gc f32 [C][LDF]; red f32 [D]
@@ -941,39 +465,6 @@ void set_smem(K kernel, size_t bytes) {
 
 // ===================================================================== launchers
 int ahb_gdn_supported(int D_) { return D_ == D ? C : 0; }
-
-void ahb_gdn_intra_fwd(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
-                       float scale, int B, int L, int H, void* wt, void* u, void* qg, void* kg, float* aqk,
-                       float* gcl, float* a_out, cudaStream_t st) {
-  static bool init = false;
-  if (!init) { set_smem(gdn_intra_fwd_kernel, SMEM_INTRA); init = true; }
-  dim3 grid(L / C, H, B);
-  gdn_intra_fwd_kernel<<<grid, NTH, SMEM_INTRA, st>>>(
-      (const bf16*)q, (const bf16*)k, (const bf16*)v, g, (const bf16*)bg, (const bf16*)wg, scale, L, H, (bf16*)wt,
-      (bf16*)u, (bf16*)qg, (bf16*)kg, aqk, gcl, a_out);
-}
-
-void ahb_gdn_inter_fwd(const void* wt, const void* u, const void* qg, const void* kg, const float* aqk,
-                       const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
-                       void* h_store, void* vn_store, cudaStream_t st) {
-  static bool init = false;
-  if (!init) { set_smem(gdn_inter_fwd_kernel, SMEM_INTER_F); init = true; }
-  dim3 grid(D / BV, H, B);
-  gdn_inter_fwd_kernel<<<grid, 128, SMEM_INTER_F, st>>>(
-      (const bf16*)wt, (const bf16*)u, (const bf16*)qg, (const bf16*)kg, aqk, gcl, scale, L, H, L / C, h0, (bf16*)o,
-      h_final, (bf16*)h_store, (bf16*)vn_store);
-}
-
-void ahb_gdn_inter_bwd(const void* wt, const void* qg, const void* kg, const float* aqk, const float* gcl,
-                       const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
-                       void* dvn_store, float* dh0, cudaStream_t st) {
-  static bool init = false;
-  if (!init) { set_smem(gdn_inter_bwd_kernel, SMEM_INTER_B); init = true; }
-  dim3 grid(D / BV, H, B);
-  gdn_inter_bwd_kernel<<<grid, 128, SMEM_INTER_B, st>>>((const bf16*)wt, (const bf16*)qg, (const bf16*)kg, aqk, gcl,
-                                                        (const bf16*)dout, scale, L, H, L / C, dh_final,
-                                                        (bf16*)dh_store, (bf16*)dvn_store, dh0);
-}
 
 void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void* dout, const void* h_store,
                         const void* dh_store, const void* vn_store, const void* dvn_store, float scale, int B, int L,

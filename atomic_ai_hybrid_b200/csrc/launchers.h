@@ -29,15 +29,20 @@ void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* a
 
 // gdn.cu (head dim 128, chunk 64; all sequence tensors (B, L, H, 128), chunk tensors (B, H, L/64, 64, .))
 int ahb_gdn_supported(int D);
-void ahb_gdn_intra_fwd(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
-                       float scale, int B, int L, int H, void* wt, void* u, void* qg, void* kg, float* aqk,
-                       float* gcl, float* a_out, cudaStream_t st);
-void ahb_gdn_inter_fwd(const void* wt, const void* u, const void* qg, const void* kg, const float* aqk,
-                       const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
-                       void* h_store, void* vn_store, cudaStream_t st);
-void ahb_gdn_inter_bwd(const void* wt, const void* qg, const void* kg, const float* aqk, const float* gcl,
-                       const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
-                       void* dvn_store, float* dh0, cudaStream_t st);
+// gdn_tc.cu: chunk-local forward and the two state recurrences on tcgen05.  The chunk
+// intermediates wt/u/qg/kg (B, H, L/64, 64 x 128) and aqk (B, H, L/64, 64 x 64) are bf16 tile
+// images in the 128-byte-swizzled shared-memory layout; a_out is plain fp32 (B, H, L/64, 64, 64);
+// h_store / vn_store / dh_store / dvn_store are plain bf16 row-major chunk tensors.
+// Return 0, or a negative code when a launch or set-up failed; `err` receives device timeouts.
+int ahb_gdn_chunk_fwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                         float scale, int B, int L, int H, void* wt_t, void* u_t, void* qg_t, void* kg_t, void* aqk_t,
+                         float* gcl, float* a_out, int* err, cudaStream_t st);
+int ahb_gdn_state_fwd_tc(const void* wt_t, const void* u_t, const void* qg_t, const void* kg_t, const void* aqk_t,
+                         const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
+                         void* h_store, void* vn_store, int* err, cudaStream_t st);
+int ahb_gdn_state_bwd_tc(const void* wt_t, const void* qg_t, const void* kg_t, const void* aqk_t, const float* gcl,
+                         const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
+                         void* dvn_store, float* dh0, int* err, cudaStream_t st);
 void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void* dout, const void* h_store,
                         const void* dh_store, const void* vn_store, const void* dvn_store, float scale, int B, int L,
                         int H, float* dq_p, float* dk_p, float* dgc_p, float* dwt, float* dgcl, float* daqk,
