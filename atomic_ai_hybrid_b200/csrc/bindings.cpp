@@ -157,7 +157,7 @@ struct GdnShapes { int B, L, H, NC; };
 
 GdnShapes gdn_shapes(const torch::Tensor& q) {
   int B = (int)q.size(0), L = (int)q.size(1), H = (int)q.size(2), D = (int)q.size(3);
-  TORCH_CHECK(ahb_gdn_supported(D) == 64, "gdn2: head dim must be 128");
+  TORCH_CHECK(D == 128, "gdn2: head dim must be 128");
   TORCH_CHECK(L % 64 == 0, "gdn2: sequence length must be a multiple of 64");
   return {B, L, H, L / 64};
 }
@@ -170,7 +170,7 @@ void check_rc(int rc, const char* what) {
 }
 
 // Chunk intermediates of the forward: tile images wt, u, qg, kg (B,H,NC,64,128) and aqk
-// (B,H,NC,64,64) bf16, gcl (B,H,NC,128) fp32, and A (B,H,NC,64,64) fp32 when `want_a`.
+// (B,H,NC,64,64) bf16, gcl (B,H,NC,128) fp32, and the tile image of A (B,H,NC,64,64) bf16 when `want_a`.
 struct GdnChunk { torch::Tensor wt, u, qg, kg, aqk, gcl, A; };
 
 GdnChunk gdn_chunk(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& g,
@@ -185,11 +185,11 @@ GdnChunk gdn_chunk(const torch::Tensor& q, const torch::Tensor& k, const torch::
   c.kg = torch::empty_like(c.wt);
   c.aqk = torch::empty({s.B, s.H, s.NC, 64, 64}, bf);
   c.gcl = torch::empty({s.B, s.H, s.NC, 128}, f32);
-  if (want_a) c.A = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
+  if (want_a) c.A = torch::empty({s.B, s.H, s.NC, 64, 64}, bf);
   check_rc(ahb_gdn_chunk_fwd_tc(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(),
                                 wg.data_ptr(), scale, s.B, s.L, s.H, c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(),
                                 c.kg.data_ptr(), c.aqk.data_ptr(), c.gcl.data_ptr<float>(),
-                                want_a ? c.A.data_ptr<float>() : nullptr, err_word().data_ptr<int>(), cur_stream()),
+                                want_a ? c.A.data_ptr() : nullptr, err_word().data_ptr<int>(), cur_stream()),
            "ahb_gdn_chunk_fwd_tc");
   return c;
 }
@@ -221,7 +221,6 @@ static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const tor
                                                torch::Tensor aqk, const torch::Tensor& gcl,
                                                const torch::Tensor& A, torch::Tensor hs, torch::Tensor vn) {
   auto s = gdn_shapes(q);
-  auto f32 = q.options().dtype(at::kFloat);
   auto st = cur_stream();
   auto dhs = torch::empty_like(hs);
   auto dvn = torch::empty({s.B, s.H, s.NC, 64, 128}, q.options());
@@ -230,30 +229,15 @@ static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const tor
                                 err_word().data_ptr<int>(), st),
            "ahb_gdn_state_bwd_tc");
   qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor(); aqk = torch::Tensor();
-  auto dq_p = torch::empty({s.B, s.H, s.NC, 64, 128}, f32);
-  auto dk_p = torch::empty_like(dq_p), dgc_p = torch::empty_like(dq_p), dwt = torch::empty_like(dq_p);
-  auto dgcl = torch::empty_like(gcl);
-  auto daqk = torch::empty({s.B, s.H, s.NC, 64, 64}, f32);
-  ahb_gdn_bwd_states(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), doc.data_ptr(), hs.data_ptr(), dhs.data_ptr(),
-                     vn.data_ptr(), dvn.data_ptr(), sc, s.B, s.L, s.H, dq_p.data_ptr<float>(),
-                     dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(), dwt.data_ptr<float>(), dgcl.data_ptr<float>(),
-                     daqk.data_ptr<float>(), st);
-  check_launch("ahb_gdn_bwd_states");
-  hs = torch::Tensor(); dhs = torch::Tensor(); vn = torch::Tensor();
-  auto dv = torch::empty_like(q), dw = torch::empty_like(q);
-  auto dbk_wy = torch::empty_like(dq_p), dgc_wy = torch::empty_like(dq_p);
-  auto dakk = torch::empty_like(daqk);
-  ahb_gdn_bwd_wy(k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), wg.data_ptr(), A.data_ptr<float>(),
-                 dvn.data_ptr(), dwt.data_ptr<float>(), s.B, s.L, s.H, dv.data_ptr(), dw.data_ptr(),
-                 dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dakk.data_ptr<float>(), st);
-  check_launch("ahb_gdn_bwd_wy");
-  auto dq = torch::empty_like(q), dk = torch::empty_like(q), db = torch::empty_like(q);
+  auto dq = torch::empty_like(q), dk = torch::empty_like(q), dv = torch::empty_like(q), db = torch::empty_like(q),
+       dw = torch::empty_like(q);
   auto dg = torch::empty_like(g);
-  ahb_gdn_bwd_intra(q.data_ptr(), k.data_ptr(), g.data_ptr<float>(), bg.data_ptr(), daqk.data_ptr<float>(),
-                    dakk.data_ptr<float>(), dq_p.data_ptr<float>(), dk_p.data_ptr<float>(), dgc_p.data_ptr<float>(),
-                    dbk_wy.data_ptr<float>(), dgc_wy.data_ptr<float>(), dgcl.data_ptr<float>(), sc, s.B, s.L, s.H,
-                    dq.data_ptr(), dk.data_ptr(), db.data_ptr(), dg.data_ptr<float>(), st);
-  check_launch("ahb_gdn_bwd_intra");
+  check_rc(ahb_gdn_chunk_bwd_tc(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), bg.data_ptr(),
+                                wg.data_ptr(), doc.data_ptr(), hs.data_ptr(), dhs.data_ptr(), vn.data_ptr(),
+                                dvn.data_ptr(), A.data_ptr(), sc, s.B, s.L, s.H, dq.data_ptr(), dk.data_ptr(),
+                                dv.data_ptr(), db.data_ptr(), dw.data_ptr(), dg.data_ptr<float>(),
+                                err_word().data_ptr<int>(), st),
+           "ahb_gdn_chunk_bwd_tc");
   return {dq, dk, dv, dg, db, dw};
 }
 

@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     const float* __restrict__ g, const bf16* __restrict__ bg, const bf16* __restrict__ wg, float scale, int L,
     int H, unsigned char* __restrict__ wt_t, unsigned char* __restrict__ u_t, unsigned char* __restrict__ qg_t,
     unsigned char* __restrict__ kg_t, unsigned char* __restrict__ aqk_t, float* __restrict__ gcl_o,
-    float* __restrict__ a_o, int* __restrict__ err) {
+    unsigned char* __restrict__ at_t, int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* R1 = smem;
@@ -86,7 +86,19 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   }
   if (warp == 0) sm100::tmem_alloc(tmem_slot, 256);
 
-  // 1. g -> GC, cumulative sum per channel (thread d owns channel d)
+  // 1. g -> GC, cumulative sum per channel (thread d owns channel d); the q / k / b rows of
+  //    step 2 are requested first so their latency overlaps the scan
+  constexpr int UNITS = (C * D / 8) / F1_THREADS;  // 16-byte units per thread and tile
+  uint4 qa[UNITS], ka[UNITS], ba[UNITS];
+#pragma unroll
+  for (int it = 0; it < UNITS; ++it) {
+    const int u_ = it * F1_THREADS + tid;
+    const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
+    qa[it] = *reinterpret_cast<const uint4*>(q + gi);
+    ka[it] = *reinterpret_cast<const uint4*>(k + gi);
+    ba[it] = *reinterpret_cast<const uint4*>(bg + gi);
+  }
+#pragma unroll
   for (int e = tid; e < C * (D / 4); e += F1_THREADS) {
     const int r = e >> 5, c4 = (e & 31) << 2;
     *reinterpret_cast<float4*>(GC + r * D + c4) = *reinterpret_cast<const float4*>(g + ix.row(b, t0 + r, h) + c4);
@@ -121,14 +133,14 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   //    qg = q e^gc and kg = k e^{gcl - gc} go straight out as tile images
   unsigned char* qg_c = qg_t + cb * TILE_CD;
   unsigned char* kg_c = kg_t + cb * TILE_CD;
-  for (int it = 0; it < (C * D / 8) / F1_THREADS; ++it) {
+#pragma unroll
+  for (int it = 0; it < UNITS; ++it) {
     const int u_ = it * F1_THREADS + tid;
     const int i = u_ >> 4, c = (u_ & 15) << 3;
-    const int64_t gi = ix.row(b, t0 + i, h) + c;
     float qv[8], kv[8], bv[8];
-    unpack8(*reinterpret_cast<const uint4*>(q + gi), qv);
-    unpack8(*reinterpret_cast<const uint4*>(k + gi), kv);
-    unpack8(*reinterpret_cast<const uint4*>(bg + gi), bv);
+    unpack8(qa[it], qv);
+    unpack8(ka[it], kv);
+    unpack8(ba[it], bv);
     const float* gci = GC + i * D + c;
     const float* gcr = GC + (i & ~15) * D + c;
     const float* gcl = GC + (C - 1) * D + c;
@@ -150,16 +162,19 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   // 3. key operands per reference block and the score MMAs (region I = TMEM columns [64 I, 64 I + 64))
   constexpr uint32_t IDESC_S[4] = {sm100::idesc_bf16(128, 16, false, false), sm100::idesc_bf16(128, 32, false, false),
                                    sm100::idesc_bf16(128, 48, false, false), sm100::idesc_bf16(128, 64, false, false)};
+#pragma unroll
   for (int I = 0; I < 4; ++I) {
     unsigned char* buf = R2 + (I & 1) * TILE_CD;
     if (I >= 2 && !wait_bar(bars + I - 2, 0, err, 0x4701)) flags[4] = 1;
-    const int rows = 16 * (I + 1);
     const bool exact = flags[I];
     const float* gcr = GC + 16 * I * D;
-    for (int u_ = tid; u_ < rows * 16; u_ += F1_THREADS) {
+    // rows j < 16 (I + 1): the k rows held from step 2 are units 0 .. 2 (I + 1) - 1 of this thread
+#pragma unroll
+    for (int it = 0; it < 2 * (I + 1); ++it) {
+      const int u_ = it * F1_THREADS + tid;
       const int j = u_ >> 4, c = (u_ & 15) << 3;
       float kv[8], o[8];
-      unpack8(*reinterpret_cast<const uint4*>(k + ix.row(b, t0 + j, h) + c), kv);
+      unpack8(ka[it], kv);
       const float* gcj = GC + j * D + c;
       const bool zero = exact && j >= 16 * I;
 #pragma unroll
@@ -283,7 +298,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       }
       __syncthreads();
     }
-    // A out: fp32 rows for the chunk-parallel backward, bf16 operand tile (rows i, columns j)
+    // A out: bf16 operand tile (rows i, columns j), also as a tile image for the backward
     unsigned char* AT = R2 + 24576;
     for (int e = tid; e < C * 8; e += F1_THREADS) {
       const int i = e >> 3, c = (e & 7) << 3;
@@ -291,24 +306,28 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
 #pragma unroll
       for (int t = 0; t < 8; ++t) x[t] = AF[i * F1_LDA + c + t];
       st_chunk8(smem_u32(AT) + sw_off16(C, i, c), x);
-      if (a_o) {
-        float* dst = a_o + cb * C * C + i * C + c;
-        *reinterpret_cast<float4*>(dst) = make_float4(x[0], x[1], x[2], x[3]);
-        *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
-      }
+      if (at_t) *reinterpret_cast<uint4*>(at_t + cb * TILE_CC + sw_off16(C, i, c)) = pack8(x);
     }
     __syncthreads();
 
     // 6. (b k) e^gc and (w v) tiles (rows j, columns d) in R1
-    for (int it = 0; it < (C * D / 8) / F1_THREADS; ++it) {
+    uint4 wa[UNITS], va[UNITS];
+#pragma unroll
+    for (int it = 0; it < UNITS; ++it) {
+      const int u_ = it * F1_THREADS + tid;
+      const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
+      wa[it] = *reinterpret_cast<const uint4*>(wg + gi);
+      va[it] = *reinterpret_cast<const uint4*>(v + gi);
+    }
+#pragma unroll
+    for (int it = 0; it < UNITS; ++it) {
       const int u_ = it * F1_THREADS + tid;
       const int i = u_ >> 4, c = (u_ & 15) << 3;
-      const int64_t gi = ix.row(b, t0 + i, h) + c;
       float kv[8], bv[8], wv[8], vv[8], x[8], y[8];
-      unpack8(*reinterpret_cast<const uint4*>(k + gi), kv);
-      unpack8(*reinterpret_cast<const uint4*>(bg + gi), bv);
-      unpack8(*reinterpret_cast<const uint4*>(wg + gi), wv);
-      unpack8(*reinterpret_cast<const uint4*>(v + gi), vv);
+      unpack8(ka[it], kv);
+      unpack8(ba[it], bv);
+      unpack8(wa[it], wv);
+      unpack8(va[it], vv);
       const float* gci = GC + i * D + c;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -389,8 +408,8 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     const unsigned char* __restrict__ wt_t, const unsigned char* __restrict__ u_t,
     const unsigned char* __restrict__ qg_t, const unsigned char* __restrict__ kg_t,
     const unsigned char* __restrict__ aqk_t, const float* __restrict__ gcl, float scale, int L, int H, int NC,
-    const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final, bf16* __restrict__ h_store,
-    bf16* __restrict__ vn_store, int* __restrict__ err) {
+    const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final, unsigned char* __restrict__ h_store,
+    unsigned char* __restrict__ vn_store, int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F2_BARS);  // full[2], mma1, mma2
@@ -441,7 +460,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
 #pragma unroll
     for (int c = 0; c < D; c += 8) {
       st_chunk8(sH + sw_off16(D, dk, c), hr + c);
-      if (h_store) *reinterpret_cast<uint4*>(h_store + cbn * D * D + dk * D + c) = pack8(hr + c);
+      if (h_store) *reinterpret_cast<uint4*>(h_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, c)) = pack8(hr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -474,7 +493,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = uu[e] - x[c + e];
             st_chunk8(sVN + sw_off16(C, i, 32 * p + c), y);
-            if (vn_store) *reinterpret_cast<uint4*>(vn_store + cbn * C * D + i * D + 32 * p + c) = pack8(y);
+            if (vn_store) *reinterpret_cast<uint4*>(vn_store + cbn * TILE_CD + sw_off16(C, i, 32 * p + c)) = pack8(y);
           }
       }
     }
@@ -556,7 +575,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     const __grid_constant__ CUtensorMap tm_do, const unsigned char* __restrict__ wt_t,
     const unsigned char* __restrict__ qg_t, const unsigned char* __restrict__ kg_t,
     const unsigned char* __restrict__ aqk_t, const float* __restrict__ gcl, float scale, int L, int H, int NC,
-    const float* __restrict__ dh_final, bf16* __restrict__ dh_store, bf16* __restrict__ dvn_store,
+    const float* __restrict__ dh_final, unsigned char* __restrict__ dh_store, unsigned char* __restrict__ dvn_store,
     float* __restrict__ dh0, int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -612,7 +631,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
 #pragma unroll
     for (int c = 0; c < D; c += 8) {
       st_chunk8(sDH + sw_off16(D, dk, c), dr + c);
-      *reinterpret_cast<uint4*>(dh_store + cbn * D * D + dk * D + c) = pack8(dr + c);
+      *reinterpret_cast<uint4*>(dh_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, c)) = pack8(dr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -642,7 +661,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             st_chunk8(sDVN + sw_off16(C, i, 32 * p + c), x + c);
-            *reinterpret_cast<uint4*>(dvn_store + cbn * C * D + i * D + 32 * p + c) = pack8(x + c);
+            *reinterpret_cast<uint4*>(dvn_store + cbn * TILE_CD + sw_off16(C, i, 32 * p + c)) = pack8(x + c);
           }
       }
     }
@@ -687,6 +706,488 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   if (warp == 0) sm100::tmem_dealloc(tmem, 512);
 }
 
+// ============================================================ chunk-parallel backward
+// One CTA per chunk, 256 threads.  Everything per (row i, channel d) is held transposed: the
+// M = 128 accumulators have the channel as TMEM lane, so thread d assembles channel d of the
+// chunk and runs the reverse cumulative sum of dg down its own column.
+// Reference B2-B5 (`atomic_ops/kernel_bwd_b2_dav.py:17-51`, `kernel_bwd_b3_wy_dqkg.py:33-148`,
+// `kernel_bwd_b4_intra.py:57-165`, `kernel_bwd_b5_reverse_cumsum.py:17-24`).
+//   states:  P1 = h do^T, P2 = dh' vn^T, P3 = h dvn^T   ([dk][i], M = 128)
+//            Gqk = do vn^T (causal)                     ([i][j], M = 64)
+//   WY:      dA = dvn (w v)^T + dw~ (bk e^gc)^T, dw~ = -P3^T (strictly lower)
+//            d(wv)^T = dvn^T A, dbke^T = dw~^T A        ([d][j], M = 128) -> dv, dw
+//            T = dA A^T, Gkk = -(A^T T) (strictly lower)
+//   intra:   row side per reference block I (r = 16 I): dq_b, dbk_b for the rows of block I
+//              [d][i] += (k e^{gc_r - gc})[j][d] G[i][j]      then x e^{gc_i - gc_r}
+//            column side per key block J (s = 16 J + 15): dk_b for the columns of block J
+//              [d][j] += (x e^{gc - gc_s})[i][d] G^T[j][i]    then x e^{gc_s - gc_j}
+//            (diagonal blocks with a 16-row decay span > 60: exact per-channel sums instead)
+//   assembly: dq, dk, db, dgc; dg = reverse cumsum of dgc (+ dgcl at the last row)
+// Exact per-channel sums of a diagonal 16 x 16 block of the intra backward (channel d, row /
+// column i of block [i0, i0 + 16)), exponent floored at -20 as in the reference; used only for
+// blocks whose decay span is too wide for the factorised products.
+__device__ __noinline__ void bc_exact_diag(const unsigned char* G, const float* GC, const bf16* q, const bf16* k,
+                                           const bf16* bg, SeqIdx ix, int b, int64_t t0, int h, int d, int i0,
+                                           int i, float scale, float& dq_b, float& dbk_b, float& dk_b) {
+  const float gci = GC[i * D + d];
+  for (int j = i0; j <= i; ++j) {
+    const int64_t gj = ix.row(b, t0 + j, h) + d;
+    const float e = __expf(fmaxf(gci - GC[j * D + d], -20.f));
+    const float kj = __bfloat162float(k[gj]);
+    dq_b += scale * __bfloat162float(*reinterpret_cast<const bf16*>(G + sw_off(128, i, j))) * kj * e;
+    if (j < i) dbk_b += __bfloat162float(*reinterpret_cast<const bf16*>(G + sw_off(128, C + i, j))) * kj * e;
+  }
+  for (int i2 = i; i2 < i0 + 16; ++i2) {
+    const int64_t g2 = ix.row(b, t0 + i2, h) + d;
+    const float e = __expf(fmaxf(GC[i2 * D + d] - gci, -20.f));
+    float t = scale * __bfloat162float(*reinterpret_cast<const bf16*>(G + sw_off(128, i2, i))) *
+              __bfloat162float(q[g2]);
+    if (i2 > i)
+      t += __bfloat162float(*reinterpret_cast<const bf16*>(G + sw_off(128, C + i2, i))) *
+           __bfloat162float(bg[g2]) * __bfloat162float(k[g2]);
+    dk_b += t * e;
+  }
+}
+
+constexpr int BC_THREADS = 256;
+constexpr int BC_H = 0, BC_DH = 32768, BC_DO = 65536, BC_VN = 81920, BC_DVN = 98304, BC_AT = 114688;
+constexpr int BC_GC = 122880;  // fp32 [64][128]
+constexpr int BC_BAR = BC_GC + 32768;
+// reuse after the state products: WV @0, BKE @16K, DWT (rows dk, columns i) @32K, DA @48K, T @56K,
+// G (rows: Gqk i, then Gkk i; columns j) @64K, GT (rows: Gqk^T j, then Gkk^T j) @80K;
+// row-side key operands @0 / @16K; column-side operands (q part, bk part) @0+16K / @32K+48K
+constexpr int BC_WV = 0, BC_BKE = 16384, BC_DWT = 32768, BC_DA = 49152, BC_T = 57344, BC_G = 65536, BC_GT = 81920;
+// assembly: plain q, k, b rows over the dead column-side buffer 1 and the dv_new tile
+constexpr int BC_QP = 32768, BC_KP = 49152, BC_BP = 98304;
+constexpr size_t BC_SMEM = 1024 + BC_BAR + 512;
+
+__global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
+    const __grid_constant__ CUtensorMap tm_do, const bf16* __restrict__ q, const bf16* __restrict__ k,
+    const bf16* __restrict__ v, const float* __restrict__ g, const bf16* __restrict__ bg,
+    const bf16* __restrict__ wgate, const unsigned char* __restrict__ hs_t, const unsigned char* __restrict__ dhs_t,
+    const unsigned char* __restrict__ vn_t, const unsigned char* __restrict__ dvn_t,
+    const unsigned char* __restrict__ at_t, float scale, int L, int H, bf16* __restrict__ dq_o,
+    bf16* __restrict__ dk_o, bf16* __restrict__ dv_o, bf16* __restrict__ db_o, bf16* __restrict__ dw_o,
+    float* __restrict__ dg_o, int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t S = smem_u32(smem);
+  float* GC = reinterpret_cast<float*>(smem + BC_GC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BC_BAR);  // 0 load, 1 states, 2 WY, 3 T, 4 Gkk, 5-8 rows, 9-12 cols
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);          // [0..3] exact diagonal block, [4] abort
+  float* span_w = reinterpret_cast<float*>(flags + 8);         // [4][4]
+  float* dgcl_s = span_w + 16;                                 // [128]
+  float* tail_s = dgcl_s + 128;                                // [128] reverse-sum hand-over between warpgroups
+
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quarter = warp & 3, wg = warp >> 2;
+  const SeqIdx ix{L, H};
+  const int64_t t0 = (int64_t)n * C;
+  const int64_t cb = ((int64_t)b * H + h) * NC + n;
+
+  if (tid == 0) {
+    for (int i = 0; i < 13; ++i) sm100::mbar_init(bars + i, 1);
+    flags[4] = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tm_do);
+  }
+  if (warp == 0) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    sm100::mbar_expect_tx(bars, 2 * (2 * TILE_CD) + 3 * TILE_CD + TILE_CC);
+    bulk_g2s(smem + BC_H, hs_t + cb * (2 * TILE_CD), 2 * TILE_CD, bars);
+    bulk_g2s(smem + BC_DH, dhs_t + cb * (2 * TILE_CD), 2 * TILE_CD, bars);
+    bulk_g2s(smem + BC_VN, vn_t + cb * TILE_CD, TILE_CD, bars);
+    bulk_g2s(smem + BC_DVN, dvn_t + cb * TILE_CD, TILE_CD, bars);
+    bulk_g2s(smem + BC_AT, at_t + cb * TILE_CC, TILE_CC, bars);
+    tma_load_3d(smem + BC_DO, &tm_do, bars, 0, h, (int)(b * L + t0));
+    tma_load_3d(smem + BC_DO + TILE_CD / 2, &tm_do, bars, 64, h, (int)(b * L + t0));
+  }
+  // this thread's 16-byte units of the chunk's q, k, b, w, v rows (unit it: row 16 it + tid / 16,
+  // columns 8 (tid % 16) ..), requested up front and kept in registers for every later use
+  constexpr int BU = (C * D / 8) / BC_THREADS;
+  uint4 qa[BU], ka[BU], ba[BU], wa[BU], va[BU];
+#pragma unroll
+  for (int it = 0; it < BU; ++it) {
+    const int64_t gi = ix.row(b, t0 + 16 * it + (tid >> 4), h) + ((tid & 15) << 3);
+    qa[it] = *reinterpret_cast<const uint4*>(q + gi);
+    ka[it] = *reinterpret_cast<const uint4*>(k + gi);
+    ba[it] = *reinterpret_cast<const uint4*>(bg + gi);
+    wa[it] = *reinterpret_cast<const uint4*>(wgate + gi);
+    va[it] = *reinterpret_cast<const uint4*>(v + gi);
+  }
+#pragma unroll
+  for (int e = tid; e < C * (D / 4); e += BC_THREADS) {
+    const int r = e >> 5, c4 = (e & 31) << 2;
+    *reinterpret_cast<float4*>(GC + r * D + c4) = *reinterpret_cast<const float4*>(g + ix.row(b, t0 + r, h) + c4);
+  }
+  __syncthreads();
+  if (!wait_bar(bars, 0, err, 0x4731)) flags[4] = 1;
+  // state products (one thread issues; the others scan g meanwhile)
+  if (tid == 0 && !flags[4]) {
+    sm100::tc_fence_after();
+    constexpr uint32_t ID_P = sm100::idesc_bf16(128, 64, false, false);
+    constexpr uint32_t ID_G = sm100::idesc_bf16(64, 64, false, false);
+    auto fh = [&](int s) { return kdesc(S + BC_H, D, s); };
+    mma_steps(tmem + 0, fh, [&](int s) { return kdesc(S + BC_DO, C, s); }, D / 16, ID_P, false);
+    mma_steps(tmem + 64, [&](int s) { return kdesc(S + BC_DH, D, s); }, [&](int s) { return kdesc(S + BC_VN, C, s); },
+              D / 16, ID_P, false);
+    mma_steps(tmem + 128, fh, [&](int s) { return kdesc(S + BC_DVN, C, s); }, D / 16, ID_P, false);
+    mma_steps(tmem + 192, [&](int s) { return kdesc(S + BC_DO, C, s); }, [&](int s) { return kdesc(S + BC_VN, C, s); },
+              D / 16, ID_G, false);
+    sm100::umma_commit(bars + 1);
+  }
+  if (tid < D) {
+    const int d = tid;
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) {
+      s += GC[r * D + d];
+      GC[r * D + d] = s;
+    }
+    float sp[4];
+#pragma unroll
+    for (int I = 0; I < 4; ++I) sp[I] = warp_max(GC[16 * I * D + d] - GC[(16 * I + 15) * D + d]);
+    if (lane == 0)
+#pragma unroll
+      for (int I = 0; I < 4; ++I) span_w[warp * 4 + I] = sp[I];
+    // e^{gcl} sum_dv dh'[d][dv] h[d][dv] (state rows d of the two tile images)
+    float acc = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < D; c += 8) {
+      float a8[8], b8[8];
+      unpack8(*reinterpret_cast<const uint4*>(smem + BC_H + sw_off16(D, d, c)), a8);
+      unpack8(*reinterpret_cast<const uint4*>(smem + BC_DH + sw_off16(D, d, c)), b8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += a8[e] * b8[e];
+    }
+    dgcl_s[d] = __expf(s) * acc;
+  }
+  __syncthreads();
+  if (tid < 4) {
+    const float m = fmaxf(fmaxf(span_w[tid], span_w[4 + tid]), fmaxf(span_w[8 + tid], span_w[12 + tid]));
+    flags[tid] = !(m <= 60.f);
+  }
+  if (!wait_bar(bars + 1, 0, err, 0x4732)) flags[4] = 1;
+  sm100::tc_fence_after();
+  // WV = w v and BKE = (b k) e^gc over the dead state tiles; the H region is free once the
+  // state products completed
+#pragma unroll
+  for (int it = 0; it < BU; ++it) {
+    const int i = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+    float kv[8], bv[8], wv[8], vv[8], x[8], y[8];
+    unpack8(ka[it], kv);
+    unpack8(ba[it], bv);
+    unpack8(wa[it], wv);
+    unpack8(va[it], vv);
+    const float* gci = GC + i * D + c;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      x[e] = wv[e] * vv[e];
+      y[e] = bv[e] * kv[e] * __expf(gci[e]);
+    }
+    st_chunk8(S + BC_WV + sw_off16(C, i, c), x);
+    st_chunk8(S + BC_BKE + sw_off16(C, i, c), y);
+  }
+  // dw~^T = -P3 -> DWT tile (rows dk, columns i); warpgroup wg takes columns [32 wg, 32 wg + 32)
+  {
+    const int dk = 32 * quarter + lane;
+    float x[32];
+    tmem_ld32(tmem_at(tmem, quarter, 128 + 32 * wg), x);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) x[c] = -x[c];
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) st_chunk8(S + BC_DWT + sw_off16(D, dk, 32 * wg + c), x + c);
+  }
+  // Gqk = do vn^T (causal) -> rows 0-63 of G and G^T (warpgroup 0, lanes 0-15: row i)
+  if (wg == 0) {
+    const int i = 16 * quarter + lane;
+    float x[64];
+    tmem_ld32(tmem_at(tmem, quarter, 192), x);
+    tmem_ld32(tmem_at(tmem, quarter, 224), x + 32);
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) x[j] = j <= i ? x[j] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_G + sw_off16(128, i, c), x + c);
+      unsigned char* gt = smem + BC_GT;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        *reinterpret_cast<bf16*>(gt + sw_off(128, j, i)) = __float2bfloat16_rn(x[j]);
+    }
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (flags[4]) goto bc_teardown;
+  // WY products: dA (M = 64) -> [256, 320); d(wv)^T -> [320, 384); dbke^T -> [384, 448)
+  if (tid == 0) {
+    sm100::tc_fence_after();
+    mma_steps(tmem + 256, [&](int s) { return kdesc(S + BC_DVN, C, s); }, [&](int s) { return kdesc(S + BC_WV, C, s); },
+              D / 16, sm100::idesc_bf16(64, 64, false, false), false);
+    mma_steps(tmem + 256, [&](int s) { return mndesc(S + BC_DWT, D, s); }, [&](int s) { return kdesc(S + BC_BKE, C, s); },
+              D / 16, sm100::idesc_bf16(64, 64, true, false), true);
+    auto fat = [&](int s) { return mndesc(S + BC_AT, C, s); };
+    mma_steps(tmem + 320, [&](int s) { return mndesc(S + BC_DVN, C, s); }, fat, C / 16,
+              sm100::idesc_bf16(128, 64, true, true), false);
+    mma_steps(tmem + 384, [&](int s) { return kdesc(S + BC_DWT, D, s); }, fat, C / 16,
+              sm100::idesc_bf16(128, 64, false, true), false);
+    sm100::umma_commit(bars + 2);
+  }
+  if (!wait_bar(bars + 2, 0, err, 0x4733)) flags[4] = 1;
+  sm100::tc_fence_after();
+  // dA strictly lower -> DA tile (rows i, columns l)
+  if (wg == 0) {
+    const int i = 16 * quarter + lane;
+    float x[64];
+    tmem_ld32(tmem_at(tmem, quarter, 256), x);
+    tmem_ld32(tmem_at(tmem, quarter, 288), x + 32);
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) x[j] = j < i ? x[j] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_DA + sw_off16(C, i, c), x + c);
+    }
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && !flags[4]) {
+    sm100::tc_fence_after();
+    mma_steps(tmem + 448, [&](int s) { return kdesc(S + BC_DA, C, s); }, [&](int s) { return kdesc(S + BC_AT, C, s); },
+              C / 16, sm100::idesc_bf16(64, 64, false, false), false);
+    sm100::umma_commit(bars + 3);
+  }
+  // dv, dw from d(wv)^T (lane = channel d, column j): transposed through shared memory (fp32 rows
+  // j over the dead (w v | bke) tiles), then row units times the held v / w rows
+  {
+    const int d = 32 * quarter + lane;
+    float* DWV = reinterpret_cast<float*>(smem + BC_WV);
+    float x[32];
+    tmem_ld32(tmem_at(tmem, quarter, 320 + 32 * wg), x);
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) DWV[(32 * wg + jj) * D + d] = x[jj];
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < BU; ++it) {
+      const int j = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+      float vv[8], ww[8], y[8], z[8];
+      unpack8(va[it], vv);
+      unpack8(wa[it], ww);
+      const float4 a0 = *reinterpret_cast<const float4*>(DWV + j * D + c);
+      const float4 a1 = *reinterpret_cast<const float4*>(DWV + j * D + c + 4);
+      const float xx[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        y[e] = xx[e] * vv[e];
+        z[e] = xx[e] * ww[e];
+      }
+      const int64_t gi = ix.row(b, t0 + j, h) + c;
+      *reinterpret_cast<uint4*>(dw_o + gi) = pack8(y);
+      *reinterpret_cast<uint4*>(dv_o + gi) = pack8(z);
+    }
+  }
+  if (!wait_bar(bars + 3, 0, err, 0x4734)) flags[4] = 1;
+  sm100::tc_fence_after();
+  // T = dA A^T -> T tile (rows l, columns j)
+  if (wg == 0) {
+    const int i = 16 * quarter + lane;
+    float x[64];
+    tmem_ld32(tmem_at(tmem, quarter, 448), x);
+    tmem_ld32(tmem_at(tmem, quarter, 480), x + 32);
+    if (lane < 16)
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_T + sw_off16(C, i, c), x + c);
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && !flags[4]) {
+    sm100::tc_fence_after();
+    mma_steps(tmem + 256, [&](int s) { return mndesc(S + BC_AT, C, s); }, [&](int s) { return mndesc(S + BC_T, C, s); },
+              C / 16, sm100::idesc_bf16(64, 64, true, true), false);
+    sm100::umma_commit(bars + 4);
+  }
+  if (!wait_bar(bars + 4, 0, err, 0x4735)) flags[4] = 1;
+  sm100::tc_fence_after();
+  // Gkk = -(A^T T) strictly lower -> rows 64-127 of G and G^T
+  if (wg == 0) {
+    const int i = 16 * quarter + lane;
+    float x[64];
+    tmem_ld32(tmem_at(tmem, quarter, 256), x);
+    tmem_ld32(tmem_at(tmem, quarter, 288), x + 32);
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) x[j] = j < i ? -x[j] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_G + sw_off16(128, C + i, c), x + c);
+      unsigned char* gt = smem + BC_GT;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        *reinterpret_cast<bf16*>(gt + sw_off(128, C + j, i)) = __float2bfloat16_rn(x[j]);
+    }
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (flags[4]) goto bc_teardown;
+  // intra, row side: per reference block I, key operand (k e^{gc_r - gc})[j][d] for j <= 16 I + 15;
+  // dq_b -> TMEM [128 + 32 I, +16), dbk_b -> [144 + 32 I, +16) (lane d, column i - 16 I)
+#pragma unroll
+  for (int I = 0; I < 4; ++I) {
+    const uint32_t buf = S + (I & 1) * TILE_CD;
+    if (I >= 2 && !wait_bar(bars + 5 + I - 2, 0, err, 0x4736)) flags[4] = 1;
+    const bool exact = flags[I];
+    const float* gcr = GC + 16 * I * D;
+#pragma unroll
+    for (int it = 0; it <= I; ++it) {
+      const int j = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+      float kv[8], o[8];
+      unpack8(ka[it], kv);
+      const bool zero = exact && j >= 16 * I;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gcr[c + e] - GC[j * D + c + e]);
+      st_chunk8(buf + sw_off16(C, j, c), o);
+    }
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t ID_R = sm100::idesc_bf16(128, 16, true, false);
+      auto fa = [&](int s) { return mndesc(buf, C, s); };
+      mma_steps(tmem + 128 + 32 * I, fa, [&](int s) { return kdesc(S + BC_G + 2048 * I, 128, s); }, I + 1, ID_R, false);
+      mma_steps(tmem + 144 + 32 * I, fa, [&](int s) { return kdesc(S + BC_G + 8192 + 2048 * I, 128, s); }, I + 1, ID_R,
+                false);
+      sm100::umma_commit(bars + 5 + I);
+    }
+  }
+  // intra, column side: per key block J with reference s = 16 J + 15 (its last row), operands
+  // (scale q e^{gc - gc_s}) and ((b k) e^{gc - gc_s}) for rows i >= 16 J (<= 1 below the block);
+  // dk_b -> TMEM [448 + 16 J, +16) (lane d, column j - 16 J), later times e^{gc_s - gc_j} <= 1
+#pragma unroll
+  for (int J = 0; J < 4; ++J) {
+    const uint32_t bq = S + (J & 1) * 32768, bk2 = bq + TILE_CD;
+    if (J == 0) {
+      if (!wait_bar(bars + 7, 0, err, 0x4737) || !wait_bar(bars + 8, 0, err, 0x4737)) flags[4] = 1;
+    } else if (J >= 2) {
+      if (!wait_bar(bars + 9 + J - 2, 0, err, 0x4738)) flags[4] = 1;
+    }
+    const bool exact = flags[J];
+    const float* gcr = GC + (16 * J + 15) * D;
+#pragma unroll
+    for (int it = J; it < BU; ++it) {
+      const int i = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+      float qv[8], kv[8], bv[8], xq[8], xk[8];
+      unpack8(qa[it], qv);
+      unpack8(ka[it], kv);
+      unpack8(ba[it], bv);
+      const bool zero = exact && i < 16 * J + 16;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float er = zero ? 0.f : __expf(GC[i * D + c + e] - gcr[c + e]);
+        xq[e] = scale * qv[e] * er;
+        xk[e] = bv[e] * kv[e] * er;
+      }
+      st_chunk8(bq + sw_off16(C, i, c), xq);
+      st_chunk8(bk2 + sw_off16(C, i, c), xk);
+    }
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      sm100::tc_fence_after();
+      constexpr uint32_t ID_C = sm100::idesc_bf16(128, 16, true, false);
+      const uint32_t dcol = tmem + 448 + 16 * J;
+      for (int s = J; s < 4; ++s)
+        sm100::umma_bf16(dcol, mndesc(bq, C, s), kdesc(S + BC_GT + 2048 * J, 128, s), ID_C, s > J ? 1u : 0u);
+      for (int s = J; s < 4; ++s)
+        sm100::umma_bf16(dcol, mndesc(bk2, C, s), kdesc(S + BC_GT + 8192 + 2048 * J, 128, s), ID_C, 1u);
+      sm100::umma_commit(bars + 9 + J);
+    }
+  }
+  if (!wait_bar(bars + 11, 0, err, 0x4739) || !wait_bar(bars + 12, 0, err, 0x4739)) flags[4] = 1;
+  sm100::tc_fence_after();
+  // plain row-major q, k, b tiles (256-byte rows) for the per-channel assembly reads
+#pragma unroll
+  for (int it = 0; it < BU; ++it) {
+    const int off = (16 * it + (tid >> 4)) * 256 + ((tid & 15) << 4);
+    *reinterpret_cast<uint4*>(smem + BC_QP + off) = qa[it];
+    *reinterpret_cast<uint4*>(smem + BC_KP + off) = ka[it];
+    *reinterpret_cast<uint4*>(smem + BC_BP + off) = ba[it];
+  }
+  __syncthreads();
+  if (flags[4]) goto bc_teardown;
+  {
+    // assembly: thread d = channel, warpgroup wg = rows [32 wg, 32 wg + 32), one 16-row block at a time
+    const int d = 32 * quarter + lane;
+    float* DGC = reinterpret_cast<float*>(smem);  // dgc rows (the operand buffers are dead)
+    const unsigned char* G = smem + BC_G;
+    const float gcl = GC[(C - 1) * D + d];
+    float dgcl_part = 0.f;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      const int I = 2 * wg + half, i0 = 16 * I;
+      float p1[16], p2[16], w3[16], rq[16], rk[16], ck[16];
+      tmem_ld16(tmem_at(tmem, quarter, i0), p1);
+      tmem_ld16(tmem_at(tmem, quarter, 64 + i0), p2);
+      tmem_ld16(tmem_at(tmem, quarter, 384 + i0), w3);
+      tmem_ld16(tmem_at(tmem, quarter, 128 + 32 * I), rq);
+      tmem_ld16(tmem_at(tmem, quarter, 144 + 32 * I), rk);
+      tmem_ld16(tmem_at(tmem, quarter, 448 + i0), ck);
+      const float gr = GC[i0 * D + d], gs = GC[(i0 + 15) * D + d];
+      const bool exact = flags[I];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int i = i0 + r;
+        const int64_t gi = ix.row(b, t0 + i, h) + d;
+        const int po = i * 256 + 2 * d;
+        const float qi = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_QP + po));
+        const float ki = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_KP + po));
+        const float bi = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_BP + po));
+        const float gci = GC[i * D + d];
+        float dq_b = scale * __expf(gci - gr) * rq[r];
+        float dbk_b = __expf(gci - gr) * rk[r];
+        float dk_b = __expf(gs - gci) * ck[r];
+        if (exact) bc_exact_diag(G, GC, q, k, bg, ix, b, t0, h, d, i0, i, scale, dq_b, dbk_b, dk_b);
+        const float eg = __expf(gci), el = __expf(gcl - gci);
+        const float dq_a = scale * p1[r] * eg, dk_a = p2[r] * el, dbk_wy = w3[r] * eg;
+        const float bki = bi * ki;
+        const float dbk = dbk_wy + dbk_b;
+        dq_o[gi] = __float2bfloat16_rn(dq_a + dq_b);
+        dk_o[gi] = __float2bfloat16_rn(dk_a + dk_b + dbk * bi);
+        db_o[gi] = __float2bfloat16_rn(dbk * ki);
+        DGC[i * D + d] = dq_a * qi - dk_a * ki + dbk_wy * bki + qi * dq_b + bki * dbk_b - ki * dk_b;
+        dgcl_part += dk_a * ki;
+      }
+    }
+    // dg = dgcl + reverse cumulative sum of dgc; rows 32-63 (warpgroup 1) hand their total to rows 0-31
+    float tot = 0.f;
+    for (int r = 0; r < 32; ++r) tot += DGC[(32 * wg + r) * D + d];
+    if (wg == 1) {
+      tail_s[d] = tot;
+      dgcl_s[d] += dgcl_part;  // after the first barrier below warpgroup 0 adds its own part
+    }
+    __syncthreads();
+    if (wg == 0) dgcl_s[d] += dgcl_part;
+    __syncthreads();
+    float run = dgcl_s[d] + (wg == 0 ? tail_s[d] : 0.f);
+    for (int r = 31; r >= 0; --r) {
+      const int i = 32 * wg + r;
+      run += DGC[i * D + d];
+      dg_o[ix.row(b, t0 + i, h) + d] = run;
+    }
+  }
+bc_teardown:
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+}
+
 template <class K>
 int set_smem(K kernel, size_t bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess ? 0 : -3;
@@ -697,13 +1198,13 @@ int set_smem(K kernel, size_t bytes) {
 // ===================================================================== launchers
 int ahb_gdn_chunk_fwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
                          float scale, int B, int L, int H, void* wt_t, void* u_t, void* qg_t, void* kg_t, void* aqk_t,
-                         float* gcl, float* a_out, int* err, cudaStream_t st) {
+                         float* gcl, void* at_t, int* err, cudaStream_t st) {
   static int init = set_smem(gdn_chunk_fwd_tc, F1_SMEM);
   if (init) return init;
   gdn_chunk_fwd_tc<<<dim3(L / C, H, B), F1_THREADS, F1_SMEM, st>>>(
       (const bf16*)q, (const bf16*)k, (const bf16*)v, g, (const bf16*)bg, (const bf16*)wg, scale, L, H,
       (unsigned char*)wt_t, (unsigned char*)u_t, (unsigned char*)qg_t, (unsigned char*)kg_t, (unsigned char*)aqk_t,
-      gcl, a_out, err);
+      gcl, (unsigned char*)at_t, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -714,8 +1215,8 @@ int ahb_gdn_state_fwd_tc(const void* wt_t, const void* u_t, const void* qg_t, co
   if (init) return init;
   gdn_state_fwd_tc<<<dim3(H, B), F2_THREADS, F2_SMEM, st>>>(
       (const unsigned char*)wt_t, (const unsigned char*)u_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
-      (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, h0, (bf16*)o, h_final, (bf16*)h_store, (bf16*)vn_store,
-      err);
+      (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, h0, (bf16*)o, h_final, (unsigned char*)h_store,
+      (unsigned char*)vn_store, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -728,6 +1229,22 @@ int ahb_gdn_state_bwd_tc(const void* wt_t, const void* qg_t, const void* kg_t, c
   if (tmap_seq_bf16(&tm, dout, (int64_t)B * L, H, D, C)) return -20;
   gdn_state_bwd_tc<<<dim3(H, B), B1_THREADS, B1_SMEM, st>>>(
       tm, (const unsigned char*)wt_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
-      (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, dh_final, (bf16*)dh_store, (bf16*)dvn_store, dh0, err);
+      (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, dh_final, (unsigned char*)dh_store,
+      (unsigned char*)dvn_store, dh0, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+int ahb_gdn_chunk_bwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                         const void* dout, const void* hs_t, const void* dhs_t, const void* vn_t, const void* dvn_t,
+                         const void* at_t, float scale, int B, int L, int H, void* dq, void* dk, void* dv, void* db,
+                         void* dw, float* dg, int* err, cudaStream_t st) {
+  static int init = set_smem(gdn_chunk_bwd_tc, BC_SMEM);
+  if (init) return init;
+  CUtensorMap tm;
+  if (tmap_seq_bf16(&tm, dout, (int64_t)B * L, H, D, C)) return -20;
+  gdn_chunk_bwd_tc<<<dim3(L / C, H, B), BC_THREADS, BC_SMEM, st>>>(
+      tm, (const bf16*)q, (const bf16*)k, (const bf16*)v, g, (const bf16*)bg, (const bf16*)wg,
+      (const unsigned char*)hs_t, (const unsigned char*)dhs_t, (const unsigned char*)vn_t, (const unsigned char*)dvn_t,
+      (const unsigned char*)at_t, scale, L, H, (bf16*)dq, (bf16*)dk, (bf16*)dv, (bf16*)db, (bf16*)dw, dg, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }

@@ -27,33 +27,25 @@ void ahb_embedding_fwd(const int64_t* ids, const void* emb, int edtype, void* ou
 void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* acc, int64_t T, int D, int64_t V,
                        cudaStream_t st);
 
-// gdn.cu (head dim 128, chunk 64; all sequence tensors (B, L, H, 128), chunk tensors (B, H, L/64, 64, .))
-int ahb_gdn_supported(int D);
+// GDN-2 (head dim 128, chunk 64; sequence tensors (B, L, H, 128), chunk tensors (B, H, L/64, ...))
 // gdn_tc.cu: chunk-local forward and the two state recurrences on tcgen05.  The chunk
 // intermediates wt/u/qg/kg (B, H, L/64, 64 x 128) and aqk (B, H, L/64, 64 x 64) are bf16 tile
-// images in the 128-byte-swizzled shared-memory layout; a_out is plain fp32 (B, H, L/64, 64, 64);
-// h_store / vn_store / dh_store / dvn_store are plain bf16 row-major chunk tensors.
+// images in the 128-byte-swizzled shared-memory layout, as are at_t (A, 64 x 64), h_store /
+// dh_store (128 x 128 per chunk) and vn_store / dvn_store (64 x 128 per chunk).
 // Return 0, or a negative code when a launch or set-up failed; `err` receives device timeouts.
 int ahb_gdn_chunk_fwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
                          float scale, int B, int L, int H, void* wt_t, void* u_t, void* qg_t, void* kg_t, void* aqk_t,
-                         float* gcl, float* a_out, int* err, cudaStream_t st);
+                         float* gcl, void* at_t, int* err, cudaStream_t st);
 int ahb_gdn_state_fwd_tc(const void* wt_t, const void* u_t, const void* qg_t, const void* kg_t, const void* aqk_t,
                          const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
                          void* h_store, void* vn_store, int* err, cudaStream_t st);
 int ahb_gdn_state_bwd_tc(const void* wt_t, const void* qg_t, const void* kg_t, const void* aqk_t, const float* gcl,
                          const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
                          void* dvn_store, float* dh0, int* err, cudaStream_t st);
-void ahb_gdn_bwd_states(const void* q, const void* k, const float* g, const void* dout, const void* h_store,
-                        const void* dh_store, const void* vn_store, const void* dvn_store, float scale, int B, int L,
-                        int H, float* dq_p, float* dk_p, float* dgc_p, float* dwt, float* dgcl, float* daqk,
-                        cudaStream_t st);
-void ahb_gdn_bwd_wy(const void* k, const void* v, const float* g, const void* bg, const void* wg,
-                    const float* a_store, const void* dvn_store, const float* dwt, int B, int L, int H, void* dv,
-                    void* dw, float* dbk_wy, float* dgc_wy, float* dakk, cudaStream_t st);
-void ahb_gdn_bwd_intra(const void* q, const void* k, const float* g, const void* bg, const float* daqk,
-                       const float* dakk, const float* dq_p, const float* dk_p, const float* dgc_p,
-                       const float* dbk_wy, const float* dgc_wy, const float* dgcl, float scale, int B, int L, int H,
-                       void* dq, void* dk, void* db, float* dg, cudaStream_t st);
+int ahb_gdn_chunk_bwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
+                         const void* dout, const void* hs_t, const void* dhs_t, const void* vn_t, const void* dvn_t,
+                         const void* at_t, float scale, int B, int L, int H, void* dq, void* dk, void* dv, void* db,
+                         void* dw, float* dg, int* err, cudaStream_t st);
 
 // ssd.cu (head dim 64, d_state 128, chunk 64; x, dt (B,L,H,64); B, C (B,L,128); A (H,) fp32)
 int ahb_ssd_supported(int P, int N);

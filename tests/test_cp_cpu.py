@@ -2,7 +2,6 @@
 the scans pass their states across the segment boundaries, the convolutions a halo, MLA
 the latent of every position.  The loss and gradients equal the single-rank model's."""
 import os
-import socket
 
 import pytest
 import torch
@@ -13,14 +12,9 @@ from atomic_ai_hybrid_b200 import get_preset
 from atomic_ai_hybrid_b200.models import HybridMoEModel
 from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
 from atomic_ai_hybrid_b200.training.loss import compute_loss
+from _dist import collect, free_port as _port, threads_per_rank
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
 
 
 def _cfg(kind):
@@ -33,7 +27,7 @@ def _cfg(kind):
 def _worker(rank, world, port, kind, q, cp=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+    torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.parallel.cp import init_context_parallel
         cfg = _cfg(kind)
@@ -85,7 +79,7 @@ def test_cp_matches_single_rank(kind, world, cp):
     procs = [ctx.Process(target=_worker, args=(r, world, port, kind, q, cp)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in procs)
+    res = dict(collect(procs, q, len(procs), 600))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

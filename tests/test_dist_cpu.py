@@ -2,7 +2,6 @@
 reduce-scatter / all-gather must reproduce single-process training on the same
 global batch."""
 import os
-import socket
 
 import pytest
 import torch
@@ -12,14 +11,9 @@ import torch.multiprocessing as mp
 from atomic_ai_hybrid_b200 import get_preset
 from atomic_ai_hybrid_b200.models import HybridMoEModel
 from atomic_ai_hybrid_b200.training.trainer import Trainer
+from _dist import collect, free_port as _port, threads_per_rank
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
 
 
 def _cfg():
@@ -37,7 +31,7 @@ def _run(rank, world, port, out_path, steps):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
-        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # no oversubscription of the cores
+        torch.set_num_threads(threads_per_rank(world))
     cfg = _cfg()
     torch.manual_seed(0)
     m = HybridMoEModel(cfg, compute_dtype=torch.float32)

@@ -2,7 +2,6 @@
 the model with its routed experts split over 2, 4 or 8 ranks gives the single-rank loss and
 gradients, and trains like it."""
 import os
-import socket
 
 import pytest
 import torch
@@ -13,14 +12,9 @@ from atomic_ai_hybrid_b200 import get_preset
 from atomic_ai_hybrid_b200.models import HybridMoEModel
 from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
 from atomic_ai_hybrid_b200.training.loss import compute_loss
+from _dist import collect, free_port as _port, threads_per_rank
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
 
 
 def _cfg(world=2):
@@ -31,7 +25,7 @@ def _cfg(world=2):
 def _worker(rank, world, port, q, ep=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # no oversubscription of the cores
+    torch.set_num_threads(threads_per_rank(world))
     try:
         cfg = _cfg(world)
         # every rank: the single-rank model on the whole global batch (2 sequences per rank)
@@ -91,7 +85,7 @@ def test_ep_collective_matches_single_rank(world, ep):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q, ep)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    res = dict(collect(procs, q, len(procs), 300))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

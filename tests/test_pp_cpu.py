@@ -2,7 +2,6 @@
 first with the embedding, the last with the final norm and the tied LM head) train like
 the single-rank model -- same losses and gradient norms per step, same weights after."""
 import os
-import socket
 
 import pytest
 import torch
@@ -14,12 +13,7 @@ from atomic_ai_hybrid_b200.models import HybridMoEModel
 from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+from _dist import collect, free_port as _port, threads_per_rank
 
 
 def _cfg(layers):
@@ -32,7 +26,7 @@ def _run(rank, world, port, steps, layers, q, schedule="1f1b", dp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
-        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+        torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.training.trainer import Trainer
         from atomic_ai_hybrid_b200.parallel.pp import PipelineTrainer
@@ -79,7 +73,7 @@ def _reference(steps, layers):
     q = ctx.Queue()
     p1 = ctx.Process(target=_run, args=(0, 1, _port(), steps, layers, q))
     p1.start()
-    _, ref_hist, ref, _ = q.get(timeout=300)
+    (_, ref_hist, ref, _), = collect([p1], q, 1)
     p1.join(timeout=60)
     return ref_hist, ref
 
@@ -91,7 +85,7 @@ def _pipeline(world, steps, layers, schedule, dp=1):
     procs = [ctx.Process(target=_run, args=(r, world, port, steps, layers, q, schedule, dp)) for r in range(world)]
     for p in procs:
         p.start()
-    got = [q.get(timeout=300) for _ in procs]
+    got = collect(procs, q, len(procs))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -137,7 +131,7 @@ def test_pipeline_with_data_parallel_replicas():
 def _ckpt(rank, world, port, root, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+    torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
         from atomic_ai_hybrid_b200.parallel.pp import PipelineTrainer
@@ -174,7 +168,7 @@ def test_pp_checkpoint_restores_single_rank(tmp_path):
     procs = [ctx.Process(target=_ckpt, args=(r, 2, port, str(tmp_path), q)) for r in range(2)]
     for p in procs:
         p.start()
-    msgs = [q.get(timeout=300) for _ in range(3)]
+    msgs = collect(procs, q, 3)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -3,7 +3,6 @@ split over 2 ranks (token rows split between the mixers) must give the loss and
 gradients of the single-rank model with the same weights, and training with the
 tensor-parallel trainer must follow single-rank training."""
 import os
-import socket
 
 import pytest
 import torch
@@ -14,14 +13,9 @@ from atomic_ai_hybrid_b200 import get_preset
 from atomic_ai_hybrid_b200.models import HybridMoEModel
 from atomic_ai_hybrid_b200.parallel.context import ParallelContext, set_parallel_context
 from atomic_ai_hybrid_b200.training.loss import compute_loss
+from _dist import collect, free_port as _port, threads_per_rank
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
 
 
 def _cfg(kind, world=2):
@@ -42,7 +36,7 @@ def _loss_grads(model, ids):
 def _parity(rank, world, port, kind, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+    torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, shard_tensor
         cfg = _cfg(kind, world)
@@ -99,7 +93,7 @@ def test_tp_forward_backward_matches_single_rank(kind, world):
     procs = [ctx.Process(target=_parity, args=(r, world, port, kind, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in procs]
+    res = collect(procs, q, len(procs))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -114,7 +108,7 @@ def _train(rank, world, port, steps, q, optimizer="adamw"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if world > 1:
         dist.init_process_group("gloo", rank=rank, world_size=world)
-        torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+        torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, unshard_tensors, shard_spec
         from atomic_ai_hybrid_b200.training.trainer import Trainer
@@ -169,13 +163,13 @@ def test_tp2_training_follows_single_rank(optimizer):
     steps = 3
     p1 = ctx.Process(target=_train, args=(0, 1, _port(), steps, q, optimizer))
     p1.start()
-    ref_hist, ref = q.get(timeout=300)
+    (ref_hist, ref), = collect([p1], q, 1)
     p1.join(timeout=60)
     port = _port()
     procs = [ctx.Process(target=_train, args=(r, 2, port, steps, q, optimizer)) for r in range(2)]
     for p in procs:
         p.start()
-    hist, got = q.get(timeout=300)
+    (hist, got), = collect(procs, q, 1)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -207,7 +201,7 @@ def test_tp_checkpoint_pieces_reassemble_for_any_world():
 def _ckpt(rank, world, port, root, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))  # one share of the cores per rank
+    torch.set_num_threads(threads_per_rank(world))
     try:
         from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
         from atomic_ai_hybrid_b200.parallel.tp import init_tensor_parallel, load_full_state, shard_spec, unshard_tensors
@@ -275,7 +269,7 @@ def test_tp_checkpoint_restores_into_tp_and_single_rank(tmp_path):
     procs = [ctx.Process(target=_ckpt, args=(r, 2, port, str(tmp_path), q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    res = dict(collect(procs, q, len(procs), 300))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
