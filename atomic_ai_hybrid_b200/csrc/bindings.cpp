@@ -300,54 +300,78 @@ void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Ten
               "ssd: B, C must be (B,L,128)");
 }
 
-static std::vector<torch::Tensor> ssd_fwd_impl(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
-                                               torch::Tensor Cm) {
-  check_ssd(x, dt, A, Bm, Cm);
+struct SsdFwd { torch::Tensor y, sin_t, dec_t, cl; };
+
+// Forward (chunk kernel + state recurrence); with `keep_states` also the per-chunk incoming
+// states (tile images) the backward needs, beside the decay images and last cumsums.
+static SsdFwd ssd_forward(const torch::Tensor& x, const torch::Tensor& dt, const torch::Tensor& A,
+                          const torch::Tensor& Bm, const torch::Tensor& Cm, bool keep_states, bool want_y) {
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
-  auto f32 = x.options().dtype(at::kFloat);
-  auto sbuf = torch::empty({B, H, NC, 64, 128}, f32);
-  auto cuml = torch::empty({B, H, NC, 64}, f32);
-  auto y = torch::empty_like(x);
-  ahb_ssd_fwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
-              sbuf.data_ptr<float>(), cuml.data_ptr<float>(), nullptr, nullptr, y.data_ptr(), cur_stream());
-  check_launch("ahb_ssd_fwd");
-  return {y, sbuf, cuml};
+  auto bf = x.options();
+  SsdFwd f;
+  auto send = torch::empty({B, H, NC, 128, 64}, bf);
+  auto yd = torch::empty({B, H, NC, 64, 64}, bf);
+  f.dec_t = torch::empty({B, H, NC, 64, 64}, bf);
+  f.cl = torch::empty({B, H, NC, 64}, x.options().dtype(at::kFloat));
+  if (keep_states) f.sin_t = torch::empty({B, H, NC, 128, 64}, bf);
+  f.y = torch::empty_like(x);
+  check_rc(ahb_ssd_fwd_tc(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
+                          send.data_ptr(), yd.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), nullptr, nullptr,
+                          f.y.data_ptr(), keep_states ? f.sin_t.data_ptr() : nullptr, err_word().data_ptr<int>(),
+                          cur_stream()),
+           "ahb_ssd_fwd_tc");
+  (void)want_y;
+  return f;
 }
 
 torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm, torch::Tensor Cm) {
-  return ssd_fwd_impl(x, dt, A, Bm, Cm)[0];
+  check_ssd(x, dt, A, Bm, Cm);
+  return ssd_forward(x, dt, A, Bm, Cm, false, true).y;
 }
 
-// Forward for training: {y, chunk states (scanned), chunk decay cumsums}; ssd_bwd takes them back.
+// Forward for training: {y, incoming states (tile images), decay images, last cumsums}; ssd_bwd
+// takes the last three back.
 std::vector<torch::Tensor> ssd_fwd_train(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
                                          torch::Tensor Cm) {
-  return ssd_fwd_impl(x, dt, A, Bm, Cm);
+  check_ssd(x, dt, A, Bm, Cm);
+  auto f = ssd_forward(x, dt, A, Bm, Cm, true, true);
+  return {f.y, f.sin_t, f.dec_t, f.cl};
 }
 
 std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
                                    torch::Tensor Cm, torch::Tensor dy, c10::optional<torch::Tensor> states,
-                                   c10::optional<torch::Tensor> cumsums) {
+                                   c10::optional<torch::Tensor> decays, c10::optional<torch::Tensor> cumsums) {
   check_ssd(x, dt, A, Bm, Cm);
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
   auto dyc = dy.to(at::kBFloat16).contiguous();
   auto f32 = x.options().dtype(at::kFloat);
-  const bool ready = states.has_value() && states->defined() && cumsums.has_value() && cumsums->defined();
-  auto sbuf = ready ? *states : torch::empty({B, H, NC, 64, 128}, f32);
-  auto gbuf = torch::empty({B, H, NC, 64, 128}, f32);
-  auto cuml = ready ? *cumsums : torch::empty({B, H, NC, 64}, f32);
-  if (ready)
-    TORCH_CHECK(sbuf.is_contiguous() && sbuf.numel() == (int64_t)B * H * NC * 64 * 128 && cuml.numel() ==
-                    (int64_t)B * H * NC * 64, "ssd_bwd: saved states do not match");
+  const bool ready = states.has_value() && states->defined() && decays.has_value() && decays->defined() &&
+                     cumsums.has_value() && cumsums->defined();
+  SsdFwd f;
+  if (ready) {
+    f.sin_t = *states;
+    f.dec_t = *decays;
+    f.cl = *cumsums;
+    TORCH_CHECK(f.sin_t.numel() == (int64_t)B * H * NC * 128 * 64 && f.dec_t.numel() == (int64_t)B * H * NC * 64 * 64 &&
+                    f.cl.numel() == (int64_t)B * H * NC * 64,
+                "ssd_bwd: saved states do not match");
+  } else {
+    f = ssd_forward(x, dt, A, Bm, Cm, true, false);
+  }
+  auto st = cur_stream();
+  auto dse = torch::empty({B, H, NC, 128, 64}, x.options());
+  check_rc(ahb_ssd_state_bwd_tc(Cm.data_ptr(), dyc.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), B, L, H,
+                                nullptr, dse.data_ptr(), nullptr, err_word().data_ptr<int>(), st),
+           "ahb_ssd_state_bwd_tc");
   auto dx = torch::empty_like(x), ddt = torch::empty_like(x);
   auto dB = torch::empty(Bm.sizes(), f32), dC = torch::empty(Cm.sizes(), f32);
   auto dA = torch::zeros({H}, f32);
   const int G = ahb_ssd_head_groups(H);
   auto dBp = torch::empty({G, B, L, 128}, f32), dCp = torch::empty({G, B, L, 128}, f32);
-  ahb_ssd_bwd(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B, L,
-              H, sbuf.data_ptr<float>(), cuml.data_ptr<float>(), gbuf.data_ptr<float>(), dx.data_ptr(),
-              ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(),
-              dCp.data_ptr<float>(), ready ? 1 : 0, cur_stream());
-  check_launch("ahb_ssd_bwd");
+  ahb_ssd_bwd_chunk(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B,
+                    L, H, f.sin_t.data_ptr(), dse.data_ptr(), dx.data_ptr(), ddt.data_ptr(), dB.data_ptr<float>(),
+                    dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(), dCp.data_ptr<float>(), st);
+  check_launch("ahb_ssd_bwd_chunk");
   return {dx, ddt, dA, dB, dC};
 }
 
@@ -1224,7 +1248,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_fwd_train", &ssd_fwd_train);
   m.def("ssd_fwd", &ssd_fwd);
   m.def("ssd_bwd", &ssd_bwd, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"), py::arg("dy"),
-        py::arg("states") = py::none(), py::arg("cumsums") = py::none());
+        py::arg("states") = py::none(), py::arg("decays") = py::none(), py::arg("cumsums") = py::none());
   m.def("gemm_dense", &gemm_dense);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_error_reset", &gemm_error_reset);

@@ -56,13 +56,15 @@ AHB_DEVICE void load_xp_tile(bf16* dst, const bf16* src, const SIdx& ix, int b, 
         *reinterpret_cast<const uint4*>(src + ix.xp(b, (int64_t)n * C + r, h) + c8);
   }
 }
-// fp32 (P x N) state tile -> bf16 smem [P][LDN]
-AHB_DEVICE void load_state_bf(bf16* dst, const float* src) {
-  for (int i = threadIdx.x; i < P * (N / 4); i += blockDim.x) {
-    int r = i / (N / 4), c4 = (i % (N / 4)) * 4;
-    float4 v = *reinterpret_cast<const float4*>(src + r * N + c4);
-    st2(dst + r * LDN + c4, v.x, v.y);
-    st2(dst + r * LDN + c4 + 2, v.z, v.w);
+// state tile image (bf16, rows s = 0..127, columns p = 0..63, 128-byte swizzle) -> smem [P][LDN]
+AHB_DEVICE void load_state_bf(bf16* dst, const unsigned char* img) {
+  for (int u = threadIdx.x; u < N * (P / 8); u += blockDim.x) {
+    const int s = u >> 3, c8 = (u & 7) << 3;
+    const int off = (s >> 3) * 1024 + (s & 7) * 128 + (((c8 >> 3) ^ (s & 7)) << 4);
+    const uint4 w = *reinterpret_cast<const uint4*>(img + off);
+    const bf16* e = reinterpret_cast<const bf16*>(&w);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[(c8 + k) * LDN + s] = e[k];
   }
 }
 // c = cumsum(clip(dt*A, +-20)), clipped to +-1e4 (reference sanitize)
@@ -158,176 +160,6 @@ AHB_DEVICE void compute_cb(float* cb_s, const bf16* c_s, const bf16* b_s) {
              [&](int r, int c, float& v) { cb_s[r * LDCC + c] = sanitize(v, 1e4f); });
 }
 
-// ============================================================ forward: chunk states
-constexpr size_t SMEM_STATE_F = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
-
-__global__ void __launch_bounds__(512, 1) ssd_state_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
-                                                            const float* __restrict__ A, const bf16* __restrict__ Bm,
-                                                            int L, int H, float* __restrict__ send,
-                                                            float* __restrict__ cuml) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* b_s = reinterpret_cast<bf16*>(smem);
-  bf16* x_s = b_s + C * LDN;
-  bf16* dt_s = x_s + C * LDP;
-  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
-  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
-  const SIdx ix{L, H, NC};
-  const int warp = threadIdx.x >> 5;
-  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
-  load_bn_tile(b_s, Bm, ix, b, n);
-  for (int h = h0; h < h0 + hpg; ++h) {
-    load_xp_tile(x_s, x, ix, b, n, h);
-    load_xp_tile(dt_s, dt, ix, b, n, h);
-    cum_decay(cum, dt_s, A[h]);
-    const int64_t cb = ix.ch(b, h, n);
-    if (threadIdx.x < P) cuml[cb * P + threadIdx.x] = cum[(C - 1) * LDPF + threadIdx.x];
-    // S_end[p, s] = sum_j (dBx[j,p] e^{cL-c_j}) B[j,s]
-    const float* cl = cum + (C - 1) * LDPF;
-    auto fa = [&](int rp, int kj) -> uint32_t {
-      return pack2(dbx(x_s, dt_s, kj, rp) * __expf(fmaxf(cl[rp] - cum[kj * LDPF + rp], -20.f)),
-                   dbx(x_s, dt_s, kj + 1, rp) * __expf(fmaxf(cl[rp] - cum[(kj + 1) * LDPF + rp], -20.f)));
-    };
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, fa, KNB16{b_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, C);
-    float* out = send + cb * P * N;
-    for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = sanitize(v, 1e4f); });
-    __syncthreads();
-  }
-}
-
-// ============================================================ state scan (forward / reverse)
-// forward: buf holds S_end on entry and S_in on exit; reverse: buf holds G on entry, dS_end on exit.
-__global__ void __launch_bounds__(256) ssd_scan_kernel(float* __restrict__ buf, const float* __restrict__ cuml,
-                                                       int H, int NC, int reverse, const float* __restrict__ s0,
-                                                       float* __restrict__ s_final) {
-  const int e = blockIdx.x * 256 + threadIdx.x;  // element of P x N
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int p = e / N;
-  const int64_t base = ((int64_t)b * H + h) * NC;
-  float S = s0 ? s0[((int64_t)b * H + h) * P * N + e] : 0.f;
-  constexpr int U = 8;  // loads for U chunks are issued before the dependent updates
-  if (!reverse) {
-    for (int n0 = 0; n0 < NC; n0 += U) {
-      float se[U], dc[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int n = n0 + u;
-        se[u] = n < NC ? buf[(base + n) * P * N + e] : 0.f;
-        dc[u] = n < NC ? __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) : 1.f;
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int n = n0 + u;
-        if (n < NC) {
-          buf[(base + n) * P * N + e] = S;
-          S = sanitize(S * dc[u] + se[u], 1e4f);
-        }
-      }
-    }
-  } else {
-    for (int n0 = NC - 1; n0 >= 0; n0 -= U) {
-      float gn[U], dc[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int n = n0 - u;
-        gn[u] = n >= 0 ? buf[(base + n) * P * N + e] : 0.f;
-        dc[u] = n >= 0 ? __expf(fmaxf(cuml[(base + n) * P + p], -20.f)) : 1.f;
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int n = n0 - u;
-        if (n >= 0) {
-          buf[(base + n) * P * N + e] = S;
-          S = S * dc[u] + gn[u];
-        }
-      }
-    }
-  }
-  if (s_final) s_final[((int64_t)b * H + h) * P * N + e] = S;
-}
-
-// ============================================================ forward: outputs
-constexpr size_t SMEM_OUT_F = 2 * C * LDN * 2 + C * LDCC * 4 + 2 * C * LDP * 2 + C * LDPF * 4 + P * LDN * 2;
-
-__global__ void __launch_bounds__(512, 1) ssd_out_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ dt,
-                                                          const float* __restrict__ A, const bf16* __restrict__ Bm,
-                                                          const bf16* __restrict__ Cm, const float* __restrict__ sin,
-                                                          int L, int H, bf16* __restrict__ y) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* b_s = reinterpret_cast<bf16*>(smem);
-  bf16* c_s = b_s + C * LDN;
-  float* cb_s = reinterpret_cast<float*>(c_s + C * LDN);
-  bf16* x_s = reinterpret_cast<bf16*>(cb_s + C * LDCC);
-  bf16* dt_s = x_s + C * LDP;
-  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
-  bf16* sin_s = reinterpret_cast<bf16*>(cum + C * LDPF);
-  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
-  const SIdx ix{L, H, NC};
-  const int warp = threadIdx.x >> 5;
-  load_bn_tile(b_s, Bm, ix, b, n);
-  load_bn_tile(c_s, Cm, ix, b, n);
-  __syncthreads();
-  compute_cb(cb_s, c_s, b_s);
-  const int I = warp & 3, n0 = 16 * (warp >> 2);
-  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
-  for (int h = h0; h < h0 + hpg; ++h) {
-    const int64_t cb = ix.ch(b, h, n);
-    load_xp_tile(x_s, x, ix, b, n, h);
-    load_xp_tile(dt_s, dt, ix, b, n, h);
-    load_state_bf(sin_s, sin + cb * P * N);
-    cum_decay(cum, dt_s, A[h]);
-    float yd[2][4], yo[2][4];
-    ydiag_tile<2>(yd, cb_s, x_s, dt_s, cum, I, n0);
-    yoff_tile<2>(yo, c_s, sin_s, cum, I, n0);
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int c = n0 + 8 * j + 2 * t;
-      const int r = 16 * I + g;
-      st2(y + ix.xp(b, (int64_t)n * C + r, h) + c, sanitize(sanitize(yd[j][0], 1e4f) + sanitize(yo[j][0], 1e4f), 1e4f),
-          sanitize(sanitize(yd[j][1], 1e4f) + sanitize(yo[j][1], 1e4f), 1e4f));
-      st2(y + ix.xp(b, (int64_t)n * C + r + 8, h) + c,
-          sanitize(sanitize(yd[j][2], 1e4f) + sanitize(yo[j][2], 1e4f), 1e4f),
-          sanitize(sanitize(yd[j][3], 1e4f) + sanitize(yo[j][3], 1e4f), 1e4f));
-    }
-    __syncthreads();
-  }
-}
-
-// ============================================================ backward: G = (dy e^c)^T C  per chunk/head
-constexpr size_t SMEM_G = C * LDN * 2 + 2 * C * LDP * 2 + C * LDPF * 4;
-
-__global__ void __launch_bounds__(512, 1) ssd_dstate_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dt,
-                                                         const float* __restrict__ A, const bf16* __restrict__ Cm,
-                                                         int L, int H, float* __restrict__ gbuf) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  bf16* c_s = reinterpret_cast<bf16*>(smem);
-  bf16* dy_s = c_s + C * LDN;
-  bf16* dt_s = dy_s + C * LDP;
-  float* cum = reinterpret_cast<float*>(dt_s + C * LDP);
-  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
-  const SIdx ix{L, H, NC};
-  const int warp = threadIdx.x >> 5;
-  load_bn_tile(c_s, Cm, ix, b, n);
-  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
-  for (int h = h0; h < h0 + hpg; ++h) {
-    load_xp_tile(dy_s, dy, ix, b, n, h);
-    load_xp_tile(dt_s, dt, ix, b, n, h);
-    cum_decay(cum, dt_s, A[h]);
-    auto fa = [&](int rp, int ki) -> uint32_t {
-      return pack2(bf(dy_s[ki * LDP + rp]) * __expf(fmaxf(cum[ki * LDPF + rp], -20.f)),
-                   bf(dy_s[(ki + 1) * LDP + rp]) * __expf(fmaxf(cum[(ki + 1) * LDPF + rp], -20.f)));
-    };
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4>(acc, fa, KNB16{c_s, LDN}, 16 * (warp & 3), 32 * (warp >> 2), 0, C);
-    float* out = gbuf + ix.ch(b, h, n) * P * N;
-    for_acc<4>(acc, 16 * (warp & 3), 32 * (warp >> 2), [&](int r, int c, float& v) { out[r * N + c] = v; });
-    __syncthreads();
-  }
-}
-
 // ============================================================ backward: per chunk, all heads
 // smem: b, c bf16 [C][LDN]; cb, dcb f32 [C][LDCC]; x, dt, dy bf16 [C][LDP]; cum, dc, ddbx f32 [C][LDPF];
 //       sin, dse bf16 [P][LDN]
@@ -337,7 +169,7 @@ constexpr size_t SMEM_BWD =
 __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ dt, const float* __restrict__ A,
     const bf16* __restrict__ Bm, const bf16* __restrict__ Cm, const bf16* __restrict__ dy,
-    const float* __restrict__ sin, const float* __restrict__ dse, int L, int H, bf16* __restrict__ dx,
+    const unsigned char* __restrict__ sin_t, const unsigned char* __restrict__ dse_t, int L, int H, bf16* __restrict__ dx,
     bf16* __restrict__ ddt, float* __restrict__ dB, float* __restrict__ dC, float* __restrict__ dA) {
   extern __shared__ __align__(16) unsigned char smem[];
   bf16* b_s = reinterpret_cast<bf16*>(smem);
@@ -374,8 +206,8 @@ __global__ void __launch_bounds__(512, 1) ssd_bwd_chunk_kernel(
     load_xp_tile(x_s, x, ix, b, n, h);
     load_xp_tile(dt_s, dt, ix, b, n, h);
     load_xp_tile(dy_s, dy, ix, b, n, h);
-    load_state_bf(sin_s, sin + cbi * P * N);
-    load_state_bf(dse_s, dse + cbi * P * N);
+    load_state_bf(sin_s, sin_t + cbi * (P * N * 2));
+    load_state_bf(dse_s, dse_t + cbi * (P * N * 2));
     if (tid < P) dcl_s[tid] = 0.f;
     cum_decay(cum, dt_s, Ah);
     const float* cl = cum + (C - 1) * LDPF;
@@ -588,116 +420,28 @@ void set_smem(K kernel, size_t bytes) {
 
 }  // namespace
 
-int ahb_ssd_supported(int P_, int N_) { return (P_ == P && N_ == N) ? C : 0; }
-
-void ahb_ssd_fwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
-                 float* state_buf, float* cuml, const float* s0, float* s_final, void* y, cudaStream_t st) {
-  static bool init = false;
-  if (!init) {
-    set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
-    set_smem(ssd_out_fwd_kernel, SMEM_OUT_F);
-    init = true;
-  }
-  const int NC = L / C;
-  const int G = head_groups(H);
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                 (const bf16*)Bm, L, H, state_buf, cuml);
-  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, s0, s_final);
-  if (y)
-    ssd_out_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_OUT_F, st>>>((const bf16*)x, (const bf16*)dt, A,
-                                                               (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
-                                                               (bf16*)y);
-}
-
 int ahb_ssd_head_groups(int H) { return head_groups(H); }
 
 // dB_part / dC_part: (G, B, L, N) fp32 scratch with G = ahb_ssd_head_groups(H); the sums over
-// head groups are written to dB / dC.
-void ahb_ssd_bwd(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
-                 int B, int L, int H, float* state_buf, float* cuml, float* g_buf, void* dx, void* ddt, float* dB,
-                 float* dC, float* dA, float* dB_part, float* dC_part, int states_ready, cudaStream_t st) {
+// head groups are written to dB / dC.  sin_t / dse_t: per chunk-head state and state-gradient
+// tile images (bf16, rows s, columns p) from ahb_ssd_fwd_tc / ahb_ssd_state_bwd_tc.
+void ahb_ssd_bwd_chunk(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
+                       int B, int L, int H, const void* sin_t, const void* dse_t, void* dx, void* ddt, float* dB,
+                       float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st) {
   static bool init = false;
   if (!init) {
-    set_smem(ssd_state_fwd_kernel, SMEM_STATE_F);
-    set_smem(ssd_dstate_kernel, SMEM_G);
     set_smem(ssd_bwd_chunk_kernel, SMEM_BWD);
     init = true;
   }
   const int NC = L / C;
   const int G = head_groups(H);
-  if (!states_ready) {  // otherwise state_buf / cuml hold the forward's scanned chunk states
-    ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, st>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                   (const bf16*)Bm, L, H, state_buf, cuml);
-    ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  }
-  ssd_dstate_kernel<<<dim3(NC, B, G), 512, SMEM_G, st>>>((const bf16*)dy, (const bf16*)dt, A, (const bf16*)Cm, L, H,
-                                                         g_buf);
-  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, st>>>(g_buf, cuml, H, NC, 1, nullptr, nullptr);
   ssd_bwd_chunk_kernel<<<dim3(NC, B, G), 512, SMEM_BWD, st>>>((const bf16*)x, (const bf16*)dt, A, (const bf16*)Bm,
-                                                             (const bf16*)Cm, (const bf16*)dy, state_buf, g_buf, L, H,
-                                                             (bf16*)dx, (bf16*)ddt, dB_part, dC_part, dA);
+                                                             (const bf16*)Cm, (const bf16*)dy,
+                                                             (const unsigned char*)sin_t,
+                                                             (const unsigned char*)dse_t, L, H, (bf16*)dx, (bf16*)ddt,
+                                                             dB_part, dC_part, dA);
   const int64_t n = (int64_t)B * L * N;
   const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
   sum_groups_kernel<<<blocks, 256, 0, st>>>(dB_part, G, n, dB);
   sum_groups_kernel<<<blocks, 256, 0, st>>>(dC_part, G, n, dC);
-}
-
-// ============================================================ allocation-free forward
-// See ssd_noalloc.h: scratch for the chunk states lives in this fixed device array.
-#include <cstdio>
-#include <mutex>
-#include "ssd_noalloc.h"
-
-static __device__ __align__(256) unsigned char g_ssd_noalloc_scratch[AHB_SSD_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-constexpr int kMaxDevices = 64;
-void* g_noalloc_ptr[kMaxDevices] = {};
-std::mutex g_noalloc_mu;
-}  // namespace
-
-extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm,
-                                   int B, int L, int H, void* y, cudaStream_t stream) {
-  if (!x || !dt || !A || !Bm || !Cm || !y || B <= 0 || L <= 0 || H <= 0 || L % C != 0) return AHB_NOALLOC_EINVAL;
-  const int NC = L / C;
-  const unsigned long long chunk_heads = (unsigned long long)B * H * NC;
-  if (chunk_heads > AHB_SSD_NOALLOC_MAX_CHUNK_HEADS) {
-    fprintf(stderr,
-            "ahb_ssd_fwd_noalloc: B*H*(L/64) = %llu exceeds the fixed scratch limit of %u chunk-heads (%u bytes)\n",
-            chunk_heads, (unsigned)AHB_SSD_NOALLOC_MAX_CHUNK_HEADS, (unsigned)AHB_SSD_NOALLOC_SCRATCH_BYTES);
-    return AHB_NOALLOC_ETOOBIG;
-  }
-  // an error left pending by earlier work is reported, not cleared: it is not this call's
-  if (cudaPeekAtLastError() != cudaSuccess) return AHB_NOALLOC_EPENDING;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AHB_NOALLOC_ESETUP;
-  void* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch) != cudaSuccess || !p) return AHB_NOALLOC_ESETUP;
-      if (cudaFuncSetAttribute(ssd_state_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)SMEM_STATE_F) != cudaSuccess ||
-          cudaFuncSetAttribute(ssd_out_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_OUT_F) !=
-              cudaSuccess)
-        return AHB_NOALLOC_ESETUP;
-      g_noalloc_ptr[dev] = p;
-    }
-    base = g_noalloc_ptr[dev];
-  }
-  float* state_buf = static_cast<float*>(base);
-  float* cuml = state_buf + chunk_heads * (unsigned long long)(P * N);
-  const int G = head_groups(H);
-  // no error was pending on entry, so a failure seen after a launch is that launch's own
-  ssd_state_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_STATE_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                     (const bf16*)Bm, L, H, state_buf, cuml);
-  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
-  ssd_scan_kernel<<<dim3(P * N / 256, H, B), 256, 0, stream>>>(state_buf, cuml, H, NC, 0, nullptr, nullptr);
-  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
-  ssd_out_fwd_kernel<<<dim3(NC, B, G), 512, SMEM_OUT_F, stream>>>((const bf16*)x, (const bf16*)dt, A,
-                                                                 (const bf16*)Bm, (const bf16*)Cm, state_buf, L, H,
-                                                                 (bf16*)y);
-  if (cudaGetLastError() != cudaSuccess) return AHB_NOALLOC_ELAUNCH;
-  return AHB_NOALLOC_OK;
 }

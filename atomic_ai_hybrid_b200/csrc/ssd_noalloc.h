@@ -9,14 +9,15 @@
 // buffer; the chunk-state scratch the forward needs comes from a fixed array in
 // device memory that every GPU loading this library holds until process exit.
 //
-//   Limit: B * H * (L / 64) <= AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (the 32 MiB scratch
-//   holds 64 x 128 fp32 states plus 64 decay sums per (batch, head, chunk)).
+//   Limit: B * H * (L / 64) <= AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (the 32 MiB scratch holds,
+//   per (batch, head, chunk), the chunk's end state, its intra-chunk output and decay factors
+//   in bf16 and its 64 last decay sums: 33,024 bytes).
 //   Shapes: x, dt (B, L, H, 64) bf16; A (H,) fp32; Bm, Cm (B, L, 128) bf16;
 //   y (B, L, H, 64) bf16; L a multiple of 64; all pointers on the current device.
 //
-// The first call on each device looks up the scratch array's device address
-// (cudaGetSymbolAddress) and sets the kernels' shared-memory limits; make that
-// first call before any stream capture begins.  Every call shares the one
+// The first call on each device looks up the device addresses of the scratch array and
+// of a fixed timeout word (cudaGetSymbolAddress) and sets the kernels' shared-memory
+// limits; make that first call before any stream capture begins.  Every call shares the one
 // scratch array, so calls whose executions overlap on the GPU (different
 // streams without ordering, or concurrent host threads) race on it; calls
 // ordered on one stream are safe.  Nothing in the scratch needs to start at

@@ -38,3 +38,22 @@ inline int tmap_seq_bf16(CUtensorMap* m, const void* ptr, int64_t BL, int64_t H,
 }
 
 }  // namespace ahb
+
+namespace ahb {
+
+// bf16 row-major (rows, cols) matrix as a 2-D map; box {64, box_rows} with 128-byte swizzle
+// (one box = a box_rows x 64 slab).
+inline int tmap_2d_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  TmapEncodeFn fn = tmap_encode_fn();
+  if (!fn || !ptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+}  // namespace ahb

@@ -5,8 +5,8 @@ from __future__ import annotations
 
 
 class LaunchCounter:
-    MULTI = {"gdn_fwd": 2, "gdn_fwd_train": 2, "gdn_bwd": 6, "gdn_bwd_saved": 4, "ssd_fwd": 3, "ssd_fwd_train": 3,
-             "ssd_bwd": 7, "moe_fwd": 7, "moe_bwd": 8, "ce_fused_fwd": 2, "ce_fused_bwd": 2, "add_rmsnorm_bwd": 2,
+    MULTI = {"gdn_fwd": 2, "gdn_fwd_train": 2, "gdn_bwd": 4, "gdn_bwd_saved": 2, "ssd_fwd": 2, "ssd_fwd_train": 2,
+             "ssd_bwd": 4, "moe_fwd": 7, "moe_bwd": 8, "ce_fused_fwd": 2, "ce_fused_bwd": 2, "add_rmsnorm_bwd": 2,
              "norm_gate_bwd": 2}
 
     def __init__(self):
