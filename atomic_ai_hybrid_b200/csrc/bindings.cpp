@@ -300,7 +300,7 @@ void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Ten
               "ssd: B, C must be (B,L,128)");
 }
 
-struct SsdFwd { torch::Tensor y, sin_t, dec_t, cl; };
+struct SsdFwd { torch::Tensor y, sin_t, dec_t, cl, yd_t; };
 
 // Forward (chunk kernel + state recurrence); with `keep_states` also the per-chunk incoming
 // states (tile images) the backward needs, beside the decay images and last cumsums.
@@ -310,13 +310,13 @@ static SsdFwd ssd_forward(const torch::Tensor& x, const torch::Tensor& dt, const
   auto bf = x.options();
   SsdFwd f;
   auto send = torch::empty({B, H, NC, 128, 64}, bf);
-  auto yd = torch::empty({B, H, NC, 64, 64}, bf);
+  f.yd_t = torch::empty({B, H, NC, 64, 64}, x.options().dtype(at::kFloat));
   f.dec_t = torch::empty({B, H, NC, 64, 64}, bf);
   f.cl = torch::empty({B, H, NC, 64}, x.options().dtype(at::kFloat));
   if (keep_states) f.sin_t = torch::empty({B, H, NC, 128, 64}, bf);
   f.y = torch::empty_like(x);
   check_rc(ahb_ssd_fwd_tc(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
-                          send.data_ptr(), yd.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), nullptr, nullptr,
+                          send.data_ptr(), f.yd_t.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), nullptr, nullptr,
                           f.y.data_ptr(), keep_states ? f.sin_t.data_ptr() : nullptr, err_word().data_ptr<int>(),
                           cur_stream()),
            "ahb_ssd_fwd_tc");
@@ -329,29 +329,32 @@ torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch:
   return ssd_forward(x, dt, A, Bm, Cm, false, true).y;
 }
 
-// Forward for training: {y, incoming states (tile images), decay images, last cumsums}; ssd_bwd
-// takes the last three back.
+// Forward for training: {y, incoming states (tile images), decay images, last cumsums, intra-chunk
+// outputs}; ssd_bwd takes the last four back.
 std::vector<torch::Tensor> ssd_fwd_train(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
                                          torch::Tensor Cm) {
   check_ssd(x, dt, A, Bm, Cm);
   auto f = ssd_forward(x, dt, A, Bm, Cm, true, true);
-  return {f.y, f.sin_t, f.dec_t, f.cl};
+  return {f.y, f.sin_t, f.dec_t, f.cl, f.yd_t};
 }
 
 std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
                                    torch::Tensor Cm, torch::Tensor dy, c10::optional<torch::Tensor> states,
-                                   c10::optional<torch::Tensor> decays, c10::optional<torch::Tensor> cumsums) {
+                                   c10::optional<torch::Tensor> decays, c10::optional<torch::Tensor> cumsums,
+                                   c10::optional<torch::Tensor> ydiag) {
   check_ssd(x, dt, A, Bm, Cm);
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
   auto dyc = dy.to(at::kBFloat16).contiguous();
   auto f32 = x.options().dtype(at::kFloat);
   const bool ready = states.has_value() && states->defined() && decays.has_value() && decays->defined() &&
-                     cumsums.has_value() && cumsums->defined();
+                     cumsums.has_value() && cumsums->defined() && ydiag.has_value() && ydiag->defined();
   SsdFwd f;
   if (ready) {
     f.sin_t = *states;
     f.dec_t = *decays;
     f.cl = *cumsums;
+    f.yd_t = *ydiag;
+    TORCH_CHECK(f.yd_t.numel() == (int64_t)B * H * NC * 64 * 64, "ssd_bwd: saved intra-chunk outputs do not match");
     TORCH_CHECK(f.sin_t.numel() == (int64_t)B * H * NC * 128 * 64 && f.dec_t.numel() == (int64_t)B * H * NC * 64 * 64 &&
                     f.cl.numel() == (int64_t)B * H * NC * 64,
                 "ssd_bwd: saved states do not match");
@@ -368,10 +371,12 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
   auto dA = torch::zeros({H}, f32);
   const int G = ahb_ssd_head_groups(H);
   auto dBp = torch::empty({G, B, L, 128}, f32), dCp = torch::empty({G, B, L, 128}, f32);
-  ahb_ssd_bwd_chunk(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), dyc.data_ptr(), B,
-                    L, H, f.sin_t.data_ptr(), dse.data_ptr(), dx.data_ptr(), ddt.data_ptr(), dB.data_ptr<float>(),
-                    dC.data_ptr<float>(), dA.data_ptr<float>(), dBp.data_ptr<float>(), dCp.data_ptr<float>(), st);
-  check_launch("ahb_ssd_bwd_chunk");
+  check_rc(ahb_ssd_bwd_chunk_tc(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(),
+                                dyc.data_ptr(), B, L, H, f.sin_t.data_ptr(), dse.data_ptr(), f.yd_t.data_ptr(),
+                                dx.data_ptr(), ddt.data_ptr(), dB.data_ptr<float>(), dC.data_ptr<float>(),
+                                dA.data_ptr<float>(), dBp.data_ptr<float>(), dCp.data_ptr<float>(),
+                                err_word().data_ptr<int>(), st),
+           "ahb_ssd_bwd_chunk_tc");
   return {dx, ddt, dA, dB, dC};
 }
 
@@ -1248,7 +1253,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_fwd_train", &ssd_fwd_train);
   m.def("ssd_fwd", &ssd_fwd);
   m.def("ssd_bwd", &ssd_bwd, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"), py::arg("dy"),
-        py::arg("states") = py::none(), py::arg("decays") = py::none(), py::arg("cumsums") = py::none());
+        py::arg("states") = py::none(), py::arg("decays") = py::none(), py::arg("cumsums") = py::none(),
+        py::arg("ydiag") = py::none());
   m.def("gemm_dense", &gemm_dense);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_error_reset", &gemm_error_reset);

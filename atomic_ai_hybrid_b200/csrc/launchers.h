@@ -48,8 +48,9 @@ int ahb_gdn_chunk_bwd_tc(const void* q, const void* k, const void* v, const floa
                          void* dw, float* dg, int* err, cudaStream_t st);
 
 // Mamba2 SSD (head dim 64, d_state 128, chunk 64; x, dt (B,L,H,64); B, C (B,L,128); A (H,) fp32)
-// ssd_tc.cu: forward (chunk kernel + state recurrence) and the reverse state-gradient recurrence.
-// Per chunk-head scratch: send_t (128 x 64 bf16 image), yd_t (64 x 64 bf16 rows), dec_t (64 x 64
+// ssd_tc.cu: forward (chunk kernel + state recurrence), the reverse state-gradient recurrence and
+// the chunk-parallel backward.
+// Per chunk-head scratch: send_t (128 x 64 bf16 image), yd_t (64 x 64 fp32 rows), dec_t (64 x 64
 // bf16 image), cl (64 fp32); sin_t / dse_t are per chunk-head 128 x 64 bf16 images (rows s,
 // columns p) of the incoming state and of the gradient reaching the chunk's end state.
 int ahb_ssd_supported(int P, int N);
@@ -58,11 +59,12 @@ int ahb_ssd_fwd_tc(const void* x, const void* dt, const float* A, const void* Bm
                    void* sin_t, int* err, cudaStream_t st);
 int ahb_ssd_state_bwd_tc(const void* Cm, const void* dy, const void* dec_t, const float* cl, int B, int L, int H,
                          const float* ds_final, void* dse_t, float* ds0, int* err, cudaStream_t st);
-// ssd.cu: chunk-parallel backward
+// chunk-parallel backward: one CTA per (chunk, batch, head group); dB_part / dC_part are (G, B, L, N)
+// fp32 scratch with G = ahb_ssd_head_groups(H), summed into dB / dC; dA (H,) is accumulated (zero it)
 int ahb_ssd_head_groups(int H);
-void ahb_ssd_bwd_chunk(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
-                       int B, int L, int H, const void* sin_t, const void* dse_t, void* dx, void* ddt, float* dB,
-                       float* dC, float* dA, float* dB_part, float* dC_part, cudaStream_t st);
+int ahb_ssd_bwd_chunk_tc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
+                         int B, int L, int H, const void* sin_t, const void* dse_t, const void* yd_t, void* dx, void* ddt,
+                         float* dB, float* dC, float* dA, float* dB_part, float* dC_part, int* err, cudaStream_t st);
 
 // moe_gemm.cu: tcgen05 grouped GEMM.  Returns 0 on success, <0 on a setup error.
 #define AHB_GEMM_DENSE 0        // C[M,N] = A[M,K] B[N,K]^T (single group)

@@ -10,8 +10,8 @@
 // device memory that every GPU loading this library holds until process exit.
 //
 //   Limit: B * H * (L / 64) <= AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (the 32 MiB scratch holds,
-//   per (batch, head, chunk), the chunk's end state, its intra-chunk output and decay factors
-//   in bf16 and its 64 last decay sums: 33,024 bytes).
+//   per (batch, head, chunk), the chunk's end state and decay factors in bf16, its intra-chunk
+//   output in fp32 and its 64 last decay sums: 41,216 bytes, so 814 chunk-heads).
 //   Shapes: x, dt (B, L, H, 64) bf16; A (H,) fp32; Bm, Cm (B, L, 128) bf16;
 //   y (B, L, H, 64) bf16; L a multiple of 64; all pointers on the current device.
 //
@@ -32,7 +32,8 @@
 #define AHB_NOALLOC_ELAUNCH -4  // a kernel launch of this call failed
 #define AHB_NOALLOC_EPENDING -5  // a CUDA error from earlier work was pending on entry (left uncleared)
 #define AHB_SSD_NOALLOC_SCRATCH_BYTES (32u << 20)
-#define AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (AHB_SSD_NOALLOC_SCRATCH_BYTES / ((64u * 128u + 64u) * 4u))
+#define AHB_SSD_NOALLOC_BYTES_PER_CHUNK_HEAD (128u * 64u * 2u + 64u * 64u * 4u + 64u * 64u * 2u + 64u * 4u)
+#define AHB_SSD_NOALLOC_MAX_CHUNK_HEADS (AHB_SSD_NOALLOC_SCRATCH_BYTES / AHB_SSD_NOALLOC_BYTES_PER_CHUNK_HEAD)
 
 #ifdef __cplusplus
 extern "C" {

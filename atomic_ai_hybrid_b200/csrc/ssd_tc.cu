@@ -11,10 +11,12 @@
 //
 // Forward in two kernels:
 //   ssd_chunk_fwd_tc (one CTA per chunk and head, chunk-parallel): C B^T, S_end^T = B^T V
-//     (M = 128 state rows) and y_diag^T per 16-row reference block (the pairwise decay split at
-//     r = 16 I, rows e^{c_i - c_r} <= 1, keys e^{c_r - c_j}; blocks whose decay span exceeds 60
-//     are summed exactly per channel); writes S_end^T and the decay e^{max(c,-20)} as swizzled
-//     tile images, y_diag^T rows and the chunk's last cumsum.
+//     (M = 128 state rows) and y_diag^T: the blocks below the diagonal per 16-row reference block
+//     (the pairwise decay split at r = 16 I, rows e^{c_i - c_r} <= 1, keys e^{c_r - c_j} <= 1) on
+//     the tensor cores, the diagonal 16 x 16 blocks exactly per channel in fp32 (exponent floored
+//     at -20 as the reference); writes S_end^T and the decay e^{max(c,-20)} as swizzled
+//     tile images, y_diag^T rows (fp32: the backward's decay gradient cancels heavily) and the
+//     chunk's last cumsum.
 //   ssd_state_fwd_tc (one CTA per batch and head, chunk-sequential): the fp32 state lives in
 //     registers (thread s holds S^T row s); per chunk y_off^T = S C^T on the tensor cores, the
 //     output y, and (for the backward) the incoming state as a tile image.
@@ -49,7 +51,7 @@ constexpr size_t S1_SMEM = 1024 + S1_BAR + 256;
 __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_dt, const float* __restrict__ A,
-    int L, int H, unsigned char* __restrict__ send_t, bf16* __restrict__ yd_t, unsigned char* __restrict__ dec_t,
+    int L, int H, unsigned char* __restrict__ send_t, float* __restrict__ yd_t, unsigned char* __restrict__ dec_t,
     float* __restrict__ cl_o, int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -57,8 +59,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   float* CUM = reinterpret_cast<float*>(smem + S1_CUM);  // [i][p]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S1_BAR);  // 0 load, 1 CB, 2 S_end, 3-6 y_diag blocks
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0..3] exact diagonal block, [4] abort
-  float* span_w = reinterpret_cast<float*>(flags + 8);  // [2 warps][4]
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [4] abort
 
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -98,15 +99,8 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       CUM[i * P + p] = fminf(fmaxf(s, -1e4f), 1e4f);
     }
     cl_o[ch * P + p] = CUM[(C - 1) * P + p];
-    float sp[4];
-#pragma unroll
-    for (int I = 0; I < 4; ++I) sp[I] = warp_max(CUM[16 * I * P + p] - CUM[(16 * I + 15) * P + p]);
-    if (lane == 0)
-#pragma unroll
-      for (int I = 0; I < 4; ++I) span_w[warp * 4 + I] = sp[I];
   }
   __syncthreads();
-  if (tid < 4) flags[tid] = !(fmaxf(span_w[tid], span_w[4 + tid]) <= 60.f);
   // V = dBx e^{max(cl - c, -20)}  (rows j, columns p)
 #pragma unroll
   for (int it = 0; it < (C * P / 8) / S1_THREADS; ++it) {
@@ -148,32 +142,38 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   __syncthreads();
   // y_diag^T per reference block I (r = 16 I): W[j][p] = dBx e^{c_r - c_j} for keys j <= 16 I + 15,
   // D[p][i in block I] += W^T CB^T  -> TMEM columns [128 + 16 I, +16)
+  // The key operand is split into bf16 hi + lo parts (two MMAs): the backward's decay gradient
+  // cancels these sums against the matching column sums, which bf16 alone would not resolve.
 #pragma unroll
   for (int I = 0; I < 4; ++I) {
     const uint32_t buf = S + ((I & 1) ? S1_W1 : S1_W0);
+    const uint32_t blo = S + S1_C + (I & 1) * T_CP;  // the C tile is dead once CB is formed
     if (I >= 2 && !wait_bar(bars + 3 + I - 2, 0, err, 0x5303)) flags[4] = 1;
-    const bool exact = flags[I];
 #pragma unroll
     for (int it = 0; it <= I; ++it) {
       const int u_ = it * S1_THREADS + tid;
       const int j = u_ >> 3, c = (u_ & 7) << 3;
-      float xv[8], dv[8], o[8];
+      float xv[8], dv[8], o[8], lo[8];
       unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
-      const bool zero = exact && j >= 16 * I;
+      const bool zero = j >= 16 * I;  // the diagonal block is summed exactly below
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
+      for (int e = 0; e < 8; ++e) {
         o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(CUM[16 * I * P + c + e] - CUM[j * P + c + e]);
+        lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
+      }
       st_chunk8(buf + sw_off16(C, j, c), o);
+      st_chunk8(blo + sw_off16(C, j, c), lo);
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
     if (tid == 0 && !flags[4]) {
       sm100::tc_fence_after();
-      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(buf, C, k); },
-                [&](int k) { return kdesc(S + S1_CB + 2048 * I, C, k); }, I + 1, sm100::idesc_bf16(64, 16, true, false),
-                false);
+      constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
+      auto fcb = [&](int k) { return kdesc(S + S1_CB + 2048 * I, C, k); };
+      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(buf, C, k); }, fcb, I + 1, ID, false);
+      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(blo, C, k); }, fcb, I + 1, ID, true);
       sm100::umma_commit(bars + 3 + I);
     }
   }
@@ -198,37 +198,71 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
         *reinterpret_cast<uint4*>(dst + sw_off16(N, s, 32 * half + c)) = pack8(y);
       }
     }
-    // y_diag^T row p (lanes 0-15 of each quarter): fp32 rows into the dead W buffers, then the
-    // exact diagonal sums where needed, then bf16 rows out
+    // y_diag^T row p (lanes 0-15 of each quarter): the off-diagonal blocks from TMEM as fp32 rows
+    // into the dead W buffers; then the diagonal 16 x 16 blocks summed exactly per channel (fp32,
+    // exponent floored at -20: these terms dominate and the backward's decay gradient cancels
+    // them against the matching column sums); then fp32 rows out
     float* YD = reinterpret_cast<float*>(smem + S1_W0);  // [p][i]
-    const int p = 16 * warp + lane;
-    float y[64];
-    tmem_ld32(tmem_at(tmem, warp, 128), y);
-    tmem_ld32(tmem_at(tmem, warp, 160), y + 32);
-    if (lane < 16) {
+    {
+      const int p = 16 * warp + lane;
+      float y[64];
+      tmem_ld32(tmem_at(tmem, warp, 128), y);
+      tmem_ld32(tmem_at(tmem, warp, 160), y + 32);
+      if (lane < 16)
 #pragma unroll
-      for (int i = 0; i < 64; ++i) YD[p * C + i] = y[i] * __expf(CUM[i * P + p] - CUM[(i & ~15) * P + p]);
-      for (int I = 0; I < 4; ++I) {
-        if (!flags[I]) continue;
-        for (int i = 16 * I; i < 16 * I + 16; ++i) {
-          float acc = 0.f;
-          for (int j = 16 * I; j <= i; ++j) {
-            const float cb = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, i, j)));
-            const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_X + sw_off(C, j, p)));
-            const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_DT + sw_off(C, j, p)));
-            acc += cb * clip4(dv * xv) * __expf(fmaxf(CUM[i * P + p] - CUM[j * P + p], -20.f));
+        for (int i = 0; i < 64; ++i) YD[p * C + i] = y[i] * __expf(CUM[i * P + p] - CUM[(i & ~15) * P + p]);
+    }
+    __syncthreads();
+    {
+      // two threads per channel p, two blocks each: y[i] += e^{c_i - c_r} sum_{j<=i} CB[i][j] (dBx_j e^{c_r - c_j})
+      // with r the block's first row (fp32 factors; per-pair exponents where the block's span could
+      // overflow them)
+      const int p = tid & 63;
+#pragma unroll 1
+      for (int I = tid >> 6; I < 4; I += 2) {
+        const int r = 16 * I;
+        const float cr = CUM[r * P + p];
+        float u[16], w[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float ct = CUM[(r + t) * P + p];
+          const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_X + sw_off(C, r + t, p)));
+          const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_DT + sw_off(C, r + t, p)));
+          u[t] = __expf(ct - cr);
+          w[t] = clip4(dv * xv);
+        }
+        const bool wide = !(cr - CUM[(r + 15) * P + p] <= 80.f);
+        if (!wide) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) w[t] *= __expf(cr - CUM[(r + t) * P + p]);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j <= i; ++j)
+              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) * w[j];
+            YD[p * C + r + i] += u[i] * acc;
           }
-          YD[p * C + i] += acc;
+        } else {
+          for (int i = 0; i < 16; ++i) {
+            const float ci = CUM[(r + i) * P + p];
+            float acc = 0.f;
+            for (int j = 0; j <= i; ++j)
+              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) * w[j] *
+                     __expf(fmaxf(ci - CUM[(r + j) * P + p], -20.f));
+            YD[p * C + r + i] += acc;
+          }
         }
       }
-      bf16* dst2 = yd_t + ch * (C * P) + p * C;
+    }
+    __syncthreads();
+    if (tid < P) {
+      const int p = tid;
+      float* dst2 = yd_t + ch * (C * P) + p * C;
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = clip4(YD[p * C + c + e]);
-        *reinterpret_cast<uint4*>(dst2 + c) = pack8(o);
-      }
+      for (int c = 0; c < 64; c += 4)
+        *reinterpret_cast<float4*>(dst2 + c) = make_float4(clip4(YD[p * C + c]), clip4(YD[p * C + c + 1]),
+                                                           clip4(YD[p * C + c + 2]), clip4(YD[p * C + c + 3]));
     }
     // decay e^{max(c, -20)} as a tile image (rows i, columns p)
 #pragma unroll
@@ -263,7 +297,7 @@ constexpr size_t S2_SMEM = 1024 + S2_BAR + 256;
 
 __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
     const __grid_constant__ CUtensorMap tm_c, const unsigned char* __restrict__ send_t,
-    const bf16* __restrict__ yd_t, const unsigned char* __restrict__ dec_t, const float* __restrict__ cl,
+    const float* __restrict__ yd_t, const unsigned char* __restrict__ dec_t, const float* __restrict__ cl,
     int L, int H, int NC, const float* __restrict__ s0, bf16* __restrict__ y, unsigned char* __restrict__ sin_t,
     float* __restrict__ s_final, int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -329,10 +363,10 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
     }
     // carry the state: S <- clip(S e^{max(cl, -20)} + S_end)   (S_end^T row s from the image)
     const int p0 = 16 * warp + lane;  // channel of this lane in the y epilogue (lanes 0-15)
-    uint4 ydr[8];
+    float4 ydr[16];
     if (lane < 16)
 #pragma unroll
-      for (int q8 = 0; q8 < 8; ++q8) ydr[q8] = *reinterpret_cast<const uint4*>(yd_t + c * (C * P) + p0 * C + 8 * q8);
+      for (int q4 = 0; q4 < 16; ++q4) ydr[q4] = *reinterpret_cast<const float4*>(yd_t + c * (C * P) + p0 * C + 4 * q4);
     if (!wait_bar(bars + st, (n >> 1) & 1, err, 0x5312)) *abort_flag = 1;  // every thread reads the stage
     {
       const float* clp = reinterpret_cast<const float*>(smem + S2_CL + st * 256);
@@ -356,8 +390,8 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
         bf16* Y = reinterpret_cast<bf16*>(smem + S2_Y);
 #pragma unroll
         for (int q8 = 0; q8 < 8; ++q8) {
-          float yd[8];
-          unpack8(ydr[q8], yd);
+          const float yd[8] = {ydr[2 * q8].x, ydr[2 * q8].y, ydr[2 * q8].z, ydr[2 * q8].w,
+                               ydr[2 * q8 + 1].x, ydr[2 * q8 + 1].y, ydr[2 * q8 + 1].z, ydr[2 * q8 + 1].w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int i = 8 * q8 + e;
@@ -416,7 +450,7 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const int h = blockIdx.x, b = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t bh = (int64_t)b * H + h;
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) sm100::mbar_init(bars + i, 1);
@@ -513,15 +547,460 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
   if (warp == 0) sm100::tmem_dealloc(tmem, 64);
 }
 
+// ============================================================ chunk-parallel backward
+// One CTA per (chunk, batch, head group), 128 threads; the heads of the group run in turn.
+// Shared by the heads: B, C tiles, the causal CB = C B^T (as rows and transposed), the fp32 sum
+// of dCB over the heads, and dC, dB accumulated in TMEM over the heads.  Per head
+// (reference MB1-MB4, `atomic_ops/kernel_mamba2_bwd_b2_intra.py:32-180`,
+// `kernel_mamba2_bwd_b1_state.py:132-249`, `mamba2_bwd_a_dA_reference.py:60-115`):
+//   dC  += (dy e^{max(c,-20)}) S_in            dB += (dBx e^{max(cl-c,-20)}) dS_end
+//   dds^T = dS_end B^T   (state part of d(dBx), per channel)
+//   dCB[i][j] += sum_p (dy e^{c_i - c_r})[i][p] (dBx e^{c_r - c_j})[j][p]   per row block (r = 16 I)
+//   ddd^T[p][j] = sum_{i >= 16 J + 16} (dy e^{c_i - c_s})[i][p] CB[i][j]  per key block (s = 16 J + 15),
+//            plus the diagonal block exactly per channel
+//   y_off^T = S_in C^T ; then per channel p, rows i = 63 .. 0: dc, its reverse cumulative sum g,
+//   ddt = d(dBx) x + g A [unclipped], dx = d(dBx) dt, dA_h += g dt
+// and after the heads dC += dCB B, dB += dCB^T C (dCB summed over the heads), written per group.
+constexpr int SB_THREADS = 128;
+constexpr int SB_B = 0, SB_C = 16384, SB_CB = 32768, SB_CBT = 40960, SB_DCB = 49152, SB_X = 65536, SB_DT = 73728,
+              SB_DY = 81920, SB_S = 90112, SB_DS = 106496, SB_CUM = 122880, SB_DYR = 139264, SB_BI0 = 147456,
+              SB_BI1 = 155648, SB_DYD = 163840, SB_V = 172032, SB_DYS0 = 180224, SB_DYS1 = 188416, SB_BAR = 196608;
+// per-head outputs dx, ddt staged as plain [i][p] bf16 rows over the dead phase-1 operands, and the
+// diagonal part of ddd (fp32 [p][j]) after them
+constexpr int SB_OX = SB_DYR, SB_ODT = SB_DYR + T_CP, SB_DDG = SB_BI1;
+constexpr size_t SB_SMEM = 1024 + SB_BAR + 256;
+// TMEM columns: dC [0,128) and dB [128,256) (M = 64, N = 128); dCB per row block I at 256 + 8 I (I + 1)
+// (widths 16, 32, 48, 64); dds^T [416, 480); later ddd^T per key block J at 256 + 16 J and
+// y_off^T [320, 384)
+constexpr int TM_DC = 0, TM_DB = 128, TM_DCB = 256, TM_DDS = 416, TM_DDD = 256, TM_YO = 320;
+
+AHB_DEVICE int dcb_off(int I) { return 8 * I * (I + 1); }
+
+// Exact per-channel sum of the diagonal block J for the intra part of d(dBx) at row i, channel p:
+// sum over rows i2 >= i of the block of CB[i2][i] dy[i2][p] e^{max(c_i2 - c_i, -20)}, in fp32 like
+// the forward's diagonal blocks (the decay gradient cancels the two).
+__device__ __noinline__ float sb_exact_ddd(const unsigned char* smem, const float* CUM, int p, int i, int J);
+
+__global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
+    const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_c,
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_dt,
+    const __grid_constant__ CUtensorMap tm_dy, const float* __restrict__ A, const unsigned char* __restrict__ sin_t,
+    const unsigned char* __restrict__ dse_t, const float* __restrict__ yd_t, int L, int H, bf16* __restrict__ dx_o,
+    bf16* __restrict__ ddt_o, float* __restrict__ dA_o, float* __restrict__ dB_part, float* __restrict__ dC_part,
+    int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t S = smem_u32(smem);
+  float* CUM = reinterpret_cast<float*>(smem + SB_CUM);  // [i][p]
+  float* DCB = reinterpret_cast<float*>(smem + SB_DCB);  // [i][j]
+  // barriers: 0 B/C, 1 CB, 2 head loads, 3 phase 1, 4-7 dCB blocks, 8-11 ddd blocks, 12 y_off, 13 final
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SB_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0..3] exact diagonal blocks of this head, [4] abort
+  float* span_w = reinterpret_cast<float*>(flags + 8);  // [2][4]
+
+  const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
+  const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = b * L + n * C;
+  if (tid == 0) {
+    for (int i = 0; i < 14; ++i) sm100::mbar_init(bars + i, 1);
+    flags[4] = 0;
+    sm100::fence_barrier_init();
+    sm100::mbar_expect_tx(bars, 2 * T_CN);
+    sm100::tma_load_2d(smem + SB_B, &tm_b, bars, 0, row0);
+    sm100::tma_load_2d(smem + SB_B + T_CN / 2, &tm_b, bars, 64, row0);
+    sm100::tma_load_2d(smem + SB_C, &tm_c, bars, 0, row0);
+    sm100::tma_load_2d(smem + SB_C + T_CN / 2, &tm_c, bars, 64, row0);
+  }
+  if (warp == 0) sm100::tmem_alloc(tmem_slot, 512);
+  for (int e = tid; e < C * C; e += SB_THREADS) DCB[e] = 0.f;
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (!wait_bar(bars, 0, err, 0x5331)) flags[4] = 1;
+  if (tid == 0 && !flags[4]) {  // CB = C B^T into the (not yet used) dCB columns
+    sm100::tc_fence_after();
+    mma_steps(tmem + TM_DCB, [&](int s) { return kdesc(S + SB_C, C, s); }, [&](int s) { return kdesc(S + SB_B, C, s); },
+              N / 16, sm100::idesc_bf16(64, 64, false, false), false);
+    sm100::umma_commit(bars + 1);
+  }
+  if (!wait_bar(bars + 1, 0, err, 0x5332)) flags[4] = 1;
+  sm100::tc_fence_after();
+  {  // causal CB -> rows tile (i, j) and transposed tile (j, i)
+    const int i = 16 * warp + lane;
+    float x[64];
+    tmem_ld32(tmem_at(tmem, warp, TM_DCB), x);
+    tmem_ld32(tmem_at(tmem, warp, TM_DCB + 32), x + 32);
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) x[j] = j <= i ? clip4(x[j]) : 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) st_chunk8(S + SB_CB + sw_off16(C, i, c), x + c);
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        *reinterpret_cast<bf16*>(smem + SB_CBT + sw_off(C, j, i)) = __float2bfloat16_rn(x[j]);
+    }
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (flags[4]) goto sb_teardown;
+  for (int hh = 0; hh < hpg; ++hh) {
+    const int h = h0 + hh;
+    const uint32_t ph = hh & 1;
+    const int64_t ch = ((int64_t)b * H + h) * NC + n;
+    const float Ah = A[h];
+    if (tid == 0) {
+      sm100::mbar_expect_tx(bars + 2, 3 * T_CP + 2 * T_NP);
+      tma_load_3d(smem + SB_X, &tm_x, bars + 2, 0, h, row0);
+      tma_load_3d(smem + SB_DT, &tm_dt, bars + 2, 0, h, row0);
+      tma_load_3d(smem + SB_DY, &tm_dy, bars + 2, 0, h, row0);
+      bulk_g2s(smem + SB_S, sin_t + ch * T_NP, T_NP, bars + 2);
+      bulk_g2s(smem + SB_DS, dse_t + ch * T_NP, T_NP, bars + 2);
+    }
+    if (!wait_bar(bars + 2, ph, err, 0x5333)) flags[4] = 1;
+    if (tid < P) {  // decay cumsum of channel p; span of each 16-row block
+      const int p = tid;
+      float s = 0.f;
+      for (int i = 0; i < C; ++i) {
+        const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
+        s += fminf(fmaxf(dtv * Ah, -20.f), 20.f);
+        CUM[i * P + p] = fminf(fmaxf(s, -1e4f), 1e4f);
+      }
+      float sp[4];
+#pragma unroll
+      for (int I = 0; I < 4; ++I) sp[I] = warp_max(CUM[16 * I * P + p] - CUM[(16 * I + 15) * P + p]);
+      if (lane == 0)
+#pragma unroll
+        for (int I = 0; I < 4; ++I) span_w[warp * 4 + I] = sp[I];
+    }
+    __syncthreads();
+    if (tid < 4) flags[tid] = !(fmaxf(span_w[tid], span_w[4 + tid]) <= 60.f);
+    // DYR = dy e^{c - c_r(i)}, DYD = dy e^{max(c,-20)}, V = dBx e^{max(cl - c, -20)}  (rows, columns p)
+#pragma unroll
+    for (int it = 0; it < (C * P / 8) / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int i = u_ >> 3, c = (u_ & 7) << 3;
+      float dy[8], xv[8], dv[8], r8[8], d8[8], v8[8];
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, i, c)), xv);
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, i, c)), dv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float ci = CUM[i * P + c + e];
+        r8[e] = dy[e] * __expf(ci - CUM[(i & ~15) * P + c + e]);
+        d8[e] = dy[e] * __expf(fmaxf(ci, -20.f));
+        v8[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(CUM[(C - 1) * P + c + e] - ci, -20.f));
+      }
+      st_chunk8(S + SB_DYR + sw_off16(C, i, c), r8);
+      st_chunk8(S + SB_DYD + sw_off16(C, i, c), d8);
+      st_chunk8(S + SB_V + sw_off16(C, i, c), v8);
+    }
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && !flags[4]) {
+      sm100::tc_fence_after();
+      const bool acc = hh > 0;
+      mma_steps(tmem + TM_DC, [&](int k) { return kdesc(S + SB_DYD, C, k); }, [&](int k) { return kdesc(S + SB_S, N, k); },
+                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
+      mma_steps(tmem + TM_DB, [&](int k) { return kdesc(S + SB_V, C, k); }, [&](int k) { return kdesc(S + SB_DS, N, k); },
+                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
+      mma_steps(tmem + TM_DDS, [&](int k) { return mndesc(S + SB_DS, N, k); }, [&](int k) { return kdesc(S + SB_B, C, k); },
+                N / 16, sm100::idesc_bf16(64, 64, true, false), false);
+      sm100::umma_commit(bars + 3);
+    }
+    // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15
+#pragma unroll
+    for (int I = 0; I < 4; ++I) {
+      const uint32_t buf = S + ((I & 1) ? SB_BI1 : SB_BI0);
+      if (I >= 2 && !wait_bar(bars + 4 + I - 2, ph, err, 0x5334)) flags[4] = 1;
+      const bool exact = flags[I];
+#pragma unroll
+      for (int it = 0; it <= I; ++it) {
+        const int u_ = it * SB_THREADS + tid;
+        const int j = u_ >> 3, c = (u_ & 7) << 3;
+        float xv[8], dv[8], o[8];
+        unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
+        unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
+        const bool zero = exact && j >= 16 * I;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(CUM[16 * I * P + c + e] - CUM[j * P + c + e]);
+        st_chunk8(buf + sw_off16(C, j, c), o);
+      }
+      fence_async_smem();
+      sm100::tc_fence_before();
+      __syncthreads();
+      if (tid == 0 && !flags[4]) {
+        sm100::tc_fence_after();
+        mma_steps(tmem + TM_DCB + dcb_off(I), [&](int k) { return kdesc(S + SB_DYR, C, k); },
+                  [&](int k) { return kdesc(buf, C, k); }, P / 16, sm100::idesc_bf16(64, 16 * (I + 1), false, false),
+                  false);
+        sm100::umma_commit(bars + 4 + I);
+      }
+    }
+    if (!wait_bar(bars + 3, ph, err, 0x5335) || !wait_bar(bars + 6, ph, err, 0x5335) ||
+        !wait_bar(bars + 7, ph, err, 0x5335))
+      flags[4] = 1;
+    sm100::tc_fence_after();
+    {  // dCB rows i = 16 warp + lane (block I = warp) into the fp32 sum over the heads
+      const int i = 16 * warp + lane, I = warp;
+      float x[64];
+#pragma unroll
+      for (int p4 = 0; p4 < 4; ++p4)
+        if (p4 <= I) tmem_ld16(tmem_at(tmem, warp, TM_DCB + dcb_off(I) + 16 * p4), x + 16 * p4);
+      if (lane < 16) {
+#pragma unroll
+        for (int p4 = 0; p4 < 4; ++p4)
+          if (p4 <= I)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int j = 16 * p4 + e;
+              if (j <= i) DCB[i * C + j] += x[16 * p4 + e];
+            }
+        if (flags[I]) {  // exact per-channel sums on the diagonal block
+          for (int j = 16 * I; j <= i; ++j) {
+            float acc = 0.f;
+            for (int p = 0; p < P; ++p) {
+              const float dyv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i, p)));
+              const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, j, p)));
+              const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, j, p)));
+              acc += dyv * clip4(dv * xv) * __expf(fmaxf(CUM[i * P + p] - CUM[j * P + p], -20.f));
+            }
+            DCB[i * C + j] += acc;
+          }
+        }
+      }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (flags[4]) break;
+    // phase 2: ddd^T per key block J (reference s = 16 J + 15) and y_off^T
+#pragma unroll
+    for (int J = 0; J < 4; ++J) {
+      const uint32_t buf = S + ((J & 1) ? SB_DYS1 : SB_DYS0);
+      const uint32_t blo = S + SB_DYR + (J & 1) * T_CP;  // hi / lo split, as the forward's key operand
+      if (J >= 2 && !wait_bar(bars + 8 + J - 2, ph, err, 0x5336)) flags[4] = 1;
+      const float* cs = CUM + (16 * J + 15) * P;
+#pragma unroll
+      for (int it = J; it < 4; ++it) {
+        const int u_ = it * SB_THREADS + tid;
+        const int i = u_ >> 3, c = (u_ & 7) << 3;
+        float dy[8], o[8], lo[8];
+        unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
+        const bool zero = i < 16 * J + 16;  // the diagonal block is summed exactly in the epilogue
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[e] = zero ? 0.f : dy[e] * __expf(CUM[i * P + c + e] - cs[c + e]);
+          lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
+        }
+        st_chunk8(buf + sw_off16(C, i, c), o);
+        st_chunk8(blo + sw_off16(C, i, c), lo);
+      }
+      fence_async_smem();
+      sm100::tc_fence_before();
+      __syncthreads();
+      if (tid == 0 && !flags[4]) {
+        sm100::tc_fence_after();
+        constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
+        for (int k = J; k < 4; ++k)
+          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(buf, C, k), kdesc(S + SB_CBT + 2048 * J, C, k), ID,
+                           k > J ? 1u : 0u);
+        for (int k = J; k < 4; ++k)
+          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(blo, C, k), kdesc(S + SB_CBT + 2048 * J, C, k), ID, 1u);
+        if (J == 3)
+          mma_steps(tmem + TM_YO, [&](int k) { return mndesc(S + SB_S, N, k); },
+                    [&](int k) { return kdesc(S + SB_C, C, k); }, N / 16, sm100::idesc_bf16(64, 64, true, false), false);
+        sm100::umma_commit(bars + 8 + J);
+      }
+    }
+    {
+      // diagonal blocks of ddd, two threads per channel, two blocks each, while the MMAs run:
+      // ddd[j] = e^{c_s - c_j} sum_{i>=j} CB[i][j] (dy_i e^{c_i - c_s}) with s the block's last row
+      float* DDG = reinterpret_cast<float*>(smem + SB_DDG);  // [p][j]
+      const int p = tid & 63;
+#pragma unroll 1
+      for (int J = tid >> 6; J < 4; J += 2) {
+        const int r = 16 * J;
+        const float cs = CUM[(r + 15) * P + p];
+        float u[16], v[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float ct = CUM[(r + t) * P + p];
+          u[t] = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, r + t, p)));
+          v[t] = __expf(cs - ct);
+        }
+        const bool wide = !(CUM[r * P + p] - cs <= 80.f);
+        if (!wide) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) u[t] *= __expf(CUM[(r + t) * P + p] - cs);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = j; i < 16; ++i)
+              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_CB + sw_off(C, r + i, r + j))) * u[i];
+            DDG[p * C + r + j] = v[j] * acc;
+          }
+        } else {
+          for (int j = 0; j < 16; ++j) DDG[p * C + r + j] = sb_exact_ddd(smem, CUM, p, r + j, J);
+        }
+      }
+    }
+    if (!wait_bar(bars + 10, ph, err, 0x5337) || !wait_bar(bars + 11, ph, err, 0x5337)) flags[4] = 1;
+    sm100::tc_fence_after();
+    __syncthreads();
+    {
+      // per channel p = 16 warp + lane (lanes 0-15): dc, its reverse cumulative sum and the outputs
+      const int p = 16 * warp + lane;
+      float dds[64];
+      tmem_ld32(tmem_at(tmem, warp, TM_DDS), dds);
+      tmem_ld32(tmem_at(tmem, warp, TM_DDS + 32), dds + 32);
+      float dcl = 0.f, dAh = 0.f, g = 0.f, cl = 0.f;
+      bf16* OX = reinterpret_cast<bf16*>(smem + SB_OX);
+      bf16* ODT = reinterpret_cast<bf16*>(smem + SB_ODT);
+      if (lane < 16) {
+        cl = CUM[(C - 1) * P + p];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float dlt = cl - CUM[j * P + p];
+          const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, j, p)));
+          const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, j, p)));
+          if (dlt > -20.f) dcl += clip4(dv * xv) * dds[j] * __expf(dlt);
+        }
+        float car = 0.f;
+        for (int s = 0; s < N; ++s)
+          car += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DS + sw_off(N, s, p))) *
+                 __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_S + sw_off(N, s, p)));
+        if (cl > -20.f) dcl += car * __expf(cl);
+      }
+#pragma unroll
+      for (int J = 3; J >= 0; --J) {
+        float ddd[16], yo[16];
+        tmem_ld16(tmem_at(tmem, warp, TM_DDD + 16 * J), ddd);
+        tmem_ld16(tmem_at(tmem, warp, TM_YO + 16 * J), yo);
+        if (lane < 16) {
+          float ydv[16];
+          const float* ydr = yd_t + ch * (C * P) + p * C + 16 * J;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(ydr + 4 * q4);
+            ydv[4 * q4] = v4.x; ydv[4 * q4 + 1] = v4.y; ydv[4 * q4 + 2] = v4.z; ydv[4 * q4 + 3] = v4.w;
+          }
+          const float cs = CUM[(16 * J + 15) * P + p];
+#pragma unroll
+          for (int r = 15; r >= 0; --r) {
+            const int i = 16 * J + r;
+            const float ci = CUM[i * P + p];
+            const float dyv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i, p)));
+            const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
+            const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
+            const float bx = clip4(dtv * xv);
+            const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[p * C + i];
+            const float dlt = cl - ci;
+            const float ds = dds[i] * __expf(fmaxf(dlt, -20.f));
+            float dc = dyv * ydv[r] - bx * dd;
+            if (ci > -20.f) dc += dyv * yo[r] * __expf(ci);
+            if (dlt > -20.f) dc -= bx * ds;
+            if (i == C - 1) dc += dcl;
+            g += dc;
+            const float pre = dtv * Ah;
+            const float gA = (pre > -20.f && pre < 20.f) ? g : 0.f;
+            const float ddbx = dd + ds;
+            OX[i * P + p] = __float2bfloat16_rn(ddbx * dtv);
+            ODT[i * P + p] = __float2bfloat16_rn(ddbx * xv + gA * Ah);
+            dAh += gA * dtv;
+          }
+        }
+      }
+      dAh = warp_sum(dAh);
+      if (lane == 0) atomicAdd(dA_o + h, dAh);
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < (C * P / 8) / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int i = u_ >> 3, c8 = (u_ & 7) << 3;
+      const int64_t gi = (((int64_t)b * L + (int64_t)n * C + i) * H + h) * P + c8;
+      *reinterpret_cast<uint4*>(dx_o + gi) = *reinterpret_cast<const uint4*>(smem + SB_OX + (i * P + c8) * 2);
+      *reinterpret_cast<uint4*>(ddt_o + gi) = *reinterpret_cast<const uint4*>(smem + SB_ODT + (i * P + c8) * 2);
+    }
+    __syncthreads();
+  }
+  if (flags[4]) goto sb_teardown;
+  // dC += dCB B and dB += dCB^T C with dCB summed over the group's heads
+#pragma unroll
+  for (int it = 0; it < (C * C / 8) / SB_THREADS; ++it) {
+    const int u_ = it * SB_THREADS + tid;
+    const int i = u_ >> 3, c = (u_ & 7) << 3;
+    st_chunk8(S + SB_CB + sw_off16(C, i, c), DCB + i * C + c);
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    sm100::tc_fence_after();
+    mma_steps(tmem + TM_DC, [&](int k) { return kdesc(S + SB_CB, C, k); }, [&](int k) { return mndesc(S + SB_B, C, k); },
+              C / 16, sm100::idesc_bf16(64, 128, false, true), true);
+    mma_steps(tmem + TM_DB, [&](int k) { return mndesc(S + SB_CB, C, k); }, [&](int k) { return mndesc(S + SB_C, C, k); },
+              C / 16, sm100::idesc_bf16(64, 128, true, true), true);
+    sm100::umma_commit(bars + 13);
+  }
+  if (!wait_bar(bars + 13, 0, err, 0x5338)) goto sb_teardown;
+  sm100::tc_fence_after();
+  {
+    const int i = 16 * warp + lane;
+    const int64_t off = (((int64_t)blockIdx.z * gridDim.y + b) * L + (int64_t)n * C + i) * N;
+#pragma unroll 1
+    for (int q = 0; q < 8; ++q) {
+      float x[32];
+      tmem_ld32(tmem_at(tmem, warp, (q < 4 ? TM_DC : TM_DB) + 32 * (q & 3)), x);
+      if (lane < 16) {
+        float* dst = (q < 4 ? dC_part : dB_part) + off + 32 * (q & 3);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+      }
+    }
+  }
+sb_teardown:
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+}
+
+__global__ void sum_groups_tc(const float* __restrict__ part, int G, int64_t n, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int g = 0; g < G; ++g) s += part[g * n + i];
+    out[i] = s;
+  }
+}
+
+__device__ __noinline__ float sb_exact_ddd(const unsigned char* smem, const float* CUM, int p, int i, int J) {
+  float acc = 0.f;
+  const float ci = CUM[i * P + p];
+  for (int i2 = i; i2 < 16 * J + 16; ++i2) {
+    const float cb = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_CB + sw_off(C, i2, i)));
+    const float dy = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i2, p)));
+    acc += cb * dy * __expf(fmaxf(CUM[i2 * P + p] - ci, -20.f));
+  }
+  return acc;
+}
+
 template <class K>
 int set_smem_tc(K kernel, size_t bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess ? 0 : -3;
 }
 
 // S1 + S2 on the given scratch (per chunk-head: S_end^T image, y_diag^T rows, decay image, last
-// cumsum; these are SSD_SCRATCH_PER_CHUNK_HEAD bytes in this order within one chunk-head's slot)
+// cumsum)
 int ssd_forward(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
-                unsigned char* send_t, bf16* yd_t, unsigned char* dec_t, float* cl, const float* s0, float* s_final,
+                unsigned char* send_t, float* yd_t, unsigned char* dec_t, float* cl, const float* s0, float* s_final,
                 void* y, unsigned char* sin_t, int* err, cudaStream_t st) {
   static int i1 = set_smem_tc(ssd_chunk_fwd_tc, S1_SMEM);
   static int i2 = set_smem_tc(ssd_state_fwd_tc, S2_SMEM);
@@ -545,8 +1024,35 @@ int ahb_ssd_supported(int P_, int N_) { return (P_ == P && N_ == N) ? C : 0; }
 int ahb_ssd_fwd_tc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, int B, int L, int H,
                    void* send_t, void* yd_t, void* dec_t, float* cl, const float* s0, float* s_final, void* y,
                    void* sin_t, int* err, cudaStream_t st) {
-  return ssd_forward(x, dt, A, Bm, Cm, B, L, H, (unsigned char*)send_t, (bf16*)yd_t, (unsigned char*)dec_t, cl, s0,
+  return ssd_forward(x, dt, A, Bm, Cm, B, L, H, (unsigned char*)send_t, (float*)yd_t, (unsigned char*)dec_t, cl, s0,
                      s_final, y, (unsigned char*)sin_t, err, st);
+}
+
+int ahb_ssd_head_groups(int H) {
+  for (int g : {8, 4, 2}) if (H % g == 0) return g;
+  return 1;
+}
+
+int ahb_ssd_bwd_chunk_tc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
+                         int B, int L, int H, const void* sin_t, const void* dse_t, const void* yd_t, void* dx, void* ddt,
+                         float* dB, float* dC, float* dA, float* dB_part, float* dC_part, int* err, cudaStream_t st) {
+  static int i1 = set_smem_tc(ssd_chunk_bwd_tc, SB_SMEM);
+  if (i1) return -3;
+  CUtensorMap tb, tc, tx, tdt, tdy;
+  if (tmap_2d_bf16(&tb, Bm, (int64_t)B * L, N, C) || tmap_2d_bf16(&tc, Cm, (int64_t)B * L, N, C) ||
+      tmap_seq_bf16(&tx, x, (int64_t)B * L, H, P, C) || tmap_seq_bf16(&tdt, dt, (int64_t)B * L, H, P, C) ||
+      tmap_seq_bf16(&tdy, dy, (int64_t)B * L, H, P, C))
+    return -20;
+  const int G = ahb_ssd_head_groups(H);
+  ssd_chunk_bwd_tc<<<dim3(L / C, B, G), SB_THREADS, SB_SMEM, st>>>(
+      tb, tc, tx, tdt, tdy, A, (const unsigned char*)sin_t, (const unsigned char*)dse_t, (const float*)yd_t, L, H,
+      (bf16*)dx, (bf16*)ddt, dA, dB_part, dC_part, err);
+  if (cudaGetLastError() != cudaSuccess) return -4;
+  const int64_t n = (int64_t)B * L * N;
+  const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  sum_groups_tc<<<blocks, 256, 0, st>>>(dB_part, G, n, dB);
+  sum_groups_tc<<<blocks, 256, 0, st>>>(dC_part, G, n, dC);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
 int ahb_ssd_state_bwd_tc(const void* Cm, const void* dy, const void* dec_t, const float* cl, int B, int L, int H,
@@ -574,7 +1080,7 @@ constexpr int kMaxDevices = 64;
 void* g_noalloc_ptr[kMaxDevices] = {};
 int* g_noalloc_err[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
-static_assert(T_NP + C * P * 2 + T_CP + P * 4 == (64 * 128 + 64) * 4, "scratch per chunk-head");
+static_assert(T_NP + C * P * 4 + T_CP + P * 4 == AHB_SSD_NOALLOC_BYTES_PER_CHUNK_HEAD, "scratch per chunk-head");
 }  // namespace
 
 extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm,
@@ -607,8 +1113,8 @@ extern "C" int ahb_ssd_fwd_noalloc(const void* x, const void* dt, const float* A
     errp = g_noalloc_err[dev];
   }
   unsigned char* send_t = base;
-  bf16* yd_t = reinterpret_cast<bf16*>(send_t + chunk_heads * T_NP);
-  unsigned char* dec_t = reinterpret_cast<unsigned char*>(yd_t) + chunk_heads * (C * P * 2);
+  float* yd_t = reinterpret_cast<float*>(send_t + chunk_heads * T_NP);
+  unsigned char* dec_t = reinterpret_cast<unsigned char*>(yd_t) + chunk_heads * (C * P * 4);
   float* cl = reinterpret_cast<float*>(dec_t + chunk_heads * T_CP);
   const int rc = ssd_forward(x, dt, A, Bm, Cm, B, L, H, send_t, yd_t, dec_t, cl, nullptr, nullptr, y, nullptr, errp,
                              stream);

@@ -197,9 +197,9 @@ def gdn2(q, k, v, w, b, g, scale, chunk):
 
 class _SSD(torch.autograd.Function):
     """sm_100a Mamba2 SSD (head dim 64, d_state 128, chunk 64): 2 launches forward
-    (chunk kernel, state recurrence); the backward reuses the forward's per-chunk states
-    (4 launches: reverse state-gradient recurrence, chunk backward, two group sums) or
-    recomputes them (6)."""
+    (chunk kernel, state recurrence); the backward reuses the forward's per-chunk states and
+    intra-chunk outputs (4 launches: reverse state-gradient recurrence, chunk backward, two
+    group sums) or recomputes them (6)."""
 
     @staticmethod
     def forward(ctx, dt, A, Bm, Cm, x):
@@ -207,8 +207,8 @@ class _SSD(torch.autograd.Function):
         dt, Bm, Cm, x = (t.to(bf).contiguous() for t in (dt, Bm, Cm, x))
         A = A.float().contiguous()
         if any(ctx.needs_input_grad) and not SCAN_RECOMPUTE:
-            y, states, decays, cums = ext().ssd_fwd_train(x, dt, A, Bm, Cm)
-            ctx.save_for_backward(dt, A, Bm, Cm, x, states, decays, cums)
+            y, *saved = ext().ssd_fwd_train(x, dt, A, Bm, Cm)
+            ctx.save_for_backward(dt, A, Bm, Cm, x, *saved)
         else:
             y = ext().ssd_fwd(x, dt, A, Bm, Cm)
             ctx.save_for_backward(dt, A, Bm, Cm, x)

@@ -37,20 +37,21 @@ def test_ssd_forward(B, L, H, shift):
     assert _rel(y, y_ref) < 2e-2, _rel(y, y_ref)
 
 
-@pytest.mark.parametrize("B,L,H,shift", [(1, 128, 1, -4.0), (2, 192, 2, -1.0), (1, 128, 2, 2.0)])
+@pytest.mark.parametrize("B,L,H,shift", [(1, 128, 1, -4.0), (2, 192, 2, -1.0), (1, 128, 2, 2.0), (2, 256, 3, -1.0)])
 def test_ssd_backward(B, L, H, shift):
+    """Gradients against an fp64 oracle on the same bf16-rounded inputs.  dA is an (H,) sum of
+    ~B*L*64 products of both signs whose intra-chunk parts cancel (the gradient of a decay shift);
+    the kernel keeps the cancelling sums at fp32 precision (exact diagonal blocks, two-term bf16
+    operands elsewhere), so dA is held to 5e-2 like the per-element gradients."""
     ins = _inputs(B, L, H, 3, shift)
     xs = [t.clone().requires_grad_(True) for t in ins]
     y = K.ssd(*xs, 64)
     dy = torch.randn_like(y)
     (y.float() * dy.float()).sum().backward()
-    rs = [t.detach().float().clone().requires_grad_(True) for t in ins]
+    rs = [t.detach().double().clone().requires_grad_(True) for t in ins]
     y2, _ = R.ssd_chunked(*rs, 64)
-    (y2 * dy.float()).sum().backward()
+    (y2 * dy.double()).sum().backward()
     for name, a, r in zip(["dt", "A", "B", "C", "x"], xs, rs):
         assert torch.isfinite(a.grad).all(), name
         err = _rel(a.grad, r.grad)
-        # dA is a (H,) sum of ~B*L*64 bf16-rounded products of both signs; the
-        # cancellation leaves a larger relative error than the per-element grads.
-        tol = 0.3 if name == "A" else 5e-2
-        assert err < tol, (name, err)
+        assert err < 5e-2, (name, err)

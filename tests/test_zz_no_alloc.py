@@ -44,8 +44,8 @@ def _call(fn, x, dt, A, Bm, Cm, y):
               torch.cuda.current_stream().cuda_stream)
 
 
-# the largest problem the fixed scratch holds: B * H * (L / 64) = 1 * 8 * 127 = 1016 chunk-heads
-MAX_CASE = (1, 127 * 64, 8)
+# the largest problem the fixed scratch holds: B * H * (L / 64) = 1 * 2 * 407 = 814 chunk-heads
+MAX_CASE = (1, 407 * 64, 2)
 
 
 def test_noalloc_ssd_forward_matches_allocating_entry_point():
@@ -66,9 +66,9 @@ def test_noalloc_ssd_forward_matches_allocating_entry_point():
 
 def test_noalloc_rejects_oversized_problem():
     fn = _fn()
-    # one chunk-head beyond the fixed scratch (1 * 8 * 128 = 1024 > 1016), and a far larger one:
+    # one chunk-head beyond the fixed scratch (1 * 5 * 163 = 815 > 814), and a far larger one:
     # both rejected before any launch
-    for B, L, H in [(1, 128 * 64, 8), (64, 8192, 64)]:
+    for B, L, H in [(1, 163 * 64, 5), (64, 8192, 64)]:
         x, dt, A, Bm, Cm = _inputs(1, 64, 1, 0)
         y = torch.empty_like(x)
         rc = fn(x.data_ptr(), dt.data_ptr(), A.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), B, L, H, y.data_ptr(),
