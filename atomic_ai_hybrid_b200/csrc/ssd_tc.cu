@@ -41,6 +41,11 @@ constexpr int T_CN = C * N * 2;   // 64 x 128 bf16 tile (16 KB)
 constexpr int T_NP = N * P * 2;   // 128 x 64 bf16 tile (16 KB)
 
 AHB_DEVICE float clip4(float x) { return sanitize(x, 1e4f); }
+// 8 consecutive fp32 of a shared-memory row (two 16-byte loads)
+AHB_DEVICE void ld8f(const float* src, float* o) {
+  const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
 
 // ============================================================ chunk-parallel forward
 constexpr int S1_THREADS = 128;
@@ -109,9 +114,11 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     float xv[8], dv[8], o[8];
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
+    float cj[8], cl8[8];
+    ld8f(CUM + j * P + c, cj);
+    ld8f(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      o[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(CUM[(C - 1) * P + c + e] - CUM[j * P + c + e], -20.f));
+    for (int e = 0; e < 8; ++e) o[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - cj[e], -20.f));
     st_chunk8(S + S1_V + sw_off16(C, j, c), o);
   }
   fence_async_smem();
@@ -157,9 +164,12 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
       const bool zero = j >= 16 * I;  // the diagonal block is summed exactly below
+      float cj[8], cr8[8];
+      ld8f(CUM + j * P + c, cj);
+      ld8f(CUM + 16 * I * P + c, cr8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(CUM[16 * I * P + c + e] - CUM[j * P + c + e]);
+        o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
         lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
       }
       st_chunk8(buf + sw_off16(C, j, c), o);
@@ -222,13 +232,11 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       for (int I = tid >> 6; I < 4; I += 2) {
         const int r = 16 * I;
         const float cr = CUM[r * P + p];
-        float u[16], w[16];
+        float w[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float ct = CUM[(r + t) * P + p];
           const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_X + sw_off(C, r + t, p)));
           const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_DT + sw_off(C, r + t, p)));
-          u[t] = __expf(ct - cr);
           w[t] = clip4(dv * xv);
         }
         const bool wide = !(cr - CUM[(r + 15) * P + p] <= 80.f);
@@ -241,7 +249,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
 #pragma unroll
             for (int j = 0; j <= i; ++j)
               acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) * w[j];
-            YD[p * C + r + i] += u[i] * acc;
+            YD[p * C + r + i] += __expf(CUM[(r + i) * P + p] - cr) * acc;
           }
         } else {
           for (int i = 0; i < 16; ++i) {
@@ -269,9 +277,10 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     for (int it = 0; it < (C * P / 8) / S1_THREADS; ++it) {
       const int u_ = it * S1_THREADS + tid;
       const int i = u_ >> 3, c = (u_ & 7) << 3;
-      float o[8];
+      float o[8], ci[8];
+      ld8f(CUM + i * P + c, ci);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = __expf(fmaxf(CUM[i * P + c + e], -20.f));
+      for (int e = 0; e < 8; ++e) o[e] = __expf(fmaxf(ci[e], -20.f));
       *reinterpret_cast<uint4*>(dec_t + ch * T_CP + sw_off16(C, i, c)) = pack8(o);
     }
   }
@@ -561,13 +570,13 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
 //   y_off^T = S_in C^T ; then per channel p, rows i = 63 .. 0: dc, its reverse cumulative sum g,
 //   ddt = d(dBx) x + g A [unclipped], dx = d(dBx) dt, dA_h += g dt
 // and after the heads dC += dCB B, dB += dCB^T C (dCB summed over the heads), written per group.
-constexpr int SB_THREADS = 128;
+constexpr int SB_THREADS = 256;
 constexpr int SB_B = 0, SB_C = 16384, SB_CB = 32768, SB_CBT = 40960, SB_DCB = 49152, SB_X = 65536, SB_DT = 73728,
               SB_DY = 81920, SB_S = 90112, SB_DS = 106496, SB_CUM = 122880, SB_DYR = 139264, SB_BI0 = 147456,
               SB_BI1 = 155648, SB_DYD = 163840, SB_V = 172032, SB_DYS0 = 180224, SB_DYS1 = 188416, SB_BAR = 196608;
 // per-head outputs dx, ddt staged as plain [i][p] bf16 rows over the dead phase-1 operands, and the
 // diagonal part of ddd (fp32 [p][j]) after them
-constexpr int SB_OX = SB_DYR, SB_ODT = SB_DYR + T_CP, SB_DDG = SB_BI1;
+constexpr int SB_OX = SB_DYR, SB_ODT = SB_DYR + T_CP, SB_DDG = SB_BI1, SB_XCH = SB_DDG + 16384;
 constexpr size_t SB_SMEM = 1024 + SB_BAR + 256;
 // TMEM columns: dC [0,128) and dB [128,256) (M = 64, N = 128); dCB per row block I at 256 + 8 I (I + 1)
 // (widths 16, 32, 48, 64); dds^T [416, 480); later ddd^T per key block J at 256 + 16 J and
@@ -601,7 +610,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
 
   const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
   const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quarter = warp & 3, wg = warp >> 2;
   const int row0 = b * L + n * C;
   if (tid == 0) {
     for (int i = 0; i < 14; ++i) sm100::mbar_init(bars + i, 1);
@@ -628,7 +637,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
   }
   if (!wait_bar(bars + 1, 0, err, 0x5332)) flags[4] = 1;
   sm100::tc_fence_after();
-  {  // causal CB -> rows tile (i, j) and transposed tile (j, i)
+  if (wg == 0) {  // causal CB -> rows tile (i, j) and transposed tile (j, i)
     const int i = 16 * warp + lane;
     float x[64];
     tmem_ld32(tmem_at(tmem, warp, TM_DCB), x);
@@ -687,12 +696,15 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, i, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, i, c)), dv);
+      float c8[8], cr8[8], cl8[8];
+      ld8f(CUM + i * P + c, c8);
+      ld8f(CUM + (i & ~15) * P + c, cr8);
+      ld8f(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float ci = CUM[i * P + c + e];
-        r8[e] = dy[e] * __expf(ci - CUM[(i & ~15) * P + c + e]);
-        d8[e] = dy[e] * __expf(fmaxf(ci, -20.f));
-        v8[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(CUM[(C - 1) * P + c + e] - ci, -20.f));
+        r8[e] = dy[e] * __expf(c8[e] - cr8[e]);
+        d8[e] = dy[e] * __expf(fmaxf(c8[e], -20.f));
+        v8[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - c8[e], -20.f));
       }
       st_chunk8(S + SB_DYR + sw_off16(C, i, c), r8);
       st_chunk8(S + SB_DYD + sw_off16(C, i, c), d8);
@@ -719,16 +731,17 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       if (I >= 2 && !wait_bar(bars + 4 + I - 2, ph, err, 0x5334)) flags[4] = 1;
       const bool exact = flags[I];
 #pragma unroll
-      for (int it = 0; it <= I; ++it) {
-        const int u_ = it * SB_THREADS + tid;
+      for (int u_ = tid; u_ < 16 * (I + 1) * 8; u_ += SB_THREADS) {
         const int j = u_ >> 3, c = (u_ & 7) << 3;
         float xv[8], dv[8], o[8];
         unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
         unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
         const bool zero = exact && j >= 16 * I;
+        float cj[8], cr8[8];
+        ld8f(CUM + j * P + c, cj);
+        ld8f(CUM + 16 * I * P + c, cr8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(CUM[16 * I * P + c + e] - CUM[j * P + c + e]);
+        for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
         st_chunk8(buf + sw_off16(C, j, c), o);
       }
       fence_async_smem();
@@ -746,7 +759,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
         !wait_bar(bars + 7, ph, err, 0x5335))
       flags[4] = 1;
     sm100::tc_fence_after();
-    {  // dCB rows i = 16 warp + lane (block I = warp) into the fp32 sum over the heads
+    if (wg == 0) {  // dCB rows i = 16 warp + lane (block I = warp) into the fp32 sum over the heads
       const int i = 16 * warp + lane, I = warp;
       float x[64];
 #pragma unroll
@@ -786,15 +799,17 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       if (J >= 2 && !wait_bar(bars + 8 + J - 2, ph, err, 0x5336)) flags[4] = 1;
       const float* cs = CUM + (16 * J + 15) * P;
 #pragma unroll
-      for (int it = J; it < 4; ++it) {
-        const int u_ = it * SB_THREADS + tid;
+      for (int u_ = 16 * J * 8 + tid; u_ < C * 8; u_ += SB_THREADS) {
         const int i = u_ >> 3, c = (u_ & 7) << 3;
         float dy[8], o[8], lo[8];
         unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
         const bool zero = i < 16 * J + 16;  // the diagonal block is summed exactly in the epilogue
+        float ci[8], cs8[8];
+        ld8f(CUM + i * P + c, ci);
+        ld8f(cs + c, cs8);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          o[e] = zero ? 0.f : dy[e] * __expf(CUM[i * P + c + e] - cs[c + e]);
+          o[e] = zero ? 0.f : dy[e] * __expf(ci[e] - cs8[e]);
           lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
         }
         st_chunk8(buf + sw_off16(C, i, c), o);
@@ -818,21 +833,18 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       }
     }
     {
-      // diagonal blocks of ddd, two threads per channel, two blocks each, while the MMAs run:
+      // diagonal blocks of ddd, four threads per channel, one block each, while the MMAs run:
       // ddd[j] = e^{c_s - c_j} sum_{i>=j} CB[i][j] (dy_i e^{c_i - c_s}) with s the block's last row
       float* DDG = reinterpret_cast<float*>(smem + SB_DDG);  // [p][j]
       const int p = tid & 63;
-#pragma unroll 1
-      for (int J = tid >> 6; J < 4; J += 2) {
+      {
+        const int J = tid >> 6;
         const int r = 16 * J;
         const float cs = CUM[(r + 15) * P + p];
-        float u[16], v[16];
+        float u[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const float ct = CUM[(r + t) * P + p];
+        for (int t = 0; t < 16; ++t)
           u[t] = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, r + t, p)));
-          v[t] = __expf(cs - ct);
-        }
         const bool wide = !(CUM[r * P + p] - cs <= 80.f);
         if (!wide) {
 #pragma unroll
@@ -843,7 +855,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
 #pragma unroll
             for (int i = j; i < 16; ++i)
               acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_CB + sw_off(C, r + i, r + j))) * u[i];
-            DDG[p * C + r + j] = v[j] * acc;
+            DDG[p * C + r + j] = __expf(cs - CUM[(r + j) * P + p]) * acc;
           }
         } else {
           for (int j = 0; j < 16; ++j) DDG[p * C + r + j] = sb_exact_ddd(smem, CUM, p, r + j, J);
@@ -854,34 +866,33 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     sm100::tc_fence_after();
     __syncthreads();
     {
-      // per channel p = 16 warp + lane (lanes 0-15): dc, its reverse cumulative sum and the outputs
-      const int p = 16 * warp + lane;
-      float dds[64];
-      tmem_ld32(tmem_at(tmem, warp, TM_DDS), dds);
-      tmem_ld32(tmem_at(tmem, warp, TM_DDS + 32), dds + 32);
-      float dcl = 0.f, dAh = 0.f, g = 0.f, cl = 0.f;
+      // per channel p = 16 quarter + lane (lanes 0-15), two threads per channel: warpgroup 0 rows
+      // 32-63, warpgroup 1 rows 0-31.  Pass 1 (descending rows): dc without the last row's extra
+      // term and its local suffix sums, d(dBx), dx; the two halves then exchange the upper suffix
+      // total and the parts of that extra term (state carry and the state part of d(dBx)); pass 2:
+      // g, ddt and dA.
+      const int p = 16 * quarter + lane;
+      const int jb = wg == 0 ? 2 : 0;  // first of this thread's two blocks
+      float* XCH = reinterpret_cast<float*>(smem + SB_XCH);  // [0,64) upper suffix total, [64,192) dcl parts
+      float dds[32];
+      tmem_ld32(tmem_at(tmem, quarter, TM_DDS + 16 * jb), dds);
+      float suf[32], ddbx[32];
+      float dclp = 0.f, local = 0.f, cl = 0.f;
       bf16* OX = reinterpret_cast<bf16*>(smem + SB_OX);
-      bf16* ODT = reinterpret_cast<bf16*>(smem + SB_ODT);
       if (lane < 16) {
         cl = CUM[(C - 1) * P + p];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float dlt = cl - CUM[j * P + p];
-          const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, j, p)));
-          const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, j, p)));
-          if (dlt > -20.f) dcl += clip4(dv * xv) * dds[j] * __expf(dlt);
-        }
         float car = 0.f;
-        for (int s = 0; s < N; ++s)
+        for (int s = 64 * (1 - wg); s < 64 * (2 - wg); ++s)
           car += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DS + sw_off(N, s, p))) *
                  __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_S + sw_off(N, s, p)));
-        if (cl > -20.f) dcl += car * __expf(cl);
+        if (cl > -20.f) dclp += car * __expf(cl);
       }
 #pragma unroll
-      for (int J = 3; J >= 0; --J) {
+      for (int jj = 1; jj >= 0; --jj) {
+        const int J = jb + jj;
         float ddd[16], yo[16];
-        tmem_ld16(tmem_at(tmem, warp, TM_DDD + 16 * J), ddd);
-        tmem_ld16(tmem_at(tmem, warp, TM_YO + 16 * J), yo);
+        tmem_ld16(tmem_at(tmem, quarter, TM_DDD + 16 * J), ddd);
+        tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * J), yo);
         if (lane < 16) {
           float ydv[16];
           const float* ydr = yd_t + ch * (C * P) + p * C + 16 * J;
@@ -893,7 +904,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           const float cs = CUM[(16 * J + 15) * P + p];
 #pragma unroll
           for (int r = 15; r >= 0; --r) {
-            const int i = 16 * J + r;
+            const int i = 16 * J + r, il = 16 * jj + r;
             const float ci = CUM[i * P + p];
             const float dyv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i, p)));
             const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
@@ -901,19 +912,39 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
             const float bx = clip4(dtv * xv);
             const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[p * C + i];
             const float dlt = cl - ci;
-            const float ds = dds[i] * __expf(fmaxf(dlt, -20.f));
+            const float ds = dds[il] * __expf(fmaxf(dlt, -20.f));
             float dc = dyv * ydv[r] - bx * dd;
             if (ci > -20.f) dc += dyv * yo[r] * __expf(ci);
-            if (dlt > -20.f) dc -= bx * ds;
-            if (i == C - 1) dc += dcl;
-            g += dc;
-            const float pre = dtv * Ah;
-            const float gA = (pre > -20.f && pre < 20.f) ? g : 0.f;
-            const float ddbx = dd + ds;
-            OX[i * P + p] = __float2bfloat16_rn(ddbx * dtv);
-            ODT[i * P + p] = __float2bfloat16_rn(ddbx * xv + gA * Ah);
-            dAh += gA * dtv;
+            if (dlt > -20.f) {
+              dc -= bx * ds;
+              dclp += bx * ds;
+            }
+            local += dc;
+            suf[il] = local;
+            ddbx[il] = dd + ds;
+            OX[i * P + p] = __float2bfloat16_rn(ddbx[il] * dtv);
           }
+        }
+      }
+      if (lane < 16) {
+        if (wg == 0) XCH[p] = local;
+        XCH[64 + 64 * wg + p] = dclp;
+      }
+      __syncthreads();
+      float dAh = 0.f;
+      if (lane < 16) {
+        const float off = XCH[64 + p] + XCH[128 + p] + (wg == 1 ? XCH[p] : 0.f);
+        bf16* ODT = reinterpret_cast<bf16*>(smem + SB_ODT);
+#pragma unroll
+        for (int il = 0; il < 32; ++il) {
+          const int i = 16 * jb + il;
+          const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
+          const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
+          const float g = off + suf[il];
+          const float pre = dtv * Ah;
+          const float gA = (pre > -20.f && pre < 20.f) ? g : 0.f;
+          ODT[i * P + p] = __float2bfloat16_rn(ddbx[il] * xv + gA * Ah);
+          dAh += gA * dtv;
         }
       }
       dAh = warp_sum(dAh);
@@ -953,12 +984,13 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
   if (!wait_bar(bars + 13, 0, err, 0x5338)) goto sb_teardown;
   sm100::tc_fence_after();
   {
-    const int i = 16 * warp + lane;
+    // warpgroup 0 reads dC, warpgroup 1 dB (rows i = 16 quarter + lane, lanes 0-15)
+    const int i = 16 * quarter + lane;
     const int64_t off = (((int64_t)blockIdx.z * gridDim.y + b) * L + (int64_t)n * C + i) * N;
 #pragma unroll 1
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 4 * wg; q < 4 * wg + 4; ++q) {
       float x[32];
-      tmem_ld32(tmem_at(tmem, warp, (q < 4 ? TM_DC : TM_DB) + 32 * (q & 3)), x);
+      tmem_ld32(tmem_at(tmem, quarter, (q < 4 ? TM_DC : TM_DB) + 32 * (q & 3)), x);
       if (lane < 16) {
         float* dst = (q < 4 ? dC_part : dB_part) + off + 32 * (q & 3);
 #pragma unroll
