@@ -48,7 +48,7 @@ AHB_DEVICE void ld8f(const float* src, float* o) {
 }
 
 // ============================================================ chunk-parallel forward
-constexpr int S1_THREADS = 128;
+constexpr int S1_THREADS = 256;
 constexpr int S1_B = 0, S1_C = 16384, S1_X = 32768, S1_DT = 40960, S1_CB = 49152, S1_V = 57344, S1_W0 = 65536,
               S1_W1 = 73728, S1_CUM = 81920, S1_BAR = 98304;
 constexpr size_t S1_SMEM = 1024 + S1_BAR + 256;
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [4] abort
 
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quarter = warp & 3, wg = warp >> 2;
   const int row0 = b * L + n * C;
   const int64_t ch = ((int64_t)b * H + h) * NC + n;
   if (tid == 0) {
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   }
   if (!wait_bar(bars + 1, 0, err, 0x5302)) flags[4] = 1;
   sm100::tc_fence_after();
-  {  // causal CB rows (lanes 0-15 of each quarter) -> bf16 K-major tile (rows i, columns j <= i)
+  if (wg == 0) {  // causal CB rows (lanes 0-15 of each quarter) -> bf16 K-major tile (rows i, columns j <= i)
     const int i = 16 * warp + lane;
     float x[64];
     tmem_ld32(tmem_at(tmem, warp, 0), x);
@@ -157,8 +157,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     const uint32_t blo = S + S1_C + (I & 1) * T_CP;  // the C tile is dead once CB is formed
     if (I >= 2 && !wait_bar(bars + 3 + I - 2, 0, err, 0x5303)) flags[4] = 1;
 #pragma unroll
-    for (int it = 0; it <= I; ++it) {
-      const int u_ = it * S1_THREADS + tid;
+    for (int u_ = tid; u_ < 16 * (I + 1) * 8; u_ += S1_THREADS) {
       const int j = u_ >> 3, c = (u_ & 7) << 3;
       float xv[8], dv[8], o[8], lo[8];
       unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
@@ -193,13 +192,14 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   __syncthreads();
   if (flags[4]) goto s1_teardown;
   {
-    // S_end^T rows (lane = state row s) -> tile image (rows s, columns p)
-    const int s = 32 * warp + lane;
+    // S_end^T rows (lane = state row s) -> tile image (rows s, columns p); warpgroup wg takes
+    // columns [32 wg, 32 wg + 32)
+    const int s = 32 * quarter + lane;
     unsigned char* dst = send_t + ch * T_NP;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    {
+      const int half = wg;
       float x[32];
-      tmem_ld32(tmem_at(tmem, warp, 64 + 32 * half), x);
+      tmem_ld32(tmem_at(tmem, quarter, 64 + 32 * half), x);
 #pragma unroll
       for (int c = 0; c < 32; c += 8) {
         float y[8];
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     // exponent floored at -20: these terms dominate and the backward's decay gradient cancels
     // them against the matching column sums); then fp32 rows out
     float* YD = reinterpret_cast<float*>(smem + S1_W0);  // [p][i]
-    {
+    if (wg == 0) {
       const int p = 16 * warp + lane;
       float y[64];
       tmem_ld32(tmem_at(tmem, warp, 128), y);
@@ -224,12 +224,12 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     }
     __syncthreads();
     {
-      // two threads per channel p, two blocks each: y[i] += e^{c_i - c_r} sum_{j<=i} CB[i][j] (dBx_j e^{c_r - c_j})
+      // four threads per channel p, one block each: y[i] += e^{c_i - c_r} sum_{j<=i} CB[i][j] (dBx_j e^{c_r - c_j})
       // with r the block's first row (fp32 factors; per-pair exponents where the block's span could
       // overflow them)
       const int p = tid & 63;
-#pragma unroll 1
-      for (int I = tid >> 6; I < 4; I += 2) {
+      {
+        const int I = tid >> 6;
         const int r = 16 * I;
         const float cr = CUM[r * P + p];
         float w[16];

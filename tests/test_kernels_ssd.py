@@ -39,19 +39,39 @@ def test_ssd_forward(B, L, H, shift):
 
 @pytest.mark.parametrize("B,L,H,shift", [(1, 128, 1, -4.0), (2, 192, 2, -1.0), (1, 128, 2, 2.0), (2, 256, 3, -1.0)])
 def test_ssd_backward(B, L, H, shift):
-    """Gradients against an fp64 oracle on the same bf16-rounded inputs.  dA is an (H,) sum of
-    ~B*L*64 products of both signs whose intra-chunk parts cancel (the gradient of a decay shift);
-    the kernel keeps the cancelling sums at fp32 precision (exact diagonal blocks, two-term bf16
-    operands elsewhere), so dA is held to 5e-2 like the per-element gradients."""
-    ins = _inputs(B, L, H, 3, shift)
+    """Gradients against an fp64 oracle on the same bf16-rounded inputs (per-element gradients
+    to 5e-2 relative).  dA[h] = sum_{b,t,p} g * dt over ~B*L*64 terms of both signs, g the
+    reverse cumulative sum of the decay gradient; for some dy a head's sum nearly cancels, so it is
+    checked per head against 5e-2 of its value plus 1e-3 of sum |g dt| (g from the oracle's own
+    dt / x gradients: ddt = g A + d(dBx) x, dx = d(dBx) dt) -- a missed or doubled term is off by
+    a sizeable part of that sum."""
+    _check_backward(B, L, H, shift, seed=3)
+
+
+def _check_backward(B, L, H, shift, seed):
+    ins = _inputs(B, L, H, seed, shift)
     xs = [t.clone().requires_grad_(True) for t in ins]
     y = K.ssd(*xs, 64)
-    dy = torch.randn_like(y)
+    dy = torch.randn(y.shape, generator=torch.Generator(device=dev).manual_seed(seed + 100), device=dev).to(y.dtype)
     (y.float() * dy.float()).sum().backward()
     rs = [t.detach().double().clone().requires_grad_(True) for t in ins]
     y2, _ = R.ssd_chunked(*rs, 64)
     (y2 * dy.double()).sum().backward()
     for name, a, r in zip(["dt", "A", "B", "C", "x"], xs, rs):
         assert torch.isfinite(a.grad).all(), name
-        err = _rel(a.grad, r.grad)
-        assert err < 5e-2, (name, err)
+        if name == "A":
+            dt64, x64, A64 = rs[0].detach(), rs[4].detach(), rs[1].detach()
+            g_dt = (rs[0].grad * dt64 - rs[4].grad * x64) / A64.view(1, 1, -1, 1)  # g * dt per element
+            scale = g_dt.abs().sum(dim=(0, 1, 3))
+            err = (a.grad.double() - r.grad).abs()
+            bound = 5e-2 * r.grad.abs() + 1e-3 * scale
+            assert (err <= bound).all(), (name, err.tolist(), bound.tolist())
+        else:
+            err = _rel(a.grad, r.grad)
+            assert err < 5e-2, (name, err)
+
+
+def test_ssd_production_shape_forward_backward():
+    """The op-benchmark shape per sequence (T = 4096, H = 32, P = 64, N = 128): 64 chunks per head,
+    all four head groups of the chunk backward, against the fp64 oracle."""
+    _check_backward(1, 4096, 32, -4.0, seed=5)
