@@ -192,8 +192,9 @@ class CheckpointManager:
                         o = s.offset - st.lo
                         mu, nu = _find(moments, f"mu/{name}", s, ep), _find(moments, f"nu/{name}", s, ep)
                         if load_optimizer and mu is not None and tuple(mu.shape) == tuple(s.shape):
-                            opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(st.device))
-                            opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(st.device))
+                            # into the moments' own memory (pinned host memory when they are staged)
+                            opt.m[o:o + s.numel].copy_(mu.reshape(-1).to(opt.m.device))
+                            opt.v[o:o + s.numel].copy_(nu.reshape(-1).to(opt.v.device))
                     restored.append(name)
                 if load_optimizer:
                     opt.count = int(meta.get("opt_count", 0))

@@ -197,7 +197,10 @@ def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> No
                      schedule=args.pipeline_schedule, local_moments_on_host=args.offload_local_moments)
         print(f"[MEMORY] plan per GPU: state {p['state_total_gb']} GB + activations ~{p['activations_gb_est']} GB "
               f"+ reserve {p['reserve_gb']} GB = {p['total_gb']} of {p['hbm_gb']} GB"
-              + ("" if p["fits"] else "  -- DOES NOT FIT: reduce the micro-batch or enable --remat"), flush=True)
+              + (f"; pinned host {p['host_pinned_gb_per_rank']} GB per rank, {p['host_pinned_gb_per_node']} GB "
+                 f"per node of {p['host_ram_gb']} GB RAM" if p["host_pinned_gb_per_rank"] else "")
+              + ("" if p["fits"] else "  -- DOES NOT FIT: reduce the micro-batch, enable --remat"
+                 + (" or keep the moments on the device" if not p["host_fits"] else "")), flush=True)
     except Exception as e:  # the plan never stops a run
         print(f"[MEMORY] plan unavailable: {e!r}", flush=True)
 

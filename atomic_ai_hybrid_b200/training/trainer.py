@@ -108,6 +108,7 @@ class Trainer:
         self._loss_sum = torch.zeros((), device=dev)
         self._n_micro = 0
         self.cuda_graph = cuda_graph and dev.type == "cuda"
+        self.phase_events = None  # dict name -> [cuda.Event] when a caller times the step phases
         if dev.type == "cuda":
             # the model's construction-time parameter tensors were replaced by views of the
             # flat store: hand their cached blocks back so that libraries allocating outside
@@ -190,7 +191,16 @@ class Trainer:
         self._n_micro = 0
 
     # ------------------------------------------------------------ apply
+    def _mark(self, name: str) -> None:
+        """Record a CUDA event at a phase boundary when the caller asked for phase timing
+        (``self.phase_events`` is a dict name -> list of events; off by default)."""
+        if self.phase_events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.phase_events.setdefault(name, []).append(e)
+
     def apply(self, n_accum: Optional[int] = None) -> Dict[str, torch.Tensor]:
+        self._mark("apply")
         n = n_accum if n_accum is not None else max(self._n_micro, 1)
         frac = None
         if self._n_micro > 0:
@@ -204,14 +214,17 @@ class Trainer:
             self.comm.begin_step()
         elif self.comm is not None:
             self.comm.reduce_scatter_grads()
+        self._mark("optimizer")
         # every rank's loss is the mean over its own tokens, and the reduction sums the
         # ranks: dividing by n_accum * world gives the gradient of the global-batch mean
         with nvtx_range("optimizer"):
             out = self.opt.step(n * self.world, frac)
+        self._mark("end_barrier")
         if self.fused_comm:
             self.comm.end_step()
         elif self.comm is not None:
             self.comm.all_gather_params()
+        self._mark("done")
         out["loss"] = self._loss_sum / max(self._n_micro, 1)
         self.reset_accumulators()
         # step diagnostics: the previous step's events print now ([FWD-DIAG], [RESID-DIAG], ...)
@@ -222,6 +235,7 @@ class Trainer:
     def train_step(self, micro_batches: List[Dict[str, torch.Tensor]]):
         if self.cuda_graph and (self._graph is None or self._graph_key != self._key(micro_batches[0])):
             self.build_graph(micro_batches[0])
+        self._mark("micro")
         for b in micro_batches:
             self.micro_step(b)
         return self.apply(len(micro_batches))

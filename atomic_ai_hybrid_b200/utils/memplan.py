@@ -29,12 +29,14 @@ the trainer would build, and adds an activation estimate:
 from __future__ import annotations
 
 import argparse
+import os
 import json
 from typing import Dict, Optional
 
 import torch
 
 HBM_BYTES = 183_359 * 2 ** 20          # B200 memory as nvidia-smi reports it
+GPUS_PER_NODE = 8
 CONTEXT_RESERVE = 2 * 10 ** 9          # CUDA context, NCCL and library workspaces
 ACT_BYTES_PER_TOKEN_LAYER_D = 81.0     # calibrated on the 1-GPU benchmark step (module doc)
 
@@ -45,7 +47,7 @@ def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torc
     from ..optim.store import is_ep_local
     named = list(module.named_parameters())
     out = {"replicated_params": 0, "local_params": 0, "master": 0.0, "grad": 0.0, "compute": 0.0,
-           "optimizer": 0.0}
+           "optimizer": 0.0, "host_pinned": 0.0}
     meta = torch.device("meta")
     rep = [n for n, p in named if not is_ep_local(n, p)]
     loc = [n for n, p in named if is_ep_local(n, p)]
@@ -66,7 +68,17 @@ def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torc
         out["compute"] += 2.0 * st.cnumel
         if not local_moments_on_host:
             out["optimizer"] += 8.0 * st.shard
+        else:  # the two fp32 moments move to pinned host memory of the rank's node
+            out["host_pinned"] += 8.0 * st.shard
     return out
+
+
+def host_ram_bytes() -> Optional[int]:
+    """Physical memory of this machine (None where the page counts are unavailable)."""
+    try:
+        return int(os.sysconf("SC_PAGE_SIZE")) * int(os.sysconf("SC_PHYS_PAGES"))
+    except (ValueError, OSError, AttributeError):
+        return None
 
 
 def activation_bytes(cfg, micro_batch: int, seq_len: int, layers: int, tp: int = 1, cp: int = 1,
@@ -82,8 +94,13 @@ def activation_bytes(cfg, micro_batch: int, seq_len: int, layers: int, tp: int =
 def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int = 1, ep: int = 1, cp: int = 1,
          pp: int = 1, accum_steps: int = 1, remat: bool = False, schedule: str = "1f1b",
          compute_dtype: torch.dtype = torch.bfloat16, local_grad_bytes: int = 4,
-         local_moments_on_host: bool = False) -> Dict:
-    """Memory of the most loaded rank of a layout, in bytes and GB (1e9)."""
+         local_moments_on_host: bool = False, host_ram_gb: Optional[float] = None) -> Dict:
+    """Memory of the most loaded rank of a layout, in bytes and GB (1e9).
+
+    With ``local_moments_on_host`` the rank-local AdamW moments live in pinned host memory:
+    ``host_pinned_gb_per_rank`` and ``host_pinned_gb_per_node`` (up to 8 ranks per node) count
+    them, and the layout fits only while a node's share stays within half of ``host_ram_gb``
+    (default: this machine's physical memory)."""
     from ..models import HybridMoEModel
     from ..parallel.context import ParallelContext, get_parallel_context, set_parallel_context
     for n, v in (("tp", tp), ("ep", ep), ("cp", cp), ("pp", pp)):
@@ -114,13 +131,23 @@ def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int
     state_total = state["master"] + state["grad"] + state["compute"] + state["optimizer"]
     total = state_total + act + CONTEXT_RESERVE
     gb = lambda x: round(x / 1e9, 2)  # noqa: E731
+    # pinned host memory: per rank, and for the ranks of one node (up to 8 GPUs per node); the
+    # node check keeps half of the machine's RAM free for the data loader, checkpoint snapshots
+    # and the OS
+    ranks_per_node = min(world, GPUS_PER_NODE)
+    host_node = state["host_pinned"] * ranks_per_node
+    ram = host_ram_gb * 1e9 if host_ram_gb is not None else host_ram_bytes()
+    host_fits = bool(host_node == 0 or (ram is not None and host_node <= 0.5 * ram))
     return {
         "layout": {"world": world, "tp": tp, "ep": ep, "cp": cp, "pp": pp, "dp": world // (tp * cp * pp),
                    "micro_batch": micro_batch, "seq_len": seq_len, "remat": remat, "stage": stage},
         "params_replicated": state["replicated_params"], "params_local": state["local_params"],
         "state_gb": {k: gb(state[k]) for k in ("master", "grad", "compute", "optimizer")},
         "state_total_gb": gb(state_total), "activations_gb_est": gb(act), "reserve_gb": gb(CONTEXT_RESERVE),
-        "total_gb": gb(total), "hbm_gb": gb(HBM_BYTES), "fits": bool(total <= HBM_BYTES),
+        "total_gb": gb(total), "hbm_gb": gb(HBM_BYTES),
+        "host_pinned_gb_per_rank": gb(state["host_pinned"]), "host_pinned_gb_per_node": gb(host_node),
+        "host_ram_gb": gb(ram) if ram is not None else None, "host_fits": host_fits,
+        "fits": bool(total <= HBM_BYTES and host_fits),
     }
 
 
@@ -138,6 +165,8 @@ def main(argv: Optional[list] = None) -> Dict:
     ap.add_argument("--local-grad-bytes", type=int, default=4, help="gradient bytes of rank-local parameters")
     ap.add_argument("--offload-local-moments", action="store_true", default=None,
                     help="AdamW moments of rank-local parameters in host memory")
+    ap.add_argument("--host-ram-gb", type=float, default=None,
+                    help="host memory of one node for the pinned-moment check (default: this machine's)")
     a = ap.parse_args(argv)
     train: Dict = {}
     if a.config:
@@ -160,7 +189,8 @@ def main(argv: Optional[list] = None) -> Dict:
                remat=bool(a.remat if a.remat is not None else train.get("remat", False)),
                local_grad_bytes=a.local_grad_bytes,
                local_moments_on_host=bool(a.offload_local_moments if a.offload_local_moments is not None
-                                          else train.get("offload_local_moments", False)))
+                                          else train.get("offload_local_moments", False)),
+               host_ram_gb=a.host_ram_gb)
     print(json.dumps(out))
     return out
 

@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override num_layers (debug only; invalid for the bench)")
     ap.add_argument("--optimizer", default="adamw", choices=["adamw", "hybrid"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-scan-ops", action="store_true",
+                    help="skip the scan-operator figures measured after the timed region")
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA-graph capture of the micro-step")
     ap.add_argument("--ep", type=int, default=1,
                     help="expert-parallel ranks (1 or the number of GPUs): routed experts split over the GPUs")
@@ -231,12 +233,15 @@ def main():
     sampler.start()
     launch_counter.reset()
     launch_counter.enable()
+    trainer.phase_events = {} if args.impl == "cuda" else None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
         out = trainer.train_step(batches_dev())
     ev1.record()
     torch.cuda.synchronize()
+    phases = step_phases(trainer.phase_events, args.steps, world)
+    trainer.phase_events = None
     launches = launch_counter.count
     if trainer.cuda_graph:  # kernels inside the replayed micro-step graph
         launches += trainer.graph_kernel_launches * n_micro * args.steps
@@ -279,6 +284,9 @@ def main():
                "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": 4,
                "loss": float(out["loss"].item())}
 
+    scan = None
+    if args.impl == "cuda" and not args.no_scan_ops and rank == 0:
+        scan = scan_ops(dev)
     if rank == 0:
         line = {
             "metric": "train tokens/sec (box, max over ranks)",
@@ -302,9 +310,54 @@ def main():
                        "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1) if dev.type == "cuda" else None,
                        "l2": "inputs larger than L2 (11+ GB of weights streamed per micro-step)"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
+            "phases_ms": phases,
         }
+        if scan is not None:
+            line["scan_ops"] = scan
         print(json.dumps(line), flush=True)
     shutdown(trainer, world)
+
+
+def step_phases(events, steps: int, world: int):
+    """Per-step device time of the training step's phases over the timed steps, max over
+    ranks: the micro-steps (forward, backward, accumulation), the barrier before the optimizer,
+    the optimizer (with the NVLink peer-memory reduce-scatter fused into its first pass and the
+    all-gather into its update), and the barrier after it."""
+    if not events or len(events.get("micro", [])) != steps:
+        return None
+    spans = {"micro_steps": ("micro", "apply"), "begin_barrier": ("apply", "optimizer"),
+             "optimizer_fused_comm": ("optimizer", "end_barrier"), "end_barrier": ("end_barrier", "done")}
+    vals = []
+    for a, b in spans.values():
+        vals.append(sum(x.elapsed_time(y) for x, y in zip(events[a], events[b])) / steps)
+    t = torch.tensor(vals, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {k: round(float(v), 3) for k, v in zip(spans, t.tolist())}
+
+
+def scan_ops(dev):
+    """The scan operators at the benchmark's operator configuration (GDN-2 B 8, T 4096, H 16,
+    D 128; Mamba2 SSD B 8, T 4096, H 32, P 64, N 128), forward + backward, bf16, CUDA events with
+    an L2 flush between iterations; TFLOP/s of the chunked algorithm's matmul FLOPs and the
+    fraction of the HBM roofline (minimum input / output bytes over the measured copy bandwidth)."""
+    from atomic_ai_hybrid_b200.utils import opbench
+    peaks = {}
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    out = {}
+    for name, fn, H in (("gdn2", opbench.bench_gdn, 16), ("ssd", opbench.bench_ssd, 32)):
+        r = fn(8, 4096, H, 2, 5, flush)
+        out[name] = {"ms": round(r["ms"], 3), "tflops": round(r["tflops"], 1),
+                     "hbm_roofline_fraction": round(r["min_io_gb_s"] / hbm, 3), "shape": f"B8 T4096 H{H}"}
+    del flush
+    torch.cuda.empty_cache()
+    return out
 
 
 def shutdown(trainer, world: int, deadline_s: float = 120.0) -> None:

@@ -61,15 +61,37 @@ def test_benchmark_config_plans():
 
 
 def test_run_files_for_eight_gpus():
-    """The 8-GPU run files fit as written (configuration 5 with its rank-local AdamW
-    moments in host memory; without that it does not: ``test_benchmark_config_plans``)."""
+    """The 8-GPU run files fit as written on a node with 2 TB of host memory (configuration 5
+    with its rank-local AdamW moments in pinned host memory, 82 GB per rank and 657 GB per
+    node; without that it does not: ``test_benchmark_config_plans``); on a 512 GB node
+    configuration 5's moments do not fit."""
     import os
     root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "atomic_ai_hybrid_b200",
                         "configs")
     for name, fits in (("config3_hybrid_1b.yaml", True), ("config4_hybrid_7b_ep8.yaml", True),
                        ("config5_hybrid_long_tp8.yaml", True)):
-        out = memplan.main(["--config", os.path.join(root, name), "--world", "8"])
+        out = memplan.main(["--config", os.path.join(root, name), "--world", "8", "--host-ram-gb", "2048"])
         assert out["fits"] is fits, (name, out)
+    c5 = memplan.main(["--config", os.path.join(root, "config5_hybrid_long_tp8.yaml"), "--world", "8",
+                       "--host-ram-gb", "512"])
+    assert not c5["fits"] and not c5["host_fits"] and c5["total_gb"] <= c5["hbm_gb"]
+    assert abs(c5["host_pinned_gb_per_rank"] - 82.1) < 1.0
+    assert abs(c5["host_pinned_gb_per_node"] - 8 * c5["host_pinned_gb_per_rank"]) < 0.1
+
+
+def test_host_pinned_accounting():
+    """Moments kept on the device count 8 bytes per rank-local parameter in HBM and none on
+    the host; staged ones move exactly those bytes to the host figures."""
+    cfg = get_preset("hybrid_1b")
+    kw = dict(world=2, ep=2, micro_batch=1, seq_len=256)
+    dev = memplan.plan(cfg, **kw)
+    host = memplan.plan(cfg, local_moments_on_host=True, host_ram_gb=1e4, **kw)
+    assert dev["host_pinned_gb_per_rank"] == 0 and dev["host_fits"]
+    moved = dev["state_gb"]["optimizer"] - host["state_gb"]["optimizer"]
+    assert moved > 1.0 and abs(moved - host["host_pinned_gb_per_rank"]) < 0.02
+    assert abs(host["host_pinned_gb_per_node"] - 2 * host["host_pinned_gb_per_rank"]) < 0.02
+    tight = memplan.plan(cfg, local_moments_on_host=True, host_ram_gb=host["host_pinned_gb_per_node"], **kw)
+    assert not tight["host_fits"] and not tight["fits"]
 
 
 def test_offloaded_moments_train_like_device_moments(tmp_path):

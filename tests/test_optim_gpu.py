@@ -37,3 +37,49 @@ def test_fused_step_matches_eager(labeler):
             torch.testing.assert_close(stores[1].compute_view(s1).float(), stores[0].compute_view(s0).float(),
                                        rtol=1e-2, atol=1e-3)
     assert not bool(info["is_finite"])
+
+
+def test_offloaded_moments_on_cuda(tmp_path):
+    """``offload_moments`` with the store on the GPU: the moments live in pinned host memory,
+    three steps give bit-identical parameters and moments to device moments on the same
+    (eager) update path and match the fused kernel's step, and the host moments survive a
+    checkpoint round trip."""
+    from atomic_ai_hybrid_b200.ckpt.manager import CheckpointManager
+    cfg = get_preset("reference_tiny", d_model=256, n_heads=2, d_ff=256, num_experts=5)
+    dev = torch.device("cuda", 0)
+    runs = {}
+    for name, offload, impl in (("device_eager", False, "eager"), ("offload", True, "cuda"),
+                                ("device_fused", False, "cuda")):
+        torch.manual_seed(0)
+        m = HybridMoEModel(cfg, compute_dtype=torch.bfloat16).to(dev)
+        st = FlatParamStore(m, label_adamw_only, grad_scale_of, compute_dtype=torch.bfloat16, device=dev)
+        opt = HybridOptimizer(st, total_steps=100, offload_moments=offload)
+        opt.schedule.warmup = 1
+        if offload:
+            assert opt.m.device.type == "cpu" and opt.v.device.type == "cpu"
+            assert opt.m.is_pinned() and opt.v.is_pinned()
+            assert not opt.uses_kernels()
+        g = torch.Generator(device=dev).manual_seed(1)
+        for _ in range(3):
+            st.grad.copy_(torch.randn(st.grad.shape, device=dev, generator=g) * 0.01)
+            with ops.impl(impl):
+                opt.step(1)
+        torch.cuda.synchronize()
+        runs[name] = (st, opt)
+    (s0, o0), (s1, o1), (s2, o2) = runs["device_eager"], runs["offload"], runs["device_fused"]
+    assert torch.equal(s1.master, s0.master)
+    assert torch.equal(o1.m, o0.m.cpu()) and torch.equal(o1.v, o0.v.cpu())
+    torch.testing.assert_close(s1.master, s2.master, rtol=2e-5, atol=2e-6)
+    torch.testing.assert_close(o1.m, o2.m.cpu(), rtol=2e-5, atol=1e-9)
+
+    class _T:  # the two attributes a checkpoint reads
+        pass
+    t = _T()
+    t.store, t.opt = s1, o1
+    CheckpointManager(str(tmp_path), "latest").save(3, t, asynchronous=False)
+    m_ref, v_ref = o1.m.clone(), o1.v.clone()
+    o1.m.zero_()
+    o1.v.zero_()
+    CheckpointManager(str(tmp_path), "latest").restore(3, t)
+    assert torch.equal(o1.m, m_ref) and torch.equal(o1.v, v_ref)
+    assert o1.m.device.type == "cpu" and o1.m.is_pinned() and o1.v.is_pinned()
