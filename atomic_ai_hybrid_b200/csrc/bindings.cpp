@@ -6,6 +6,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "launchers.h"
+#include <cstdlib>
 
 namespace {
 
@@ -169,6 +170,18 @@ void check_rc(int rc, const char* what) {
   check_launch(what);
 }
 
+// A (B,H,R,C) fp32 state argument: checked and made contiguous, or undefined when absent.
+static torch::Tensor state_arg(const c10::optional<torch::Tensor>& t, const torch::Tensor& like, int64_t B, int64_t H,
+                               int64_t R, int64_t Cc, const char* what) {
+  if (!t.has_value() || !t->defined()) return torch::Tensor();
+  TORCH_CHECK(t->is_cuda() && t->device() == like.device() && t->dim() == 4 && t->size(0) == B && t->size(1) == H &&
+                  t->size(2) == R && t->size(3) == Cc,
+              what, ": expected a (", B, ",", H, ",", R, ",", Cc, ") CUDA tensor");
+  return t->to(at::kFloat).contiguous();
+}
+
+static float* fptr(const torch::Tensor& t) { return t.defined() ? t.data_ptr<float>() : nullptr; }
+
 // Chunk intermediates of the forward: tile images wt, u, qg, kg (B,H,NC,64,128) and aqk
 // (B,H,NC,64,64) bf16, gcl (B,H,NC,128) fp32, and the tile image of A (B,H,NC,64,64) bf16 when `want_a`.
 struct GdnChunk { torch::Tensor wt, u, qg, kg, aqk, gcl, A; };
@@ -195,16 +208,18 @@ GdnChunk gdn_chunk(const torch::Tensor& q, const torch::Tensor& k, const torch::
 }
 
 std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                   torch::Tensor bg, torch::Tensor wg, double scale, bool want_state) {
+                                   torch::Tensor bg, torch::Tensor wg, double scale, bool want_state,
+                                   c10::optional<torch::Tensor> h0) {
   for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
   check_gdn(g, at::kFloat, "g");
   auto s = gdn_shapes(q);
+  auto h0c = state_arg(h0, q, s.B, s.H, 128, 128, "gdn2 h0");
   auto c = gdn_chunk(q, k, v, g, bg, wg, (float)scale, false);
   auto o = torch::empty_like(q);
   torch::Tensor hf;
   if (want_state) hf = torch::empty({s.B, s.H, 128, 128}, q.options().dtype(at::kFloat));
   check_rc(ahb_gdn_state_fwd_tc(c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(), c.kg.data_ptr(), c.aqk.data_ptr(),
-                                c.gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, nullptr, o.data_ptr(),
+                                c.gcl.data_ptr<float>(), (float)scale, s.B, s.L, s.H, fptr(h0c), o.data_ptr(),
                                 want_state ? hf.data_ptr<float>() : nullptr, nullptr, nullptr,
                                 err_word().data_ptr<int>(), cur_stream()),
            "ahb_gdn_state_fwd_tc");
@@ -213,20 +228,25 @@ std::vector<torch::Tensor> gdn_fwd(torch::Tensor q, torch::Tensor k, torch::Tens
 }
 
 // Backward from the chunk intermediates of the forward (wt, qg, kg, aqk, gcl, A and the
-// per-chunk states hs / vn): reverse state recurrence, then the chunk-local backward.
+// per-chunk states hs / vn): reverse state recurrence (from the gradient of the final state
+// when given; it returns the gradient of the initial state when `want_dh0`), then the
+// chunk-local backward.
 static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                                                const torch::Tensor& g, const torch::Tensor& bg,
                                                const torch::Tensor& wg, const torch::Tensor& doc, float sc,
                                                torch::Tensor wt, torch::Tensor qg, torch::Tensor kg,
                                                torch::Tensor aqk, const torch::Tensor& gcl,
-                                               const torch::Tensor& A, torch::Tensor hs, torch::Tensor vn) {
+                                               const torch::Tensor& A, torch::Tensor hs, torch::Tensor vn,
+                                               const torch::Tensor& dhf, bool want_dh0) {
   auto s = gdn_shapes(q);
   auto st = cur_stream();
   auto dhs = torch::empty_like(hs);
   auto dvn = torch::empty({s.B, s.H, s.NC, 64, 128}, q.options());
+  torch::Tensor dh0;
+  if (want_dh0) dh0 = torch::empty({s.B, s.H, 128, 128}, q.options().dtype(at::kFloat));
   check_rc(ahb_gdn_state_bwd_tc(wt.data_ptr(), qg.data_ptr(), kg.data_ptr(), aqk.data_ptr(), gcl.data_ptr<float>(),
-                                doc.data_ptr(), sc, s.B, s.L, s.H, nullptr, dhs.data_ptr(), dvn.data_ptr(), nullptr,
-                                err_word().data_ptr<int>(), st),
+                                doc.data_ptr(), sc, s.B, s.L, s.H, fptr(dhf), dhs.data_ptr(), dvn.data_ptr(),
+                                fptr(dh0), err_word().data_ptr<int>(), st),
            "ahb_gdn_state_bwd_tc");
   qg = torch::Tensor(); kg = torch::Tensor(); wt = torch::Tensor(); aqk = torch::Tensor();
   auto dq = torch::empty_like(q), dk = torch::empty_like(q), dv = torch::empty_like(q), db = torch::empty_like(q),
@@ -238,52 +258,72 @@ static std::vector<torch::Tensor> gdn_bwd_core(const torch::Tensor& q, const tor
                                 dv.data_ptr(), db.data_ptr(), dw.data_ptr(), dg.data_ptr<float>(),
                                 err_word().data_ptr<int>(), st),
            "ahb_gdn_chunk_bwd_tc");
+  if (want_dh0) return {dq, dk, dv, dg, db, dw, dh0};
   return {dq, dk, dv, dg, db, dw};
 }
 
 static void gdn_states(const GdnChunk& c, const torch::Tensor& q, float sc, torch::Tensor* o, torch::Tensor& hs,
-                       torch::Tensor& vn) {
+                       torch::Tensor& vn, const torch::Tensor& h0 = torch::Tensor(),
+                       torch::Tensor* hf = nullptr) {
   auto s = gdn_shapes(q);
   hs = torch::empty({s.B, s.H, s.NC, 128, 128}, q.options());
   vn = torch::empty({s.B, s.H, s.NC, 64, 128}, q.options());
+  if (hf) *hf = torch::empty({s.B, s.H, 128, 128}, q.options().dtype(at::kFloat));
   check_rc(ahb_gdn_state_fwd_tc(c.wt.data_ptr(), c.u.data_ptr(), c.qg.data_ptr(), c.kg.data_ptr(), c.aqk.data_ptr(),
-                                c.gcl.data_ptr<float>(), sc, s.B, s.L, s.H, nullptr, o ? o->data_ptr() : nullptr,
-                                nullptr, hs.data_ptr(), vn.data_ptr(), err_word().data_ptr<int>(), cur_stream()),
+                                c.gcl.data_ptr<float>(), sc, s.B, s.L, s.H, fptr(h0), o ? o->data_ptr() : nullptr,
+                                hf ? hf->data_ptr<float>() : nullptr, hs.data_ptr(), vn.data_ptr(),
+                                err_word().data_ptr<int>(), cur_stream()),
            "ahb_gdn_state_fwd_tc");
 }
 
 // Forward for training: also returns the chunk intermediates the backward needs
-// {o, wt, qg, kg, aqk, gcl, A, hs, vn}, so nothing is recomputed there.
+// {o, wt, qg, kg, aqk, gcl, A, hs, vn}, so nothing is recomputed there; the recurrence starts
+// from `h0` (B,H,128,128) when given, and `want_final` appends the final state (fp32).
 std::vector<torch::Tensor> gdn_fwd_train(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                         torch::Tensor bg, torch::Tensor wg, double scale) {
+                                         torch::Tensor bg, torch::Tensor wg, double scale,
+                                         c10::optional<torch::Tensor> h0, bool want_final) {
   for (auto* t : {&q, &k, &v, &bg, &wg}) check_gdn(*t, at::kBFloat16, "q/k/v/b/w");
   check_gdn(g, at::kFloat, "g");
+  auto s = gdn_shapes(q);
+  auto h0c = state_arg(h0, q, s.B, s.H, 128, 128, "gdn2 h0");
   auto c = gdn_chunk(q, k, v, g, bg, wg, (float)scale, true);
   auto o = torch::empty_like(q);
-  torch::Tensor hs, vn;
-  gdn_states(c, q, (float)scale, &o, hs, vn);
+  torch::Tensor hs, vn, hf;
+  gdn_states(c, q, (float)scale, &o, hs, vn, h0c, want_final ? &hf : nullptr);
+  if (want_final) return {o, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn, hf};
   return {o, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn};
 }
 
+// `dh_final`: gradient of the final state (or none); `want_dh0` appends the gradient of the
+// initial state to {dq, dk, dv, dg, db, dw}.
 std::vector<torch::Tensor> gdn_bwd_saved(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
                                          torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale,
-                                         std::vector<torch::Tensor> saved) {
+                                         std::vector<torch::Tensor> saved, c10::optional<torch::Tensor> dh_final,
+                                         bool want_dh0) {
   TORCH_CHECK(saved.size() == 8, "gdn_bwd_saved: expects {wt, qg, kg, aqk, gcl, A, hs, vn}");
+  auto s = gdn_shapes(q);
   auto doc = dout.to(at::kBFloat16).contiguous();
+  auto dhf = state_arg(dh_final, q, s.B, s.H, 128, 128, "gdn2 dh_final");
   return gdn_bwd_core(q, k, v, g, bg, wg, doc, (float)scale, saved[0], saved[1], saved[2], saved[3], saved[4],
-                      saved[5], saved[6], saved[7]);
+                      saved[5], saved[6], saved[7], dhf, want_dh0);
 }
 
-// Backward that recomputes the forward's chunk intermediates (memory-lean path).
+// Backward that recomputes the forward's chunk intermediates (memory-lean path); `h0` is the
+// forward's initial state.
 std::vector<torch::Tensor> gdn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
-                                   torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale) {
+                                   torch::Tensor bg, torch::Tensor wg, torch::Tensor dout, double scale,
+                                   c10::optional<torch::Tensor> h0, c10::optional<torch::Tensor> dh_final,
+                                   bool want_dh0) {
+  auto s = gdn_shapes(q);
   auto doc = dout.to(at::kBFloat16).contiguous();
   const float sc = (float)scale;
+  auto h0c = state_arg(h0, q, s.B, s.H, 128, 128, "gdn2 h0");
+  auto dhf = state_arg(dh_final, q, s.B, s.H, 128, 128, "gdn2 dh_final");
   auto c = gdn_chunk(q, k, v, g, bg, wg, sc, true);
   torch::Tensor hs, vn;
-  gdn_states(c, q, sc, nullptr, hs, vn);
+  gdn_states(c, q, sc, nullptr, hs, vn, h0c);
   c.u = torch::Tensor();
-  return gdn_bwd_core(q, k, v, g, bg, wg, doc, sc, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn);
+  return gdn_bwd_core(q, k, v, g, bg, wg, doc, sc, c.wt, c.qg, c.kg, c.aqk, c.gcl, c.A, hs, vn, dhf, want_dh0);
 }
 
 // ------------------------------------------------------------ Mamba2 SSD
@@ -300,15 +340,18 @@ void check_ssd(const torch::Tensor& x, const torch::Tensor& dt, const torch::Ten
               "ssd: B, C must be (B,L,128)");
 }
 
-struct SsdFwd { torch::Tensor y, sin_t, dec_t, cl, yd_t; };
+struct SsdFwd { torch::Tensor y, sin_t, dec_t, cl, yd_t, s_final; };
 
-// Forward (chunk kernel + state recurrence); with `keep_states` also the per-chunk incoming
-// states (tile images) the backward needs, beside the decay images and last cumsums.
+// Forward (chunk kernel + state recurrence, from the initial state `s0` (B,H,64,128) when
+// defined); with `keep_states` also the per-chunk incoming states (tile images) the backward
+// needs, beside the decay images and last cumsums; `want_final` keeps the final state (fp32).
 static SsdFwd ssd_forward(const torch::Tensor& x, const torch::Tensor& dt, const torch::Tensor& A,
-                          const torch::Tensor& Bm, const torch::Tensor& Cm, bool keep_states, bool want_y) {
+                          const torch::Tensor& Bm, const torch::Tensor& Cm, bool keep_states, bool want_y,
+                          const torch::Tensor& s0 = torch::Tensor(), bool want_final = false) {
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
   auto bf = x.options();
   SsdFwd f;
+  if (want_final) f.s_final = torch::empty({B, H, 64, 128}, x.options().dtype(at::kFloat));
   auto send = torch::empty({B, H, NC, 128, 64}, bf);
   f.yd_t = torch::empty({B, H, NC, 64, 64}, x.options().dtype(at::kFloat));
   f.dec_t = torch::empty({B, H, NC, 64, 64}, bf);
@@ -316,7 +359,8 @@ static SsdFwd ssd_forward(const torch::Tensor& x, const torch::Tensor& dt, const
   if (keep_states) f.sin_t = torch::empty({B, H, NC, 128, 64}, bf);
   f.y = torch::empty_like(x);
   check_rc(ahb_ssd_fwd_tc(x.data_ptr(), dt.data_ptr(), A.data_ptr<float>(), Bm.data_ptr(), Cm.data_ptr(), B, L, H,
-                          send.data_ptr(), f.yd_t.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), nullptr, nullptr,
+                          send.data_ptr(), f.yd_t.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), fptr(s0),
+                          fptr(f.s_final),
                           f.y.data_ptr(), keep_states ? f.sin_t.data_ptr() : nullptr, err_word().data_ptr<int>(),
                           cur_stream()),
            "ahb_ssd_fwd_tc");
@@ -330,20 +374,29 @@ torch::Tensor ssd_fwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch:
 }
 
 // Forward for training: {y, incoming states (tile images), decay images, last cumsums, intra-chunk
-// outputs}; ssd_bwd takes the last four back.
+// outputs}; ssd_bwd takes the last four back.  The recurrence starts from `s0` (B,H,64,128)
+// when given; `want_final` appends the final state (fp32).
 std::vector<torch::Tensor> ssd_fwd_train(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
-                                         torch::Tensor Cm) {
+                                         torch::Tensor Cm, c10::optional<torch::Tensor> s0, bool want_final) {
   check_ssd(x, dt, A, Bm, Cm);
-  auto f = ssd_forward(x, dt, A, Bm, Cm, true, true);
+  auto s0c = state_arg(s0, x, x.size(0), x.size(2), 64, 128, "ssd s0");
+  auto f = ssd_forward(x, dt, A, Bm, Cm, true, true, s0c, want_final);
+  if (want_final) return {f.y, f.sin_t, f.dec_t, f.cl, f.yd_t, f.s_final};
   return {f.y, f.sin_t, f.dec_t, f.cl, f.yd_t};
 }
 
+// {dx, ddt, dA, dB, dC} (+ the gradient of the initial state with `want_ds0`); `s0` is the
+// forward's initial state (used when the saved states are absent and the forward reruns),
+// `ds_final` the gradient of its final state.
 std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Tensor A, torch::Tensor Bm,
                                    torch::Tensor Cm, torch::Tensor dy, c10::optional<torch::Tensor> states,
                                    c10::optional<torch::Tensor> decays, c10::optional<torch::Tensor> cumsums,
-                                   c10::optional<torch::Tensor> ydiag) {
+                                   c10::optional<torch::Tensor> ydiag, c10::optional<torch::Tensor> s0,
+                                   c10::optional<torch::Tensor> ds_final, bool want_ds0) {
   check_ssd(x, dt, A, Bm, Cm);
   int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), NC = L / 64;
+  auto s0c = state_arg(s0, x, B, H, 64, 128, "ssd s0");
+  auto dsf = state_arg(ds_final, x, B, H, 64, 128, "ssd ds_final");
   auto dyc = dy.to(at::kBFloat16).contiguous();
   auto f32 = x.options().dtype(at::kFloat);
   const bool ready = states.has_value() && states->defined() && decays.has_value() && decays->defined() &&
@@ -359,12 +412,14 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
                     f.cl.numel() == (int64_t)B * H * NC * 64,
                 "ssd_bwd: saved states do not match");
   } else {
-    f = ssd_forward(x, dt, A, Bm, Cm, true, false);
+    f = ssd_forward(x, dt, A, Bm, Cm, true, false, s0c);
   }
   auto st = cur_stream();
   auto dse = torch::empty({B, H, NC, 128, 64}, x.options());
+  torch::Tensor ds0;
+  if (want_ds0) ds0 = torch::empty({B, H, 64, 128}, f32);
   check_rc(ahb_ssd_state_bwd_tc(Cm.data_ptr(), dyc.data_ptr(), f.dec_t.data_ptr(), f.cl.data_ptr<float>(), B, L, H,
-                                nullptr, dse.data_ptr(), nullptr, err_word().data_ptr<int>(), st),
+                                fptr(dsf), dse.data_ptr(), fptr(ds0), err_word().data_ptr<int>(), st),
            "ahb_ssd_state_bwd_tc");
   auto dx = torch::empty_like(x), ddt = torch::empty_like(x);
   auto dB = torch::empty(Bm.sizes(), f32), dC = torch::empty(Cm.sizes(), f32);
@@ -377,6 +432,7 @@ std::vector<torch::Tensor> ssd_bwd(torch::Tensor x, torch::Tensor dt, torch::Ten
                                 dA.data_ptr<float>(), dBp.data_ptr<float>(), dCp.data_ptr<float>(),
                                 err_word().data_ptr<int>(), st),
            "ahb_ssd_bwd_chunk_tc");
+  if (want_ds0) return {dx, ddt, dA, dB, dC, ds0};
   return {dx, ddt, dA, dB, dC};
 }
 
@@ -400,26 +456,43 @@ void gemm_error_reset() { err_word().zero_(); }
 
 void gemm_check(int rc, const char* what) { TORCH_CHECK(rc == 0, "moe_gemm (", what, ") setup failed: code ", rc); }
 
-// Generic access for tests: C = A B^T (A: M x K, B: N x K, bf16, K-major), single group
-torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b) {
+// Generic access for tests: C = A B^T (A: M x K, B: N x K, bf16, K-major), single group; `pair` runs
+// the CTA-pair kernel (256 x 256 tiles; rows of the last tile beyond M are read as zeros and not
+// stored).
+torch::Tensor gemm_dense(torch::Tensor a, torch::Tensor b, bool pair) {
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.is_contiguous() && b.is_contiguous() &&
               b.scalar_type() == at::kBFloat16, "gemm_dense: bf16 contiguous");
   int64_t M = a.size(0), K = a.size(1), N = b.size(0);
-  TORCH_CHECK(M % 128 == 0 && K % 64 == 0 && N % 256 == 0, "gemm_dense: M%128, K%64, N%256");
-  auto off = torch::arange(0, M + 1, M, torch::dtype(torch::kInt32).device(a.device()));
+  TORCH_CHECK(K % 64 == 0 && N % 32 == 0 && (pair || M % 128 == 0), "gemm_dense: K%64, N%32, M%128 (single CTA)");
+  const int64_t Mp = pair ? (M + 255) / 256 * 256 : M;
+  auto off = torch::arange(0, Mp + 1, Mp, torch::dtype(torch::kInt32).device(a.device()));
   auto c = torch::empty({M, N}, a.options());
-  int rc = ahb_moe_gemm(AHB_GEMM_DENSE, a.data_ptr(), nullptr, M, K, b.data_ptr(), nullptr, N, K, 0,
-                        off.data_ptr<int>(), 1, (int)N, 0, (int)K, (int)(K / 64), c.data_ptr(), nullptr, nullptr,
-                        nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream());
+  int rc = ahb_moe_gemm(AHB_GEMM_DENSE | (pair ? AHB_GEMM_PAIR : 0), a.data_ptr(), nullptr, M, K, b.data_ptr(),
+                        nullptr, N, K, 0, off.data_ptr<int>(), 1, (int)N, 0, (int)K, (int)(K / 64), c.data_ptr(),
+                        nullptr, nullptr, nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream(),
+                        nullptr, pair ? (int)M : 0);
   gemm_check(rc, "dense");
   return c;
 }
 
-// Expert FFN on expert-grouped rows (segments of `off`, padded to 128 rows):
-// returns {a1, a3 (empty for GELU), h, ys}.
+// CTA-pair grouped GEMMs (256 x 256 tiles over two SMs) for the local MoE layer, whose routing
+// then pads each expert's segment to 256 rows; AHB_MOE_PAIR=0 keeps the single-CTA kernel and
+// 128-row segments.  Fixed for the process, so a forward and its backward agree.
+static bool moe_pair() {
+  static const bool on = [] {
+    const char* e = std::getenv("AHB_MOE_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Expert FFN on expert-grouped rows (segments of `off`, padded to 128 rows, or to 256 with
+// `pair`, which runs the M-grouped GEMMs on CTA pairs): returns {a1, a3 (empty for GELU), h, ys}.
 static std::vector<torch::Tensor> moe_expert_fwd_impl(const torch::Tensor& xs, const torch::Tensor& off, int64_t R,
                                                       const torch::Tensor& w1, const torch::Tensor& w2,
-                                                      const c10::optional<torch::Tensor>& w3, bool swiglu) {
+                                                      const c10::optional<torch::Tensor>& w3, bool swiglu,
+                                                      bool pair = false) {
+  const int PM = pair ? AHB_GEMM_PAIR : 0;
   const int d = (int)xs.size(1), E = (int)w1.size(0), F = (int)w1.size(2);
   TORCH_CHECK(d % 256 == 0 && F % 256 == 0, "moe: d_model and d_ff must be multiples of 256");
   TORCH_CHECK(E <= 192, "moe: at most 192 experts per call");
@@ -432,18 +505,18 @@ static std::vector<torch::Tensor> moe_expert_fwd_impl(const torch::Tensor& xs, c
   if (swiglu) {
     TORCH_CHECK(w3.has_value(), "moe: swiglu needs w3");
     a3 = torch::empty_like(h);
-    rc = ahb_moe_gemm(AHB_GEMM_FWD_SWIGLU, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), w3->data_ptr(),
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_SWIGLU | PM, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), w3->data_ptr(),
                       (int64_t)E * d, F, d, off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(),
                       a3.data_ptr(), nullptr, nullptr, 1e3f, err, num_sms(), st);
   } else {
-    rc = ahb_moe_gemm(AHB_GEMM_FWD_GELU, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_GELU | PM, xs.data_ptr(), nullptr, R, d, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
                       off.data_ptr<int>(), E, F, 0, d, d / 64, h.data_ptr(), a1.data_ptr(), nullptr, nullptr, nullptr,
                       1e3f, err, num_sms(), st);
     a3 = torch::empty({0}, xs.options());
   }
   gemm_check(rc, "fwd up");
   auto ys = torch::empty({R, d}, xs.options());
-  rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, h.data_ptr(), nullptr, R, F, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+  rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN | PM, h.data_ptr(), nullptr, R, F, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
                     off.data_ptr<int>(), E, d, 0, F, F / 64, ys.data_ptr(), nullptr, nullptr, nullptr, nullptr, 1e3f,
                     err, num_sms(), st);
   gemm_check(rc, "fwd down");
@@ -451,13 +524,16 @@ static std::vector<torch::Tensor> moe_expert_fwd_impl(const torch::Tensor& xs, c
 }
 
 // Backward of the expert FFN from the row gradients dys (padding rows zero): weight
-// gradients are ADDED into dw*_acc; returns the row gradients dxs.
+// gradients are ADDED into dw*_acc; returns the row gradients dxs.  The K-grouped weight
+// gradients always run on CTA pairs (their rows are d_model / d_ff, multiples of 256); the
+// M-grouped products do with `pair` (segments padded to 256 rows).
 static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::Tensor& off, const torch::Tensor& xs,
                                          const torch::Tensor& a1, const torch::Tensor& a3, const torch::Tensor& h,
                                          const torch::Tensor& w1, const torch::Tensor& w2,
                                          const c10::optional<torch::Tensor>& w3, const torch::Tensor& dw1_acc,
                                          const torch::Tensor& dw2_acc, const c10::optional<torch::Tensor>& dw3_acc,
-                                         bool swiglu) {
+                                         bool swiglu, bool pair = false) {
+  const int PM = pair ? AHB_GEMM_PAIR : 0, PW = moe_pair() ? AHB_GEMM_PAIR : 0;
   const int64_t R = xs.size(0);
   const int d = (int)xs.size(1), E = (int)w1.size(0), F = (int)w1.size(2);
   auto st = cur_stream();
@@ -469,37 +545,37 @@ static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::
   int rc;
   if (swiglu) {
     dA3 = torch::empty_like(dA1);
-    rc = ahb_moe_gemm(AHB_GEMM_DH_SWIGLU, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d,
+    rc = ahb_moe_gemm(AHB_GEMM_DH_SWIGLU | PM, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d,
                       F, off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), dA3.data_ptr(), nullptr,
                       a1.data_ptr(), a3.data_ptr(), 0.f, err, num_sms(), st);
   } else {
-    rc = ahb_moe_gemm(AHB_GEMM_DH_GELU, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
+    rc = ahb_moe_gemm(AHB_GEMM_DH_GELU | PM, dys.data_ptr(), nullptr, R, d, w2.data_ptr(), nullptr, (int64_t)E * F, d, F,
                       off.data_ptr<int>(), E, F, 0, d, d / 64, dA1.data_ptr(), nullptr, nullptr, a1.data_ptr(),
                       nullptr, 0.f, err, num_sms(), st);
   }
   gemm_check(rc, "dh");
-  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, h.data_ptr(), nullptr, R, F, dys.data_ptr(), nullptr, R, d, 0,
+  rc = ahb_moe_gemm(AHB_GEMM_WGRAD | PW, h.data_ptr(), nullptr, R, F, dys.data_ptr(), nullptr, R, d, 0,
                     off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
                     0.f, err, num_sms(), st);
   gemm_check(rc, "wgrad w2");
   auto dxs = torch::empty({R, d}, xs.options());
   if (swiglu) {
-    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), dA3.data_ptr(), R, F, w1.data_ptr(), w3->data_ptr(),
+    rc = ahb_moe_gemm(AHB_GEMM_DX | PM, dA1.data_ptr(), dA3.data_ptr(), R, F, w1.data_ptr(), w3->data_ptr(),
                       (int64_t)E * d, F, d, off.data_ptr<int>(), E, d, 0, 2 * F, F / 64, dxs.data_ptr(), nullptr,
                       nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "dx");
     TORCH_CHECK(dw3_acc.has_value(), "moe_bwd: dw3_acc");
     check_acc(*dw3_acc, w3->numel(), "dw3_acc");
-    rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), dA3.data_ptr(), R, F, 0,
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL | PW, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), dA3.data_ptr(), R, F, 0,
                       off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), dw3_acc->data_ptr<float>(),
                       nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "wgrad w1/w3");
   } else {
-    rc = ahb_moe_gemm(AHB_GEMM_DX, dA1.data_ptr(), nullptr, R, F, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
+    rc = ahb_moe_gemm(AHB_GEMM_DX | PM, dA1.data_ptr(), nullptr, R, F, w1.data_ptr(), nullptr, (int64_t)E * d, F, d,
                       off.data_ptr<int>(), E, d, 0, F, F / 64, dxs.data_ptr(), nullptr, nullptr, nullptr, nullptr,
                       0.f, err, num_sms(), st);
     gemm_check(rc, "dx");
-    rc = ahb_moe_gemm(AHB_GEMM_WGRAD, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), nullptr, R, F, 0,
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD | PW, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), nullptr, R, F, 0,
                       off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
                       nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "wgrad w1");
@@ -522,17 +598,19 @@ std::vector<torch::Tensor> moe_fwd(torch::Tensor x, torch::Tensor top_idx, torch
   auto i32 = torch::dtype(torch::kInt32).device(dev);
   auto eidx = top_idx.t().contiguous().to(torch::kInt32);
   auto gatec = gate.to(at::kFloat).contiguous();
-  const int64_t Rcap = ((int64_t)T * k + (int64_t)E * 128 + 127) / 128 * 128;
+  const bool pair = moe_pair();
+  const int pad = pair ? 256 : 128;
+  const int64_t Rcap = ((int64_t)T * k + (int64_t)E * pad + pad - 1) / pad * pad;
   auto counts = torch::empty({E}, i32), off = torch::empty({E + 1}, i32);
   auto pos = torch::empty({(int64_t)T * k}, i32), row_src = torch::empty({Rcap}, i32);
   auto st = cur_stream();
   ahb_moe_route(eidx.data_ptr<int>(), T, k, E, counts.data_ptr<int>(), off.data_ptr<int>(), pos.data_ptr<int>(),
-                row_src.data_ptr<int>(), Rcap, st);
+                row_src.data_ptr<int>(), Rcap, st, pad);
   check_launch("ahb_moe_route");
   auto xs = torch::empty({Rcap, d}, x.options());
   ahb_moe_gather(x.data_ptr(), row_src.data_ptr<int>(), Rcap, d, xs.data_ptr(), st);
   check_launch("ahb_moe_gather");
-  auto g = moe_expert_fwd_impl(xs, off, Rcap, w1, w2, w3, swiglu);
+  auto g = moe_expert_fwd_impl(xs, off, Rcap, w1, w2, w3, swiglu, pair);
   auto a1 = g[0], a3 = g[1], h = g[2], ys = g[3];
   auto out = torch::empty_like(x);
   const void* sh = nullptr;
@@ -564,7 +642,7 @@ std::vector<torch::Tensor> moe_bwd(torch::Tensor dout, torch::Tensor gate, torch
   ahb_moe_combine_bwd(doc.data_ptr(), ys.data_ptr(), pos.data_ptr<int>(), gatec.data_ptr<float>(), T, k, d,
                       dys.data_ptr(), dgate.data_ptr<float>(), st);
   check_launch("ahb_moe_combine_bwd");
-  auto dxs = moe_expert_bwd_impl(dys, off, xs, a1, a3, h, w1, w2, w3, dw1_acc, dw2_acc, dw3_acc, swiglu);
+  auto dxs = moe_expert_bwd_impl(dys, off, xs, a1, a3, h, w1, w2, w3, dw1_acc, dw2_acc, dw3_acc, swiglu, moe_pair());
   auto dx = torch::empty({T, d}, xs.options());
   ahb_moe_scatter_add(dxs.data_ptr(), pos.data_ptr<int>(), T, k, d, dx.data_ptr(), st);
   check_launch("ahb_moe_scatter_add");
@@ -1246,16 +1324,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("accumulate_", &accumulate_);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd_", &embedding_bwd_);
-  m.def("gdn_fwd", &gdn_fwd);
-  m.def("gdn_bwd", &gdn_bwd);
-  m.def("gdn_fwd_train", &gdn_fwd_train);
-  m.def("gdn_bwd_saved", &gdn_bwd_saved);
-  m.def("ssd_fwd_train", &ssd_fwd_train);
+  m.def("gdn_fwd", &gdn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("bg"), py::arg("wg"),
+        py::arg("scale"), py::arg("want_state"), py::arg("h0") = py::none());
+  m.def("gdn_bwd", &gdn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("bg"), py::arg("wg"),
+        py::arg("dout"), py::arg("scale"), py::arg("h0") = py::none(), py::arg("dh_final") = py::none(),
+        py::arg("want_dh0") = false);
+  m.def("gdn_fwd_train", &gdn_fwd_train, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("bg"),
+        py::arg("wg"), py::arg("scale"), py::arg("h0") = py::none(), py::arg("want_final") = false);
+  m.def("gdn_bwd_saved", &gdn_bwd_saved, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("bg"),
+        py::arg("wg"), py::arg("dout"), py::arg("scale"), py::arg("saved"), py::arg("dh_final") = py::none(),
+        py::arg("want_dh0") = false);
+  m.def("ssd_fwd_train", &ssd_fwd_train, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"),
+        py::arg("s0") = py::none(), py::arg("want_final") = false);
   m.def("ssd_fwd", &ssd_fwd);
   m.def("ssd_bwd", &ssd_bwd, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"), py::arg("dy"),
         py::arg("states") = py::none(), py::arg("decays") = py::none(), py::arg("cumsums") = py::none(),
-        py::arg("ydiag") = py::none());
-  m.def("gemm_dense", &gemm_dense);
+        py::arg("ydiag") = py::none(), py::arg("s0") = py::none(), py::arg("ds_final") = py::none(),
+        py::arg("want_ds0") = false);
+  m.def("gemm_dense", &gemm_dense, py::arg("a"), py::arg("b"), py::arg("pair") = false);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_error_reset", &gemm_error_reset);
   m.def("moe_fwd", &moe_fwd);

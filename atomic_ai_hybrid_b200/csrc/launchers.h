@@ -76,15 +76,19 @@ int ahb_ssd_bwd_chunk_tc(const void* x, const void* dt, const float* A, const vo
 #define AHB_GEMM_DX 6           // dX = dA1 W1_e^T (+ dA3 W3_e^T)
 #define AHB_GEMM_WGRAD 7        // dW_e += A_e^T B_e   (fp32 accumulate)
 #define AHB_GEMM_WGRAD_DUAL 8   // dW1_e += X_e^T dA1_e, dW3_e += X_e^T dA3_e
+// or-ed into the kind: run the CTA-pair kernel (cta_group::2, 256 x 256 tiles); M-grouped
+// group offsets must then be multiples of 256 rows, K-grouped Mout a multiple of 256
+#define AHB_GEMM_PAIR 0x100
 int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
                  const void* aux1, float clip, int* err, int num_sms, cudaStream_t st,
-                 const float* alpha = nullptr);
+                 const float* alpha = nullptr, int m_limit = 0);
 
 // moe.cu: routing positions, gather / combine (+ backward)
+// segments padded to multiples of `pad` rows (128, or 256 for the CTA-pair GEMMs)
 void ahb_moe_route(const int* eidx, int T, int k, int E, int* counts, int* off, int* pos, int* row_src, int64_t R_cap,
-                   cudaStream_t st);
+                   cudaStream_t st, int pad = 128);
 void ahb_moe_gather(const void* x, const int* row_src, int64_t R, int d, void* xs, cudaStream_t st);
 void ahb_moe_zero_pad(void* m, const int* row_src, int64_t R, int d, cudaStream_t st);
 void ahb_moe_combine(const void* ys, const int* pos, const float* gate, const void* shared, int T, int k, int d,

@@ -3,8 +3,8 @@
 // Assignments are ordered like the reference's replicated token matrix:
 // a = j*T + t for top-k choice j of token t.  Rows of the expert-sorted matrix
 // keep that order inside each expert (a stable sort by expert id), and every
-// expert's segment is padded to a multiple of 128 rows so the grouped GEMM's
-// tiles never straddle two experts; padding rows are zero.
+// expert's segment is padded to a multiple of 128 rows (256 for the CTA-pair
+// GEMMs) so the grouped GEMM's tiles never straddle two experts; padding rows are zero.
 #include "common.cuh"
 #include "launchers.h"
 
@@ -188,11 +188,11 @@ __global__ void moe_zero_pad_kernel(bf16* __restrict__ m, const int* __restrict_
 }  // namespace
 
 void ahb_moe_route(const int* eidx, int T, int k, int E, int* counts, int* off, int* pos, int* row_src, int64_t R_cap,
-                   cudaStream_t st) {
+                   cudaStream_t st, int pad) {
   const int64_t n = (int64_t)T * k;
   cudaMemsetAsync(row_src, 0xff, R_cap * sizeof(int), st);
   moe_count_kernel<<<E, 1024, 0, st>>>(eidx, n, counts);
-  moe_offsets_kernel<<<1, 32, 0, st>>>(counts, E, 128, off);
+  moe_offsets_kernel<<<1, 32, 0, st>>>(counts, E, pad, off);
   moe_positions_kernel<<<E, 1024, 0, st>>>(eidx, n, T, off, pos, row_src);
 }
 

@@ -67,6 +67,7 @@ struct Params {
   // tile m_rot on, so that the ranks start on different destinations
   void* out_tab[MAX_PEERS];
   int m_rot;
+  int m_limit;  // M-grouped: rows at or beyond it are not stored (0: every row of the padded groups)
 };
 
 AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
@@ -122,6 +123,118 @@ AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, T
     t.nkb = (off[t.e + 1] - off[t.e]) / BK;
   }
   return true;
+}
+
+// Epilogue of one accumulator tile for the 32 rows of one epilogue warp: `tb` is the warp's TMEM
+// lane quarter at the accumulator, `row_base` the tile row of its lane 0 (rows at or beyond
+// `m_limit`, when set, are not written).
+template <int EPI, int NB>
+AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, uint32_t tb, int row_base, int lane,
+                              unsigned char* stg_base, int q) {
+  constexpr int BNA = 256 / NB;
+  const int row = row_base + lane;
+  const int n0 = t.n0 * BNA;
+  const bool live = p.m_limit <= 0 || row < p.m_limit;
+  const float alpha = p.alpha ? *p.alpha : 1.f;
+  if constexpr (EPI == EPI_STORE_PEER) {
+    bf16* stg = reinterpret_cast<bf16*>(stg_base) + q * 32 * STG_LD;
+#pragma unroll 1
+    for (int c = 0; c < BNA / 32; ++c) {
+      if (n0 + c * 32 >= p.N) break;
+      float v0[32];
+      tmem_ld32(tb + c * 32, v0);
+      store_bf16x32(stg + lane * STG_LD + c * 32, v0);
+    }
+    __syncwarp();
+    // row r of the warp's 32: lanes write its 256 columns as one 512-byte segment
+    bf16* dst = static_cast<bf16*>(p.out_tab[t.e]) + static_cast<int64_t>(row_base - off[t.e]) * p.N;
+    const int col = n0 + lane * 8;
+    if (col < p.N) {
+#pragma unroll 4
+      for (int r = 0; r < 32; ++r)
+        *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r) * p.N + col) =
+            *reinterpret_cast<const uint4*>(stg + r * STG_LD + lane * 8);
+    }
+    __syncwarp();
+  }
+#pragma unroll 1
+  for (int c = 0; c < (EPI == EPI_STORE_PEER ? 0 : BNA / 32); ++c) {
+    const int col = n0 + c * 32;
+    if (col >= p.N) break;  // partial last tile (N % 32 == 0)
+    float v0[32];
+    tmem_ld32(tb + c * 32, v0);
+    const int64_t o = static_cast<int64_t>(row) * p.N + col;
+    if constexpr (EPI == EPI_STORE) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i] * alpha, p.clip);
+      store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
+    } else if constexpr (EPI == EPI_SWIGLU_FWD) {
+      float v1[32], h[32];
+      tmem_ld32(tb + BNA + c * 32, v1);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v0[i] = clampf(v0[i], p.clip);
+        v1[i] = clampf(v1[i], p.clip);
+        h[i] = v0[i] * sigmoidf_(v0[i]) * v1[i];
+      }
+      store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
+      store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
+      store_bf16x32(static_cast<bf16*>(p.out2) + o, v1);
+    } else if constexpr (EPI == EPI_GELU_FWD) {
+      float h[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v0[i] = clampf(v0[i], p.clip);
+        h[i] = gelu_t(v0[i]);
+      }
+      store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
+      store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
+    } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+      float d1[32], d3[32];
+      bf16 a1v[32], a3v[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
+        *reinterpret_cast<uint4*>(a3v + i) = *reinterpret_cast<const uint4*>(p.aux1 + o + i);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a1 = __bfloat162float(a1v[i]), a3 = __bfloat162float(a3v[i]);
+        const float s = sigmoidf_(a1);
+        d1[i] = v0[i] * a3 * s * (1.f + a1 * (1.f - s));
+        d3[i] = v0[i] * a1 * s;
+      }
+      store_bf16x32(static_cast<bf16*>(p.out0) + o, d1);
+      store_bf16x32(static_cast<bf16*>(p.out1) + o, d3);
+    } else if constexpr (EPI == EPI_GELU_BWD) {
+      bf16 a1v[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1v[i]));
+      store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
+    } else {  // EPI_ACC: out_e[row, col] += acc  (fp32, (E, Mout, N))
+      const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
+      float* d0p = static_cast<float*>(p.out0) + oo;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 x = *reinterpret_cast<float4*>(d0p + i);
+        x.x += alpha * v0[i]; x.y += alpha * v0[i + 1]; x.z += alpha * v0[i + 2]; x.w += alpha * v0[i + 3];
+        *reinterpret_cast<float4*>(d0p + i) = x;
+      }
+      if constexpr (NB == 2) {
+        float v1[32];
+        tmem_ld32(tb + BNA + c * 32, v1);
+        float* d1p = static_cast<float*>(p.out1) + oo;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 x = *reinterpret_cast<float4*>(d1p + i);
+          x.x += alpha * v1[i]; x.y += alpha * v1[i + 1]; x.z += alpha * v1[i + 2]; x.w += alpha * v1[i + 3];
+          *reinterpret_cast<float4*>(d1p + i) = x;
+        }
+      }
+    }
+  }
 }
 
 template <bool KGROUP, bool A_MN, bool B_MN, int NB, int EPI>
@@ -276,108 +389,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
       if (!mbar_wait(tfull + acc, acc_phase, abort_flag, p.err, 4)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
-      const int row = t.m0 + row_in_tile;
-      const int n0 = t.n0 * BNA;
-      const float alpha = p.alpha ? *p.alpha : 1.f;
-      if constexpr (EPI == EPI_STORE_PEER) {
-        bf16* stg = reinterpret_cast<bf16*>(smem + NST * STAGE_BYTES + 1024) + q * 32 * STG_LD;
-#pragma unroll 1
-        for (int c = 0; c < BNA / 32; ++c) {
-          if (n0 + c * 32 >= p.N) break;
-          float v0[32];
-          tmem_ld32(tb + c * 32, v0);
-          store_bf16x32(stg + lane * STG_LD + c * 32, v0);
-        }
-        __syncwarp();
-        // row r of the warp's 32: lanes write its 256 columns as one 512-byte segment
-        bf16* dst = static_cast<bf16*>(p.out_tab[t.e]) + static_cast<int64_t>(t.m0 + q * 32 - off[t.e]) * p.N;
-        const int col = n0 + lane * 8;
-        if (col < p.N) {
-#pragma unroll 4
-          for (int r = 0; r < 32; ++r)
-            *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r) * p.N + col) =
-                *reinterpret_cast<const uint4*>(stg + r * STG_LD + lane * 8);
-        }
-        __syncwarp();
-      }
-#pragma unroll 1
-      for (int c = 0; c < (EPI == EPI_STORE_PEER ? 0 : BNA / 32); ++c) {
-        const int col = n0 + c * 32;
-        if (col >= p.N) break;  // partial last tile (N % 32 == 0)
-        float v0[32];
-        tmem_ld32(tb + c * 32, v0);
-        const int64_t o = static_cast<int64_t>(row) * p.N + col;
-        if constexpr (EPI == EPI_STORE) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i] * alpha, p.clip);
-          store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
-        } else if constexpr (EPI == EPI_SWIGLU_FWD) {
-          float v1[32], h[32];
-          tmem_ld32(tb + BNA + c * 32, v1);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v0[i] = clampf(v0[i], p.clip);
-            v1[i] = clampf(v1[i], p.clip);
-            h[i] = v0[i] * sigmoidf_(v0[i]) * v1[i];
-          }
-          store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
-          store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
-          store_bf16x32(static_cast<bf16*>(p.out2) + o, v1);
-        } else if constexpr (EPI == EPI_GELU_FWD) {
-          float h[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v0[i] = clampf(v0[i], p.clip);
-            h[i] = gelu_t(v0[i]);
-          }
-          store_bf16x32(static_cast<bf16*>(p.out0) + o, h);
-          store_bf16x32(static_cast<bf16*>(p.out1) + o, v0);
-        } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-          float d1[32], d3[32];
-          bf16 a1v[32], a3v[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
-            *reinterpret_cast<uint4*>(a3v + i) = *reinterpret_cast<const uint4*>(p.aux1 + o + i);
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float a1 = __bfloat162float(a1v[i]), a3 = __bfloat162float(a3v[i]);
-            const float s = sigmoidf_(a1);
-            d1[i] = v0[i] * a3 * s * (1.f + a1 * (1.f - s));
-            d3[i] = v0[i] * a1 * s;
-          }
-          store_bf16x32(static_cast<bf16*>(p.out0) + o, d1);
-          store_bf16x32(static_cast<bf16*>(p.out1) + o, d3);
-        } else if constexpr (EPI == EPI_GELU_BWD) {
-          bf16 a1v[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(a1v + i) = *reinterpret_cast<const uint4*>(p.aux0 + o + i);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1v[i]));
-          store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
-        } else {  // EPI_ACC: out_e[row, col] += acc  (fp32, (E, Mout, N))
-          const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
-          float* d0p = static_cast<float*>(p.out0) + oo;
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float4 x = *reinterpret_cast<float4*>(d0p + i);
-            x.x += alpha * v0[i]; x.y += alpha * v0[i + 1]; x.z += alpha * v0[i + 2]; x.w += alpha * v0[i + 3];
-            *reinterpret_cast<float4*>(d0p + i) = x;
-          }
-          if constexpr (NB == 2) {
-            float v1[32];
-            tmem_ld32(tb + BNA + c * 32, v1);
-            float* d1p = static_cast<float*>(p.out1) + oo;
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              float4 x = *reinterpret_cast<float4*>(d1p + i);
-              x.x += alpha * v1[i]; x.y += alpha * v1[i + 1]; x.z += alpha * v1[i + 2]; x.w += alpha * v1[i + 3];
-              *reinterpret_cast<float4*>(d1p + i) = x;
-            }
-          }
-        }
-      }
+      epilogue_tile<EPI, NB>(p, off, t, tb, t.m0 + q * 32, lane, smem + NST * STAGE_BYTES + 1024, q);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + acc);
@@ -391,6 +403,218 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- CTA-pair kernel
+// The same GEMMs with one tcgen05.mma spanning the two CTAs of a cluster (cta_group::2): a pair
+// computes a 256 x 256 tile (NB = 2: two 256 x 128 accumulators), each CTA loading its 128 rows
+// of A and its half of the B columns, so a CTA streams 32 KB of operands per 64-deep k-block
+// instead of 48 KB for a 128 x 256 tile.  Six 32 KB stages.  Only the leader CTA (rank 0) runs
+// the MMA role; both CTAs' TMA loads complete on the leader's `full` barrier; its commits
+// arrive on `empty` / `tfull` of both CTAs; both CTAs' epilogue warps release an accumulator on
+// the leader's `tempty`.  M-grouped groups (and K-grouped Mout) must be multiples of 256 rows.
+constexpr int PAIR_BM = 256, PAIR_STAGES = 6;
+constexpr int PAIR_A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's 128 rows
+constexpr int PAIR_B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the 256 columns
+constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
+constexpr size_t PAIR_SMEM = (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024 + 1024;
+
+template <bool KGROUP>
+AHB_DEVICE void decode_pair(const Params& p, const int* off, int tile, int n_tiles, Tile& t) {
+  if (!KGROUP) {
+    const int m_total = off[p.E] / PAIR_BM;
+    const int mt = tile / n_tiles, nt = tile % n_tiles;
+    t.m0 = mt * PAIR_BM;
+    int e = 0;
+    while (e + 1 < p.E && off[e + 1] <= t.m0) ++e;
+    t.e = e;
+    t.n0 = nt;
+    t.k0row = 0;
+    t.nkb = p.kb_total;
+    (void)m_total;
+  } else {
+    const int m_tiles = p.Mout / PAIR_BM;
+    const int per_e = m_tiles * n_tiles;
+    t.e = tile / per_e;
+    const int r = tile % per_e;
+    t.m0 = (r / n_tiles) * PAIR_BM;
+    t.n0 = r % n_tiles;
+    t.k0row = off[t.e];
+    t.nkb = (off[t.e + 1] - off[t.e]) / BK;
+  }
+}
+
+template <bool KGROUP, bool A_MN, bool B_MN, int NB, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gemm_pair_kernel(const __grid_constant__ Params p) {
+  constexpr int BNA = 256 / NB;       // columns per accumulator (the pair's N of one MMA)
+  constexpr int HALF = BNA / 2;       // B columns of one MMA held by this CTA
+  constexpr uint32_t IDESC = idesc_bf16(PAIR_BM, BNA, A_MN, B_MN);
+  static_assert(EPI != EPI_STORE_PEER, "peer-store epilogue runs on the single-CTA kernel");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PAIR_STAGES * PAIR_STAGE_BYTES);
+  uint64_t* empty = full + PAIR_STAGES;
+  uint64_t* tfull = empty + PAIR_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* off = const_cast<int*>(reinterpret_cast<const int*>(tmem_slot + 2));  // E+1 ints (E <= 192)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i <= p.E; i += NTHREADS) off[i] = p.grp_off[i];
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive or load completes
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = (p.N + BNA - 1) / BNA;
+  const int total = KGROUP ? p.E * (p.Mout / PAIR_BM) * n_tiles : (off[p.E] / PAIR_BM) * n_tiles;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    prefetch_tmap(&p.ta0);
+    prefetch_tmap(&p.tb0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = cid; tile < total && ok; tile += ncl) {
+      Tile t;
+      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
+      const int n0 = t.n0 * BNA;
+      const int mrow = t.m0 + 128 * (int)rank;
+      for (int kb = 0; kb < t.nkb; ++kb) {
+        if (!mbar_wait(empty + stage, phase ^ 1, abort_flag, p.err, 11)) { ok = false; break; }
+        unsigned char* sa = smem + stage * PAIR_STAGE_BYTES;
+        unsigned char* sb = sa + PAIR_A_BYTES;
+        const uint32_t fb = mapa_shared(full + stage, 0);
+        if (rank == 0) mbar_expect_tx(full + stage, 2 * PAIR_STAGE_BYTES);
+        const int part = (!KGROUP && kb >= p.kb_split) ? 1 : 0;
+        const int kk = (part ? kb - p.kb_split : kb) * BK;
+        const CUtensorMap* ma = part ? &p.ta1 : &p.ta0;
+        if (!KGROUP) {
+          if (A_MN) {
+            tma_load_2d_pair(sa, ma, fb, mrow, kk);
+            tma_load_2d_pair(sa + 8192, ma, fb, mrow + 64, kk);
+          } else {
+            tma_load_2d_pair(sa, ma, fb, kk, mrow);
+          }
+        } else {
+          const int r = t.k0row + kb * BK;
+          tma_load_2d_pair(sa, ma, fb, mrow, r);
+          tma_load_2d_pair(sa + 8192, ma, fb, mrow + 64, r);
+        }
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const CUtensorMap* mb = (NB == 2) ? (nb ? &p.tb1 : &p.tb0) : (part ? &p.tb1 : &p.tb0);
+          unsigned char* sbn = sb + nb * HALF * BK * 2;
+          const int c0 = n0 + HALF * (int)rank;
+          if (!KGROUP) {
+            if (B_MN) {
+#pragma unroll
+              for (int i = 0; i < HALF / 64; ++i) tma_load_2d_pair(sbn + i * 8192, mb, fb, c0 + 64 * i, t.e * p.b_rows + kk);
+            } else {
+              tma_load_2d_pair(sbn, mb, fb, kk, t.e * p.b_rows + c0);
+            }
+          } else {
+            const int r = t.k0row + kb * BK;
+#pragma unroll
+            for (int i = 0; i < HALF / 64; ++i) tma_load_2d_pair(sbn + i * 8192, mb, fb, c0 + 64 * i, r);
+          }
+        }
+        if (++stage == PAIR_STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) {  // let copies already in flight land before the CTA exits
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 2000000ull) {}
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int tile = cid; tile < total && ok; tile += ncl) {
+      Tile t;
+      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
+      if (t.nkb == 0) continue;
+      if (!mbar_wait(tempty + acc, acc_phase ^ 1, abort_flag, p.err, 12)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d0 = tmem_base + acc * 256;
+      for (int kb = 0; kb < t.nkb; ++kb) {
+        if (!mbar_wait(full + stage, phase, abort_flag, p.err, 13)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * PAIR_STAGE_BYTES);
+        const uint32_t sb = sa + PAIR_A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = A_MN ? smem_desc(sa + k * 2048, 8192, 1024) : smem_desc(sa + k * 32, 16, 1024);
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            const uint32_t sbn = sb + nb * HALF * BK * 2;
+            const uint64_t bd = B_MN ? smem_desc(sbn + k * 2048, 8192, 1024) : smem_desc(sbn + k * 32, 16, 1024);
+            umma_bf16_pair(d0 + nb * BNA, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+        }
+        issued = true;
+        umma_commit_pair(empty + stage, 0x3);
+        if (++stage == PAIR_STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      umma_commit_pair(tfull + acc, 0x3);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (!ok && issued) {  // wait (bounded) for the MMAs already issued before freeing TMEM
+      umma_commit_pair(drain, 0x1);
+      volatile int dummy = 0;
+      mbar_wait(drain, 0, &dummy, nullptr, 0, 100000000ull);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t tempty0 = mapa_shared(tempty, 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cid; tile < total; tile += ncl) {
+      Tile t;
+      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
+      if (t.nkb == 0) continue;
+      if (!mbar_wait(tfull + acc, acc_phase, abort_flag, p.err, 14)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
+      epilogue_tile<EPI, NB>(p, off, t, tb, t.m0 + 128 * (int)rank + q * 32, lane, nullptr, q);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into this CTA's TMEM and shared memory are done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------- host side
@@ -437,13 +661,28 @@ int launch(const Params& p, int grid, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
+template <bool KG, bool AMN, bool BMN, int NB, int EPI>
+int launch_pair(const Params& p, int grid, cudaStream_t st) {
+  auto k = moe_gemm_pair_kernel<KG, AMN, BMN, NB, EPI>;
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PAIR_SMEM) != cudaSuccess) return -3;
+    init = true;
+  }
+  k<<<grid, NTHREADS, PAIR_SMEM, st>>>(p);  // cluster dims (2, 1, 1) are part of the kernel
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
 }  // namespace
 
 // kind: see launchers.h (AHB_GEMM_*)
 int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
-                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st, const float* alpha) {
+                 const void* aux1, float clip, int* err, int num_sms, cudaStream_t st, const float* alpha,
+                 int m_limit) {
+  const bool pair = (kind & AHB_GEMM_PAIR) != 0;
+  kind &= ~AHB_GEMM_PAIR;
   if (E < 1 || E > 192 || N % 32 != 0 || K % 64 != 0) return -10;  // offsets live in the kernel's smem tail
   Params p;
   memset(&p, 0, sizeof(p));
@@ -462,21 +701,39 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
   p.clip = clip;
   p.alpha = alpha;
   p.err = err;
+  p.m_limit = m_limit;
   const bool kg = kind == AHB_GEMM_WGRAD || kind == AHB_GEMM_WGRAD_DUAL;
   const bool a_mn = kg;
   const bool b_mn = kg || kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_FWD_GELU || kind == AHB_GEMM_FWD_DOWN;
   const int nb = (kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_WGRAD_DUAL) ? 2 : 1;
   const int bna = 256 / nb;
   if (N % bna != 0 && kind != AHB_GEMM_DENSE && kind != AHB_GEMM_FWD_DOWN) return -11;
-  if (kg && Mout % BM != 0) return -12;
+  if (kg && Mout % (pair ? PAIR_BM : BM) != 0) return -12;
+  // a CTA of a pair loads half of each accumulator's columns of B
+  const int b_box = b_mn ? 64 : (pair ? bna / 2 : bna);
   int rc = 0;
   rc |= make_map(&p.ta0, a0, a_rows, a_cols, a_cols, a_mn ? 64 : BM);
   if (a1) rc |= make_map(&p.ta1, a1, a_rows, a_cols, a_cols, a_mn ? 64 : BM);
-  rc |= make_map(&p.tb0, b0, b_rows_total, b_cols, b_cols, b_mn ? 64 : bna);
-  if (b1) rc |= make_map(&p.tb1, b1, b_rows_total, b_cols, b_cols, b_mn ? 64 : bna);
+  rc |= make_map(&p.tb0, b0, b_rows_total, b_cols, b_cols, b_box);
+  if (b1) rc |= make_map(&p.tb1, b1, b_rows_total, b_cols, b_cols, b_box);
   if (!a1) p.ta1 = p.ta0;
   if (!b1) p.tb1 = p.tb0;
   if (rc) return -20;
+  if (pair) {
+    const int grid = (num_sms / 2) * 2;
+    switch (kind) {
+      case AHB_GEMM_DENSE: return launch_pair<false, false, false, 1, EPI_STORE>(p, grid, st);
+      case AHB_GEMM_FWD_SWIGLU: return launch_pair<false, false, true, 2, EPI_SWIGLU_FWD>(p, grid, st);
+      case AHB_GEMM_FWD_GELU: return launch_pair<false, false, true, 1, EPI_GELU_FWD>(p, grid, st);
+      case AHB_GEMM_FWD_DOWN: return launch_pair<false, false, true, 1, EPI_STORE>(p, grid, st);
+      case AHB_GEMM_DH_SWIGLU: return launch_pair<false, false, false, 1, EPI_SWIGLU_BWD>(p, grid, st);
+      case AHB_GEMM_DH_GELU: return launch_pair<false, false, false, 1, EPI_GELU_BWD>(p, grid, st);
+      case AHB_GEMM_DX: return launch_pair<false, false, false, 1, EPI_STORE>(p, grid, st);
+      case AHB_GEMM_WGRAD: return launch_pair<true, true, true, 1, EPI_ACC>(p, grid, st);
+      case AHB_GEMM_WGRAD_DUAL: return launch_pair<true, true, true, 2, EPI_ACC>(p, grid, st);
+      default: return -30;
+    }
+  }
   const int grid = num_sms;
   switch (kind) {
     case AHB_GEMM_DENSE: return launch<false, false, false, 1, EPI_STORE>(p, grid, st);

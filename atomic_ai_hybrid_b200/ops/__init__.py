@@ -117,20 +117,22 @@ def conv1d(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], silu: bo
 
 
 # ---------------------------------------------------------------- sequence mixers
-def gdn2(q, k, v, w, b, g, scale: float = 1.0, chunk: int = 64) -> torch.Tensor:
-    """GDN-2 chunked delta rule; ``(B,L,H,D)`` inputs, per-channel gates."""
+def gdn2(q, k, v, w, b, g, scale: float = 1.0, chunk: int = 64, h0=None, return_final: bool = False):
+    """GDN-2 chunked delta rule; ``(B,L,H,D)`` inputs, per-channel gates.  ``h0`` (B,H,D,D)
+    is the state before the first token; ``return_final`` returns ``(o, h_final)``."""
     if use_cuda(q):
-        return _k().gdn2(q, k, v, w, b, g, scale, chunk)
-    o, _ = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
-    return o
+        return _k().gdn2(q, k, v, w, b, g, scale, chunk, h0=h0, return_final=return_final)
+    o, hf = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, h0=h0, checkpoint_chunks=True)
+    return (o, hf) if return_final else o
 
 
-def ssd(dt, A, Bm, Cm, x, chunk: int = 64) -> torch.Tensor:
-    """Mamba2 SSD; ``dt, x (B,L,H,P)``, ``A (H,)``, ``B, C (B,L,N)``."""
+def ssd(dt, A, Bm, Cm, x, chunk: int = 64, state0=None, return_final: bool = False):
+    """Mamba2 SSD; ``dt, x (B,L,H,P)``, ``A (H,)``, ``B, C (B,L,N)``.  ``state0`` (B,H,P,N)
+    is the state before the first token; ``return_final`` returns ``(y, s_final)``."""
     if use_cuda(x):
-        return _k().ssd(dt, A, Bm, Cm, x, chunk)
-    y, _ = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
-    return y
+        return _k().ssd(dt, A, Bm, Cm, x, chunk, state0=state0, return_final=return_final)
+    y, sf = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, state0=state0, checkpoint_chunks=True)
+    return (y, sf) if return_final else y
 
 
 def attention(q, k, v, sm_scale: float) -> torch.Tensor:

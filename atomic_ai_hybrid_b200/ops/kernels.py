@@ -146,32 +146,46 @@ SCAN_RECOMPUTE = os.environ.get("AHB_SCAN_RECOMPUTE", "0") == "1"
 class _GDN2(torch.autograd.Function):
     """sm_100a chunked GDN-2 (head dim 128, chunk 64): 2 launches forward; the
     backward runs 4 launches on the saved chunk intermediates (WY factors, scores,
-    per-chunk states), or 6 when it recomputes them."""
+    per-chunk states), or 6 when it recomputes them.  ``h0`` (B,H,128,128), the state
+    before the first token, and the returned final state are differentiable (reference
+    initial-state path: `atomic_ops/kernel_trainable_B6.py:187-193`)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g, b, w, scale):
+    def forward(ctx, q, k, v, g, b, w, scale, h0, want_final):
         bf = torch.bfloat16
         q, k, v, b, w = (t.to(bf).contiguous() for t in (q, k, v, b, w))
         g = g.float().contiguous()
+        h0 = h0.float().contiguous() if h0 is not None else None
         keep = any(ctx.needs_input_grad) and not SCAN_RECOMPUTE
+        hf = None
         if keep:
-            o, *inter = ext().gdn_fwd_train(q, k, v, g, b, w, scale)
+            o, *inter = ext().gdn_fwd_train(q, k, v, g, b, w, scale, h0, want_final)
+            if want_final:
+                hf = inter.pop()
         else:
-            (o,) = ext().gdn_fwd(q, k, v, g, b, w, scale, False)
+            outs = ext().gdn_fwd(q, k, v, g, b, w, scale, want_final, h0)
+            o, hf = outs[0], (outs[1] if want_final else None)
             inter = []
         ctx.n_inter = len(inter)
-        ctx.save_for_backward(q, k, v, g, b, w, *inter)
+        ctx.has_h0 = h0 is not None
+        ctx.save_for_backward(q, k, v, g, b, w, *((h0,) if h0 is not None else ()), *inter)
         ctx.scale = scale
-        return o
+        ctx.want_final = want_final
+        return (o, hf) if want_final else o
 
     @staticmethod
-    def backward(ctx, do):
-        q, k, v, g, b, w, *inter = ctx.saved_tensors
+    def backward(ctx, do, dhf=None):
+        q, k, v, g, b, w, *rest = ctx.saved_tensors
+        h0 = rest.pop(0) if ctx.has_h0 else None
+        inter = rest
+        want_dh0 = ctx.has_h0 and ctx.needs_input_grad[7]
+        dhf = dhf.float().contiguous() if dhf is not None else None
         if inter:
-            dq, dk, dv, dg, db, dw = ext().gdn_bwd_saved(q, k, v, g, b, w, do.contiguous(), ctx.scale, inter)
+            grads = ext().gdn_bwd_saved(q, k, v, g, b, w, do.contiguous(), ctx.scale, inter, dhf, want_dh0)
         else:
-            dq, dk, dv, dg, db, dw = ext().gdn_bwd(q, k, v, g, b, w, do.contiguous(), ctx.scale)
-        return dq, dk, dv, dg, db, dw, None
+            grads = ext().gdn_bwd(q, k, v, g, b, w, do.contiguous(), ctx.scale, h0, dhf, want_dh0)
+        dq, dk, dv, dg, db, dw = grads[:6]
+        return dq, dk, dv, dg, db, dw, None, (grads[6] if want_dh0 else None), None
 
 
 _WARNED = set()
@@ -184,51 +198,69 @@ def _unsupported(what: str) -> None:
               f"using the PyTorch chunked path", flush=True)
 
 
-def gdn2(q, k, v, w, b, g, scale, chunk):
+def gdn2(q, k, v, w, b, g, scale, chunk, h0=None, return_final=False):
     """``(B,L,H,128)`` GDN-2 with per-channel gates; ``chunk`` is fixed at 64 in the kernel
-    (results do not depend on the chunk length).  Other head dims or lengths that are
+    (results do not depend on the chunk length).  ``h0`` (B,H,128,128) is the state before
+    the first token (zero when None); ``return_final`` also returns the fp32 state after the
+    last one, as ``(o, h_final)``; both carry gradients.  Other head dims or lengths that are
     not a multiple of 64 run the PyTorch chunked path."""
     if q.shape[-1] != 128 or q.shape[1] % 64:
         _unsupported(f"gdn2 D={q.shape[-1]} L={q.shape[1]}")
-        o, _ = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
-        return o
-    return _GDN2.apply(q, k, v, g, b, w, float(scale))
+        o, hf = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, h0=h0, checkpoint_chunks=True)
+        return (o, hf) if return_final else o
+    return _GDN2.apply(q, k, v, g, b, w, float(scale), h0, bool(return_final))
 
 
 class _SSD(torch.autograd.Function):
     """sm_100a Mamba2 SSD (head dim 64, d_state 128, chunk 64): 2 launches forward
     (chunk kernel, state recurrence); the backward reuses the forward's per-chunk states and
     intra-chunk outputs (4 launches: reverse state-gradient recurrence, chunk backward, two
-    group sums) or recomputes them (6)."""
+    group sums) or recomputes them (6).  ``s0`` (B,H,64,128), the state before the first
+    token, and the returned final state are differentiable (reference initial-state path:
+    `atomic_ops/kernel_mamba2_trainable_B6.py:137-155`)."""
 
     @staticmethod
-    def forward(ctx, dt, A, Bm, Cm, x):
+    def forward(ctx, dt, A, Bm, Cm, x, s0, want_final):
         bf = torch.bfloat16
         dt, Bm, Cm, x = (t.to(bf).contiguous() for t in (dt, Bm, Cm, x))
         A = A.float().contiguous()
-        if any(ctx.needs_input_grad) and not SCAN_RECOMPUTE:
-            y, *saved = ext().ssd_fwd_train(x, dt, A, Bm, Cm)
-            ctx.save_for_backward(dt, A, Bm, Cm, x, *saved)
+        s0 = s0.float().contiguous() if s0 is not None else None
+        sf = None
+        if any(ctx.needs_input_grad) and not SCAN_RECOMPUTE or s0 is not None or want_final:
+            y, *saved = ext().ssd_fwd_train(x, dt, A, Bm, Cm, s0, want_final)
+            if want_final:
+                sf = saved.pop()
+            if not any(ctx.needs_input_grad) or SCAN_RECOMPUTE:
+                saved = []
         else:
             y = ext().ssd_fwd(x, dt, A, Bm, Cm)
-            ctx.save_for_backward(dt, A, Bm, Cm, x)
-        return y
+            saved = []
+        ctx.has_s0 = s0 is not None
+        ctx.save_for_backward(dt, A, Bm, Cm, x, *((s0,) if s0 is not None else ()), *saved)
+        return (y, sf) if want_final else y
 
     @staticmethod
-    def backward(ctx, dy):
+    def backward(ctx, dy, dsf=None):
         dt, A, Bm, Cm, x, *st = ctx.saved_tensors
-        dx, ddt, dA, dB, dC = ext().ssd_bwd(x, dt, A, Bm, Cm, dy.contiguous(), *st)
-        return ddt, dA, dB.to(Bm.dtype), dC.to(Cm.dtype), dx
+        s0 = st.pop(0) if ctx.has_s0 else None
+        want_ds0 = ctx.has_s0 and ctx.needs_input_grad[5]
+        dsf = dsf.float().contiguous() if dsf is not None else None
+        saved = st if st else [None] * 4
+        grads = ext().ssd_bwd(x, dt, A, Bm, Cm, dy.contiguous(), *saved, s0, dsf, want_ds0)
+        dx, ddt, dA, dB, dC = grads[:5]
+        return ddt, dA, dB.to(Bm.dtype), dC.to(Cm.dtype), dx, (grads[5] if want_ds0 else None), None
 
 
-def ssd(dt, A, Bm, Cm, x, chunk):
+def ssd(dt, A, Bm, Cm, x, chunk, state0=None, return_final=False):
     """``dt, x (B,L,H,64)``, ``A (H,)``, ``B, C (B,L,128)``; chunk fixed at 64 in the kernel.
-    Other head dims / state sizes run the PyTorch chunked path."""
+    ``state0`` (B,H,64,128) is the state before the first token (zero when None);
+    ``return_final`` also returns the fp32 state after the last one, as ``(y, s_final)``;
+    both carry gradients.  Other head dims / state sizes run the PyTorch chunked path."""
     if x.shape[-1] != 64 or Bm.shape[-1] != 128 or x.shape[1] % 64:
         _unsupported(f"ssd P={x.shape[-1]} N={Bm.shape[-1]} L={x.shape[1]}")
-        y, _ = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
-        return y
-    return _SSD.apply(dt, A, Bm, Cm, x)
+        y, sf = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, state0=state0, checkpoint_chunks=True)
+        return (y, sf) if return_final else y
+    return _SSD.apply(dt, A, Bm, Cm, x, state0, bool(return_final))
 
 
 class _Attention(torch.autograd.Function):

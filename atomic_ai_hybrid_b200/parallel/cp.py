@@ -110,24 +110,34 @@ class CPGroup:
         return h
 
     def gdn2_scan(self, q, k, v, g, b, w, scale: float, chunk: int):
-        from ..ops import reference as R
-        o0, S = R.gdn2_chunked(q, k, v, g, b, w, scale, chunk, checkpoint_chunks=True)
+        """This segment's GDN-2 output given the states of the segments before it: the local
+        scan from zero (output ``o0``, final state ``S``), the segment's state transfer ``T``
+        (the final state of a scan from the identity with ``v = 0``: ``h -> T h``), the
+        incoming state folded over the earlier ranks, and the output of that state carried
+        through the segment (``v = 0``).  On CUDA the three scans are the sm_100a kernels
+        with their initial-state inputs and gradients."""
+        from .. import ops
+        o0, S = ops.gdn2(q, k, v, w, b, g, scale, chunk, return_final=True)
         B, L, H, D = q.shape
-        eye = torch.eye(D, dtype=S.dtype, device=q.device).expand(B, H, D, D).contiguous()
-        _, T = R.gdn2_chunked(q, k, torch.zeros_like(k), g, b, w, scale, chunk, h0=eye, checkpoint_chunks=True)
+        eye = torch.eye(D, dtype=torch.float32, device=q.device).expand(B, H, D, D).contiguous()
+        zv = torch.zeros_like(v)
+        _, T = ops.gdn2(q, k, zv, w, b, g, scale, chunk, h0=eye, return_final=True)
         Ts, Ss = self.gather(T), self.gather(S)
         h_in = self._fold(Ts, Ss, lambda Tj, h: Tj @ h)
-        oc, _ = R.gdn2_chunked(q, k, torch.zeros_like(v), g, b, w, scale, chunk, h0=h_in, checkpoint_chunks=True)
+        oc = ops.gdn2(q, k, zv, w, b, g, scale, chunk, h0=h_in)
         return o0 + oc
 
     def ssd_scan(self, dt, A, Bm, Cm, x, chunk: int):
-        from ..ops import reference as R
-        y0, S = R.ssd_chunked(dt, A, Bm, Cm, x, chunk, checkpoint_chunks=True)
-        _, T = R.ssd_chunked(dt, A, Bm, Cm, torch.zeros_like(x), chunk, state0=torch.ones_like(S),
-                             checkpoint_chunks=True)
+        """Mamba2 SSD of this segment given the earlier segments' states (as ``gdn2_scan``;
+        the transfer of a segment is a per-(head, channel) decay, the final state of a scan
+        from ones with ``x = 0``)."""
+        from .. import ops
+        y0, S = ops.ssd(dt, A, Bm, Cm, x, chunk, return_final=True)
+        zx = torch.zeros_like(x)
+        _, T = ops.ssd(dt, A, Bm, Cm, zx, chunk, state0=torch.ones_like(S), return_final=True)
         Ts, Ss = self.gather(T), self.gather(S)
         h_in = self._fold(Ts, Ss, lambda Tj, h: Tj * h)
-        yc, _ = R.ssd_chunked(dt, A, Bm, Cm, torch.zeros_like(x), chunk, state0=h_in, checkpoint_chunks=True)
+        yc = ops.ssd(dt, A, Bm, Cm, zx, chunk, state0=h_in)
         return y0 + yc
 
 

@@ -175,6 +175,21 @@ def bench_conv(B, T, C, warmup, iters, flush, mode="fwdbwd"):
     return {"op": "conv1d", "mode": mode, "B": B, "T": T, "C": C, "ms": ms, "min_io_gb_s": io / ms / 1e6}
 
 
+def bench_gemm(M, K, N, warmup, iters, flush):
+    """C = A B^T at one shape: the single-CTA and CTA-pair tcgen05 kernels and cuBLAS."""
+    from ..ops._ext import ext
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    fl = 2.0 * M * K * N
+    out = {"op": "gemm", "M": M, "K": K, "N": N}
+    for name, fn in (("single_cta", lambda: ext().gemm_dense(a, b, pair=False)),
+                     ("cta_pair", lambda: ext().gemm_dense(a, b, pair=True)),
+                     ("cublas", lambda: torch.mm(a, b.t()))):
+        ms = _timeit(fn, warmup, iters, flush)
+        out[name] = {"ms": ms, "tflops": fl / ms / 1e9}
+    return out
+
+
 def bench_gemm_rs(W, n, K, N, warmup, iters, flush):
     """The tensor-parallel GEMM + reduce-scatter kernel on one GPU: the W destination
     slots are local buffers (the NVLink stores become local stores), so this measures
@@ -194,7 +209,9 @@ def bench_gemm_rs(W, n, K, N, warmup, iters, flush):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs"])
+    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs", "gemm"])
+    ap.add_argument("--K", type=int, default=2048)
+    ap.add_argument("--N", type=int, default=2048)
     ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--T", type=int, default=4096)
@@ -216,6 +233,8 @@ def main(argv=None):
         r = bench_router(a.B * a.T, 2048, 32, 4, a.warmup, a.iters, flush, a.mode)
     elif a.op == "glue":
         r = bench_glue(a.B * a.T, 2048, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "gemm":
+        r = bench_gemm(a.B * a.T, a.K, a.N, a.warmup, a.iters, flush)
     elif a.op == "gemm_rs":
         r = bench_gemm_rs(2, a.B * a.T // 2, 512, 4096, a.warmup, a.iters, flush)
     else:

@@ -77,3 +77,31 @@ def test_gdn_production_shape_forward_backward():
         assert torch.isfinite(a.grad).all(), name
         err = _rel(a.grad, r.grad)
         assert err < 5e-2, (name, err)
+
+
+@pytest.mark.parametrize("recompute", [False, True])
+def test_gdn_initial_state_and_final_state(recompute, monkeypatch):
+    """``h0`` in and the final state out, both with gradients (saved-intermediates and
+    recompute backward paths), against the fp32 chunked oracle started from the same state;
+    the loss also reads the final state, so its gradient enters the reverse recurrence."""
+    monkeypatch.setattr(K, "SCAN_RECOMPUTE", recompute)
+    B, L, H = 2, 256, 2
+    ins = _inputs(B, L, H, 7)
+    g_ = torch.Generator(device=dev).manual_seed(8)
+    h0 = (torch.randn(B, H, 128, 128, generator=g_, device=dev) * 0.1)
+    xs = [t.clone().requires_grad_(True) for t in ins]
+    hx = h0.clone().requires_grad_(True)
+    o, hf = K.gdn2(xs[0], xs[1], xs[2], xs[5], xs[4], xs[3], 1.0, 64, h0=hx, return_final=True)
+    do = torch.randn_like(o)
+    dhf = torch.randn_like(hf) * 0.1
+    ((o.float() * do.float()).sum() + (hf * dhf).sum()).backward()
+    rs = [t.detach().float().clone().requires_grad_(True) for t in ins]
+    hr = h0.clone().requires_grad_(True)
+    o2, hf2 = R.gdn2_chunked(rs[0], rs[1], rs[2], rs[3], rs[4], rs[5], 1.0, 64, h0=hr)
+    ((o2 * do.float()).sum() + (hf2 * dhf).sum()).backward()
+    assert _rel(o, o2) < 2e-2, _rel(o, o2)
+    assert _rel(hf, hf2) < 2e-2, _rel(hf, hf2)
+    for name, a, r in zip("qkvgbw", xs, rs):
+        assert torch.isfinite(a.grad).all(), name
+        assert _rel(a.grad, r.grad) < 5e-2, (name, _rel(a.grad, r.grad))
+    assert _rel(hx.grad, hr.grad) < 3e-2, _rel(hx.grad, hr.grad)

@@ -27,6 +27,22 @@ def test_gemm_dense(M, K, N):
     assert _rel(c, ref) < 1e-2, _rel(c, ref)
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 64, 256), (512, 2048, 512), (1000, 320, 768), (4096, 2048, 2048)])
+def test_gemm_dense_cta_pair(M, K, N):
+    """The CTA-pair kernel (cta_group::2, 256 x 256 tiles over two SMs) against fp32, including a
+    last tile that runs past M (rows read as zeros, not stored)."""
+    ext().gemm_error_reset()
+    torch.manual_seed(2)
+    a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=dev, dtype=torch.bfloat16)
+    c = ext().gemm_dense(a, b, pair=True)
+    torch.cuda.synchronize()
+    assert KN.gemm_error() == 0
+    ref = a.float() @ b.float().t()
+    assert _rel(c, ref) < 1e-2, _rel(c, ref)
+    assert torch.equal(c, ext().gemm_dense(a, b, pair=True))  # deterministic
+
+
 def _moe_ref(x, top_idx, gate, w1, w2, w3, shared, act):
     T, d = x.shape
     E = w1.shape[0]

@@ -75,3 +75,31 @@ def test_ssd_production_shape_forward_backward():
     """The op-benchmark shape per sequence (T = 4096, H = 32, P = 64, N = 128): 64 chunks per head,
     all four head groups of the chunk backward, against the fp64 oracle."""
     _check_backward(1, 4096, 32, -4.0, seed=5)
+
+
+@pytest.mark.parametrize("recompute", [False, True])
+def test_ssd_initial_state_and_final_state(recompute, monkeypatch):
+    """``state0`` in and the final state out, both with gradients (saved-states and
+    recompute backward paths), against the fp64 oracle started from the same state; the loss
+    also reads the final state, so its gradient enters the reverse recurrence."""
+    monkeypatch.setattr(K, "SCAN_RECOMPUTE", recompute)
+    B, L, H = 2, 256, 3
+    ins = _inputs(B, L, H, 11, -1.0)
+    g_ = torch.Generator(device=dev).manual_seed(12)
+    s0 = torch.randn(B, H, 64, 128, generator=g_, device=dev) * 0.5
+    xs = [t.clone().requires_grad_(True) for t in ins]
+    sx = s0.clone().requires_grad_(True)
+    y, sf = K.ssd(*xs, 64, state0=sx, return_final=True)
+    dy = torch.randn(y.shape, generator=g_, device=dev).to(y.dtype)
+    dsf = torch.randn(sf.shape, generator=g_, device=dev) * 0.1
+    ((y.float() * dy.float()).sum() + (sf * dsf).sum()).backward()
+    rs = [t.detach().double().clone().requires_grad_(True) for t in ins]
+    sr = s0.double().clone().requires_grad_(True)
+    y2, sf2 = R.ssd_chunked(*rs, 64, state0=sr)
+    ((y2 * dy.double()).sum() + (sf2 * dsf.double()).sum()).backward()
+    assert _rel(y, y2) < 2e-2, _rel(y, y2)
+    assert _rel(sf, sf2) < 2e-2, _rel(sf, sf2)
+    for name, a, r in zip(["dt", "A", "B", "C", "x"], xs, rs):
+        assert torch.isfinite(a.grad).all(), name
+        assert _rel(a.grad, r.grad) < 5e-2, (name, _rel(a.grad, r.grad))
+    assert _rel(sx.grad, sr.grad) < 2e-2, _rel(sx.grad, sr.grad)

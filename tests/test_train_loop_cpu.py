@@ -8,6 +8,7 @@ import socket
 import numpy as np
 import pytest
 import torch.multiprocessing as mp
+from _dist import free_port, load_factor, threads_per_rank
 
 from atomic_ai_hybrid_b200.training.loop import TrainArgs, main_execution
 
@@ -64,9 +65,11 @@ def test_sigterm_triggers_emergency_save(tmp_path, monkeypatch):
     assert meta["tag"] == "EMERGENCY_SIGNAL"
 
 
-def _rank_main(rank, world, port, tmp):
+def _rank_main(rank, world, port, tmp, pg_timeout_s):
+    import torch
+    torch.set_num_threads(threads_per_rank(world))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="10", AHB_INJECT_RAISE_STEP="2",
+                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S=str(pg_timeout_s), AHB_INJECT_RAISE_STEP="2",
                       AHB_INJECT_RAISE_RANK="1")
     try:
         main_execution(_args(tmp, max_steps=5, global_batch=2, accum_steps=1))
@@ -79,16 +82,16 @@ def _rank_main(rank, world, port, tmp):
 def test_failing_rank_ends_peers_with_error(tmp_path):
     """Rank 1 raises at step 2; rank 0, waiting in that step's collective, ends with an
     error naming rank 1 and its exception (the notice posted through the store)."""
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
+    port = free_port()
+    # the collective timeout bounds how long rank 0 waits in step 2 for the failed rank; under a
+    # loaded machine the healthy steps before it are slower, so it scales with the load
+    lf = load_factor()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path), int(20 * lf))) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=240)
+        p.join(timeout=240 * lf)
     assert all(p.exitcode not in (0, None) for p in procs), [p.exitcode for p in procs]
     err0 = (tmp_path / "err0.txt").read_text()
     assert err0.startswith("PeerFailure") and "rank 1 at step 2" in err0 and "injected failure" in err0, err0
