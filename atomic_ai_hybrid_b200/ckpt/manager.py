@@ -209,6 +209,8 @@ def _stores(trainer):
     yield trainer.store, trainer.opt, False
     if getattr(trainer, "ep_store", None) is not None:
         yield trainer.ep_store, trainer.ep_opt, True
+    if getattr(trainer, "xp_store", None) is not None:  # the experts with bf16 gradient accumulators
+        yield trainer.xp_store, trainer.xp_opt, True
 
 
 def _expert_range(s, ep: bool):

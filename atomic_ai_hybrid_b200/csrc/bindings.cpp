@@ -5,8 +5,11 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAGraphsC10Utils.h>
 #include "launchers.h"
 #include <cstdlib>
+#include <map>
+#include <mutex>
 
 namespace {
 
@@ -25,6 +28,14 @@ void check_cuda(const torch::Tensor& t, const char* n) {
 void check_acc(const torch::Tensor& t, int64_t n, const char* name) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == n, name,
               " must be a contiguous fp32 CUDA tensor with ", n, " elements");
+}
+
+// expert weight-gradient accumulators: fp32, or bf16 for a store with 16-bit gradients
+static bool check_acc_16(const torch::Tensor& t, int64_t n, const char* name) {
+  TORCH_CHECK(t.is_cuda() && (t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16) &&
+                  t.is_contiguous() && t.numel() == n,
+              name, " must be a contiguous fp32 or bf16 CUDA tensor with ", n, " elements");
+  return t.scalar_type() == at::kBFloat16;
 }
 
 // Fail loudly if a launch of this binding was rejected (bad configuration,
@@ -533,12 +544,14 @@ static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::
                                          const c10::optional<torch::Tensor>& w3, const torch::Tensor& dw1_acc,
                                          const torch::Tensor& dw2_acc, const c10::optional<torch::Tensor>& dw3_acc,
                                          bool swiglu, bool pair = false) {
-  const int PM = pair ? AHB_GEMM_PAIR : 0, PW = moe_pair() ? AHB_GEMM_PAIR : 0;
+  const int PM = pair ? AHB_GEMM_PAIR : 0;
+  int PW = moe_pair() ? AHB_GEMM_PAIR : 0;
   const int64_t R = xs.size(0);
   const int d = (int)xs.size(1), E = (int)w1.size(0), F = (int)w1.size(2);
   auto st = cur_stream();
-  check_acc(dw1_acc, w1.numel(), "dw1_acc");
-  check_acc(dw2_acc, w2.numel(), "dw2_acc");
+  const bool a16 = check_acc_16(dw1_acc, w1.numel(), "dw1_acc");
+  TORCH_CHECK(check_acc_16(dw2_acc, w2.numel(), "dw2_acc") == a16, "moe_bwd: accumulators of one dtype");
+  if (a16) PW |= AHB_GEMM_ACC_BF16;
   int* err = err_word().data_ptr<int>();
   auto dA1 = torch::empty({R, F}, xs.options());
   torch::Tensor dA3;
@@ -555,7 +568,7 @@ static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::
   }
   gemm_check(rc, "dh");
   rc = ahb_moe_gemm(AHB_GEMM_WGRAD | PW, h.data_ptr(), nullptr, R, F, dys.data_ptr(), nullptr, R, d, 0,
-                    off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
+                    off.data_ptr<int>(), E, d, F, 0, 0, dw2_acc.data_ptr(), nullptr, nullptr, nullptr, nullptr,
                     0.f, err, num_sms(), st);
   gemm_check(rc, "wgrad w2");
   auto dxs = torch::empty({R, d}, xs.options());
@@ -565,9 +578,9 @@ static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::
                       nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "dx");
     TORCH_CHECK(dw3_acc.has_value(), "moe_bwd: dw3_acc");
-    check_acc(*dw3_acc, w3->numel(), "dw3_acc");
+    TORCH_CHECK(check_acc_16(*dw3_acc, w3->numel(), "dw3_acc") == a16, "moe_bwd: accumulators of one dtype");
     rc = ahb_moe_gemm(AHB_GEMM_WGRAD_DUAL | PW, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), dA3.data_ptr(), R, F, 0,
-                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), dw3_acc->data_ptr<float>(),
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr(), dw3_acc->data_ptr(),
                       nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "wgrad w1/w3");
   } else {
@@ -576,7 +589,7 @@ static torch::Tensor moe_expert_bwd_impl(const torch::Tensor& dys, const torch::
                       0.f, err, num_sms(), st);
     gemm_check(rc, "dx");
     rc = ahb_moe_gemm(AHB_GEMM_WGRAD | PW, xs.data_ptr(), nullptr, R, d, dA1.data_ptr(), nullptr, R, F, 0,
-                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
+                      off.data_ptr<int>(), E, F, d, 0, 0, dw1_acc.data_ptr(), nullptr, nullptr, nullptr,
                       nullptr, 0.f, err, num_sms(), st);
     gemm_check(rc, "wgrad w1");
   }
@@ -795,9 +808,13 @@ void optim_prepare(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, to
                    torch::Tensor master, double inv, torch::Tensor red, torch::Tensor flags,
                    c10::optional<torch::Tensor> grad_peers, int64_t lo) {
   TORCH_CHECK(red.scalar_type() == at::kDouble && flags.scalar_type() == at::kInt, "optim_prepare: red f64, flags i32");
+  TORCH_CHECK(grad_shard.scalar_type() == at::kFloat || grad_shard.scalar_type() == at::kBFloat16,
+              "optim_prepare: fp32 or bf16 gradients");
   auto pt = peer_table(grad_peers);
+  TORCH_CHECK(pt.second == 0 || grad_shard.scalar_type() == at::kFloat, "optim_prepare: peer gradients are fp32");
   ahb_optim_prepare(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
-                    (int)(cstart.numel() - 1), (int)nblocks, grad_shard.data_ptr<float>(), master.data_ptr<float>(),
+                    (int)(cstart.numel() - 1), (int)nblocks, grad_shard.data_ptr(),
+                    grad_shard.scalar_type() == at::kBFloat16, master.data_ptr<float>(),
                     (float)inv, red.data_ptr<double>(), flags.data_ptr<int>(),
                     reinterpret_cast<const float* const*>(pt.first), pt.second, lo, cur_stream());
   check_launch("ahb_optim_prepare");
@@ -808,6 +825,8 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
                  c10::optional<torch::Tensor> frac, std::vector<double> lr, std::vector<double> wd, double bc1,
                  double bc2, c10::optional<torch::Tensor> compute_peers) {
   TORCH_CHECK(lr.size() == 5 && wd.size() == 5, "optim_apply: 5 labels");
+  TORCH_CHECK(grad_shard.scalar_type() == at::kFloat || grad_shard.scalar_type() == at::kBFloat16,
+              "optim_apply: fp32 or bf16 gradients");
   AhbOptimArgs a;
   for (int i = 0; i < 5; ++i) { a.lr[i] = (float)lr[i]; a.wd[i] = (float)wd[i]; }
   a.bc1 = (float)bc1;
@@ -822,7 +841,8 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
   }
   ahb_optim_apply(reinterpret_cast<const AhbSegInfo*>(segs.data_ptr<uint8_t>()), cstart.data_ptr<int>(),
                   (int)(cstart.numel() - 1), (int)nblocks, master.data_ptr<float>(), m.data_ptr<float>(),
-                  v.data_ptr<float>(), grad_shard.data_ptr<float>(), coef.data_ptr<float>(), compute.data_ptr(), fp, fe,
+                  v.data_ptr<float>(), grad_shard.data_ptr(), grad_shard.scalar_type() == at::kBFloat16,
+                  coef.data_ptr<float>(), compute.data_ptr(), fp, fe,
                   a, peer_table(compute_peers).first, peer_table(compute_peers).second, cur_stream());
   check_launch("ahb_optim_apply");
 }
@@ -1264,52 +1284,154 @@ void memcpy_async(int64_t dst, int64_t src, int64_t nbytes, int64_t stream) {
                                reinterpret_cast<cudaStream_t>(stream)) == 0, "memcpy_async failed");
 }
 
-// ------------------------------------------------------------ fused LM head + cross entropy
-// forward: logits = h W^T (bf16, tcgen05), then loss + dlogits in place.  Returns {sum_loss, count, dlogits, hpad}
-std::vector<torch::Tensor> ce_fused_fwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, double ls) {
-  TORCH_CHECK(h.is_cuda() && h.scalar_type() == at::kBFloat16 && h.dim() == 2, "ce: h bf16 (T,d)");
-  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.is_contiguous() && W.dim() == 2, "ce: W bf16 (V,d)");
-  const int64_t T = h.size(0), d = h.size(1), V = W.size(0);
-  TORCH_CHECK(W.size(1) == d && d % 256 == 0 && V % 64 == 0, "ce: d % 256 == 0 and V % 64 == 0");
-  const int64_t Tp = (T + 127) / 128 * 128;
-  auto hp = h.contiguous();
-  auto lab = labels.to(at::kLong).contiguous();
-  if (Tp != T) {
-    hp = torch::cat({hp, torch::zeros({Tp - T, d}, h.options())}, 0);
-    lab = torch::cat({lab, torch::full({Tp - T}, -100, lab.options())}, 0);
-  }
-  auto logits = torch::empty({Tp, V}, h.options());
-  auto off = torch::arange(0, Tp + 1, Tp, torch::dtype(torch::kInt32).device(h.device()));
-  int rc = ahb_moe_gemm(AHB_GEMM_DENSE, hp.data_ptr(), nullptr, Tp, d, W.data_ptr(), nullptr, V, d, 0,
-                        off.data_ptr<int>(), 1, (int)V, 0, (int)d, (int)(d / 64), logits.data_ptr(), nullptr, nullptr,
-                        nullptr, nullptr, 0.f, err_word().data_ptr<int>(), num_sms(), cur_stream());
-  gemm_check(rc, "ce logits");
-  auto acc = torch::zeros({2}, h.options().dtype(at::kFloat));
-  ahb_ce_rows(logits.data_ptr(), lab.data_ptr<int64_t>(), Tp, (int)V, (float)ls, acc.data_ptr<float>(),
-              acc.data_ptr<float>() + 1, cur_stream());
-  check_launch("ahb_ce_rows");
-  return {acc.narrow(0, 0, 1), acc.narrow(0, 1, 1), logits, hp};
+// ------------------------------------------------------------ dense projections (tcgen05 GEMM)
+// y = x W (+ b) for a kernel W (in, out), its input gradient dx (+)= dy W^T and its fp32 weight
+// gradient acc += x^T dy, on the grouped GEMM with one group (CTA pairs from 256 rows on).
+static bool dense_pair(int64_t M) { return moe_pair() && M >= 256; }
+
+// {0, M padded to `tile`} on the device, made once per (device, padded M) and kept: the grouped
+// GEMM reads its group offsets from device memory, and a fresh tensor per call would add a
+// launch to every projection (and an allocation inside captured graphs)
+static torch::Tensor dense_off(int64_t M, int64_t tile, const torch::Device& dev) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int64_t>, torch::Tensor> cache;
+  const int64_t Mp = (M + tile - 1) / tile * tile;
+  if (c10::cuda::currentStreamCaptureStatusMayInitCtx() != c10::cuda::CaptureStatus::None)  // a device write,
+    return torch::arange(0, Mp + 1, Mp, torch::dtype(torch::kInt32).device(dev));          // no host copy
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair((int)dev.index(), Mp);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto t = torch::tensor({0, (int)Mp}, torch::dtype(torch::kInt32)).to(dev);
+  cache.emplace(key, t);
+  return t;
 }
 
-// backward: dh = g * dlogits W ; dW_acc += g * dlogits^T h   (g: device scalar)
-torch::Tensor ce_fused_bwd(torch::Tensor dlogits, torch::Tensor hp, torch::Tensor W, torch::Tensor g,
-                           torch::Tensor dW_acc, int64_t T) {
-  const int64_t Tp = hp.size(0), d = hp.size(1), V = W.size(0);
+static void check_dense(const torch::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.is_contiguous(), "dense: ", n,
+              " must be a contiguous 2-D bf16 CUDA tensor");
+}
+
+torch::Tensor dense_fwd(torch::Tensor x, torch::Tensor W, c10::optional<torch::Tensor> bias) {
+  check_dense(x, "x");
+  check_dense(W, "W");
+  const int64_t M = x.size(0), K = x.size(1), N = W.size(1);
+  TORCH_CHECK(W.size(0) == K && K % 64 == 0 && N % 32 == 0, "dense_fwd: x (M,K), W (K,N), K % 64, N % 32");
+  torch::Tensor bc;
+  if (bias.has_value() && bias->defined()) {
+    bc = bias->to(at::kBFloat16).contiguous();
+    TORCH_CHECK(bc.numel() == N, "dense_fwd: bias of N elements");
+  }
+  const bool pair = dense_pair(M);
+  auto off = dense_off(M, pair ? 256 : 128, x.device());
+  auto y = torch::empty({M, N}, x.options());
+  int rc = ahb_dense_gemm(0, x.data_ptr(), W.data_ptr(), M, (int)K, (int)N, bc.defined() ? bc.data_ptr() : nullptr,
+                          nullptr, y.data_ptr(), off.data_ptr<int>(), err_word().data_ptr<int>(), num_sms(),
+                          cur_stream(), pair);
+  gemm_check(rc, "dense fwd");
+  return y;
+}
+
+// dx (M, in) = dy (M, out) W^T, plus dx's previous value when `accumulate`
+void dense_dgrad(torch::Tensor dy, torch::Tensor W, torch::Tensor dx, bool accumulate) {
+  check_dense(dy, "dy");
+  check_dense(W, "W");
+  check_dense(dx, "dx");
+  const int64_t M = dy.size(0), Nout = dy.size(1), Kin = W.size(0);
+  TORCH_CHECK(W.size(1) == Nout && dx.size(0) == M && dx.size(1) == Kin && Nout % 64 == 0 && Kin % 32 == 0,
+              "dense_dgrad: dy (M,out), W (in,out), dx (M,in), out % 64, in % 32");
+  const bool pair = dense_pair(M);
+  auto off = dense_off(M, pair ? 256 : 128, dy.device());
+  int rc = ahb_dense_gemm(1, dy.data_ptr(), W.data_ptr(), M, (int)Nout, (int)Kin, nullptr,
+                          accumulate ? dx.data_ptr() : nullptr, dx.data_ptr(), off.data_ptr<int>(),
+                          err_word().data_ptr<int>(), num_sms(), cur_stream(), pair);
+  gemm_check(rc, "dense dgrad");
+}
+
+// acc (in, out) fp32 += x (M, in)^T dy (M, out)
+void dense_wgrad(torch::Tensor x, torch::Tensor dy, torch::Tensor acc) {
+  check_dense(x, "x");
+  check_dense(dy, "dy");
+  const int64_t M = x.size(0), K = x.size(1), N = dy.size(1);
+  TORCH_CHECK(dy.size(0) == M && acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() &&
+                  acc.numel() == K * N && K % 128 == 0 && N % 32 == 0,
+              "dense_wgrad: x (M,in), dy (M,out), fp32 acc (in,out), in % 128, out % 32");
+  const bool pair = moe_pair() && K % 256 == 0;
+  auto off = dense_off(M, 64, x.device());
+  int rc = ahb_dense_gemm(2, x.data_ptr(), dy.data_ptr(), M, (int)K, (int)N, nullptr, nullptr, acc.data_ptr(),
+                          off.data_ptr<int>(), err_word().data_ptr<int>(), num_sms(), cur_stream(), pair);
+  gemm_check(rc, "dense wgrad");
+}
+
+// ------------------------------------------------------------ fused LM head + cross entropy
+// The logits h W^T exist only tile by tile inside the head GEMM.  Forward: per-(row, vocabulary
+// tile) partials from the GEMM epilogue, combined per row into lse and the summed loss; returns
+// {sum_loss, count, lse}.  Backward: for each chunk of at most `chunk_rows` rows the GEMM recomputes
+// the logits into bf16 dlogits (chunk x V), then dh = g dlogits W and dW_acc += g dlogits^T h.
+static bool ce_pair(int64_t rows) { return moe_pair() && rows >= 256; }
+
+std::vector<torch::Tensor> ce_online_fwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, double ls) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == at::kBFloat16 && h.dim() == 2 && h.is_contiguous(),
+              "ce: h contiguous bf16 (T,d)");
+  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.is_contiguous() && W.dim() == 2, "ce: W bf16 (V,d)");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == h.size(0),
+              "ce: labels contiguous int64 (T,)");
+  const int64_t T = h.size(0), d = h.size(1), V = W.size(0);
+  TORCH_CHECK(W.size(1) == d && d % 64 == 0 && V % 64 == 0, "ce: d % 64 == 0 and V % 64 == 0");
+  const bool pair = ce_pair(T);
+  const int64_t tile = pair ? 256 : 128, Tp = (T + tile - 1) / tile * tile;
+  const int ntiles = (int)((V + 255) / 256);
+  auto f32 = h.options().dtype(at::kFloat);
+  auto part = torch::empty({T, ntiles, 4}, f32);
+  auto off = dense_off(Tp, tile, h.device());
+  int rc = ahb_ce_gemm(false, h.data_ptr(), T, (int)d, W.data_ptr(), (int)V, off.data_ptr<int>(),
+                       labels.data_ptr<int64_t>(), nullptr, (float)ls, part.data_ptr(), err_word().data_ptr<int>(),
+                       num_sms(), cur_stream(), pair);
+  gemm_check(rc, "ce logits partials");
+  auto lse = torch::empty({T}, f32);
+  auto acc = torch::zeros({2}, f32);
+  ahb_ce_combine(part.data_ptr(), ntiles, labels.data_ptr<int64_t>(), T, (int)V, (float)ls, lse.data_ptr<float>(),
+                 acc.data_ptr<float>(), acc.data_ptr<float>() + 1, cur_stream());
+  check_launch("ahb_ce_combine");
+  return {acc.narrow(0, 0, 1), acc.narrow(0, 1, 1), lse};
+}
+
+torch::Tensor ce_online_bwd(torch::Tensor h, torch::Tensor W, torch::Tensor labels, torch::Tensor lse, double ls,
+                            torch::Tensor g, torch::Tensor dW_acc, int64_t chunk_rows) {
+  const int64_t T = h.size(0), d = h.size(1), V = W.size(0);
   check_acc(dW_acc, V * d, "dW_acc");
-  auto gc = g.to(at::kFloat).reshape({1}).contiguous();
-  auto off = torch::arange(0, Tp + 1, Tp, torch::dtype(torch::kInt32).device(hp.device()));
-  auto dh = torch::empty({Tp, d}, hp.options());
-  int* err = err_word().data_ptr<int>();
-  int rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN, dlogits.data_ptr(), nullptr, Tp, V, W.data_ptr(), nullptr, V, d, 0,
-                        off.data_ptr<int>(), 1, (int)d, 0, (int)V, (int)(V / 64), dh.data_ptr(), nullptr, nullptr,
-                        nullptr, nullptr, 0.f, err, num_sms(), cur_stream(), gc.data_ptr<float>());
-  gemm_check(rc, "ce dh");
   TORCH_CHECK(V % 128 == 0, "ce: V must be a multiple of 128 for the weight gradient");
-  rc = ahb_moe_gemm(AHB_GEMM_WGRAD, dlogits.data_ptr(), nullptr, Tp, V, hp.data_ptr(), nullptr, Tp, d, 0,
-                    off.data_ptr<int>(), 1, (int)d, (int)V, 0, 0, dW_acc.data_ptr<float>(), nullptr, nullptr, nullptr,
-                    nullptr, 0.f, err, num_sms(), cur_stream(), gc.data_ptr<float>());
-  gemm_check(rc, "ce dW");
-  return dh.narrow(0, 0, T);
+  TORCH_CHECK(chunk_rows >= 256 && chunk_rows % 256 == 0, "ce: chunk_rows a positive multiple of 256");
+  auto gc = g.to(at::kFloat).reshape({1}).contiguous();
+  auto dh = torch::empty({T, d}, h.options());
+  const int64_t cap = std::min<int64_t>(chunk_rows, (T + 255) / 256 * 256);
+  auto dl = torch::empty({cap, V}, h.options());
+  int* err = err_word().data_ptr<int>();
+  auto st = cur_stream();
+  const char* hb = static_cast<const char*>(h.data_ptr());
+  for (int64_t r0 = 0; r0 < T; r0 += chunk_rows) {
+    const int64_t rows = std::min<int64_t>(chunk_rows, T - r0);
+    const bool pair = ce_pair(rows);
+    const int64_t tile = pair ? 256 : 128, rp = (rows + tile - 1) / tile * tile;
+    auto off = dense_off(rp, tile, h.device());
+    const void* hc = hb + r0 * d * 2;
+    int rc = ahb_ce_gemm(true, hc, rows, (int)d, W.data_ptr(), (int)V, off.data_ptr<int>(),
+                         labels.data_ptr<int64_t>() + r0, lse.data_ptr<float>() + r0, (float)ls, dl.data_ptr(), err,
+                         num_sms(), st, pair);
+    gemm_check(rc, "ce dlogits");
+    // dh rows of the chunk (rows beyond it are not stored)
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN | (pair ? AHB_GEMM_PAIR : 0), dl.data_ptr(), nullptr, rp, V, W.data_ptr(),
+                      nullptr, V, d, 0, off.data_ptr<int>(), 1, (int)d, 0, (int)V, (int)(V / 64),
+                      static_cast<char*>(dh.data_ptr()) + r0 * d * 2, nullptr, nullptr, nullptr, nullptr, 0.f, err,
+                      num_sms(), st, gc.data_ptr<float>(), (int)rows);
+    gemm_check(rc, "ce dh");
+    // dW += dlogits^T h over the chunk's rows (the padding rows of dlogits are zero)
+    rc = ahb_moe_gemm(AHB_GEMM_WGRAD, dl.data_ptr(), nullptr, rp, V, hc, nullptr, rows, d, 0, off.data_ptr<int>(), 1,
+                      (int)d, (int)V, 0, 0, dW_acc.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr, 0.f, err,
+                      num_sms(), st, gc.data_ptr<float>());
+    gemm_check(rc, "ce dW");
+  }
+  return dh;
 }
 
 }  // namespace
@@ -1347,8 +1469,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_fwd", &moe_fwd);
   m.def("moe_bwd", &moe_bwd);
   m.def("optim_make_table", &optim_make_table);
-  m.def("ce_fused_fwd", &ce_fused_fwd);
-  m.def("ce_fused_bwd", &ce_fused_bwd);
+  m.def("dense_fwd", &dense_fwd, py::arg("x"), py::arg("W"), py::arg("bias") = py::none());
+  m.def("dense_dgrad", &dense_dgrad);
+  m.def("dense_wgrad", &dense_wgrad);
+  m.def("ce_online_fwd", &ce_online_fwd);
+  m.def("ce_online_bwd", &ce_online_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, py::arg("x"), py::arg("delta"), py::arg("scale"), py::arg("clip"),

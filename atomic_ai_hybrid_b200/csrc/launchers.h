@@ -79,6 +79,8 @@ int ahb_ssd_bwd_chunk_tc(const void* x, const void* dt, const float* A, const vo
 // or-ed into the kind: run the CTA-pair kernel (cta_group::2, 256 x 256 tiles); M-grouped
 // group offsets must then be multiples of 256 rows, K-grouped Mout a multiple of 256
 #define AHB_GEMM_PAIR 0x100
+// or-ed into a weight-gradient kind: the accumulators are bf16 (fp32 sums rounded once per add)
+#define AHB_GEMM_ACC_BF16 0x200
 int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64_t a_cols, const void* b0,
                  const void* b1, int64_t b_rows_total, int64_t b_cols, int b_rows_per_group, const int* grp_off,
                  int E, int N, int Mout, int K, int kb_split, void* out0, void* out1, void* out2, const void* aux0,
@@ -121,11 +123,12 @@ struct AhbOptimArgs {
   float bc1, bc2;
 };
 int ahb_optim_chunk();
-void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
+// grad: fp32, or bf16 with grad_bf16 (a store with 16-bit gradient accumulators)
+void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, void* grad, bool grad_bf16,
                        const float* master, float inv, double* red, int* flags, const float* const* gpeers,
                        int npeers, int64_t lo, cudaStream_t st);
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
-                     const float* grad, const float* coef, void* compute, const float* frac, int fracE,
+                     const void* grad, bool grad_bf16, const float* coef, void* compute, const float* frac, int fracE,
                      AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st);
 
 // fused_norm.cu: residual add + clip + RMSNorm, RMSNorm x SiLU gate, GDN gates, per-head L2 norm, Mamba2 dt
@@ -211,5 +214,15 @@ void ahb_copy_out(const void* src, void* const* peers_dev, int world, int64_t of
                   cudaStream_t st);
 
 // ce.cu: label-smoothed cross entropy over bf16 logits rows, gradient written in place
-void ahb_ce_rows(void* logits, const int64_t* labels, int64_t R, int V, float ls, float* loss_sum, float* count,
-                 cudaStream_t st);
+// Dense projections on the grouped GEMM (moe_gemm.cu): mode 0 y = x W (+ bias) (+ beta_src), mode 1
+// y = dy W^T (+ beta_src), mode 2 acc fp32 += x^T dy; grp_off = {0, M padded to the tile height}
+int ahb_dense_gemm(int mode, const void* a, const void* b, int64_t M, int K, int N, const void* bias,
+                   const void* beta_src, void* out, const int* grp_off, int* err, int num_sms, cudaStream_t st,
+                   bool pair);
+// LM-head GEMM with a cross-entropy epilogue (moe_gemm.cu; see there), and the row combine of its
+// forward partials: lse per row, sum of the label-smoothed losses and of the valid rows (ce.cu)
+int ahb_ce_gemm(bool bwd, const void* h, int64_t rows, int d, const void* W, int V, const int* grp_off,
+                const int64_t* labels, const float* lse, float ls, void* out, int* err, int num_sms, cudaStream_t st,
+                bool pair);
+void ahb_ce_combine(const void* partials, int ntiles, const int64_t* labels, int64_t T, int V, float ls, float* lse,
+                    float* loss_sum, float* count, cudaStream_t st);

@@ -36,7 +36,7 @@ constexpr int B_BYTES = 256 * BK * 2;  // 32 KB (NB * BNacc = 256 columns)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_GELU_FWD = 2, EPI_SWIGLU_BWD = 3, EPI_GELU_BWD = 4, EPI_ACC = 5,
-           EPI_STORE_PEER = 6 };
+           EPI_STORE_PEER = 6, EPI_CE_FWD = 7, EPI_CE_BWD = 8 };
 
 constexpr int MAX_PEERS = 8;
 // EPI_STORE_PEER stages each warp's 32 x 256 output rows in shared memory and writes every row
@@ -68,6 +68,17 @@ struct Params {
   void* out_tab[MAX_PEERS];
   int m_rot;
   int m_limit;  // M-grouped: rows at or beyond it are not stored (0: every row of the padded groups)
+  // LM-head cross entropy (EPI_CE_*): token labels (-100 = masked), row log-sum-exp (backward),
+  // label smoothing weights sp = 1 - ls and sn = ls / (V - 1), vocabulary tiles per row
+  const int64_t* labels;
+  const float* row_lse;
+  float ce_sp, ce_sn;
+  int ce_tiles;
+  // EPI_STORE extras (dense projections): bias per output column, and a bf16 matrix of the
+  // output's shape added to the product (accumulation over several launches, beta = 1)
+  const bf16* bias;
+  const bf16* beta_src;
+  int acc_bf16;  // EPI_ACC into bf16 accumulators (AHB_GEMM_ACC_BF16)
 };
 
 AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
@@ -94,6 +105,17 @@ AHB_DEVICE void store_bf16x32(bf16* dst, const float* v) {
     w.w = *reinterpret_cast<uint32_t*>(&p3);
     *reinterpret_cast<uint4*>(dst + i) = w;
   }
+}
+
+// 32 consecutive bf16 accumulators += alpha * v (read, add in fp32, round once)
+AHB_DEVICE void acc_add_bf16(bf16* d, const float* v, float alpha) {
+  bf16 cur[32];
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(cur + i) = *reinterpret_cast<const uint4*>(d + i);
+  float o[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o[i] = __bfloat162float(cur[i]) + alpha * v[i];
+  store_bf16x32(d, o);
 }
 
 struct Tile {
@@ -136,6 +158,56 @@ AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, ui
   const int n0 = t.n0 * BNA;
   const bool live = p.m_limit <= 0 || row < p.m_limit;
   const float alpha = p.alpha ? *p.alpha : 1.f;
+  if constexpr (EPI == EPI_CE_FWD || EPI == EPI_CE_BWD) {
+    // logits of this row over the tile's vocabulary columns, rounded to bf16 and clipped as the
+    // row kernel of the unfused head reads them (reference `optimizer.py:244-312`)
+    const int64_t lab = live ? p.labels[row] : -100;
+    const bool valid = lab != -100;
+    const int y = valid ? (int)(lab < 0 ? 0 : (lab >= p.N ? p.N - 1 : lab)) : -1;
+    if constexpr (EPI == EPI_CE_FWD) {
+      // per-row partials of this tile: running max, sum of e^{z - max}, z at the label, sum of z
+      float m = -INFINITY, s = 0.f, zs = 0.f, zy = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BNA / 32; ++c) {
+        const int col = n0 + c * 32;
+        if (col >= p.N) break;
+        float v[32];
+        tmem_ld32(tb + c * 32, v);
+        float cm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = sanitize(__bfloat162float(__float2bfloat16_rn(v[i])), 1e4f);
+          cm = fmaxf(cm, v[i]);
+          zs += v[i];
+          if (col + i == y) zy = v[i];
+        }
+        const float mn = fmaxf(m, cm);
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) a += __expf(v[i] - mn);
+        s = s * __expf(m - mn) + a;
+        m = mn;
+      }
+      if (live) reinterpret_cast<float4*>(p.out0)[static_cast<int64_t>(row) * p.ce_tiles + t.n0] = make_float4(m, s, zy, zs);
+    } else {
+      // d loss_row / d z = softmax - sn - (sp - sn) [v == y]; zero on masked and padding rows
+      const float lse = valid ? p.row_lse[row] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BNA / 32; ++c) {
+        const int col = n0 + c * 32;
+        if (col >= p.N) break;
+        float v[32];
+        tmem_ld32(tb + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float z = sanitize(__bfloat162float(__float2bfloat16_rn(v[i])), 1e4f);
+          v[i] = valid ? __expf(z - lse) - p.ce_sn - (col + i == y ? p.ce_sp - p.ce_sn : 0.f) : 0.f;
+        }
+        store_bf16x32(static_cast<bf16*>(p.out0) + static_cast<int64_t>(row) * p.N + col, v);
+      }
+    }
+    return;
+  }
   if constexpr (EPI == EPI_STORE_PEER) {
     bf16* stg = reinterpret_cast<bf16*>(stg_base) + q * 32 * STG_LD;
 #pragma unroll 1
@@ -166,8 +238,24 @@ AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, ui
     const int64_t o = static_cast<int64_t>(row) * p.N + col;
     if constexpr (EPI == EPI_STORE) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i] * alpha, p.clip);
-      store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
+      for (int i = 0; i < 32; ++i) v0[i] = v0[i] * alpha;
+      if (p.bias) {
+        bf16 bv[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(bv + i) = *reinterpret_cast<const uint4*>(p.bias + col + i);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v0[i] += __bfloat162float(bv[i]);
+      }
+      if (p.beta_src && live) {
+        bf16 sv[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) *reinterpret_cast<uint4*>(sv + i) = *reinterpret_cast<const uint4*>(p.beta_src + o + i);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v0[i] += __bfloat162float(sv[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v0[i] = clampf(v0[i], p.clip);
+      if (live) store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
     } else if constexpr (EPI == EPI_SWIGLU_FWD) {
       float v1[32], h[32];
       tmem_ld32(tb + BNA + c * 32, v1);
@@ -213,24 +301,32 @@ AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, ui
 #pragma unroll
       for (int i = 0; i < 32; ++i) v0[i] *= gelu_t_grad(__bfloat162float(a1v[i]));
       store_bf16x32(static_cast<bf16*>(p.out0) + o, v0);
-    } else {  // EPI_ACC: out_e[row, col] += acc  (fp32, (E, Mout, N))
+    } else {  // EPI_ACC: out_e[row, col] += acc  ((E, Mout, N), fp32 or, with acc_bf16, bf16)
       const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
-      float* d0p = static_cast<float*>(p.out0) + oo;
+      if (p.acc_bf16) {  // the product summed in fp32, rounded once as it is added
+        acc_add_bf16(static_cast<bf16*>(p.out0) + oo, v0, alpha);
+      } else {
+        float* d0p = static_cast<float*>(p.out0) + oo;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float4 x = *reinterpret_cast<float4*>(d0p + i);
-        x.x += alpha * v0[i]; x.y += alpha * v0[i + 1]; x.z += alpha * v0[i + 2]; x.w += alpha * v0[i + 3];
-        *reinterpret_cast<float4*>(d0p + i) = x;
+        for (int i = 0; i < 32; i += 4) {
+          float4 x = *reinterpret_cast<float4*>(d0p + i);
+          x.x += alpha * v0[i]; x.y += alpha * v0[i + 1]; x.z += alpha * v0[i + 2]; x.w += alpha * v0[i + 3];
+          *reinterpret_cast<float4*>(d0p + i) = x;
+        }
       }
       if constexpr (NB == 2) {
         float v1[32];
         tmem_ld32(tb + BNA + c * 32, v1);
-        float* d1p = static_cast<float*>(p.out1) + oo;
+        if (p.acc_bf16) {
+          acc_add_bf16(static_cast<bf16*>(p.out1) + oo, v1, alpha);
+        } else {
+          float* d1p = static_cast<float*>(p.out1) + oo;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          float4 x = *reinterpret_cast<float4*>(d1p + i);
-          x.x += alpha * v1[i]; x.y += alpha * v1[i + 1]; x.z += alpha * v1[i + 2]; x.w += alpha * v1[i + 3];
-          *reinterpret_cast<float4*>(d1p + i) = x;
+          for (int i = 0; i < 32; i += 4) {
+            float4 x = *reinterpret_cast<float4*>(d1p + i);
+            x.x += alpha * v1[i]; x.y += alpha * v1[i + 1]; x.z += alpha * v1[i + 2]; x.w += alpha * v1[i + 3];
+            *reinterpret_cast<float4*>(d1p + i) = x;
+          }
         }
       }
     }
@@ -682,7 +778,8 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
                  const void* aux1, float clip, int* err, int num_sms, cudaStream_t st, const float* alpha,
                  int m_limit) {
   const bool pair = (kind & AHB_GEMM_PAIR) != 0;
-  kind &= ~AHB_GEMM_PAIR;
+  const bool acc16 = (kind & AHB_GEMM_ACC_BF16) != 0;
+  kind &= ~(AHB_GEMM_PAIR | AHB_GEMM_ACC_BF16);
   if (E < 1 || E > 192 || N % 32 != 0 || K % 64 != 0) return -10;  // offsets live in the kernel's smem tail
   Params p;
   memset(&p, 0, sizeof(p));
@@ -702,12 +799,16 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
   p.alpha = alpha;
   p.err = err;
   p.m_limit = m_limit;
+  p.acc_bf16 = acc16 ? 1 : 0;
   const bool kg = kind == AHB_GEMM_WGRAD || kind == AHB_GEMM_WGRAD_DUAL;
   const bool a_mn = kg;
   const bool b_mn = kg || kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_FWD_GELU || kind == AHB_GEMM_FWD_DOWN;
   const int nb = (kind == AHB_GEMM_FWD_SWIGLU || kind == AHB_GEMM_WGRAD_DUAL) ? 2 : 1;
   const int bna = 256 / nb;
-  if (N % bna != 0 && kind != AHB_GEMM_DENSE && kind != AHB_GEMM_FWD_DOWN) return -11;
+  // a partial last column tile is fine where the epilogue stops at N (store, fp32 accumulate)
+  if (N % bna != 0 && kind != AHB_GEMM_DENSE && kind != AHB_GEMM_FWD_DOWN && kind != AHB_GEMM_DX &&
+      kind != AHB_GEMM_WGRAD)
+    return -11;
   if (kg && Mout % (pair ? PAIR_BM : BM) != 0) return -12;
   // a CTA of a pair loads half of each accumulator's columns of B
   const int b_box = b_mn ? 64 : (pair ? bna / 2 : bna);
@@ -747,6 +848,96 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
     case AHB_GEMM_WGRAD_DUAL: return launch<true, true, true, 2, EPI_ACC>(p, grid, st);
     default: return -30;
   }
+}
+
+// Dense projection pieces on the grouped GEMM (one group; rows padded to the tile height, rows
+// at or beyond M read as zeros and not stored):
+//   mode 0  y = x W (+ bias) (+ beta_src)    x (M,K) K-major, W (K,N) MN-major
+//   mode 1  y = dy W^T (+ beta_src)          dy (M,K) K-major, W (N,K) K-major (W^T of an (N,K) kernel)
+//   mode 2  acc (K,N) fp32 += x^T dy          x (M,K), dy (M,N), contraction over the M rows
+int ahb_dense_gemm(int mode, const void* a, const void* b, int64_t M, int K, int N, const void* bias,
+                   const void* beta_src, void* out, const int* grp_off, int* err, int num_sms, cudaStream_t st,
+                   bool pair) {
+  if (K % BK != 0 || N % 32 != 0 || M <= 0) return -10;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.grp_off = grp_off;
+  p.E = 1;
+  p.N = N;
+  p.err = err;
+  p.out0 = out;
+  p.bias = static_cast<const bf16*>(bias);
+  p.beta_src = static_cast<const bf16*>(beta_src);
+  int rc = 0;
+  if (mode == 2) {  // K-grouped: Mout = K rows of the weight, contraction over the M token rows
+    if (K % (pair ? PAIR_BM : BM) != 0) return -12;
+    p.Mout = K;
+    rc |= make_map(&p.ta0, a, M, K, K, 64);
+    rc |= make_map(&p.tb0, b, M, N, N, 64);
+  } else {
+    p.kb_split = K / BK;
+    p.kb_total = K / BK;
+    p.m_limit = (int)M;
+    rc |= make_map(&p.ta0, a, M, K, K, BM);
+    if (mode == 0) rc |= make_map(&p.tb0, b, K, N, N, 64);      // W (K rows, N cols), MN-major
+    else rc |= make_map(&p.tb0, b, N, K, K, pair ? 128 : 256);   // W (N rows, K cols), K-major
+    p.b_rows = mode == 0 ? K : N;
+  }
+  if (rc) return -20;
+  p.ta1 = p.ta0;
+  p.tb1 = p.tb0;
+  const int g2 = (num_sms / 2) * 2;
+  if (pair) {
+    switch (mode) {
+      case 0: return launch_pair<false, false, true, 1, EPI_STORE>(p, g2, st);
+      case 1: return launch_pair<false, false, false, 1, EPI_STORE>(p, g2, st);
+      default: return launch_pair<true, true, true, 1, EPI_ACC>(p, g2, st);
+    }
+  }
+  switch (mode) {
+    case 0: return launch<false, false, true, 1, EPI_STORE>(p, num_sms, st);
+    case 1: return launch<false, false, false, 1, EPI_STORE>(p, num_sms, st);
+    default: return launch<true, true, true, 1, EPI_ACC>(p, num_sms, st);
+  }
+}
+
+// LM-head GEMM logits = h W^T (h: rows x d, W: V x d, both K-major) with a cross-entropy epilogue that
+// never stores the logits: `bwd` false writes per-(row, 256-column tile) partials (max, sum-exp,
+// label logit, logit sum) as float4 [rows][ce_tiles]; `bwd` true writes bf16 dlogits [rows_pad][V]
+// (zeros on masked rows and rows at or beyond `rows`).  Rows are padded to the tile height (256
+// with `pair`): h rows beyond `rows` read as zeros.
+int ahb_ce_gemm(bool bwd, const void* h, int64_t rows, int d, const void* W, int V, const int* grp_off,
+                const int64_t* labels, const float* lse, float ls, void* out, int* err, int num_sms, cudaStream_t st,
+                bool pair) {
+  if (d % BK != 0 || V % 32 != 0 || rows <= 0) return -10;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.grp_off = grp_off;
+  p.E = 1;
+  p.N = V;
+  p.kb_split = d / BK;
+  p.kb_total = d / BK;
+  p.b_rows = 0;
+  p.out0 = out;
+  p.err = err;
+  p.m_limit = (int)rows;
+  p.labels = labels;
+  p.row_lse = lse;
+  p.ce_sp = 1.f - ls;
+  p.ce_sn = ls > 0.f ? ls / (float)(V - 1) : 0.f;
+  p.ce_tiles = (V + 255) / 256;
+  int rc = make_map(&p.ta0, h, rows, d, d, BM);
+  rc |= make_map(&p.tb0, W, V, d, d, pair ? 128 : 256);
+  if (rc) return -20;
+  p.ta1 = p.ta0;
+  p.tb1 = p.tb0;
+  if (pair) {
+    const int grid = (num_sms / 2) * 2;
+    return bwd ? launch_pair<false, false, false, 1, EPI_CE_BWD>(p, grid, st)
+               : launch_pair<false, false, false, 1, EPI_CE_FWD>(p, grid, st);
+  }
+  return bwd ? launch<false, false, false, 1, EPI_CE_BWD>(p, num_sms, st)
+             : launch<false, false, false, 1, EPI_CE_FWD>(p, num_sms, st);
 }
 
 // GEMM -> reduce-scatter over peer memory: out rows of group g (rows [grp_off[g], grp_off[g+1]) of A)

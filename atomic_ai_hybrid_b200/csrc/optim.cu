@@ -38,9 +38,14 @@ AHB_DEVICE int find_seg(const int* cstart, int S, int b) {
   return lo;
 }
 
+AHB_DEVICE void put_g(float* p, float v) { *p = v; }
+AHB_DEVICE void put_g(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// G: gradient element type (fp32, or bf16 for a store whose accumulators are 16-bit)
+template <typename G>
 __global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo* __restrict__ segs,
                                                                 const int* __restrict__ cstart, int S,
-                                                                float* __restrict__ grad,
+                                                                G* __restrict__ grad,
                                                                 const float* __restrict__ master, float inv,
                                                                 double* __restrict__ red, int* __restrict__ flags,
                                                                 const float* const* __restrict__ gpeers, int npeers,
@@ -64,13 +69,13 @@ __global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo
         for (int r = 0; r < npeers; ++r) a += gpeers[r][lo + idx];
         a *= inv;
       } else {
-        a = grad[idx] * inv;
+        a = to_f(grad[idx]) * inv;
       }
       sa += a * a;
       const bool fin = isfinite(a);
       nonfin |= !fin;
       const float g = (fin ? a : 0.f) * sg.gscale;
-      grad[idx] = g;
+      put_g(grad + idx, g);
       sgq += g * g;
     }
     clipped |= fabsf(master[idx]) >= 100.f;
@@ -87,10 +92,11 @@ __global__ void __launch_bounds__(THREADS) optim_prepare_kernel(const AhbSegInfo
 
 AHB_DEVICE float signf_(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
+template <typename G>
 __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* __restrict__ segs,
                                                               const int* __restrict__ cstart, int S,
                                                               float* __restrict__ master, float* __restrict__ m,
-                                                              float* __restrict__ v, const float* __restrict__ grad,
+                                                              float* __restrict__ v, const G* __restrict__ grad,
                                                               const float* __restrict__ coef_p,
                                                               uint16_t* __restrict__ compute,
                                                               const float* __restrict__ frac, int fracE,
@@ -111,17 +117,17 @@ __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* 
     const int64_t idx = sg.off + j;
     float p = master[idx];
     if (lab == AHB_LABEL_MUON) {
-      if (rg) p += -lr * grad[idx] - lr * wd * p;
+      if (rg) p += -lr * to_f(grad[idx]) - lr * wd * p;
     } else if (lab == AHB_LABEL_LION) {
       if (rg) {
-        const float g = grad[idx] * coef;
+        const float g = to_f(grad[idx]) * coef;
         const float mm = m[idx];
         const float u = signf_(0.1f * g + 0.9f * mm) + wd * p;
         m[idx] = 0.99f * mm + 0.01f * g;
         p -= lr * u;
       }
     } else if (lab == AHB_LABEL_ADAMW_DECAY || lab == AHB_LABEL_ADAMW_NODECAY) {
-      const float g = rg ? grad[idx] * coef : 0.f;
+      const float g = rg ? to_f(grad[idx]) * coef : 0.f;
       const float mm = 0.9f * m[idx] + 0.1f * g;
       const float vv = 0.999f * v[idx] + 0.001f * g * g;
       m[idx] = mm;
@@ -153,20 +159,30 @@ __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* 
 
 }  // namespace
 
-void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* grad,
+void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, void* grad, bool grad_bf16,
                        const float* master, float inv, double* red, int* flags, const float* const* gpeers,
                        int npeers, int64_t lo, cudaStream_t st) {
   if (nblocks <= 0) return;
-  optim_prepare_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, grad, master, inv, red, flags, gpeers, npeers,
-                                                    lo);
+  if (grad_bf16)
+    optim_prepare_kernel<bf16><<<nblocks, THREADS, 0, st>>>(segs, cstart, S, (bf16*)grad, master, inv, red, flags,
+                                                            gpeers, npeers, lo);
+  else
+    optim_prepare_kernel<float><<<nblocks, THREADS, 0, st>>>(segs, cstart, S, (float*)grad, master, inv, red, flags,
+                                                             gpeers, npeers, lo);
 }
 
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
-                     const float* grad, const float* coef, void* compute, const float* frac, int fracE,
+                     const void* grad, bool grad_bf16, const float* coef, void* compute, const float* frac, int fracE,
                      AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st) {
   if (nblocks <= 0) return;
-  optim_apply_kernel<<<nblocks, THREADS, 0, st>>>(segs, cstart, S, master, m, v, grad, coef, (uint16_t*)compute,
-                                                  frac, fracE, args, (uint16_t* const*)cpeers, npeers);
+  if (grad_bf16)
+    optim_apply_kernel<bf16><<<nblocks, THREADS, 0, st>>>(segs, cstart, S, master, m, v, (const bf16*)grad, coef,
+                                                          (uint16_t*)compute, frac, fracE, args,
+                                                          (uint16_t* const*)cpeers, npeers);
+  else
+    optim_apply_kernel<float><<<nblocks, THREADS, 0, st>>>(segs, cstart, S, master, m, v, (const float*)grad, coef,
+                                                           (uint16_t*)compute, frac, fracE, args,
+                                                           (uint16_t* const*)cpeers, npeers);
 }
 
 int ahb_optim_chunk() { return CHUNK; }

@@ -23,7 +23,7 @@ class _Counted:
             return fn
 
         def call(*a, **k):
-            launch_counter.add(name)
+            launch_counter.add(name, a, k)
             return fn(*a, **k)
         return call
 

@@ -297,25 +297,35 @@ def grouped_ffn(x_sorted, group_sizes, w1, w2, w3, act):
                          None if w3 is None else w3.to(dt), act)
 
 
+# rows per backward chunk of the LM head: the chunk's bf16 dlogits (rows x V) are the head's only
+# vocabulary-wide buffer (8192 x 50304: 824 MB); the forward stores no logits at all
+CE_CHUNK_ROWS = int(os.environ.get("AHB_CE_CHUNK_ROWS", "8192"))
+
+
 class _FusedCE(torch.autograd.Function):
-    """Tied LM head + label-smoothed CE: bf16 logits from the tcgen05 GEMM (as the
-    reference computes them), loss and dlogits in one pass, then dh and the fp32
-    weight gradient from two more GEMMs in backward."""
+    """Tied LM head + label-smoothed CE that never stores the logits: the tcgen05 head GEMM
+    reduces each (row, 256-column vocabulary tile) to online-softmax partials in its epilogue
+    and a combine kernel forms the row log-sum-exp and the loss; the backward recomputes the
+    logits tile by tile into dlogits for one row chunk at a time, followed by the dh and fp32
+    weight-gradient GEMMs (reference `optimizer.py:244-312`, chunked cross entropy)."""
 
     @staticmethod
     def forward(ctx, h, labels, weight, ls):
         wb = weight if weight.dtype == torch.bfloat16 else weight.to(torch.bfloat16)
-        sum_loss, count, dlogits, hp = ext().ce_fused_fwd(h.to(torch.bfloat16), wb.contiguous(), labels, ls)
-        ctx.save_for_backward(dlogits, hp)
-        ctx.weight, ctx.wb, ctx.T = weight, wb, h.shape[0]
+        wb = wb.contiguous()
+        hb = h.to(torch.bfloat16).contiguous()
+        lab = labels.to(torch.long).contiguous()
+        sum_loss, count, lse = ext().ce_online_fwd(hb, wb, lab, ls)
+        ctx.save_for_backward(hb, lab, lse)
+        ctx.weight, ctx.wb, ctx.ls = weight, wb, ls
         ctx.hdtype = h.dtype
         return sum_loss.reshape(()), count.reshape(())
 
     @staticmethod
     def backward(ctx, g_loss, g_count):
-        dlogits, hp = ctx.saved_tensors
+        hb, lab, lse = ctx.saved_tensors
         acc, direct = _acc_for(ctx.weight)
-        dh = ext().ce_fused_bwd(dlogits, hp, ctx.wb.contiguous(), g_loss.reshape(1), acc, ctx.T)
+        dh = ext().ce_online_bwd(hb, ctx.wb, lab, lse, ctx.ls, g_loss.reshape(1), acc, CE_CHUNK_ROWS)
         return dh.to(ctx.hdtype), None, _ret_grad(ctx.weight, acc, direct), None
 
 
@@ -451,10 +461,22 @@ def dt_act(u):
 _ADDMM_F32 = None  # whether cuBLAS accumulates bf16 products straight into fp32 (probed once)
 
 
+def _dense_ok(x2, w) -> bool:
+    """Shapes and types the tcgen05 dense GEMM takes for ``x2 (M, K) @ w (K, N)``."""
+    return (x2.is_cuda and x2.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.dim() == 2
+            and w.shape[0] % 64 == 0 and w.shape[1] % 32 == 0)
+
+
 def _wgrad_acc(acc, x2, dy2):
-    """``acc (in, out) fp32 += x2^T dy2`` with bf16 inputs, accumulated by the GEMM
-    itself (beta = 1, fp32 output) when the library offers it."""
+    """``acc (in, out) fp32 += x2^T dy2`` with bf16 inputs: the tcgen05 K-grouped GEMM adds into
+    the fp32 accumulator in its epilogue; shapes it does not cover run one library GEMM with
+    beta = 1 and fp32 output."""
     global _ADDMM_F32
+    if (x2.is_cuda and x2.dtype == torch.bfloat16 and dy2.dtype == torch.bfloat16 and acc.dtype == torch.float32
+            and acc.is_contiguous() and x2.shape[1] % 128 == 0 and dy2.shape[1] % 32 == 0):
+        ext().dense_wgrad(x2.contiguous(), dy2.contiguous(), acc)
+        return
+    _unsupported(f"dense weight gradient in={x2.shape[1]} out={dy2.shape[1]}")
     if _ADDMM_F32 is not False:
         try:
             torch.addmm(acc, x2.t(), dy2, out_dtype=torch.float32, out=acc)
@@ -478,10 +500,12 @@ def bias_grad(b, dy2):
 
 
 class _MultiLinear(torch.autograd.Function):
-    """Several projections of one input, ``y_i = x W_i (+ b_i)`` (cuBLAS).  The
-    backward accumulates ``dx = sum_i dy_i W_i^T`` in one buffer (beta = 1) instead of
-    separate gradients that autograd adds, and adds the weight gradients of
-    store-backed matrices straight into their fp32 accumulators."""
+    """Several projections of one input, ``y_i = x W_i (+ b_i)``, on the tcgen05 dense GEMM
+    (CTA pairs, bias added in the epilogue; reference `model.py:405-427,575-613`).  The
+    backward accumulates ``dx = sum_i dy_i W_i^T`` in one buffer (each GEMM after the first
+    adds the previous value in its epilogue) and adds the weight gradients of store-backed
+    matrices straight into their fp32 accumulators from the GEMM epilogue.  Shapes the kernel
+    does not cover (in % 64, out % 32) run library GEMMs."""
 
     @staticmethod
     def forward(ctx, x, n, *wb):
@@ -490,7 +514,11 @@ class _MultiLinear(torch.autograd.Function):
         outs = []
         for w, b in zip(ws, bs):
             wc = w if w.dtype == x.dtype else w.to(x.dtype)
-            y = torch.addmm(b.to(x.dtype), x2, wc) if b is not None else torch.mm(x2, wc)
+            if _dense_ok(x2, wc):
+                y = ext().dense_fwd(x2.contiguous(), wc.contiguous(), b)
+            else:
+                _unsupported(f"dense projection in={wc.shape[0]} out={wc.shape[1]}")
+                y = torch.addmm(b.to(x.dtype), x2, wc) if b is not None else torch.mm(x2, wc)
             outs.append(y.view(*x.shape[:-1], w.shape[1]))
         ctx.save_for_backward(x, *ws)
         ctx.n, ctx.has_b = n, [b is not None for b in bs]
@@ -509,10 +537,17 @@ class _MultiLinear(torch.autograd.Function):
                 dws.append(None)
                 dbs.append(None)
                 continue
-            dy2 = dy.reshape(-1, dy.shape[-1]).to(x.dtype)
+            dy2 = dy.reshape(-1, dy.shape[-1]).to(x.dtype).contiguous()
             wc = w if w.dtype == x.dtype else w.to(x.dtype)
             if ctx.needs_input_grad[0]:
-                if dx is None:
+                if dy2.is_cuda and dy2.dtype == torch.bfloat16 and wc.dtype == torch.bfloat16 and \
+                        wc.shape[1] % 64 == 0 and wc.shape[0] % 32 == 0:
+                    first = dx is None
+                    if first:
+                        dx = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+                    ext().dense_dgrad(dy2, wc.contiguous(), dx, not first)
+                elif dx is None:
+                    _unsupported(f"dense input gradient in={wc.shape[0]} out={wc.shape[1]}")
                     dx = torch.mm(dy2, wc.t())
                 else:
                     torch.addmm(dx, dy2, wc.t(), out=dx)
@@ -521,7 +556,9 @@ class _MultiLinear(torch.autograd.Function):
                 _wgrad_acc(acc.view(w.shape), x2, dy2)
                 dws.append(None)
             else:
-                dws.append((x2.t() @ dy2).to(w.dtype))
+                g32 = torch.zeros(w.shape, dtype=torch.float32, device=x.device)
+                _wgrad_acc(g32, x2, dy2)
+                dws.append(g32.to(w.dtype))
             dbs.append(bias_grad(b_params[len(dbs)], dy2) if hb else None)
         if dx is not None:
             dx = dx.view(x.shape)

@@ -158,7 +158,7 @@ class HybridOptimizer:
             if not s.param.requires_grad:
                 continue
             sl = self._sl(s)
-            avg = gbuf[sl] * inv
+            avg = gbuf[sl].float() * inv
             red[0] += avg.double().square().sum().float() * self.norm_share
             if not torch.isfinite(avg).all():
                 red[3 + self.group_idx[diag_group_of(s.name)]] = 1.0
@@ -181,7 +181,7 @@ class HybridOptimizer:
         for s in self.owned:
             if s.label == "muon" and s.param.requires_grad:
                 sl = self._sl(s)
-                g = (gbuf[sl] * coef).view(s.shape)
+                g = (gbuf[sl].float() * coef).view(s.shape)
                 gbuf[sl] = _muon_direction(s, g, ns).reshape(-1)
         if use_k:
             K.optim_apply(self, lrs, coef, assignment_frac)  # also writes the compute copy
@@ -215,16 +215,16 @@ class HybridOptimizer:
             lab = s.label
             lr = lrs[lab]
             if lab == "muon" and s.param.requires_grad:
-                p.add_(-lr * gbuf[sl] - lr * 0.01 * p)
+                p.add_(-lr * gbuf[sl].float() - lr * 0.01 * p)
             elif lab == "lion" and s.param.requires_grad:
-                g = gbuf[sl] * coef
+                g = gbuf[sl].float() * coef
                 m = self._stage(self.m, sl, p.device)
                 upd = torch.sign(0.1 * g + 0.9 * m) + 0.1 * p
                 m.mul_(0.99).add_(0.01 * g)
                 p.add_(-lr * upd)
                 self._unstage(self.m, sl, m)
             elif lab.startswith("adamw"):
-                g = gbuf[sl] * coef if s.param.requires_grad else torch.zeros_like(p)
+                g = gbuf[sl].float() * coef if s.param.requires_grad else torch.zeros_like(p)
                 m, v = self._stage(self.m, sl, p.device), self._stage(self.v, sl, p.device)
                 m.mul_(0.9).add_(0.1 * g)
                 v.mul_(0.999).add_(0.001 * g * g)

@@ -69,7 +69,13 @@ class FlatParamStore:
                  grad_scale_fn: Callable[[str], float], world: int = 1, rank: int = 0,
                  compute_dtype: torch.dtype = torch.bfloat16, device=None,
                  keep_fp32: Callable[[str, torch.Tensor], bool] = default_keep_fp32,
-                 param_filter: Optional[Callable[[str, torch.Tensor], bool]] = None):
+                 param_filter: Optional[Callable[[str, torch.Tensor], bool]] = None,
+                 grad_dtype: torch.dtype = torch.float32):
+        # ``grad_dtype`` bf16: 16-bit gradient accumulators (each weight-gradient GEMM sums in
+        # fp32 and rounds once as it adds); only for stores whose gradients come from kernels
+        # that accumulate into bf16 (the expert-parallel experts)
+        if grad_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"gradient accumulators are fp32 or bf16, not {grad_dtype}")
         self.world, self.rank = world, rank
         self.compute_dtype = compute_dtype
         named = [(n, p) for n, p in model.named_parameters() if param_filter is None or param_filter(n, p)]
@@ -106,7 +112,7 @@ class FlatParamStore:
         half = torch.float32 if all32 else compute_dtype
         self.half_dtype = torch.bfloat16 if half == torch.float32 else half
         self.master = torch.zeros(self.shard, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.grad = torch.zeros(self.numel, dtype=grad_dtype, device=device)
         self.compute = torch.zeros(self.cnumel, dtype=self.half_dtype, device=device)
         self._hooks = []
         for s in self.segs:
@@ -143,9 +149,9 @@ class FlatParamStore:
             return
         g = self.grad_view(s)
         p._ahb_grad_acc = g
-        if s.fp32:
+        if s.fp32 and g.dtype == torch.float32:
             p.grad = g
-        else:
+        else:  # autograd's gradient is added into the accumulator (bf16 ones round here)
             def hook(param, g=g):
                 if param.grad is not None:
                     g.add_(param.grad)
@@ -165,8 +171,9 @@ class FlatParamStore:
 
     def zero_grad(self) -> None:
         self.grad.zero_()
+        direct = self.grad.dtype == torch.float32  # fp32 parameters bound to their accumulators
         for s in self.segs:
-            if s.fp32 and s.param.requires_grad:
+            if s.fp32 and direct and s.param.requires_grad:
                 s.param.grad = self.grad_view(s)
 
     def publish_owned(self) -> None:

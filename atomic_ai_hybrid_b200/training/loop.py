@@ -108,6 +108,10 @@ class TrainArgs:
     # AdamW moments of the rank-local parameters (expert blocks, tensor-parallel pieces) in
     # host memory: 8 bytes per such parameter off the GPU (configuration 5 needs it)
     offload_local_moments: bool = False
+    # bf16 gradient accumulators for the expert-parallel experts (their own local store; each
+    # micro-step's weight-gradient GEMM sums in fp32 and rounds once as it adds): 2 bytes per
+    # expert parameter off the GPU, with the moments kept there (configuration 5 fits this way)
+    expert_grad_bf16: bool = False
 
 
 def _dist_setup():
@@ -194,7 +198,8 @@ def _print_memory_plan(args: TrainArgs, cfg, world: int, micro_batch: int) -> No
             p = plan(cfg, world=world, micro_batch=micro_batch, seq_len=args.seq_len, tp=max(1, args.tensor_parallel),
                      ep=max(1, args.expert_parallel), cp=max(1, args.context_parallel),
                      pp=max(1, args.pipeline_parallel), accum_steps=args.accum_steps, remat=args.remat,
-                     schedule=args.pipeline_schedule, local_moments_on_host=args.offload_local_moments)
+                     schedule=args.pipeline_schedule, local_moments_on_host=args.offload_local_moments,
+                     expert_grad_bytes=2 if args.expert_grad_bf16 else 4)
         print(f"[MEMORY] plan per GPU: state {p['state_total_gb']} GB + activations ~{p['activations_gb_est']} GB "
               f"+ reserve {p['reserve_gb']} GB = {p['total_gb']} of {p['hbm_gb']} GB"
               + (f"; pinned host {p['host_pinned_gb_per_rank']} GB per rank, {p['host_pinned_gb_per_node']} GB "
@@ -281,7 +286,8 @@ def _train(args: TrainArgs, rank: int, world: int, dev, health: Optional[PeerHea
     else:
         trainer = Trainer(model, total_steps=total_steps, optimizer=args.optimizer, compute_dtype=cdt, device=dev,
                           cuda_graph=args.cuda_graph and dev.type == "cuda", skip_nonfinite=args.skip_nonfinite,
-                          ep_max_tokens=ep_tokens, offload_local_moments=args.offload_local_moments)
+                          ep_max_tokens=ep_tokens, offload_local_moments=args.offload_local_moments,
+                          expert_grad_bf16=args.expert_grad_bf16)
 
     if rank == 0 and dev.type == "cuda":
         _print_memory_plan(args, cfg, world, per_rank)

@@ -23,6 +23,8 @@ def reset_router(trainer, seed: int = 1234, stddev: float = 0.02, verbose: bool 
     stores = [(trainer.store, trainer.opt)]
     if getattr(trainer, "ep_store", None) is not None:
         stores.append((trainer.ep_store, trainer.ep_opt))
+    if getattr(trainer, "xp_store", None) is not None:
+        stores.append((trainer.xp_store, trainer.xp_opt))
     for st, opt in stores:
         for s in st.segs:
             key = path_key(s.name)

@@ -36,7 +36,7 @@ class Trainer:
                  group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
                  ce_chunk_size: int = 2048, collinearity_coef: Optional[float] = None,
                  skip_nonfinite: bool = False, cuda_graph: bool = False, ep_max_tokens: int = 0,
-                 offload_local_moments: bool = False):
+                 offload_local_moments: bool = False, expert_grad_bf16: bool = False):
         self.model = model
         self.cfg = model.cfg
         self.group = group
@@ -55,9 +55,21 @@ class Trainer:
         from ..parallel.context import get_parallel_context
         self.local_group = get_parallel_context().local_group
         self.ep_store = None
+        # ``expert_grad_bf16``: the expert-parallel experts get a local store of their own with
+        # bf16 gradient accumulators (the MoE weight-gradient GEMMs add into them, rounding once
+        # per micro-step); the tensor-parallel pieces keep fp32 ones in ``ep_store``
+        self.xp_store = None
         if ep_params:
-            self.ep_store = FlatParamStore(model, label_fn, grad_scale_of, 1, 0, compute_dtype=compute_dtype,
-                                           device=device, param_filter=is_ep_local)
+            experts = (lambda n, p: bool(getattr(p, "_ahb_ep_local", False))) if expert_grad_bf16 else None
+            if experts is not None and any(experts(n, p) for n, p in model.named_parameters()):
+                self.xp_store = FlatParamStore(model, label_fn, grad_scale_of, 1, 0, compute_dtype=compute_dtype,
+                                               device=device, param_filter=experts, grad_dtype=torch.bfloat16)
+                rest = lambda n, p: is_ep_local(n, p) and not experts(n, p)  # noqa: E731
+            else:
+                rest = is_ep_local
+            if any(rest(n, p) for n, p in model.named_parameters()):
+                self.ep_store = FlatParamStore(model, label_fn, grad_scale_of, 1, 0, compute_dtype=compute_dtype,
+                                               device=device, param_filter=rest)
         self.comm = None
         if self.world > 1:
             from ..parallel.context import ParallelContext, set_parallel_context
@@ -68,15 +80,20 @@ class Trainer:
             self.comm = make_shard_comm(self.store, group, comm)
         self.opt = HybridOptimizer(self.store, total_steps, reduce_fn=self._allreduce_sum,
                                    skip_nonfinite=skip_nonfinite)
-        self.ep_opt = None
-        if self.ep_store is not None:
+        self.ep_opt = self.xp_opt = None
+        for name in ("ep", "xp"):
+            st = getattr(self, f"{name}_store")
+            if st is None:
+                continue
             # ``offload_local_moments``: the rank-local parameters' AdamW moments in host memory
-            self.ep_opt = HybridOptimizer(self.ep_store, total_steps, offload_moments=offload_local_moments)
-            self.ep_opt.schedule = self.opt.schedule  # one learning-rate schedule for both stores
+            o = HybridOptimizer(st, total_steps, offload_moments=offload_local_moments)
+            o.schedule = self.opt.schedule  # one learning-rate schedule for every store
             if self.local_group is not None:
                 # every replica adds the same statistics to the cross-rank sum
-                self.ep_opt.norm_share = 1.0 / dist.get_world_size(self.local_group)
-            self.opt.partners.append(self.ep_opt)
+                o.norm_share = 1.0 / dist.get_world_size(self.local_group)
+            self.opt.partners.append(o)
+            setattr(self, f"{name}_opt", o)
+        if self.local_stores():
             pc = get_parallel_context()
             if pc.tp is not None and pc.tp.world > 1:
                 # the head-split layers run eager (per-call peer barriers carry host epochs)
@@ -182,10 +199,15 @@ class Trainer:
         self._graph_key = self._key(batch)
         self.reset_accumulators()
 
+    def local_stores(self):
+        """The rank-local stores (tensor-parallel pieces / experts; experts separately with
+        bf16 gradients under ``expert_grad_bf16``)."""
+        return [st for st in (self.ep_store, self.xp_store) if st is not None]
+
     def reset_accumulators(self) -> None:
         self.store.zero_grad()
-        if self.ep_store is not None:
-            self.ep_store.zero_grad()
+        for st in self.local_stores():
+            st.zero_grad()
         self._frac_sum.zero_()
         self._loss_sum.zero_()
         self._n_micro = 0
@@ -208,8 +230,9 @@ class Trainer:
             if self.world > 1:
                 dist.all_reduce(frac, group=self.group)
                 frac = frac / self.world
-        if self.local_group is not None and self.ep_store is not None:
-            dist.all_reduce(self.ep_store.grad, group=self.local_group)
+        if self.local_group is not None:
+            for st in self.local_stores():
+                dist.all_reduce(st.grad, group=self.local_group)
         if self.fused_comm:
             self.comm.begin_step()
         elif self.comm is not None:
@@ -253,7 +276,7 @@ class Trainer:
             torch.cuda.synchronize()
         if self.comm is not None and hasattr(self.comm, "close"):
             self.comm.close()
-        if self.ep_store is not None:
+        if self.local_stores():
             from ..parallel.context import get_parallel_context
             pc = get_parallel_context()
             if pc.ep is not None:

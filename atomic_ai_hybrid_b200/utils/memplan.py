@@ -42,7 +42,11 @@ ACT_BYTES_PER_TOKEN_LAYER_D = 81.0     # calibrated on the 1-GPU benchmark step 
 
 
 def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torch.dtype,
-                  local_grad_bytes: int = 4, local_moments_on_host: bool = False) -> Dict[str, float]:
+                  local_grad_bytes: int = 4, local_moments_on_host: bool = False,
+                  expert_grad_bytes: Optional[int] = None) -> Dict[str, float]:
+    """``local_grad_bytes``: gradient bytes per rank-local parameter; ``expert_grad_bytes``
+    (default: the same) for the expert-parallel experts among them, which can keep bf16
+    accumulators in a store of their own."""
     from ..optim import FlatParamStore, grad_scale_of, label_adamw_only
     from ..optim.store import is_ep_local
     named = list(module.named_parameters())
@@ -64,7 +68,9 @@ def _stores_bytes(module: torch.nn.Module, shard_world: int, compute_dtype: torc
                             param_filter=is_ep_local)
         out["local_params"] = sum(s.numel for s in st.segs)
         out["master"] += 4.0 * st.shard
-        out["grad"] += float(local_grad_bytes) * st.numel
+        eg = local_grad_bytes if expert_grad_bytes is None else expert_grad_bytes
+        n_exp = sum(s.numel for s in st.segs if getattr(s.param, "_ahb_ep_local", False))
+        out["grad"] += float(local_grad_bytes) * (st.numel - n_exp) + float(eg) * n_exp
         out["compute"] += 2.0 * st.cnumel
         if not local_moments_on_host:
             out["optimizer"] += 8.0 * st.shard
@@ -94,7 +100,8 @@ def activation_bytes(cfg, micro_batch: int, seq_len: int, layers: int, tp: int =
 def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int = 1, ep: int = 1, cp: int = 1,
          pp: int = 1, accum_steps: int = 1, remat: bool = False, schedule: str = "1f1b",
          compute_dtype: torch.dtype = torch.bfloat16, local_grad_bytes: int = 4,
-         local_moments_on_host: bool = False, host_ram_gb: Optional[float] = None) -> Dict:
+         local_moments_on_host: bool = False, host_ram_gb: Optional[float] = None,
+         expert_grad_bytes: Optional[int] = None) -> Dict:
     """Memory of the most loaded rank of a layout, in bytes and GB (1e9).
 
     With ``local_moments_on_host`` the rank-local AdamW moments live in pinned host memory:
@@ -118,14 +125,16 @@ def plan(cfg, world: int = 1, micro_batch: int = 1, seq_len: int = 4096, tp: int
         best = None
         for s in range(pp):
             part = PipelineStage(model, pp, s)
-            b = _stores_bytes(part, world // pp, compute_dtype, local_grad_bytes, local_moments_on_host)
+            b = _stores_bytes(part, world // pp, compute_dtype, local_grad_bytes, local_moments_on_host,
+                              expert_grad_bytes)
             tot = b["master"] + b["grad"] + b["compute"] + b["optimizer"]
             if best is None or tot > best[0]:
                 best = (tot, b, s, len(part.layer_ids))
         _, state, stage, layers = best
         in_flight = min(pp - stage, accum_steps) if schedule == "1f1b" else accum_steps
     else:
-        state = _stores_bytes(model, world, compute_dtype, local_grad_bytes, local_moments_on_host)
+        state = _stores_bytes(model, world, compute_dtype, local_grad_bytes, local_moments_on_host,
+                              expert_grad_bytes)
         layers, in_flight, stage = cfg.num_layers, 1, None
     act = activation_bytes(cfg, micro_batch, seq_len, layers, tp, cp, in_flight, remat)
     state_total = state["master"] + state["grad"] + state["compute"] + state["optimizer"]
@@ -165,6 +174,8 @@ def main(argv: Optional[list] = None) -> Dict:
     ap.add_argument("--local-grad-bytes", type=int, default=4, help="gradient bytes of rank-local parameters")
     ap.add_argument("--offload-local-moments", action="store_true", default=None,
                     help="AdamW moments of rank-local parameters in host memory")
+    ap.add_argument("--expert-grad-bf16", action="store_true", default=None,
+                    help="bf16 gradient accumulators for the expert-parallel experts")
     ap.add_argument("--host-ram-gb", type=float, default=None,
                     help="host memory of one node for the pinned-moment check (default: this machine's)")
     a = ap.parse_args(argv)
@@ -190,7 +201,9 @@ def main(argv: Optional[list] = None) -> Dict:
                local_grad_bytes=a.local_grad_bytes,
                local_moments_on_host=bool(a.offload_local_moments if a.offload_local_moments is not None
                                           else train.get("offload_local_moments", False)),
-               host_ram_gb=a.host_ram_gb)
+               host_ram_gb=a.host_ram_gb,
+               expert_grad_bytes=2 if (a.expert_grad_bf16 if a.expert_grad_bf16 is not None
+                                       else train.get("expert_grad_bf16", False)) else None)
     print(json.dumps(out))
     return out
 

@@ -20,6 +20,8 @@ def main(argv=None):
     ap.add_argument("--micro-batch", type=int, default=4)
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--top", type=int, default=60)
+    ap.add_argument("--copies", action="store_true",
+                    help="also list the PyTorch copy / contiguous / cat operators with their input shapes")
     a = ap.parse_args(argv)
     from .. import get_preset, ops
     from ..models import HybridMoEModel
@@ -41,9 +43,16 @@ def main(argv=None):
         tr.train_step(b)
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    acts = [ProfilerActivity.CUDA] + ([ProfilerActivity.CPU] if a.copies else [])
+    with profile(activities=acts, record_shapes=a.copies) as prof:
         tr.micro_step(b[0])
         torch.cuda.synchronize()
+    if a.copies:
+        cops = [e for e in prof.key_averages(group_by_input_shape=True)
+                if e.key in ("aten::copy_", "aten::contiguous", "aten::clone", "aten::cat", "aten::to",
+                             "aten::_to_copy", "aten::reshape") and e.device_time_total > 0]
+        for e in sorted(cops, key=lambda e: -e.device_time_total)[:30]:
+            print(f"[copy] {e.device_time_total / 1000:8.2f} ms x{e.count:4d} {e.key} {e.input_shapes}")
     rows = sorted([(e.self_device_time_total, e.count, e.key) for e in prof.key_averages()
                    if e.self_device_time_total > 0], reverse=True)
     tot = sum(r[0] for r in rows)

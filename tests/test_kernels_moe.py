@@ -89,3 +89,33 @@ def test_moe_forward_backward(act, T, d, F, E, k):
         assert a.grad is not None, name
         err = _rel(a.grad, r.grad)
         assert err < 3e-2, (name, err)
+
+
+def test_moe_weight_gradients_into_bf16_accumulators():
+    """Expert weight gradients added into bf16 accumulators (a store with 16-bit gradients):
+    the GEMM epilogue sums in fp32 and rounds once per add, so two backward passes match the
+    fp32 accumulators to bf16 precision."""
+    ext().gemm_error_reset()
+    torch.manual_seed(3)
+    T, d, F, E, k = 1024, 512, 256, 8, 2
+    x = (torch.randn(T, d, device=dev) * 0.5).to(torch.bfloat16)
+    logits = torch.randn(T, E, device=dev)
+    top_idx = torch.topk(logits, k, -1).indices
+    gate = torch.softmax(logits.gather(1, top_idx), -1)
+    ws = [(torch.randn(E, d, F, device=dev) * d ** -0.5).to(torch.bfloat16),
+          (torch.randn(E, F, d, device=dev) * F ** -0.5).to(torch.bfloat16),
+          (torch.randn(E, d, F, device=dev) * d ** -0.5).to(torch.bfloat16)]
+    dout = torch.randn(T, d, device=dev).to(torch.bfloat16)
+    accs = {}
+    for dt in (torch.float32, torch.bfloat16):
+        wa = [w.clone().requires_grad_(True) for w in ws]
+        for w in wa:
+            w._ahb_grad_acc = torch.zeros(w.shape, dtype=dt, device=dev)
+        for _ in range(2):
+            out = KN.moe_forward(x, top_idx, gate, wa[0], wa[1], wa[2], None, "swiglu")
+            out.backward(dout)
+        torch.cuda.synchronize()
+        accs[dt] = [w._ahb_grad_acc.float() for w in wa]
+    assert KN.gemm_error() == 0
+    for a, r in zip(accs[torch.bfloat16], accs[torch.float32]):
+        assert _rel(a, r) < 1e-2, _rel(a, r)

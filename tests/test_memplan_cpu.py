@@ -61,10 +61,10 @@ def test_benchmark_config_plans():
 
 
 def test_run_files_for_eight_gpus():
-    """The 8-GPU run files fit as written on a node with 2 TB of host memory (configuration 5
-    with its rank-local AdamW moments in pinned host memory, 82 GB per rank and 657 GB per
-    node; without that it does not: ``test_benchmark_config_plans``); on a 512 GB node
-    configuration 5's moments do not fit."""
+    """The 8-GPU run files fit as written (configuration 5 with bf16 gradient accumulators for
+    its 9.7 B expert weights per GPU; with fp32 ones it does not: ``test_benchmark_config_plans``).
+    The alternative layout with the rank-local AdamW moments in pinned host memory takes 82 GB
+    per rank and 657 GB per node: it does not fit a 512 GB node."""
     import os
     root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "atomic_ai_hybrid_b200",
                         "configs")
@@ -72,8 +72,10 @@ def test_run_files_for_eight_gpus():
                        ("config5_hybrid_long_tp8.yaml", True)):
         out = memplan.main(["--config", os.path.join(root, name), "--world", "8", "--host-ram-gb", "2048"])
         assert out["fits"] is fits, (name, out)
+    c5 = memplan.main(["--config", os.path.join(root, "config5_hybrid_long_tp8.yaml"), "--world", "8"])
+    assert c5["fits"] and c5["host_pinned_gb_per_rank"] == 0 and c5["total_gb"] < c5["hbm_gb"]
     c5 = memplan.main(["--config", os.path.join(root, "config5_hybrid_long_tp8.yaml"), "--world", "8",
-                       "--host-ram-gb", "512"])
+                       "--host-ram-gb", "512", "--offload-local-moments"])
     assert not c5["fits"] and not c5["host_fits"] and c5["total_gb"] <= c5["hbm_gb"]
     assert abs(c5["host_pinned_gb_per_rank"] - 82.1) < 1.0
     assert abs(c5["host_pinned_gb_per_node"] - 8 * c5["host_pinned_gb_per_rank"]) < 0.1

@@ -83,3 +83,32 @@ def test_offloaded_moments_on_cuda(tmp_path):
     CheckpointManager(str(tmp_path), "latest").restore(3, t)
     assert torch.equal(o1.m, m_ref) and torch.equal(o1.v, v_ref)
     assert o1.m.device.type == "cpu" and o1.m.is_pinned() and o1.v.is_pinned()
+
+
+def test_fused_step_with_bf16_gradients():
+    """A store with bf16 gradient accumulators steps like one with fp32 accumulators holding
+    the same (bf16-representable) gradients: the fused kernels read and scale either type."""
+    cfg = get_preset("reference_tiny", d_model=256, n_heads=2, d_ff=256, num_experts=5)
+    dev = torch.device("cuda", 0)
+    runs, grads = [], None
+    for gdt in (torch.float32, torch.bfloat16):
+        torch.manual_seed(0)
+        m = HybridMoEModel(cfg, compute_dtype=torch.bfloat16).to(dev)
+        st = FlatParamStore(m, label_adamw_only, grad_scale_of, compute_dtype=torch.bfloat16, device=dev,
+                            grad_dtype=gdt)
+        assert st.grad.dtype == gdt
+        if grads is None:
+            g = torch.Generator(device=dev).manual_seed(4)
+            grads = [(torch.randn(st.grad.numel(), device=dev, generator=g) * 0.01).to(torch.bfloat16)
+                     for _ in range(3)]
+        opt = HybridOptimizer(st, total_steps=100)
+        opt.schedule.warmup = 1
+        assert opt.uses_kernels()
+        for gr in grads:
+            st.grad.copy_(gr.to(gdt))
+            with ops.impl("cuda"):
+                opt.step(1)
+        torch.cuda.synchronize()
+        runs.append((st.master.clone(), opt.m.clone(), opt.v.clone()))
+    for a, b in zip(*runs):
+        torch.testing.assert_close(b, a, rtol=1e-2, atol=1e-6)

@@ -207,6 +207,41 @@ def test_training_loop_with_expert_parallelism(tmp_path, world):
     assert any("routed_w1#experts[2:4]" in k for k in keys), sorted(keys)[:10]
 
 
+def _ep_bf16_rank_main(rank, world, port, tmp, flag):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")
+    import torch
+    torch.set_num_threads(threads_per_rank(world))
+    _write_data(tmp)
+    out = main_execution(_args(tmp, data_dir=tmp, data_prefixes=["src"], expert_parallel=2, max_steps=3,
+                               checkpoint_every_s=0.0, global_batch=world, expert_grad_bf16=flag))
+    with open(os.path.join(tmp, f"out{rank}.json"), "w") as f:
+        json.dump({"losses": [float(x) for x in out["losses"]], "global_step": out["global_step"]}, f)
+
+
+def test_expert_bf16_gradients_train_like_fp32(tmp_path):
+    """--ep 2 with the experts' gradients in bf16 accumulators (a local store of their own):
+    three steps with the per-step losses of the fp32-accumulator run (to 2e-2), and the
+    checkpoint still holds each rank's block of experts."""
+    losses = {}
+    for flag in (False, True):
+        d = tmp_path / ("bf16" if flag else "fp32")
+        d.mkdir()
+        port = free_port()
+        mp.spawn(_ep_bf16_rank_main, args=(2, port, str(d), flag), nprocs=2, join=True)
+        outs = [json.load(open(os.path.join(d, f"out{r}.json"))) for r in range(2)]
+        assert all(o["global_step"] == 3 for o in outs), outs
+        losses[flag] = outs[0]["losses"]
+    assert len(losses[True]) == len(losses[False]) == 3
+    for a, b in zip(losses[True], losses[False]):
+        assert abs(a - b) <= 2e-2 * abs(b), (losses[True], losses[False])
+    from atomic_ai_hybrid_b200.ckpt.safetensors_io import load_file
+    root = os.path.join(tmp_path, "bf16", "latest")
+    step = max((x for x in os.listdir(root) if x.isdigit()), key=int)
+    keys = load_file(os.path.join(root, step, "params-rank1.safetensors")).keys()
+    assert any("routed_w1#experts[2:4]" in k for k in keys), sorted(keys)[:10]
+
+
 def _cp_rank_main(rank, world, port, tmp):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), AHB_PG_TIMEOUT_S="60")

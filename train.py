@@ -61,6 +61,8 @@ def parse(argv=None) -> TrainArgs:
     ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward (long context)")
     ap.add_argument("--offload-local-moments", action="store_true",
                     help="AdamW moments of expert blocks / tensor-parallel pieces in host memory")
+    ap.add_argument("--expert-grad-bf16", action="store_true",
+                    help="bf16 gradient accumulators for the expert-parallel experts")
     ap.add_argument("--cp", type=int, default=1,
                     help="context-parallel group size (sequence segments); world / cp data-parallel replicas")
     ap.add_argument("--pp", type=int, default=1,
@@ -92,7 +94,8 @@ def parse(argv=None) -> TrainArgs:
                      pipeline_parallel=a.pp, pipeline_schedule=a.pp_schedule, hf_repo_id=a.hf_repo_id,
                      hf_bucket_id=a.hf_bucket_id, resume_source=a.resume_source, eval_batches=a.eval_batches,
                      early_stop_patience=a.early_stop_patience, val_split=a.val_split,
-                     dataset_fraction=a.dataset_fraction, offload_local_moments=a.offload_local_moments)
+                     dataset_fraction=a.dataset_fraction, offload_local_moments=a.offload_local_moments,
+                     expert_grad_bf16=a.expert_grad_bf16)
 
 
 def apply_yaml_train_section(args: TrainArgs, argv=None) -> TrainArgs:
