@@ -220,27 +220,77 @@ __global__ void __launch_bounds__(NT) router_fwd_kernel(
 }
 
 // ------------------------------------------------------------------ backward: dcos, dtemp, dx
-// kn2: 2 x (d, EP) bf16 (hi, mid of kn).  dcos_out (T, EP) fp32 with zero padding.
+// kn2: 2 x (d, EP) bf16 (hi, mid of kn).  bhl_out (T, 2 EP) bf16: the hi and lo terms of r_t dcos_t
+// (the operand of the dkn kernel), zero on padded experts.
+//
+// Per token: dl, dcos, dtemp as in the forward's statistics; then dx = sanitize(r dxn - x r^2 S, 1e3)
+// with dxn = dcos kn^T and S = sum_e dcos_e cos_e (= r x . dxn, since cos_e = r x . kn_e: the dot
+// product needs no second pass over d).  The d columns run in slices of 64: the slice of kn (hi and
+// mid) and of x are staged by cp.async one slice ahead, dx goes out through a shared tile as 16-byte
+// row segments.
+constexpr int RB_SL = 64;           // d columns per slice
+constexpr int RB_XS = RB_SL + 8;    // bf16 stride of the x / dx tiles (16-byte rows, spread banks)
+
+template <int NTE>
+struct RbLayout {
+  static constexpr int EP = NTE * 8;
+  static constexpr int KS = EP + 8;  // bf16 stride of a staged kn row
+  static constexpr size_t DC = 0;                                         // float [TOKC][EMAX + 1]
+  static constexpr size_t SS = DC + (size_t)TOKC * (EMAX + 1) * 4;        // float [TOKC]
+  static constexpr size_t KN = SS + (size_t)TOKC * 4;                     // bf16 [2 buf][2 term][RB_SL][KS]
+  static constexpr size_t XT = KN + (size_t)2 * 2 * RB_SL * KS * 2;       // bf16 [2 buf][TOKC][RB_XS]
+  static constexpr size_t OT = XT + (size_t)2 * TOKC * RB_XS * 2;         // bf16 [TOKC][RB_XS]
+  static constexpr size_t BYTES = OT + (size_t)TOKC * RB_XS * 2;
+};
+
 template <int NTE>
 __global__ void __launch_bounds__(NT) router_bwd_tokens_kernel(
     const bf16* __restrict__ x, const bf16* __restrict__ kn2, const float* __restrict__ temp_p,
     const float* __restrict__ logits, const float* __restrict__ cosv, const float* __restrict__ rn_in,
     const int64_t* __restrict__ top_idx, const float* __restrict__ gate, const float* __restrict__ dgate,
     const float* __restrict__ dps, const float* __restrict__ dlse_sq_p, int64_t T, int d, int E, int k,
-    float* __restrict__ dcos_out, float* __restrict__ dtemp, bf16* __restrict__ dx) {
-  constexpr int EP = NTE * 8;
-  constexpr int KS = (EP + 15) / 16;  // k-steps over the (padded) experts
-  __shared__ float dc[TOKC][EMAX + 1];
+    bf16* __restrict__ bhl_out, float* __restrict__ dtemp, bf16* __restrict__ dx) {
+  using Lay = RbLayout<NTE>;
+  constexpr int EP = Lay::EP;
+  constexpr int KSTEPS = (EP + 15) / 16;  // k-steps over the (padded) experts
+  extern __shared__ __align__(16) unsigned char rb_smem[];
+  float(*dc)[EMAX + 1] = reinterpret_cast<float(*)[EMAX + 1]>(rb_smem + Lay::DC);
+  float* Srow = reinterpret_cast<float*>(rb_smem + Lay::SS);
+  bf16* knt = reinterpret_cast<bf16*>(rb_smem + Lay::KN);
+  bf16* xt = reinterpret_cast<bf16*>(rb_smem + Lay::XT);
+  bf16* ot = reinterpret_cast<bf16*>(rb_smem + Lay::OT);
   const int64_t t0 = (int64_t)blockIdx.x * TOKC;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const float temp = *temp_p;
   const float dlse_sq = dlse_sq_p ? *dlse_sq_p : 0.f;
+  const int nsl = d / RB_SL;
+  // stage slice `sl` of kn (rows c, hi and mid) and of x (the CTA's 64 tokens) into buffer sl & 1
+  auto issue = [&](int sl) {
+    bf16* kb = knt + (size_t)(sl & 1) * 2 * RB_SL * Lay::KS;
+    bf16* xb = xt + (size_t)(sl & 1) * TOKC * RB_XS;
+    constexpr int KCH = EP / 8;  // 16-byte chunks per kn row
+    for (int i = tid; i < 2 * RB_SL * KCH; i += NT) {
+      const int term = i / (RB_SL * KCH), r = (i / KCH) % RB_SL, q = i % KCH;
+      const bf16* src = kn2 + (int64_t)term * d * EP + (int64_t)(sl * RB_SL + r) * EP + 8 * q;
+      cp16z(kb + (term * RB_SL + r) * Lay::KS + 8 * q, src, true);
+    }
+    for (int i = tid; i < TOKC * (RB_SL / 8); i += NT) {
+      const int r = i / (RB_SL / 8), q = i % (RB_SL / 8);
+      const int64_t t = t0 + r;
+      cp16z(xb + r * RB_XS + 8 * q, x + (t < T ? t : 0) * d + sl * RB_SL + 8 * q, t < T);
+    }
+    cp_commit();
+  };
+  issue(0);  // the first slice loads while the per-token part runs
   for (int i = tid; i < TOKC * (EMAX + 1); i += NT) (&dc[0][0])[i] = 0.f;
   __syncthreads();
   float dtp = 0.f;
   for (int r = w; r < TOKC; r += NT / 32) {
     const int64_t t = t0 + r;
-    if (t >= T) break;
+    if (t >= T) {
+      if (lane == 0) Srow[r] = 0.f;
+      continue;
+    }
     float l[2], p[2], dl[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -273,6 +323,8 @@ __global__ void __launch_bounds__(NT) router_bwd_tokens_kernel(
       const float v = gate[t * k + j] * (dgate[t * k + j] - gd);
       if ((e & 31) == lane) dl[e >> 5] += v;
     }
+    const float rt = rn_in[t];
+    float sdot = 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int e = lane + 32 * h;
@@ -283,21 +335,27 @@ __global__ void __launch_bounds__(NT) router_bwd_tokens_kernel(
           const float dpre = fabsf(c * temp) <= 8.f ? dl[h] : 0.f;
           dtp += dpre * c;
           d_c = dpre * temp;
+          sdot += d_c * c;
         }
         dc[r][e] = d_c;
-        dcos_out[t * EP + e] = d_c;
+        const float v = rt * d_c;
+        const bf16 hi = __float2bfloat16_rn(v);
+        bhl_out[t * 2 * EP + e] = hi;
+        bhl_out[t * 2 * EP + EP + e] = __float2bfloat16_rn(v - __bfloat162float(hi));
       }
     }
+    sdot = warp_sum(sdot);
+    if (lane == 0) Srow[r] = sdot;
   }
   dtp = warp_sum(dtp);
   if (lane == 0) atomicAdd(dtemp, dtp);
   __syncthreads();
-  // dxn = dcos kn^T for the warp's 16 tokens: A = dcos (hi + lo), B(e, c) = kn[c][e] (hi + mid)
-  uint32_t ahi[KS][4], alo[KS][4];
+  // A = dcos (hi + lo) of the warp's 16 tokens; B(e, c) = kn[c][e] (hi + mid)
+  uint32_t ahi[KSTEPS][4], alo[KSTEPS][4];
+  const int g = lane >> 2, tq = lane & 3;
   {
-    const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
-    for (int s = 0; s < KS; ++s) {
+    for (int s = 0; s < KSTEPS; ++s) {
       const int kc[4][2] = {{g, 16 * s + 2 * tq}, {g + 8, 16 * s + 2 * tq}, {g, 16 * s + 2 * tq + 8},
                             {g + 8, 16 * s + 2 * tq + 8}};
 #pragma unroll
@@ -311,102 +369,124 @@ __global__ void __launch_bounds__(NT) router_bwd_tokens_kernel(
       }
     }
   }
-  const int g = lane >> 2, tq = lane & 3;
-  const int64_t ta = t0 + 16 * w + g, tb = ta + 8;
-  const float rna = ta < T ? rn_in[ta] : 0.f, rnb = tb < T ? rn_in[tb] : 0.f;
-  const bf16* khi = kn2;
-  const bf16* kmid = kn2 + (int64_t)d * EP;
-  float dot_a = 0.f, dot_b = 0.f;
-  for (int pass = 0; pass < 2; ++pass) {
-    for (int n0 = 0; n0 < d; n0 += 64) {
-      float acc[8][4];
-      zero_acc<8>(acc);
+  const int ra = 16 * w + g, rb = ra + 8;
+  const float rna = t0 + ra < T ? rn_in[t0 + ra] : 0.f, rnb = t0 + rb < T ? rn_in[t0 + rb] : 0.f;
+  const float qa = rna * rna * Srow[ra], qb = rnb * rnb * Srow[rb];
+  for (int sl = 0; sl < nsl; ++sl) {
+    if (sl + 1 < nsl) {
+      issue(sl + 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    const bf16* kb = knt + (size_t)(sl & 1) * 2 * RB_SL * Lay::KS;
+    const bf16* xb = xt + (size_t)(sl & 1) * TOKC * RB_XS;
+    float acc[8][4];
+    zero_acc<8>(acc);
 #pragma unroll
-      for (int s = 0; s < KS; ++s) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int col = n0 + 8 * j + g;
-          const int kk = 16 * s + 2 * tq;
-          uint32_t bh[2], bm[2];
-          bh[0] = kk < EP ? *reinterpret_cast<const uint32_t*>(khi + (int64_t)col * EP + kk) : 0u;
-          bh[1] = kk + 8 < EP ? *reinterpret_cast<const uint32_t*>(khi + (int64_t)col * EP + kk + 8) : 0u;
-          bm[0] = kk < EP ? *reinterpret_cast<const uint32_t*>(kmid + (int64_t)col * EP + kk) : 0u;
-          bm[1] = kk + 8 < EP ? *reinterpret_cast<const uint32_t*>(kmid + (int64_t)col * EP + kk + 8) : 0u;
-          mma16816(acc[j], ahi[s], bh);
-          mma16816(acc[j], ahi[s], bm);
-          mma16816(acc[j], alo[s], bh);
-        }
-      }
+    for (int s = 0; s < KSTEPS; ++s) {
+      const int kk = 16 * s + 2 * tq;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = n0 + 8 * j + 2 * tq;
-        const float2 xa = ta < T ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + ta * d + c))
-                                 : make_float2(0.f, 0.f);
-        const float2 xb = tb < T ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + tb * d + c))
-                                 : make_float2(0.f, 0.f);
-        if (pass == 0) {
-          dot_a += xa.x * acc[j][0] + xa.y * acc[j][1];
-          dot_b += xb.x * acc[j][2] + xb.y * acc[j][3];
-        } else {
-          if (ta < T)
-            *reinterpret_cast<__nv_bfloat162*>(dx + ta * d + c) = __floats2bfloat162_rn(
-                sanitize(rna * acc[j][0] - xa.x * rna * rna * rna * dot_a, 1e3f),
-                sanitize(rna * acc[j][1] - xa.y * rna * rna * rna * dot_a, 1e3f));
-          if (tb < T)
-            *reinterpret_cast<__nv_bfloat162*>(dx + tb * d + c) = __floats2bfloat162_rn(
-                sanitize(rnb * acc[j][2] - xb.x * rnb * rnb * rnb * dot_b, 1e3f),
-                sanitize(rnb * acc[j][3] - xb.y * rnb * rnb * rnb * dot_b, 1e3f));
-        }
+        const int c = 8 * j + g;
+        const bf16* rh = kb + c * Lay::KS;
+        const bf16* rm = kb + (RB_SL + c) * Lay::KS;
+        uint32_t bh[2], bm[2];
+        bh[0] = kk < EP ? *reinterpret_cast<const uint32_t*>(rh + kk) : 0u;
+        bh[1] = kk + 8 < EP ? *reinterpret_cast<const uint32_t*>(rh + kk + 8) : 0u;
+        bm[0] = kk < EP ? *reinterpret_cast<const uint32_t*>(rm + kk) : 0u;
+        bm[1] = kk + 8 < EP ? *reinterpret_cast<const uint32_t*>(rm + kk + 8) : 0u;
+        mma16816(acc[j], ahi[s], bh);
+        mma16816(acc[j], ahi[s], bm);
+        mma16816(acc[j], alo[s], bh);
       }
     }
-    if (pass == 0) {  // the 4 lanes of a row share it
 #pragma unroll
-      for (int o = 1; o < 4; o <<= 1) {
-        dot_a += __shfl_xor_sync(0xffffffffu, dot_a, o);
-        dot_b += __shfl_xor_sync(0xffffffffu, dot_b, o);
-      }
+    for (int j = 0; j < 8; ++j) {
+      const int c = 8 * j + 2 * tq;
+      const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xb + ra * RB_XS + c));
+      const float2 xb2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xb + rb * RB_XS + c));
+      *reinterpret_cast<__nv_bfloat162*>(ot + ra * RB_XS + c) = __floats2bfloat162_rn(
+          sanitize(rna * acc[j][0] - xa.x * qa, 1e3f), sanitize(rna * acc[j][1] - xa.y * qa, 1e3f));
+      *reinterpret_cast<__nv_bfloat162*>(ot + rb * RB_XS + c) = __floats2bfloat162_rn(
+          sanitize(rnb * acc[j][2] - xb2.x * qb, 1e3f), sanitize(rnb * acc[j][3] - xb2.y * qb, 1e3f));
+    }
+    __syncthreads();  // the dx tile is complete; this slice's buffers may be refilled
+    for (int i = tid; i < TOKC * (RB_SL / 8); i += NT) {
+      const int r = i / (RB_SL / 8), q = i % (RB_SL / 8);
+      const int64_t t = t0 + r;
+      if (t < T)
+        *reinterpret_cast<uint4*>(dx + t * d + sl * RB_SL + 8 * q) =
+            *reinterpret_cast<const uint4*>(ot + r * RB_XS + 8 * q);
     }
   }
 }
 
 // ------------------------------------------------------------------ backward: dkn
-// dkn[c][e] += sum_t x[t][c] (r_t dcos[t][e]); CTA = 64 columns of d (4 warps x 16) x a token range.
+// dkn[c][e] += sum_t x[t][c] (r_t dcos[t][e]) with r dcos as bf16 hi + lo terms (written by the
+// tokens kernel); CTA = 64 columns of d (4 warps x 16) x a token range, chunks of 64 tokens of x and
+// of the terms staged by cp.async one chunk ahead.
+constexpr int RK_TC = 64;
+
 template <int NTE>
-__global__ void __launch_bounds__(NT) router_bwd_kn_kernel(const bf16* __restrict__ x,
-                                                          const float* __restrict__ rn_in,
-                                                          const float* __restrict__ dcos, int64_t T, int d,
-                                                          int E, int64_t tok_per_cta, float* __restrict__ dkn) {
-  constexpr int EP = NTE * 8;
-  constexpr int TC = 32;  // tokens per staged chunk
-  __shared__ __align__(16) bf16 xs[TC * LDX];
-  __shared__ bf16 bh[TC][EP + 2], bl[TC][EP + 2];
+struct RkLayout {
+  static constexpr int EP = NTE * 8;
+  static constexpr int BS = EP + 8;  // bf16 stride of a staged term row
+  static constexpr size_t XS = 0;                                      // bf16 [2][RK_TC][RB_XS]
+  static constexpr size_t BT = XS + (size_t)2 * RK_TC * RB_XS * 2;     // bf16 [2][2 term][RK_TC][BS]
+  static constexpr size_t BYTES = BT + (size_t)2 * 2 * RK_TC * BS * 2;
+};
+
+template <int NTE>
+__global__ void __launch_bounds__(NT) router_bwd_kn_kernel(const bf16* __restrict__ x, const bf16* __restrict__ bhl,
+                                                          int64_t T, int d, int E, int64_t tok_per_cta,
+                                                          float* __restrict__ dkn) {
+  using Lay = RkLayout<NTE>;
+  constexpr int EP = Lay::EP;
+  extern __shared__ __align__(16) unsigned char rk_smem[];
+  bf16* xs = reinterpret_cast<bf16*>(rk_smem + Lay::XS);
+  bf16* bt = reinterpret_cast<bf16*>(rk_smem + Lay::BT);
   const int c0 = blockIdx.x * 64;
   const int64_t ta = (int64_t)blockIdx.y * tok_per_cta;
   const int64_t tb = ta + tok_per_cta < T ? ta + tok_per_cta : T;
   const int tid = threadIdx.x, w = tid >> 5;
+  const int nch = (int)((tb - ta + RK_TC - 1) / RK_TC);
+  auto issue = [&](int ch) {
+    const int64_t q0 = ta + (int64_t)ch * RK_TC;
+    bf16* xb = xs + (size_t)(ch & 1) * RK_TC * RB_XS;
+    bf16* bb = bt + (size_t)(ch & 1) * 2 * RK_TC * Lay::BS;
+    for (int i = tid; i < RK_TC * 8; i += NT) {
+      const int r = i >> 3, q = i & 7;
+      const int64_t t = q0 + r;
+      cp16z(xb + r * RB_XS + 8 * q, x + (t < tb ? t : ta) * d + c0 + 8 * q, t < tb);
+    }
+    constexpr int BCH = EP / 8;
+    for (int i = tid; i < 2 * RK_TC * BCH; i += NT) {
+      const int term = i / (RK_TC * BCH), r = (i / BCH) % RK_TC, q = i % BCH;
+      const int64_t t = q0 + r;
+      cp16z(bb + (term * RK_TC + r) * Lay::BS + 8 * q, bhl + (t < tb ? t : ta) * 2 * EP + term * EP + 8 * q,
+            t < tb);
+    }
+    cp_commit();
+  };
   float acc[NTE][4];
   zero_acc<NTE>(acc);
-  for (int64_t q0 = ta; q0 < tb; q0 += TC) {
-    __syncthreads();
-    for (int idx = tid; idx < TC * 8; idx += NT) {
-      const int r = idx >> 3, c8 = (idx & 7) * 8;
-      const int64_t t = q0 + r;
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (t < tb) u = *reinterpret_cast<const uint4*>(x + t * d + c0 + c8);
-      *reinterpret_cast<uint4*>(xs + r * LDX + c8) = u;
-    }
-    for (int idx = tid; idx < TC * EP; idx += NT) {
-      const int r = idx / EP, e = idx % EP;
-      const int64_t t = q0 + r;
-      const float v = t < tb ? dcos[t * EP + e] * rn_in[t] : 0.f;
-      const bf16 h = __float2bfloat16_rn(v);
-      bh[r][e] = h;
-      bl[r][e] = __float2bfloat16_rn(v - __bfloat162float(h));
+  if (nch > 0) issue(0);
+  for (int ch = 0; ch < nch; ++ch) {
+    if (ch + 1 < nch) {
+      issue(ch + 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
     }
     __syncthreads();
-    // A(m = column, k = token) = xs[k][m]; B(k = token, n = expert) = b[k][n]
-    warp_mma<NTE>(acc, ColA16{xs, LDX}, KNB16{&bh[0][0], EP + 2}, 16 * w, 0, 0, TC);
-    warp_mma<NTE>(acc, ColA16{xs, LDX}, KNB16{&bl[0][0], EP + 2}, 16 * w, 0, 0, TC);
+    const bf16* xb = xs + (size_t)(ch & 1) * RK_TC * RB_XS;
+    const bf16* bb = bt + (size_t)(ch & 1) * 2 * RK_TC * Lay::BS;
+    // A(m = column, k = token) = xs[k][m]; B(k = token, n = expert) = term[k][n]
+    warp_mma<NTE>(acc, ColA16{xb, RB_XS}, KNB16{bb, Lay::BS}, 16 * w, 0, 0, RK_TC);
+    warp_mma<NTE>(acc, ColA16{xb, RB_XS}, KNB16{bb + RK_TC * Lay::BS, Lay::BS}, 16 * w, 0, 0, RK_TC);
+    __syncthreads();  // both reads of this buffer are done before it is refilled
   }
   for_acc<NTE>(acc, 16 * w, 0, [&](int r, int c, float& v) {
     if (c < E) atomicAdd(dkn + (int64_t)(c0 + r) * E + c, v);
@@ -454,18 +534,38 @@ void ahb_router_bwd(const void* x, const void* kn2, const float* temp, const flo
                     const float* rn, const int64_t* top_idx, const float* gate, const float* dgate, const float* dps,
                     const float* dlse_sq, int64_t T, int d, int E, int k, float* dcos, float* dtemp, void* dx,
                     float* dkn, cudaStream_t st) {
+  // dcos: (T, EP) fp32 scratch, used here as (T, 2 EP) bf16 hi / lo terms of r dcos
   if (T <= 0) return;
   const int grid = (int)((T + TOKC - 1) / TOKC);
   const int EP = ahb_router_padded_experts(E);
-#define RB(N) router_bwd_tokens_kernel<N><<<grid, NT, 0, st>>>((const bf16*)x, (const bf16*)kn2, temp, logits, cosv, \
-    rn, top_idx, gate, dgate, dps, dlse_sq, T, d, E, k, dcos, dtemp, (bf16*)dx)
+  bf16* bhl = reinterpret_cast<bf16*>(dcos);
+#define RB(N)                                                                                                      \
+  do {                                                                                                             \
+    static bool init = false;                                                                                      \
+    if (!init) {                                                                                                   \
+      cudaFuncSetAttribute(router_bwd_tokens_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,               \
+                           (int)RbLayout<N>::BYTES);                                                               \
+      init = true;                                                                                                 \
+    }                                                                                                              \
+    router_bwd_tokens_kernel<N><<<grid, NT, RbLayout<N>::BYTES, st>>>((const bf16*)x, (const bf16*)kn2, temp,      \
+        logits, cosv, rn, top_idx, gate, dgate, dps, dlse_sq, T, d, E, k, bhl, dtemp, (bf16*)dx);                 \
+  } while (0)
   if (EP == 16) RB(2); else if (EP == 32) RB(4); else if (EP == 48) RB(6); else RB(8);
 #undef RB
   const int nx = d / 64;
   int ny = (2 * sm_count() + nx - 1) / nx;
-  const int64_t per = ((T + ny - 1) / ny + 31) / 32 * 32;
+  const int64_t per = ((T + ny - 1) / ny + RK_TC - 1) / RK_TC * RK_TC;
   ny = (int)((T + per - 1) / per);
-#define RK(N) router_bwd_kn_kernel<N><<<dim3(nx, ny), NT, 0, st>>>((const bf16*)x, rn, dcos, T, d, E, per, dkn)
+#define RK(N)                                                                                                      \
+  do {                                                                                                             \
+    static bool init = false;                                                                                      \
+    if (!init) {                                                                                                   \
+      cudaFuncSetAttribute(router_bwd_kn_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
+                           (int)RkLayout<N>::BYTES);                                                               \
+      init = true;                                                                                                 \
+    }                                                                                                              \
+    router_bwd_kn_kernel<N><<<dim3(nx, ny), NT, RkLayout<N>::BYTES, st>>>((const bf16*)x, bhl, T, d, E, per, dkn); \
+  } while (0)
   if (EP == 16) RK(2); else if (EP == 32) RK(4); else if (EP == 48) RK(6); else RK(8);
 #undef RK
 }

@@ -849,12 +849,16 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
         if (!wide) {
 #pragma unroll
           for (int t = 0; t < 16; ++t) u[t] *= __expf(CUM[(r + t) * P + p] - cs);
+          // column j of the block = row r + j of CB^T: two 16-byte chunks (rows i < j are the
+          // causal mask's zeros), read by every thread of the block (broadcast)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
+            float cb[16];
+            unpack8(*reinterpret_cast<const uint4*>(smem + SB_CBT + sw_off16(C, r + j, r)), cb);
+            unpack8(*reinterpret_cast<const uint4*>(smem + SB_CBT + sw_off16(C, r + j, r + 8)), cb + 8);
             float acc = 0.f;
 #pragma unroll
-            for (int i = j; i < 16; ++i)
-              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_CB + sw_off(C, r + i, r + j))) * u[i];
+            for (int i = j; i < 16; ++i) acc += cb[i] * u[i];
             DDG[p * C + r + j] = __expf(cs - CUM[(r + j) * P + p]) * acc;
           }
         } else {
@@ -866,84 +870,103 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     sm100::tc_fence_after();
     __syncthreads();
     {
-      // per channel p = 16 quarter + lane (lanes 0-15), two threads per channel: warpgroup 0 rows
-      // 32-63, warpgroup 1 rows 0-31.  Pass 1 (descending rows): dc without the last row's extra
-      // term and its local suffix sums, d(dBx), dx; the two halves then exchange the upper suffix
-      // total and the parts of that extra term (state carry and the state part of d(dBx)); pass 2:
-      // g, ddt and dA.
-      const int p = 16 * quarter + lane;
-      const int jb = wg == 0 ? 2 : 0;  // first of this thread's two blocks
-      float* XCH = reinterpret_cast<float*>(smem + SB_XCH);  // [0,64) upper suffix total, [64,192) dcl parts
-      float dds[32];
-      tmem_ld32(tmem_at(tmem, quarter, TM_DDS + 16 * jb), dds);
-      float suf[32], ddbx[32];
-      float dclp = 0.f, local = 0.f, cl = 0.f;
+      // four threads per channel p = 16 quarter + (lane & 15), one 16-row block each, in descending
+      // row order k = 2 wg + (lane >> 4): block J = 3 - k (warpgroup 0 rows 32-63, lanes 0-15 the
+      // upper block).  The M = 64 accumulators hold channel p in lane p & 15 of the quarter, so the
+      // lower block's values reach lanes 16-31 by shuffle.  Pass 1 (descending rows): dc without the
+      // last row's extra term and its local suffix sums, d(dBx), dx; the four threads then exchange
+      // their suffix totals and the parts of that extra term (state carry and the state part of
+      // d(dBx)); pass 2: g, ddt and dA.
+      const int hf = lane >> 4, cl16 = lane & 15;
+      const int p = 16 * quarter + cl16;
+      const int jb = wg == 0 ? 2 : 0;       // lower of the warpgroup's two blocks
+      const int J = jb + 1 - hf;            // this thread's block
+      const int kq = 2 * wg + hf;           // position in the descending row order
+      float* XCH = reinterpret_cast<float*>(smem + SB_XCH);  // [k][p]: suffix totals; [4 + k][p]: dcl parts
+      float dds[16], ddd[16], yo[16];
+      {
+        float a32[32], lo16[16], hi16[16];
+        tmem_ld32(tmem_at(tmem, quarter, TM_DDS + 16 * jb), a32);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, a32[e], cl16);
+          dds[e] = hf ? sh : a32[16 + e];
+        }
+        tmem_ld16(tmem_at(tmem, quarter, TM_DDD + 16 * jb), lo16);
+        tmem_ld16(tmem_at(tmem, quarter, TM_DDD + 16 * (jb + 1)), hi16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, lo16[e], cl16);
+          ddd[e] = hf ? sh : hi16[e];
+        }
+        tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * jb), lo16);
+        tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * (jb + 1)), hi16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, lo16[e], cl16);
+          yo[e] = hf ? sh : hi16[e];
+        }
+      }
+      float suf[16], ddbx[16];
+      float dclp = 0.f, local = 0.f;
+      const float cl = CUM[(C - 1) * P + p];
       bf16* OX = reinterpret_cast<bf16*>(smem + SB_OX);
-      if (lane < 16) {
-        cl = CUM[(C - 1) * P + p];
+      {
         float car = 0.f;
-        for (int s = 64 * (1 - wg); s < 64 * (2 - wg); ++s)
+        for (int s = 32 * kq; s < 32 * kq + 32; ++s)
           car += __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DS + sw_off(N, s, p))) *
                  __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_S + sw_off(N, s, p)));
         if (cl > -20.f) dclp += car * __expf(cl);
       }
+      {
+        float ydv[16];
+        const float* ydr = yd_t + ch * (C * P) + p * C + 16 * J;
 #pragma unroll
-      for (int jj = 1; jj >= 0; --jj) {
-        const int J = jb + jj;
-        float ddd[16], yo[16];
-        tmem_ld16(tmem_at(tmem, quarter, TM_DDD + 16 * J), ddd);
-        tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * J), yo);
-        if (lane < 16) {
-          float ydv[16];
-          const float* ydr = yd_t + ch * (C * P) + p * C + 16 * J;
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 v4 = *reinterpret_cast<const float4*>(ydr + 4 * q4);
-            ydv[4 * q4] = v4.x; ydv[4 * q4 + 1] = v4.y; ydv[4 * q4 + 2] = v4.z; ydv[4 * q4 + 3] = v4.w;
-          }
-          const float cs = CUM[(16 * J + 15) * P + p];
-#pragma unroll
-          for (int r = 15; r >= 0; --r) {
-            const int i = 16 * J + r, il = 16 * jj + r;
-            const float ci = CUM[i * P + p];
-            const float dyv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i, p)));
-            const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
-            const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
-            const float bx = clip4(dtv * xv);
-            const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[p * C + i];
-            const float dlt = cl - ci;
-            const float ds = dds[il] * __expf(fmaxf(dlt, -20.f));
-            float dc = dyv * ydv[r] - bx * dd;
-            if (ci > -20.f) dc += dyv * yo[r] * __expf(ci);
-            if (dlt > -20.f) {
-              dc -= bx * ds;
-              dclp += bx * ds;
-            }
-            local += dc;
-            suf[il] = local;
-            ddbx[il] = dd + ds;
-            OX[i * P + p] = __float2bfloat16_rn(ddbx[il] * dtv);
-          }
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(ydr + 4 * q4);
+          ydv[4 * q4] = v4.x; ydv[4 * q4 + 1] = v4.y; ydv[4 * q4 + 2] = v4.z; ydv[4 * q4 + 3] = v4.w;
         }
-      }
-      if (lane < 16) {
-        if (wg == 0) XCH[p] = local;
-        XCH[64 + 64 * wg + p] = dclp;
-      }
-      __syncthreads();
-      float dAh = 0.f;
-      if (lane < 16) {
-        const float off = XCH[64 + p] + XCH[128 + p] + (wg == 1 ? XCH[p] : 0.f);
-        bf16* ODT = reinterpret_cast<bf16*>(smem + SB_ODT);
+        const float cs = CUM[(16 * J + 15) * P + p];
 #pragma unroll
-        for (int il = 0; il < 32; ++il) {
-          const int i = 16 * jb + il;
+        for (int r = 15; r >= 0; --r) {
+          const int i = 16 * J + r;
+          const float ci = CUM[i * P + p];
+          const float dyv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DY + sw_off(C, i, p)));
           const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
           const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
-          const float g = off + suf[il];
+          const float bx = clip4(dtv * xv);
+          const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[p * C + i];
+          const float dlt = cl - ci;
+          const float ds = dds[r] * __expf(fmaxf(dlt, -20.f));
+          float dc = dyv * ydv[r] - bx * dd;
+          if (ci > -20.f) dc += dyv * yo[r] * __expf(ci);
+          if (dlt > -20.f) {
+            dc -= bx * ds;
+            dclp += bx * ds;
+          }
+          local += dc;
+          suf[r] = local;
+          ddbx[r] = dd + ds;
+          OX[i * P + p] = __float2bfloat16_rn(ddbx[r] * dtv);
+        }
+      }
+      XCH[kq * 64 + p] = local;
+      XCH[(4 + kq) * 64 + p] = dclp;
+      __syncthreads();
+      float dAh = 0.f;
+      {
+        float off = XCH[4 * 64 + p] + XCH[5 * 64 + p] + XCH[6 * 64 + p] + XCH[7 * 64 + p];
+        for (int k2 = 0; k2 < kq; ++k2) off += XCH[k2 * 64 + p];
+        bf16* ODT = reinterpret_cast<bf16*>(smem + SB_ODT);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const int i = 16 * J + r;
+          const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
+          const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
+          const float g = off + suf[r];
           const float pre = dtv * Ah;
           const float gA = (pre > -20.f && pre < 20.f) ? g : 0.f;
-          ODT[i * P + p] = __float2bfloat16_rn(ddbx[il] * xv + gA * Ah);
+          ODT[i * P + p] = __float2bfloat16_rn(ddbx[r] * xv + gA * Ah);
           dAh += gA * dtv;
         }
       }
