@@ -1246,11 +1246,13 @@ void copy_out(torch::Tensor src, torch::Tensor peers, int64_t off_bytes) {
 
 // acc (N,) fp32 += column sums of dy (M, N) bf16: the bias gradient added into the gradient store
 void bias_grad_acc(torch::Tensor dy, torch::Tensor acc) {
-  TORCH_CHECK(dy.is_cuda() && dy.scalar_type() == at::kBFloat16 && dy.dim() == 2 && dy.is_contiguous() &&
-                  dy.size(1) % 8 == 0, "bias_grad_acc: dy bf16 (M, N), N % 8 == 0");
+  TORCH_CHECK(dy.is_cuda() && dy.scalar_type() == at::kBFloat16 && dy.dim() == 2 && dy.stride(1) == 1 &&
+                  dy.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0 &&
+                  dy.size(1) % 8 == 0,
+              "bias_grad_acc: dy bf16 (M, N), N % 8 == 0, unit column stride, 16-byte-aligned rows");
   TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() == dy.size(1),
               "bias_grad_acc: acc fp32 (N,)");
-  ahb_bias_grad_acc(dy.data_ptr(), dy.size(0), (int)dy.size(1), acc.data_ptr<float>(), cur_stream());
+  ahb_bias_grad_acc(dy.data_ptr(), dy.size(0), (int)dy.size(1), dy.stride(0), acc.data_ptr<float>(), cur_stream());
   check_launch("ahb_bias_grad_acc");
 }
 
@@ -1307,9 +1309,12 @@ static torch::Tensor dense_off(int64_t M, int64_t tile, const torch::Device& dev
   return t;
 }
 
+// 2-D bf16 with unit column stride and 16-byte-aligned rows (a column slice of wider rows is fine)
 static void check_dense(const torch::Tensor& t, const char* n) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.is_contiguous(), "dense: ", n,
-              " must be a contiguous 2-D bf16 CUDA tensor");
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 &&
+                  t.stride(0) % 8 == 0 && t.stride(0) >= t.size(1) &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "dense: ", n, " must be a 2-D bf16 CUDA tensor with unit column stride and 16-byte-aligned rows");
 }
 
 torch::Tensor dense_fwd(torch::Tensor x, torch::Tensor W, c10::optional<torch::Tensor> bias) {
@@ -1325,9 +1330,9 @@ torch::Tensor dense_fwd(torch::Tensor x, torch::Tensor W, c10::optional<torch::T
   const bool pair = dense_pair(M);
   auto off = dense_off(M, pair ? 256 : 128, x.device());
   auto y = torch::empty({M, N}, x.options());
-  int rc = ahb_dense_gemm(0, x.data_ptr(), W.data_ptr(), M, (int)K, (int)N, bc.defined() ? bc.data_ptr() : nullptr,
-                          nullptr, y.data_ptr(), off.data_ptr<int>(), err_word().data_ptr<int>(), num_sms(),
-                          cur_stream(), pair);
+  int rc = ahb_dense_gemm(0, x.data_ptr(), x.stride(0), W.data_ptr(), W.stride(0), M, (int)K, (int)N,
+                          bc.defined() ? bc.data_ptr() : nullptr, nullptr, y.data_ptr(), off.data_ptr<int>(),
+                          err_word().data_ptr<int>(), num_sms(), cur_stream(), pair);
   gemm_check(rc, "dense fwd");
   return y;
 }
@@ -1337,13 +1342,14 @@ void dense_dgrad(torch::Tensor dy, torch::Tensor W, torch::Tensor dx, bool accum
   check_dense(dy, "dy");
   check_dense(W, "W");
   check_dense(dx, "dx");
+  TORCH_CHECK(dx.is_contiguous(), "dense_dgrad: dx contiguous");
   const int64_t M = dy.size(0), Nout = dy.size(1), Kin = W.size(0);
   TORCH_CHECK(W.size(1) == Nout && dx.size(0) == M && dx.size(1) == Kin && Nout % 64 == 0 && Kin % 32 == 0,
               "dense_dgrad: dy (M,out), W (in,out), dx (M,in), out % 64, in % 32");
   const bool pair = dense_pair(M);
   auto off = dense_off(M, pair ? 256 : 128, dy.device());
-  int rc = ahb_dense_gemm(1, dy.data_ptr(), W.data_ptr(), M, (int)Nout, (int)Kin, nullptr,
-                          accumulate ? dx.data_ptr() : nullptr, dx.data_ptr(), off.data_ptr<int>(),
+  int rc = ahb_dense_gemm(1, dy.data_ptr(), dy.stride(0), W.data_ptr(), W.stride(0), M, (int)Nout, (int)Kin,
+                          nullptr, accumulate ? dx.data_ptr() : nullptr, dx.data_ptr(), off.data_ptr<int>(),
                           err_word().data_ptr<int>(), num_sms(), cur_stream(), pair);
   gemm_check(rc, "dense dgrad");
 }
@@ -1358,8 +1364,9 @@ void dense_wgrad(torch::Tensor x, torch::Tensor dy, torch::Tensor acc) {
               "dense_wgrad: x (M,in), dy (M,out), fp32 acc (in,out), in % 128, out % 32");
   const bool pair = moe_pair() && K % 256 == 0;
   auto off = dense_off(M, 64, x.device());
-  int rc = ahb_dense_gemm(2, x.data_ptr(), dy.data_ptr(), M, (int)K, (int)N, nullptr, nullptr, acc.data_ptr(),
-                          off.data_ptr<int>(), err_word().data_ptr<int>(), num_sms(), cur_stream(), pair);
+  int rc = ahb_dense_gemm(2, x.data_ptr(), x.stride(0), dy.data_ptr(), dy.stride(0), M, (int)K, (int)N, nullptr,
+                          nullptr, acc.data_ptr(), off.data_ptr<int>(), err_word().data_ptr<int>(), num_sms(),
+                          cur_stream(), pair);
   gemm_check(rc, "dense wgrad");
 }
 

@@ -129,8 +129,8 @@ __global__ void colsum_add_kernel(const float* __restrict__ part, int nb, int D,
 // acc[c] += sum_r dy[r, c]  (dy bf16 (M, N) row-major, N % 8 == 0).  A block covers 256 columns
 // (32 threads x 8 columns, 16-byte loads) and a slice of the rows (8 row lanes); the row lanes
 // are reduced in shared memory and each column gets one fp32 atomic per block.
-__global__ void bias_grad_kernel(const __nv_bfloat16* __restrict__ dy, int64_t M, int N, int64_t rows_per,
-                                 float* __restrict__ acc) {
+__global__ void bias_grad_kernel(const __nv_bfloat16* __restrict__ dy, int64_t M, int N, int64_t ld,
+                                 int64_t rows_per, float* __restrict__ acc) {
   __shared__ float red[8][257];
   const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
   const int c0 = blockIdx.x * 256 + cg * 8;
@@ -138,7 +138,7 @@ __global__ void bias_grad_kernel(const __nv_bfloat16* __restrict__ dy, int64_t M
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (c0 < N) {
     for (int64_t r = r_lo + rl; r < r_hi; r += 8) {
-      const uint4 u = *reinterpret_cast<const uint4*>(dy + r * N + c0);
+      const uint4 u = *reinterpret_cast<const uint4*>(dy + r * ld + c0);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -160,7 +160,7 @@ __global__ void bias_grad_kernel(const __nv_bfloat16* __restrict__ dy, int64_t M
   }
 }
 
-void ahb_bias_grad_acc(const void* dy, int64_t M, int N, float* acc, cudaStream_t st) {
+void ahb_bias_grad_acc(const void* dy, int64_t M, int N, int64_t ld, float* acc, cudaStream_t st) {
   if (M <= 0 || N <= 0) return;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -170,7 +170,7 @@ void ahb_bias_grad_acc(const void* dy, int64_t M, int N, float* acc, cudaStream_
   int64_t rows_per = (M + gy - 1) / gy;
   rows_per = (rows_per + 7) / 8 * 8;
   gy = (M + rows_per - 1) / rows_per;
-  bias_grad_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>((const __nv_bfloat16*)dy, M, N, rows_per, acc);
+  bias_grad_kernel<<<dim3(gx, (unsigned)gy), 256, 0, st>>>((const __nv_bfloat16*)dy, M, N, ld, rows_per, acc);
 }
 
 // ----------------------------------------------------------------- causal conv1d

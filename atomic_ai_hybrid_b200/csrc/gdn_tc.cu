@@ -404,6 +404,10 @@ constexpr int F2_VN = F2_H + 2 * TILE_CD;         // v_new tile (rows i, columns
 constexpr int F2_BARS = F2_VN + TILE_CD;
 constexpr size_t F2_SMEM = 1024 + F2_BARS + 256;
 
+// NH = 2: the value columns split over two CTAs per (batch, head) (blockIdx.z = half; the columns of
+// the state and of v_new evolve independently), for batches with fewer (batch, head) pairs than half
+// the SMs; each CTA keeps 64 columns and writes its slab of the per-chunk images.
+template <int NH>
 __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     const unsigned char* __restrict__ wt_t, const unsigned char* __restrict__ u_t,
     const unsigned char* __restrict__ qg_t, const unsigned char* __restrict__ kg_t,
@@ -417,7 +421,10 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const uint32_t sH = smem_u32(smem + F2_H), sVN = smem_u32(smem + F2_VN);
 
-  const int h = blockIdx.x, b = blockIdx.y;
+  constexpr int DV = D / NH;  // value columns of this CTA
+  constexpr uint32_t TCOLS = NH == 1 ? 512 : 256;
+  // TMEM: V [0, DV), O1 [DV, 2 DV), O2 [2 DV, 3 DV), HH [3 DV, 4 DV)
+  const int h = blockIdx.x, b = blockIdx.y, v0 = DV * (int)blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t bh = (int64_t)b * H + h;
   const SeqIdx ix{L, H};
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     *abort_flag = 0;
     sm100::fence_barrier_init();
   }
-  if (warp == 0) sm100::tmem_alloc(tmem_slot, 512);
+  if (warp == 0) sm100::tmem_alloc(tmem_slot, TCOLS);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -446,21 +453,22 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     if (NC > 1) issue(1);
   }
   const int dk = tid;
-  float hr[D];
+  float hr[DV];
 #pragma unroll
-  for (int c = 0; c < D; ++c) hr[c] = h0 ? h0[(bh * D + dk) * D + c] : 0.f;
+  for (int c = 0; c < DV; ++c) hr[c] = h0 ? h0[(bh * D + dk) * D + v0 + c] : 0.f;
 
-  constexpr uint32_t ID_ROWS = sm100::idesc_bf16(64, 128, false, true);  // chunk rows x dv
-  constexpr uint32_t ID_STATE = sm100::idesc_bf16(128, 128, true, true);  // dk x dv
+  constexpr uint32_t ID_ROWS = sm100::idesc_bf16(64, DV, false, true);  // chunk rows x dv
+  constexpr uint32_t ID_STATE = sm100::idesc_bf16(128, DV, true, true);  // dk x dv
   int n = 0;
   for (; n < NC; ++n) {
     const int64_t cbn = bh * NC + n;
     const uint32_t st = smem_u32(smem + (n & 1) * F2_STAGE);
     // state row dk -> operand tile (MN-major B: rows dk, columns dv) and the per-chunk store
 #pragma unroll
-    for (int c = 0; c < D; c += 8) {
+    for (int c = 0; c < DV; c += 8) {
       st_chunk8(sH + sw_off16(D, dk, c), hr + c);
-      if (h_store) *reinterpret_cast<uint4*>(h_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, c)) = pack8(hr + c);
+      if (h_store)
+        *reinterpret_cast<uint4*>(h_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, v0 + c)) = pack8(hr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -471,7 +479,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
       if (!*abort_flag) {
         auto fh = [&](int s) { return mndesc(sH, D, s); };
         mma_steps(tmem, [&](int s) { return kdesc(st, C, s); }, fh, D / 16, ID_ROWS, false);
-        mma_steps(tmem + 128, [&](int s) { return kdesc(st + TILE_CD, C, s); }, fh, D / 16, ID_ROWS, false);
+        mma_steps(tmem + DV, [&](int s) { return kdesc(st + TILE_CD, C, s); }, fh, D / 16, ID_ROWS, false);
       }
       sm100::umma_commit(bars + 2);
     }
@@ -482,18 +490,19 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
       const int i = 16 * warp + lane;
       const unsigned char* u_c = u_t + cbn * TILE_CD;
 #pragma unroll 1
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < DV / 32; ++p) {
         float x[32];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
         if (lane < 16)
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             float uu[8], y[8];
-            unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, 32 * p + c)), uu);
+            unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, v0 + 32 * p + c)), uu);
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = uu[e] - x[c + e];
             st_chunk8(sVN + sw_off16(C, i, 32 * p + c), y);
-            if (vn_store) *reinterpret_cast<uint4*>(vn_store + cbn * TILE_CD + sw_off16(C, i, 32 * p + c)) = pack8(y);
+            if (vn_store)
+              *reinterpret_cast<uint4*>(vn_store + cbn * TILE_CD + sw_off16(C, i, v0 + 32 * p + c)) = pack8(y);
           }
       }
     }
@@ -504,8 +513,8 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     if (tid == 0) {
       sm100::tc_fence_after();
       auto fvn = [&](int s) { return mndesc(sVN, C, s); };
-      mma_steps(tmem + 256, [&](int s) { return kdesc(st + 3 * TILE_CD, C, s); }, fvn, C / 16, ID_ROWS, false);
-      mma_steps(tmem + 384, [&](int s) { return mndesc(st + 2 * TILE_CD, C, s); }, fvn, C / 16, ID_STATE, false);
+      mma_steps(tmem + 2 * DV, [&](int s) { return kdesc(st + 3 * TILE_CD, C, s); }, fvn, C / 16, ID_ROWS, false);
+      mma_steps(tmem + 3 * DV, [&](int s) { return mndesc(st + 2 * TILE_CD, C, s); }, fvn, C / 16, ID_STATE, false);
       sm100::umma_commit(bars + 3);
     }
     if (!wait_bar(bars + 3, n & 1, err, 0x4713)) *abort_flag = 1;
@@ -514,26 +523,26 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
       const int i = 16 * warp + lane;
       bf16* orow = o + ix.row(b, (int64_t)n * C + i, h);
 #pragma unroll 1
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < DV / 32; ++p) {
         float x1[32], x2[32];
-        tmem_ld32(tmem_at(tmem, warp, 128 + 32 * p), x1);
-        tmem_ld32(tmem_at(tmem, warp, 256 + 32 * p), x2);
+        tmem_ld32(tmem_at(tmem, warp, DV + 32 * p), x1);
+        tmem_ld32(tmem_at(tmem, warp, 2 * DV + 32 * p), x2);
         if (lane < 16)
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             float y[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = guard(scale * x1[c + e] + x2[c + e]);
-            *reinterpret_cast<uint4*>(orow + 32 * p + c) = pack8(y);
+            *reinterpret_cast<uint4*>(orow + v0 + 32 * p + c) = pack8(y);
           }
       }
     }
     {
       const float eg = __expf(gcl[cbn * D + dk]);
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < DV / 32; ++p) {
         float x[32];
-        tmem_ld32(tmem_at(tmem, warp, 384 + 32 * p), x);
+        tmem_ld32(tmem_at(tmem, warp, 3 * DV + 32 * p), x);
 #pragma unroll
         for (int e = 0; e < 32; ++e) hr[32 * p + e] = sanitize(eg * hr[32 * p + e] + x[e], 1e4f);
       }
@@ -545,7 +554,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   }
   if (h_final && n == NC)
 #pragma unroll
-    for (int c = 0; c < D; ++c) h_final[(bh * D + dk) * D + c] = hr[c];
+    for (int c = 0; c < DV; ++c) h_final[(bh * D + dk) * D + v0 + c] = hr[c];
   if (*abort_flag && tid == 0) {  // let copies in flight land before the CTA exits
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -553,7 +562,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+  if (warp == 0) sm100::tmem_dealloc(tmem, TCOLS);
 }
 
 // ============================================================ state recurrence, backward
@@ -571,6 +580,8 @@ constexpr int B1_DVN = B1_DH + 2 * TILE_CD;
 constexpr int B1_BARS = B1_DVN + TILE_CD;
 constexpr size_t B1_SMEM = 1024 + B1_BARS + 256;
 
+// NH = 2: the value columns split over two CTAs per (batch, head), as in the forward.
+template <int NH>
 __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     const __grid_constant__ CUtensorMap tm_do, const unsigned char* __restrict__ wt_t,
     const unsigned char* __restrict__ qg_t, const unsigned char* __restrict__ kg_t,
@@ -584,7 +595,10 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const uint32_t sDH = smem_u32(smem + B1_DH), sDVN = smem_u32(smem + B1_DVN);
 
-  const int h = blockIdx.x, b = blockIdx.y;
+  constexpr int DV = D / NH;  // value columns of this CTA
+  constexpr uint32_t TCOLS = NH == 1 ? 512 : 256;
+  // TMEM: DVN [0, DV), D1 [DV, 2 DV), D2 [2 DV, 3 DV)
+  const int h = blockIdx.x, b = blockIdx.y, v0 = DV * (int)blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t bh = (int64_t)b * H + h;
   if (tid == 0) {
@@ -593,7 +607,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     sm100::fence_barrier_init();
     sm100::prefetch_tmap(&tm_do);
   }
-  if (warp == 0) sm100::tmem_alloc(tmem_slot, 512);
+  if (warp == 0) sm100::tmem_alloc(tmem_slot, TCOLS);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -602,36 +616,36 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   auto issue = [&](int n, int s) {
     unsigned char* st = smem + s * B1_STAGE;
     const int64_t c = bh * NC + n;
-    sm100::mbar_expect_tx(bars + s, B1_STAGE);
+    sm100::mbar_expect_tx(bars + s, B1_STAGE - (NH == 2 ? TILE_CD / 2 : 0));
     bulk_g2s(st, wt_t + c * TILE_CD, TILE_CD, bars + s);
     bulk_g2s(st + TILE_CD, qg_t + c * TILE_CD, TILE_CD, bars + s);
     bulk_g2s(st + 2 * TILE_CD, kg_t + c * TILE_CD, TILE_CD, bars + s);
     bulk_g2s(st + 3 * TILE_CD, aqk_t + c * TILE_CC, TILE_CC, bars + s);
     const int row = b * L + n * C;
-    tma_load_3d(st + B1_DO, &tm_do, bars + s, 0, h, row);
-    tma_load_3d(st + B1_DO + TILE_CD / 2, &tm_do, bars + s, 64, h, row);
+    tma_load_3d(st + B1_DO, &tm_do, bars + s, v0, h, row);  // this CTA's 64-column box(es) of do
+    if (NH == 1) tma_load_3d(st + B1_DO + TILE_CD / 2, &tm_do, bars + s, 64, h, row);
   };
   if (tid == 0) {
     issue(NC - 1, 0);
     if (NC > 1) issue(NC - 2, 1);
   }
   const int dk = tid;
-  float dr[D];
+  float dr[DV];
 #pragma unroll
-  for (int c = 0; c < D; ++c) dr[c] = dh_final ? dh_final[(bh * D + dk) * D + c] : 0.f;
+  for (int c = 0; c < DV; ++c) dr[c] = dh_final ? dh_final[(bh * D + dk) * D + v0 + c] : 0.f;
 
-  constexpr uint32_t ID_RR = sm100::idesc_bf16(64, 128, true, true);    // rows i x dv, A = Aqk^T (MN)
-  constexpr uint32_t ID_RK = sm100::idesc_bf16(64, 128, false, true);   // rows i x dv, A = kg (K-major)
-  constexpr uint32_t ID_ST = sm100::idesc_bf16(128, 128, true, true);   // dk x dv
+  constexpr uint32_t ID_RR = sm100::idesc_bf16(64, DV, true, true);    // rows i x dv, A = Aqk^T (MN)
+  constexpr uint32_t ID_RK = sm100::idesc_bf16(64, DV, false, true);   // rows i x dv, A = kg (K-major)
+  constexpr uint32_t ID_ST = sm100::idesc_bf16(128, DV, true, true);   // dk x dv
   int it = 0;
   for (; it < NC; ++it) {
     const int n = NC - 1 - it, s = it & 1;
     const int64_t cbn = bh * NC + n;
     const uint32_t st = smem_u32(smem + s * B1_STAGE);
 #pragma unroll
-    for (int c = 0; c < D; c += 8) {
+    for (int c = 0; c < DV; c += 8) {
       st_chunk8(sDH + sw_off16(D, dk, c), dr + c);
-      *reinterpret_cast<uint4*>(dh_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, c)) = pack8(dr + c);
+      *reinterpret_cast<uint4*>(dh_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, v0 + c)) = pack8(dr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -645,7 +659,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
         mma_steps(tmem, [&](int k) { return mndesc(st + 3 * TILE_CD, C, k); }, fdo, C / 16, ID_RR, false);
         mma_steps(tmem, [&](int k) { return kdesc(st + 2 * TILE_CD, C, k); }, [&](int k) { return mndesc(sDH, D, k); },
                   D / 16, ID_RK, true);
-        mma_steps(tmem + 128, [&](int k) { return mndesc(st + TILE_CD, C, k); }, fdo, C / 16, ID_ST, false);
+        mma_steps(tmem + DV, [&](int k) { return mndesc(st + TILE_CD, C, k); }, fdo, C / 16, ID_ST, false);
       }
       sm100::umma_commit(bars + 2);
     }
@@ -654,14 +668,14 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     {
       const int i = 16 * warp + lane;
 #pragma unroll 1
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < DV / 32; ++p) {
         float x[32];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
         if (lane < 16)
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             st_chunk8(sDVN + sw_off16(C, i, 32 * p + c), x + c);
-            *reinterpret_cast<uint4*>(dvn_store + cbn * TILE_CD + sw_off16(C, i, 32 * p + c)) = pack8(x + c);
+            *reinterpret_cast<uint4*>(dvn_store + cbn * TILE_CD + sw_off16(C, i, v0 + 32 * p + c)) = pack8(x + c);
           }
       }
     }
@@ -671,8 +685,8 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     if (*abort_flag) break;
     if (tid == 0) {
       sm100::tc_fence_after();
-      mma_steps(tmem + 256, [&](int k) { return mndesc(st, C, k); }, [&](int k) { return mndesc(sDVN, C, k); }, C / 16,
-                ID_ST, false);
+      mma_steps(tmem + 2 * DV, [&](int k) { return mndesc(st, C, k); }, [&](int k) { return mndesc(sDVN, C, k); },
+                C / 16, ID_ST, false);
       sm100::umma_commit(bars + 3);
     }
     if (!wait_bar(bars + 3, it & 1, err, 0x4723)) *abort_flag = 1;
@@ -680,10 +694,10 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     {
       const float eg = __expf(gcl[cbn * D + dk]);
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < DV / 32; ++p) {
         float x1[32], x2[32];
-        tmem_ld32(tmem_at(tmem, warp, 128 + 32 * p), x1);
-        tmem_ld32(tmem_at(tmem, warp, 256 + 32 * p), x2);
+        tmem_ld32(tmem_at(tmem, warp, DV + 32 * p), x1);
+        tmem_ld32(tmem_at(tmem, warp, 2 * DV + 32 * p), x2);
 #pragma unroll
         for (int e = 0; e < 32; ++e) dr[32 * p + e] = eg * dr[32 * p + e] + scale * x1[e] - x2[e];
       }
@@ -695,7 +709,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   }
   if (dh0 && it == NC)
 #pragma unroll
-    for (int c = 0; c < D; ++c) dh0[(bh * D + dk) * D + c] = dr[c];
+    for (int c = 0; c < DV; ++c) dh0[(bh * D + dk) * D + v0 + c] = dr[c];
   if (*abort_flag && tid == 0) {
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -703,7 +717,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
-  if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+  if (warp == 0) sm100::tmem_dealloc(tmem, TCOLS);
 }
 
 // ============================================================ chunk-parallel backward
@@ -1208,26 +1222,40 @@ int ahb_gdn_chunk_fwd_tc(const void* q, const void* k, const void* v, const floa
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
+// the value columns split over two CTAs when the (batch, head) pairs fill at most half the SMs
+static bool gdn_state_split(int B, int H) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return 2 * B * H <= sms;
+}
+
 int ahb_gdn_state_fwd_tc(const void* wt_t, const void* u_t, const void* qg_t, const void* kg_t, const void* aqk_t,
                          const float* gcl, float scale, int B, int L, int H, const float* h0, void* o, float* h_final,
                          void* h_store, void* vn_store, int* err, cudaStream_t st) {
-  static int init = set_smem(gdn_state_fwd_tc, F2_SMEM);
+  static int init = set_smem(gdn_state_fwd_tc<1>, F2_SMEM) | set_smem(gdn_state_fwd_tc<2>, F2_SMEM);
   if (init) return init;
-  gdn_state_fwd_tc<<<dim3(H, B), F2_THREADS, F2_SMEM, st>>>(
+  const bool split = gdn_state_split(B, H);
+  auto k = split ? gdn_state_fwd_tc<2> : gdn_state_fwd_tc<1>;
+  k<<<dim3(H, B, split ? 2 : 1), F2_THREADS, F2_SMEM, st>>>(
       (const unsigned char*)wt_t, (const unsigned char*)u_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
       (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, h0, (bf16*)o, h_final, (unsigned char*)h_store,
       (unsigned char*)vn_store, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
-
 int ahb_gdn_state_bwd_tc(const void* wt_t, const void* qg_t, const void* kg_t, const void* aqk_t, const float* gcl,
                          const void* dout, float scale, int B, int L, int H, const float* dh_final, void* dh_store,
                          void* dvn_store, float* dh0, int* err, cudaStream_t st) {
-  static int init = set_smem(gdn_state_bwd_tc, B1_SMEM);
+  static int init = set_smem(gdn_state_bwd_tc<1>, B1_SMEM) | set_smem(gdn_state_bwd_tc<2>, B1_SMEM);
   if (init) return init;
   CUtensorMap tm;
   if (tmap_seq_bf16(&tm, dout, (int64_t)B * L, H, D, C)) return -20;
-  gdn_state_bwd_tc<<<dim3(H, B), B1_THREADS, B1_SMEM, st>>>(
+  const bool split = gdn_state_split(B, H);
+  auto k = split ? gdn_state_bwd_tc<2> : gdn_state_bwd_tc<1>;
+  k<<<dim3(H, B, split ? 2 : 1), B1_THREADS, B1_SMEM, st>>>(
       tm, (const unsigned char*)wt_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
       (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, dh_final, (unsigned char*)dh_store,
       (unsigned char*)dvn_store, dh0, err);

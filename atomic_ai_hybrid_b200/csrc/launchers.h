@@ -204,7 +204,8 @@ void ahb_symm_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t e
                       cudaStream_t st);
 void ahb_reduce_scatter_f32(const float* const* peers_dev, int world, int64_t lo, int64_t n, float* out,
                             cudaStream_t st);
-void ahb_bias_grad_acc(const void* dy, int64_t M, int N, float* acc, cudaStream_t st);
+// acc (N,) += column sums of dy (M, N) with row stride ld (elements, a multiple of 8)
+void ahb_bias_grad_acc(const void* dy, int64_t M, int N, int64_t ld, float* acc, cudaStream_t st);
 // tensor parallelism over peer memory
 int ahb_gemm_rs_peer(const void* a, int64_t a_rows, int64_t K, const void* b, int64_t N, const int* grp_off, int W,
                      void* const* out_tab, int m_rot, int* err, int num_sms, cudaStream_t st);
@@ -216,9 +217,9 @@ void ahb_copy_out(const void* src, void* const* peers_dev, int world, int64_t of
 // ce.cu: label-smoothed cross entropy over bf16 logits rows, gradient written in place
 // Dense projections on the grouped GEMM (moe_gemm.cu): mode 0 y = x W (+ bias) (+ beta_src), mode 1
 // y = dy W^T (+ beta_src), mode 2 acc fp32 += x^T dy; grp_off = {0, M padded to the tile height}
-int ahb_dense_gemm(int mode, const void* a, const void* b, int64_t M, int K, int N, const void* bias,
-                   const void* beta_src, void* out, const int* grp_off, int* err, int num_sms, cudaStream_t st,
-                   bool pair);
+int ahb_dense_gemm(int mode, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int K, int N,
+                   const void* bias, const void* beta_src, void* out, const int* grp_off, int* err, int num_sms,
+                   cudaStream_t st, bool pair);
 // LM-head GEMM with a cross-entropy epilogue (moe_gemm.cu; see there), and the row combine of its
 // forward partials: lse per row, sum of the label-smoothed losses and of the valid rows (ce.cu)
 int ahb_ce_gemm(bool bwd, const void* h, int64_t rows, int d, const void* W, int V, const int* grp_off,

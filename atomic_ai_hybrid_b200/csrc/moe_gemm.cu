@@ -79,6 +79,7 @@ struct Params {
   const bf16* bias;
   const bf16* beta_src;
   int acc_bf16;  // EPI_ACC into bf16 accumulators (AHB_GEMM_ACC_BF16)
+  int sk_nkb;    // CTA-pair kernel, one K-grouped group: stream-K over tiles x sk_nkb k-blocks (0: off)
 };
 
 AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
@@ -152,7 +153,7 @@ AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, T
 // `m_limit`, when set, are not written).
 template <int EPI, int NB>
 AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, uint32_t tb, int row_base, int lane,
-                              unsigned char* stg_base, int q) {
+                              unsigned char* stg_base, int q, bool atomic = false) {
   constexpr int BNA = 256 / NB;
   const int row = row_base + lane;
   const int n0 = t.n0 * BNA;
@@ -305,6 +306,12 @@ AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, ui
       const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
       if (p.acc_bf16) {  // the product summed in fp32, rounded once as it is added
         acc_add_bf16(static_cast<bf16*>(p.out0) + oo, v0, alpha);
+      } else if (atomic) {  // a piece of a tile split between pairs (stream-K)
+        float* d0p = static_cast<float*>(p.out0) + oo;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          atomicAdd(reinterpret_cast<float4*>(d0p + i),
+                    make_float4(alpha * v0[i], alpha * v0[i + 1], alpha * v0[i + 2], alpha * v0[i + 3]));
       } else {
         float* d0p = static_cast<float*>(p.out0) + oo;
 #pragma unroll
@@ -475,7 +482,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int row_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -509,7 +515,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
 // the MMA role; both CTAs' TMA loads complete on the leader's `full` barrier; its commits
 // arrive on `empty` / `tfull` of both CTAs; both CTAs' epilogue warps release an accumulator on
 // the leader's `tempty`.  M-grouped groups (and K-grouped Mout) must be multiples of 256 rows.
-constexpr int PAIR_BM = 256, PAIR_STAGES = 6;
+// Seven 32 KB stages (224 KB of the 227 KB a CTA may take).
+//
+// Stream-K (one K-grouped group, `sk_nkb` > 0): a 2048 x 2048 weight gradient has 64 tiles for 74
+// pairs, a wave 86 % full whatever the tile size.  Each pair then takes an equal share of the
+// (tile, k-block) iterations; a pair that covers a whole tile adds it as usual, the pieces of a
+// tile split between pairs are added with fp32 atomics.
+constexpr int PAIR_BM = 256, PAIR_STAGES = 7;
 constexpr int PAIR_A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's 128 rows
 constexpr int PAIR_B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the 256 columns
 constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
@@ -539,6 +551,51 @@ AHB_DEVICE void decode_pair(const Params& p, const int* off, int tile, int n_til
     t.nkb = (off[t.e + 1] - off[t.e]) / BK;
   }
 }
+
+// One unit of work of a pair: a tile and its k-blocks [kb0, kb1); `whole` when they are all of the
+// tile's.  Every role of both CTAs walks the same sequence.
+struct PairWork {
+  Tile t;
+  int kb0, kb1;
+  bool whole;
+};
+
+template <bool KGROUP>
+struct PairSched {
+  const Params& p;
+  const int* off;
+  int n_tiles, total, ncl;
+  int tile;             // next tile (plain schedule)
+  int64_t u, u_end;     // iteration range (stream-K)
+  AHB_DEVICE PairSched(const Params& p_, const int* off_, int n_tiles_, int total_, int cid, int ncl_)
+      : p(p_), off(off_), n_tiles(n_tiles_), total(total_), ncl(ncl_), tile(cid), u(0), u_end(0) {
+    if (KGROUP && p.sk_nkb > 0) {
+      const int64_t W = (int64_t)total * p.sk_nkb;
+      u = W * cid / ncl;
+      u_end = W * (cid + 1) / ncl;
+    }
+  }
+  AHB_DEVICE bool next(PairWork& w) {
+    if (KGROUP && p.sk_nkb > 0) {
+      if (u >= u_end) return false;
+      const int tl = (int)(u / p.sk_nkb);
+      decode_pair<KGROUP>(p, off, tl, n_tiles, w.t);
+      w.kb0 = (int)(u % p.sk_nkb);
+      const int64_t left = u_end - u;
+      w.kb1 = left < (int64_t)(p.sk_nkb - w.kb0) ? w.kb0 + (int)left : p.sk_nkb;
+      w.whole = w.kb0 == 0 && w.kb1 == p.sk_nkb;
+      u += w.kb1 - w.kb0;
+      return true;
+    }
+    if (tile >= total) return false;
+    decode_pair<KGROUP>(p, off, tile, n_tiles, w.t);
+    w.kb0 = 0;
+    w.kb1 = w.t.nkb;
+    w.whole = true;
+    tile += ncl;
+    return true;
+  }
+};
 
 template <bool KGROUP, bool A_MN, bool B_MN, int NB, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gemm_pair_kernel(const __grid_constant__ Params p) {
@@ -590,12 +647,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gem
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = cid; tile < total && ok; tile += ncl) {
-      Tile t;
-      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
+    PairSched<KGROUP> sched(p, off, n_tiles, total, cid, ncl);
+    PairWork wk;
+    while (ok && sched.next(wk)) {
+      const Tile& t = wk.t;
       const int n0 = t.n0 * BNA;
       const int mrow = t.m0 + 128 * (int)rank;
-      for (int kb = 0; kb < t.nkb; ++kb) {
+      for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
         if (!mbar_wait(empty + stage, phase ^ 1, abort_flag, p.err, 11)) { ok = false; break; }
         unsigned char* sa = smem + stage * PAIR_STAGE_BYTES;
         unsigned char* sb = sa + PAIR_A_BYTES;
@@ -649,14 +707,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gem
     uint32_t acc_phase = 0;
     bool ok = true;
     bool issued = false;
-    for (int tile = cid; tile < total && ok; tile += ncl) {
-      Tile t;
-      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
-      if (t.nkb == 0) continue;
+    PairSched<KGROUP> sched(p, off, n_tiles, total, cid, ncl);
+    PairWork wk;
+    while (ok && sched.next(wk)) {
+      if (wk.kb1 <= wk.kb0) continue;
       if (!mbar_wait(tempty + acc, acc_phase ^ 1, abort_flag, p.err, 12)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d0 = tmem_base + acc * 256;
-      for (int kb = 0; kb < t.nkb; ++kb) {
+      for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
         if (!mbar_wait(full + stage, phase, abort_flag, p.err, 13)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + stage * PAIR_STAGE_BYTES);
@@ -668,7 +726,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gem
           for (int nb = 0; nb < NB; ++nb) {
             const uint32_t sbn = sb + nb * HALF * BK * 2;
             const uint64_t bd = B_MN ? smem_desc(sbn + k * 2048, 8192, 1024) : smem_desc(sbn + k * 32, 16, 1024);
-            umma_bf16_pair(d0 + nb * BNA, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16_pair(d0 + nb * BNA, ad, bd, IDESC, (kb > wk.kb0 || k != 0) ? 1u : 0u);
           }
         }
         issued = true;
@@ -691,14 +749,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gem
     const uint32_t tempty0 = mapa_shared(tempty, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = cid; tile < total; tile += ncl) {
-      Tile t;
-      decode_pair<KGROUP>(p, off, tile, n_tiles, t);
-      if (t.nkb == 0) continue;
+    PairSched<KGROUP> sched(p, off, n_tiles, total, cid, ncl);
+    PairWork wk;
+    while (sched.next(wk)) {
+      if (wk.kb1 <= wk.kb0) continue;
       if (!mbar_wait(tfull + acc, acc_phase, abort_flag, p.err, 14)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
-      epilogue_tile<EPI, NB>(p, off, t, tb, t.m0 + 128 * (int)rank + q * 32, lane, nullptr, q);
+      epilogue_tile<EPI, NB>(p, off, wk.t, tb, wk.t.m0 + 128 * (int)rank + q * 32, lane, nullptr, q, !wk.whole);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * acc);
@@ -852,13 +910,14 @@ int ahb_moe_gemm(int kind, const void* a0, const void* a1, int64_t a_rows, int64
 
 // Dense projection pieces on the grouped GEMM (one group; rows padded to the tile height, rows
 // at or beyond M read as zeros and not stored):
+// (lda / ldb: row strides in elements, multiples of 8: A and B may be column slices of wider rows)
 //   mode 0  y = x W (+ bias) (+ beta_src)    x (M,K) K-major, W (K,N) MN-major
 //   mode 1  y = dy W^T (+ beta_src)          dy (M,K) K-major, W (N,K) K-major (W^T of an (N,K) kernel)
 //   mode 2  acc (K,N) fp32 += x^T dy          x (M,K), dy (M,N), contraction over the M rows
-int ahb_dense_gemm(int mode, const void* a, const void* b, int64_t M, int K, int N, const void* bias,
-                   const void* beta_src, void* out, const int* grp_off, int* err, int num_sms, cudaStream_t st,
-                   bool pair) {
-  if (K % BK != 0 || N % 32 != 0 || M <= 0) return -10;
+int ahb_dense_gemm(int mode, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int K, int N,
+                   const void* bias, const void* beta_src, void* out, const int* grp_off, int* err, int num_sms,
+                   cudaStream_t st, bool pair) {
+  if (K % BK != 0 || N % 32 != 0 || M <= 0 || lda % 8 != 0 || ldb % 8 != 0) return -10;
   Params p;
   memset(&p, 0, sizeof(p));
   p.grp_off = grp_off;
@@ -872,15 +931,21 @@ int ahb_dense_gemm(int mode, const void* a, const void* b, int64_t M, int K, int
   if (mode == 2) {  // K-grouped: Mout = K rows of the weight, contraction over the M token rows
     if (K % (pair ? PAIR_BM : BM) != 0) return -12;
     p.Mout = K;
-    rc |= make_map(&p.ta0, a, M, K, K, 64);
-    rc |= make_map(&p.tb0, b, M, N, N, 64);
+    if (pair) {  // stream-K when whole tiles would leave the pairs' last wave well short of full
+      const int ncl = num_sms / 2, tiles = (K / PAIR_BM) * ((N + 255) / 256);
+      const int waves = (tiles + ncl - 1) / ncl;
+      const int nkb = (int)((M + BK - 1) / BK);
+      if (tiles >= 16 && (double)tiles / ((double)waves * ncl) < 0.95 && nkb >= 8) p.sk_nkb = nkb;
+    }
+    rc |= make_map(&p.ta0, a, M, K, lda, 64);
+    rc |= make_map(&p.tb0, b, M, N, ldb, 64);
   } else {
     p.kb_split = K / BK;
     p.kb_total = K / BK;
     p.m_limit = (int)M;
-    rc |= make_map(&p.ta0, a, M, K, K, BM);
-    if (mode == 0) rc |= make_map(&p.tb0, b, K, N, N, 64);      // W (K rows, N cols), MN-major
-    else rc |= make_map(&p.tb0, b, N, K, K, pair ? 128 : 256);   // W (N rows, K cols), K-major
+    rc |= make_map(&p.ta0, a, M, K, lda, BM);
+    if (mode == 0) rc |= make_map(&p.tb0, b, K, N, ldb, 64);      // W (K rows, N cols), MN-major
+    else rc |= make_map(&p.tb0, b, N, K, ldb, pair ? 128 : 256);   // W (N rows, K cols), K-major
     p.b_rows = mode == 0 ? K : N;
   }
   if (rc) return -20;

@@ -47,6 +47,28 @@ AHB_DEVICE void ld8f(const float* src, float* o) {
   o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
 }
 
+// Decay cumsum of the chunk for 256 threads: CUM[i][p] = clamp(sum_{i' <= i} clamp(dt[i'][p] A, +-20),
+// +-1e4), four threads per channel p (rows [16 k, 16 k + 16) for k = tid >> 6), the block totals of
+// the rows before a block added through `part` (4 x 64 floats of shared memory).  The forward and
+// backward chunk kernels both use it, so their cumsums agree bit for bit.  Ends with __syncthreads.
+AHB_DEVICE void chunk_cumsum(const unsigned char* dt_tile, float Ah, float* CUM, float* part, int tid) {
+  const int p = tid & 63, k = tid >> 6;
+  float v[16], s = 0.f;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(dt_tile + sw_off(C, 16 * k + t, p)));
+    s += fminf(fmaxf(dtv * Ah, -20.f), 20.f);
+    v[t] = s;
+  }
+  part[k * 64 + p] = s;
+  __syncthreads();
+  float off = 0.f;
+  for (int k2 = 0; k2 < k; ++k2) off += part[k2 * 64 + p];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) CUM[(16 * k + t) * P + p] = fminf(fmaxf(off + v[t], -1e4f), 1e4f);
+  __syncthreads();
+}
+
 // ============================================================ chunk-parallel forward
 constexpr int S1_THREADS = 256;
 constexpr int S1_B = 0, S1_C = 16384, S1_X = 32768, S1_DT = 40960, S1_CB = 49152, S1_V = 57344, S1_W0 = 65536,
@@ -95,17 +117,9 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     sm100::umma_commit(bars + 1);
   }
   const float Ah = A[h];
-  if (tid < P) {  // decay cumsum of channel p; span of each 16-row block
-    const int p = tid;
-    float s = 0.f;
-    for (int i = 0; i < C; ++i) {
-      const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_DT + sw_off(C, i, p)));
-      s += fminf(fmaxf(dtv * Ah, -20.f), 20.f);
-      CUM[i * P + p] = fminf(fmaxf(s, -1e4f), 1e4f);
-    }
-    cl_o[ch * P + p] = CUM[(C - 1) * P + p];
-  }
-  __syncthreads();
+  // decay cumsum (block totals exchanged in the V buffer, written only after it)
+  chunk_cumsum(smem + S1_DT, Ah, CUM, reinterpret_cast<float*>(smem + S1_V), tid);
+  if (tid < P) cl_o[ch * P + tid] = CUM[(C - 1) * P + tid];
   // V = dBx e^{max(cl - c, -20)}  (rows j, columns p)
 #pragma unroll
   for (int it = 0; it < (C * P / 8) / S1_THREADS; ++it) {
@@ -132,17 +146,21 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   }
   if (!wait_bar(bars + 1, 0, err, 0x5302)) flags[4] = 1;
   sm100::tc_fence_after();
-  if (wg == 0) {  // causal CB rows (lanes 0-15 of each quarter) -> bf16 K-major tile (rows i, columns j <= i)
-    const int i = 16 * warp + lane;
-    float x[64];
-    tmem_ld32(tmem_at(tmem, warp, 0), x);
-    tmem_ld32(tmem_at(tmem, warp, 32), x + 32);
-    if (lane < 16) {
+  {  // causal CB -> bf16 K-major tile (rows i, columns j <= i): row i = 16 quarter + (lane & 15) sits
+     // in lane i & 15 of the quarter (M = 64); four threads per row, 16 columns each (lanes 16-31
+     // take theirs by shuffle)
+    const int hf = lane >> 4, i = 16 * quarter + (lane & 15), j0 = 32 * wg + 16 * hf;
+    float x[32], y[16];
+    tmem_ld32(tmem_at(tmem, quarter, 32 * wg), x);
 #pragma unroll
-      for (int j = 0; j < 64; ++j) x[j] = j <= i ? clip4(x[j]) : 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) st_chunk8(S + S1_CB + sw_off16(C, i, c), x + c);
+    for (int e = 0; e < 16; ++e) {
+      const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+      y[e] = hf ? sh : x[e];
     }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) y[e] = j0 + e <= i ? clip4(y[e]) : 0.f;
+    st_chunk8(S + S1_CB + sw_off16(C, i, j0), y);
+    st_chunk8(S + S1_CB + sw_off16(C, i, j0 + 8), y + 8);
   }
   fence_async_smem();
   sm100::tc_fence_before();
@@ -213,14 +231,18 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     // exponent floored at -20: these terms dominate and the backward's decay gradient cancels
     // them against the matching column sums); then fp32 rows out
     float* YD = reinterpret_cast<float*>(smem + S1_W0);  // [p][i]
-    if (wg == 0) {
-      const int p = 16 * warp + lane;
-      float y[64];
-      tmem_ld32(tmem_at(tmem, warp, 128), y);
-      tmem_ld32(tmem_at(tmem, warp, 160), y + 32);
-      if (lane < 16)
+    {  // channel p = 16 quarter + (lane & 15), rows [32 wg + 16 hf, +16): one reference block per thread
+      const int hf = lane >> 4, p = 16 * quarter + (lane & 15), i0 = 32 * wg + 16 * hf;
+      float x[32], y[16];
+      tmem_ld32(tmem_at(tmem, quarter, 128 + 32 * wg), x);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) YD[p * C + i] = y[i] * __expf(CUM[i * P + p] - CUM[(i & ~15) * P + p]);
+      for (int e = 0; e < 16; ++e) {
+        const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+        y[e] = hf ? sh : x[e];
+      }
+      const float cr = CUM[i0 * P + p];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) YD[p * C + i0 + e] = y[e] * __expf(CUM[(i0 + e) * P + p] - cr);
     }
     __syncthreads();
     {
@@ -244,31 +266,36 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
 #pragma unroll
           for (int t = 0; t < 16; ++t) w[t] *= __expf(cr - CUM[(r + t) * P + p]);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 16; ++i) {  // row r + i of CB: two 16-byte chunks, read by the whole block
+            float cb[16];
+            unpack8(*reinterpret_cast<const uint4*>(smem + S1_CB + sw_off16(C, r + i, r)), cb);
+            unpack8(*reinterpret_cast<const uint4*>(smem + S1_CB + sw_off16(C, r + i, r + 8)), cb + 8);
             float acc = 0.f;
 #pragma unroll
-            for (int j = 0; j <= i; ++j)
-              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) * w[j];
+            for (int j = 0; j <= i; ++j) acc += cb[j] * w[j];
             YD[p * C + r + i] += __expf(CUM[(r + i) * P + p] - cr) * acc;
           }
         } else {
+#pragma unroll 1
           for (int i = 0; i < 16; ++i) {
             const float ci = CUM[(r + i) * P + p];
             float acc = 0.f;
-            for (int j = 0; j <= i; ++j)
-              acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) * w[j] *
-                     __expf(fmaxf(ci - CUM[(r + j) * P + p], -20.f));
+#pragma unroll
+            for (int j = 0; j < 16; ++j)  // register indices stay constant: j <= i as a predicate
+              if (j <= i)
+                acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) *
+                       w[j] * __expf(fmaxf(ci - CUM[(r + j) * P + p], -20.f));
             YD[p * C + r + i] += acc;
           }
         }
       }
     }
     __syncthreads();
-    if (tid < P) {
-      const int p = tid;
+    {  // fp32 rows out: channel p = tid >> 2, a quarter of its 64 rows per thread
+      const int p = tid >> 2, c0 = 16 * (tid & 3);
       float* dst2 = yd_t + ch * (C * P) + p * C;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4)
+      for (int c = c0; c < c0 + 16; c += 4)
         *reinterpret_cast<float4*>(dst2 + c) = make_float4(clip4(YD[p * C + c]), clip4(YD[p * C + c + 1]),
                                                            clip4(YD[p * C + c + 2]), clip4(YD[p * C + c + 3]));
     }
@@ -670,14 +697,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       bulk_g2s(smem + SB_DS, dse_t + ch * T_NP, T_NP, bars + 2);
     }
     if (!wait_bar(bars + 2, ph, err, 0x5333)) flags[4] = 1;
-    if (tid < P) {  // decay cumsum of channel p; span of each 16-row block
+    // decay cumsum (block totals exchanged in the DYR buffer, written only after it)
+    chunk_cumsum(smem + SB_DT, Ah, CUM, reinterpret_cast<float*>(smem + SB_DYR), tid);
+    if (tid < P) {  // span of each 16-row block
       const int p = tid;
-      float s = 0.f;
-      for (int i = 0; i < C; ++i) {
-        const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
-        s += fminf(fmaxf(dtv * Ah, -20.f), 20.f);
-        CUM[i * P + p] = fminf(fmaxf(s, -1e4f), 1e4f);
-      }
       float sp[4];
 #pragma unroll
       for (int I = 0; I < 4; ++I) sp[I] = warp_max(CUM[16 * I * P + p] - CUM[(16 * I + 15) * P + p]);

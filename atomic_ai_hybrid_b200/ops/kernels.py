@@ -461,6 +461,14 @@ def dt_act(u):
 _ADDMM_F32 = None  # whether cuBLAS accumulates bf16 products straight into fp32 (probed once)
 
 
+def _rows(t):
+    """``t`` as the dense GEMM reads it: unit column stride and 16-byte-aligned rows (a column slice
+    of a wider buffer stays a view; anything else is copied)."""
+    if t.stride(-1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0:
+        return t
+    return t.contiguous()
+
+
 def _dense_ok(x2, w) -> bool:
     """Shapes and types the tcgen05 dense GEMM takes for ``x2 (M, K) @ w (K, N)``."""
     return (x2.is_cuda and x2.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.dim() == 2
@@ -474,7 +482,7 @@ def _wgrad_acc(acc, x2, dy2):
     global _ADDMM_F32
     if (x2.is_cuda and x2.dtype == torch.bfloat16 and dy2.dtype == torch.bfloat16 and acc.dtype == torch.float32
             and acc.is_contiguous() and x2.shape[1] % 128 == 0 and dy2.shape[1] % 32 == 0):
-        ext().dense_wgrad(x2.contiguous(), dy2.contiguous(), acc)
+        ext().dense_wgrad(_rows(x2), _rows(dy2), acc)
         return
     _unsupported(f"dense weight gradient in={x2.shape[1]} out={dy2.shape[1]}")
     if _ADDMM_F32 is not False:
@@ -494,7 +502,7 @@ def bias_grad(b, dy2):
     acc = getattr(b, "_ahb_grad_acc", None) if b is not None else None
     if (acc is not None and dy2.is_cuda and dy2.dtype == torch.bfloat16 and dy2.shape[1] % 8 == 0
             and acc.dtype == torch.float32 and acc.numel() == dy2.shape[1]):
-        ext().bias_grad_acc(dy2.contiguous(), acc.view(-1))
+        ext().bias_grad_acc(_rows(dy2), acc.view(-1))
         return None
     return dy2.sum(0, dtype=torch.float32)
 
@@ -515,7 +523,7 @@ class _MultiLinear(torch.autograd.Function):
         for w, b in zip(ws, bs):
             wc = w if w.dtype == x.dtype else w.to(x.dtype)
             if _dense_ok(x2, wc):
-                y = ext().dense_fwd(x2.contiguous(), wc.contiguous(), b)
+                y = ext().dense_fwd(_rows(x2), wc.contiguous(), b)
             else:
                 _unsupported(f"dense projection in={wc.shape[0]} out={wc.shape[1]}")
                 y = torch.addmm(b.to(x.dtype), x2, wc) if b is not None else torch.mm(x2, wc)
@@ -537,7 +545,7 @@ class _MultiLinear(torch.autograd.Function):
                 dws.append(None)
                 dbs.append(None)
                 continue
-            dy2 = dy.reshape(-1, dy.shape[-1]).to(x.dtype).contiguous()
+            dy2 = dy.reshape(-1, dy.shape[-1]).to(x.dtype)
             wc = w if w.dtype == x.dtype else w.to(x.dtype)
             if ctx.needs_input_grad[0]:
                 if dy2.is_cuda and dy2.dtype == torch.bfloat16 and wc.dtype == torch.bfloat16 and \
@@ -545,7 +553,7 @@ class _MultiLinear(torch.autograd.Function):
                     first = dx is None
                     if first:
                         dx = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
-                    ext().dense_dgrad(dy2, wc.contiguous(), dx, not first)
+                    ext().dense_dgrad(_rows(dy2), wc.contiguous(), dx, not first)
                 elif dx is None:
                     _unsupported(f"dense input gradient in={wc.shape[0]} out={wc.shape[1]}")
                     dx = torch.mm(dy2, wc.t())

@@ -187,6 +187,14 @@ def bench_gemm(M, K, N, warmup, iters, flush):
                      ("cublas", lambda: torch.mm(a, b.t()))):
         ms = _timeit(fn, warmup, iters, flush)
         out[name] = {"ms": ms, "tflops": fl / ms / 1e9}
+    # weight gradient of a projection K -> N over M tokens, added into an fp32 accumulator
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    dy = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    acc = torch.zeros(K, N, device="cuda", dtype=torch.float32)
+    for name, fn in (("wgrad_tcgen05", lambda: ext().dense_wgrad(x, dy, acc)),
+                     ("wgrad_cublas", lambda: torch.addmm(acc, x.t(), dy, out_dtype=torch.float32, out=acc))):
+        ms = _timeit(fn, warmup, iters, flush)
+        out[name] = {"ms": ms, "tflops": fl / ms / 1e9}
     return out
 
 

@@ -65,3 +65,32 @@ def test_linear_multi_matches_fp32():
     for w, r in zip(ws, wr):
         assert _rel(w.grad, r.grad) < 1e-2, _rel(w.grad, r.grad)
     assert _rel(bs[1].grad, br[1].grad) < 1e-2
+
+
+def test_dense_strided_operands():
+    """Column slices of wider row-major buffers (as a fused kernel's outputs are handed out)
+    enter the GEMMs and the bias-gradient kernel as views, without copies, and give the same
+    results as contiguous operands."""
+    from atomic_ai_hybrid_b200.ops.kernels import bias_grad
+    g = torch.Generator(device=dev).manual_seed(5)
+    M, K, N = 1000, 512, 256
+    xw = torch.randn(M, 3 * K, device=dev, generator=g).to(torch.bfloat16)
+    dyw = torch.randn(M, 2 * N, device=dev, generator=g).to(torch.bfloat16)
+    x, dy = xw[:, K:2 * K], dyw[:, N:]
+    assert not x.is_contiguous() and not dy.is_contiguous()
+    W = (torch.randn(K, N, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16)
+    y = ext().dense_fwd(x, W, None)
+    assert torch.equal(y, ext().dense_fwd(x.contiguous(), W, None))
+    dx = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+    ext().dense_dgrad(dy, W, dx, False)
+    dx2 = torch.empty_like(dx)
+    ext().dense_dgrad(dy.contiguous(), W, dx2, False)
+    assert torch.equal(dx, dx2)
+    a1, a2 = torch.zeros(K, N, device=dev), torch.zeros(K, N, device=dev)
+    ext().dense_wgrad(x, dy, a1)
+    ext().dense_wgrad(x.contiguous(), dy.contiguous(), a2)
+    assert torch.equal(a1, a2)
+    b = torch.zeros(N, device=dev, dtype=torch.bfloat16)
+    b._ahb_grad_acc = torch.zeros(N, device=dev)
+    assert bias_grad(b, dy) is None
+    torch.testing.assert_close(b._ahb_grad_acc, dy.float().sum(0), rtol=1e-3, atol=1e-2)

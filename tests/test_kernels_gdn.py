@@ -43,7 +43,9 @@ def test_gdn_forward_scale_matches_token_serial():
     assert _rel(o, o_ref) < 2e-2
 
 
-@pytest.mark.parametrize("B,L,H,decay", [(1, 128, 1, 1.0), (2, 256, 2, 0.1), (1, 192, 1, 4.0)])
+# (5, 128, 16): 80 (batch, head) pairs keep the whole state in one CTA each; the smaller shapes split
+# the value columns over two CTAs (the state kernels' two launch forms)
+@pytest.mark.parametrize("B,L,H,decay", [(1, 128, 1, 1.0), (2, 256, 2, 0.1), (1, 192, 1, 4.0), (5, 128, 16, 1.0)])
 def test_gdn_backward(B, L, H, decay):
     ins = _inputs(B, L, H, 2, decay)
     xs = [t.clone().requires_grad_(True) for t in ins]

@@ -1,9 +1,11 @@
-"""Loss-curve parity: 200 optimizer steps of a small hybrid model through the
-sm_100a kernels (fused layers, tcgen05 MoE, fused optimizer) and through the eager
-PyTorch implementation (reference scans, SDPA, cuBLAS, PyTorch optimizer ops) from
-the same weights on the same data must give the same loss curve: mean loss and the
-10-step windows of the last 100 steps within 1e-2 relative, the fast-falling first 100
-steps within 5e-2 (the two paths round differently, so a one-step delay is allowed)."""
+"""Loss-curve parity: 200 optimizer steps of a hybrid_1b-width model (d_model 2048, 16 GDN-2
+heads of 128, 32 Mamba2 heads of 64, expert hidden 1024; two layers, 8 experts) through the
+sm_100a kernels (fused layers, tcgen05 GEMMs, fused optimizer) and through the eager PyTorch
+implementation (reference scans, SDPA, cuBLAS, PyTorch optimizer ops) from the same weights on
+the same data, compared step by step: every step of the last 100 within 1e-2 relative, every
+step of the fast-falling first 100 within 2e-2 (the two paths round differently, so the curves
+can be a fraction of a step apart while the loss falls fast; measured on a B200: at most 1.0e-2
+over the first 100 steps, 4.3e-3 over the last 100).  The measured per-step spread is printed."""
 import pytest
 import torch
 
@@ -39,20 +41,16 @@ def _curve(impl, cfg, data, dev):
 def test_kernel_and_eager_loss_curves_agree():
     from atomic_ai_hybrid_b200 import get_preset
     dev = torch.device("cuda", 0)
-    cfg = get_preset("hybrid_1b", d_model=512, n_heads=4, n_heads_ssm=8, num_layers=2, d_ff=256,
-                     n_routed_experts=8, top_k=2, vocab_size=1024, d_state=128, router_noise_std=0.0,
-                     layer_types=("gdn2", "mamba2"))
+    cfg = get_preset("hybrid_1b", num_layers=2, n_routed_experts=8, top_k=2, vocab_size=1024,
+                     router_noise_std=0.0, layer_types=("gdn2", "mamba2"))
     data = _data(cfg, 200, 4, 256, dev)
     k = _curve("cuda", cfg, data, dev)
     e = _curve("eager", cfg, data, dev)
     rel = (k - e).abs() / e.abs()
     assert torch.isfinite(k).all() and torch.isfinite(e).all()
     assert k[-20:].mean() < 0.8 * k[:5].mean(), ("the model does not learn the corpus", k[:5], k[-20:])
-    # windows of 10 steps (the per-step losses of two bf16 paths jitter independently); while the
-    # loss falls fast (first 100 steps) a step of delay shows as a few percent, after it the
-    # curves must agree to 1e-2, and so must the mean loss over all 200 steps
-    kw, ew = k.view(20, 10).mean(1), e.view(20, 10).mean(1)
-    wrel = (kw - ew).abs() / ew.abs()
-    assert abs(k.mean() - e.mean()) / e.mean() < 1e-2, (k.mean(), e.mean())
-    assert wrel[10:].max() < 1e-2, (kw, ew)
-    assert wrel[:10].max() < 5e-2, (kw, ew)
+    print(f"[loss-curve] per-step relative difference: steps 0-99 max {rel[:100].max():.4f} "
+          f"mean {rel[:100].mean():.4f}; steps 100-199 max {rel[100:].max():.4f} mean {rel[100:].mean():.4f}; "
+          f"final loss kernel {k[-1]:.4f} eager {e[-1]:.4f}")
+    assert rel[100:].max() < 1e-2, (rel[100:].max(), k[100:], e[100:])
+    assert rel[:100].max() < 2e-2, (rel[:100].max(), k[:100], e[:100])
