@@ -116,13 +116,24 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const T* __restrict__ 
   }
 }
 
-// out[c] += sum_b part[b * D + c]
-__global__ void colsum_add_kernel(const float* __restrict__ part, int nb, int D, float* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= D) return;
+// out[c] += sum_b part[b * D + c]: a block of 256 threads covers 32 columns, its 8 warps sum every
+// 8th row (lane = column, coalesced), and the warps' sums are added in a fixed order
+__global__ void __launch_bounds__(256) colsum_add_kernel(const float* __restrict__ part, int nb, int D,
+                                                         float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < nb; ++b) s += part[(int64_t)b * D + c];
-  out[c] += s;
+  if (c < D)
+    for (int b = w; b < nb; b += 8) s += part[(int64_t)b * D + c];
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][lane];
+    out[c] += t;
+  }
 }
 
 // ----------------------------------------------------------------- bias gradient
@@ -742,12 +753,12 @@ void ahb_rmsnorm_bwd(const void* dy, const void* x, const float* scale, const fl
   float* ds = dscale_acc ? dscale_part : nullptr;
   if (dtype == AHB_BF16) rms_bwd_t<bf16>(dy, x, scale, rstd, dx, ds, M, D, st);
   else rms_bwd_t<float>(dy, x, scale, rstd, dx, ds, M, D, st);
-  if (dscale_acc) colsum_add_kernel<<<(D + 255) / 256, 256, 0, st>>>(dscale_part, rms_bwd_blocks(M, D), D, dscale_acc);
+  if (dscale_acc) colsum_add_kernel<<<(D + 31) / 32, 256, 0, st>>>(dscale_part, rms_bwd_blocks(M, D), D, dscale_acc);
 }
 
 void ahb_colsum_add(const float* part, int nb, int D, float* out, cudaStream_t st) {
   if (D <= 0 || nb <= 0) return;
-  colsum_add_kernel<<<(D + 255) / 256, 256, 0, st>>>(part, nb, D, out);
+  colsum_add_kernel<<<(D + 31) / 32, 256, 0, st>>>(part, nb, D, out);
 }
 
 void ahb_conv1d_fwd(const void* x, int64_t xs, const void* w, int wdtype, const float* bias, void* y, int B, int L,

@@ -352,32 +352,25 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     }
     if (!wait_bar(bars + 4, 0, err, 0x4704)) goto teardown;
     sm100::tc_fence_after();
-    // 8. rows i = 16 warp + lane (lanes 0-15) of w~ and u out as tile images
+    // 8. rows i = 16 warp + (lane & 15) of w~ and u out as tile images: lanes 0-15 hold the rows
+    //    (M = 64), lanes 16-31 take the upper 16 columns of each 32-column load by shuffle
     {
-      const int i = 16 * warp + lane;
+      const int i = 16 * warp + (lane & 15), hf = lane >> 4;
       unsigned char* wt_c = wt_t + cb * TILE_CD;
       unsigned char* u_c = u_t + cb * TILE_CD;
 #pragma unroll 1
-      for (int p = 0; p < 4; ++p) {
-        float x[32];
+      for (int p = 0; p < 8; ++p) {
+        unsigned char* dst = p < 4 ? wt_c : u_c;
+        const int col = 32 * (p & 3) + 16 * hf;
+        float x[32], y[16];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
-        if (lane < 16)
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = guard(x[c + e]);
-            *reinterpret_cast<uint4*>(wt_c + sw_off16(C, i, 32 * p + c)) = pack8(y);
-          }
-        tmem_ld32(tmem_at(tmem, warp, 128 + 32 * p), x);
-        if (lane < 16)
-#pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = guard(x[c + e]);
-            *reinterpret_cast<uint4*>(u_c + sw_off16(C, i, 32 * p + c)) = pack8(y);
-          }
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+          y[e] = guard(hf ? sh : x[e]);
+        }
+        *reinterpret_cast<uint4*>(dst + sw_off16(C, i, col)) = pack8(y);
+        *reinterpret_cast<uint4*>(dst + sw_off16(C, i, col + 8)) = pack8(y + 8);
       }
     }
   }
@@ -720,6 +713,34 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   if (warp == 0) sm100::tmem_dealloc(tmem, TCOLS);
 }
 
+// Row i of an M = 64 accumulator (TMEM columns [col0, col0 + 64)) -> bf16 row i + row_off of a
+// 128B-swizzled tile of R rows, on all 256 threads: row i = 16 quarter + (lane & 15) sits in lane
+// i & 15 of its lane quarter, so four threads share a row (warpgroup wg takes columns
+// [32 wg, 32 wg + 32), lanes 16-31 the upper 16 of them by shuffle).  MODE gives the stored value:
+// 0 causal (j <= i), 1 strictly lower (j < i), 2 all, 3 negated strictly lower; with `gt` the row is
+// also stored transposed, as column i of rows t_row + j of a tile of Rt rows.  Not inlined: its
+// registers stay out of the caller's.
+template <int MODE>
+__device__ __noinline__ void rows64_out(uint32_t tmem, int col0, int quarter, int wg, int lane, uint32_t dst, int R,
+                                        int row_off, unsigned char* gt, int Rt, int t_row) {
+  const int hf = lane >> 4, i = 16 * quarter + (lane & 15), j0 = 32 * wg + 16 * hf;
+  float x[32], y[16];
+  tmem_ld32(tmem_at(tmem, quarter, col0 + 32 * wg), x);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+    const float v = hf ? sh : x[e];
+    const int j = j0 + e;
+    y[e] = MODE == 0 ? (j <= i ? v : 0.f) : MODE == 1 ? (j < i ? v : 0.f) : MODE == 2 ? v : (j < i ? -v : 0.f);
+  }
+  st_chunk8(dst + sw_off16(R, row_off + i, j0), y);
+  st_chunk8(dst + sw_off16(R, row_off + i, j0 + 8), y + 8);
+  if (gt)
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      *reinterpret_cast<bf16*>(gt + sw_off(Rt, t_row + j0 + e, i)) = __float2bfloat16_rn(y[e]);
+}
+
 // ============================================================ chunk-parallel backward
 // One CTA per chunk, 256 threads.  Everything per (row i, channel d) is held transposed: the
 // M = 128 accumulators have the channel as TMEM lane, so thread d assembles channel d of the
@@ -916,23 +937,8 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
 #pragma unroll
     for (int c = 0; c < 32; c += 8) st_chunk8(S + BC_DWT + sw_off16(D, dk, 32 * wg + c), x + c);
   }
-  // Gqk = do vn^T (causal) -> rows 0-63 of G and G^T (warpgroup 0, lanes 0-15: row i)
-  if (wg == 0) {
-    const int i = 16 * quarter + lane;
-    float x[64];
-    tmem_ld32(tmem_at(tmem, quarter, 192), x);
-    tmem_ld32(tmem_at(tmem, quarter, 224), x + 32);
-    if (lane < 16) {
-#pragma unroll
-      for (int j = 0; j < 64; ++j) x[j] = j <= i ? x[j] : 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_G + sw_off16(128, i, c), x + c);
-      unsigned char* gt = smem + BC_GT;
-#pragma unroll
-      for (int j = 0; j < 64; ++j)
-        *reinterpret_cast<bf16*>(gt + sw_off(128, j, i)) = __float2bfloat16_rn(x[j]);
-    }
-  }
+  // Gqk = do vn^T (causal) -> rows 0-63 of G and G^T
+  rows64_out<0>(tmem, 192, quarter, wg, lane, S + BC_G, 128, 0, smem + BC_GT, 128, 0);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
@@ -954,18 +960,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   if (!wait_bar(bars + 2, 0, err, 0x4733)) flags[4] = 1;
   sm100::tc_fence_after();
   // dA strictly lower -> DA tile (rows i, columns l)
-  if (wg == 0) {
-    const int i = 16 * quarter + lane;
-    float x[64];
-    tmem_ld32(tmem_at(tmem, quarter, 256), x);
-    tmem_ld32(tmem_at(tmem, quarter, 288), x + 32);
-    if (lane < 16) {
-#pragma unroll
-      for (int j = 0; j < 64; ++j) x[j] = j < i ? x[j] : 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_DA + sw_off16(C, i, c), x + c);
-    }
-  }
+  rows64_out<1>(tmem, 256, quarter, wg, lane, S + BC_DA, C, 0, nullptr, 0, 0);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
@@ -1007,15 +1002,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   if (!wait_bar(bars + 3, 0, err, 0x4734)) flags[4] = 1;
   sm100::tc_fence_after();
   // T = dA A^T -> T tile (rows l, columns j)
-  if (wg == 0) {
-    const int i = 16 * quarter + lane;
-    float x[64];
-    tmem_ld32(tmem_at(tmem, quarter, 448), x);
-    tmem_ld32(tmem_at(tmem, quarter, 480), x + 32);
-    if (lane < 16)
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_T + sw_off16(C, i, c), x + c);
-  }
+  rows64_out<2>(tmem, 448, quarter, wg, lane, S + BC_T, C, 0, nullptr, 0, 0);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
@@ -1028,22 +1015,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   if (!wait_bar(bars + 4, 0, err, 0x4735)) flags[4] = 1;
   sm100::tc_fence_after();
   // Gkk = -(A^T T) strictly lower -> rows 64-127 of G and G^T
-  if (wg == 0) {
-    const int i = 16 * quarter + lane;
-    float x[64];
-    tmem_ld32(tmem_at(tmem, quarter, 256), x);
-    tmem_ld32(tmem_at(tmem, quarter, 288), x + 32);
-    if (lane < 16) {
-#pragma unroll
-      for (int j = 0; j < 64; ++j) x[j] = j < i ? -x[j] : 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) st_chunk8(S + BC_G + sw_off16(128, C + i, c), x + c);
-      unsigned char* gt = smem + BC_GT;
-#pragma unroll
-      for (int j = 0; j < 64; ++j)
-        *reinterpret_cast<bf16*>(gt + sw_off(128, C + j, i)) = __float2bfloat16_rn(x[j]);
-    }
-  }
+  rows64_out<3>(tmem, 256, quarter, wg, lane, S + BC_G, 128, C, smem + BC_GT, 128, C);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();

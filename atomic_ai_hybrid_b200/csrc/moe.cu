@@ -35,38 +35,60 @@ __global__ void moe_offsets_kernel(const int* __restrict__ counts, int E, int pa
   }
 }
 
-// pos[a] = off[e] + stable rank of a among assignments to e; row_src[pos] = token (grid E, block 1024)
+// pos[a] = off[e] + stable rank of a among assignments to e; row_src[pos] = token (grid E, block 1024).
+// Each pass covers 4096 assignments, four consecutive ones per thread (one 16-byte load): the rank is
+// the thread's own prefix, plus a warp shuffle scan of the per-thread counts, plus an exclusive scan
+// of the 32 warp totals.
 __global__ void __launch_bounds__(1024) moe_positions_kernel(const int* __restrict__ eidx, int64_t n, int T,
                                                              const int* __restrict__ off, int* __restrict__ pos,
                                                              int* __restrict__ row_src) {
-  __shared__ int warp_tot[32];
-  __shared__ int carry;
+  __shared__ int warp_ex[32];
+  __shared__ int pass_tot;
   const int e = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
   const int base = off[e];
-  for (int64_t a0 = 0; a0 < n; a0 += blockDim.x) {
-    const int64_t a = a0 + threadIdx.x;
-    const int f = (a < n && eidx[a] == e) ? 1 : 0;
-    const unsigned m = __ballot_sync(0xffffffffu, f);
-    const int wpre = __popc(m & ((1u << lane) - 1));
-    if (lane == 0) warp_tot[wid] = __popc(m);
+  int carry = 0;  // rows of expert e in the passes before (the same in every thread)
+  for (int64_t a0 = 0; a0 < n; a0 += 4 * 1024) {
+    const int64_t a = a0 + 4 * (int64_t)threadIdx.x;
+    int f[4];
+    if (a + 3 < n) {
+      const int4 v = *reinterpret_cast<const int4*>(eidx + a);
+      f[0] = v.x == e; f[1] = v.y == e; f[2] = v.z == e; f[3] = v.w == e;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) f[q] = (a + q < n && eidx[a + q] == e) ? 1 : 0;
+    }
+    const int cnt = f[0] + f[1] + f[2] + f[3];
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_ex[wid] = incl;
     __syncthreads();
-    int before = 0;
-    for (int w = 0; w < wid; ++w) before += warp_tot[w];
-    if (f) {
-      const int p = base + carry + before + wpre;
-      pos[a] = p;
-      row_src[p] = (int)(a % T);
+    if (wid == 0) {
+      const int v = warp_ex[lane];
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      warp_ex[lane] = inc - v;
+      if (lane == 31) pass_tot = inc;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int tot = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += warp_tot[w];
-      carry += tot;
-    }
-    __syncthreads();
+    int r = base + carry + warp_ex[wid] + incl - cnt;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (f[q]) {
+        pos[a + q] = r;
+        row_src[r] = (int)((a + q) % T);
+        ++r;
+      }
+    carry += pass_tot;
+    __syncthreads();  // warp_ex and pass_tot are rewritten by the next pass
   }
 }
 

@@ -79,7 +79,6 @@ struct Params {
   const bf16* bias;
   const bf16* beta_src;
   int acc_bf16;  // EPI_ACC into bf16 accumulators (AHB_GEMM_ACC_BF16)
-  int sk_nkb;    // CTA-pair kernel, one K-grouped group: stream-K over tiles x sk_nkb k-blocks (0: off)
 };
 
 AHB_DEVICE float clampf(float x, float c) { return c > 0.f ? fminf(fmaxf(x, -c), c) : x; }
@@ -153,7 +152,7 @@ AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, T
 // `m_limit`, when set, are not written).
 template <int EPI, int NB>
 AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, uint32_t tb, int row_base, int lane,
-                              unsigned char* stg_base, int q, bool atomic = false) {
+                              unsigned char* stg_base, int q) {
   constexpr int BNA = 256 / NB;
   const int row = row_base + lane;
   const int n0 = t.n0 * BNA;
@@ -306,12 +305,6 @@ AHB_DEVICE void epilogue_tile(const Params& p, const int* off, const Tile& t, ui
       const int64_t oo = (static_cast<int64_t>(t.e) * p.Mout + row) * p.N + col;
       if (p.acc_bf16) {  // the product summed in fp32, rounded once as it is added
         acc_add_bf16(static_cast<bf16*>(p.out0) + oo, v0, alpha);
-      } else if (atomic) {  // a piece of a tile split between pairs (stream-K)
-        float* d0p = static_cast<float*>(p.out0) + oo;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          atomicAdd(reinterpret_cast<float4*>(d0p + i),
-                    make_float4(alpha * v0[i], alpha * v0[i + 1], alpha * v0[i + 2], alpha * v0[i + 3]));
       } else {
         float* d0p = static_cast<float*>(p.out0) + oo;
 #pragma unroll
@@ -515,12 +508,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) moe_gemm_kernel(const __grid_cons
 // the MMA role; both CTAs' TMA loads complete on the leader's `full` barrier; its commits
 // arrive on `empty` / `tfull` of both CTAs; both CTAs' epilogue warps release an accumulator on
 // the leader's `tempty`.  M-grouped groups (and K-grouped Mout) must be multiples of 256 rows.
-// Seven 32 KB stages (224 KB of the 227 KB a CTA may take).
-//
-// Stream-K (one K-grouped group, `sk_nkb` > 0): a 2048 x 2048 weight gradient has 64 tiles for 74
-// pairs, a wave 86 % full whatever the tile size.  Each pair then takes an equal share of the
-// (tile, k-block) iterations; a pair that covers a whole tile adds it as usual, the pieces of a
-// tile split between pairs are added with fp32 atomics.
+// Seven 32 KB stages (224 KB of the 227 KB a CTA may take).  A weight gradient of 2048 x 2048 has
+// 64 tiles for 74 pairs (any power-of-two tile count leaves the last wave short of 74 or 148); the
+// pairs walk the token dimension in lockstep, so the rows they read stay in L2 (an even split of
+// the (tile, k-block) iterations over the pairs spreads them over all of x and dy and re-read
+// them from DRAM five times: measured, no faster).
 constexpr int PAIR_BM = 256, PAIR_STAGES = 7;
 constexpr int PAIR_A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's 128 rows
 constexpr int PAIR_B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the 256 columns
@@ -552,12 +544,11 @@ AHB_DEVICE void decode_pair(const Params& p, const int* off, int tile, int n_til
   }
 }
 
-// One unit of work of a pair: a tile and its k-blocks [kb0, kb1); `whole` when they are all of the
-// tile's.  Every role of both CTAs walks the same sequence.
+// One unit of work of a pair: a tile and its k-blocks [kb0, kb1).  Every role of both CTAs walks
+// the same sequence: tiles cid, cid + ncl, ...
 struct PairWork {
   Tile t;
   int kb0, kb1;
-  bool whole;
 };
 
 template <bool KGROUP>
@@ -565,33 +556,14 @@ struct PairSched {
   const Params& p;
   const int* off;
   int n_tiles, total, ncl;
-  int tile;             // next tile (plain schedule)
-  int64_t u, u_end;     // iteration range (stream-K)
+  int tile;
   AHB_DEVICE PairSched(const Params& p_, const int* off_, int n_tiles_, int total_, int cid, int ncl_)
-      : p(p_), off(off_), n_tiles(n_tiles_), total(total_), ncl(ncl_), tile(cid), u(0), u_end(0) {
-    if (KGROUP && p.sk_nkb > 0) {
-      const int64_t W = (int64_t)total * p.sk_nkb;
-      u = W * cid / ncl;
-      u_end = W * (cid + 1) / ncl;
-    }
-  }
+      : p(p_), off(off_), n_tiles(n_tiles_), total(total_), ncl(ncl_), tile(cid) {}
   AHB_DEVICE bool next(PairWork& w) {
-    if (KGROUP && p.sk_nkb > 0) {
-      if (u >= u_end) return false;
-      const int tl = (int)(u / p.sk_nkb);
-      decode_pair<KGROUP>(p, off, tl, n_tiles, w.t);
-      w.kb0 = (int)(u % p.sk_nkb);
-      const int64_t left = u_end - u;
-      w.kb1 = left < (int64_t)(p.sk_nkb - w.kb0) ? w.kb0 + (int)left : p.sk_nkb;
-      w.whole = w.kb0 == 0 && w.kb1 == p.sk_nkb;
-      u += w.kb1 - w.kb0;
-      return true;
-    }
     if (tile >= total) return false;
     decode_pair<KGROUP>(p, off, tile, n_tiles, w.t);
     w.kb0 = 0;
     w.kb1 = w.t.nkb;
-    w.whole = true;
     tile += ncl;
     return true;
   }
@@ -756,7 +728,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1) moe_gem
       if (!mbar_wait(tfull + acc, acc_phase, abort_flag, p.err, 14)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
-      epilogue_tile<EPI, NB>(p, off, wk.t, tb, wk.t.m0 + 128 * (int)rank + q * 32, lane, nullptr, q, !wk.whole);
+      epilogue_tile<EPI, NB>(p, off, wk.t, tb, wk.t.m0 + 128 * (int)rank + q * 32, lane, nullptr, q);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * acc);
@@ -931,12 +903,6 @@ int ahb_dense_gemm(int mode, const void* a, int64_t lda, const void* b, int64_t 
   if (mode == 2) {  // K-grouped: Mout = K rows of the weight, contraction over the M token rows
     if (K % (pair ? PAIR_BM : BM) != 0) return -12;
     p.Mout = K;
-    if (pair) {  // stream-K when whole tiles would leave the pairs' last wave well short of full
-      const int ncl = num_sms / 2, tiles = (K / PAIR_BM) * ((N + 255) / 256);
-      const int waves = (tiles + ncl - 1) / ncl;
-      const int nkb = (int)((M + BK - 1) / BK);
-      if (tiles >= 16 && (double)tiles / ((double)waves * ncl) < 0.95 && nkb >= 8) p.sk_nkb = nkb;
-    }
     rc |= make_map(&p.ta0, a, M, K, lda, 64);
     rc |= make_map(&p.tb0, b, M, N, ldb, 64);
   } else {
