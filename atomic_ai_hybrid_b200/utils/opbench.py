@@ -135,6 +135,41 @@ def bench_router(T, d, E, k, warmup, iters, flush, mode="fwdbwd"):
             "min_io_gb_s": T * d * 2 * (3 if mode == "fwdbwd" else 1) / ms / 1e6, "tflops": fl / ms / 1e9}
 
 
+def bench_attn(B, T, H, D, warmup, iters, flush, mode="fwdbwd"):
+    """Causal flash attention (``attention.cu``) on (B, H, T, D) bf16."""
+    from ..ops import kernels as K
+    dev = "cuda"
+    q, k, v = (torch.randn(B, H, T, D, device=dev).to(torch.bfloat16).requires_grad_(True) for _ in range(3))
+    do = torch.randn(B, H, T, D, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        o = K.attention(q, k, v, D ** -0.5)
+        if mode == "fwdbwd":
+            torch.autograd.backward(o, do)
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = 2 * B * H * T * T * D * (1 if mode == "fwd" else 3.5)  # causal: QK^T and PV at half; backward 2.5x
+    return {"op": "attention", "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9}
+
+
+def bench_ce(T, d, V, warmup, iters, flush, mode="fwdbwd"):
+    """Tied LM head + label-smoothed cross entropy (no stored logits)."""
+    from ..ops import kernels as K
+    dev = "cuda"
+    h = (torch.randn(T, d, device=dev) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    W = (torch.randn(V, d, device=dev) * 0.02).to(torch.bfloat16).requires_grad_(True)
+    labels = torch.randint(0, V, (T,), device=dev)
+
+    def run():
+        s, c = K.cross_entropy(h, labels, W, 0.1)
+        if mode == "fwdbwd":
+            (s / c).backward()
+
+    ms = _timeit(run, warmup, iters, flush)
+    fl = 2 * T * d * V * (1 if mode == "fwd" else 4)  # forward logits; backward recomputes them, dh, dW
+    return {"op": "ce", "mode": mode, "T": T, "d": d, "V": V, "ms": ms, "tflops": fl / ms / 1e9}
+
+
 def bench_glue(T, d, warmup, iters, flush, mode="fwdbwd"):
     """Residual add + clip + RMSNorm and RMSNorm x SiLU gate (fused row kernels)."""
     from ..ops import kernels as K
@@ -217,7 +252,8 @@ def bench_gemm_rs(W, n, K, N, warmup, iters, flush):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="gdn", choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs", "gemm"])
+    ap.add_argument("--op", default="gdn",
+                    choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs", "gemm", "attn", "ce"])
     ap.add_argument("--K", type=int, default=2048)
     ap.add_argument("--N", type=int, default=2048)
     ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
@@ -241,6 +277,10 @@ def main(argv=None):
         r = bench_router(a.B * a.T, 2048, 32, 4, a.warmup, a.iters, flush, a.mode)
     elif a.op == "glue":
         r = bench_glue(a.B * a.T, 2048, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "attn":
+        r = bench_attn(a.B, a.T, a.H or 16, 128, a.warmup, a.iters, flush, a.mode)
+    elif a.op == "ce":
+        r = bench_ce(a.B * a.T, a.K, 50304, a.warmup, a.iters, flush, a.mode)
     elif a.op == "gemm":
         r = bench_gemm(a.B * a.T, a.K, a.N, a.warmup, a.iters, flush)
     elif a.op == "gemm_rs":

@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="disable CUDA-graph capture of the micro-step")
     ap.add_argument("--ep", type=int, default=1,
                     help="expert-parallel ranks (1 or the number of GPUs): routed experts split over the GPUs")
+    ap.add_argument("--expert-grad-bf16", action="store_true",
+                    help="bf16 gradient accumulators for the expert-parallel experts (the long-context layout)")
+    ap.add_argument("--remat", action="store_true", help="recompute each layer in the backward")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel ranks (heads split, tokens split between the mixers); each group of "
                          "--tp GPUs trains on --seqs-per-gpu x --tp sequences per step")
@@ -189,7 +192,7 @@ def main():
     # the model draws every full tensor and keeps this rank's pieces: one seed for all ranks
     torch.manual_seed(1234)
     with torch.device(dev):
-        model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16)
+        model = HybridMoEModel(cfg, compute_dtype=torch.bfloat16, remat=args.remat)
     # N(0, 0.02) init of every matrix (benchmark spec), norms at 1, biases 0; replicated
     # matrices draw the same values on every rank, tensor- / expert-parallel pieces their own
     from atomic_ai_hybrid_b200.parallel.tp import shard_spec
@@ -206,7 +209,8 @@ def main():
     # the eager baseline keeps NCCL collectives; the CUDA path uses the peer-memory fused step
     trainer = Trainer(model, total_steps=1000, optimizer=args.optimizer, compute_dtype=torch.bfloat16, device=dev,
                       cuda_graph=use_graph, comm="nccl" if args.impl == "eager" else "auto",
-                      ep_max_tokens=args.micro_batch * args.seq_len // tp if args.ep > 1 else 0)
+                      ep_max_tokens=args.micro_batch * args.seq_len // tp if args.ep > 1 else 0,
+                      expert_grad_bf16=args.expert_grad_bf16)
     trainer.opt.schedule.warmup = 1  # non-zero learning rate from the first step
 
     n_micro = max(1, args.seqs_per_gpu * tp // mb)
