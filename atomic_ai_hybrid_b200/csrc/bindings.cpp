@@ -176,6 +176,22 @@ GdnShapes gdn_shapes(const torch::Tensor& q) {
 
 torch::Tensor& err_word();
 
+void check_rc(int rc, const char* what);
+
+// Points the scan kernels' per-phase cycle counters at `counters` (int64 (128,) on the device:
+// SSD kernels slots 0-63, GDN kernels 64-127) or switches them off (None).
+void phase_prof(c10::optional<torch::Tensor> counters) {
+  char* p = nullptr;
+  if (counters) {
+    TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == torch::kInt64 && counters->numel() >= 128 &&
+                    counters->is_contiguous(),
+                "phase_prof: int64 CUDA tensor of 128 counters");
+    p = static_cast<char*>(counters->data_ptr());
+  }
+  check_rc(ahb_ssd_phase_prof(p), "ahb_ssd_phase_prof");
+  check_rc(ahb_gdn_phase_prof(p ? p + 64 * 8 : nullptr), "ahb_gdn_phase_prof");
+}
+
 void check_rc(int rc, const char* what) {
   TORCH_CHECK(rc == 0, "atomic_ai_hybrid_b200: ", what, " failed with code ", rc);
   check_launch(what);
@@ -1466,6 +1482,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_fwd_train", &ssd_fwd_train, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"),
         py::arg("s0") = py::none(), py::arg("want_final") = false);
   m.def("ssd_fwd", &ssd_fwd);
+  m.def("phase_prof", &phase_prof, py::arg("counters"));
   m.def("ssd_bwd", &ssd_bwd, py::arg("x"), py::arg("dt"), py::arg("A"), py::arg("Bm"), py::arg("Cm"), py::arg("dy"),
         py::arg("states") = py::none(), py::arg("decays") = py::none(), py::arg("cumsums") = py::none(),
         py::arg("ydiag") = py::none(), py::arg("s0") = py::none(), py::arg("ds_final") = py::none(),

@@ -27,6 +27,7 @@
 #include "sm100.cuh"
 #include "umma.cuh"
 #include "launchers.h"
+#include "phase_prof.cuh"
 #include "tmap.h"
 
 using namespace ahb;
@@ -53,7 +54,7 @@ struct SeqIdx {
 // shared memory: R1 (32 KB) stacked score rows, later A fp32, later (bk e^gc | w v) tiles;
 //                R2 (32 KB) key operands (two buffers), later Akk fp32 and the A tile; GC (32 KB)
 constexpr int F1_THREADS = 128;
-constexpr int F1_LDA = C + 1;  // fp32 row stride of the 64 x 64 work matrices
+constexpr int F1_LDA = C + 4;  // fp32 row stride of Akk: 16-byte rows, row starts spread over the banks
 constexpr size_t F1_SMEM = 1024 + 3 * 32768 + 256;
 
 __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0..3] exact diagonal block, [4] abort
   float* span_w = reinterpret_cast<float*>(flags + 8);  // [4 warps][4 blocks]
+  PhaseClock pc(0);
 
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pc.mark(0);
   {
     const int d = tid;
     float s = 0.f;
@@ -128,6 +131,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     flags[tid] = !(m <= 60.f);  // NaN spans take the exact path too
   }
   __syncthreads();
+  pc.mark(1);
 
   // 2. stacked score rows: R1 rows 0-63 = q e^{gc - gc_r}, rows 64-127 = (b k) e^{gc - gc_r};
   //    qg = q e^gc and kg = k e^{gcl - gc} go straight out as tile images
@@ -191,11 +195,13 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       sm100::umma_commit(bars + I);
     }
   }
+  pc.mark(2);
   if (!wait_bar(bars + 2, 0, err, 0x4702) || !wait_bar(bars + 3, 0, err, 0x4703)) flags[4] = 1;
   sm100::tc_fence_after();
+  pc.mark(3);
 
   // 4. scores out of TMEM: lane m of quarter q is row m = 32 q + lane of the stack
-  float* AKK = reinterpret_cast<float*>(R2);  // fp32 [64][65]
+  float* AKK = reinterpret_cast<float*>(R2);  // fp32 [64][F1_LDA]
   {
     const int m = 32 * warp + lane;
     const bool is_q = m < C;
@@ -247,99 +253,111 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(aqk_c + sw_off16(C, i, c)) = pack8(row + c);
     } else {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) AKK[i * F1_LDA + j] = row[j];
+      for (int j = 0; j < 64; j += 4)
+        *reinterpret_cast<float4*>(AKK + i * F1_LDA + j) = make_float4(row[j], row[j + 1], row[j + 2], row[j + 3]);
     }
   }
   sm100::tc_fence_before();
   __syncthreads();
+  pc.mark(4);
+  const long long t_after4 = clock64();
   if (flags[4]) goto teardown;
   {
-    // 5. A = (I + Akk)^-1 in fp32: diagonal 16 x 16 blocks by substitution (warp w: block w),
-    //    then X_IJ = -X_II sum_{K=J}^{I-1} Akk_IK X_KJ by block distance
-    float* AF = reinterpret_cast<float*>(R1);
-    float* TS = AF + C * F1_LDA;
-    for (int e = tid; e < C * C; e += F1_THREADS) {
-      const int r = e >> 6, c = e & 63;
-      if ((c >> 4) != (r >> 4)) AF[r * F1_LDA + c] = 0.f;
-    }
-    {
-      const int base = 16 * warp;
-      for (int i = 0; i < 16; ++i) {
-        float x = 0.f;
-        if (lane < 16) {
-          x = lane == i ? 1.f : 0.f;
-          for (int j = lane; j < i; ++j) x -= AKK[(base + i) * F1_LDA + base + j] * AF[(base + j) * F1_LDA + base + lane];
-        }
-        __syncwarp();
-        if (lane < 16) AF[(base + i) * F1_LDA + base + lane] = lane <= i ? x : 0.f;
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    for (int dist = 1; dist < 4; ++dist) {
-      const int np = 4 - dist;
-      for (int e = tid; e < np * 256; e += F1_THREADS) {
-        const int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
-        const int J = p, I = p + dist;
-        float s = 0.f;
-        for (int K = J; K < I; ++K)
-#pragma unroll 4
-          for (int kk = 0; kk < 16; ++kk)
-            s += AKK[(16 * I + ii) * F1_LDA + 16 * K + kk] * AF[(16 * K + kk) * F1_LDA + 16 * J + cc];
-        TS[e] = s;
-      }
-      __syncthreads();
-      for (int e = tid; e < np * 256; e += F1_THREADS) {
-        const int p = e >> 8, ii = (e >> 4) & 15, cc = e & 15;
-        const int J = p, I = p + dist;
-        float s = 0.f;
-        for (int m = 0; m <= ii; ++m) s += AF[(16 * I + ii) * F1_LDA + 16 * I + m] * TS[(p << 8) + (m << 4) + cc];
-        AF[(16 * I + ii) * F1_LDA + 16 * J + cc] = guard(-s);
-      }
-      __syncthreads();
-    }
-    // A out: bf16 operand tile (rows i, columns j), also as a tile image for the backward
+    // 5. A = (I + Akk)^-1 in fp32 by forward substitution, one column c per thread (threads 0-63), in
+    //    16-row blocks: the block's x_i = acc_i - sum_{j in block, j < i} Akk_ij x_j (registers),
+    //    then acc_i -= sum_{j in block} Akk_ij x_j for the rows below (fp32 [i][c] in the first half
+    //    of R1, acc_i = [i == c] before any update).  Akk rows are read as broadcast 16-byte vectors;
+    //    entries outside the diagonal 16 x 16 blocks are guarded.
     unsigned char* AT = R2 + 24576;
-    for (int e = tid; e < C * 8; e += F1_THREADS) {
-      const int i = e >> 3, c = (e & 7) << 3;
-      float x[8];
+    if (tid < C) {
+      const int c = tid;
+      float* ACC = reinterpret_cast<float*>(R1);  // [i][c]
+#pragma unroll 1
+      for (int B = 0; B < 4; ++B) {
+        float x[16];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) x[t] = AF[i * F1_LDA + c + t];
-      st_chunk8(smem_u32(AT) + sw_off16(C, i, c), x);
-      if (at_t) *reinterpret_cast<uint4*>(at_t + cb * TILE_CC + sw_off16(C, i, c)) = pack8(x);
+        for (int r = 0; r < 16; ++r) {
+          const int i = 16 * B + r;
+          const float* Li = AKK + i * F1_LDA + 16 * B;
+          float s0 = B == 0 ? (i == c ? 1.f : 0.f) : ACC[i * C + c], s1 = 0.f;
+#pragma unroll
+          for (int j = 0; j + 3 < r; j += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(Li + j);
+            s0 -= l4.x * x[j] + l4.z * x[j + 2];
+            s1 -= l4.y * x[j + 1] + l4.w * x[j + 3];
+          }
+#pragma unroll
+          for (int j = r & ~3; j < r; ++j) s0 -= Li[j] * x[j];
+          const float v_ = s0 + s1;
+          x[r] = B != (c >> 4) ? guard(v_) : v_;
+          *reinterpret_cast<bf16*>(AT + sw_off(C, i, c)) = __float2bfloat16_rn(x[r]);
+        }
+#pragma unroll 2
+        for (int i = 16 * B + 16; i < C; ++i) {
+          const float4* Li = reinterpret_cast<const float4*>(AKK + i * F1_LDA + 16 * B);
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 l4 = Li[q];
+            s0 += l4.x * x[4 * q] + l4.z * x[4 * q + 2];
+            s1 += l4.y * x[4 * q + 1] + l4.w * x[4 * q + 3];
+          }
+          const float prev = B == 0 ? (i == c ? 1.f : 0.f) : ACC[i * C + c];
+          ACC[i * C + c] = prev - (s0 + s1);
+        }
+      }
+    } else {
+      // 6b. (w v) tile (rows j, columns d) in the second half of R1: 1024 units over 64 threads,
+      //     four per batch of loads
+      const int t2 = tid - C;
+#pragma unroll 1
+      for (int b4 = 0; b4 < 4; ++b4) {
+        uint4 wa[4], va[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u_ = (4 * b4 + q) * C + t2;
+          const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
+          wa[q] = *reinterpret_cast<const uint4*>(wg + gi);
+          va[q] = *reinterpret_cast<const uint4*>(v + gi);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u_ = (4 * b4 + q) * C + t2;
+          float wv[8], vv[8];
+          unpack8(wa[q], wv);
+          unpack8(va[q], vv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) wv[e] *= vv[e];
+          st_chunk8(sR1 + TILE_CD + sw_off16(C, u_ >> 4, (u_ & 15) << 3), wv);
+        }
+      }
     }
+    pc.warp_mark(10, t_after4);
     __syncthreads();
-
-    // 6. (b k) e^gc and (w v) tiles (rows j, columns d) in R1
-    uint4 wa[UNITS], va[UNITS];
-#pragma unroll
-    for (int it = 0; it < UNITS; ++it) {
-      const int u_ = it * F1_THREADS + tid;
-      const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
-      wa[it] = *reinterpret_cast<const uint4*>(wg + gi);
-      va[it] = *reinterpret_cast<const uint4*>(v + gi);
-    }
+    pc.mark(5);
+    // 6a. (b k) e^gc tile (rows j, columns d) over the accumulators in the first half of R1
 #pragma unroll
     for (int it = 0; it < UNITS; ++it) {
       const int u_ = it * F1_THREADS + tid;
       const int i = u_ >> 4, c = (u_ & 15) << 3;
-      float kv[8], bv[8], wv[8], vv[8], x[8], y[8];
+      float kv[8], bv[8], x[8];
       unpack8(ka[it], kv);
       unpack8(ba[it], bv);
-      unpack8(wa[it], wv);
-      unpack8(va[it], vv);
       const float* gci = GC + i * D + c;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        x[e] = bv[e] * kv[e] * __expf(gci[e]);
-        y[e] = wv[e] * vv[e];
-      }
+      for (int e = 0; e < 8; ++e) x[e] = bv[e] * kv[e] * __expf(gci[e]);
       st_chunk8(sR1 + sw_off16(C, i, c), x);
-      st_chunk8(sR1 + TILE_CD + sw_off16(C, i, c), y);
     }
+    pc.mark(9);
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    // A as a tile image for the backward
+    if (at_t)
+#pragma unroll
+      for (int e = tid; e < C * 8; e += F1_THREADS)
+        *reinterpret_cast<uint4*>(at_t + cb * TILE_CC + 16 * e) = *reinterpret_cast<const uint4*>(AT + 16 * e);
+    pc.mark(6);
     // 7. w~ = A (bk e^gc) -> TMEM columns [0, 128); u = A (w v) -> [128, 256)   (M = 64)
     if (tid == 0) {
       sm100::tc_fence_after();
@@ -352,6 +370,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     }
     if (!wait_bar(bars + 4, 0, err, 0x4704)) goto teardown;
     sm100::tc_fence_after();
+    pc.mark(7);
     // 8. rows i = 16 warp + (lane & 15) of w~ and u out as tile images: lanes 0-15 hold the rows
     //    (M = 64), lanes 16-31 take the upper 16 columns of each 32-column load by shuffle
     {
@@ -378,7 +397,9 @@ teardown:
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
+  pc.mark(8);
   if (warp == 0) sm100::tmem_dealloc(tmem, 256);
+  pc.done();
 }
 
 // ============================================================ state recurrence, forward
@@ -391,7 +412,8 @@ teardown:
 //   o = scale O1 + O2 ; h <- e^{gcl} h + HH (clip 1e4)
 // (reference `atomic_ops/kernel_d_pipeline.py:94-158`, the inter-chunk combine with state)
 constexpr int F2_THREADS = 128;
-constexpr int F2_STAGE = 3 * TILE_CD + TILE_CC;  // w~, qg, kg, Aqk tile images
+constexpr int F2_STAGE = 4 * TILE_CD + TILE_CC;  // w~, qg, kg, Aqk tile images, this CTA's u columns
+constexpr int F2_U = 3 * TILE_CD + TILE_CC;       // offset of u inside a stage
 constexpr int F2_H = 2 * F2_STAGE;                // state tile (rows dk, columns dv), 32 KB
 constexpr int F2_VN = F2_H + 2 * TILE_CD;         // v_new tile (rows i, columns dv), 16 KB
 constexpr int F2_BARS = F2_VN + TILE_CD;
@@ -413,6 +435,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const uint32_t sH = smem_u32(smem + F2_H), sVN = smem_u32(smem + F2_VN);
+  PhaseClock pc(32);
 
   constexpr int DV = D / NH;  // value columns of this CTA
   constexpr uint32_t TCOLS = NH == 1 ? 512 : 256;
@@ -435,11 +458,12 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   auto issue = [&](int n) {
     unsigned char* st = smem + (n & 1) * F2_STAGE;
     const int64_t c = bh * NC + n;
-    sm100::mbar_expect_tx(bars + (n & 1), F2_STAGE);
+    sm100::mbar_expect_tx(bars + (n & 1), F2_U + DV * C * 2);
     bulk_g2s(st, wt_t + c * TILE_CD, TILE_CD, bars + (n & 1));
     bulk_g2s(st + TILE_CD, qg_t + c * TILE_CD, TILE_CD, bars + (n & 1));
     bulk_g2s(st + 2 * TILE_CD, kg_t + c * TILE_CD, TILE_CD, bars + (n & 1));
     bulk_g2s(st + 3 * TILE_CD, aqk_t + c * TILE_CC, TILE_CC, bars + (n & 1));
+    bulk_g2s(st + F2_U, u_t + c * TILE_CD + (v0 >> 6) * (C * 128), DV * C * 2, bars + (n & 1));
   };
   if (tid == 0) {
     issue(0);
@@ -460,14 +484,18 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
 #pragma unroll
     for (int c = 0; c < DV; c += 8) {
       st_chunk8(sH + sw_off16(D, dk, c), hr + c);
-      if (h_store)
-        *reinterpret_cast<uint4*>(h_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, v0 + c)) = pack8(hr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(0);
     if (tid == 0) {
+      if (h_store) {  // the state tile image: this CTA's column half (or both) as one bulk store
+        bulk_s2g(h_store + cbn * (2 * TILE_CD) + (v0 >> 6) * (D * 128), smem + F2_H, DV * D * 2);
+        bulk_commit();
+      }
       if (!wait_bar(bars + (n & 1), (n >> 1) & 1, err, 0x4711)) *abort_flag = 1;
+      pc.mark(6);
       sm100::tc_fence_after();
       if (!*abort_flag) {
         auto fh = [&](int s) { return mndesc(sH, D, s); };
@@ -478,10 +506,12 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     }
     if (!wait_bar(bars + 2, n & 1, err, 0x4712)) *abort_flag = 1;
     sm100::tc_fence_after();
+    pc.mark(1);
     // v_new rows i = 16 warp + lane (lanes 0-15)
     {
       const int i = 16 * warp + lane;
-      const unsigned char* u_c = u_t + cbn * TILE_CD;
+      const unsigned char* u_c = smem + (n & 1) * F2_STAGE + F2_U;  // this CTA's columns
+      if (!wait_bar(bars + (n & 1), (n >> 1) & 1, err, 0x4714)) *abort_flag = 1;  // every thread reads u
 #pragma unroll 1
       for (int p = 0; p < DV / 32; ++p) {
         float x[32];
@@ -490,20 +520,23 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             float uu[8], y[8];
-            unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, v0 + 32 * p + c)), uu);
+            unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, 32 * p + c)), uu);
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = uu[e] - x[c + e];
             st_chunk8(sVN + sw_off16(C, i, 32 * p + c), y);
-            if (vn_store)
-              *reinterpret_cast<uint4*>(vn_store + cbn * TILE_CD + sw_off16(C, i, v0 + 32 * p + c)) = pack8(y);
           }
       }
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(2);
     if (*abort_flag) break;
     if (tid == 0) {
+      if (vn_store) {
+        bulk_s2g(vn_store + cbn * TILE_CD + (v0 >> 6) * (C * 128), smem + F2_VN, DV * C * 2);
+        bulk_commit();
+      }
       sm100::tc_fence_after();
       auto fvn = [&](int s) { return mndesc(sVN, C, s); };
       mma_steps(tmem + 2 * DV, [&](int s) { return kdesc(st + 3 * TILE_CD, C, s); }, fvn, C / 16, ID_ROWS, false);
@@ -512,6 +545,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     }
     if (!wait_bar(bars + 3, n & 1, err, 0x4713)) *abort_flag = 1;
     sm100::tc_fence_after();
+    pc.mark(3);
     if (o) {
       const int i = 16 * warp + lane;
       bf16* orow = o + ix.row(b, (int64_t)n * C + i, h);
@@ -530,6 +564,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
           }
       }
     }
+    pc.mark(4);
     {
       const float eg = __expf(gcl[cbn * D + dk]);
 #pragma unroll
@@ -540,14 +575,17 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
         for (int e = 0; e < 32; ++e) hr[32 * p + e] = sanitize(eg * hr[32 * p + e] + x[e], 1e4f);
       }
     }
+    if (tid == 0) bulk_wait_read();  // the h / v_new tiles are rewritten in the next step
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(5);
     if (*abort_flag) break;
     if (tid == 0 && n + 2 < NC) issue(n + 2);
   }
   if (h_final && n == NC)
 #pragma unroll
     for (int c = 0; c < DV; ++c) h_final[(bh * D + dk) * D + v0 + c] = hr[c];
+  if (tid == 0) bulk_wait_all();
   if (*abort_flag && tid == 0) {  // let copies in flight land before the CTA exits
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -556,6 +594,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
   __syncthreads();
   sm100::tc_fence_after();
   if (warp == 0) sm100::tmem_dealloc(tmem, TCOLS);
+  pc.done();
 }
 
 // ============================================================ state recurrence, backward
@@ -587,6 +626,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const uint32_t sDH = smem_u32(smem + B1_DH), sDVN = smem_u32(smem + B1_DVN);
+  PhaseClock pc(48);
 
   constexpr int DV = D / NH;  // value columns of this CTA
   constexpr uint32_t TCOLS = NH == 1 ? 512 : 256;
@@ -638,13 +678,16 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
 #pragma unroll
     for (int c = 0; c < DV; c += 8) {
       st_chunk8(sDH + sw_off16(D, dk, c), dr + c);
-      *reinterpret_cast<uint4*>(dh_store + cbn * (2 * TILE_CD) + sw_off16(D, dk, v0 + c)) = pack8(dr + c);
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    pc.mark(0);
+    if (tid == 0) {  // the dh tile image: this CTA's column half (or both) as one bulk store
+      bulk_s2g(dh_store + cbn * (2 * TILE_CD) + (v0 >> 6) * (D * 128), smem + B1_DH, DV * D * 2);
+      bulk_commit();
       if (!wait_bar(bars + s, (it >> 1) & 1, err, 0x4721)) *abort_flag = 1;
+      pc.mark(6);
       sm100::tc_fence_after();
       if (!*abort_flag) {
         const uint32_t sdo = st + B1_DO;
@@ -658,6 +701,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     }
     if (!wait_bar(bars + 2, it & 1, err, 0x4722)) *abort_flag = 1;
     sm100::tc_fence_after();
+    pc.mark(1);
     {
       const int i = 16 * warp + lane;
 #pragma unroll 1
@@ -668,15 +712,17 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             st_chunk8(sDVN + sw_off16(C, i, 32 * p + c), x + c);
-            *reinterpret_cast<uint4*>(dvn_store + cbn * TILE_CD + sw_off16(C, i, v0 + 32 * p + c)) = pack8(x + c);
           }
       }
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(2);
     if (*abort_flag) break;
     if (tid == 0) {
+      bulk_s2g(dvn_store + cbn * TILE_CD + (v0 >> 6) * (C * 128), smem + B1_DVN, DV * C * 2);
+      bulk_commit();
       sm100::tc_fence_after();
       mma_steps(tmem + 2 * DV, [&](int k) { return mndesc(st, C, k); }, [&](int k) { return mndesc(sDVN, C, k); },
                 C / 16, ID_ST, false);
@@ -684,6 +730,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     }
     if (!wait_bar(bars + 3, it & 1, err, 0x4723)) *abort_flag = 1;
     sm100::tc_fence_after();
+    pc.mark(3);
     {
       const float eg = __expf(gcl[cbn * D + dk]);
 #pragma unroll
@@ -695,14 +742,17 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
         for (int e = 0; e < 32; ++e) dr[32 * p + e] = eg * dr[32 * p + e] + scale * x1[e] - x2[e];
       }
     }
+    if (tid == 0) bulk_wait_read();  // the dh / dv_new tiles are rewritten in the next step
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(5);
     if (*abort_flag) break;
     if (tid == 0 && it + 2 < NC) issue(n - 2, s);
   }
   if (dh0 && it == NC)
 #pragma unroll
     for (int c = 0; c < DV; ++c) dh0[(bh * D + dk) * D + v0 + c] = dr[c];
+  if (tid == 0) bulk_wait_all();
   if (*abort_flag && tid == 0) {
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -711,6 +761,7 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
   __syncthreads();
   sm100::tc_fence_after();
   if (warp == 0) sm100::tmem_dealloc(tmem, TCOLS);
+  pc.done();
 }
 
 // Row i of an M = 64 accumulator (TMEM columns [col0, col0 + 64)) -> bf16 row i + row_off of a
@@ -794,6 +845,16 @@ constexpr int BC_BAR = BC_GC + 32768;
 constexpr int BC_WV = 0, BC_BKE = 16384, BC_DWT = 32768, BC_DA = 49152, BC_T = 57344, BC_G = 65536, BC_GT = 81920;
 // assembly: plain q, k, b rows over the dead column-side buffer 1 and the dv_new tile
 constexpr int BC_QP = 32768, BC_KP = 49152, BC_BP = 98304;
+// intra-chunk operand regions: row block I (16 (I + 1) rows) at bc_row_off(I) in [0, 40K); column
+// block J (64 - 16 J rows; part 0 = q, 1 = b k) at bc_col_off(J, part): blocks 0 and 3 in the free
+// [40K, 64K) and [96K, 120K), blocks 1 and 2 over the row blocks once their MMAs are done
+AHB_DEVICE int bc_row_off(int I) { return I == 0 ? 0 : (I == 1 ? 4096 : (I == 2 ? 12288 : 24576)); }
+AHB_DEVICE int bc_col_off(int J, int part) {
+  if (J == 0) return part ? 98304 : 40960;
+  if (J == 3) return part ? 114688 : 57344;
+  if (J == 1) return part ? 12288 : 0;
+  return part ? 32768 : 24576;
+}
 constexpr size_t BC_SMEM = 1024 + BC_BAR + 512;
 
 __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
@@ -808,12 +869,13 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t S = smem_u32(smem);
   float* GC = reinterpret_cast<float*>(smem + BC_GC);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BC_BAR);  // 0 load, 1 states, 2 WY, 3 T, 4 Gkk, 5-8 rows, 9-12 cols
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BC_BAR);  // 0 load, 1 states, 2 WY, 3 T, 4 Gkk, 5 rows, 6-7 columns
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);          // [0..3] exact diagonal block, [4] abort
   float* span_w = reinterpret_cast<float*>(flags + 8);         // [4][4]
   float* dgcl_s = span_w + 16;                                 // [128]
   float* tail_s = dgcl_s + 128;                                // [128] reverse-sum hand-over between warpgroups
+  PhaseClock pc(16);
 
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quarter = warp & 3, wg = warp >> 2;
@@ -862,6 +924,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   }
   __syncthreads();
   if (!wait_bar(bars, 0, err, 0x4731)) flags[4] = 1;
+  pc.mark(0);
   // state products (one thread issues; the others scan g meanwhile)
   if (tid == 0 && !flags[4]) {
     sm100::tc_fence_after();
@@ -907,6 +970,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     flags[tid] = !(m <= 60.f);
   }
   if (!wait_bar(bars + 1, 0, err, 0x4732)) flags[4] = 1;
+  pc.mark(1);
   sm100::tc_fence_after();
   // WV = w v and BKE = (b k) e^gc over the dead state tiles; the H region is free once the
   // state products completed
@@ -942,6 +1006,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
+  pc.mark(2);
   if (flags[4]) goto bc_teardown;
   // WY products: dA (M = 64) -> [256, 320); d(wv)^T -> [320, 384); dbke^T -> [384, 448)
   if (tid == 0) {
@@ -958,12 +1023,14 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     sm100::umma_commit(bars + 2);
   }
   if (!wait_bar(bars + 2, 0, err, 0x4733)) flags[4] = 1;
+  pc.mark(3);
   sm100::tc_fence_after();
   // dA strictly lower -> DA tile (rows i, columns l)
   rows64_out<1>(tmem, 256, quarter, wg, lane, S + BC_DA, C, 0, nullptr, 0, 0);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
+  pc.mark(4);
   if (tid == 0 && !flags[4]) {
     sm100::tc_fence_after();
     mma_steps(tmem + 448, [&](int s) { return kdesc(S + BC_DA, C, s); }, [&](int s) { return kdesc(S + BC_AT, C, s); },
@@ -999,6 +1066,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
       *reinterpret_cast<uint4*>(dv_o + gi) = pack8(z);
     }
   }
+  pc.mark(5);
   if (!wait_bar(bars + 3, 0, err, 0x4734)) flags[4] = 1;
   sm100::tc_fence_after();
   // T = dA A^T -> T tile (rows l, columns j)
@@ -1013,19 +1081,21 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     sm100::umma_commit(bars + 4);
   }
   if (!wait_bar(bars + 4, 0, err, 0x4735)) flags[4] = 1;
+  pc.mark(6);
   sm100::tc_fence_after();
   // Gkk = -(A^T T) strictly lower -> rows 64-127 of G and G^T
   rows64_out<3>(tmem, 256, quarter, wg, lane, S + BC_G, 128, C, smem + BC_GT, 128, C);
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
+  pc.mark(7);
   if (flags[4]) goto bc_teardown;
-  // intra, row side: per reference block I, key operand (k e^{gc_r - gc})[j][d] for j <= 16 I + 15;
-  // dq_b -> TMEM [128 + 32 I, +16), dbk_b -> [144 + 32 I, +16) (lane d, column i - 16 I)
+  // intra, row side: per reference block I, key operand (k e^{gc_r - gc})[j][d] for j <= 16 I + 15
+  // (16 (I + 1) rows at [0, 40K): offsets 0, 4K, 12K, 24K); dq_b -> TMEM [128 + 32 I, +16),
+  // dbk_b -> [144 + 32 I, +16) (lane d, column i - 16 I).  All four blocks in one pass.
 #pragma unroll
   for (int I = 0; I < 4; ++I) {
-    const uint32_t buf = S + (I & 1) * TILE_CD;
-    if (I >= 2 && !wait_bar(bars + 5 + I - 2, 0, err, 0x4736)) flags[4] = 1;
+    const uint32_t buf = S + bc_row_off(I);
     const bool exact = flags[I];
     const float* gcr = GC + 16 * I * D;
 #pragma unroll
@@ -1036,66 +1106,82 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
       const bool zero = exact && j >= 16 * I;
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gcr[c + e] - GC[j * D + c + e]);
-      st_chunk8(buf + sw_off16(C, j, c), o);
+      st_chunk8(buf + sw_off16(16 * (I + 1), j, c), o);
     }
-    fence_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      sm100::tc_fence_after();
-      constexpr uint32_t ID_R = sm100::idesc_bf16(128, 16, true, false);
-      auto fa = [&](int s) { return mndesc(buf, C, s); };
+  }
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    sm100::tc_fence_after();
+    constexpr uint32_t ID_R = sm100::idesc_bf16(128, 16, true, false);
+#pragma unroll
+    for (int I = 0; I < 4; ++I) {
+      const uint32_t buf = S + bc_row_off(I);
+      auto fa = [&](int s) { return mndesc(buf, 16 * (I + 1), s); };
       mma_steps(tmem + 128 + 32 * I, fa, [&](int s) { return kdesc(S + BC_G + 2048 * I, 128, s); }, I + 1, ID_R, false);
       mma_steps(tmem + 144 + 32 * I, fa, [&](int s) { return kdesc(S + BC_G + 8192 + 2048 * I, 128, s); }, I + 1, ID_R,
                 false);
-      sm100::umma_commit(bars + 5 + I);
     }
+    sm100::umma_commit(bars + 5);
   }
   // intra, column side: per key block J with reference s = 16 J + 15 (its last row), operands
-  // (scale q e^{gc - gc_s}) and ((b k) e^{gc - gc_s}) for rows i >= 16 J (<= 1 below the block);
-  // dk_b -> TMEM [448 + 16 J, +16) (lane d, column j - 16 J), later times e^{gc_s - gc_j} <= 1
+  // (scale q e^{gc - gc_s}) and ((b k) e^{gc - gc_s}) for rows i >= 16 J (<= 1 below the block),
+  // packed to those 64 - 16 J rows; dk_b -> TMEM [448 + 16 J, +16) (lane d, column j - 16 J), later
+  // times e^{gc_s - gc_j} <= 1.  Blocks 0 and 3 go to the free [40K, 64K) and [96K, 120K) while the
+  // row-side MMAs run, blocks 1 and 2 to the row-side buffers once those MMAs are done.
 #pragma unroll
-  for (int J = 0; J < 4; ++J) {
-    const uint32_t bq = S + (J & 1) * 32768, bk2 = bq + TILE_CD;
-    if (J == 0) {
-      if (!wait_bar(bars + 7, 0, err, 0x4737) || !wait_bar(bars + 8, 0, err, 0x4737)) flags[4] = 1;
-    } else if (J >= 2) {
-      if (!wait_bar(bars + 9 + J - 2, 0, err, 0x4738)) flags[4] = 1;
-    }
-    const bool exact = flags[J];
-    const float* gcr = GC + (16 * J + 15) * D;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && !wait_bar(bars + 5, 0, err, 0x4737)) flags[4] = 1;
 #pragma unroll
-    for (int it = J; it < BU; ++it) {
-      const int i = 16 * it + (tid >> 4), c = (tid & 15) << 3;
-      float qv[8], kv[8], bv[8], xq[8], xk[8];
-      unpack8(qa[it], qv);
-      unpack8(ka[it], kv);
-      unpack8(ba[it], bv);
-      const bool zero = exact && i < 16 * J + 16;
+    for (int jj = 0; jj < 2; ++jj) {
+      const int J = pass == 0 ? 3 * jj : 1 + jj;
+      const int R = 64 - 16 * J;
+      const uint32_t bq = S + bc_col_off(J, 0), bk2 = S + bc_col_off(J, 1);
+      const bool exact = flags[J];
+      const float* gcr = GC + (16 * J + 15) * D;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float er = zero ? 0.f : __expf(GC[i * D + c + e] - gcr[c + e]);
-        xq[e] = scale * qv[e] * er;
-        xk[e] = bv[e] * kv[e] * er;
+      for (int it = J; it < BU; ++it) {
+        const int i = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+        float qv[8], kv[8], bv[8], xq[8], xk[8];
+        unpack8(qa[it], qv);
+        unpack8(ka[it], kv);
+        unpack8(ba[it], bv);
+        const bool zero = exact && i < 16 * J + 16;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float er = zero ? 0.f : __expf(GC[i * D + c + e] - gcr[c + e]);
+          xq[e] = scale * qv[e] * er;
+          xk[e] = bv[e] * kv[e] * er;
+        }
+        st_chunk8(bq + sw_off16(R, i - 16 * J, c), xq);
+        st_chunk8(bk2 + sw_off16(R, i - 16 * J, c), xk);
       }
-      st_chunk8(bq + sw_off16(C, i, c), xq);
-      st_chunk8(bk2 + sw_off16(C, i, c), xk);
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 && !flags[4]) {
       sm100::tc_fence_after();
       constexpr uint32_t ID_C = sm100::idesc_bf16(128, 16, true, false);
-      const uint32_t dcol = tmem + 448 + 16 * J;
-      for (int s = J; s < 4; ++s)
-        sm100::umma_bf16(dcol, mndesc(bq, C, s), kdesc(S + BC_GT + 2048 * J, 128, s), ID_C, s > J ? 1u : 0u);
-      for (int s = J; s < 4; ++s)
-        sm100::umma_bf16(dcol, mndesc(bk2, C, s), kdesc(S + BC_GT + 8192 + 2048 * J, 128, s), ID_C, 1u);
-      sm100::umma_commit(bars + 9 + J);
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int J = pass == 0 ? 3 * jj : 1 + jj;
+        const int R = 64 - 16 * J;
+        // descriptor bases shifted down by J K-steps: K step s (rows 16 s ..) sits at 2048 (s - J)
+        const uint32_t bq = S + bc_col_off(J, 0) - 2048 * J, bk2 = S + bc_col_off(J, 1) - 2048 * J;
+        const uint32_t dcol = tmem + 448 + 16 * J;
+        for (int s = J; s < 4; ++s)
+          sm100::umma_bf16(dcol, mndesc(bq, R, s), kdesc(S + BC_GT + 2048 * J, 128, s), ID_C, s > J ? 1u : 0u);
+        for (int s = J; s < 4; ++s)
+          sm100::umma_bf16(dcol, mndesc(bk2, R, s), kdesc(S + BC_GT + 8192 + 2048 * J, 128, s), ID_C, 1u);
+      }
+      sm100::umma_commit(bars + 6 + pass);
     }
   }
-  if (!wait_bar(bars + 11, 0, err, 0x4739) || !wait_bar(bars + 12, 0, err, 0x4739)) flags[4] = 1;
+  pc.mark(8);
+  if (!wait_bar(bars + 6, 0, err, 0x4739) || !wait_bar(bars + 7, 0, err, 0x4739)) flags[4] = 1;
+  pc.mark(9);
   sm100::tc_fence_after();
   // plain row-major q, k, b tiles (256-byte rows) for the per-channel assembly reads
 #pragma unroll
@@ -1106,6 +1192,7 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     *reinterpret_cast<uint4*>(smem + BC_BP + off) = ba[it];
   }
   __syncthreads();
+  pc.mark(10);
   if (flags[4]) goto bc_teardown;
   {
     // assembly: thread d = channel, warpgroup wg = rows [32 wg, 32 wg + 32), one 16-row block at a time
@@ -1171,7 +1258,9 @@ bc_teardown:
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
+  pc.mark(11);
   if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+  pc.done();
 }
 
 template <class K>
@@ -1182,6 +1271,8 @@ int set_smem(K kernel, size_t bytes) {
 }  // namespace
 
 // ===================================================================== launchers
+AHB_PHASE_PROF_SETTER(ahb_gdn_phase_prof)
+
 int ahb_gdn_chunk_fwd_tc(const void* q, const void* k, const void* v, const float* g, const void* bg, const void* wg,
                          float scale, int B, int L, int H, void* wt_t, void* u_t, void* qg_t, void* kg_t, void* aqk_t,
                          float* gcl, void* at_t, int* err, cudaStream_t st) {

@@ -62,6 +62,9 @@ int ahb_ssd_state_bwd_tc(const void* Cm, const void* dy, const void* dec_t, cons
 // chunk-parallel backward: one CTA per (chunk, batch, head group); dB_part / dC_part are (G, B, L, N)
 // fp32 scratch with G = ahb_ssd_head_groups(H), summed into dB / dC; dA (H,) is accumulated (zero it)
 int ahb_ssd_head_groups(int H);
+// diagnostics: per-phase cycle counters of the scan kernels (uint64[64] per file or null; phase_prof.cuh)
+int ahb_ssd_phase_prof(void* counters);
+int ahb_gdn_phase_prof(void* counters);
 int ahb_ssd_bwd_chunk_tc(const void* x, const void* dt, const float* A, const void* Bm, const void* Cm, const void* dy,
                          int B, int L, int H, const void* sin_t, const void* dse_t, const void* yd_t, void* dx, void* ddt,
                          float* dB, float* dC, float* dA, float* dB_part, float* dC_part, int* err, cudaStream_t st);

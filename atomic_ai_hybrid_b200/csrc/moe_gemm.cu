@@ -67,6 +67,10 @@ struct Params {
   // tile m_rot on, so that the ranks start on different destinations
   void* out_tab[MAX_PEERS];
   int m_rot;
+  // M-grouped raster: 0 = N tiles fastest (the A row tile stays hot), 1 = M tiles fastest (the B
+  // column tile stays hot while the CTAs sweep the rows: the LM head, whose vocabulary matrix is
+  // larger than L2 and would otherwise be read once per row tile)
+  int m_fast;
   int m_limit;  // M-grouped: rows at or beyond it are not stored (0: every row of the padded groups)
   // LM-head cross entropy (EPI_CE_*): token labels (-100 = masked), row log-sum-exp (backward),
   // label smoothing weights sp = 1 - ls and sn = ls / (V - 1), vocabulary tiles per row
@@ -126,7 +130,8 @@ template <bool KGROUP>
 AHB_DEVICE bool decode(const Params& p, const int* off, int tile, int n_tiles, Tile& t) {
   if (!KGROUP) {
     const int m_total = off[p.E] / BM;
-    const int mt = (tile / n_tiles + p.m_rot) % m_total, nt = tile % n_tiles;
+    const int mt = p.m_fast ? (tile % m_total + p.m_rot) % m_total : (tile / n_tiles + p.m_rot) % m_total;
+    const int nt = p.m_fast ? tile / m_total : tile % n_tiles;
     t.m0 = mt * BM;
     int e = 0;
     while (e + 1 < p.E && off[e + 1] <= t.m0) ++e;
@@ -523,7 +528,7 @@ template <bool KGROUP>
 AHB_DEVICE void decode_pair(const Params& p, const int* off, int tile, int n_tiles, Tile& t) {
   if (!KGROUP) {
     const int m_total = off[p.E] / PAIR_BM;
-    const int mt = tile / n_tiles, nt = tile % n_tiles;
+    const int mt = p.m_fast ? tile % m_total : tile / n_tiles, nt = p.m_fast ? tile / m_total : tile % n_tiles;
     t.m0 = mt * PAIR_BM;
     int e = 0;
     while (e + 1 < p.E && off[e + 1] <= t.m0) ++e;
@@ -531,7 +536,6 @@ AHB_DEVICE void decode_pair(const Params& p, const int* off, int tile, int n_til
     t.n0 = nt;
     t.k0row = 0;
     t.nkb = p.kb_total;
-    (void)m_total;
   } else {
     const int m_tiles = p.Mout / PAIR_BM;
     const int per_e = m_tiles * n_tiles;
@@ -957,6 +961,7 @@ int ahb_ce_gemm(bool bwd, const void* h, int64_t rows, int d, const void* W, int
   p.ce_sp = 1.f - ls;
   p.ce_sn = ls > 0.f ? ls / (float)(V - 1) : 0.f;
   p.ce_tiles = (V + 255) / 256;
+  p.m_fast = 1;
   int rc = make_map(&p.ta0, h, rows, d, d, BM);
   rc |= make_map(&p.tb0, W, V, d, d, pair ? 128 : 256);
   if (rc) return -20;

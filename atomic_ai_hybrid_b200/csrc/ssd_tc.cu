@@ -28,6 +28,7 @@
 #include "umma.cuh"
 #include "tmap.h"
 #include "launchers.h"
+#include "phase_prof.cuh"
 
 using namespace ahb;
 using namespace ahb::umma;
@@ -71,8 +72,9 @@ AHB_DEVICE void chunk_cumsum(const unsigned char* dt_tile, float Ah, float* CUM,
 
 // ============================================================ chunk-parallel forward
 constexpr int S1_THREADS = 256;
+// byte offsets; W (16 KB) holds the y_diag key operands, then the fp32 y_diag rows
 constexpr int S1_B = 0, S1_C = 16384, S1_X = 32768, S1_DT = 40960, S1_CB = 49152, S1_V = 57344, S1_W0 = 65536,
-              S1_W1 = 73728, S1_CUM = 81920, S1_BAR = 98304;
+              S1_CUM = 81920, S1_BAR = 98304;
 constexpr size_t S1_SMEM = 1024 + S1_BAR + 256;
 
 __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
@@ -84,9 +86,10 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t S = smem_u32(smem);
   float* CUM = reinterpret_cast<float*>(smem + S1_CUM);  // [i][p]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S1_BAR);  // 0 load, 1 CB, 2 S_end, 3-6 y_diag blocks
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S1_BAR);  // 0 load, 1 CB, 2 S_end, 3 y_diag blocks
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [4] abort
+  PhaseClock pc(0);
 
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z, NC = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quarter = warp & 3, wg = warp >> 2;
@@ -109,7 +112,9 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pc.mark(0);
   if (!wait_bar(bars, 0, err, 0x5301)) flags[4] = 1;
+  pc.mark(1);
   if (tid == 0 && !flags[4]) {  // CB = C B^T  (M = 64 rows i, N = 64 keys j)
     sm100::tc_fence_after();
     mma_steps(tmem, [&](int s) { return kdesc(S + S1_C, C, s); }, [&](int s) { return kdesc(S + S1_B, C, s); }, N / 16,
@@ -144,6 +149,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
               C / 16, sm100::idesc_bf16(128, 64, true, true), false);
     sm100::umma_commit(bars + 2);
   }
+  pc.mark(2);
   if (!wait_bar(bars + 1, 0, err, 0x5302)) flags[4] = 1;
   sm100::tc_fence_after();
   {  // causal CB -> bf16 K-major tile (rows i, columns j <= i): row i = 16 quarter + (lane & 15) sits
@@ -165,49 +171,55 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
-  // y_diag^T per reference block I (r = 16 I): W[j][p] = dBx e^{c_r - c_j} for keys j <= 16 I + 15,
+  pc.mark(3);
+  // y_diag^T per reference block I (r = 16 I): W[j][p] = dBx e^{c_r - c_j} for keys j < 16 I (the
+  // diagonal block is summed exactly below, so block 0 has no tensor-core part),
   // D[p][i in block I] += W^T CB^T  -> TMEM columns [128 + 16 I, +16)
   // The key operand is split into bf16 hi + lo parts (two MMAs): the backward's decay gradient
   // cancels these sums against the matching column sums, which bf16 alone would not resolve.
+  // Blocks 1-3 are built in one pass (768 units), packed: block I's K steps 0 .. I - 1 (2 KB each)
+  // from 0, 2 KB, 6 KB of the hi (W) and lo (dead C tile) regions.
 #pragma unroll
-  for (int I = 0; I < 4; ++I) {
-    const uint32_t buf = S + ((I & 1) ? S1_W1 : S1_W0);
-    const uint32_t blo = S + S1_C + (I & 1) * T_CP;  // the C tile is dead once CB is formed
-    if (I >= 2 && !wait_bar(bars + 3 + I - 2, 0, err, 0x5303)) flags[4] = 1;
+  for (int it = 0; it < 768 / S1_THREADS; ++it) {
+    const int u_ = it * S1_THREADS + tid;
+    const int I = u_ < 128 ? 1 : (u_ < 384 ? 2 : 3);
+    const int lu = u_ - (I == 1 ? 0 : (I == 2 ? 128 : 384));
+    const int j = lu >> 3, c = (lu & 7) << 3;
+    const int boff = I == 1 ? 0 : (I == 2 ? 2048 : 6144);
+    float xv[8], dv[8], o[8], lo[8];
+    unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
+    unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
+    float cj[8], cr8[8];
+    ld8f(CUM + j * P + c, cj);
+    ld8f(CUM + 16 * I * P + c, cr8);
 #pragma unroll
-    for (int u_ = tid; u_ < 16 * (I + 1) * 8; u_ += S1_THREADS) {
-      const int j = u_ >> 3, c = (u_ & 7) << 3;
-      float xv[8], dv[8], o[8], lo[8];
-      unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
-      unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
-      const bool zero = j >= 16 * I;  // the diagonal block is summed exactly below
-      float cj[8], cr8[8];
-      ld8f(CUM + j * P + c, cj);
-      ld8f(CUM + 16 * I * P + c, cr8);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
-        lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
-      }
-      st_chunk8(buf + sw_off16(C, j, c), o);
-      st_chunk8(blo + sw_off16(C, j, c), lo);
+    for (int e = 0; e < 8; ++e) {
+      o[e] = clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
+      lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
     }
-    fence_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !flags[4]) {
-      sm100::tc_fence_after();
-      constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
-      auto fcb = [&](int k) { return kdesc(S + S1_CB + 2048 * I, C, k); };
-      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(buf, C, k); }, fcb, I + 1, ID, false);
-      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(blo, C, k); }, fcb, I + 1, ID, true);
-      sm100::umma_commit(bars + 3 + I);
-    }
+    st_chunk8(S + S1_W0 + boff + sw_off16(C, j, c), o);
+    st_chunk8(S + S1_C + boff + sw_off16(C, j, c), lo);  // the C tile is dead once CB is formed
   }
-  if (!wait_bar(bars + 2, 0, err, 0x5304) || !wait_bar(bars + 5, 0, err, 0x5304) || !wait_bar(bars + 6, 0, err, 0x5304))
-    flags[4] = 1;
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && !flags[4]) {
+    sm100::tc_fence_after();
+    constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
+#pragma unroll
+    for (int I = 1; I < 4; ++I) {
+      const int boff = I == 1 ? 0 : (I == 2 ? 2048 : 6144);
+      auto fcb = [&](int k) { return kdesc(S + S1_CB + 2048 * I, C, k); };
+      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(S + S1_W0 + boff, C, k); }, fcb, I, ID, false);
+      mma_steps(tmem + 128 + 16 * I, [&](int k) { return mndesc(S + S1_C + boff, C, k); }, fcb, I, ID, true);
+    }
+    sm100::umma_commit(bars + 3);
+  }
+  pc.mark(4);
+  if (!wait_bar(bars + 2, 0, err, 0x5304) || !wait_bar(bars + 3, 0, err, 0x5304)) flags[4] = 1;
   sm100::tc_fence_after();
   __syncthreads();
+  pc.mark(5);
   if (flags[4]) goto s1_teardown;
   {
     // S_end^T rows (lane = state row s) -> tile image (rows s, columns p); warpgroup wg takes
@@ -230,7 +242,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     // into the dead W buffers; then the diagonal 16 x 16 blocks summed exactly per channel (fp32,
     // exponent floored at -20: these terms dominate and the backward's decay gradient cancels
     // them against the matching column sums); then fp32 rows out
-    float* YD = reinterpret_cast<float*>(smem + S1_W0);  // [p][i]
+    float* YD = reinterpret_cast<float*>(smem + S1_W0);  // [i][p]
     {  // channel p = 16 quarter + (lane & 15), rows [32 wg + 16 hf, +16): one reference block per thread
       const int hf = lane >> 4, p = 16 * quarter + (lane & 15), i0 = 32 * wg + 16 * hf;
       float x[32], y[16];
@@ -238,13 +250,14 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
-        y[e] = hf ? sh : x[e];
+        y[e] = hf ? sh : (i0 == 0 ? 0.f : x[e]);  // block 0 has no tensor-core part
       }
       const float cr = CUM[i0 * P + p];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) YD[p * C + i0 + e] = y[e] * __expf(CUM[(i0 + e) * P + p] - cr);
+      for (int e = 0; e < 16; ++e) YD[(i0 + e) * P + p] = y[e] * __expf(CUM[(i0 + e) * P + p] - cr);
     }
     __syncthreads();
+    pc.mark(6);
     {
       // four threads per channel p, one block each: y[i] += e^{c_i - c_r} sum_{j<=i} CB[i][j] (dBx_j e^{c_r - c_j})
       // with r the block's first row (fp32 factors; per-pair exponents where the block's span could
@@ -273,7 +286,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
             float acc = 0.f;
 #pragma unroll
             for (int j = 0; j <= i; ++j) acc += cb[j] * w[j];
-            YD[p * C + r + i] += __expf(CUM[(r + i) * P + p] - cr) * acc;
+            YD[(r + i) * P + p] += __expf(CUM[(r + i) * P + p] - cr) * acc;
           }
         } else {
 #pragma unroll 1
@@ -285,19 +298,21 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
               if (j <= i)
                 acc += __bfloat162float(*reinterpret_cast<const bf16*>(smem + S1_CB + sw_off(C, r + i, r + j))) *
                        w[j] * __expf(fmaxf(ci - CUM[(r + j) * P + p], -20.f));
-            YD[p * C + r + i] += acc;
+            YD[(r + i) * P + p] += acc;
           }
         }
       }
     }
     __syncthreads();
-    {  // fp32 rows out: channel p = tid >> 2, a quarter of its 64 rows per thread
-      const int p = tid >> 2, c0 = 16 * (tid & 3);
-      float* dst2 = yd_t + ch * (C * P) + p * C;
+    pc.mark(7);
+    {  // fp32 rows [i][p] out as 16-byte vectors
+      float* dst2 = yd_t + ch * (C * P);
 #pragma unroll
-      for (int c = c0; c < c0 + 16; c += 4)
-        *reinterpret_cast<float4*>(dst2 + c) = make_float4(clip4(YD[p * C + c]), clip4(YD[p * C + c + 1]),
-                                                           clip4(YD[p * C + c + 2]), clip4(YD[p * C + c + 3]));
+      for (int it = 0; it < (C * P / 4) / S1_THREADS; ++it) {
+        const int e4 = 4 * (it * S1_THREADS + tid);
+        const float4 v4 = *reinterpret_cast<const float4*>(YD + e4);
+        *reinterpret_cast<float4*>(dst2 + e4) = make_float4(clip4(v4.x), clip4(v4.y), clip4(v4.z), clip4(v4.w));
+      }
     }
     // decay e^{max(c, -20)} as a tile image (rows i, columns p)
 #pragma unroll
@@ -315,7 +330,9 @@ s1_teardown:
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
+  pc.mark(8);
   if (warp == 0) sm100::tmem_dealloc(tmem, 256);
+  pc.done();
 }
 
 // ============================================================ state recurrence, forward
@@ -399,10 +416,10 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
     }
     // carry the state: S <- clip(S e^{max(cl, -20)} + S_end)   (S_end^T row s from the image)
     const int p0 = 16 * warp + lane;  // channel of this lane in the y epilogue (lanes 0-15)
-    float4 ydr[16];
+    float ydr[C];
     if (lane < 16)
 #pragma unroll
-      for (int q4 = 0; q4 < 16; ++q4) ydr[q4] = *reinterpret_cast<const float4*>(yd_t + c * (C * P) + p0 * C + 4 * q4);
+      for (int i = 0; i < C; ++i) ydr[i] = yd_t[c * (C * P) + i * P + p0];
     if (!wait_bar(bars + st, (n >> 1) & 1, err, 0x5312)) *abort_flag = 1;  // every thread reads the stage
     {
       const float* clp = reinterpret_cast<const float*>(smem + S2_CL + st * 256);
@@ -425,15 +442,9 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
         const unsigned char* dec = smem + st * S2_STAGE + T_CN + T_NP;
         bf16* Y = reinterpret_cast<bf16*>(smem + S2_Y);
 #pragma unroll
-        for (int q8 = 0; q8 < 8; ++q8) {
-          const float yd[8] = {ydr[2 * q8].x, ydr[2 * q8].y, ydr[2 * q8].z, ydr[2 * q8].w,
-                               ydr[2 * q8 + 1].x, ydr[2 * q8 + 1].y, ydr[2 * q8 + 1].z, ydr[2 * q8 + 1].w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int i = 8 * q8 + e;
-            const float dh = __bfloat162float(*reinterpret_cast<const bf16*>(dec + sw_off(C, i, p0)));
-            Y[i * P + p0] = __float2bfloat16_rn(clip4(yd[e] + clip4(yo[i] * dh)));
-          }
+        for (int i = 0; i < C; ++i) {
+          const float dh = __bfloat162float(*reinterpret_cast<const bf16*>(dec + sw_off(C, i, p0)));
+          Y[i * P + p0] = __float2bfloat16_rn(clip4(ydr[i] + clip4(yo[i] * dh)));
         }
       }
     }
@@ -600,17 +611,26 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
 constexpr int SB_THREADS = 256;
 constexpr int SB_B = 0, SB_C = 16384, SB_CB = 32768, SB_CBT = 40960, SB_DCB = 49152, SB_X = 65536, SB_DT = 73728,
               SB_DY = 81920, SB_S = 90112, SB_DS = 106496, SB_CUM = 122880, SB_DYR = 139264, SB_BI0 = 147456,
-              SB_BI1 = 155648, SB_DYD = 163840, SB_V = 172032, SB_DYS0 = 180224, SB_DYS1 = 188416, SB_BAR = 196608;
+              SB_BI1 = 155648, SB_DYD = 163840, SB_V = 172032, SB_DYS0 = 180224, SB_DYS1 = 188416, SB_YD = 196608,
+              SB_BAR = 212992;
 // per-head outputs dx, ddt staged as plain [i][p] bf16 rows over the dead phase-1 operands, and the
 // diagonal part of ddd (fp32 [p][j]) after them
 constexpr int SB_OX = SB_DYR, SB_ODT = SB_DYR + T_CP, SB_DDG = SB_BI1, SB_XCH = SB_DDG + 16384;
 constexpr size_t SB_SMEM = 1024 + SB_BAR + 256;
 // TMEM columns: dC [0,128) and dB [128,256) (M = 64, N = 128); dCB per row block I at 256 + 8 I (I + 1)
-// (widths 16, 32, 48, 64); dds^T [416, 480); later ddd^T per key block J at 256 + 16 J and
+// (widths 16, 32, 48, 64); dds^T [416, 480); later ddd^T per key block J < 3 at 256 + 16 J and
 // y_off^T [320, 384)
 constexpr int TM_DC = 0, TM_DB = 128, TM_DCB = 256, TM_DDS = 416, TM_DDD = 256, TM_YO = 320;
 
 AHB_DEVICE int dcb_off(int I) { return 8 * I * (I + 1); }
+// fp32 dCB sum [i][j], row i rotated by i words: the 16 rows of a readout warp hit 16 banks
+AHB_DEVICE int dcb_at(int i, int j) { return i * C + ((i + j) & (C - 1)); }
+// key operand buffer of dCB row block I (rows j <= 16 I + 15)
+AHB_DEVICE int dcb_buf(int I) { return I == 0 ? SB_BI0 : (I == 1 ? SB_BI1 : (I == 2 ? SB_DYS0 : SB_DYS1)); }
+// hi / lo operand bases of ddd block J (K steps J + 1 .. 3 stored from 6 KB, 10 KB, 12 KB down:
+// regions DYS0 and DYR, 12 KB each)
+AHB_DEVICE int ddd_hi(int J) { return SB_DYS0 + (J == 0 ? 0 : (J == 1 ? 6144 : 10240)) - 2048 * (J + 1); }
+AHB_DEVICE int ddd_lo(int J) { return SB_DYR + (J == 0 ? 0 : (J == 1 ? 6144 : 10240)) - 2048 * (J + 1); }
 
 // Exact per-channel sum of the diagonal block J for the intra part of d(dBx) at row i, channel p:
 // sum over rows i2 >= i of the block of CB[i2][i] dy[i2][p] e^{max(c_i2 - c_i, -20)}, in fp32 like
@@ -629,11 +649,12 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
   const uint32_t S = smem_u32(smem);
   float* CUM = reinterpret_cast<float*>(smem + SB_CUM);  // [i][p]
   float* DCB = reinterpret_cast<float*>(smem + SB_DCB);  // [i][j]
-  // barriers: 0 B/C, 1 CB, 2 head loads, 3 phase 1, 4-7 dCB blocks, 8-11 ddd blocks, 12 y_off, 13 final
+  // barriers: 0 B/C, 1 CB, 2 head loads, 3 phase 1, 4 dCB blocks, 8 ddd blocks and y_off, 13 final
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SB_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0..3] exact diagonal blocks of this head, [4] abort
   float* span_w = reinterpret_cast<float*>(flags + 8);  // [2][4]
+  PhaseClock pc(16);
 
   const int n = blockIdx.x, b = blockIdx.y, NC = gridDim.x;
   const int hpg = H / gridDim.z, h0 = blockIdx.z * hpg;
@@ -682,6 +703,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
   fence_async_smem();
   sm100::tc_fence_before();
   __syncthreads();
+  pc.mark(0);
   if (flags[4]) goto sb_teardown;
   for (int hh = 0; hh < hpg; ++hh) {
     const int h = h0 + hh;
@@ -689,14 +711,16 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     const int64_t ch = ((int64_t)b * H + h) * NC + n;
     const float Ah = A[h];
     if (tid == 0) {
-      sm100::mbar_expect_tx(bars + 2, 3 * T_CP + 2 * T_NP);
+      sm100::mbar_expect_tx(bars + 2, 3 * T_CP + 2 * T_NP + C * P * 4);
       tma_load_3d(smem + SB_X, &tm_x, bars + 2, 0, h, row0);
       tma_load_3d(smem + SB_DT, &tm_dt, bars + 2, 0, h, row0);
       tma_load_3d(smem + SB_DY, &tm_dy, bars + 2, 0, h, row0);
       bulk_g2s(smem + SB_S, sin_t + ch * T_NP, T_NP, bars + 2);
       bulk_g2s(smem + SB_DS, dse_t + ch * T_NP, T_NP, bars + 2);
+      bulk_g2s(smem + SB_YD, yd_t + ch * (C * P), C * P * 4, bars + 2);  // intra-chunk y rows [i][p]
     }
     if (!wait_bar(bars + 2, ph, err, 0x5333)) flags[4] = 1;
+    pc.mark(1);
     // decay cumsum (block totals exchanged in the DYR buffer, written only after it)
     chunk_cumsum(smem + SB_DT, Ah, CUM, reinterpret_cast<float*>(smem + SB_DYR), tid);
     if (tid < P) {  // span of each 16-row block
@@ -709,6 +733,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
         for (int I = 0; I < 4; ++I) span_w[warp * 4 + I] = sp[I];
     }
     __syncthreads();
+    pc.mark(2);
     if (tid < 4) flags[tid] = !(fmaxf(span_w[tid], span_w[4 + tid]) <= 60.f);
     // DYR = dy e^{c - c_r(i)}, DYD = dy e^{max(c,-20)}, V = dBx e^{max(cl - c, -20)}  (rows, columns p)
 #pragma unroll
@@ -736,6 +761,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(3);
     if (tid == 0 && !flags[4]) {
       sm100::tc_fence_after();
       const bool acc = hh > 0;
@@ -747,56 +773,57 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
                 N / 16, sm100::idesc_bf16(64, 64, true, false), false);
       sm100::umma_commit(bars + 3);
     }
-    // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15
+    // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15, the four blocks'
+    // operands (BI0, BI1, DYS0, DYS1; 1280 16-byte units) in one pass, then the four MMAs
 #pragma unroll
-    for (int I = 0; I < 4; ++I) {
-      const uint32_t buf = S + ((I & 1) ? SB_BI1 : SB_BI0);
-      if (I >= 2 && !wait_bar(bars + 4 + I - 2, ph, err, 0x5334)) flags[4] = 1;
-      const bool exact = flags[I];
+    for (int it = 0; it < 1280 / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int I = u_ < 128 ? 0 : (u_ < 384 ? 1 : (u_ < 768 ? 2 : 3));
+      const int lu = u_ - 64 * I * (I + 1);
+      const int j = lu >> 3, c = (lu & 7) << 3;
+      float xv[8], dv[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
+      const bool zero = flags[I] && j >= 16 * I;
+      float cj[8], cr8[8];
+      ld8f(CUM + j * P + c, cj);
+      ld8f(CUM + 16 * I * P + c, cr8);
 #pragma unroll
-      for (int u_ = tid; u_ < 16 * (I + 1) * 8; u_ += SB_THREADS) {
-        const int j = u_ >> 3, c = (u_ & 7) << 3;
-        float xv[8], dv[8], o[8];
-        unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
-        unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
-        const bool zero = exact && j >= 16 * I;
-        float cj[8], cr8[8];
-        ld8f(CUM + j * P + c, cj);
-        ld8f(CUM + 16 * I * P + c, cr8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
-        st_chunk8(buf + sw_off16(C, j, c), o);
-      }
-      fence_async_smem();
-      sm100::tc_fence_before();
-      __syncthreads();
-      if (tid == 0 && !flags[4]) {
-        sm100::tc_fence_after();
-        mma_steps(tmem + TM_DCB + dcb_off(I), [&](int k) { return kdesc(S + SB_DYR, C, k); },
-                  [&](int k) { return kdesc(buf, C, k); }, P / 16, sm100::idesc_bf16(64, 16 * (I + 1), false, false),
-                  false);
-        sm100::umma_commit(bars + 4 + I);
-      }
+      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
+      st_chunk8(S + dcb_buf(I) + sw_off16(C, j, c), o);
     }
-    if (!wait_bar(bars + 3, ph, err, 0x5335) || !wait_bar(bars + 6, ph, err, 0x5335) ||
-        !wait_bar(bars + 7, ph, err, 0x5335))
-      flags[4] = 1;
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && !flags[4]) {
+      sm100::tc_fence_after();
+#pragma unroll
+      for (int I = 0; I < 4; ++I)
+        mma_steps(tmem + TM_DCB + dcb_off(I), [&](int k) { return kdesc(S + SB_DYR, C, k); },
+                  [&](int k) { return kdesc(S + dcb_buf(I), C, k); }, P / 16,
+                  sm100::idesc_bf16(64, 16 * (I + 1), false, false), false);
+      sm100::umma_commit(bars + 4);
+    }
+    pc.mark(4);
+    if (!wait_bar(bars + 3, ph, err, 0x5335) || !wait_bar(bars + 4, ph, err, 0x5335)) flags[4] = 1;
+    pc.mark(5);
     sm100::tc_fence_after();
-    if (wg == 0) {  // dCB rows i = 16 warp + lane (block I = warp) into the fp32 sum over the heads
-      const int i = 16 * warp + lane, I = warp;
-      float x[64];
+    {  // dCB rows i = 16 quarter + lane (block I = quarter) into the fp32 sum over the heads; the
+       // warpgroups take alternate 16-column blocks
+      const int i = 16 * quarter + lane, I = quarter;
 #pragma unroll
-      for (int p4 = 0; p4 < 4; ++p4)
-        if (p4 <= I) tmem_ld16(tmem_at(tmem, warp, TM_DCB + dcb_off(I) + 16 * p4), x + 16 * p4);
-      if (lane < 16) {
-#pragma unroll
-        for (int p4 = 0; p4 < 4; ++p4)
-          if (p4 <= I)
+      for (int p4 = wg; p4 < 4; p4 += 2)
+        if (p4 <= I) {
+          float x[16];
+          tmem_ld16(tmem_at(tmem, quarter, TM_DCB + dcb_off(I) + 16 * p4), x);
+          if (lane < 16)
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int j = 16 * p4 + e;
-              if (j <= i) DCB[i * C + j] += x[16 * p4 + e];
+              if (j <= i) DCB[dcb_at(i, j)] += x[e];
             }
+        }
+      if (wg == (I & 1) && lane < 16) {  // the warp that added block p4 = I
         if (flags[I]) {  // exact per-channel sums on the diagonal block
           for (int j = 16 * I; j <= i; ++j) {
             float acc = 0.f;
@@ -806,59 +833,62 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
               const float dv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, j, p)));
               acc += dyv * clip4(dv * xv) * __expf(fmaxf(CUM[i * P + p] - CUM[j * P + p], -20.f));
             }
-            DCB[i * C + j] += acc;
+            DCB[dcb_at(i, j)] += acc;
           }
         }
       }
     }
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(6);
     if (flags[4]) break;
     // phase 2: ddd^T per key block J (reference s = 16 J + 15) and y_off^T
+    // ddd^T blocks J = 0..2 below the diagonal block (rows i >= 16 J + 16; block 3 has none) as bf16
+    // hi + lo operands, packed: block J's K steps J + 1 .. 3 (2 KB each) at hi / lo bases shifted
+    // down by 2 KB (J + 1); one pass (768 units), then the MMAs and y_off^T
 #pragma unroll
-    for (int J = 0; J < 4; ++J) {
-      const uint32_t buf = S + ((J & 1) ? SB_DYS1 : SB_DYS0);
-      const uint32_t blo = S + SB_DYR + (J & 1) * T_CP;  // hi / lo split, as the forward's key operand
-      if (J >= 2 && !wait_bar(bars + 8 + J - 2, ph, err, 0x5336)) flags[4] = 1;
-      const float* cs = CUM + (16 * J + 15) * P;
+    for (int it = 0; it < 768 / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int J = u_ < 384 ? 0 : (u_ < 640 ? 1 : 2);
+      const int lu = u_ - (J == 0 ? 0 : (J == 1 ? 384 : 640));
+      const int i = 16 * (J + 1) + (lu >> 3), c = (lu & 7) << 3;
+      float dy[8], o[8], lo[8];
+      unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
+      float ci[8], cs8[8];
+      ld8f(CUM + i * P + c, ci);
+      ld8f(CUM + (16 * J + 15) * P + c, cs8);
 #pragma unroll
-      for (int u_ = 16 * J * 8 + tid; u_ < C * 8; u_ += SB_THREADS) {
-        const int i = u_ >> 3, c = (u_ & 7) << 3;
-        float dy[8], o[8], lo[8];
-        unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
-        const bool zero = i < 16 * J + 16;  // the diagonal block is summed exactly in the epilogue
-        float ci[8], cs8[8];
-        ld8f(CUM + i * P + c, ci);
-        ld8f(cs + c, cs8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          o[e] = zero ? 0.f : dy[e] * __expf(ci[e] - cs8[e]);
-          lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
-        }
-        st_chunk8(buf + sw_off16(C, i, c), o);
-        st_chunk8(blo + sw_off16(C, i, c), lo);
+      for (int e = 0; e < 8; ++e) {
+        o[e] = dy[e] * __expf(ci[e] - cs8[e]);
+        lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
       }
-      fence_async_smem();
-      sm100::tc_fence_before();
-      __syncthreads();
-      if (tid == 0 && !flags[4]) {
-        sm100::tc_fence_after();
-        constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
-        for (int k = J; k < 4; ++k)
-          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(buf, C, k), kdesc(S + SB_CBT + 2048 * J, C, k), ID,
-                           k > J ? 1u : 0u);
-        for (int k = J; k < 4; ++k)
-          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(blo, C, k), kdesc(S + SB_CBT + 2048 * J, C, k), ID, 1u);
-        if (J == 3)
-          mma_steps(tmem + TM_YO, [&](int k) { return mndesc(S + SB_S, N, k); },
-                    [&](int k) { return kdesc(S + SB_C, C, k); }, N / 16, sm100::idesc_bf16(64, 64, true, false), false);
-        sm100::umma_commit(bars + 8 + J);
-      }
+      st_chunk8(S + ddd_hi(J) + sw_off16(C, i, c), o);
+      st_chunk8(S + ddd_lo(J) + sw_off16(C, i, c), lo);
     }
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && !flags[4]) {
+      sm100::tc_fence_after();
+      constexpr uint32_t ID = sm100::idesc_bf16(64, 16, true, false);
+#pragma unroll
+      for (int J = 0; J < 3; ++J) {
+        for (int k = J + 1; k < 4; ++k)
+          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(S + ddd_hi(J), C, k), kdesc(S + SB_CBT + 2048 * J, C, k),
+                           ID, k > J + 1 ? 1u : 0u);
+        for (int k = J + 1; k < 4; ++k)
+          sm100::umma_bf16(tmem + TM_DDD + 16 * J, mndesc(S + ddd_lo(J), C, k), kdesc(S + SB_CBT + 2048 * J, C, k),
+                           ID, 1u);
+      }
+      mma_steps(tmem + TM_YO, [&](int k) { return mndesc(S + SB_S, N, k); },
+                [&](int k) { return kdesc(S + SB_C, C, k); }, N / 16, sm100::idesc_bf16(64, 64, true, false), false);
+      sm100::umma_commit(bars + 8);
+    }
+    pc.mark(7);
     {
       // diagonal blocks of ddd, four threads per channel, one block each, while the MMAs run:
       // ddd[j] = e^{c_s - c_j} sum_{i>=j} CB[i][j] (dy_i e^{c_i - c_s}) with s the block's last row
-      float* DDG = reinterpret_cast<float*>(smem + SB_DDG);  // [p][j]
+      float* DDG = reinterpret_cast<float*>(smem + SB_DDG);  // [j][p]
       const int p = tid & 63;
       {
         const int J = tid >> 6;
@@ -882,16 +912,18 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
             float acc = 0.f;
 #pragma unroll
             for (int i = j; i < 16; ++i) acc += cb[i] * u[i];
-            DDG[p * C + r + j] = __expf(cs - CUM[(r + j) * P + p]) * acc;
+            DDG[(r + j) * P + p] = __expf(cs - CUM[(r + j) * P + p]) * acc;
           }
         } else {
-          for (int j = 0; j < 16; ++j) DDG[p * C + r + j] = sb_exact_ddd(smem, CUM, p, r + j, J);
+          for (int j = 0; j < 16; ++j) DDG[(r + j) * P + p] = sb_exact_ddd(smem, CUM, p, r + j, J);
         }
       }
     }
-    if (!wait_bar(bars + 10, ph, err, 0x5337) || !wait_bar(bars + 11, ph, err, 0x5337)) flags[4] = 1;
+    pc.mark(8);
+    if (!wait_bar(bars + 8, ph, err, 0x5337)) flags[4] = 1;
     sm100::tc_fence_after();
     __syncthreads();
+    pc.mark(9);
     {
       // four threads per channel p = 16 quarter + (lane & 15), one 16-row block each, in descending
       // row order k = 2 wg + (lane >> 4): block J = 3 - k (warpgroup 0 rows 32-63, lanes 0-15 the
@@ -920,7 +952,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const float sh = __shfl_sync(0xffffffffu, lo16[e], cl16);
-          ddd[e] = hf ? sh : hi16[e];
+          ddd[e] = hf ? sh : (J == 3 ? 0.f : hi16[e]);  // block 3 is all diagonal: no MMA part
         }
         tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * jb), lo16);
         tmem_ld16(tmem_at(tmem, quarter, TM_YO + 16 * (jb + 1)), hi16);
@@ -942,13 +974,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
         if (cl > -20.f) dclp += car * __expf(cl);
       }
       {
-        float ydv[16];
-        const float* ydr = yd_t + ch * (C * P) + p * C + 16 * J;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 v4 = *reinterpret_cast<const float4*>(ydr + 4 * q4);
-          ydv[4 * q4] = v4.x; ydv[4 * q4 + 1] = v4.y; ydv[4 * q4 + 2] = v4.z; ydv[4 * q4 + 3] = v4.w;
-        }
+        const float* ydr = reinterpret_cast<const float*>(smem + SB_YD);  // [i][p]
         const float cs = CUM[(16 * J + 15) * P + p];
 #pragma unroll
         for (int r = 15; r >= 0; --r) {
@@ -958,10 +984,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           const float xv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_X + sw_off(C, i, p)));
           const float dtv = __bfloat162float(*reinterpret_cast<const bf16*>(smem + SB_DT + sw_off(C, i, p)));
           const float bx = clip4(dtv * xv);
-          const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[p * C + i];
+          const float dd = ddd[r] * __expf(cs - ci) + reinterpret_cast<const float*>(smem + SB_DDG)[i * P + p];
           const float dlt = cl - ci;
           const float ds = dds[r] * __expf(fmaxf(dlt, -20.f));
-          float dc = dyv * ydv[r] - bx * dd;
+          float dc = dyv * ydr[i * P + p] - bx * dd;
           if (ci > -20.f) dc += dyv * yo[r] * __expf(ci);
           if (dlt > -20.f) {
             dc -= bx * ds;
@@ -976,6 +1002,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       XCH[kq * 64 + p] = local;
       XCH[(4 + kq) * 64 + p] = dclp;
       __syncthreads();
+      pc.mark(10);
       float dAh = 0.f;
       {
         float off = XCH[4 * 64 + p] + XCH[5 * 64 + p] + XCH[6 * 64 + p] + XCH[7 * 64 + p];
@@ -998,6 +1025,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     }
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(11);
 #pragma unroll
     for (int it = 0; it < (C * P / 8) / SB_THREADS; ++it) {
       const int u_ = it * SB_THREADS + tid;
@@ -1007,6 +1035,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       *reinterpret_cast<uint4*>(ddt_o + gi) = *reinterpret_cast<const uint4*>(smem + SB_ODT + (i * P + c8) * 2);
     }
     __syncthreads();
+    pc.mark(12);
   }
   if (flags[4]) goto sb_teardown;
   // dC += dCB B and dB += dCB^T C with dCB summed over the group's heads
@@ -1014,7 +1043,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
   for (int it = 0; it < (C * C / 8) / SB_THREADS; ++it) {
     const int u_ = it * SB_THREADS + tid;
     const int i = u_ >> 3, c = (u_ & 7) << 3;
-    st_chunk8(S + SB_CB + sw_off16(C, i, c), DCB + i * C + c);
+    float r8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r8[e] = DCB[dcb_at(i, c + e)];
+    st_chunk8(S + SB_CB + sw_off16(C, i, c), r8);
   }
   fence_async_smem();
   sm100::tc_fence_before();
@@ -1048,7 +1080,9 @@ sb_teardown:
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
+  pc.mark(13);
   if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+  pc.done();
 }
 
 __global__ void sum_groups_tc(const float* __restrict__ part, int G, int64_t n, float* __restrict__ out) {
@@ -1105,6 +1139,8 @@ int ahb_ssd_fwd_tc(const void* x, const void* dt, const float* A, const void* Bm
   return ssd_forward(x, dt, A, Bm, Cm, B, L, H, (unsigned char*)send_t, (float*)yd_t, (unsigned char*)dec_t, cl, s0,
                      s_final, y, (unsigned char*)sin_t, err, st);
 }
+
+AHB_PHASE_PROF_SETTER(ahb_ssd_phase_prof)
 
 int ahb_ssd_head_groups(int H) {
   for (int g : {8, 4, 2}) if (H % g == 0) return g;

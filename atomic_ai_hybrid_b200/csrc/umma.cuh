@@ -110,6 +110,18 @@ AHB_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b
                : "memory");
 }
 
+// 1-D bulk copy shared -> global (16-byte aligned, size multiple of 16) in the issuing thread's
+// bulk group; bulk_commit closes the group, bulk_wait_read lets the thread reuse the source once
+// the copies have read it, bulk_wait_all waits for the writes too
+AHB_DEVICE void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+AHB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+AHB_DEVICE void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+AHB_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // 3-D TMA tile load (no multicast)
 AHB_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(

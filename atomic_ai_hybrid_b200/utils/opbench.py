@@ -40,7 +40,55 @@ def _timeit(fn, warmup: int, iters: int, flush: torch.Tensor) -> float:
     return times[len(times) // 2]
 
 
-def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd"):
+# per-phase cycle counters of the scan kernels (csrc/phase_prof.cuh): slot base, phase names; names
+# starting with "@" are per-warp arrival times, not phases of the sum
+_PHASES = {
+    "ssd_chunk_fwd_tc": (0, ["setup", "load wait", "cumsum + V", "CB out", "y_diag blocks", "MMA wait", "YD rows",
+                             "diagonal blocks", "rows out"]),
+    "ssd_chunk_bwd_tc": (16, ["setup + CB", "head loads", "cumsum", "phase-1 tiles", "dCB blocks", "MMA wait",
+                              "dCB readout", "ddd blocks", "diagonal ddd", "MMA wait", "pass 1", "pass 2",
+                              "row stores", "dC / dB"]),
+    "gdn_chunk_fwd_tc": (64, ["setup + g", "cumsum", "rows + score MMAs", "score wait", "scores out",
+                              "inverse + w v tile", "sync + A image", "w~ / u MMA", "w~ / u out", "bk tile",
+                              "@warp 0 at inverse sync", "@warp 1 at inverse sync", "@warp 2 at inverse sync",
+                              "@warp 3 at inverse sync"]),
+    "gdn_chunk_bwd_tc": (80, ["loads", "state products", "WV / dw~ / Gqk out", "WY wait", "dA out", "dv / dw",
+                              "T, A^T T", "Gkk out", "intra blocks", "intra wait", "plain tiles", "assembly"]),
+    # summed over the chunk steps; "load wait" (thread 0 waiting for the tiles) precedes the first MMA
+    "gdn_state_fwd_tc": (96, ["h out", "V, O1 MMA", "v_new out", "O2, HH MMA", "o out", "h update",
+                              "load wait"]),
+    "gdn_state_bwd_tc": (112, ["dh out", "DVN, D1 MMA", "dv_new out", "D2 MMA", "-", "dh update", "load wait"]),
+}
+
+
+def _phase_report(fn, prefix):
+    """One call of ``fn`` with the scan kernels' phase counters on: mean SM cycles per CTA of
+    every phase of the kernels whose name starts with ``prefix``."""
+    from ..ops._ext import ext
+    cnt = torch.zeros(128, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    ext().phase_prof(cnt)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ext().phase_prof(None)
+    c = cnt.cpu().tolist()
+    out = {}
+    for name, (base, phases) in _PHASES.items():
+        if not name.startswith(prefix):
+            continue
+        ctas = c[base + 15]
+        if not ctas:
+            continue
+        cyc = [c[base + i] / ctas for i in range(len(phases))]
+        tot = sum(v for p, v in zip(phases, cyc) if not p.startswith("@"))
+        out[name] = {"ctas": ctas, "cycles_per_cta": round(tot),
+                     "phases": {p: [round(v), round(v / tot, 3)] for p, v in zip(phases, cyc)}}
+    return out
+
+
+def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
     from ..ops import kernels as K
     from ..ops.reference import flops_gdn_chunked
     D = 128
@@ -62,11 +110,14 @@ def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd"):
     ms = _timeit(run, warmup, iters, flush)
     fl = flops_gdn_chunked(B, T, H, D, 64) * (3 if mode == "fwdbwd" else 1)
     io_bytes = B * T * H * D * (2 * 5 + 4) * (3 if mode == "fwdbwd" else 1)
-    return {"op": "gdn2", "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9,
-            "min_io_gb_s": io_bytes / ms / 1e6}
+    r = {"op": "gdn2", "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9,
+         "min_io_gb_s": io_bytes / ms / 1e6}
+    if phases:
+        r["phases"] = _phase_report(run, "gdn")
+    return r
 
 
-def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd"):
+def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
     from ..ops import kernels as K
     from ..ops.reference import flops_ssd_chunked
     P, N = 64, 128
@@ -87,8 +138,11 @@ def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd"):
     ms = _timeit(run, warmup, iters, flush)
     fl = flops_ssd_chunked(B, T, H, P, N, 64) * (3 if mode == "fwdbwd" else 1)
     io_bytes = (B * T * H * P * 2 * 3 + B * T * N * 2 * 2) * (3 if mode == "fwdbwd" else 1)
-    return {"op": "ssd", "mode": mode, "B": B, "T": T, "H": H, "P": P, "N": N, "ms": ms, "tflops": fl / ms / 1e9,
-            "min_io_gb_s": io_bytes / ms / 1e6}
+    r = {"op": "ssd", "mode": mode, "B": B, "T": T, "H": H, "P": P, "N": N, "ms": ms, "tflops": fl / ms / 1e9,
+         "min_io_gb_s": io_bytes / ms / 1e6}
+    if phases:
+        r["phases"] = _phase_report(run, "ssd")
+    return r
 
 
 def bench_moe(T, d, F_, E, k, warmup, iters, flush, mode="fwdbwd"):
@@ -262,15 +316,17 @@ def main(argv=None):
     ap.add_argument("--H", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--phases", action="store_true",
+                    help="gdn / ssd: also report the scan kernels' per-phase cycles (one extra call)")
     a = ap.parse_args(argv)
     from .. import ops
     ops.set_impl("cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
     torch.manual_seed(0)
     if a.op == "gdn":
-        r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode)
+        r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode, a.phases)
     elif a.op == "ssd":
-        r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode)
+        r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode, a.phases)
     elif a.op == "moe":
         r = bench_moe(a.B * a.T, 2048, 1024, 32, 4, a.warmup, a.iters, flush, a.mode)
     elif a.op == "router":
