@@ -54,7 +54,9 @@ struct SeqIdx {
 // shared memory: R1 (32 KB) stacked score rows, later A fp32, later (bk e^gc | w v) tiles;
 //                R2 (32 KB) key operands (two buffers), later Akk fp32 and the A tile; GC (32 KB)
 constexpr int F1_THREADS = 128;
-constexpr int F1_LDA = C + 4;  // fp32 row stride of Akk: 16-byte rows, row starts spread over the banks
+// fp32 Akk [64][64] with its 16-byte column groups XOR-swizzled by the row: the writers (one row per
+// lane, same group) spread over the banks, the readers (whole warp, one row) get a broadcast
+AHB_DEVICE int akk_at(int i, int j4) { return i * C + ((j4 ^ (i & 15)) << 2); }
 constexpr size_t F1_SMEM = 1024 + 3 * 32768 + 256;
 
 __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   pc.mark(3);
 
   // 4. scores out of TMEM: lane m of quarter q is row m = 32 q + lane of the stack
-  float* AKK = reinterpret_cast<float*>(R2);  // fp32 [64][F1_LDA]
+  float* AKK = reinterpret_cast<float*>(R2);  // fp32 [64][64], akk_at
   {
     const int m = 32 * warp + lane;
     const bool is_q = m < C;
@@ -247,18 +249,22 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       const bool keep = is_q ? (j <= i) : (j < i);
       row[j] = keep ? guard(is_q ? row[j] * scale : row[j]) : 0.f;
     }
-    if (is_q) {
-      unsigned char* aqk_c = aqk_t + cb * TILE_CC;
+    if (is_q) {  // the Aqk tile image, staged for one bulk store (per-lane row stores stall the warps)
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(aqk_c + sw_off16(C, i, c)) = pack8(row + c);
+      for (int c = 0; c < 64; c += 8) *reinterpret_cast<uint4*>(R2 + 16384 + sw_off16(C, i, c)) = pack8(row + c);
+      fence_async_smem();
     } else {
 #pragma unroll
       for (int j = 0; j < 64; j += 4)
-        *reinterpret_cast<float4*>(AKK + i * F1_LDA + j) = make_float4(row[j], row[j + 1], row[j + 2], row[j + 3]);
+        *reinterpret_cast<float4*>(AKK + akk_at(i, j >> 2)) = make_float4(row[j], row[j + 1], row[j + 2], row[j + 3]);
     }
   }
   sm100::tc_fence_before();
   __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(aqk_t + cb * TILE_CC, R2 + 16384, TILE_CC);
+    bulk_commit();
+  }
   pc.mark(4);
   const long long t_after4 = clock64();
   if (flags[4]) goto teardown;
@@ -278,27 +284,25 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
           const int i = 16 * B + r;
-          const float* Li = AKK + i * F1_LDA + 16 * B;
           float s0 = B == 0 ? (i == c ? 1.f : 0.f) : ACC[i * C + c], s1 = 0.f;
 #pragma unroll
           for (int j = 0; j + 3 < r; j += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(Li + j);
+            const float4 l4 = *reinterpret_cast<const float4*>(AKK + akk_at(i, 4 * B + (j >> 2)));
             s0 -= l4.x * x[j] + l4.z * x[j + 2];
             s1 -= l4.y * x[j + 1] + l4.w * x[j + 3];
           }
 #pragma unroll
-          for (int j = r & ~3; j < r; ++j) s0 -= Li[j] * x[j];
+          for (int j = r & ~3; j < r; ++j) s0 -= AKK[akk_at(i, 4 * B + (j >> 2)) + (j & 3)] * x[j];
           const float v_ = s0 + s1;
           x[r] = B != (c >> 4) ? guard(v_) : v_;
           *reinterpret_cast<bf16*>(AT + sw_off(C, i, c)) = __float2bfloat16_rn(x[r]);
         }
 #pragma unroll 2
         for (int i = 16 * B + 16; i < C; ++i) {
-          const float4* Li = reinterpret_cast<const float4*>(AKK + i * F1_LDA + 16 * B);
           float s0 = 0.f, s1 = 0.f;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const float4 l4 = Li[q];
+            const float4 l4 = *reinterpret_cast<const float4*>(AKK + akk_at(i, 4 * B + q));
             s0 += l4.x * x[4 * q] + l4.z * x[4 * q + 2];
             s1 += l4.y * x[4 * q + 1] + l4.w * x[4 * q + 3];
           }
@@ -371,15 +375,14 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     if (!wait_bar(bars + 4, 0, err, 0x4704)) goto teardown;
     sm100::tc_fence_after();
     pc.mark(7);
-    // 8. rows i = 16 warp + (lane & 15) of w~ and u out as tile images: lanes 0-15 hold the rows
-    //    (M = 64), lanes 16-31 take the upper 16 columns of each 32-column load by shuffle
+    // 8. rows i = 16 warp + (lane & 15) of w~ and u as tile images: lanes 0-15 hold the rows
+    //    (M = 64), lanes 16-31 take the upper 16 columns of each 32-column load by shuffle; staged
+    //    over the dead operands in R1, then two bulk stores
     {
       const int i = 16 * warp + (lane & 15), hf = lane >> 4;
-      unsigned char* wt_c = wt_t + cb * TILE_CD;
-      unsigned char* u_c = u_t + cb * TILE_CD;
 #pragma unroll 1
       for (int p = 0; p < 8; ++p) {
-        unsigned char* dst = p < 4 ? wt_c : u_c;
+        unsigned char* dst = R1 + (p < 4 ? 0 : TILE_CD);
         const int col = 32 * (p & 3) + 16 * hf;
         float x[32], y[16];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
@@ -392,8 +395,16 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
         *reinterpret_cast<uint4*>(dst + sw_off16(C, i, col + 8)) = pack8(y + 8);
       }
     }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      bulk_s2g(wt_t + cb * TILE_CD, R1, TILE_CD);
+      bulk_s2g(u_t + cb * TILE_CD, R1 + TILE_CD, TILE_CD);
+      bulk_commit();
+    }
   }
 teardown:
+  if (tid == 0) bulk_wait_all();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -416,7 +427,8 @@ constexpr int F2_STAGE = 4 * TILE_CD + TILE_CC;  // w~, qg, kg, Aqk tile images,
 constexpr int F2_U = 3 * TILE_CD + TILE_CC;       // offset of u inside a stage
 constexpr int F2_H = 2 * F2_STAGE;                // state tile (rows dk, columns dv), 32 KB
 constexpr int F2_VN = F2_H + 2 * TILE_CD;         // v_new tile (rows i, columns dv), 16 KB
-constexpr int F2_BARS = F2_VN + TILE_CD;
+constexpr int F2_O = F2_VN + TILE_CD;            // o rows (two 64-column swizzled boxes), 16 KB
+constexpr int F2_BARS = F2_O + TILE_CD;
 constexpr size_t F2_SMEM = 1024 + F2_BARS + 256;
 
 // NH = 2: the value columns split over two CTAs per (batch, head) (blockIdx.z = half; the columns of
@@ -424,7 +436,7 @@ constexpr size_t F2_SMEM = 1024 + F2_BARS + 256;
 // the SMs; each CTA keeps 64 columns and writes its slab of the per-chunk images.
 template <int NH>
 __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
-    const unsigned char* __restrict__ wt_t, const unsigned char* __restrict__ u_t,
+    const __grid_constant__ CUtensorMap tm_o, const unsigned char* __restrict__ wt_t, const unsigned char* __restrict__ u_t,
     const unsigned char* __restrict__ qg_t, const unsigned char* __restrict__ kg_t,
     const unsigned char* __restrict__ aqk_t, const float* __restrict__ gcl, float scale, int L, int H, int NC,
     const float* __restrict__ h0, bf16* __restrict__ o, float* __restrict__ h_final, unsigned char* __restrict__ h_store,
@@ -533,6 +545,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     pc.mark(2);
     if (*abort_flag) break;
     if (tid == 0) {
+      if (o) bulk_wait_read();  // the previous chunk's o box is read before the epilogue below rewrites it
       if (vn_store) {
         bulk_s2g(vn_store + cbn * TILE_CD + (v0 >> 6) * (C * 128), smem + F2_VN, DV * C * 2);
         bulk_commit();
@@ -546,9 +559,8 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     if (!wait_bar(bars + 3, n & 1, err, 0x4713)) *abort_flag = 1;
     sm100::tc_fence_after();
     pc.mark(3);
-    if (o) {
+    if (o) {  // o rows into the swizzled boxes; stored by TMA after the chunk's last barrier
       const int i = 16 * warp + lane;
-      bf16* orow = o + ix.row(b, (int64_t)n * C + i, h);
 #pragma unroll 1
       for (int p = 0; p < DV / 32; ++p) {
         float x1[32], x2[32];
@@ -560,9 +572,10 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
             float y[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = guard(scale * x1[c + e] + x2[c + e]);
-            *reinterpret_cast<uint4*>(orow + v0 + 32 * p + c) = pack8(y);
+            *reinterpret_cast<uint4*>(smem + F2_O + sw_off16(C, i, 32 * p + c)) = pack8(y);
           }
       }
+      fence_async_smem();
     }
     pc.mark(4);
     {
@@ -579,6 +592,12 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     sm100::tc_fence_before();
     __syncthreads();
     pc.mark(5);
+    if (tid == 0 && o) {
+#pragma unroll
+      for (int hb = 0; hb < DV / 64; ++hb)
+        tma_store_3d(&tm_o, smem + F2_O + hb * (C * 128), v0 + 64 * hb, h, b * L + n * C);
+      bulk_commit();
+    }
     if (*abort_flag) break;
     if (tid == 0 && n + 2 < NC) issue(n + 2);
   }
@@ -1302,9 +1321,12 @@ int ahb_gdn_state_fwd_tc(const void* wt_t, const void* u_t, const void* qg_t, co
   static int init = set_smem(gdn_state_fwd_tc<1>, F2_SMEM) | set_smem(gdn_state_fwd_tc<2>, F2_SMEM);
   if (init) return init;
   const bool split = gdn_state_split(B, H);
+  CUtensorMap tmo;
+  memset(&tmo, 0, sizeof(tmo));
+  if (o && tmap_seq_bf16(&tmo, o, (int64_t)B * L, H, D, C)) return -20;
   auto k = split ? gdn_state_fwd_tc<2> : gdn_state_fwd_tc<1>;
   k<<<dim3(H, B, split ? 2 : 1), F2_THREADS, F2_SMEM, st>>>(
-      (const unsigned char*)wt_t, (const unsigned char*)u_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
+      tmo, (const unsigned char*)wt_t, (const unsigned char*)u_t, (const unsigned char*)qg_t, (const unsigned char*)kg_t,
       (const unsigned char*)aqk_t, gcl, scale, L, H, L / C, h0, (bf16*)o, h_final, (unsigned char*)h_store,
       (unsigned char*)vn_store, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;

@@ -122,6 +122,14 @@ AHB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "
 AHB_DEVICE void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 AHB_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 3-D TMA tile store from a swizzled shared-memory box (coordinates non-negative), in the issuing
+// thread's bulk group
+AHB_DEVICE void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 // 3-D TMA tile load (no multicast)
 AHB_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
