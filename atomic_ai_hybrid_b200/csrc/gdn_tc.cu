@@ -147,9 +147,10 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     unpack8(qa[it], qv);
     unpack8(ka[it], kv);
     unpack8(ba[it], bv);
-    const float* gci = GC + i * D + c;
-    const float* gcr = GC + (i & ~15) * D + c;
-    const float* gcl = GC + (C - 1) * D + c;
+    float gci[8], gcr[8], gcl[8];
+    ld8f_x(GC + i * D + c, gci);
+    ld8f_x(GC + (i & ~15) * D + c, gcr);
+    ld8f_x(GC + (C - 1) * D + c, gcl);
     float a[8], bk[8], qg[8], kg[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -181,10 +182,12 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       const int j = u_ >> 4, c = (u_ & 15) << 3;
       float kv[8], o[8];
       unpack8(ka[it], kv);
-      const float* gcj = GC + j * D + c;
+      float gcj[8], gr8[8];
+      ld8f_x(GC + j * D + c, gcj);
+      ld8f_x(gcr + c, gr8);
       const bool zero = exact && j >= 16 * I;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gcr[c + e] - gcj[e]);
+      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gr8[e] - gcj[e]);
       st_chunk8(smem_u32(buf) + sw_off16(C, j, c), o);
     }
     fence_async_smem();
@@ -347,7 +350,8 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
       float kv[8], bv[8], x[8];
       unpack8(ka[it], kv);
       unpack8(ba[it], bv);
-      const float* gci = GC + i * D + c;
+      float gci[8];
+      ld8f_x(GC + i * D + c, gci);
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[e] = bv[e] * kv[e] * __expf(gci[e]);
       st_chunk8(sR1 + sw_off16(C, i, c), x);
@@ -1001,7 +1005,8 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     unpack8(ba[it], bv);
     unpack8(wa[it], wv);
     unpack8(va[it], vv);
-    const float* gci = GC + i * D + c;
+    float gci[8];
+    ld8f_x(GC + i * D + c, gci);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       x[e] = wv[e] * vv[e];
@@ -1123,8 +1128,11 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
       float kv[8], o[8];
       unpack8(ka[it], kv);
       const bool zero = exact && j >= 16 * I;
+      float gcj[8], gr8[8];
+      ld8f_x(GC + j * D + c, gcj);
+      ld8f_x(gcr + c, gr8);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gcr[c + e] - GC[j * D + c + e]);
+      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gr8[e] - gcj[e]);
       st_chunk8(buf + sw_off16(16 * (I + 1), j, c), o);
     }
   }
@@ -1167,9 +1175,12 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
         unpack8(ka[it], kv);
         unpack8(ba[it], bv);
         const bool zero = exact && i < 16 * J + 16;
+        float gci[8], gr8[8];
+        ld8f_x(GC + i * D + c, gci);
+        ld8f_x(gcr + c, gr8);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float er = zero ? 0.f : __expf(GC[i * D + c + e] - gcr[c + e]);
+          const float er = zero ? 0.f : __expf(gci[e] - gr8[e]);
           xq[e] = scale * qv[e] * er;
           xk[e] = bv[e] * kv[e] * er;
         }

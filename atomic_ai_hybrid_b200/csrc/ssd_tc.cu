@@ -42,11 +42,6 @@ constexpr int T_CN = C * N * 2;   // 64 x 128 bf16 tile (16 KB)
 constexpr int T_NP = N * P * 2;   // 128 x 64 bf16 tile (16 KB)
 
 AHB_DEVICE float clip4(float x) { return sanitize(x, 1e4f); }
-// 8 consecutive fp32 of a shared-memory row (two 16-byte loads)
-AHB_DEVICE void ld8f(const float* src, float* o) {
-  const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
-  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
-}
 
 // Decay cumsum of the chunk for 256 threads: CUM[i][p] = clamp(sum_{i' <= i} clamp(dt[i'][p] A, +-20),
 // +-1e4), four threads per channel p (rows [16 k, 16 k + 16) for k = tid >> 6), the block totals of
@@ -134,8 +129,8 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
     float cj[8], cl8[8];
-    ld8f(CUM + j * P + c, cj);
-    ld8f(CUM + (C - 1) * P + c, cl8);
+    ld8f_x(CUM + j * P + c, cj);
+    ld8f_x(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - cj[e], -20.f));
     st_chunk8(S + S1_V + sw_off16(C, j, c), o);
@@ -190,8 +185,8 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
     float cj[8], cr8[8];
-    ld8f(CUM + j * P + c, cj);
-    ld8f(CUM + 16 * I * P + c, cr8);
+    ld8f_x(CUM + j * P + c, cj);
+    ld8f_x(CUM + 16 * I * P + c, cr8);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       o[e] = clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
@@ -320,7 +315,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       const int u_ = it * S1_THREADS + tid;
       const int i = u_ >> 3, c = (u_ & 7) << 3;
       float o[8], ci[8];
-      ld8f(CUM + i * P + c, ci);
+      ld8f_x(CUM + i * P + c, ci);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = __expf(fmaxf(ci[e], -20.f));
       *reinterpret_cast<uint4*>(dec_t + ch * T_CP + sw_off16(C, i, c)) = pack8(o);
@@ -745,9 +740,9 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, i, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, i, c)), dv);
       float c8[8], cr8[8], cl8[8];
-      ld8f(CUM + i * P + c, c8);
-      ld8f(CUM + (i & ~15) * P + c, cr8);
-      ld8f(CUM + (C - 1) * P + c, cl8);
+      ld8f_x(CUM + i * P + c, c8);
+      ld8f_x(CUM + (i & ~15) * P + c, cr8);
+      ld8f_x(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         r8[e] = dy[e] * __expf(c8[e] - cr8[e]);
@@ -786,8 +781,8 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
       const bool zero = flags[I] && j >= 16 * I;
       float cj[8], cr8[8];
-      ld8f(CUM + j * P + c, cj);
-      ld8f(CUM + 16 * I * P + c, cr8);
+      ld8f_x(CUM + j * P + c, cj);
+      ld8f_x(CUM + 16 * I * P + c, cr8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
       st_chunk8(S + dcb_buf(I) + sw_off16(C, j, c), o);
@@ -855,8 +850,8 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       float dy[8], o[8], lo[8];
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
       float ci[8], cs8[8];
-      ld8f(CUM + i * P + c, ci);
-      ld8f(CUM + (16 * J + 15) * P + c, cs8);
+      ld8f_x(CUM + i * P + c, ci);
+      ld8f_x(CUM + (16 * J + 15) * P + c, cs8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         o[e] = dy[e] * __expf(ci[e] - cs8[e]);

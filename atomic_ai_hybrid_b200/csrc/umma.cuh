@@ -44,6 +44,17 @@ AHB_DEVICE uint64_t mndesc(uint32_t base, int Krows, int s) {
   return sm100::smem_desc(base + (uint32_t)(s * 2048), (uint32_t)(Krows * 128), 1024);
 }
 
+// 8 consecutive fp32 of a shared-memory row as two 16-byte loads, the halves in swapped order on
+// lanes with bit 2 set: where 8 or 16 lanes read consecutive 32-byte pieces of a row, each load then
+// meets every bank group once per row instead of half of them twice
+AHB_DEVICE void ld8f_x(const float* src, float* o) {
+  const int sw = (threadIdx.x >> 2) & 1;
+  const float4 a = *reinterpret_cast<const float4*>(src + 4 * sw);
+  const float4 b = *reinterpret_cast<const float4*>(src + 4 - 4 * sw);
+  const float4 lo = sw ? b : a, hi = sw ? a : b;
+  o[0] = lo.x; o[1] = lo.y; o[2] = lo.z; o[3] = lo.w; o[4] = hi.x; o[5] = hi.y; o[6] = hi.z; o[7] = hi.w;
+}
+
 AHB_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 AHB_DEVICE uint32_t pack_bf2(float a, float b) {
