@@ -105,8 +105,9 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
 #pragma unroll
   for (int e = tid; e < C * (D / 4); e += F1_THREADS) {
     const int r = e >> 5, c4 = (e & 31) << 2;
-    *reinterpret_cast<float4*>(GC + r * D + c4) = *reinterpret_cast<const float4*>(g + ix.row(b, t0 + r, h) + c4);
+    cp_async16(GC + r * D + c4, g + ix.row(b, t0 + r, h) + c4);  // no registers held for the gate rows
   }
+  cp_async_wait_all();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -272,33 +273,53 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
   const long long t_after4 = clock64();
   if (flags[4]) goto teardown;
   {
-    // 5. A = (I + Akk)^-1 in fp32 by forward substitution, one column c per thread (threads 0-63), in
-    //    16-row blocks: the block's x_i = acc_i - sum_{j in block, j < i} Akk_ij x_j (registers),
-    //    then acc_i -= sum_{j in block} Akk_ij x_j for the rows below (fp32 [i][c] in the first half
-    //    of R1, acc_i = [i == c] before any update).  Akk rows are read as broadcast 16-byte vectors;
-    //    entries outside the diagonal 16 x 16 blocks are guarded.
+    // 5. A = (I + Akk)^-1 in fp32 by blocked forward substitution.
+    //    (a) warp w inverts the diagonal 16 x 16 block w of (I + Akk) by substitution (lane j =
+    //        column j) into DI, rows 0-15 of the accumulator region (never read as accumulators);
+    //    (b) one column c per thread (threads 0-63), block by block: the block's x = DI_B acc_B
+    //        (independent dot products, no chain over the rows), then acc_i -= sum_{j in block}
+    //        Akk_ij x_j for the rows below (fp32 [i][c] in the first half of R1, acc_i = [i == c]
+    //        before any update).  Entries outside the diagonal blocks are guarded.
     unsigned char* AT = R2 + 24576;
+    float* ACC = reinterpret_cast<float*>(R1);  // [i][c]
+    float* DI = ACC;                            // [w][r][j], 4 x 16 x 16
+    if (lane < 16) {
+      const int j = lane, w = warp;
+      float y[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int i = 16 * w + r;
+        float s = r == j ? 1.f : 0.f;
+#pragma unroll
+        for (int k = 0; k < r; ++k) s -= AKK[akk_at(i, 4 * w + (k >> 2)) + (k & 3)] * y[k];
+        y[r] = r < j ? 0.f : s;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) DI[(16 * w + r) * 16 + j] = y[r];
+    }
+    __syncthreads();
     if (tid < C) {
       const int c = tid;
-      float* ACC = reinterpret_cast<float*>(R1);  // [i][c]
 #pragma unroll 1
       for (int B = 0; B < 4; ++B) {
-        float x[16];
+        float a[16], x[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) a[r] = B == 0 ? (r == c ? 1.f : 0.f) : ACC[(16 * B + r) * C + c];
+        const float* Dw = DI + 256 * B;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-          const int i = 16 * B + r;
-          float s0 = B == 0 ? (i == c ? 1.f : 0.f) : ACC[i * C + c], s1 = 0.f;
+          float s0 = a[r], s1 = 0.f;
 #pragma unroll
-          for (int j = 0; j + 3 < r; j += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(AKK + akk_at(i, 4 * B + (j >> 2)));
-            s0 -= l4.x * x[j] + l4.z * x[j + 2];
-            s1 -= l4.y * x[j + 1] + l4.w * x[j + 3];
+          for (int k = 0; k + 3 < r; k += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(Dw + 16 * r + k);
+            s0 += d4.x * a[k] + d4.z * a[k + 2];
+            s1 += d4.y * a[k + 1] + d4.w * a[k + 3];
           }
 #pragma unroll
-          for (int j = r & ~3; j < r; ++j) s0 -= AKK[akk_at(i, 4 * B + (j >> 2)) + (j & 3)] * x[j];
+          for (int k = r & ~3; k < r; ++k) s0 += Dw[16 * r + k] * a[k];
           const float v_ = s0 + s1;
           x[r] = B != (c >> 4) ? guard(v_) : v_;
-          *reinterpret_cast<bf16*>(AT + sw_off(C, i, c)) = __float2bfloat16_rn(x[r]);
+          *reinterpret_cast<bf16*>(AT + sw_off(C, 16 * B + r, c)) = __float2bfloat16_rn(x[r]);
         }
 #pragma unroll 2
         for (int i = 16 * B + 16; i < C; ++i) {
@@ -943,8 +964,9 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
 #pragma unroll
   for (int e = tid; e < C * (D / 4); e += BC_THREADS) {
     const int r = e >> 5, c4 = (e & 31) << 2;
-    *reinterpret_cast<float4*>(GC + r * D + c4) = *reinterpret_cast<const float4*>(g + ix.row(b, t0 + r, h) + c4);
+    cp_async16(GC + r * D + c4, g + ix.row(b, t0 + r, h) + c4);  // no registers held for the gate rows
   }
+  cp_async_wait_all();
   __syncthreads();
   if (!wait_bar(bars, 0, err, 0x4731)) flags[4] = 1;
   pc.mark(0);

@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     // S_end^T rows (lane = state row s) -> tile image (rows s, columns p); warpgroup wg takes
     // columns [32 wg, 32 wg + 32)
     const int s = 32 * quarter + lane;
-    unsigned char* dst = send_t + ch * T_NP;
+    unsigned char* dst = smem + S1_C;  // staged over the dead C tile for one bulk store
     {
       const int half = wg;
       float x[32];
@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
         for (int e = 0; e < 8; ++e) y[e] = clip4(x[c + e]);
         *reinterpret_cast<uint4*>(dst + sw_off16(N, s, 32 * half + c)) = pack8(y);
       }
+      fence_async_smem();
     }
     // y_diag^T row p (lanes 0-15 of each quarter): the off-diagonal blocks from TMEM as fp32 rows
     // into the dead W buffers; then the diagonal 16 x 16 blocks summed exactly per channel (fp32,
@@ -252,6 +253,10 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       for (int e = 0; e < 16; ++e) YD[(i0 + e) * P + p] = y[e] * __expf(CUM[(i0 + e) * P + p] - cr);
     }
     __syncthreads();
+    if (tid == 0) {
+      bulk_s2g(send_t + ch * T_NP, smem + S1_C, T_NP);
+      bulk_commit();
+    }
     pc.mark(6);
     {
       // four threads per channel p, one block each: y[i] += e^{c_i - c_r} sum_{j<=i} CB[i][j] (dBx_j e^{c_r - c_j})
@@ -322,6 +327,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
     }
   }
 s1_teardown:
+  if (tid == 0) bulk_wait_all();
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -354,6 +360,7 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S2_BAR);  // full[2], mma
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  PhaseClock pc(32);
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t bh = (int64_t)b * H + h;
@@ -396,12 +403,16 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
 #pragma unroll
     for (int p = 0; p < P; p += 8) {
       st_chunk8(Sb + S2_S + sw_off16(N, s, p), S + p);
-      if (sin_t) *reinterpret_cast<uint4*>(sin_t + c * T_NP + sw_off16(N, s, p)) = pack8(S + p);
     }
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(0);
     if (tid == 0) {
+      if (sin_t) {  // the chunk's start state image, one bulk store of the operand tile
+        bulk_s2g(sin_t + c * T_NP, smem + S2_S, T_NP);
+        bulk_commit();
+      }
       if (!wait_bar(bars + st, (n >> 1) & 1, err, 0x5311)) *abort_flag = 1;
       sm100::tc_fence_after();
       if (!*abort_flag)
@@ -427,8 +438,10 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
         for (int e = 0; e < 8; ++e) S[p + e] = clip4(S[p + e] * __expf(fmaxf(clp[p + e], -20.f)) + e8[e]);
       }
     }
+    pc.mark(1);
     if (!wait_bar(bars + 2, n & 1, err, 0x5313)) *abort_flag = 1;
     sm100::tc_fence_after();
+    pc.mark(2);
     {
       float yo[64];
       tmem_ld32(tmem_at(tmem, warp, 0), yo);
@@ -443,8 +456,10 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
         }
       }
     }
+    if (tid == 0) bulk_wait_read();  // the state tile is rewritten in the next step
     sm100::tc_fence_before();
     __syncthreads();
+    pc.mark(3);
     if (*abort_flag) break;
     if (tid == 0 && n + 2 < NC) issue(n + 2);
 #pragma unroll
@@ -458,6 +473,7 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
   if (s_final && n == NC)
 #pragma unroll
     for (int p = 0; p < P; ++p) s_final[(bh * P + p) * N + s] = S[p];
+  if (tid == 0) bulk_wait_all();
   if (*abort_flag && tid == 0) {
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -466,6 +482,7 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
   __syncthreads();
   sm100::tc_fence_after();
   if (warp == 0) sm100::tmem_dealloc(tmem, 64);
+  pc.done();
 }
 
 // ============================================================ state recurrence, backward
@@ -477,7 +494,8 @@ constexpr int B1S_THREADS = 128;
 constexpr int B1S_STAGE = T_CN + 2 * T_CP;  // C tile, dy tile, decay image
 constexpr int B1S_CL = 2 * B1S_STAGE;
 constexpr int B1S_DYD = B1S_CL + 1024;
-constexpr int B1S_BAR = B1S_DYD + T_CP;
+constexpr int B1S_G = B1S_DYD + T_CP;  // state-gradient image (rows s, columns p) for the bulk store
+constexpr int B1S_BAR = B1S_G + T_NP;
 constexpr size_t B1S_SMEM = 1024 + B1S_BAR + 256;
 
 __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
@@ -533,7 +551,7 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
     const uint32_t sp = Sb + st * B1S_STAGE;
 #pragma unroll
     for (int p = 0; p < P; p += 8)
-      *reinterpret_cast<uint4*>(dse_t + c * T_NP + sw_off16(N, s, p)) = pack8(G + p);
+      st_chunk8(Sb + B1S_G + sw_off16(N, s, p), G + p);
     if (!wait_bar(bars + st, (it >> 1) & 1, err, 0x5321)) *abort_flag = 1;
 #pragma unroll
     for (int k8 = 0; k8 < (C * P / 8) / B1S_THREADS; ++k8) {
@@ -551,6 +569,8 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
     __syncthreads();
     if (*abort_flag) break;
     if (tid == 0) {
+      bulk_s2g(dse_t + c * T_NP, smem + B1S_G, T_NP);
+      bulk_commit();
       sm100::tc_fence_after();
       mma_steps(tmem, [&](int k) { return mndesc(sp, C, k); }, [&](int k) { return mndesc(Sb + B1S_DYD, C, k); }, C / 16,
                 sm100::idesc_bf16(128, 64, true, true), false);
@@ -571,6 +591,7 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
         }
       }
     }
+    if (tid == 0) bulk_wait_read();  // the gradient image is rewritten in the next step
     sm100::tc_fence_before();
     __syncthreads();
     if (*abort_flag) break;
@@ -579,6 +600,7 @@ __global__ void __launch_bounds__(B1S_THREADS, 1) ssd_state_bwd_tc(
   if (ds0 && it == NC)
 #pragma unroll
     for (int p = 0; p < P; ++p) ds0[(bh * P + p) * N + s] = G[p];
+  if (tid == 0) bulk_wait_all();
   if (*abort_flag && tid == 0) {
     const uint64_t t0 = sm100::globaltimer();
     while (sm100::globaltimer() - t0 < 2000000ull) {}
@@ -1138,6 +1160,9 @@ int ahb_ssd_fwd_tc(const void* x, const void* dt, const float* A, const void* Bm
 AHB_PHASE_PROF_SETTER(ahb_ssd_phase_prof)
 
 int ahb_ssd_head_groups(int H) {
+  // eight heads per CTA where there are 32 or more: the chunk's B / C tiles, C B^T and the dB / dC
+  // epilogue are shared by more heads and there are fewer partial sums to add
+  if (H >= 32 && H % 8 == 0) return H / 8;
   for (int g : {8, 4, 2}) if (H % g == 0) return g;
   return 1;
 }

@@ -55,6 +55,13 @@ AHB_DEVICE void ld8f_x(const float* src, float* o) {
   o[0] = lo.x; o[1] = lo.y; o[2] = lo.z; o[3] = lo.w; o[4] = hi.x; o[5] = hi.y; o[6] = hi.z; o[7] = hi.w;
 }
 
+// 16-byte asynchronous copy global -> shared that holds no registers; cp_async_wait_all waits for
+// this thread's copies
+AHB_DEVICE void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+AHB_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 AHB_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 AHB_DEVICE uint32_t pack_bf2(float a, float b) {

@@ -48,6 +48,9 @@ _PHASES = {
     "ssd_chunk_bwd_tc": (16, ["setup + CB", "head loads", "cumsum", "phase-1 tiles", "dCB blocks", "MMA wait",
                               "dCB readout", "ddd blocks", "diagonal ddd", "MMA wait", "pass 1", "pass 2",
                               "row stores", "dC / dB"]),
+    # summed over the chunk steps
+    "ssd_state_fwd_tc": (32, ["S out + previous y rows", "yd loads + state carry", "y_off MMA wait",
+                              "y epilogue"]),
     "gdn_chunk_fwd_tc": (64, ["setup + g", "cumsum", "rows + score MMAs", "score wait", "scores out",
                               "inverse + w v tile", "sync + A image", "w~ / u MMA", "w~ / u out", "bk tile",
                               "@warp 0 at inverse sync", "@warp 1 at inverse sync", "@warp 2 at inverse sync",
