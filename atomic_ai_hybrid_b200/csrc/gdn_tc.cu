@@ -544,24 +544,30 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     if (!wait_bar(bars + 2, n & 1, err, 0x4712)) *abort_flag = 1;
     sm100::tc_fence_after();
     pc.mark(1);
-    // v_new rows i = 16 warp + lane (lanes 0-15)
+    // v_new rows i = 16 warp + (lane & 15) (M = 64: lanes 0-15 hold them); lanes 16-31 take the
+    // upper 16 columns of each 32-column load by shuffle
     {
-      const int i = 16 * warp + lane;
+      const int i = 16 * warp + (lane & 15), hf = lane >> 4;
       const unsigned char* u_c = smem + (n & 1) * F2_STAGE + F2_U;  // this CTA's columns
       if (!wait_bar(bars + (n & 1), (n >> 1) & 1, err, 0x4714)) *abort_flag = 1;  // every thread reads u
 #pragma unroll 1
       for (int p = 0; p < DV / 32; ++p) {
-        float x[32];
+        float x[32], xs[16];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
-        if (lane < 16)
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float uu[8], y[8];
-            unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, 32 * p + c)), uu);
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+          xs[e] = hf ? sh : x[e];
+        }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = uu[e] - x[c + e];
-            st_chunk8(sVN + sw_off16(C, i, 32 * p + c), y);
-          }
+        for (int c = 0; c < 16; c += 8) {
+          const int col = 32 * p + 16 * hf + c;
+          float uu[8], y[8];
+          unpack8(*reinterpret_cast<const uint4*>(u_c + sw_off16(C, i, col)), uu);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] = uu[e] - xs[c + e];
+          st_chunk8(sVN + sw_off16(C, i, col), y);
+        }
       }
     }
     fence_async_smem();
@@ -584,21 +590,23 @@ __global__ void __launch_bounds__(F2_THREADS, 1) gdn_state_fwd_tc(
     if (!wait_bar(bars + 3, n & 1, err, 0x4713)) *abort_flag = 1;
     sm100::tc_fence_after();
     pc.mark(3);
-    if (o) {  // o rows into the swizzled boxes; stored by TMA after the chunk's last barrier
-      const int i = 16 * warp + lane;
+    if (o) {  // o rows into the swizzled boxes (all lanes, as v_new); stored by TMA after the chunk's last barrier
+      const int i = 16 * warp + (lane & 15), hf = lane >> 4;
 #pragma unroll 1
       for (int p = 0; p < DV / 32; ++p) {
-        float x1[32], x2[32];
+        float x1[32], x2[32], ys[16];
         tmem_ld32(tmem_at(tmem, warp, DV + 32 * p), x1);
         tmem_ld32(tmem_at(tmem, warp, 2 * DV + 32 * p), x2);
-        if (lane < 16)
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            float y[8];
+        for (int e = 0; e < 32; ++e) x1[e] = scale * x1[e] + x2[e];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = guard(scale * x1[c + e] + x2[c + e]);
-            *reinterpret_cast<uint4*>(smem + F2_O + sw_off16(C, i, 32 * p + c)) = pack8(y);
-          }
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, x1[16 + e], lane & 15);
+          ys[e] = guard(hf ? sh : x1[e]);
+        }
+#pragma unroll
+        for (int c = 0; c < 16; c += 8)
+          *reinterpret_cast<uint4*>(smem + F2_O + sw_off16(C, i, 32 * p + 16 * hf + c)) = pack8(ys + c);
       }
       fence_async_smem();
     }
@@ -746,17 +754,19 @@ __global__ void __launch_bounds__(B1_THREADS, 1) gdn_state_bwd_tc(
     if (!wait_bar(bars + 2, it & 1, err, 0x4722)) *abort_flag = 1;
     sm100::tc_fence_after();
     pc.mark(1);
-    {
-      const int i = 16 * warp + lane;
+    {  // dv_new rows i = 16 warp + (lane & 15); lanes 16-31 take the upper 16 columns by shuffle
+      const int i = 16 * warp + (lane & 15), hf = lane >> 4;
 #pragma unroll 1
       for (int p = 0; p < DV / 32; ++p) {
-        float x[32];
+        float x[32], xs[16];
         tmem_ld32(tmem_at(tmem, warp, 32 * p), x);
-        if (lane < 16)
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            st_chunk8(sDVN + sw_off16(C, i, 32 * p + c), x + c);
-          }
+        for (int e = 0; e < 16; ++e) {
+          const float sh = __shfl_sync(0xffffffffu, x[16 + e], lane & 15);
+          xs[e] = hf ? sh : x[e];
+        }
+#pragma unroll
+        for (int c = 0; c < 16; c += 8) st_chunk8(sDVN + sw_off16(C, i, 32 * p + 16 * hf + c), xs + c);
       }
     }
     fence_async_smem();

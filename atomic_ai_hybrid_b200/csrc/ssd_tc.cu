@@ -421,11 +421,12 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
       sm100::umma_commit(bars + 2);
     }
     // carry the state: S <- clip(S e^{max(cl, -20)} + S_end)   (S_end^T row s from the image)
-    const int p0 = 16 * warp + lane;  // channel of this lane in the y epilogue (lanes 0-15)
-    float ydr[C];
-    if (lane < 16)
+    // y epilogue: channel p0 = 16 warp + (lane & 15) (M = 64: lanes 0-15 hold it), rows [ih, ih + 32)
+    // per lane, lanes 16-31 taking rows 32-63 by shuffle
+    const int p0 = 16 * warp + (lane & 15), ih = 32 * (lane >> 4);
+    float ydr[32];
 #pragma unroll
-      for (int i = 0; i < C; ++i) ydr[i] = yd_t[c * (C * P) + i * P + p0];
+    for (int i = 0; i < 32; ++i) ydr[i] = yd_t[c * (C * P) + (ih + i) * P + p0];
     if (!wait_bar(bars + st, (n >> 1) & 1, err, 0x5312)) *abort_flag = 1;  // every thread reads the stage
     {
       const float* clp = reinterpret_cast<const float*>(smem + S2_CL + st * 256);
@@ -443,17 +444,21 @@ __global__ void __launch_bounds__(S2_THREADS, 1) ssd_state_fwd_tc(
     sm100::tc_fence_after();
     pc.mark(2);
     {
-      float yo[64];
+      float yo[64], z[32];
       tmem_ld32(tmem_at(tmem, warp, 0), yo);
       tmem_ld32(tmem_at(tmem, warp, 32), yo + 32);
-      if (lane < 16) {
-        const unsigned char* dec = smem + st * S2_STAGE + T_CN + T_NP;
-        bf16* Y = reinterpret_cast<bf16*>(smem + S2_Y);
 #pragma unroll
-        for (int i = 0; i < C; ++i) {
-          const float dh = __bfloat162float(*reinterpret_cast<const bf16*>(dec + sw_off(C, i, p0)));
-          Y[i * P + p0] = __float2bfloat16_rn(clip4(ydr[i] + clip4(yo[i] * dh)));
-        }
+      for (int e = 0; e < 32; ++e) {
+        const float sh = __shfl_sync(0xffffffffu, yo[32 + e], lane & 15);
+        z[e] = ih ? sh : yo[e];
+      }
+      const unsigned char* dec = smem + st * S2_STAGE + T_CN + T_NP;
+      bf16* Y = reinterpret_cast<bf16*>(smem + S2_Y);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int r = ih + i;
+        const float dh = __bfloat162float(*reinterpret_cast<const bf16*>(dec + sw_off(C, r, p0)));
+        Y[r * P + p0] = __float2bfloat16_rn(clip4(ydr[i] + clip4(z[i] * dh)));
       }
     }
     if (tid == 0) bulk_wait_read();  // the state tile is rewritten in the next step
@@ -789,6 +794,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       mma_steps(tmem + TM_DDS, [&](int k) { return mndesc(S + SB_DS, N, k); }, [&](int k) { return kdesc(S + SB_B, C, k); },
                 N / 16, sm100::idesc_bf16(64, 64, true, false), false);
       sm100::umma_commit(bars + 3);
+      pc.mark(14);
     }
     // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15, the four blocks'
     // operands (BI0, BI1, DYS0, DYS1; 1280 16-byte units) in one pass, then the four MMAs

@@ -47,7 +47,7 @@ _PHASES = {
                              "diagonal blocks", "rows out"]),
     "ssd_chunk_bwd_tc": (16, ["setup + CB", "head loads", "cumsum", "phase-1 tiles", "dCB blocks", "MMA wait",
                               "dCB readout", "ddd blocks", "diagonal ddd", "MMA wait", "pass 1", "pass 2",
-                              "row stores", "dC / dB"]),
+                              "row stores", "dC / dB", "phase-1 MMA issue"]),
     # summed over the chunk steps
     "ssd_state_fwd_tc": (32, ["S out + previous y rows", "yd loads + state carry", "y_off MMA wait",
                               "y epilogue"]),
