@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
 #pragma unroll
         for (int r = 0; r < 16; ++r) a[r] = B == 0 ? (r == c ? 1.f : 0.f) : ACC[(16 * B + r) * C + c];
         const float* Dw = DI + 256 * B;
+        // all loads before any store of the block (the compiler cannot tell the regions apart)
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
           float s0 = a[r], s1 = 0.f;
@@ -319,19 +320,29 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
           for (int k = r & ~3; k < r; ++k) s0 += Dw[16 * r + k] * a[k];
           const float v_ = s0 + s1;
           x[r] = B != (c >> 4) ? guard(v_) : v_;
-          *reinterpret_cast<bf16*>(AT + sw_off(C, 16 * B + r, c)) = __float2bfloat16_rn(x[r]);
         }
-#pragma unroll 2
-        for (int i = 16 * B + 16; i < C; ++i) {
-          float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 l4 = *reinterpret_cast<const float4*>(AKK + akk_at(i, 4 * B + q));
-            s0 += l4.x * x[4 * q] + l4.z * x[4 * q + 2];
-            s1 += l4.y * x[4 * q + 1] + l4.w * x[4 * q + 3];
+        for (int r = 0; r < 16; ++r)
+          *reinterpret_cast<bf16*>(AT + sw_off(C, 16 * B + r, c)) = __float2bfloat16_rn(x[r]);
+        // rows below, eight at a time: the group's loads come before its stores
+#pragma unroll 1
+        for (int i0 = 16 * B + 16; i0 < C; i0 += 8) {
+          float prev[8], upd[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) prev[t] = B == 0 ? (i0 + t == c ? 1.f : 0.f) : ACC[(i0 + t) * C + c];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 l4 = *reinterpret_cast<const float4*>(AKK + akk_at(i0 + t, 4 * B + q));
+              s0 += l4.x * x[4 * q] + l4.z * x[4 * q + 2];
+              s1 += l4.y * x[4 * q + 1] + l4.w * x[4 * q + 3];
+            }
+            upd[t] = prev[t] - (s0 + s1);
           }
-          const float prev = B == 0 ? (i == c ? 1.f : 0.f) : ACC[i * C + c];
-          ACC[i * C + c] = prev - (s0 + s1);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) ACC[(i0 + t) * C + c] = upd[t];
         }
       }
     } else {
@@ -363,19 +374,26 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     pc.warp_mark(10, t_after4);
     __syncthreads();
     pc.mark(5);
-    // 6a. (b k) e^gc tile (rows j, columns d) over the accumulators in the first half of R1
+    // 6a. (b k) e^gc tile (rows j, columns d) over the accumulators in the first half of R1 (all
+    //     the gate loads before the stores)
+    {
+      float xb[UNITS][8];
 #pragma unroll
-    for (int it = 0; it < UNITS; ++it) {
-      const int u_ = it * F1_THREADS + tid;
-      const int i = u_ >> 4, c = (u_ & 15) << 3;
-      float kv[8], bv[8], x[8];
-      unpack8(ka[it], kv);
-      unpack8(ba[it], bv);
-      float gci[8];
-      ld8f_x(GC + i * D + c, gci);
+      for (int it = 0; it < UNITS; ++it) {
+        const int u_ = it * F1_THREADS + tid;
+        const int i = u_ >> 4, c = (u_ & 15) << 3;
+        float kv[8], bv[8], gci[8];
+        unpack8(ka[it], kv);
+        unpack8(ba[it], bv);
+        ld8f_x(GC + i * D + c, gci);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = bv[e] * kv[e] * __expf(gci[e]);
-      st_chunk8(sR1 + sw_off16(C, i, c), x);
+        for (int e = 0; e < 8; ++e) xb[it][e] = bv[e] * kv[e] * __expf(gci[e]);
+      }
+#pragma unroll
+      for (int it = 0; it < UNITS; ++it) {
+        const int u_ = it * F1_THREADS + tid;
+        st_chunk8(sR1 + sw_off16(C, u_ >> 4, (u_ & 15) << 3), xb[it]);
+      }
     }
     pc.mark(9);
     fence_async_smem();
@@ -1149,24 +1167,31 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
   // intra, row side: per reference block I, key operand (k e^{gc_r - gc})[j][d] for j <= 16 I + 15
   // (16 (I + 1) rows at [0, 40K): offsets 0, 4K, 12K, 24K); dq_b -> TMEM [128 + 32 I, +16),
   // dbk_b -> [144 + 32 I, +16) (lane d, column i - 16 I).  All four blocks in one pass.
+  {
+    float ob[10][8];  // the ten units' operands, stored after all their gate loads
 #pragma unroll
-  for (int I = 0; I < 4; ++I) {
-    const uint32_t buf = S + bc_row_off(I);
-    const bool exact = flags[I];
-    const float* gcr = GC + 16 * I * D;
+    for (int I = 0; I < 4; ++I) {
+      const bool exact = flags[I];
+      const float* gcr = GC + 16 * I * D;
 #pragma unroll
-    for (int it = 0; it <= I; ++it) {
-      const int j = 16 * it + (tid >> 4), c = (tid & 15) << 3;
-      float kv[8], o[8];
-      unpack8(ka[it], kv);
-      const bool zero = exact && j >= 16 * I;
-      float gcj[8], gr8[8];
-      ld8f_x(GC + j * D + c, gcj);
-      ld8f_x(gcr + c, gr8);
+      for (int it = 0; it <= I; ++it) {
+        const int j = 16 * it + (tid >> 4), c = (tid & 15) << 3;
+        float kv[8];
+        unpack8(ka[it], kv);
+        const bool zero = exact && j >= 16 * I;
+        float gcj[8], gr8[8];
+        ld8f_x(GC + j * D + c, gcj);
+        ld8f_x(gcr + c, gr8);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : kv[e] * __expf(gr8[e] - gcj[e]);
-      st_chunk8(buf + sw_off16(16 * (I + 1), j, c), o);
+        for (int e = 0; e < 8; ++e) ob[I * (I + 1) / 2 + it][e] = zero ? 0.f : kv[e] * __expf(gr8[e] - gcj[e]);
+      }
     }
+#pragma unroll
+    for (int I = 0; I < 4; ++I)
+#pragma unroll
+      for (int it = 0; it <= I; ++it)
+        st_chunk8(S + bc_row_off(I) + sw_off16(16 * (I + 1), 16 * it + (tid >> 4), (tid & 15) << 3),
+                  ob[I * (I + 1) / 2 + it]);
   }
   fence_async_smem();
   sm100::tc_fence_before();
@@ -1275,10 +1300,10 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
       tmem_ld16(tmem_at(tmem, quarter, 448 + i0), ck);
       const float gr = GC[i0 * D + d], gs = GC[(i0 + 15) * D + d];
       const bool exact = flags[I];
+      float oq[16], okk[16], ob[16], og[16];  // stored after the loop (its loads first)
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
         const int i = i0 + r;
-        const int64_t gi = ix.row(b, t0 + i, h) + d;
         const int po = i * 256 + 2 * d;
         const float qi = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_QP + po));
         const float ki = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_KP + po));
@@ -1292,16 +1317,29 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
         const float dq_a = scale * p1[r] * eg, dk_a = p2[r] * el, dbk_wy = w3[r] * eg;
         const float bki = bi * ki;
         const float dbk = dbk_wy + dbk_b;
-        dq_o[gi] = __float2bfloat16_rn(dq_a + dq_b);
-        dk_o[gi] = __float2bfloat16_rn(dk_a + dk_b + dbk * bi);
-        db_o[gi] = __float2bfloat16_rn(dbk * ki);
-        DGC[i * D + d] = dq_a * qi - dk_a * ki + dbk_wy * bki + qi * dq_b + bki * dbk_b - ki * dk_b;
+        oq[r] = dq_a + dq_b;
+        okk[r] = dk_a + dk_b + dbk * bi;
+        ob[r] = dbk * ki;
+        og[r] = dq_a * qi - dk_a * ki + dbk_wy * bki + qi * dq_b + bki * dbk_b - ki * dk_b;
         dgcl_part += dk_a * ki;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int i = i0 + r;
+        const int64_t gi = ix.row(b, t0 + i, h) + d;
+        dq_o[gi] = __float2bfloat16_rn(oq[r]);
+        dk_o[gi] = __float2bfloat16_rn(okk[r]);
+        db_o[gi] = __float2bfloat16_rn(ob[r]);
+        DGC[i * D + d] = og[r];
       }
     }
     // dg = dgcl + reverse cumulative sum of dgc; rows 32-63 (warpgroup 1) hand their total to rows 0-31
-    float tot = 0.f;
-    for (int r = 0; r < 32; ++r) tot += DGC[(32 * wg + r) * D + d];
+    float dv32[32], tot = 0.f;  // this thread's 32 rows, loaded before the stores below
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      dv32[r] = DGC[(32 * wg + r) * D + d];
+      tot += dv32[r];
+    }
     if (wg == 1) {
       tail_s[d] = tot;
       dgcl_s[d] += dgcl_part;  // after the first barrier below warpgroup 0 adds its own part
@@ -1310,9 +1348,10 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
     if (wg == 0) dgcl_s[d] += dgcl_part;
     __syncthreads();
     float run = dgcl_s[d] + (wg == 0 ? tail_s[d] : 0.f);
+#pragma unroll
     for (int r = 31; r >= 0; --r) {
       const int i = 32 * wg + r;
-      run += DGC[i * D + d];
+      run += dv32[r];
       dg_o[ix.row(b, t0 + i, h) + d] = run;
     }
   }

@@ -121,19 +121,24 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   chunk_cumsum(smem + S1_DT, Ah, CUM, reinterpret_cast<float*>(smem + S1_V), tid);
   if (tid < P) cl_o[ch * P + tid] = CUM[(C - 1) * P + tid];
   // V = dBx e^{max(cl - c, -20)}  (rows j, columns p)
+  float vb[(C * P / 8) / S1_THREADS][8];  // stored after the loop (the units' loads come first)
 #pragma unroll
   for (int it = 0; it < (C * P / 8) / S1_THREADS; ++it) {
     const int u_ = it * S1_THREADS + tid;
     const int j = u_ >> 3, c = (u_ & 7) << 3;
-    float xv[8], dv[8], o[8];
+    float xv[8], dv[8];
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
     float cj[8], cl8[8];
     ld8f_x(CUM + j * P + c, cj);
     ld8f_x(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - cj[e], -20.f));
-    st_chunk8(S + S1_V + sw_off16(C, j, c), o);
+    for (int e = 0; e < 8; ++e) vb[it][e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - cj[e], -20.f));
+  }
+#pragma unroll
+  for (int it = 0; it < (C * P / 8) / S1_THREADS; ++it) {
+    const int u_ = it * S1_THREADS + tid;
+    st_chunk8(S + S1_V + sw_off16(C, u_ >> 3, (u_ & 7) << 3), vb[it]);
   }
   fence_async_smem();
   sm100::tc_fence_before();
@@ -174,14 +179,16 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
   // cancels these sums against the matching column sums, which bf16 alone would not resolve.
   // Blocks 1-3 are built in one pass (768 units), packed: block I's K steps 0 .. I - 1 (2 KB each)
   // from 0, 2 KB, 6 KB of the hi (W) and lo (dead C tile) regions.
+  float hb[768 / S1_THREADS][8], lb[768 / S1_THREADS][8];  // stored after the loop
 #pragma unroll
   for (int it = 0; it < 768 / S1_THREADS; ++it) {
     const int u_ = it * S1_THREADS + tid;
     const int I = u_ < 128 ? 1 : (u_ < 384 ? 2 : 3);
     const int lu = u_ - (I == 1 ? 0 : (I == 2 ? 128 : 384));
     const int j = lu >> 3, c = (lu & 7) << 3;
-    const int boff = I == 1 ? 0 : (I == 2 ? 2048 : 6144);
-    float xv[8], dv[8], o[8], lo[8];
+    float xv[8], dv[8];
+    float* o = hb[it];
+    float* lo = lb[it];
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_X + sw_off16(C, j, c)), xv);
     unpack8(*reinterpret_cast<const uint4*>(smem + S1_DT + sw_off16(C, j, c)), dv);
     float cj[8], cr8[8];
@@ -192,8 +199,16 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
       o[e] = clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
       lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
     }
-    st_chunk8(S + S1_W0 + boff + sw_off16(C, j, c), o);
-    st_chunk8(S + S1_C + boff + sw_off16(C, j, c), lo);  // the C tile is dead once CB is formed
+  }
+#pragma unroll
+  for (int it = 0; it < 768 / S1_THREADS; ++it) {
+    const int u_ = it * S1_THREADS + tid;
+    const int I = u_ < 128 ? 1 : (u_ < 384 ? 2 : 3);
+    const int lu = u_ - (I == 1 ? 0 : (I == 2 ? 128 : 384));
+    const int j = lu >> 3, c = (lu & 7) << 3;
+    const int boff = I == 1 ? 0 : (I == 2 ? 2048 : 6144);
+    st_chunk8(S + S1_W0 + boff + sw_off16(C, j, c), hb[it]);
+    st_chunk8(S + S1_C + boff + sw_off16(C, j, c), lb[it]);  // the C tile is dead once CB is formed
   }
   fence_async_smem();
   sm100::tc_fence_before();
@@ -278,6 +293,7 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
         if (!wide) {
 #pragma unroll
           for (int t = 0; t < 16; ++t) w[t] *= __expf(cr - CUM[(r + t) * P + p]);
+          float yv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {  // row r + i of CB: two 16-byte chunks, read by the whole block
             float cb[16];
@@ -286,8 +302,10 @@ __global__ void __launch_bounds__(S1_THREADS, 2) ssd_chunk_fwd_tc(
             float acc = 0.f;
 #pragma unroll
             for (int j = 0; j <= i; ++j) acc += cb[j] * w[j];
-            YD[(r + i) * P + p] += __expf(CUM[(r + i) * P + p] - cr) * acc;
+            yv[i] = YD[(r + i) * P + p] + __expf(CUM[(r + i) * P + p] - cr) * acc;
           }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) YD[(r + i) * P + p] = yv[i];  // after all the loads above
         } else {
 #pragma unroll 1
           for (int i = 0; i < 16; ++i) {
@@ -758,11 +776,13 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     pc.mark(2);
     if (tid < 4) flags[tid] = !(fmaxf(span_w[tid], span_w[4 + tid]) <= 60.f);
     // DYR = dy e^{c - c_r(i)}, DYD = dy e^{max(c,-20)}, V = dBx e^{max(cl - c, -20)}  (rows, columns p)
+    // outputs of both units kept until the stores after the loop (the units' loads come first)
+    float r8[2][8], d8[2][8], v8[2][8];
 #pragma unroll
     for (int it = 0; it < (C * P / 8) / SB_THREADS; ++it) {
       const int u_ = it * SB_THREADS + tid;
       const int i = u_ >> 3, c = (u_ & 7) << 3;
-      float dy[8], xv[8], dv[8], r8[8], d8[8], v8[8];
+      float dy[8], xv[8], dv[8];
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, i, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, i, c)), dv);
@@ -772,13 +792,18 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       ld8f_x(CUM + (C - 1) * P + c, cl8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        r8[e] = dy[e] * __expf(c8[e] - cr8[e]);
-        d8[e] = dy[e] * __expf(fmaxf(c8[e], -20.f));
-        v8[e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - c8[e], -20.f));
+        r8[it][e] = dy[e] * __expf(c8[e] - cr8[e]);
+        d8[it][e] = dy[e] * __expf(fmaxf(c8[e], -20.f));
+        v8[it][e] = clip4(dv[e] * xv[e]) * __expf(fmaxf(cl8[e] - c8[e], -20.f));
       }
-      st_chunk8(S + SB_DYR + sw_off16(C, i, c), r8);
-      st_chunk8(S + SB_DYD + sw_off16(C, i, c), d8);
-      st_chunk8(S + SB_V + sw_off16(C, i, c), v8);
+    }
+#pragma unroll
+    for (int it = 0; it < (C * P / 8) / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int i = u_ >> 3, c = (u_ & 7) << 3;
+      st_chunk8(S + SB_DYR + sw_off16(C, i, c), r8[it]);
+      st_chunk8(S + SB_DYD + sw_off16(C, i, c), d8[it]);
+      st_chunk8(S + SB_V + sw_off16(C, i, c), v8[it]);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -798,13 +823,15 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     }
     // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15, the four blocks'
     // operands (BI0, BI1, DYS0, DYS1; 1280 16-byte units) in one pass, then the four MMAs
+    float ob[1280 / SB_THREADS][8];  // stored after the loop (the units' loads come first)
 #pragma unroll
     for (int it = 0; it < 1280 / SB_THREADS; ++it) {
       const int u_ = it * SB_THREADS + tid;
       const int I = u_ < 128 ? 0 : (u_ < 384 ? 1 : (u_ < 768 ? 2 : 3));
       const int lu = u_ - 64 * I * (I + 1);
       const int j = lu >> 3, c = (lu & 7) << 3;
-      float xv[8], dv[8], o[8];
+      float xv[8], dv[8];
+      float* o = ob[it];
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
       const bool zero = flags[I] && j >= 16 * I;
@@ -813,7 +840,13 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       ld8f_x(CUM + 16 * I * P + c, cr8);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = zero ? 0.f : clip4(dv[e] * xv[e]) * __expf(cr8[e] - cj[e]);
-      st_chunk8(S + dcb_buf(I) + sw_off16(C, j, c), o);
+    }
+#pragma unroll
+    for (int it = 0; it < 1280 / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int I = u_ < 128 ? 0 : (u_ < 384 ? 1 : (u_ < 768 ? 2 : 3));
+      const int lu = u_ - 64 * I * (I + 1);
+      st_chunk8(S + dcb_buf(I) + sw_off16(C, lu >> 3, (lu & 7) << 3), ob[it]);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -869,13 +902,16 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     // ddd^T blocks J = 0..2 below the diagonal block (rows i >= 16 J + 16; block 3 has none) as bf16
     // hi + lo operands, packed: block J's K steps J + 1 .. 3 (2 KB each) at hi / lo bases shifted
     // down by 2 KB (J + 1); one pass (768 units), then the MMAs and y_off^T
+    float hb[768 / SB_THREADS][8], lb[768 / SB_THREADS][8];  // stored after the loop
 #pragma unroll
     for (int it = 0; it < 768 / SB_THREADS; ++it) {
       const int u_ = it * SB_THREADS + tid;
       const int J = u_ < 384 ? 0 : (u_ < 640 ? 1 : 2);
       const int lu = u_ - (J == 0 ? 0 : (J == 1 ? 384 : 640));
       const int i = 16 * (J + 1) + (lu >> 3), c = (lu & 7) << 3;
-      float dy[8], o[8], lo[8];
+      float dy[8];
+      float* o = hb[it];
+      float* lo = lb[it];
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DY + sw_off16(C, i, c)), dy);
       float ci[8], cs8[8];
       ld8f_x(CUM + i * P + c, ci);
@@ -885,8 +921,15 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
         o[e] = dy[e] * __expf(ci[e] - cs8[e]);
         lo[e] = o[e] - __bfloat162float(__float2bfloat16_rn(o[e]));
       }
-      st_chunk8(S + ddd_hi(J) + sw_off16(C, i, c), o);
-      st_chunk8(S + ddd_lo(J) + sw_off16(C, i, c), lo);
+    }
+#pragma unroll
+    for (int it = 0; it < 768 / SB_THREADS; ++it) {
+      const int u_ = it * SB_THREADS + tid;
+      const int J = u_ < 384 ? 0 : (u_ < 640 ? 1 : 2);
+      const int lu = u_ - (J == 0 ? 0 : (J == 1 ? 384 : 640));
+      const int i = 16 * (J + 1) + (lu >> 3), c = (lu & 7) << 3;
+      st_chunk8(S + ddd_hi(J) + sw_off16(C, i, c), hb[it]);
+      st_chunk8(S + ddd_lo(J) + sw_off16(C, i, c), lb[it]);
     }
     fence_async_smem();
     sm100::tc_fence_before();
@@ -927,6 +970,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           for (int t = 0; t < 16; ++t) u[t] *= __expf(CUM[(r + t) * P + p] - cs);
           // column j of the block = row r + j of CB^T: two 16-byte chunks (rows i < j are the
           // causal mask's zeros), read by every thread of the block (broadcast)
+          float dv[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float cb[16];
@@ -935,8 +979,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
             float acc = 0.f;
 #pragma unroll
             for (int i = j; i < 16; ++i) acc += cb[i] * u[i];
-            DDG[(r + j) * P + p] = __expf(cs - CUM[(r + j) * P + p]) * acc;
+            dv[j] = __expf(cs - CUM[(r + j) * P + p]) * acc;
           }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) DDG[(r + j) * P + p] = dv[j];  // after all the loads above
         } else {
           for (int j = 0; j < 16; ++j) DDG[(r + j) * P + p] = sb_exact_ddd(smem, CUM, p, r + j, J);
         }
@@ -985,7 +1031,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           yo[e] = hf ? sh : hi16[e];
         }
       }
-      float suf[16], ddbx[16];
+      float suf[16], ddbx[16], oxv[16];
       float dclp = 0.f, local = 0.f;
       const float cl = CUM[(C - 1) * P + p];
       bf16* OX = reinterpret_cast<bf16*>(smem + SB_OX);
@@ -1019,8 +1065,11 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           local += dc;
           suf[r] = local;
           ddbx[r] = dd + ds;
-          OX[i * P + p] = __float2bfloat16_rn(ddbx[r] * dtv);
+          oxv[r] = ddbx[r] * dtv;
         }
+#pragma unroll
+        for (int r = 0; r < 16; ++r)  // stores after all the loads of the loop above
+          OX[(16 * J + r) * P + p] = __float2bfloat16_rn(oxv[r]);
       }
       XCH[kq * 64 + p] = local;
       XCH[(4 + kq) * 64 + p] = dclp;
@@ -1039,9 +1088,11 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
           const float g = off + suf[r];
           const float pre = dtv * Ah;
           const float gA = (pre > -20.f && pre < 20.f) ? g : 0.f;
-          ODT[i * P + p] = __float2bfloat16_rn(ddbx[r] * xv + gA * Ah);
+          oxv[r] = ddbx[r] * xv + gA * Ah;
           dAh += gA * dtv;
         }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) ODT[(16 * J + r) * P + p] = __float2bfloat16_rn(oxv[r]);
       }
       dAh = warp_sum(dAh);
       if (lane == 0) atomicAdd(dA_o + h, dAh);

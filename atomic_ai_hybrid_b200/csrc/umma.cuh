@@ -37,11 +37,22 @@ AHB_DEVICE uint32_t sw_off16(int R, int row, int c8) {
   return (uint32_t)((c8 >> 6) * (R * 128) + (row >> 3) * 1024 + (row & 7) * 128 + ((((c8 & 63) >> 3) ^ (row & 7)) << 4));
 }
 
+// Shared-memory matrix descriptors (128-byte swizzle) for K step s.  The start-address field is
+// (base >> 4) plus the step's offset >> 4, masked to its 14 bits (both are multiples of 16; a base
+// shifted below the window by whole K steps wraps and comes back in the sum); written this way a
+// fully unrolled step loop costs an add and a mask per descriptor instead of rebuilding it from the
+// byte address.
+AHB_DEVICE uint64_t desc_const(uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
 AHB_DEVICE uint64_t kdesc(uint32_t base, int R, int s) {
-  return sm100::smem_desc(base + (uint32_t)((s >> 2) * R * 128 + (s & 3) * 32), 16, 1024);
+  return desc_const(16, 1024) |
+         static_cast<uint64_t>(((base >> 4) + (uint32_t)(((s >> 2) * R * 128 + (s & 3) * 32) >> 4)) & 0x3FFFu);
 }
 AHB_DEVICE uint64_t mndesc(uint32_t base, int Krows, int s) {
-  return sm100::smem_desc(base + (uint32_t)(s * 2048), (uint32_t)(Krows * 128), 1024);
+  return desc_const((uint32_t)(Krows * 128), 1024) | static_cast<uint64_t>(((base >> 4) + (uint32_t)(s * 128)) & 0x3FFFu);
 }
 
 // 8 consecutive fp32 of a shared-memory row as two 16-byte loads, the halves in swapped order on
@@ -117,6 +128,7 @@ AHB_DEVICE uint32_t tmem_at(uint32_t base, int q, int col) { return base + ((uin
 // Issue D (+)= A x B^T over `ks` K-steps; A/B descriptors come from functors of the step.
 template <class FA, class FB>
 AHB_DEVICE void mma_steps(uint32_t d, FA&& fa, FB&& fb, int ks, uint32_t idesc, bool acc) {
+#pragma unroll 8
   for (int s = 0; s < ks; ++s) sm100::umma_bf16(d, fa(s), fb(s), idesc, (acc || s > 0) ? 1u : 0u);
 }
 
