@@ -805,24 +805,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       st_chunk8(S + SB_DYD + sw_off16(C, i, c), d8[it]);
       st_chunk8(S + SB_V + sw_off16(C, i, c), v8[it]);
     }
-    fence_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
     pc.mark(3);
-    if (tid == 0 && !flags[4]) {
-      sm100::tc_fence_after();
-      const bool acc = hh > 0;
-      mma_steps(tmem + TM_DC, [&](int k) { return kdesc(S + SB_DYD, C, k); }, [&](int k) { return kdesc(S + SB_S, N, k); },
-                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
-      mma_steps(tmem + TM_DB, [&](int k) { return kdesc(S + SB_V, C, k); }, [&](int k) { return kdesc(S + SB_DS, N, k); },
-                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
-      mma_steps(tmem + TM_DDS, [&](int k) { return mndesc(S + SB_DS, N, k); }, [&](int k) { return kdesc(S + SB_B, C, k); },
-                N / 16, sm100::idesc_bf16(64, 64, true, false), false);
-      sm100::umma_commit(bars + 3);
-      pc.mark(14);
-    }
     // dCB of this head per row block I: keys (dBx e^{c_r - c_j}) for j <= 16 I + 15, the four blocks'
-    // operands (BI0, BI1, DYS0, DYS1; 1280 16-byte units) in one pass, then the four MMAs
+    // operands (BI0, BI1, DYS0, DYS1; 1280 16-byte units) in the same pass as the tiles above (the
+    // exact-block flags read from the span maxima: flags[] is written by threads 0-3 above)
     float ob[1280 / SB_THREADS][8];  // stored after the loop (the units' loads come first)
 #pragma unroll
     for (int it = 0; it < 1280 / SB_THREADS; ++it) {
@@ -834,7 +820,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       float* o = ob[it];
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_X + sw_off16(C, j, c)), xv);
       unpack8(*reinterpret_cast<const uint4*>(smem + SB_DT + sw_off16(C, j, c)), dv);
-      const bool zero = flags[I] && j >= 16 * I;
+      const bool zero = !(fmaxf(span_w[I], span_w[4 + I]) <= 60.f) && j >= 16 * I;
       float cj[8], cr8[8];
       ld8f_x(CUM + j * P + c, cj);
       ld8f_x(CUM + 16 * I * P + c, cr8);
@@ -851,7 +837,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
     fence_async_smem();
     sm100::tc_fence_before();
     __syncthreads();
-    if (tid == 0 && !flags[4]) {
+    if (tid == 0 && !flags[4]) {  // dCB first (its readout comes next), then dC, dB and dds
       sm100::tc_fence_after();
 #pragma unroll
       for (int I = 0; I < 4; ++I)
@@ -859,9 +845,18 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
                   [&](int k) { return kdesc(S + dcb_buf(I), C, k); }, P / 16,
                   sm100::idesc_bf16(64, 16 * (I + 1), false, false), false);
       sm100::umma_commit(bars + 4);
+      const bool acc = hh > 0;
+      mma_steps(tmem + TM_DC, [&](int k) { return kdesc(S + SB_DYD, C, k); }, [&](int k) { return kdesc(S + SB_S, N, k); },
+                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
+      mma_steps(tmem + TM_DB, [&](int k) { return kdesc(S + SB_V, C, k); }, [&](int k) { return kdesc(S + SB_DS, N, k); },
+                P / 16, sm100::idesc_bf16(64, 128, false, false), acc);
+      mma_steps(tmem + TM_DDS, [&](int k) { return mndesc(S + SB_DS, N, k); }, [&](int k) { return kdesc(S + SB_B, C, k); },
+                N / 16, sm100::idesc_bf16(64, 64, true, false), false);
+      sm100::umma_commit(bars + 3);
+      pc.mark(14);
     }
     pc.mark(4);
-    if (!wait_bar(bars + 3, ph, err, 0x5335) || !wait_bar(bars + 4, ph, err, 0x5335)) flags[4] = 1;
+    if (!wait_bar(bars + 4, ph, err, 0x5335)) flags[4] = 1;
     pc.mark(5);
     sm100::tc_fence_after();
     {  // dCB rows i = 16 quarter + lane (block I = quarter) into the fp32 sum over the heads; the
@@ -951,6 +946,8 @@ __global__ void __launch_bounds__(SB_THREADS, 1) ssd_chunk_bwd_tc(
       sm100::umma_commit(bars + 8);
     }
     pc.mark(7);
+    // the dC / dB / dds products read DYD and V, over which DDG and XCH are written below
+    if (!wait_bar(bars + 3, ph, err, 0x5336)) flags[4] = 1;
     {
       // diagonal blocks of ddd, four threads per channel, one block each, while the MMAs run:
       // ddd[j] = e^{c_s - c_j} sum_{i>=j} CB[i][j] (dy_i e^{c_i - c_s}) with s the block's last row
