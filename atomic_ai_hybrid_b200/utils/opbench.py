@@ -45,9 +45,9 @@ def _timeit(fn, warmup: int, iters: int, flush: torch.Tensor) -> float:
 _PHASES = {
     "ssd_chunk_fwd_tc": (0, ["setup", "load wait", "cumsum + V", "CB out", "y_diag blocks", "MMA wait", "YD rows",
                              "diagonal blocks", "rows out"]),
-    "ssd_chunk_bwd_tc": (16, ["setup + CB", "head loads", "cumsum", "phase-1 tiles", "dCB blocks", "MMA wait",
+    "ssd_chunk_bwd_tc": (16, ["setup + CB", "head loads", "cumsum", "phase-1 tiles", "-", "dCB MMA wait",
                               "dCB readout", "ddd blocks", "diagonal ddd", "MMA wait", "pass 1", "pass 2",
-                              "row stores", "dC / dB", "phase-1 MMA issue"]),
+                              "row stores", "dC / dB", "dCB operands + MMA issue"]),
     # summed over the chunk steps
     "ssd_state_fwd_tc": (32, ["S out + previous y rows", "yd loads + state carry", "y_off MMA wait",
                               "y epilogue"]),
