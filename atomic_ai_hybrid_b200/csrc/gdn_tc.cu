@@ -57,6 +57,26 @@ constexpr int F1_THREADS = 128;
 // fp32 Akk [64][64] with its 16-byte column groups XOR-swizzled by the row: the writers (one row per
 // lane, same group) spread over the banks, the readers (whole warp, one row) get a broadcast
 AHB_DEVICE int akk_at(int i, int j4) { return i * C + ((j4 ^ (i & 15)) << 2); }
+
+// rows [R0, R0 + 8) of x = DI acc for one diagonal block (DI unit lower triangular, [r][k] fp32 rows
+// of 16, read as broadcast 16-byte vectors); entries of blocks off the column's diagonal are guarded
+template <int R0>
+AHB_DEVICE void inv_rows(const float* Dw, const float (&a)[16], float (&xo)[8], bool off) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int rr = R0 + r;
+    float s0 = a[rr], s1 = 0.f;
+#pragma unroll
+    for (int k = 0; k + 3 < rr; k += 4) {
+      const float4 d4 = *reinterpret_cast<const float4*>(Dw + 16 * rr + k);
+      s0 += d4.x * a[k] + d4.z * a[k + 2];
+      s1 += d4.y * a[k + 1] + d4.w * a[k + 3];
+    }
+#pragma unroll
+    for (int k = rr & ~3; k < rr; ++k) s0 += Dw[16 * rr + k] * a[k];
+    xo[r] = off ? guard(s0 + s1) : s0 + s1;
+  }
+}
 constexpr size_t F1_SMEM = 1024 + 3 * 32768 + 256;
 
 __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
@@ -276,57 +296,90 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
     // 5. A = (I + Akk)^-1 in fp32 by blocked forward substitution.
     //    (a) warp w inverts the diagonal 16 x 16 block w of (I + Akk) by substitution (lane j =
     //        column j) into DI, rows 0-15 of the accumulator region (never read as accumulators);
-    //    (b) one column c per thread (threads 0-63), block by block: the block's x = DI_B acc_B
-    //        (independent dot products, no chain over the rows), then acc_i -= sum_{j in block}
-    //        Akk_ij x_j for the rows below (fp32 [i][c] in the first half of R1, acc_i = [i == c]
-    //        before any update).  Entries outside the diagonal blocks are guarded.
+    //    (b) column c by two threads, block by block: the block's x = DI_B acc_B (independent dot
+    //        products, no chain over the rows), then acc_i -= sum_{j in block} Akk_ij x_j for the
+    //        rows below (fp32 [i][c] in the first half of R1, acc_i = [i == c] before any update).
+    //        Entries outside the diagonal blocks are guarded.
     unsigned char* AT = R2 + 24576;
-    float* ACC = reinterpret_cast<float*>(R1);  // [i][c]
-    float* DI = ACC;                            // [w][r][j], 4 x 16 x 16
-    if (lane < 16) {
-      const int j = lane, w = warp;
-      float y[16];
+    float* ACC = reinterpret_cast<float*>(R1);           // [i][c]
+    float* DI = ACC;                                     // [w][r][j], 4 x 16 x 16
+    float* XS = reinterpret_cast<float*>(R2 + 16384);    // [r][c]: x of the current block
+    {
+      // 6b. (w v) tile (rows j, columns d) in the second half of R1, 8 units per thread in two
+      //     batches; the first batch's loads are in flight during the DI solve
+      uint4 wa[4], va[4];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const int i = 16 * w + r;
-        float s = r == j ? 1.f : 0.f;
-#pragma unroll
-        for (int k = 0; k < r; ++k) s -= AKK[akk_at(i, 4 * w + (k >> 2)) + (k & 3)] * y[k];
-        y[r] = r < j ? 0.f : s;
+      for (int q = 0; q < 4; ++q) {
+        const int u_ = q * F1_THREADS + tid;
+        const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
+        wa[q] = *reinterpret_cast<const uint4*>(wg + gi);
+        va[q] = *reinterpret_cast<const uint4*>(v + gi);
       }
+      if (lane < 16) {
+        const int j = lane, w = warp;
+        float y[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) DI[(16 * w + r) * 16 + j] = y[r];
+        for (int r = 0; r < 16; ++r) {
+          const int i = 16 * w + r;
+          float s = r == j ? 1.f : 0.f;
+#pragma unroll
+          for (int k = 0; k < r; ++k) s -= AKK[akk_at(i, 4 * w + (k >> 2)) + (k & 3)] * y[k];
+          y[r] = r < j ? 0.f : s;
+        }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) DI[(16 * w + r) * 16 + j] = y[r];
+      }
+#pragma unroll 1
+      for (int b2 = 0; b2 < 2; ++b2) {
+        if (b2 == 1)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int u_ = (4 + q) * F1_THREADS + tid;
+            const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
+            wa[q] = *reinterpret_cast<const uint4*>(wg + gi);
+            va[q] = *reinterpret_cast<const uint4*>(v + gi);
+          }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u_ = (4 * b2 + q) * F1_THREADS + tid;
+          float wv[8], vv[8];
+          unpack8(wa[q], wv);
+          unpack8(va[q], vv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) wv[e] *= vv[e];
+          st_chunk8(sR1 + TILE_CD + sw_off16(C, u_ >> 4, (u_ & 15) << 3), wv);
+        }
+      }
     }
+    if (tid == 0) bulk_wait_read();  // the Aqk staging tile has been read: XS reuses it
     __syncthreads();
-    if (tid < C) {
-      const int c = tid;
+    {
+      // (b) two threads per column c: thread half hh computes rows [8 hh, 8 hh + 8) of each block's
+      //     x = DI_B acc_B, the halves meet in XS, and each thread updates every other group of 8
+      //     rows below the block
+      const int c = tid & (C - 1), hh = tid >> 6;
 #pragma unroll 1
       for (int B = 0; B < 4; ++B) {
-        float a[16], x[16];
+        float a[16], xh[8], x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) a[r] = B == 0 ? (r == c ? 1.f : 0.f) : ACC[(16 * B + r) * C + c];
         const float* Dw = DI + 256 * B;
-        // all loads before any store of the block (the compiler cannot tell the regions apart)
+        const bool off = B != (c >> 4);
+        if (hh == 0)
+          inv_rows<0>(Dw, a, xh, off);
+        else
+          inv_rows<8>(Dw, a, xh, off);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          float s0 = a[r], s1 = 0.f;
-#pragma unroll
-          for (int k = 0; k + 3 < r; k += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(Dw + 16 * r + k);
-            s0 += d4.x * a[k] + d4.z * a[k + 2];
-            s1 += d4.y * a[k + 1] + d4.w * a[k + 3];
-          }
-#pragma unroll
-          for (int k = r & ~3; k < r; ++k) s0 += Dw[16 * r + k] * a[k];
-          const float v_ = s0 + s1;
-          x[r] = B != (c >> 4) ? guard(v_) : v_;
+        for (int r = 0; r < 8; ++r) {
+          XS[(8 * hh + r) * C + c] = xh[r];
+          *reinterpret_cast<bf16*>(AT + sw_off(C, 16 * B + 8 * hh + r, c)) = __float2bfloat16_rn(xh[r]);
         }
+        __syncthreads();
 #pragma unroll
-        for (int r = 0; r < 16; ++r)
-          *reinterpret_cast<bf16*>(AT + sw_off(C, 16 * B + r, c)) = __float2bfloat16_rn(x[r]);
-        // rows below, eight at a time: the group's loads come before its stores
+        for (int r = 0; r < 16; ++r) x[r] = XS[r * C + c];
+        // rows below, eight at a time, alternate groups per half: the group's loads come before its stores
 #pragma unroll 1
-        for (int i0 = 16 * B + 16; i0 < C; i0 += 8) {
+        for (int i0 = 16 * B + 16 + 8 * hh; i0 < C; i0 += 16) {
           float prev[8], upd[8];
 #pragma unroll
           for (int t = 0; t < 8; ++t) prev[t] = B == 0 ? (i0 + t == c ? 1.f : 0.f) : ACC[(i0 + t) * C + c];
@@ -344,31 +397,7 @@ __global__ void __launch_bounds__(F1_THREADS, 2) gdn_chunk_fwd_tc(
 #pragma unroll
           for (int t = 0; t < 8; ++t) ACC[(i0 + t) * C + c] = upd[t];
         }
-      }
-    } else {
-      // 6b. (w v) tile (rows j, columns d) in the second half of R1: 1024 units over 64 threads,
-      //     four per batch of loads
-      const int t2 = tid - C;
-#pragma unroll 1
-      for (int b4 = 0; b4 < 4; ++b4) {
-        uint4 wa[4], va[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int u_ = (4 * b4 + q) * C + t2;
-          const int64_t gi = ix.row(b, t0 + (u_ >> 4), h) + ((u_ & 15) << 3);
-          wa[q] = *reinterpret_cast<const uint4*>(wg + gi);
-          va[q] = *reinterpret_cast<const uint4*>(v + gi);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int u_ = (4 * b4 + q) * C + t2;
-          float wv[8], vv[8];
-          unpack8(wa[q], wv);
-          unpack8(va[q], vv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) wv[e] *= vv[e];
-          st_chunk8(sR1 + TILE_CD + sw_off16(C, u_ >> 4, (u_ & 15) << 3), wv);
-        }
+        __syncthreads();  // the rows below are complete before the next block reads them; XS is free
       }
     }
     pc.warp_mark(10, t_after4);
@@ -1300,10 +1329,10 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
       tmem_ld16(tmem_at(tmem, quarter, 448 + i0), ck);
       const float gr = GC[i0 * D + d], gs = GC[(i0 + 15) * D + d];
       const bool exact = flags[I];
-      float oq[16], okk[16], ob[16], og[16];  // stored after the loop (its loads first)
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
         const int i = i0 + r;
+        const int64_t gi = ix.row(b, t0 + i, h) + d;
         const int po = i * 256 + 2 * d;
         const float qi = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_QP + po));
         const float ki = __bfloat162float(*reinterpret_cast<const bf16*>(smem + BC_KP + po));
@@ -1317,20 +1346,11 @@ __global__ void __launch_bounds__(BC_THREADS, 1) gdn_chunk_bwd_tc(
         const float dq_a = scale * p1[r] * eg, dk_a = p2[r] * el, dbk_wy = w3[r] * eg;
         const float bki = bi * ki;
         const float dbk = dbk_wy + dbk_b;
-        oq[r] = dq_a + dq_b;
-        okk[r] = dk_a + dk_b + dbk * bi;
-        ob[r] = dbk * ki;
-        og[r] = dq_a * qi - dk_a * ki + dbk_wy * bki + qi * dq_b + bki * dbk_b - ki * dk_b;
+        dq_o[gi] = __float2bfloat16_rn(dq_a + dq_b);
+        dk_o[gi] = __float2bfloat16_rn(dk_a + dk_b + dbk * bi);
+        db_o[gi] = __float2bfloat16_rn(dbk * ki);
+        DGC[i * D + d] = dq_a * qi - dk_a * ki + dbk_wy * bki + qi * dq_b + bki * dbk_b - ki * dk_b;
         dgcl_part += dk_a * ki;
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const int i = i0 + r;
-        const int64_t gi = ix.row(b, t0 + i, h) + d;
-        dq_o[gi] = __float2bfloat16_rn(oq[r]);
-        dk_o[gi] = __float2bfloat16_rn(okk[r]);
-        db_o[gi] = __float2bfloat16_rn(ob[r]);
-        DGC[i * D + d] = og[r];
       }
     }
     // dg = dgcl + reverse cumulative sum of dgc; rows 32-63 (warpgroup 1) hand their total to rows 0-31
