@@ -863,6 +863,41 @@ void optim_apply(torch::Tensor segs, torch::Tensor cstart, int64_t nblocks, torc
   check_launch("ahb_optim_apply");
 }
 
+// Muon's Newton-Schulz iteration (reference optimizer.py:53-77) in place on X (E, r, c), fp32, each
+// matrix already divided by its norm, r <= c.  Per step: G_e = X_e X_e^T for all E matrices in one
+// grouped tcgen05 GEMM (B read K-major), Y_e = G_e X_e in a second (B read row-major), then the fused
+// update.  The GEMM operands are bf16 images of X with fp32 accumulation in TMEM; X stays fp32.
+void muon_ns(torch::Tensor X, int64_t steps) {
+  TORCH_CHECK(X.is_cuda() && X.scalar_type() == at::kFloat && X.is_contiguous() && X.dim() == 3,
+              "muon_ns: X must be a contiguous (E, r, c) fp32 CUDA tensor");
+  const int64_t E = X.size(0), r = X.size(1), c = X.size(2);
+  TORCH_CHECK(E >= 1 && E <= 192 && r <= c && r % 128 == 0 && c % 64 == 0,
+              "muon_ns: 1..192 matrices of r x c with r <= c, r % 128 == 0, c % 64 == 0");
+  const bool pair = moe_pair() && r % 256 == 0;  // CTA-pair groups start on 256-row boundaries
+  const int PM = pair ? AHB_GEMM_PAIR : 0;
+  auto ob = X.options().dtype(at::kBFloat16);
+  auto Xb = torch::empty({E * r, c}, ob);
+  auto G = torch::empty({E * r, r}, ob);
+  auto Y = torch::empty({E * r, c}, ob);
+  auto off = torch::arange(0, E * r + 1, r, torch::dtype(torch::kInt32).device(X.device()));
+  int* err = err_word().data_ptr<int>();
+  auto st = cur_stream();
+  ahb_ns_update(X.data_ptr<float>(), nullptr, Xb.data_ptr(), X.numel(), num_sms(), st);
+  check_launch("ahb_ns_update");
+  for (int64_t s = 0; s < steps; ++s) {
+    int rc = ahb_moe_gemm(AHB_GEMM_DX | PM, Xb.data_ptr(), nullptr, E * r, c, Xb.data_ptr(), nullptr, E * r, c, (int)r,
+                          off.data_ptr<int>(), (int)E, (int)r, 0, (int)c, (int)(c / 64), G.data_ptr(), nullptr,
+                          nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "muon X X^T");
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN | PM, G.data_ptr(), nullptr, E * r, r, Xb.data_ptr(), nullptr, E * r, c,
+                      (int)r, off.data_ptr<int>(), (int)E, (int)c, 0, (int)r, (int)(r / 64), Y.data_ptr(), nullptr,
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "muon G X");
+    ahb_ns_update(X.data_ptr<float>(), Y.data_ptr(), Xb.data_ptr(), X.numel(), num_sms(), st);
+    check_launch("ahb_ns_update");
+  }
+}
+
 // ------------------------------------------------------------ fused layer glue (fused_norm.cu)
 static void check_rows(const torch::Tensor& t, int64_t D, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.size(-1) == D, n,
@@ -1500,6 +1535,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_online_bwd", &ce_online_bwd);
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
+  m.def("muon_ns", &muon_ns);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, py::arg("x"), py::arg("delta"), py::arg("scale"), py::arg("clip"),
         py::arg("eps"), py::arg("stats") = py::none());
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);

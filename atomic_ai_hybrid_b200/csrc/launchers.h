@@ -133,6 +133,8 @@ void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nbl
 void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, float* master, float* m, float* v,
                      const void* grad, bool grad_bf16, const float* coef, void* compute, const float* frac, int fracE,
                      AhbOptimArgs args, void* const* cpeers, int npeers, cudaStream_t st);
+// Muon Newton-Schulz update X <- nan_to_num(1.5 X - 0.5 Y), Xb <- bf16(X) (Y null: Xb only); n % 4 == 0
+void ahb_ns_update(float* X, const void* Y, void* Xb, int64_t n, int num_sms, cudaStream_t st);
 
 // fused_norm.cu: residual add + clip + RMSNorm, RMSNorm x SiLU gate, GDN gates, per-head L2 norm, Mamba2 dt
 // (bf16 activations, fp32 scales / statistics; rows of D channels need D % 256 == 0)

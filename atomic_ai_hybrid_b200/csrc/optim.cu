@@ -157,6 +157,32 @@ __global__ void __launch_bounds__(THREADS) optim_apply_kernel(const AhbSegInfo* 
   }
 }
 
+// Muon's Newton-Schulz step after its two GEMMs (reference optimizer.py:65-75): X <- 1.5 X - 0.5 Y
+// in fp32, a non-finite result set to zero (the reference's nan_to_num after every step), and the
+// bf16 image of X that the next step's GEMMs read.  Without Y it only writes the image.  Four
+// elements per thread (the matrices are multiples of 64 columns).
+__global__ void __launch_bounds__(THREADS) ns_update_kernel(float* __restrict__ X, const bf16* __restrict__ Y,
+                                                            bf16* __restrict__ Xb, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)THREADS + threadIdx.x; i < n4; i += (int64_t)gridDim.x * THREADS) {
+    float4 x = reinterpret_cast<float4*>(X)[i];
+    float v[4] = {x.x, x.y, x.z, x.w};
+    if (Y) {
+      const uint2 yr = reinterpret_cast<const uint2*>(Y)[i];
+      const bf16* y = reinterpret_cast<const bf16*>(&yr);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float t = 1.5f * v[k] - 0.5f * __bfloat162float(y[k]);
+        v[k] = isfinite(t) ? t : 0.f;
+      }
+      reinterpret_cast<float4*>(X)[i] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    __align__(8) bf16 o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = __float2bfloat16_rn(v[k]);
+    reinterpret_cast<uint2*>(Xb)[i] = *reinterpret_cast<const uint2*>(o);
+  }
+}
+
 }  // namespace
 
 void ahb_optim_prepare(const AhbSegInfo* segs, const int* cstart, int S, int nblocks, void* grad, bool grad_bf16,
@@ -186,3 +212,11 @@ void ahb_optim_apply(const AhbSegInfo* segs, const int* cstart, int S, int nbloc
 }
 
 int ahb_optim_chunk() { return CHUNK; }
+
+void ahb_ns_update(float* X, const void* Y, void* Xb, int64_t n, int num_sms, cudaStream_t st) {
+  const int64_t n4 = n / 4;
+  if (n4 <= 0) return;
+  const int64_t want = (n4 + THREADS - 1) / THREADS;
+  const int grid = (int)(want < (int64_t)num_sms * 8 ? want : (int64_t)num_sms * 8);
+  ns_update_kernel<<<grid, THREADS, 0, st>>>(X, static_cast<const bf16*>(Y), static_cast<bf16*>(Xb), n4);
+}

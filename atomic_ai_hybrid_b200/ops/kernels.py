@@ -787,9 +787,29 @@ def gemm_error() -> int:
     return int(ext().gemm_error())
 
 
-def newton_schulz3(g):
-    """Muon orthogonalisation (three Newton-Schulz steps) with cuBLAS GEMMs."""
-    return R.newton_schulz3(g)
+def newton_schulz3(g, steps: int = 3, eps: float = 1e-4):
+    """Muon orthogonalisation (reference `optimizer.py:53-77`): ``steps`` Newton-Schulz steps
+    X <- 1.5 X - 0.5 X X^T X on the tcgen05 grouped GEMM (``muon_ns``: bf16 operands, fp32
+    accumulation, X itself kept in fp32, non-finite entries zeroed after every step).
+
+    The step commutes with transposition, so a tall matrix runs as its transpose and the Gram
+    matrix X X^T is the smaller one (r x r, r the shorter side).  The matrices of a 3-D tensor
+    (the experts) are the groups of the same two launches per step.  A shorter side that is not a
+    multiple of 128 (or a longer one not of 64) runs the fp32 PyTorch iteration instead."""
+    if not g.is_cuda or g.ndim not in (2, 3):
+        return R.newton_schulz3(g, steps, eps)
+    m = g if g.ndim == 3 else g.unsqueeze(0)
+    tall = m.shape[1] > m.shape[2]
+    r, c = (m.shape[2], m.shape[1]) if tall else (m.shape[1], m.shape[2])
+    if r % 128 or c % 64:
+        return R.newton_schulz3(g, steps, eps)
+    X = (m.transpose(1, 2) if tall else m).float()
+    nrm = torch.linalg.vector_norm(X, dim=(-2, -1), keepdim=True)
+    X = (X / torch.where(nrm < eps, torch.ones_like(nrm), nrm)).contiguous()
+    for e0 in range(0, X.shape[0], 192):  # the grouped GEMM takes at most 192 groups
+        ext().muon_ns(X[e0:e0 + 192], steps)
+    out = X.transpose(1, 2) if tall else X
+    return out.reshape(g.shape)
 
 
 # ----------------------------------------------------------------- fused optimizer

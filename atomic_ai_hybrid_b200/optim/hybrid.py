@@ -23,7 +23,8 @@ Apply step (reference `train_setup.py:490-550`), on the owned shard:
 
 On CUDA tensors every elementwise piece runs in one fused kernel per step over
 the owned segment table (``ops.kernels.optim_apply``); Muon's Newton-Schulz runs
-as batched GEMMs per matrix first.  Cross-rank reductions (norms, flags) go
+first, two grouped tcgen05 GEMMs per step for all matrices of a tensor
+(``ops.kernels.newton_schulz3``).  Cross-rank reductions (norms, flags) go
 through ``reduce_fn``.
 """
 from __future__ import annotations

@@ -4,6 +4,7 @@ the MoE grouped FFN, the fused router, the fused residual/norm glue and conv1d.
 
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op gdn --B 8 --T 4096 --H 16``
 ``python -m atomic_ai_hybrid_b200.utils.opbench --op ssd --B 8 --T 4096 --H 32``
+``python -m atomic_ai_hybrid_b200.utils.opbench --op muon --B 32 --K 2048 --N 1024`` (Muon on 32 experts)
 
 Inputs: GDN q, k ~ N(0,1) then L2-normalised per head, v ~ N(0,1),
 beta = sigmoid(N(0,1)), g = -softplus(N(0,1)) (per head, broadcast over the
@@ -91,8 +92,8 @@ def _phase_report(fn, prefix):
     return out
 
 
-def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
-    from ..ops import kernels as K
+def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False, impl="cuda"):
+    from ..ops import kernels as K, reference as R
     from ..ops.reference import flops_gdn_chunked
     D = 128
     dev = "cuda"
@@ -106,22 +107,25 @@ def bench_gdn(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
     do = torch.randn(B, T, H, D, device=dev, dtype=torch.bfloat16)
 
     def run():
-        o = K.gdn2(q, k, v, w, b, g, 1.0, 64)
+        if impl == "eager":  # the PyTorch chunked scan (checkpointed chunks), the eager baseline
+            o = R.gdn2_chunked(q, k, v, g, b, w, 1.0, 64, checkpoint_chunks=True)[0]
+        else:
+            o = K.gdn2(q, k, v, w, b, g, 1.0, 64)
         if mode == "fwdbwd":
             torch.autograd.backward(o, do)
 
     ms = _timeit(run, warmup, iters, flush)
     fl = flops_gdn_chunked(B, T, H, D, 64) * (3 if mode == "fwdbwd" else 1)
     io_bytes = B * T * H * D * (2 * 5 + 4) * (3 if mode == "fwdbwd" else 1)
-    r = {"op": "gdn2", "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9,
+    r = {"op": "gdn2", "impl": impl, "mode": mode, "B": B, "T": T, "H": H, "D": D, "ms": ms, "tflops": fl / ms / 1e9,
          "min_io_gb_s": io_bytes / ms / 1e6}
     if phases:
         r["phases"] = _phase_report(run, "gdn")
     return r
 
 
-def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
-    from ..ops import kernels as K
+def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False, impl="cuda"):
+    from ..ops import kernels as K, reference as R
     from ..ops.reference import flops_ssd_chunked
     P, N = 64, 128
     dev = "cuda"
@@ -134,14 +138,17 @@ def bench_ssd(B, T, H, warmup, iters, flush, mode="fwdbwd", phases=False):
     dy = torch.randn(B, T, H, P, device=dev, dtype=torch.bfloat16)
 
     def run():
-        y = K.ssd(dt, A, Bm, Cm, x, 64)
+        if impl == "eager":
+            y = R.ssd_chunked(dt, A, Bm, Cm, x, 64, checkpoint_chunks=True)[0]
+        else:
+            y = K.ssd(dt, A, Bm, Cm, x, 64)
         if mode == "fwdbwd":
             torch.autograd.backward(y, dy)
 
     ms = _timeit(run, warmup, iters, flush)
     fl = flops_ssd_chunked(B, T, H, P, N, 64) * (3 if mode == "fwdbwd" else 1)
     io_bytes = (B * T * H * P * 2 * 3 + B * T * N * 2 * 2) * (3 if mode == "fwdbwd" else 1)
-    r = {"op": "ssd", "mode": mode, "B": B, "T": T, "H": H, "P": P, "N": N, "ms": ms, "tflops": fl / ms / 1e9,
+    r = {"op": "ssd", "impl": impl, "mode": mode, "B": B, "T": T, "H": H, "P": P, "N": N, "ms": ms, "tflops": fl / ms / 1e9,
          "min_io_gb_s": io_bytes / ms / 1e6}
     if phases:
         r["phases"] = _phase_report(run, "ssd")
@@ -307,10 +314,25 @@ def bench_gemm_rs(W, n, K, N, warmup, iters, flush):
     return {"op": "gemm_rs_local", "W": W, "rows": W * n, "K": K, "N": N, "ms": ms, "tflops": fl / ms / 1e9}
 
 
+def bench_muon(E, a, b, warmup, iters, flush):
+    """Muon's three Newton-Schulz steps on E matrices of a x b (fp32 gradients): the grouped
+    tcgen05 path against the fp32 PyTorch iteration.  FLOPs: 3 steps x two products of
+    2 r^2 c each (r, c the shorter and longer side) per matrix."""
+    from ..ops import kernels as K, reference as R
+    g = torch.randn(E, a, b, device="cuda", dtype=torch.float32)
+    r, c = min(a, b), max(a, b)
+    fl = 3 * 2 * 2.0 * r * r * c * E
+    out = {"op": "muon_ns", "E": E, "a": a, "b": b}
+    for name, fn in (("tcgen05", lambda: K.newton_schulz3(g)), ("torch_fp32", lambda: R.newton_schulz3(g))):
+        ms = _timeit(fn, warmup, iters, flush)
+        out[name] = {"ms": ms, "tflops": fl / ms / 1e9}
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="gdn",
-                    choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs", "gemm", "attn", "ce"])
+                    choices=["gdn", "ssd", "moe", "router", "glue", "conv", "gemm_rs", "gemm", "attn", "ce", "muon"])
     ap.add_argument("--K", type=int, default=2048)
     ap.add_argument("--N", type=int, default=2048)
     ap.add_argument("--mode", default="fwdbwd", choices=["fwd", "fwdbwd"])
@@ -319,6 +341,8 @@ def main(argv=None):
     ap.add_argument("--H", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "eager"],
+                    help="gdn / ssd: the sm_100a kernels or the PyTorch chunked scans (eager baseline)")
     ap.add_argument("--phases", action="store_true",
                     help="gdn / ssd: also report the scan kernels' per-phase cycles (one extra call)")
     a = ap.parse_args(argv)
@@ -327,9 +351,9 @@ def main(argv=None):
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
     torch.manual_seed(0)
     if a.op == "gdn":
-        r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode, a.phases)
+        r = bench_gdn(a.B, a.T, a.H or 16, a.warmup, a.iters, flush, a.mode, a.phases, a.impl)
     elif a.op == "ssd":
-        r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode, a.phases)
+        r = bench_ssd(a.B, a.T, a.H or 32, a.warmup, a.iters, flush, a.mode, a.phases, a.impl)
     elif a.op == "moe":
         r = bench_moe(a.B * a.T, 2048, 1024, 32, 4, a.warmup, a.iters, flush, a.mode)
     elif a.op == "router":
@@ -342,6 +366,8 @@ def main(argv=None):
         r = bench_ce(a.B * a.T, a.K, 50304, a.warmup, a.iters, flush, a.mode)
     elif a.op == "gemm":
         r = bench_gemm(a.B * a.T, a.K, a.N, a.warmup, a.iters, flush)
+    elif a.op == "muon":
+        r = bench_muon(a.B, a.K, a.N, a.warmup, a.iters, flush)
     elif a.op == "gemm_rs":
         r = bench_gemm_rs(2, a.B * a.T // 2, 512, 4096, a.warmup, a.iters, flush)
     else:

@@ -112,3 +112,28 @@ def test_fused_step_with_bf16_gradients():
         runs.append((st.master.clone(), opt.m.clone(), opt.v.clone()))
     for a, b in zip(*runs):
         torch.testing.assert_close(b, a, rtol=1e-2, atol=1e-6)
+
+
+@pytest.mark.parametrize("shape", [(256, 512), (1024, 256), (4, 256, 768), (3, 1024, 512), (2, 2048, 1024),
+                                   (96, 160)])
+def test_muon_newton_schulz_on_tensor_cores(shape):
+    """Muon's three Newton-Schulz steps on the grouped tcgen05 GEMM (bf16 operands, fp32 X)
+    against the fp32 PyTorch iteration; (96, 160) takes the PyTorch path (sides off the tiles)."""
+    from atomic_ai_hybrid_b200.ops import kernels as K, reference as R
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    lead, (a, b) = shape[:-2], shape[-2:]
+    # a gradient-like matrix: a few strong directions over noise
+    x = (torch.randn(*lead, a, 8, device=dev, generator=g) @ torch.randn(*lead, 8, b, device=dev, generator=g)
+         + 0.1 * torch.randn(*shape, device=dev, generator=g))
+    ref = R.newton_schulz3(x)
+    out = K.newton_schulz3(x)
+    assert out.shape == x.shape and out.dtype == torch.float32
+    for i in range(out.reshape(-1, a, b).shape[0]):
+        o, r = out.reshape(-1, a, b)[i], ref.reshape(-1, a, b)[i]
+        assert ((o - r).norm() / r.norm()).item() < 2e-3, i
+    # a non-finite gradient zeroes its matrix, as the reference's nan_to_num does
+    x.view(-1, a, b)[0, 3, 5] = float("nan")
+    out = K.newton_schulz3(x)
+    assert torch.equal(out.reshape(-1, a, b)[0], torch.zeros(a, b, device=dev))
+    assert torch.isfinite(out).all()
