@@ -1005,6 +1005,96 @@ std::vector<torch::Tensor> norm_gate_bwd(torch::Tensor dy, torch::Tensor x, torc
   return {dx, dz};
 }
 
+// Tensor-parallel (head-split) RMSNorm, gated by z when given (ops.kernels.tp_norm): x (..., D) holds D
+// of the row's Dfull channels; the caller all-reduces the row sums (ss, dot) over the group between
+// the passes.
+static int64_t tp_z_stride(const c10::optional<torch::Tensor>& z, const torch::Tensor& x, int64_t D) {
+  if (!z.has_value() || !z->defined()) return 0;
+  TORCH_CHECK(z->is_cuda() && z->scalar_type() == at::kBFloat16 && z->stride(-1) == 1 && z->size(-1) == D &&
+                  z->numel() == x.numel() && z->dim() >= 2, "tp_norm: z bf16 with unit channel stride");
+  for (int i = 0; i < z->dim() - 2; ++i)
+    TORCH_CHECK(z->stride(i) == z->size(i + 1) * z->stride(i + 1), "tp_norm: z rows must be evenly strided");
+  TORCH_CHECK(z->stride(-2) % 8 == 0, "tp_norm: z row stride must be a multiple of 8");
+  return z->stride(-2);
+}
+
+static const void* opt_any(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() && t->defined() ? t->data_ptr() : nullptr;
+}
+
+torch::Tensor tp_norm_sumsq(torch::Tensor x) {
+  const int64_t D = x.size(-1);
+  TORCH_CHECK(ahb_row_supported((int)D), "tp_norm: D % 256 != 0");
+  check_rows(x, D, "x");
+  const int64_t M = x.numel() / D;
+  auto ss = torch::empty({M}, x.options().dtype(at::kFloat));
+  ahb_tp_norm_sumsq(x.data_ptr(), ss.data_ptr<float>(), M, (int)D, cur_stream());
+  check_launch("ahb_tp_norm_sumsq");
+  return ss;
+}
+
+std::vector<torch::Tensor> tp_norm_fwd(torch::Tensor x, c10::optional<torch::Tensor> z, torch::Tensor scale,
+                                       torch::Tensor ss, double eps, double inv_dfull, double zclip, double oclip) {
+  const int64_t D = x.size(-1);
+  TORCH_CHECK(ahb_row_supported((int)D), "tp_norm: D % 256 != 0");
+  check_rows(x, D, "x");
+  const int64_t zs = tp_z_stride(z, x, D);
+  const int64_t M = x.numel() / D;
+  TORCH_CHECK(ss.is_cuda() && ss.scalar_type() == at::kFloat && ss.is_contiguous() && ss.numel() == M,
+              "tp_norm: ss (rows,) fp32");
+  auto sc = scale.to(at::kFloat).contiguous();
+  TORCH_CHECK(sc.numel() == D, "tp_norm: scale of D channels");
+  auto y = torch::empty_like(x);
+  auto r = torch::empty({M}, x.options().dtype(at::kFloat));
+  ahb_tp_norm_fwd(x.data_ptr(), opt_any(z), zs, sc.data_ptr<float>(), ss.data_ptr<float>(), y.data_ptr(),
+                  r.data_ptr<float>(), M, (int)D, (float)inv_dfull, (float)eps, (float)zclip, (float)oclip,
+                  cur_stream());
+  check_launch("ahb_tp_norm_fwd");
+  return {y, r};
+}
+
+// returns {dz (empty without a gate), local dot}; the scale gradient is added into dscale_acc
+std::vector<torch::Tensor> tp_norm_bwd_dot(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> z,
+                                           torch::Tensor scale, torch::Tensor rstd, double zclip, double oclip,
+                                           c10::optional<torch::Tensor> dscale_acc) {
+  const int64_t D = x.size(-1);
+  check_rows(x, D, "x");
+  check_rows(dy, D, "dy");
+  const int64_t zs = tp_z_stride(z, x, D);
+  const int64_t M = x.numel() / D;
+  auto sc = scale.to(at::kFloat).contiguous();
+  const bool gated = opt_any(z) != nullptr;
+  auto dz = gated ? torch::empty_like(x) : torch::empty({0}, x.options());
+  auto dot = torch::empty({M}, x.options().dtype(at::kFloat));
+  const bool wacc = dscale_acc.has_value() && dscale_acc->defined();
+  torch::Tensor part;
+  if (wacc) part = torch::empty({(int64_t)ahb_row_bwd_blocks(M), D}, x.options().dtype(at::kFloat));
+  ahb_tp_norm_bwd_dot(dy.data_ptr(), x.data_ptr(), opt_any(z), zs, sc.data_ptr<float>(), rstd.data_ptr<float>(),
+                      gated ? dz.data_ptr() : nullptr, dot.data_ptr<float>(), wacc ? part.data_ptr<float>() : nullptr,
+                      M, (int)D, (float)zclip, (float)oclip, cur_stream());
+  check_launch("ahb_tp_norm_bwd_dot");
+  if (wacc) add_scale_grad(part, dscale_acc, D);
+  return {dz, dot};
+}
+
+torch::Tensor tp_norm_bwd_dx(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> z, torch::Tensor scale,
+                             torch::Tensor rstd, torch::Tensor dot, double inv_dfull, double zclip, double oclip) {
+  const int64_t D = x.size(-1);
+  check_rows(x, D, "x");
+  check_rows(dy, D, "dy");
+  const int64_t zs = tp_z_stride(z, x, D);
+  const int64_t M = x.numel() / D;
+  TORCH_CHECK(dot.is_cuda() && dot.scalar_type() == at::kFloat && dot.is_contiguous() && dot.numel() == M,
+              "tp_norm: dot (rows,) fp32");
+  auto sc = scale.to(at::kFloat).contiguous();
+  auto dx = torch::empty_like(x);
+  ahb_tp_norm_bwd_dx(dy.data_ptr(), x.data_ptr(), opt_any(z), zs, sc.data_ptr<float>(), rstd.data_ptr<float>(),
+                     dot.data_ptr<float>(), dx.data_ptr(), M, (int)D, (float)inv_dfull, (float)zclip, (float)oclip,
+                     cur_stream());
+  check_launch("ahb_tp_norm_bwd_dx");
+  return dx;
+}
+
 std::vector<torch::Tensor> gdn_gates_fwd(torch::Tensor bp, torch::Tensor wp, torch::Tensor fp, torch::Tensor decay_a,
                                          int64_t Dh) {
   const int64_t d = bp.size(-1);
@@ -1541,6 +1631,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);
   m.def("norm_gate_fwd", &norm_gate_fwd);
   m.def("norm_gate_bwd", &norm_gate_bwd);
+  m.def("tp_norm_sumsq", &tp_norm_sumsq);
+  m.def("tp_norm_fwd", &tp_norm_fwd);
+  m.def("tp_norm_bwd_dot", &tp_norm_bwd_dot);
+  m.def("tp_norm_bwd_dx", &tp_norm_bwd_dx);
   m.def("gdn_gates_fwd", &gdn_gates_fwd);
   m.def("gdn_gates_bwd", &gdn_gates_bwd);
   m.def("l2norm_heads_fwd", &l2norm_heads_fwd);

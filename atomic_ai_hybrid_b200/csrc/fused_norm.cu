@@ -235,6 +235,132 @@ __global__ void norm_gate_bwd_kernel(const bf16* __restrict__ dy, const bf16* __
   }
 }
 
+// ------------------------------------------------------------------ tensor-parallel norm
+// RMSNorm over the full width of a head-split activation, optionally gated as norm_gate: each rank
+// holds D of the row's Dfull channels, so each row statistic is a sum over the tensor-parallel group
+// that the host all-reduces between two passes.  Forward: pass 1 the local sum of squares, pass 2
+// the output from the group's sum.  Backward: pass 1 dz, the scale-gradient partials and the local
+// dot sum(g * x_hat) (g = dL/d(x_hat)), pass 2 dx = r (g - x_hat dot / Dfull) from the group's dot.
+// z == nullptr: no gate (y = clamp(rmsnorm(x) * scale, +-oclip)).
+AHB_DEVICE void tp_gate_terms(const F8& xv, const F8* zv, const F8& d, const float* sc, float r, float zclip,
+                              float oclip, float* xh, float* g, float* dn_out, F8* dzo) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    xh[i] = xv.v[i] * r;
+    const float n = xh[i] * sc[i];
+    float sz = 1.f, sg = 0.f, zc = 0.f;
+    if (zv) {
+      zc = clampf(zv->v[i], zclip);
+      sg = sigmoidf_(zc);
+      sz = zc * sg;
+    }
+    const float dout = fabsf(n * sz) <= oclip ? d.v[i] : 0.f;
+    const float dn = dout * sz;
+    if (zv) dzo->v[i] = fabsf(zv->v[i]) <= zclip ? dout * n * sg * (1.f + zc * (1.f - sg)) : 0.f;
+    dn_out[i] = dn;
+    g[i] = dn * sc[i];
+  }
+}
+
+__global__ void tp_norm_sumsq_kernel(const bf16* __restrict__ x, float* __restrict__ ss, int64_t M, int D) {
+  __shared__ float sh[32];
+  const int c0 = threadIdx.x * 8;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const F8 xv = ld8(x + row * D + c0);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += xv.v[i] * xv.v[i];
+    s = row_sum(s, sh);
+    if (threadIdx.x == 0) ss[row] = s;
+  }
+}
+
+__global__ void tp_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int64_t zs,
+                                   const float* __restrict__ scale, const float* __restrict__ ss,
+                                   bf16* __restrict__ y, float* __restrict__ rstd, int64_t M, int D, float inv_dfull,
+                                   float eps, float zclip, float oclip) {
+  const int c0 = threadIdx.x * 8;
+  float sc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sc[i] = scale[c0 + i];
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const int64_t o = row * D + c0;
+    const F8 xv = ld8(x + o);
+    const float r = rsqrtf(ss[row] * inv_dfull + eps);
+    if (threadIdx.x == 0) rstd[row] = r;
+    F8 out;
+    if (z) {
+      const F8 zv = ld8(z + row * zs + c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out.v[i] = clampf(xv.v[i] * r * sc[i] * siluf_(clampf(zv.v[i], zclip)), oclip);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out.v[i] = clampf(xv.v[i] * r * sc[i], oclip);
+    }
+    st8(y + o, out);
+  }
+}
+
+__global__ void tp_norm_bwd_dot_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                       const bf16* __restrict__ z, int64_t zs, const float* __restrict__ scale,
+                                       const float* __restrict__ rstd, bf16* __restrict__ dz, float* __restrict__ dot,
+                                       float* __restrict__ dscale_part, int64_t M, int D, float zclip, float oclip) {
+  __shared__ float sh[32];
+  const int c0 = threadIdx.x * 8;
+  float sc[8], acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    sc[i] = scale[c0 + i];
+    acc[i] = 0.f;
+  }
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const int64_t o = row * D + c0;
+    const F8 d = ld8(dy + o), xv = ld8(x + o);
+    F8 zv, dzo;
+    if (z) zv = ld8(z + row * zs + c0);
+    float xh[8], g[8], dn[8];
+    tp_gate_terms(xv, z ? &zv : nullptr, d, sc, rstd[row], zclip, oclip, xh, g, dn, &dzo);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[i] += dn[i] * xh[i];
+      s += g[i] * xh[i];
+    }
+    s = row_sum(s, sh);
+    if (threadIdx.x == 0) dot[row] = s;
+    if (z) st8(dz + o, dzo);
+  }
+  if (dscale_part) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dscale_part[(int64_t)blockIdx.x * D + c0 + i] = acc[i];
+  }
+}
+
+__global__ void tp_norm_bwd_dx_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                      const bf16* __restrict__ z, int64_t zs, const float* __restrict__ scale,
+                                      const float* __restrict__ rstd, const float* __restrict__ dot,
+                                      bf16* __restrict__ dx, int64_t M, int D, float inv_dfull, float zclip,
+                                      float oclip) {
+  const int c0 = threadIdx.x * 8;
+  float sc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sc[i] = scale[c0 + i];
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const int64_t o = row * D + c0;
+    const F8 d = ld8(dy + o), xv = ld8(x + o);
+    F8 zv, dzo;
+    if (z) zv = ld8(z + row * zs + c0);
+    const float r = rstd[row];
+    float xh[8], g[8], dn[8];
+    tp_gate_terms(xv, z ? &zv : nullptr, d, sc, r, zclip, oclip, xh, g, dn, &dzo);
+    const float dm = dot[row] * inv_dfull;
+    F8 ox;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ox.v[i] = r * (g[i] - xh[i] * dm);
+    st8(dx + o, ox);
+  }
+}
+
 // ------------------------------------------------------------------ gdn_gates
 // Elementwise over (M, d) with head h = (c / Dh); 8 channels per thread.
 __global__ void gdn_gates_fwd_kernel(const bf16* __restrict__ bp, const bf16* __restrict__ wp,
@@ -475,4 +601,36 @@ void ahb_dt_act_bwd(const void* ddt, const void* u, void* du, int64_t n, cudaStr
   const int64_t n8 = n / 8;
   if (n8 <= 0) return;
   dt_act_bwd_kernel<<<ew_grid(n8), 256, 0, st>>>((const bf16*)ddt, (const bf16*)u, (bf16*)du, n8);
+}
+
+static int tp_norm_grid(int64_t M) { return (int)(M < (int64_t)sms() * 16 ? M : (int64_t)sms() * 16); }
+
+void ahb_tp_norm_sumsq(const void* x, float* ss, int64_t M, int D, cudaStream_t st) {
+  if (M <= 0) return;
+  tp_norm_sumsq_kernel<<<tp_norm_grid(M), D / 8, 0, st>>>((const bf16*)x, ss, M, D);
+}
+
+void ahb_tp_norm_fwd(const void* x, const void* z, int64_t zs, const float* scale, const float* ss, void* y,
+                     float* rstd, int64_t M, int D, float inv_dfull, float eps, float zclip, float oclip,
+                     cudaStream_t st) {
+  if (M <= 0) return;
+  tp_norm_fwd_kernel<<<tp_norm_grid(M), D / 8, 0, st>>>((const bf16*)x, (const bf16*)z, zs, scale, ss, (bf16*)y, rstd,
+                                                        M, D, inv_dfull, eps, zclip, oclip);
+}
+
+void ahb_tp_norm_bwd_dot(const void* dy, const void* x, const void* z, int64_t zs, const float* scale,
+                         const float* rstd, void* dz, float* dot, float* dscale_part, int64_t M, int D, float zclip,
+                         float oclip, cudaStream_t st) {
+  if (M <= 0) return;
+  tp_norm_bwd_dot_kernel<<<ahb_row_bwd_blocks(M), D / 8, 0, st>>>((const bf16*)dy, (const bf16*)x, (const bf16*)z,
+                                                                  zs, scale, rstd, (bf16*)dz, dot, dscale_part, M, D,
+                                                                  zclip, oclip);
+}
+
+void ahb_tp_norm_bwd_dx(const void* dy, const void* x, const void* z, int64_t zs, const float* scale,
+                        const float* rstd, const float* dot, void* dx, int64_t M, int D, float inv_dfull, float zclip,
+                        float oclip, cudaStream_t st) {
+  if (M <= 0) return;
+  tp_norm_bwd_dx_kernel<<<tp_norm_grid(M), D / 8, 0, st>>>((const bf16*)dy, (const bf16*)x, (const bf16*)z, zs, scale,
+                                                           rstd, dot, (bf16*)dx, M, D, inv_dfull, zclip, oclip);
 }

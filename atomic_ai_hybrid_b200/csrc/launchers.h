@@ -150,6 +150,18 @@ void ahb_norm_gate_fwd(const void* x, const void* z, int64_t zs, const float* sc
 void ahb_norm_gate_bwd(const void* dy, const void* x, const void* z, int64_t zs, const float* scale, const float* rstd,
                        void* dx, void* dz, float* dscale_part, int64_t M, int D, float zclip, float oclip,
                        cudaStream_t st);
+// tensor-parallel (head-split) RMSNorm, gated when z is non-null: the row sums ss (forward) and dot
+// (backward) are all-reduced over the group between the two passes of each direction
+void ahb_tp_norm_sumsq(const void* x, float* ss, int64_t M, int D, cudaStream_t st);
+void ahb_tp_norm_fwd(const void* x, const void* z, int64_t zs, const float* scale, const float* ss, void* y,
+                     float* rstd, int64_t M, int D, float inv_dfull, float eps, float zclip, float oclip,
+                     cudaStream_t st);
+void ahb_tp_norm_bwd_dot(const void* dy, const void* x, const void* z, int64_t zs, const float* scale,
+                         const float* rstd, void* dz, float* dot, float* dscale_part, int64_t M, int D, float zclip,
+                         float oclip, cudaStream_t st);
+void ahb_tp_norm_bwd_dx(const void* dy, const void* x, const void* z, int64_t zs, const float* scale,
+                        const float* rstd, const float* dot, void* dx, int64_t M, int D, float inv_dfull, float zclip,
+                        float oclip, cudaStream_t st);
 void ahb_gdn_gates_fwd(const void* bp, const void* wp, const void* fp, const float* decay_a, void* bg, void* wg,
                        float* g, int64_t n, int d, int Dh, cudaStream_t st);
 void ahb_gdn_gates_bwd(const void* dbg, const void* dwg, const float* dg, const void* bg, const void* wg,

@@ -647,12 +647,51 @@ def gdn2_layer(mod, x):
     return _gdn2_layer_composed(mod, x)
 
 
+class _TPNorm(torch.autograd.Function):
+    """RMSNorm over the full width of a head-split activation, gated like ``norm_gate``
+    when ``z`` is given (the mixer output norms ``out_norm`` / ``ssm_out_norm``, reference
+    `model.py:652` and `model.py:520`, with the heads split over the tensor-parallel group).  Each
+    direction is two kernel passes with one all-reduce of a per-row fp32 sum between them:
+    the sum of squares in the forward, the dot of the normalised input with its gradient
+    in the backward.  Nothing else crosses the group."""
+
+    @staticmethod
+    def forward(ctx, x, z, scale, eps, d_full, tp, zclip, oclip):
+        import torch.distributed as dist
+        ss = ext().tp_norm_sumsq(x)
+        dist.all_reduce(ss, group=tp.group)
+        y, rstd = ext().tp_norm_fwd(x, z, scale, ss, eps, 1.0 / d_full, zclip, oclip)
+        ctx.save_for_backward(x, z, scale, rstd)
+        ctx.tp, ctx.inv, ctx.zclip, ctx.oclip = tp, 1.0 / d_full, zclip, oclip
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        import torch.distributed as dist
+        x, z, scale, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        acc, direct = _acc_for(scale) if ctx.needs_input_grad[2] else (None, False)
+        dz, dot = ext().tp_norm_bwd_dot(dy, x, z, scale, rstd, ctx.zclip, ctx.oclip, acc)
+        dist.all_reduce(dot, group=ctx.tp.group)
+        dx = ext().tp_norm_bwd_dx(dy, x, z, scale, rstd, dot, ctx.inv, ctx.zclip, ctx.oclip)
+        return (dx, None if z is None else dz.view(z.shape), _ret_grad(scale, acc, direct), None, None, None, None,
+                None)
+
+
+def tp_norm(x, z, scale, eps: float, d_full: int, tp, zclip: float = math.inf, oclip: float = math.inf):
+    """``clamp(rmsnorm_group(x) * scale [* silu(clamp(z, +-zclip))], +-oclip)`` for bf16 rows
+    of ``x.shape[-1] % 256 == 0`` channels, ``d_full`` channels over the group."""
+    return _TPNorm.apply(x.contiguous(), z, scale, eps, d_full, tp, zclip, oclip)
+
+
 def _out_norm_gate(mod_cfg_d, o, z, scale, zclip=math.inf, oclip=math.inf):
     """Gated RMSNorm of a mixer output; over all heads of the tensor-parallel group
     when the heads are split (all-reduced statistics)."""
     from ..parallel.tp import get_tp, tp_norm_gate
     tp = get_tp()
     if tp is not None:
+        if o.is_cuda and o.dtype == torch.bfloat16 and z.dtype == torch.bfloat16 and row_fusable(o.shape[-1]):
+            return tp_norm(o, z, scale, 1e-6, mod_cfg_d, tp, zclip=zclip, oclip=oclip)
         return tp_norm_gate(o, z, scale, 1e-6, mod_cfg_d, tp, zclip=zclip, oclip=oclip)
     return norm_gate(o, z, scale, 1e-6, zclip=zclip, oclip=oclip)
 

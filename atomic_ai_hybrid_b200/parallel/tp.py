@@ -254,7 +254,13 @@ def get_tp() -> Optional[TPGroup]:
 
 def tp_rmsnorm(x: torch.Tensor, scale: torch.Tensor, eps: float, d_full: int, tp: TPGroup) -> torch.Tensor:
     """RMSNorm over the full width of a head-split activation: the per-row sum of
-    squares is all-reduced over the tensor-parallel ranks (fp32 statistics)."""
+    squares is all-reduced over the tensor-parallel ranks (fp32 statistics).  bf16 CUDA
+    rows on the kernel path run ``ops.kernels.tp_norm`` (the result is then bf16)."""
+    from .. import ops
+    if x.is_cuda and x.dtype == torch.bfloat16 and ops.get_impl() == "cuda" and x.shape[-1] % 256 == 0 \
+            and x.shape[-1] <= 8192:
+        from ..ops.kernels import tp_norm
+        return tp_norm(x, None, scale, eps, d_full, tp)
     xf = x.float()
     ss = tp.all_reduce(xf.square().sum(-1, keepdim=True))
     return xf * torch.rsqrt(ss / d_full + eps) * scale.float()

@@ -273,3 +273,36 @@ def test_bias_grad_acc_matches_column_sums(M, N):
     ref = acc + dy.float().sum(0)
     ext().bias_grad_acc(dy, acc)
     torch.testing.assert_close(acc, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("gated,zclip,oclip", [(True, 1e2, math.inf), (True, math.inf, 3e2), (False, math.inf, math.inf)])
+def test_tp_norm_matches_full_width(gated, zclip, oclip, monkeypatch):
+    """Head-split norm kernels (ops.kernels.tp_norm) on one GPU: two ranks holding the same
+    piece are emulated by an all-reduce that doubles the row sums, so each rank's output and
+    gradients equal the first half of a full-width (2 D) norm of the piece repeated twice."""
+    import torch.distributed as dist
+    monkeypatch.setattr(dist, "all_reduce", lambda t, group=None: t.mul_(2))
+    tp = type("G", (), {"group": None})()
+    torch.manual_seed(2)
+    M, D = 129, 1024
+    x = (torch.randn(M, D, device=DEV) * 2).to(torch.bfloat16)
+    zfull = (torch.randn(M, 2 * D, device=DEV) * 4).to(torch.bfloat16)
+    z = zfull[:, D:]  # strided rows, as Mamba2's `res`
+    z[0, :4] = 150
+    scale = torch.rand(D, device=DEV) * 2 + 0.5
+    gy = torch.randn(M, D, device=DEV).to(torch.bfloat16)
+    xr, zr, sr = (torch.cat([t, t], -1).float().clone().requires_grad_(True) for t in (x, z, scale))
+    y_ref = _rms(xr, sr)
+    if gated:
+        y_ref = y_ref * F.silu(zr.clamp(-zclip, zclip))
+    y_ref = y_ref.clamp(-oclip, oclip)
+    (y_ref * torch.cat([gy, gy], -1).float()).sum().backward()
+    xk, zk, sk = x.clone().requires_grad_(True), zfull.clone().requires_grad_(True), scale.clone().requires_grad_(True)
+    y = K.tp_norm(xk, zk[:, D:] if gated else None, sk, 1e-6, 2 * D, tp, zclip, oclip)
+    y.backward(gy)
+    _close(y, y_ref[:, :D].detach(), 1e-2, 5e-2, "y")
+    _close(xk.grad, xr.grad[:, :D], 2e-2, 5e-2, "dx")
+    if gated:
+        _close(zk.grad[:, D:], zr.grad[:, :D], 2e-2, 5e-2, "dz")
+        assert not zk.grad[:, :D].any()
+    _close(sk.grad, sr.grad[:D], 1e-3, 2e-2, "dscale")
