@@ -1005,6 +1005,33 @@ std::vector<torch::Tensor> norm_gate_bwd(torch::Tensor dy, torch::Tensor x, torc
   return {dx, dz};
 }
 
+// Shared-expert SwiGLU gate: h = silu(a) * b (bf16, contiguous, equal shapes) and its backward
+static void check_swiglu(const torch::Tensor& t, const torch::Tensor& ref, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.sizes() == ref.sizes() &&
+                  t.numel() % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "swiglu: ", n, " must be a contiguous 16-byte-aligned bf16 CUDA tensor shaped like a (numel % 8 == 0)");
+}
+
+torch::Tensor swiglu_fwd(torch::Tensor a, torch::Tensor b) {
+  check_swiglu(a, a, "a");
+  check_swiglu(b, a, "b");
+  auto h = torch::empty_like(a);
+  ahb_swiglu_fwd(a.data_ptr(), b.data_ptr(), h.data_ptr(), a.numel(), cur_stream());
+  check_launch("ahb_swiglu_fwd");
+  return h;
+}
+
+std::vector<torch::Tensor> swiglu_bwd(torch::Tensor dh, torch::Tensor a, torch::Tensor b) {
+  auto dhc = dh.contiguous();
+  check_swiglu(a, a, "a");
+  check_swiglu(b, a, "b");
+  check_swiglu(dhc, a, "dh");
+  auto da = torch::empty_like(a), db = torch::empty_like(b);
+  ahb_swiglu_bwd(dhc.data_ptr(), a.data_ptr(), b.data_ptr(), da.data_ptr(), db.data_ptr(), a.numel(), cur_stream());
+  check_launch("ahb_swiglu_bwd");
+  return {da, db};
+}
+
 // Tensor-parallel (head-split) RMSNorm, gated by z when given (ops.kernels.tp_norm): x (..., D) holds D
 // of the row's Dfull channels; the caller all-reduces the row sums (ss, dot) over the group between
 // the passes.
@@ -1631,6 +1658,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);
   m.def("norm_gate_fwd", &norm_gate_fwd);
   m.def("norm_gate_bwd", &norm_gate_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
   m.def("tp_norm_sumsq", &tp_norm_sumsq);
   m.def("tp_norm_fwd", &tp_norm_fwd);
   m.def("tp_norm_bwd_dot", &tp_norm_bwd_dot);

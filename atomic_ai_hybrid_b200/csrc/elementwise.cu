@@ -850,3 +850,57 @@ void ahb_embedding_bwd(const int64_t* ids, const void* dout, int dtype, float* a
   if (dtype == AHB_BF16) embed_bwd_kernel<bf16><<<(unsigned)T, 256, 0, st>>>(ids, (const bf16*)dout, acc, T, D, V);
   else embed_bwd_kernel<float><<<(unsigned)T, 256, 0, st>>>(ids, (const float*)dout, acc, T, D, V);
 }
+
+// Shared-expert SwiGLU gate on the two up-projections (the SwiGLU configurations; the reference's
+// shared expert, atomic_ops/moe_gmm.py:396-399, is the GELU variant):
+// h = silu(a) * b in fp32 with one rounding, and its backward da = dh * b * silu'(a),
+// db = dh * silu(a).  Eight bf16 elements per thread and step (n % 8 == 0).
+__global__ void __launch_bounds__(256) swiglu_fwd_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                                                         uint4* __restrict__ h, int64_t n8) {
+  for (int64_t i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += (int64_t)gridDim.x * 256) {
+    const uint4 av = a[i], bv = b[i];
+    const bf16* ap = reinterpret_cast<const bf16*>(&av);
+    const bf16* bp = reinterpret_cast<const bf16*>(&bv);
+    uint4 ov;
+    bf16* op = reinterpret_cast<bf16*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) op[k] = __float2bfloat16_rn(siluf_(__bfloat162float(ap[k])) * __bfloat162float(bp[k]));
+    h[i] = ov;
+  }
+}
+
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint4* __restrict__ dh, const uint4* __restrict__ a,
+                                                         const uint4* __restrict__ b, uint4* __restrict__ da,
+                                                         uint4* __restrict__ db, int64_t n8) {
+  for (int64_t i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += (int64_t)gridDim.x * 256) {
+    const uint4 dv = dh[i], av = a[i], bv = b[i];
+    const bf16* dp = reinterpret_cast<const bf16*>(&dv);
+    const bf16* ap = reinterpret_cast<const bf16*>(&av);
+    const bf16* bp = reinterpret_cast<const bf16*>(&bv);
+    uint4 dav, dbv;
+    bf16* dap = reinterpret_cast<bf16*>(&dav);
+    bf16* dbp = reinterpret_cast<bf16*>(&dbv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float x = __bfloat162float(ap[k]), g = __bfloat162float(dp[k]);
+      const float sg = sigmoidf_(x);
+      dap[k] = __float2bfloat16_rn(g * __bfloat162float(bp[k]) * sg * (1.f + x * (1.f - sg)));
+      dbp[k] = __float2bfloat16_rn(g * x * sg);
+    }
+    da[i] = dav;
+    db[i] = dbv;
+  }
+}
+
+void ahb_swiglu_fwd(const void* a, const void* b, void* h, int64_t n, cudaStream_t st) {
+  const int64_t n8 = n / 8;
+  if (n8 == 0) return;
+  swiglu_fwd_kernel<<<ew_blocks(n8, 256), 256, 0, st>>>((const uint4*)a, (const uint4*)b, (uint4*)h, n8);
+}
+
+void ahb_swiglu_bwd(const void* dh, const void* a, const void* b, void* da, void* db, int64_t n, cudaStream_t st) {
+  const int64_t n8 = n / 8;
+  if (n8 == 0) return;
+  swiglu_bwd_kernel<<<ew_blocks(n8, 256), 256, 0, st>>>((const uint4*)dh, (const uint4*)a, (const uint4*)b, (uint4*)da,
+                                                        (uint4*)db, n8);
+}

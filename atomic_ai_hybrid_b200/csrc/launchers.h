@@ -20,6 +20,9 @@ void ahb_conv1d_bwd(const void* x, int64_t xs, const void* w, int wdtype, const 
                     float* dw_acc, float* db_acc, int B, int L, int C, int dtype, int silu, float clip,
                     cudaStream_t st);
 void ahb_accumulate(float* acc, const void* g, int64_t n, int dtype, float scale, cudaStream_t st);
+// h = silu(a) * b over bf16 (n % 8 == 0, 16-byte aligned) and its backward
+void ahb_swiglu_fwd(const void* a, const void* b, void* h, int64_t n, cudaStream_t st);
+void ahb_swiglu_bwd(const void* dh, const void* a, const void* b, void* da, void* db, int64_t n, cudaStream_t st);
 // out[c] += sum_b part[b * D + c]
 void ahb_colsum_add(const float* part, int nb, int D, float* out, cudaStream_t st);
 void ahb_embedding_fwd(const int64_t* ids, const void* emb, int edtype, void* out, int odtype, int64_t T, int D,

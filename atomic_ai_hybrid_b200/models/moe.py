@@ -159,9 +159,10 @@ class MoE(nn.Module):
                 from ..ops import kernels as K
                 h1, h3 = K.linear_multi(flat, [(self.shared_w1.kernel, self.shared_w1.bias),
                                                (self.shared_w3.kernel, self.shared_w3.bias)])
+                h = K.swiglu(h1, h3)
             else:
                 h1, h3 = self.shared_w1(flat), self.shared_w3(flat)
-            h = F.silu(h1) * h3
+                h = F.silu(h1) * h3
         else:
             h = R.gelu_tanh(self.shared_w1(flat))
         if self.training and self.cfg.dropout_rate > 0:

@@ -580,6 +580,30 @@ def linear_multi(x, pairs):
     return _MultiLinear.apply(x, len(pairs), *ws, *bs)
 
 
+class _SwiGLU(torch.autograd.Function):
+    """Shared-expert gate ``silu(a) * b`` on bf16 for the SwiGLU configurations (the
+    reference's shared expert, `atomic_ops/moe_gmm.py:396-399`, is the GELU variant): one
+    kernel each way, fp32 inside with one rounding per output."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return ext().swiglu_fwd(a, b)
+
+    @staticmethod
+    def backward(ctx, dh):
+        a, b = ctx.saved_tensors
+        da, db = ext().swiglu_bwd(dh, a, b)
+        return da, db
+
+
+def swiglu(a, b):
+    if (a.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and a.shape == b.shape
+            and a.is_contiguous() and b.is_contiguous() and a.numel() % 8 == 0):
+        return _SwiGLU.apply(a, b)
+    return F.silu(a) * b
+
+
 class _Router(torch.autograd.Function):
     """Fused cosine router: returns the differentiable (gate, sum_t softmax(l),
     sum_t lse^2) and the non-differentiable (top_idx, expert counts, statistics)."""

@@ -306,3 +306,19 @@ def test_tp_norm_matches_full_width(gated, zclip, oclip, monkeypatch):
         _close(zk.grad[:, D:], zr.grad[:, :D], 2e-2, 5e-2, "dz")
         assert not zk.grad[:, :D].any()
     _close(sk.grad, sr.grad[:D], 1e-3, 2e-2, "dscale")
+
+
+def test_shared_expert_swiglu():
+    """silu(a) * b kernels (shared expert of the SwiGLU configurations) against fp32 autograd."""
+    torch.manual_seed(3)
+    a = (torch.randn(1000, 264, device=DEV) * 3).to(torch.bfloat16)
+    b = torch.randn(1000, 264, device=DEV).to(torch.bfloat16)
+    dh = torch.randn(1000, 264, device=DEV).to(torch.bfloat16)
+    ar, br = a.float().requires_grad_(True), b.float().requires_grad_(True)
+    (F.silu(ar) * br).backward(dh.float())
+    ak, bk = a.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    h = K.swiglu(ak, bk)
+    h.backward(dh)
+    _close(h, F.silu(a.float()) * b.float(), 1e-2, 1e-2, "h")
+    _close(ak.grad, ar.grad, 1e-2, 1e-2, "da")
+    _close(bk.grad, br.grad, 1e-2, 1e-2, "db")
