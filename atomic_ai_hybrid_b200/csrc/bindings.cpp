@@ -898,6 +898,41 @@ void muon_ns(torch::Tensor X, int64_t steps) {
   }
 }
 
+// The same iteration on tall matrices (E >= 2 of a x b, a > b) without transposing them: the Gram
+// matrix G_e = X_e^T X_e (b x b) comes from the K-grouped GEMM (groups of a rows, summed into zeroed
+// bf16 accumulators) and Y_e = X_e G_e from the M-grouped GEMM that reads B row-major.
+void muon_ns_tall(torch::Tensor X, int64_t steps) {
+  TORCH_CHECK(X.is_cuda() && X.scalar_type() == at::kFloat && X.is_contiguous() && X.dim() == 3,
+              "muon_ns_tall: X must be a contiguous (E, a, b) fp32 CUDA tensor");
+  const int64_t E = X.size(0), a = X.size(1), b = X.size(2);
+  TORCH_CHECK(E >= 2 && E <= 192 && a > b && a % 128 == 0 && b % 128 == 0,
+              "muon_ns_tall: 2..192 matrices of a x b with a > b, a % 128 == 0, b % 128 == 0");
+  const int PM = moe_pair() && a % 256 == 0 ? AHB_GEMM_PAIR : 0;  // row groups start on 256-row boundaries
+  const int PW = moe_pair() && b % 256 == 0 ? AHB_GEMM_PAIR : 0;  // Gram rows a multiple of 256
+  auto ob = X.options().dtype(at::kBFloat16);
+  auto Xb = torch::empty({E * a, b}, ob);
+  auto G = torch::empty({E * b, b}, ob);
+  auto Y = torch::empty({E * a, b}, ob);
+  auto off = torch::arange(0, E * a + 1, a, torch::dtype(torch::kInt32).device(X.device()));
+  int* err = err_word().data_ptr<int>();
+  auto st = cur_stream();
+  ahb_ns_update(X.data_ptr<float>(), nullptr, Xb.data_ptr(), X.numel(), num_sms(), st);
+  check_launch("ahb_ns_update");
+  for (int64_t s = 0; s < steps; ++s) {
+    G.zero_();
+    int rc = ahb_moe_gemm(AHB_GEMM_WGRAD | AHB_GEMM_ACC_BF16 | PW, Xb.data_ptr(), nullptr, E * a, b, Xb.data_ptr(),
+                          nullptr, E * a, b, 0, off.data_ptr<int>(), (int)E, (int)b, (int)b, 0, 0, G.data_ptr(),
+                          nullptr, nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "muon X^T X");
+    rc = ahb_moe_gemm(AHB_GEMM_FWD_DOWN | PM, Xb.data_ptr(), nullptr, E * a, b, G.data_ptr(), nullptr, E * b, b,
+                      (int)b, off.data_ptr<int>(), (int)E, (int)b, 0, (int)b, (int)(b / 64), Y.data_ptr(), nullptr,
+                      nullptr, nullptr, nullptr, 0.f, err, num_sms(), st);
+    gemm_check(rc, "muon X G");
+    ahb_ns_update(X.data_ptr<float>(), Y.data_ptr(), Xb.data_ptr(), X.numel(), num_sms(), st);
+    check_launch("ahb_ns_update");
+  }
+}
+
 // ------------------------------------------------------------ fused layer glue (fused_norm.cu)
 static void check_rows(const torch::Tensor& t, int64_t D, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.size(-1) == D, n,
@@ -1653,6 +1688,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optim_prepare", &optim_prepare);
   m.def("optim_apply", &optim_apply);
   m.def("muon_ns", &muon_ns);
+  m.def("muon_ns_tall", &muon_ns_tall);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, py::arg("x"), py::arg("delta"), py::arg("scale"), py::arg("clip"),
         py::arg("eps"), py::arg("stats") = py::none());
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd);

@@ -855,8 +855,9 @@ def newton_schulz3(g, steps: int = 3, eps: float = 1e-4):
     X <- 1.5 X - 0.5 X X^T X on the tcgen05 grouped GEMM (``muon_ns``: bf16 operands, fp32
     accumulation, X itself kept in fp32, non-finite entries zeroed after every step).
 
-    The step commutes with transposition, so a tall matrix runs as its transpose and the Gram
-    matrix X X^T is the smaller one (r x r, r the shorter side).  The matrices of a 3-D tensor
+    The step commutes with transposition, so the Gram matrix is taken on the shorter side
+    (r x r): X X^T for a wide matrix, X^T X (K-grouped GEMM) for several tall ones, and a single
+    tall matrix runs as its transpose.  The matrices of a 3-D tensor
     (the experts) are the groups of the same two launches per step.  A shorter side that is not a
     multiple of 128 (or a longer one not of 64) runs the fp32 PyTorch iteration instead."""
     if not g.is_cuda or g.ndim not in (2, 3):
@@ -866,6 +867,19 @@ def newton_schulz3(g, steps: int = 3, eps: float = 1e-4):
     r, c = (m.shape[2], m.shape[1]) if tall else (m.shape[1], m.shape[2])
     if r % 128 or c % 64:
         return R.newton_schulz3(g, steps, eps)
+    if tall and m.shape[0] >= 2 and c % 128 == 0:
+        # several tall matrices (the experts' up-projections): X^T X from the K-grouped GEMM,
+        # no transposed copies
+        X = m.float()
+        nrm = torch.linalg.vector_norm(X, dim=(-2, -1), keepdim=True)
+        X = (X / torch.where(nrm < eps, torch.ones_like(nrm), nrm)).contiguous()
+        for e0 in range(0, X.shape[0], 192):
+            part = X[e0:e0 + 192]
+            if part.shape[0] >= 2:
+                ext().muon_ns_tall(part, steps)
+            else:  # a lone last matrix (already of norm 1) runs as its transpose
+                part.copy_(newton_schulz3(part[0], steps, eps).unsqueeze(0))
+        return X.reshape(g.shape)
     X = (m.transpose(1, 2) if tall else m).float()
     nrm = torch.linalg.vector_norm(X, dim=(-2, -1), keepdim=True)
     X = (X / torch.where(nrm < eps, torch.ones_like(nrm), nrm)).contiguous()
